@@ -1,0 +1,78 @@
+"""Communicator configuration and environment flags.
+
+Same switches as the reference (``SGLANG_MAILBOX_AR`` enables the communicator,
+``SGLANG_MAILBOX_AR_VERBOSE`` turns on build/setup logging,
+sglang/README.md:20 and sglang/mailbox_all_reduce.py:41) plus the knobs the
+B200 design adds: buffer sizes, per-TP algorithm thresholds, the device wait
+bound and an NVLS switch.
+"""
+import dataclasses
+import os
+
+MiB = 1 << 20
+
+# Reference default for the largest message handled in-house (one 24 MB half,
+# sglang/mailbox_all_reduce.py:20). Larger messages go through the chunked
+# path up to ``max_size`` here.
+REFERENCE_MAX_SIZE = 24 * MiB
+
+
+def env_flag(name: str, default: bool = False) -> bool:
+    v = os.environ.get(name)
+    if v is None:
+        return default
+    return v.strip().lower() in ("1", "true", "yes", "on")
+
+
+def mailbox_enabled() -> bool:
+    """``SGLANG_MAILBOX_AR=1`` turns the communicator on (reference flag)."""
+    return env_flag("SGLANG_MAILBOX_AR", False)
+
+
+@dataclasses.dataclass
+class CommConfig:
+    # largest message (bytes) handled by the communicator; above it the caller
+    # falls back to NCCL. The kernels chunk through the buffer, so this is a
+    # policy limit, not a buffer limit.
+    max_size: int = 256 * MiB
+    # one ping-pong data half of the symmetric buffer (two halves are mapped)
+    half_bytes: int = 64 * MiB
+    # segmented (overlap) path: bytes per slot per source rank (0 disables)
+    seg_slot_bytes: int = 8 * MiB
+    # bound of every device-side wait (the reference uses ~1 s, mailbox_ar_ext.cu:5)
+    timeout_ns: int = 2_000_000_000
+    # bound of host-side handshakes (FD exchange)
+    handshake_timeout_ms: int = 60_000
+    # use NVLS (multimem) when the GPUs expose multicast
+    nvls: bool = True
+    # one-shot (push) is used up to this many bytes, per world size
+    oneshot_max: dict = dataclasses.field(
+        default_factory=lambda: {2: 4 * MiB, 3: 1 * MiB, 4: 1 * MiB, 5: 512 << 10, 6: 512 << 10, 7: 512 << 10, 8: 512 << 10}
+    )
+    # NVLS is preferred over two-shot at/above this many bytes
+    nvls_min: int = 1 * MiB
+    # grid cap of the allreduce kernels (blocks)
+    max_blocks: int = 64
+    # CPU transport: bytes per slot of the shared-memory mailbox
+    cpu_slot_bytes: int = 32 * MiB
+    cpu_timeout_ms: int = 30_000
+    verbose: bool = False
+
+    @classmethod
+    def from_env(cls) -> "CommConfig":
+        c = cls()
+        if "MBX_MAX_SIZE" in os.environ:
+            c.max_size = int(os.environ["MBX_MAX_SIZE"])
+        if "MBX_HALF_BYTES" in os.environ:
+            c.half_bytes = int(os.environ["MBX_HALF_BYTES"])
+        if "MBX_TIMEOUT_MS" in os.environ:
+            c.timeout_ns = int(float(os.environ["MBX_TIMEOUT_MS"]) * 1e6)
+        if "MBX_NVLS" in os.environ:
+            c.nvls = env_flag("MBX_NVLS", True)
+        if os.environ.get("NCCL_NVLS_ENABLE", "1") == "0":
+            # a run that turned NVLS off for NCCL wants it off everywhere
+            c.nvls = False
+        if "MBX_MAX_BLOCKS" in os.environ:
+            c.max_blocks = int(os.environ["MBX_MAX_BLOCKS"])
+        c.verbose = env_flag("SGLANG_MAILBOX_AR_VERBOSE", False)
+        return c

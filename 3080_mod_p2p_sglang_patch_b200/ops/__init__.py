@@ -1,0 +1,174 @@
+"""sm_100a kernels of the served decoder, as torch-tensor functions.
+
+Every function dispatches to the in-tree CUDA extension; there is no PyTorch
+fallback (a missing extension raises). Scratch memory (GEMM split-K partials,
+decode split-KV partials, the GEMM error word) comes from a per-device
+workspace that is allocated once and reused, so CUDA-graph capture never
+allocates.
+"""
+import math
+
+import torch
+
+from .._ext import cuda_ext
+
+
+class _Workspace:
+    def __init__(self, device):
+        self.device = device
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
+        self.dec_o = torch.empty(0, dtype=torch.float32, device=device)
+        self.dec_lse = torch.empty(0, dtype=torch.float32, device=device)
+
+    def gemm(self, n):
+        if self.gemm_ws.numel() < n:
+            self.gemm_ws = torch.empty(max(n, 1 << 22), dtype=torch.float32, device=self.device)
+        return self.gemm_ws
+
+    def decode(self, n_o, n_lse):
+        if self.dec_o.numel() < n_o:
+            self.dec_o = torch.empty(max(n_o, 1 << 20), dtype=torch.float32, device=self.device)
+        if self.dec_lse.numel() < n_lse:
+            self.dec_lse = torch.empty(max(n_lse, 1 << 14), dtype=torch.float32, device=self.device)
+        return self.dec_o, self.dec_lse
+
+
+_WS = {}
+
+
+def workspace(device) -> _Workspace:
+    key = torch.device(device).index
+    if key is None:
+        key = torch.cuda.current_device()
+    ws = _WS.get(key)
+    if ws is None:
+        ws = _WS[key] = _Workspace(torch.device("cuda", key))
+    return ws
+
+
+def reserve(device, gemm_elems=0, decode_o=0, decode_lse=0):
+    """Pre-size the scratch buffers (call before CUDA-graph capture)."""
+    ws = workspace(device)
+    if gemm_elems:
+        ws.gemm(gemm_elems)
+    if decode_o or decode_lse:
+        ws.decode(decode_o, decode_lse)
+
+
+def gemm_error(device=None) -> int:
+    """Non-zero if a GEMM's bounded wait gave up (sticky until cleared)."""
+    return int(workspace(device or torch.cuda.current_device()).err.item())
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: torch.Tensor = None,
+         bn: int = 0, splits: int = 0) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ w[N, K]^T (+ residual), tcgen05/TMEM kernel."""
+    C = cuda_ext()
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    ws = workspace(a.device)
+    plan_bn, plan_splits = C.gemm_plan(M, N, K)
+    s = splits or plan_splits
+    wbuf = ws.gemm(s * M * N) if s > 1 else None
+    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits)
+    return out
+
+
+def rmsnorm(x, w, eps, out=None):
+    out = torch.empty_like(x) if out is None else out
+    cuda_ext().rmsnorm(x, w, out, eps)
+    return out
+
+
+def fused_add_rmsnorm(x, residual, w, eps, out=None):
+    """residual <- bf16(x + residual); returns rmsnorm(residual) * w."""
+    out = torch.empty_like(x) if out is None else out
+    cuda_ext().fused_add_rmsnorm(x, residual, w, out, eps)
+    return out
+
+
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
+    """[max_pos, head_dim] fp32 table: cos in the first half, sin in the second."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
+
+
+def rope_and_cache(qkv, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v_cache=None, q_out=None, page=16):
+    """Rotate q/k (neox), write rotated q to q_out [T, nq, 128] and k/v to the
+    paged cache at ``slots`` (int64 block*page+offset)."""
+    T = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty((T, nq, 128), dtype=qkv.dtype, device=qkv.device)
+    cuda_ext().rope_and_cache(qkv, positions, cos_sin, slots, q_out, k_cache, v_cache, nq, nkv, page)
+    return q_out
+
+
+def silu_mul(x, out=None):
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=x.dtype, device=x.device)
+    cuda_ext().silu_mul(x, out)
+    return out
+
+
+def embedding(ids, table, start=0, out=None):
+    if out is None:
+        out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device)
+    cuda_ext().embedding(ids, table, out, start)
+    return out
+
+
+def argmax(logits, offset=0, vals=None, idx=None):
+    B = logits.shape[0]
+    if vals is None:
+        vals = torch.empty(B, dtype=torch.float32, device=logits.device)
+    if idx is None:
+        idx = torch.empty(B, dtype=torch.int64, device=logits.device)
+    cuda_ext().argmax(logits, offset, vals, idx)
+    return vals, idx
+
+
+def argmax_combine(vals, idx, out=None):
+    if out is None:
+        out = torch.empty(vals.shape[1], dtype=torch.int64, device=vals.device)
+    cuda_ext().argmax_combine(vals, idx, out)
+    return out
+
+
+def prefill_tiles(q_lens, bq: int = 64):
+    """(request, q offset) pairs of the 64-row query tiles of a ragged batch."""
+    tiles = []
+    for r, n in enumerate(q_lens):
+        for off in range(0, n, bq):
+            tiles.append((r, off))
+    return torch.tensor(tiles, dtype=torch.int32).reshape(-1, 2)
+
+
+def prefill_attention(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles, scale=None, out=None):
+    if out is None:
+        out = torch.empty_like(q)
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    cuda_ext().prefill_attention(q, k_cache, v_cache, out, cu_q, kv_len, block_table, tiles, scale)
+    return out
+
+
+def decode_splits(batch: int, nkv: int, max_len: int, sms: int = 148) -> int:
+    """Split-KV factor so (batch x kv-heads x splits) fills the SMs."""
+    want = max(1, (2 * sms) // max(1, batch * nkv))
+    by_len = max(1, max_len // 256)
+    return int(min(want, by_len, 64))
+
+
+def decode_attention(q, k_cache, v_cache, kv_len, block_table, scale=None, splits=1, out=None):
+    if out is None:
+        out = torch.empty_like(q)
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    B, nq, _ = q.shape
+    po = pl = None
+    if splits > 1:
+        po, pl = workspace(q.device).decode(B * nq * splits * 128, B * nq * splits)
+    cuda_ext().decode_attention(q, k_cache, v_cache, out, kv_len, block_table, po, pl, splits, scale)
+    return out

@@ -1,0 +1,681 @@
+// Cross-GPU allreduce kernels over NVLink 5 / NVSwitch symmetric memory.
+//
+// Replaces the reference's 5/6-kernel lockstep push (waitack -> produce ->
+// flag -> wait_local -> reduce -> ack, sglang/mailbox_ar_ext.cu:124-167) with
+// ONE launch per call for every algorithm:
+//
+//   kOneShotPush  each rank stores its input into slot[rank] of every peer's
+//                 buffer ("mailbox push", the reference's data path), block
+//                 barrier, then reduces its own buffer locally.
+//   kOneShotPull  each rank copies its input into its own buffer, barrier,
+//                 then every rank loads all peers' copies over NVLink.
+//   kTwoShot      reduce-scatter by pull + all-gather by pull (2(n-1)/n bytes).
+//   kNvls         reduce-scatter with multimem.ld_reduce through the switch and
+//                 all-gather with multimem.st (NVLS), when multicast exists.
+//
+// All sums are fp32 in rank order 0..n-1 with a single final rounding (the
+// reference's mb_add semantics, sglang/mailbox_ar_ext.cu:91-99), so every rank
+// gets the bit-identical result and x + x is exact.
+//
+// Every wait is bounded by %globaltimer; a timeout records (code, block, peer,
+// phase, epoch) in host-mapped memory and the block returns. There is no trap.
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "../kernels.h"
+#include "ar_common.cuh"
+
+namespace mbx {
+
+enum Algo : int { kAuto = 0, kOneShotPush = 1, kOneShotPull = 2, kTwoShot = 3, kNvls = 4 };
+
+constexpr int kArThreads = 512;
+
+MBX_DEVICE uint32_t call_epoch(const ArCtx& c) {
+  return *reinterpret_cast<volatile uint32_t*>(c.state + kStEpoch) + 1u;
+}
+MBX_DEVICE bool poisoned(const ArCtx& c) {
+  return *reinterpret_cast<volatile uint32_t*>(c.state + kStErr) != 0u;
+}
+
+// --------------------------------------------------------------------------
+// One-shot push ("mailbox"): slot size = half / world.
+// --------------------------------------------------------------------------
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                     uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t epoch = call_epoch(c);
+  if (!poisoned(c)) {
+    const uint64_t slot = c.half_bytes / W;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (uint64_t i = i0; i < nvec; i += stride) {
+      const uint4 v = ld_nc_v4(in + i);
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int r = (c.rank + j) % W;  // stagger destinations across ranks
+        st_v4(data_half(c.bufs[r], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
+      }
+    }
+    if (block_barrier(c, 0, epoch, &s_ok)) {
+      const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+      for (uint64_t i = i0; i < nvec; i += stride) {
+        uint4 v[W];
+#pragma unroll
+        for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + i * 16);
+        float acc[Pack<T>::N] = {};
+#pragma unroll
+        for (int r = 0; r < W; ++r) unpack_add<T>(v[r], acc);
+        out[i] = pack_from<T>(acc);
+      }
+    }
+  }
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
+// One-shot pull.
+// --------------------------------------------------------------------------
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                     uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t epoch = call_epoch(c);
+  if (!poisoned(c)) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+    for (uint64_t i = i0; i < nvec; i += stride) st_v4(mine + i * 16, ld_nc_v4(in + i));
+    if (block_barrier(c, 0, epoch, &s_ok)) {
+      for (uint64_t i = i0; i < nvec; i += stride) {
+        uint4 v[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const int r = (c.rank + j) % W;
+          v[r] = ld_cg_v4(data_half(c.bufs[r], epoch, c.half_bytes) + i * 16);
+        }
+        float acc[Pack<T>::N] = {};
+#pragma unroll
+        for (int r = 0; r < W; ++r) unpack_add<T>(v[r], acc);
+        out[i] = pack_from<T>(acc);
+      }
+    }
+  }
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
+// Two-shot: chunk c of the message is owned by rank c.
+//   A: copy input -> own slot0             B: owner reduces its chunk from all
+//   slot0s into own slot1 (+ out)          C: gather the other chunks' slot1s.
+// Block b always handles the same element partition of every chunk, so the
+// pairwise block barrier orders exactly the data each block consumes.
+// --------------------------------------------------------------------------
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t epoch = call_epoch(c);
+  if (!poisoned(c)) {
+    const uint64_t slot1 = c.half_bytes / 2;
+    const uint64_t cs = (nvec + W - 1) / W;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t o0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+    for (int ch = 0; ch < W; ++ch) {
+      const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
+      for (uint64_t i = beg + o0; i < end; i += stride) st_v4(mine + i * 16, ld_nc_v4(in + i));
+    }
+    if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    {
+      const uint64_t beg = c.rank * cs, end = min(nvec, beg + cs);
+      for (uint64_t i = beg + o0; i < end; i += stride) {
+        uint4 v[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const int r = (c.rank + j) % W;
+          v[r] = ld_cg_v4(data_half(c.bufs[r], epoch, c.half_bytes) + i * 16);
+        }
+        float acc[Pack<T>::N] = {};
+#pragma unroll
+        for (int r = 0; r < W; ++r) unpack_add<T>(v[r], acc);
+        const uint4 s = pack_from<T>(acc);
+        st_v4(mine + slot1 + i * 16, s);
+        out[i] = s;
+      }
+    }
+    if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    for (int j = 1; j < W; ++j) {
+      const int p = (c.rank + j) % W;
+      const uint64_t beg = p * cs, end = min(nvec, beg + cs);
+      const char* src = data_half(c.bufs[p], epoch, c.half_bytes) + slot1;
+      for (uint64_t i = beg + o0; i < end; i += stride) out[i] = ld_cg_v4(src + i * 16);
+    }
+  }
+done:
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
+// NVLS: multimem.ld_reduce (switch-side sum, fp32 accumulation for 16-bit
+// types) + multimem.st broadcast of the owner's chunk.
+// --------------------------------------------------------------------------
+template <typename T>
+MBX_DEVICE uint4 multimem_ld_reduce(const void* mc);
+template <>
+MBX_DEVICE uint4 multimem_ld_reduce<__nv_bfloat16>(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+template <>
+MBX_DEVICE uint4 multimem_ld_reduce<__half>(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+template <>
+MBX_DEVICE uint4 multimem_ld_reduce<float>(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+MBX_DEVICE void multimem_st(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+MBX_DEVICE void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_nvls_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                             uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t epoch = call_epoch(c);
+  if (!poisoned(c)) {
+    const uint64_t slot1 = c.half_bytes / 2;
+    const uint64_t cs = (nvec + W - 1) / W;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t o0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+    char* mc = data_half(c.mc, epoch, c.half_bytes);
+    for (int ch = 0; ch < W; ++ch) {
+      const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
+      for (uint64_t i = beg + o0; i < end; i += stride) st_v4(mine + i * 16, ld_nc_v4(in + i));
+    }
+    fence_proxy_alias();
+    if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    fence_proxy_alias();
+    {
+      const uint64_t beg = c.rank * cs, end = min(nvec, beg + cs);
+      for (uint64_t i = beg + o0; i < end; i += stride) {
+        const uint4 s = multimem_ld_reduce<T>(mc + i * 16);
+        multimem_st(mc + slot1 + i * 16, s);
+      }
+    }
+    fence_proxy_alias();
+    if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    fence_proxy_alias();
+    for (int ch = 0; ch < W; ++ch) {
+      const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
+      for (uint64_t i = beg + o0; i < end; i += stride) out[i] = ld_cg_v4(mine + slot1 + i * 16);
+    }
+  }
+done:
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
+// Fused allreduce + residual add + RMSNorm (bf16, rows of H elements).
+//   ar   = bf16(sum_r in_r)                 (same rounding as a plain AR)
+//   res  = bf16(ar + residual)   -> residual (in place)
+//   out  = bf16(res * rsqrt(mean(res^2) + eps) * w)
+// One-shot push by rows, or two-shot (rows split by owner rank, all-gather of
+// the reduced rows, each rank normalises every row locally).
+// --------------------------------------------------------------------------
+MBX_DEVICE float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) s += red[i];
+  return s;
+}
+
+// res/out for one row given the reduced bf16 row `ar` (read through `ld`).
+template <typename LoadAr>
+MBX_DEVICE void residual_rmsnorm_row(LoadAr ld, uint4* residual_row, const uint4* w_row, uint4* out_row,
+                                     int hvec, int H, float eps, float* red) {
+  float ss = 0.f;
+  for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
+    float a[8] = {};
+    unpack_add<__nv_bfloat16>(ld(p), a);
+    // round the AR result to bf16 first (matches AR-then-add unfused order)
+    const uint4 arb = pack_from<__nv_bfloat16>(a);
+    float r[8] = {};
+    unpack_add<__nv_bfloat16>(arb, r);
+    unpack_add<__nv_bfloat16>(residual_row[p], r);
+    const uint4 rb = pack_from<__nv_bfloat16>(r);
+    residual_row[p] = rb;
+    float q[8] = {};
+    unpack_add<__nv_bfloat16>(rb, q);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += q[k] * q[k];
+  }
+  const float tot = block_sum(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + eps);
+  for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
+    float q[8] = {}, wv[8] = {};
+    unpack_add<__nv_bfloat16>(residual_row[p], q);
+    unpack_add<__nv_bfloat16>(w_row[p], wv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = q[k] * rstd * wv[k];
+    out_row[p] = pack_from<__nv_bfloat16>(q);
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_oneshot_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                        uint4* residual, const uint4* __restrict__ w,
+                                                                        uint4* __restrict__ out, int M, int H,
+                                                                        float eps) {
+  __shared__ bool s_ok;
+  __shared__ float red[32];
+  const uint32_t epoch = call_epoch(c);
+  const int hvec = H / 8;
+  if (!poisoned(c)) {
+    const uint64_t slot = c.half_bytes / W;
+    for (int row = blockIdx.x; row < M; row += gridDim.x) {
+      for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
+        const uint64_t i = (uint64_t)row * hvec + p;
+        const uint4 v = ld_nc_v4(in + i);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const int r = (c.rank + j) % W;
+          st_v4(data_half(c.bufs[r], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
+        }
+      }
+    }
+    if (block_barrier(c, 0, epoch, &s_ok)) {
+      const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+      for (int row = blockIdx.x; row < M; row += gridDim.x) {
+        const uint64_t base = (uint64_t)row * hvec;
+        // Reduce into a bf16 pack directly (fp32 sum, one rounding).
+        auto ld_bf16 = [&](int p) {
+          uint4 v[W];
+#pragma unroll
+          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (base + p) * 16);
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
+          return pack_from<__nv_bfloat16>(acc);
+        };
+        residual_rmsnorm_row(ld_bf16, residual + base, w, out + base, hvec, H, eps, red);
+      }
+    }
+  }
+  finish_call(c, epoch);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                        uint4* residual, const uint4* __restrict__ w,
+                                                                        uint4* __restrict__ out, int M, int H,
+                                                                        float eps) {
+  __shared__ bool s_ok;
+  __shared__ float red[32];
+  const uint32_t epoch = call_epoch(c);
+  const int hvec = H / 8;
+  if (!poisoned(c)) {
+    const uint64_t slot1 = c.half_bytes / 2;
+    const int rc = (M + W - 1) / W;
+    char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+    for (int ch = 0; ch < W; ++ch) {
+      const int beg = ch * rc, end = min(M, beg + rc);
+      for (int row = beg + blockIdx.x; row < end; row += gridDim.x)
+        for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
+          const uint64_t i = (uint64_t)row * hvec + p;
+          st_v4(mine + i * 16, ld_nc_v4(in + i));
+        }
+    }
+    if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    {
+      const int beg = c.rank * rc, end = min(M, beg + rc);
+      for (int row = beg + blockIdx.x; row < end; row += gridDim.x)
+        for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
+          const uint64_t i = (uint64_t)row * hvec + p;
+          uint4 v[W];
+#pragma unroll
+          for (int j = 0; j < W; ++j) {
+            const int r = (c.rank + j) % W;
+            v[r] = ld_cg_v4(data_half(c.bufs[r], epoch, c.half_bytes) + i * 16);
+          }
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
+          st_v4(mine + slot1 + i * 16, pack_from<__nv_bfloat16>(acc));
+        }
+    }
+    if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    for (int ch = 0; ch < W; ++ch) {
+      const int beg = ch * rc, end = min(M, beg + rc);
+      const char* src = data_half(c.bufs[ch], epoch, c.half_bytes) + slot1;
+      for (int row = beg + blockIdx.x; row < end; row += gridDim.x) {
+        const uint64_t base = (uint64_t)row * hvec;
+        auto ld = [&](int p) { return ld_cg_v4(src + (base + p) * 16); };
+        residual_rmsnorm_row(ld, residual + base, w, out + base, hvec, H, eps, red);
+      }
+    }
+  }
+done:
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
+// Segmented allreduce (overlap path). The reference pushes row segments with
+// the copy engine and flags a peer slot from the host-maintained seq
+// (sglang/mailbox_ar_ext.cu:233-342), which is not graph-replay safe. Here the
+// seq is device-resident: submit (side stream) pushes segment s into
+// slot s%3 of every peer after that peer freed the slot, then releases a
+// ready flag; wait (main stream) waits for every peer's flag, reduces, and
+// acks the slot free to each pusher.
+// --------------------------------------------------------------------------
+MBX_DEVICE uint32_t* seg_ready(char* base, int slot, int src) {
+  return reinterpret_cast<uint32_t*>(base + kSegReadyOff) + slot * kMaxRanks + src;
+}
+MBX_DEVICE uint32_t* seg_free(char* base, int slot, int src) {
+  return reinterpret_cast<uint32_t*>(base + kSegFreeOff) + slot * kMaxRanks + src;
+}
+MBX_DEVICE char* seg_data(const ArCtx& c, char* base, int slot, int src) {
+  return base + kSigBytes + 2 * c.half_bytes + ((uint64_t)slot * kMaxRanks + src) * c.seg_slot_bytes;
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) seg_submit_kernel(ArCtx c, const uint4* __restrict__ in, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t seq = *reinterpret_cast<volatile uint32_t*>(c.state + kStSegSubmit) + 1u;
+  const int slot = seq % kSegSlots;
+  if (threadIdx.x == 0) s_ok = true;
+  __syncthreads();
+  if (!poisoned(c)) {
+    // Slot reuse: every receiver must have acked seq - kSegSlots.
+    if (threadIdx.x < W && seq > (uint32_t)kSegSlots) {
+      const int r = threadIdx.x;
+      if (!wait_flag_geq(seg_free(c.bufs[c.rank], slot, r), seq - kSegSlots, c.timeout_ns)) {
+        record_error(c, kErrSegFree, blockIdx.x, r, 10, seq);
+        s_ok = false;
+      }
+    }
+    __syncthreads();
+    if (s_ok) {
+      const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+      for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+        const uint4 v = ld_nc_v4(in + i);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const int r = (c.rank + j) % W;
+          st_v4(seg_data(c, c.bufs[r], slot, c.rank) + i * 16, v);
+        }
+      }
+    }
+  }
+  // Every block's stores must land before the single ready flag per peer: the
+  // last block to finish releases the flags and advances the device seq (all
+  // blocks have read it by then).
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    const uint32_t prev = atomicAdd(c.state + kStSegSubmitDone, 1u);
+    if (prev == gridDim.x - 1) {
+      c.state[kStSegSubmitDone] = 0;
+      if (!poisoned(c))
+        for (int r = 0; r < W; ++r) st_release_sys(seg_ready(c.bufs[r], slot, c.rank), seq);
+      c.state[kStSegSubmit] = seq;
+      __threadfence();
+    }
+  }
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) seg_wait_kernel(ArCtx c, const uint4* __restrict__ local,
+                                                              uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t seq = *reinterpret_cast<volatile uint32_t*>(c.state + kStSegWait) + 1u;
+  const int slot = seq % kSegSlots;
+  if (threadIdx.x == 0) s_ok = true;
+  __syncthreads();
+  if (!poisoned(c)) {
+    if (threadIdx.x < W) {
+      const int r = threadIdx.x;
+      if (!wait_flag_geq(seg_ready(c.bufs[c.rank], slot, r), seq, c.timeout_ns)) {
+        record_error(c, kErrSegWait, blockIdx.x, r, 11, seq);
+        s_ok = false;
+      }
+    }
+    __syncthreads();
+    if (s_ok) {
+      const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+      for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+        float acc[Pack<T>::N] = {};
+#pragma unroll
+        for (int r = 0; r < W; ++r) {
+          // own contribution comes from the caller's local tensor (identical bits)
+          const uint4 v = (r == c.rank) ? ld_nc_v4(local + i) : ld_cg_v4(seg_data(c, c.bufs[c.rank], slot, r) + i * 16);
+          unpack_add<T>(v, acc);
+        }
+        out[i] = pack_from<T>(acc);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    const uint32_t prev = atomicAdd(c.state + kStSegWaitDone, 1u);
+    if (prev == gridDim.x - 1) {
+      c.state[kStSegWaitDone] = 0;
+      c.state[kStSegWait] = seq;
+      // free the slot for every pusher
+      if (!poisoned(c))
+        for (int r = 0; r < W; ++r) st_release_sys(seg_free(c.bufs[r], slot, c.rank), seq);
+      __threadfence();
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// All-gather (one-shot push): out[r] = in of rank r, for every rank r. Used
+// by the vocab-parallel argmax combine and the sequence-parallel paths.
+// --------------------------------------------------------------------------
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                  uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t epoch = call_epoch(c);
+  if (!poisoned(c)) {
+    const uint64_t slot = c.half_bytes / W;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (uint64_t i = i0; i < nvec; i += stride) {
+      const uint4 v = ld_nc_v4(in + i);
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int r = (c.rank + j) % W;
+        st_v4(data_half(c.bufs[r], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
+      }
+    }
+    if (block_barrier(c, 0, epoch, &s_ok)) {
+      const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+      for (uint64_t i = i0; i < nvec; i += stride) {
+#pragma unroll
+        for (int r = 0; r < W; ++r) out[r * nvec + i] = ld_cg_v4(mine + r * slot + i * 16);
+      }
+    }
+  }
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
+// Raw peer-store bench kernel (16-byte stores, capped grid): same role as the
+// reference's push microbench (sglang/mailbox_ar_ext.cu:201-221).
+// --------------------------------------------------------------------------
+__global__ void push_raw_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, uint64_t nvec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride)
+    st_v4(dst + i, ld_nc_v4(src + i));
+}
+
+// ==========================================================================
+// Host side
+// ==========================================================================
+#define MBX_DISPATCH_W(W_, ...)                   \
+  switch (W_) {                                   \
+    case 2: { constexpr int W = 2; __VA_ARGS__; } break; \
+    case 4: { constexpr int W = 4; __VA_ARGS__; } break; \
+    case 8: { constexpr int W = 8; __VA_ARGS__; } break; \
+    case 3: { constexpr int W = 3; __VA_ARGS__; } break; \
+    case 5: { constexpr int W = 5; __VA_ARGS__; } break; \
+    case 6: { constexpr int W = 6; __VA_ARGS__; } break; \
+    case 7: { constexpr int W = 7; __VA_ARGS__; } break; \
+    default: throw std::runtime_error("allreduce: unsupported world size " + std::to_string(W_)); \
+  }
+
+#define MBX_DISPATCH_T(D_, ...)                                  \
+  switch (D_) {                                                  \
+    case kF32: { using T = float; __VA_ARGS__; } break;          \
+    case kF16: { using T = __half; __VA_ARGS__; } break;         \
+    case kBF16: { using T = __nv_bfloat16; __VA_ARGS__; } break; \
+    default: throw std::runtime_error("allreduce: unsupported dtype id"); \
+  }
+
+static inline int ar_grid(uint64_t work_vec, int max_blocks) {
+  uint64_t g = (work_vec + kArThreads - 1) / kArThreads;
+  if (g < 1) g = 1;
+  if (g > (uint64_t)max_blocks) g = max_blocks;
+  if (g > (uint64_t)kMaxBlocks) g = kMaxBlocks;
+  return (int)g;
+}
+
+// Largest message (bytes) one launch of `algo` can carry through the buffer.
+uint64_t ar_chunk_limit(const ArCtx& c, int algo) {
+  switch (algo) {
+    case kOneShotPush: return (c.half_bytes / c.world) & ~uint64_t(15);
+    case kOneShotPull: return c.half_bytes & ~uint64_t(15);
+    case kTwoShot:
+    case kNvls: return (c.half_bytes / 2) & ~uint64_t(15);
+  }
+  return 0;
+}
+
+void ar_launch(const ArCtx& c, int algo, int dtype, const void* in, void* out, uint64_t nbytes,
+               int max_blocks, cudaStream_t stream) {
+  if (nbytes % 16 != 0) throw std::runtime_error("allreduce: byte size must be a multiple of 16");
+  if (algo == kNvls && c.mc == nullptr) throw std::runtime_error("allreduce: NVLS requested without multicast");
+  const uint64_t limit = ar_chunk_limit(c, algo);
+  if (limit == 0) throw std::runtime_error("allreduce: bad algorithm id");
+  const char* ip = static_cast<const char*>(in);
+  char* op = static_cast<char*>(out);
+  for (uint64_t off = 0; off < nbytes || (nbytes == 0 && off == 0); off += limit) {
+    const uint64_t cur = std::min(limit, nbytes - off);
+    const uint64_t nvec = cur / 16;
+    const uint4* i4 = reinterpret_cast<const uint4*>(ip + off);
+    uint4* o4 = reinterpret_cast<uint4*>(op + off);
+    const int W_ = c.world;
+    if (algo == kOneShotPush || algo == kOneShotPull) {
+      const int g = ar_grid(nvec, max_blocks);
+      MBX_DISPATCH_T(dtype, MBX_DISPATCH_W(W_, {
+        if (algo == kOneShotPush) ar_oneshot_push_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+        else ar_oneshot_pull_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+      }));
+    } else {
+      const int g = ar_grid((nvec + W_ - 1) / W_, max_blocks);
+      MBX_DISPATCH_T(dtype, MBX_DISPATCH_W(W_, {
+        if (algo == kTwoShot) ar_twoshot_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+        else ar_nvls_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+      }));
+    }
+    MBX_CUDA_CHECK(cudaGetLastError());
+    if (nbytes == 0) break;
+  }
+}
+
+void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual, const void* weight, void* out,
+                       int M, int H, float eps, int max_blocks, cudaStream_t stream) {
+  if (H % 8 != 0) throw std::runtime_error("ar_rmsnorm: hidden size must be a multiple of 8");
+  const uint64_t bytes = (uint64_t)M * H * 2;
+  const int g = std::max(1, std::min(M, std::min(max_blocks, (int)kMaxBlocks)));
+  const int W_ = c.world;
+  auto i4 = static_cast<const uint4*>(in);
+  auto r4 = static_cast<uint4*>(residual);
+  auto w4 = static_cast<const uint4*>(weight);
+  auto o4 = static_cast<uint4*>(out);
+  if (algo == kOneShotPush) {
+    if (bytes > ar_chunk_limit(c, kOneShotPush)) throw std::runtime_error("ar_rmsnorm: message exceeds one-shot slot");
+    MBX_DISPATCH_W(W_, ar_rmsnorm_oneshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+  } else {
+    if (bytes > ar_chunk_limit(c, kTwoShot)) throw std::runtime_error("ar_rmsnorm: message exceeds two-shot slot");
+    MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+  }
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nbytes, int max_blocks,
+                         cudaStream_t stream) {
+  if (nbytes % 16 != 0) throw std::runtime_error("allgather: byte size must be a multiple of 16");
+  if (nbytes > ar_chunk_limit(c, kOneShotPush)) throw std::runtime_error("allgather: message exceeds slot");
+  const uint64_t nvec = nbytes / 16;
+  const int g = ar_grid(nvec, max_blocks);
+  const int W_ = c.world;
+  MBX_DISPATCH_W(W_, ar_allgather_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(in),
+                                                                           static_cast<uint4*>(out), nvec));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream) {
+  if (nbytes % 16 != 0 || nbytes > c.seg_slot_bytes)
+    throw std::runtime_error("submit_seg: segment must be a multiple of 16 bytes and <= slot size " +
+                             std::to_string(c.seg_slot_bytes));
+  const uint64_t nvec = nbytes / 16;
+  const int g = ar_grid(nvec, max_blocks);
+  const int W_ = c.world;
+  MBX_DISPATCH_W(W_, seg_submit_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(in), nvec));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, uint64_t nbytes, int max_blocks,
+                     cudaStream_t stream) {
+  if (nbytes % 16 != 0 || nbytes > c.seg_slot_bytes)
+    throw std::runtime_error("wait_seg: bad segment size");
+  const uint64_t nvec = nbytes / 16;
+  const int g = ar_grid(nvec, max_blocks);
+  const int W_ = c.world;
+  MBX_DISPATCH_T(dtype, MBX_DISPATCH_W(W_, seg_wait_kernel<T, W><<<g, kArThreads, 0, stream>>>(
+                                              c, static_cast<const uint4*>(local), static_cast<uint4*>(out), nvec)));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void push_raw_launch(void* dst, const void* src, uint64_t nbytes, int grid_cap, cudaStream_t stream) {
+  if (nbytes % 16 != 0) throw std::runtime_error("push_raw: bytes must be a multiple of 16");
+  const uint64_t nvec = nbytes / 16;
+  uint64_t g = (nvec + 255) / 256;
+  if (g < 1) g = 1;
+  if (g > 65535) g = 65535;
+  if (grid_cap > 0 && g > (uint64_t)grid_cap) g = grid_cap;
+  push_raw_kernel<<<(unsigned)g, 256, 0, stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), nvec);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace mbx

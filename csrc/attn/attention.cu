@@ -1,0 +1,504 @@
+// Paged attention for the served decoder (head_dim 128, bf16, GQA).
+//
+//  * prefill_attention: causal, chunked prefill over a ragged batch. Each
+//    (q-tile of 64 tokens, q-head) block streams the request's keys/values
+//    from the paged cache (page 16, layout [blocks, kv_heads, 16, 128]) in
+//    64-key tiles with cp.async double buffering, computes S = QK^T and
+//    O += PV with m16n8k16 bf16 tensor-core MMAs and an online softmax in
+//    fp32 (exp2 domain). Query i of a request with kv_len L and q_len Lq sits
+//    at position L - Lq + i and attends keys 0..that position.
+//  * decode_attention: one query per request; the request's keys are split
+//    across blocks (split-KV) for parallelism at small batch, each split
+//    writes a normalised partial output and its log-sum-exp, and a combine
+//    kernel merges the splits (LSE-weighted). A single split writes the
+//    output directly.
+// The reference has no attention code (sglang provides it,
+// docs/performance.md:3-5; prefix cache noted in tests/pp_bench.py:1-2).
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "../common.cuh"
+#include "../kernels.h"
+
+namespace mbx {
+namespace {
+
+constexpr int D = 128;
+constexpr int BQ = 64;
+constexpr int BKV = 64;
+constexpr int PAGE = 16;
+constexpr int kAttnThreads = 128;
+
+MBX_DEVICE uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Swizzled [rows][128] bf16 tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
+MBX_DEVICE uint32_t swz(int row, int chunk) { return row * 256 + ((chunk ^ (row & 7)) << 4); }
+
+MBX_DEVICE void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+MBX_DEVICE void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+MBX_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MBX_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+MBX_DEVICE void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+MBX_DEVICE void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+MBX_DEVICE void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+MBX_DEVICE uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct PrefillArgs {
+  const __nv_bfloat16* q;   // [T, nq, D]
+  const __nv_bfloat16* kc;  // [blocks, nkv, PAGE, D]
+  const __nv_bfloat16* vc;
+  __nv_bfloat16* o;         // [T, nq, D]
+  const int* cu_q;          // [R+1]
+  const int* kv_len;        // [R]
+  const int* block_table;   // [R, max_blocks]
+  const int2* tiles;        // [num_tiles] (request, q offset within request)
+  int max_blocks;
+  int nq, nkv;
+  float scale_log2;         // softmax scale * log2(e)
+};
+
+// Load a 64-key K or V tile (keys kv0..kv0+63 of request r, kv head h) into a
+// swizzled smem tile; keys >= kv_end are zero-filled.
+MBX_DEVICE void load_kv_tile(uint32_t dst, const __nv_bfloat16* cache, const int* bt, int nkv, int h, int kv0,
+                             int kv_end) {
+  // 64 keys x 16 chunks = 1024 16-byte copies, 8 per thread
+#pragma unroll
+  for (int i = 0; i < (BKV * 16) / kAttnThreads; ++i) {
+    const int idx = threadIdx.x + i * kAttnThreads;
+    const int row = idx >> 4, chunk = idx & 15;
+    const int key = kv0 + row;
+    const bool valid = key < kv_end;
+    const int kk = valid ? key : 0;
+    const int blk = bt[kk / PAGE];
+    const __nv_bfloat16* src = cache + (((int64_t)blk * nkv + h) * PAGE + (kk % PAGE)) * D + chunk * 8;
+    cp_async16_zfill(dst + swz(row, chunk), src, valid);
+  }
+}
+
+__global__ void __launch_bounds__(kAttnThreads) prefill_attention_kernel(PrefillArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  // [Q 64x128][K0][V0][K1][V1], each 16 KB
+  const uint32_t sQ = smem_addr(smem);
+  const uint32_t sK[2] = {sQ + 16384, sQ + 16384 * 3};
+  const uint32_t sV[2] = {sQ + 16384 * 2, sQ + 16384 * 4};
+
+  const int2 tile = a.tiles[blockIdx.x];
+  const int r = tile.x, qoff = tile.y;
+  const int head = blockIdx.y;
+  const int kvh = head / (a.nq / a.nkv);
+  const int q_begin = a.cu_q[r], q_len = a.cu_q[r + 1] - q_begin;
+  const int L = a.kv_len[r];
+  const int pos0 = L - q_len;  // position of the request's first query
+  const int* bt = a.block_table + (int64_t)r * a.max_blocks;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+
+  // Q tile -> smem (rows beyond q_len zero-filled)
+  const int rows_here = min(BQ, q_len - qoff);
+#pragma unroll
+  for (int i = 0; i < (BQ * 16) / kAttnThreads; ++i) {
+    const int idx = threadIdx.x + i * kAttnThreads;
+    const int row = idx >> 4, chunk = idx & 15;
+    const bool valid = row < rows_here;
+    const __nv_bfloat16* src = a.q + ((int64_t)(q_begin + qoff + (valid ? row : 0)) * a.nq + head) * D + chunk * 8;
+    cp_async16_zfill(sQ + swz(row, chunk), src, valid);
+  }
+  // causal bound: last query position in this tile
+  const int last_pos = pos0 + qoff + rows_here - 1;
+  const int kv_end = min(L, last_pos + 1);
+  const int n_tiles = (kv_end + BKV - 1) / BKV;
+  if (n_tiles > 0) {
+    load_kv_tile(sK[0], a.kc, bt, a.nkv, kvh, 0, kv_end);
+    load_kv_tile(sV[0], a.vc, bt, a.nkv, kvh, 0, kv_end);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // Q fragments for this warp's 16 rows, 8 k-steps.
+  uint32_t qf[8][4];
+  {
+    const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int chunk = ks * 2 + (lane >> 4);
+      ldsm_x4(sQ + swz(row, chunk), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    }
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  const int qpos_r0 = pos0 + qoff + warp * 16 + g;  // rows g and g+8
+  const int qpos_r1 = qpos_r0 + 8;
+
+  for (int it = 0; it < n_tiles; ++it) {
+    const int buf = it & 1;
+    if (it + 1 < n_tiles) {
+      load_kv_tile(sK[buf ^ 1], a.kc, bt, a.nkv, kvh, (it + 1) * BKV, kv_end);
+      load_kv_tile(sV[buf ^ 1], a.vc, bt, a.nkv, kvh, (it + 1) * BKV, kv_end);
+    }
+    cp_async_commit();
+
+    // S = Q K^T : 16 x 64 per warp (8 n-tiles)
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int jn = 0; jn < 4; ++jn) {  // pairs of key n-tiles
+        const int key = jn * 16 + (lane & 7) + 8 * (lane >> 4);
+        const int chunk = ks * 2 + ((lane >> 3) & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(sK[buf] + swz(key, chunk), b0, b1, b2, b3);
+        mma16816(s[2 * jn], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+        mma16816(s[2 * jn + 1], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b2, b3);
+      }
+    }
+    // mask + online softmax
+    const int kv0 = it * BKV;
+    const bool need_mask = (kv0 + BKV > kv_end) || (kv0 + BKV - 1 > pos0 + qoff + warp * 16);
+    float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = s[j][e] * a.scale_log2;
+        if (need_mask) {
+          const int key = kv0 + j * 8 + 2 * t4 + (e & 1);
+          const int qp = (e < 2) ? qpos_r0 : qpos_r1;
+          if (key > qp || key >= kv_end) v = -INFINITY;
+        }
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    }
+    float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float mnew = mx[h];
+      corr[h] = (mnew == -INFINITY) ? 1.f : exp2f(m_r[h] - mnew);
+      m_r[h] = mnew;
+    }
+    uint32_t pf[4][4];  // P as A fragments, 4 k-steps of 16 keys
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mm = m_r[e >> 1];
+        p[e] = (mm == -INFINITY) ? 0.f : exp2f(s[j][e] - mm);
+        rs[e >> 1] += p[e];
+      }
+      const int kstep = j >> 1, hi = j & 1;
+      pf[kstep][hi * 2 + 0] = pack_bf16(p[0], p[1]);
+      pf[kstep][hi * 2 + 1] = pack_bf16(p[2], p[3]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      l_r[h] = l_r[h] * corr[h] + rs[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= corr[0];
+      o[j][1] *= corr[0];
+      o[j][2] *= corr[1];
+      o[j][3] *= corr[1];
+    }
+    // O += P V : for each 16-key k-step, 16 dim n-tiles (8 ldmatrix.x4.trans)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      // A-fragment register order: a0 (row g, k lo), a1 (row g+8, k lo), a2 (row g, k hi), a3 (row g+8, k hi)
+      const uint32_t a0 = pf[ks][0], a1 = pf[ks][1], a2 = pf[ks][2], a3 = pf[ks][3];
+#pragma unroll
+      for (int jn = 0; jn < 8; ++jn) {
+        const int key = ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const int chunk = jn * 2 + (lane >> 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(sV[buf] + swz(key, chunk), b0, b1, b2, b3);
+        mma16816(o[2 * jn], a0, a1, a2, a3, b0, b1);
+        mma16816(o[2 * jn + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+  }
+
+  // normalise and store
+  const float inv0 = l_r[0] > 0.f ? 1.f / l_r[0] : 0.f;
+  const float inv1 = l_r[1] > 0.f ? 1.f / l_r[1] : 0.f;
+  const int row0 = warp * 16 + g, row1 = row0 + 8;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int col = j * 8 + 2 * t4;
+    if (row0 < rows_here) {
+      __nv_bfloat16* dst = a.o + ((int64_t)(q_begin + qoff + row0) * a.nq + head) * D + col;
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16(o[j][0] * inv0, o[j][1] * inv0);
+    }
+    if (row1 < rows_here) {
+      __nv_bfloat16* dst = a.o + ((int64_t)(q_begin + qoff + row1) * a.nq + head) * D + col;
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16(o[j][2] * inv1, o[j][3] * inv1);
+    }
+  }
+}
+
+// ------------------------------------------------------------------- decode
+struct DecodeArgs {
+  const __nv_bfloat16* q;   // [B, nq, D]
+  const __nv_bfloat16* kc;
+  const __nv_bfloat16* vc;
+  __nv_bfloat16* o;         // [B, nq, D]
+  float* part_o;            // [B, nq, splits, D] (splits > 1)
+  float* part_lse;          // [B, nq, splits]
+  const int* kv_len;        // [B]
+  const int* block_table;   // [B, max_blocks]
+  int max_blocks, nq, nkv, splits;
+  float scale_log2;
+};
+
+constexpr int kDecThreads = 128;
+constexpr int kMaxG = 8;
+
+__global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(DecodeArgs a) {
+  __shared__ float sq[kMaxG][D];
+  __shared__ float sp[kMaxG][kDecThreads];
+  __shared__ float sred[kMaxG][4];
+  __shared__ float so[kMaxG][2][D];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = a.nq / a.nkv;
+  const int L = a.kv_len[b];
+  const int chunk = ((L + a.splits - 1) / a.splits + PAGE - 1) / PAGE * PAGE;
+  const int k_begin = split * chunk, k_end = min(L, k_begin + chunk);
+  const int* bt = a.block_table + (int64_t)b * a.max_blocks;
+  const int t = threadIdx.x;
+  for (int i = t; i < G * D; i += kDecThreads) {
+    const int h = i / D, d = i % D;
+    sq[h][d] = __bfloat162float(a.q[((int64_t)b * a.nq + kvh * G + h) * D + d]) * a.scale_log2;
+  }
+  __syncthreads();
+  float m[kMaxG], l[kMaxG], acc[kMaxG][2];
+#pragma unroll
+  for (int h = 0; h < kMaxG; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+    acc[h][0] = acc[h][1] = 0.f;
+  }
+  const int dp = t & 63, kpar = t >> 6;
+  for (int k0 = k_begin; k0 < k_end; k0 += kDecThreads) {
+    // scores: thread t <-> key k0 + t
+    const int key = k0 + t;
+    float sc[kMaxG];
+#pragma unroll
+    for (int h = 0; h < kMaxG; ++h) sc[h] = -INFINITY;
+    if (key < k_end) {
+      const int blk = bt[key / PAGE];
+      const uint4* kr = reinterpret_cast<const uint4*>(a.kc + (((int64_t)blk * a.nkv + kvh) * PAGE + key % PAGE) * D);
+#pragma unroll
+      for (int h = 0; h < kMaxG; ++h) sc[h] = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < 16; ++c) {
+        float kv[8] = {};
+        unpack_add<__nv_bfloat16>(kr[c], kv);
+#pragma unroll
+        for (int h = 0; h < kMaxG; ++h) {
+          if (h < G) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sc[h] += sq[h][c * 8 + j] * kv[j];
+          }
+        }
+      }
+    }
+    // per-head max over the 128 keys
+#pragma unroll
+    for (int h = 0; h < kMaxG; ++h) {
+      if (h >= G) break;
+      float v = sc[h];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if ((t & 31) == 0) sred[h][t >> 5] = v;
+    }
+    __syncthreads();
+    float mnew[kMaxG];
+#pragma unroll
+    for (int h = 0; h < kMaxG; ++h) {
+      mnew[h] = m[h];
+      if (h < G) mnew[h] = fmaxf(fmaxf(fmaxf(sred[h][0], sred[h][1]), fmaxf(sred[h][2], sred[h][3])), m[h]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < kMaxG; ++h) {
+      if (h >= G) break;
+      const float p = (sc[h] == -INFINITY) ? 0.f : exp2f(sc[h] - mnew[h]);
+      sp[h][t] = p;
+      float v = p;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if ((t & 31) == 0) sred[h][t >> 5] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < kMaxG; ++h) {
+      if (h >= G) break;
+      const float corr = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mnew[h]);
+      l[h] = l[h] * corr + (sred[h][0] + sred[h][1] + sred[h][2] + sred[h][3]);
+      acc[h][0] *= corr;
+      acc[h][1] *= corr;
+      m[h] = mnew[h];
+    }
+    // PV: thread (dp, kpar) accumulates dims 2dp, 2dp+1 over keys of parity kpar
+    const int nk = min(kDecThreads, k_end - k0);
+    for (int j = kpar; j < nk; j += 2) {
+      const int key2 = k0 + j;
+      const int blk = bt[key2 / PAGE];
+      const __nv_bfloat162 vv = *reinterpret_cast<const __nv_bfloat162*>(
+          a.vc + (((int64_t)blk * a.nkv + kvh) * PAGE + key2 % PAGE) * D + 2 * dp);
+      const float2 vf = __bfloat1622float2(vv);
+#pragma unroll
+      for (int h = 0; h < kMaxG; ++h) {
+        if (h < G) {
+          acc[h][0] += sp[h][j] * vf.x;
+          acc[h][1] += sp[h][j] * vf.y;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // combine key parities
+#pragma unroll
+  for (int h = 0; h < kMaxG; ++h) {
+    if (h < G) {
+      so[h][kpar][2 * dp] = acc[h][0];
+      so[h][kpar][2 * dp + 1] = acc[h][1];
+    }
+  }
+  __syncthreads();
+  for (int i = t; i < G * D; i += kDecThreads) {
+    const int h = i / D, d = i % D;
+    const float v = so[h][0][d] + so[h][1][d];
+    const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
+    const int qh = kvh * G + h;
+    if (a.splits == 1) {
+      a.o[((int64_t)b * a.nq + qh) * D + d] = __float2bfloat16(v * inv);
+    } else {
+      a.part_o[(((int64_t)b * a.nq + qh) * a.splits + split) * D + d] = v * inv;
+      if (d == 0)
+        a.part_lse[((int64_t)b * a.nq + qh) * a.splits + split] = (l[h] > 0.f) ? m[h] + log2f(l[h]) : -INFINITY;
+    }
+  }
+}
+
+__global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
+                                      __nv_bfloat16* __restrict__ o) {
+  // one block per (b, head), D threads
+  const int64_t bh = blockIdx.x;
+  const float* lse = part_lse + bh * splits;
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, lse[s]);
+  float den = 0.f, num = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float w = (lse[s] == -INFINITY) ? 0.f : exp2f(lse[s] - mx);
+    den += w;
+    num += w * part_o[(bh * splits + s) * D + threadIdx.x];
+  }
+  o[bh * D + threadIdx.x] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+}
+
+}  // namespace
+
+void prefill_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
+                              const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
+                              int n_tiles, int nq, int nkv, float scale, cudaStream_t s) {
+  if (n_tiles == 0) return;
+  if (nq % nkv != 0) throw std::runtime_error("attention: nq must be a multiple of nkv");
+  PrefillArgs a;
+  a.q = (const __nv_bfloat16*)q;
+  a.kc = (const __nv_bfloat16*)kc;
+  a.vc = (const __nv_bfloat16*)vc;
+  a.o = (__nv_bfloat16*)o;
+  a.cu_q = cu_q;
+  a.kv_len = kv_len;
+  a.block_table = block_table;
+  a.tiles = reinterpret_cast<const int2*>(tiles);
+  a.max_blocks = max_blocks;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  const int smem = 5 * 16384;
+  static bool attr = false;
+  if (!attr) {
+    MBX_CUDA_CHECK(cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  dim3 grid(n_tiles, nq);
+  prefill_attention_kernel<<<grid, kAttnThreads, smem, s>>>(a);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
+                             const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
+                             float* part_o, float* part_lse, float scale, cudaStream_t s) {
+  if (B == 0) return;
+  if (nq % nkv != 0 || nq / nkv > kMaxG) throw std::runtime_error("decode: group size must be <= 8");
+  DecodeArgs a;
+  a.q = (const __nv_bfloat16*)q;
+  a.kc = (const __nv_bfloat16*)kc;
+  a.vc = (const __nv_bfloat16*)vc;
+  a.o = (__nv_bfloat16*)o;
+  a.kv_len = kv_len;
+  a.block_table = block_table;
+  a.max_blocks = max_blocks;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.splits = std::max(1, splits);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  if (a.splits > 1 && (!part_o || !part_lse)) throw std::runtime_error("decode: split-KV needs scratch buffers");
+  dim3 grid(a.splits, nkv, B);
+  decode_attention_kernel<<<grid, kDecThreads, 0, s>>>(a);
+  MBX_CUDA_CHECK(cudaGetLastError());
+  if (a.splits > 1) {
+    decode_combine_kernel<<<B * nq, D, 0, s>>>(a.part_o, a.part_lse, a.splits, a.o);
+    MBX_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+}  // namespace mbx

@@ -1,0 +1,344 @@
+// Python bindings of the CUDA extension (_C): tensor checks and plumbing for
+// every sm_100a kernel (launchers declared in kernels.h), the symmetric-memory
+// API and the allreduce communicator core. Compiled by the host compiler only.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cstring>
+
+#include "kernels.h"
+#include "symm/symm.h"
+
+namespace py = pybind11;
+
+namespace mbx {
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+cudaStream_t stream_of(int64_t s) { return s == 0 ? cur_stream() : reinterpret_cast<cudaStream_t>(s); }
+
+void check_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+void check_bf16(const torch::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bf16");
+}
+
+// Fixed-address launch context of one communicator (all pointers are mapped
+// once, so CUDA-graph replays of any launch below stay valid).
+class ArComm {
+ public:
+  ArComm(int rank, int world, std::vector<int64_t> bufs, int64_t mc, int64_t state, int64_t status_dev,
+         int64_t status_host, uint64_t half_bytes, uint64_t seg_slot_bytes, uint64_t timeout_ns)
+      : status_host_(reinterpret_cast<volatile uint32_t*>(status_host)) {
+    TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)bufs.size() == world, "ArComm: bad world size");
+    std::memset(&c_, 0, sizeof(c_));
+    for (int i = 0; i < world; ++i) c_.bufs[i] = reinterpret_cast<char*>(bufs[i]);
+    c_.mc = reinterpret_cast<char*>(mc);
+    c_.state = reinterpret_cast<uint32_t*>(state);
+    c_.status = reinterpret_cast<uint32_t*>(status_dev);
+    c_.timeout_ns = timeout_ns;
+    c_.half_bytes = half_bytes;
+    c_.seg_slot_bytes = seg_slot_bytes;
+    c_.rank = rank;
+    c_.world = world;
+  }
+  void allreduce(int64_t in, int64_t out, uint64_t nbytes, int dtype, int algo, int max_blocks, int64_t stream) {
+    ar_launch(c_, algo, dtype, reinterpret_cast<const void*>(in), reinterpret_cast<void*>(out), nbytes, max_blocks,
+              stream_of(stream));
+  }
+  void ar_rmsnorm(int64_t in, int64_t residual, int64_t weight, int64_t out, int M, int H, double eps, int algo,
+                  int max_blocks, int64_t stream) {
+    ar_rmsnorm_launch(c_, algo, reinterpret_cast<const void*>(in), reinterpret_cast<void*>(residual),
+                      reinterpret_cast<const void*>(weight), reinterpret_cast<void*>(out), M, H, (float)eps,
+                      max_blocks, stream_of(stream));
+  }
+  void allgather(int64_t in, int64_t out, uint64_t nbytes, int max_blocks, int64_t stream) {
+    ar_allgather_launch(c_, reinterpret_cast<const void*>(in), reinterpret_cast<void*>(out), nbytes, max_blocks,
+                        stream_of(stream));
+  }
+  void seg_submit(int64_t in, uint64_t nbytes, int max_blocks, int64_t stream) {
+    seg_submit_launch(c_, reinterpret_cast<const void*>(in), nbytes, max_blocks, stream_of(stream));
+  }
+  void seg_wait(int64_t local, int64_t out, uint64_t nbytes, int dtype, int max_blocks, int64_t stream) {
+    seg_wait_launch(c_, dtype, reinterpret_cast<const void*>(local), reinterpret_cast<void*>(out), nbytes, max_blocks,
+                    stream_of(stream));
+  }
+  uint64_t chunk_limit(int algo) const { return ar_chunk_limit(c_, algo); }
+  std::vector<int64_t> status() const {
+    std::vector<int64_t> v(kStatusWords);
+    for (int i = 0; i < kStatusWords; ++i) v[i] = status_host_[i];
+    return v;
+  }
+  int64_t error() const { return status_host_[kStatusErr]; }
+  void clear_status() {
+    for (int i = 0; i < kStatusWords; ++i) status_host_[i] = 0;
+  }
+  bool has_multicast() const { return c_.mc != nullptr; }
+
+ private:
+  ArCtx c_;
+  volatile uint32_t* status_host_;
+};
+
+// ---------------------------------------------------------------- ops
+void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor out, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  const int H = x.size(-1);
+  TORCH_CHECK(w.numel() == H && out.numel() == x.numel(), "rmsnorm: shape mismatch");
+  rmsnorm_launch(x.data_ptr(), nullptr, w.data_ptr(), out.data_ptr(), x.numel() / H, H, (float)eps, cur_stream());
+}
+
+void fused_add_rmsnorm(torch::Tensor x, torch::Tensor residual, torch::Tensor w, torch::Tensor out, double eps) {
+  check_bf16(x, "x");
+  check_bf16(residual, "residual");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  const int H = x.size(-1);
+  TORCH_CHECK(w.numel() == H && residual.numel() == x.numel() && out.numel() == x.numel(),
+              "fused_add_rmsnorm: shape mismatch");
+  rmsnorm_launch(x.data_ptr(), residual.data_ptr(), w.data_ptr(), out.data_ptr(), x.numel() / H, H, (float)eps,
+                 cur_stream());
+}
+
+void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
+                    c10::optional<torch::Tensor> slots, torch::Tensor q_out, c10::optional<torch::Tensor> k_cache,
+                    c10::optional<torch::Tensor> v_cache, int64_t nq, int64_t nkv, int64_t page) {
+  check_bf16(qkv, "qkv");
+  check_bf16(q_out, "q_out");
+  check_cuda(positions, "positions");
+  check_cuda(cos_sin, "cos_sin");
+  TORCH_CHECK(positions.scalar_type() == torch::kInt32, "positions must be int32");
+  TORCH_CHECK(cos_sin.scalar_type() == torch::kFloat32 && cos_sin.dim() == 2 && cos_sin.size(1) == 128,
+              "cos_sin must be fp32 [P, 128]");
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(qkv.size(1) == (nq + 2 * nkv) * 128, "qkv width mismatch (head_dim must be 128)");
+  TORCH_CHECK(positions.numel() == T && q_out.numel() == T * nq * 128, "rope: shape mismatch");
+  const int64_t* sp = nullptr;
+  void *kc = nullptr, *vc = nullptr;
+  if (slots.has_value()) {
+    check_cuda(*slots, "slots");
+    TORCH_CHECK(slots->scalar_type() == torch::kInt64 && slots->numel() == T, "slots must be int64 [T]");
+    TORCH_CHECK(k_cache.has_value() && v_cache.has_value(), "caches required with slots");
+    check_bf16(*k_cache, "k_cache");
+    check_bf16(*v_cache, "v_cache");
+    TORCH_CHECK(k_cache->dim() == 4 && k_cache->size(1) == nkv && k_cache->size(2) == page && k_cache->size(3) == 128,
+                "k_cache must be [blocks, nkv, page, 128]");
+    sp = slots->data_ptr<int64_t>();
+    kc = k_cache->data_ptr();
+    vc = v_cache->data_ptr();
+  }
+  rope_and_cache_launch(qkv.data_ptr(), positions.data_ptr<int>(), cos_sin.data_ptr<float>(), sp, q_out.data_ptr(), kc,
+                        vc, T, (int)nq, (int)nkv, (int)page, cur_stream());
+}
+
+void silu_mul(torch::Tensor x, torch::Tensor out) {
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  const int I2 = x.size(-1);
+  TORCH_CHECK(out.numel() * 2 == x.numel(), "silu_mul: shape mismatch");
+  silu_mul_launch(x.data_ptr(), out.data_ptr(), x.numel() / I2, I2, cur_stream());
+}
+
+void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t start) {
+  check_bf16(table, "table");
+  check_bf16(out, "out");
+  check_cuda(ids, "ids");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32, "ids must be int32");
+  TORCH_CHECK(out.numel() == ids.numel() * table.size(1), "embedding: shape mismatch");
+  embedding_launch(ids.data_ptr<int>(), table.data_ptr(), out.data_ptr(), ids.numel(), table.size(1), start,
+                   table.size(0), cur_stream());
+}
+
+void argmax(torch::Tensor logits, int64_t offset, torch::Tensor best_val, torch::Tensor best_idx) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "argmax: logits [B, V] row-major");
+  TORCH_CHECK(logits.scalar_type() == torch::kBFloat16 || logits.scalar_type() == torch::kFloat32,
+              "argmax: bf16 or fp32 logits");
+  TORCH_CHECK(best_val.scalar_type() == torch::kFloat32 && best_idx.scalar_type() == torch::kInt64 &&
+                  best_val.numel() >= logits.size(0) && best_idx.numel() >= logits.size(0),
+              "argmax: outputs must be fp32/int64 [B]");
+  argmax_launch(logits.data_ptr(), logits.scalar_type() == torch::kBFloat16, logits.stride(0), logits.size(0),
+                logits.size(1), offset, best_val.data_ptr<float>(), best_idx.data_ptr<int64_t>(), cur_stream());
+}
+
+void argmax_combine(torch::Tensor vals, torch::Tensor idxs, torch::Tensor out) {
+  check_cuda(vals, "vals");
+  check_cuda(idxs, "idxs");
+  TORCH_CHECK(vals.dim() == 2 && idxs.sizes() == vals.sizes() && vals.scalar_type() == torch::kFloat32 &&
+                  idxs.scalar_type() == torch::kInt64,
+              "argmax_combine: fp32/int64 [W, B]");
+  argmax_combine_launch(vals.data_ptr<float>(), idxs.data_ptr<int64_t>(), vals.size(0), vals.size(1),
+                        out.data_ptr<int64_t>(), cur_stream());
+}
+
+void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, c10::optional<torch::Tensor> residual,
+          c10::optional<torch::Tensor> workspace, torch::Tensor err, int64_t bn, int64_t splits) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == torch::kBFloat16 && B.scalar_type() == torch::kBFloat16 &&
+                  C.scalar_type() == torch::kBFloat16,
+              "gemm: bf16 operands");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D operands");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm: row-major operands");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "gemm: shape mismatch");
+  TORCH_CHECK(err.scalar_type() == torch::kInt32 && err.is_cuda(), "gemm: err must be an int32 CUDA word");
+  const void* res = nullptr;
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->scalar_type() == torch::kBFloat16 && residual->sizes() == C.sizes() &&
+                    residual->strides() == C.strides(),
+                "gemm: residual must match C");
+    res = residual->data_ptr();
+  }
+  float* ws = nullptr;
+  if (workspace.has_value()) {
+    TORCH_CHECK(workspace->scalar_type() == torch::kFloat32 && workspace->is_cuda(), "gemm: fp32 workspace");
+    const int64_t need_splits = splits > 0 ? splits : gemm_plan(M, N, K).splits;
+    TORCH_CHECK(workspace->numel() >= need_splits * M * N, "gemm: workspace too small");
+    ws = workspace->data_ptr<float>();
+  }
+  const at::cuda::CUDAGuard guard(A.device());
+  gemm_launch(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), C.data_ptr(), C.stride(0), res, M, N, K, (int)bn,
+              (int)splits, ws, reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
+}
+
+std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K) {
+  GemmPlan p = gemm_plan(M, N, K);
+  return {p.bn, p.splits};
+}
+
+void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor out,
+                       torch::Tensor cu_q, torch::Tensor kv_len, torch::Tensor block_table, torch::Tensor tiles,
+                       double scale) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_bf16(k_cache, "k_cache");
+  check_bf16(v_cache, "v_cache");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128, "q must be [T, nq, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.size(3) == 128,
+              "k_cache must be [blocks, nkv, 16, 128]");
+  for (auto* t : {&cu_q, &kv_len, &block_table, &tiles}) {
+    check_cuda(*t, "index tensor");
+    TORCH_CHECK(t->scalar_type() == torch::kInt32, "index tensors must be int32");
+  }
+  TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 2, "tiles must be [n, 2]");
+  prefill_attention_launch(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), cu_q.data_ptr<int>(),
+                           kv_len.data_ptr<int>(), block_table.data_ptr<int>(), block_table.size(1),
+                           tiles.data_ptr<int>(), tiles.size(0), q.size(1), k_cache.size(1), (float)scale,
+                           cur_stream());
+}
+
+void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor out,
+                      torch::Tensor kv_len, torch::Tensor block_table, c10::optional<torch::Tensor> part_o,
+                      c10::optional<torch::Tensor> part_lse, int64_t splits, double scale) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_bf16(k_cache, "k_cache");
+  check_bf16(v_cache, "v_cache");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128, "q must be [B, nq, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.size(3) == 128,
+              "k_cache must be [blocks, nkv, 16, 128]");
+  check_cuda(kv_len, "kv_len");
+  check_cuda(block_table, "block_table");
+  const int B = q.size(0), nq = q.size(1);
+  float *po = nullptr, *pl = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "decode: split-KV needs scratch tensors");
+    TORCH_CHECK(part_o->numel() >= (int64_t)B * nq * splits * 128 && part_lse->numel() >= (int64_t)B * nq * splits,
+                "decode: scratch too small");
+    po = part_o->data_ptr<float>();
+    pl = part_lse->data_ptr<float>();
+  }
+  decode_attention_launch(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), kv_len.data_ptr<int>(),
+                          block_table.data_ptr<int>(), block_table.size(1), B, nq, k_cache.size(1), (int)splits, po,
+                          pl, (float)scale, cur_stream());
+}
+
+}  // namespace
+}  // namespace mbx
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels: symmetric memory, allreduce, tcgen05 GEMM, attention, elementwise ops";
+  using namespace mbx;
+  m.attr("SIG_BYTES") = (int64_t)kSigBytes;
+  m.attr("MAX_RANKS") = kMaxRanks;
+  m.attr("MAX_BLOCKS") = kMaxBlocks;
+  m.attr("STATE_WORDS") = (int)kStWords;
+  m.attr("STATUS_WORDS") = (int)kStatusWords;
+  m.attr("SEG_SLOTS") = kSegSlots;
+
+  py::class_<SymmAlloc>(m, "SymmAlloc")
+      .def_readonly("id", &SymmAlloc::id)
+      .def_readonly("ptr", &SymmAlloc::ptr)
+      .def_readonly("fd", &SymmAlloc::fd);
+  py::class_<HostMapped>(m, "HostMapped").def_readonly("host", &HostMapped::host).def_readonly("dev", &HostMapped::dev);
+  m.def("symm_granularity", &symm_granularity, py::arg("device"), py::arg("multicast"), py::arg("ndev"));
+  m.def("symm_create", &symm_create, py::arg("device"), py::arg("size"));
+  m.def("symm_import", &symm_import, py::arg("device"), py::arg("fd"), py::arg("size"));
+  m.def("symm_free", &symm_free, py::arg("id"));
+  m.def("mc_supported", &mc_supported, py::arg("device"));
+  m.def("mc_create", &mc_create, py::arg("ndev"), py::arg("size"));
+  m.def("mc_import", &mc_import, py::arg("fd"), py::arg("size"));
+  m.def("mc_add_device", &mc_add_device, py::arg("mc_id"), py::arg("device"));
+  m.def("mc_bind", &mc_bind, py::arg("mc_id"), py::arg("mem_id"), py::arg("size"));
+  m.def("mc_map", &mc_map, py::arg("mc_id"), py::arg("device"), py::arg("size"));
+  m.def("mc_unbind", &mc_unbind, py::arg("mc_id"), py::arg("device"), py::arg("size"));
+  m.def("close_fd", &close_fd, py::arg("fd"));
+  m.def("ipc_get_handle", [](int64_t p) { return py::bytes(ipc_get_handle(p)); }, py::arg("ptr"));
+  m.def("ipc_open", [](py::bytes h) { return ipc_open(std::string(h)); }, py::arg("handle"));
+  m.def("ipc_close", &ipc_close, py::arg("ptr"));
+  m.def("host_mapped_alloc", &host_mapped_alloc, py::arg("bytes"));
+  m.def("host_mapped_free", &host_mapped_free, py::arg("host"));
+
+  py::class_<ArComm>(m, "ArComm")
+      .def(py::init<int, int, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, uint64_t, uint64_t, uint64_t>(),
+           py::arg("rank"), py::arg("world"), py::arg("bufs"), py::arg("mc"), py::arg("state"), py::arg("status_dev"),
+           py::arg("status_host"), py::arg("half_bytes"), py::arg("seg_slot_bytes"), py::arg("timeout_ns"))
+      .def("allreduce", &ArComm::allreduce, py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("dtype"),
+           py::arg("algo"), py::arg("max_blocks"), py::arg("stream"))
+      .def("ar_rmsnorm", &ArComm::ar_rmsnorm, py::arg("inp"), py::arg("residual"), py::arg("weight"), py::arg("out"),
+           py::arg("M"), py::arg("H"), py::arg("eps"), py::arg("algo"), py::arg("max_blocks"), py::arg("stream"))
+      .def("allgather", &ArComm::allgather, py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("max_blocks"),
+           py::arg("stream"))
+      .def("seg_submit", &ArComm::seg_submit, py::arg("inp"), py::arg("nbytes"), py::arg("max_blocks"),
+           py::arg("stream"))
+      .def("seg_wait", &ArComm::seg_wait, py::arg("local"), py::arg("out"), py::arg("nbytes"), py::arg("dtype"),
+           py::arg("max_blocks"), py::arg("stream"))
+      .def("chunk_limit", &ArComm::chunk_limit, py::arg("algo"))
+      .def("status", &ArComm::status)
+      .def("error", &ArComm::error)
+      .def("clear_status", &ArComm::clear_status)
+      .def("has_multicast", &ArComm::has_multicast);
+  m.def(
+      "push_raw",
+      [](int64_t dst, int64_t src, uint64_t nbytes, int grid_cap, int64_t stream) {
+        push_raw_launch(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes, grid_cap,
+                        stream_of(stream));
+      },
+      py::arg("dst"), py::arg("src"), py::arg("nbytes"), py::arg("grid_cap"), py::arg("stream"));
+  m.def(
+      "ce_push",
+      [](int64_t dst, int64_t src, uint64_t nbytes, int64_t stream) {
+        cudaError_t e = cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes,
+                                        cudaMemcpyDeviceToDevice, stream_of(stream));
+        TORCH_CHECK(e == cudaSuccess, "ce_push: ", cudaGetErrorString(e));
+      },
+      py::arg("dst"), py::arg("src"), py::arg("nbytes"), py::arg("stream"));
+
+  m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("residual"), py::arg("workspace"),
+        py::arg("err"), py::arg("bn") = 0, py::arg("splits") = 0);
+  m.def("gemm_plan", &gemm_plan_py, py::arg("M"), py::arg("N"), py::arg("K"));
+  m.def("rmsnorm", &rmsnorm);
+  m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
+  m.def("rope_and_cache", &rope_and_cache);
+  m.def("silu_mul", &silu_mul);
+  m.def("embedding", &embedding);
+  m.def("argmax", &argmax);
+  m.def("argmax_combine", &argmax_combine);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("decode_attention", &decode_attention);
+}

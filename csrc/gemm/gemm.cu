@@ -1,0 +1,466 @@
+// Persistent tcgen05 / TMEM GEMM for sm_100a:  C[M,N] = A[M,K] * B[N,K]^T
+// (bf16 operands, both K-major as in torch's Linear: activations [T, in],
+// weights [out, in]; fp32 accumulation in tensor memory).
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0     TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte
+//              swizzle, S-stage mbarrier ring (full/empty). No multicast.
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer (M=128,
+//              N=BN, K=16 per instruction, 4 per 64-wide k-block); commits
+//              free smem stages and signal finished accumulators.
+//   warps 2-5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), convert,
+//              store; double-buffered accumulators (2 x BN TMEM columns) so the
+//              epilogue of tile i overlaps the mainloop of tile i+1.
+// Work units = (m-block, n-block, k-split), strided over the persistent grid.
+// split_k > 1 writes fp32 partials that a reduce kernel folds (decode shapes
+// with few output tiles).
+//
+// Every mbarrier wait is bounded (%globaltimer); on timeout the CTA records an
+// error word, drains its own in-flight TMA/MMA, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+
+#include "../kernels.h"
+#include "tcgen05.cuh"
+
+namespace mbx {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+
+enum EpiMode : int { kEpiBf16 = 0, kEpiF32Partial = 1, kEpiBf16AddResidual = 2 };
+
+struct GemmArgs {
+  void* out;             // bf16 C (ldc) or fp32 partials [splits][M][N]
+  const __nv_bfloat16* residual;  // kEpiBf16AddResidual: C = acc + residual (ld = ldc)
+  int64_t ldc;
+  int M, N, K;
+  int num_m, num_n, splits, kb_per_split, kb_total;
+  uint32_t* err;
+  uint64_t timeout_ns;
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kTotal = kBarOff + 256 + 1024;  // barriers + alignment slack
+};
+
+MBX_DEVICE void set_err(uint32_t* err, uint32_t code, volatile int* abort) {
+  *abort = 1;
+  if (err) atomicCAS(err, 0u, code);
+}
+
+MBX_DEVICE void store_row_bf16(__nv_bfloat16* dst, const uint32_t (&r)[32], int ncols_valid,
+                               const __nv_bfloat16* res) {
+  // r holds 32 fp32 bit patterns of consecutive columns; write ncols_valid
+  // (multiple of 8) of them as bf16 in 16-byte packs.
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (g * 8 < ncols_valid) {
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[g * 8 + j]);
+      if (res) {
+        float rr[8] = {};
+        unpack_add<__nv_bfloat16>(*reinterpret_cast<const uint4*>(res + g * 8), rr);
+        // round the GEMM result first: same as a separate bf16 add
+        const uint4 pb = pack_from<__nv_bfloat16>(f);
+        float q[8] = {};
+        unpack_add<__nv_bfloat16>(pb, q);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = q[j] + rr[j];
+      }
+      *reinterpret_cast<uint4*>(dst + g * 8) = pack_from<__nv_bfloat16>(f);
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmArgs args) {
+  using L = Smem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled tiles.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;   // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint64_t* mma_done = tempty + 2;    // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int units = args.num_m * args.num_n * args.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], kEpiWarps);
+    }
+    tc::mbar_init(mma_done, 1);
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 2 * BN);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (tc::elect_one()) {
+      tc::tma_prefetch_desc(&tmA);
+      tc::tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+        const int m = u % args.num_m;
+        const int rest = u / args.num_m;
+        const int n = rest % args.num_n;
+        const int ks = rest / args.num_n;
+        const int kb0 = ks * args.kb_per_split;
+        const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(&empty[s], ph ^ 1, abort, args.timeout_ns)) {
+            set_err(args.err, 1, abort);
+            break;
+          }
+          uint8_t* sa = smem + s * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          tc::mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+          tc::tma_load_2d(sa, &tmA, &full[s], kb * BK, m * BM);
+          tc::tma_load_2d(sb, &tmB, &full[s], kb * BK, n * BN);
+        }
+      }
+      // Drain: wait for the last (up to STAGES) loads this thread issued.
+      const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
+      for (uint32_t j = first; j < it; ++j) {
+        volatile int never = 0;
+        tc::mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &never, 200000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (tc::elect_one()) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+      uint32_t it = 0, t = 0;
+      for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++t) {
+        const int rest = u / args.num_m;
+        const int ks = rest / args.num_n;
+        const int kb0 = ks * args.kb_per_split;
+        const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        const int acc = t & 1;
+        const uint32_t aph = (t >> 1) & 1;
+        if (!tc::mbar_wait(&tempty[acc], aph ^ 1, abort, args.timeout_ns)) {
+          set_err(args.err, 2, abort);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(&full[s], ph, abort, args.timeout_ns)) {
+            set_err(args.err, 2, abort);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = tc::smem_u32(smem + s * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+          const uint64_t da = tc::sw128_kmajor_desc(sa);
+          const uint64_t db = tc::sw128_kmajor_desc(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance 16 bf16 = 32 bytes (2 in descriptor units) along K
+            tc::mma_bf16(d, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc::mma_commit(&tfull[acc]);
+      }
+      // All issued MMAs complete before TMEM is released.
+      tc::mma_commit(mma_done);
+      volatile int never = 0;
+      tc::mbar_wait(mma_done, 0, &never, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    uint32_t t = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
+      const int m = u % args.num_m;
+      const int rest = u / args.num_m;
+      const int n = rest % args.num_n;
+      const int ks = rest / args.num_n;
+      const int acc = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[acc], aph, abort, args.timeout_ns)) {
+        if (lane == 0) set_err(args.err, 3, abort);
+        break;
+      }
+      tc::tc_fence_after();
+      const int grow = m * BM + row_in_tile;
+      const bool row_ok = grow < args.M;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, r);
+        tc::tmem_ld_wait();
+        const int gcol = n * BN + c0;
+        const int valid = min(32, args.N - gcol);
+        if (row_ok && valid > 0) {
+          if (EPI == kEpiF32Partial) {
+            float* dst = static_cast<float*>(args.out) + ((int64_t)ks * args.M + grow) * args.N + gcol;
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              if (g * 4 < valid)
+                *reinterpret_cast<uint4*>(dst + g * 4) = make_uint4(r[g * 4], r[g * 4 + 1], r[g * 4 + 2], r[g * 4 + 3]);
+          } else {
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.out) + (int64_t)grow * args.ldc + gcol;
+            const __nv_bfloat16* res =
+                EPI == kEpiBf16AddResidual ? args.residual + (int64_t)grow * args.ldc + gcol : nullptr;
+            store_row_bf16(dst, r, valid, res);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem_base, 2 * BN);
+}
+
+// Sum split-K partials (fp32, in split order) into bf16 C, optional residual.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t MN, int N,
+                                     __nv_bfloat16* __restrict__ out, int64_t ldc,
+                                     const __nv_bfloat16* __restrict__ residual) {
+  const int64_t nvec = MN / 4;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = reinterpret_cast<const float4*>(part)[v];
+    for (int s = 1; s < splits; ++s) {
+      const float4 p = reinterpret_cast<const float4*>(part + s * MN)[v];
+      acc.x += p.x;
+      acc.y += p.y;
+      acc.z += p.z;
+      acc.w += p.w;
+    }
+    const int64_t e = v * 4;
+    const int64_t row = e / N, col = e % N;
+    __nv_bfloat16* o = out + row * ldc + col;
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    if (residual) {
+      const __nv_bfloat16* rr = residual + row * ldc + col;
+      float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+      float2 ra = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rr));
+      float2 rb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rr + 2));
+      lo = __floats2bfloat162_rn(a.x + ra.x, a.y + ra.y);
+      hi = __floats2bfloat162_rn(b.x + rb.x, b.y + rb.y);
+    }
+    reinterpret_cast<__nv_bfloat162*>(o)[0] = lo;
+    reinterpret_cast<__nv_bfloat162*>(o)[1] = hi;
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled unavailable (no CUDA driver)");
+  return fn;
+}
+
+struct MapKey {
+  uint64_t ptr, rows, cols, ld, box_rows;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.ptr * 0x9E3779B97F4A7C15ull;
+    h ^= k.rows + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    h ^= k.cols + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    h ^= k.ld + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    h ^= k.box_rows + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    return (size_t)h;
+  }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// 2-D bf16 row-major [rows, cols] (row stride ld elements), box = box_rows x 64,
+// 128-byte swizzle. Out-of-range rows/columns of a box read as zero.
+CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  MapKey key{(uint64_t)ptr, (uint64_t)rows, (uint64_t)cols, (uint64_t)ld, (uint64_t)box_rows};
+  {
+    std::lock_guard<std::mutex> g(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) return it->second;
+  }
+  if (((uint64_t)ptr & 15) != 0) throw std::runtime_error("gemm: operand base must be 16-byte aligned");
+  if ((ld * 2) % 16 != 0) throw std::runtime_error("gemm: row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  std::lock_guard<std::mutex> g(g_map_mu);
+  if (g_maps.size() > 8192) g_maps.clear();
+  g_maps.emplace(key, m);
+  return m;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, int EPI>
+void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
+  using L = Smem<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    MBX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, a);
+}
+
+template <int EPI>
+void launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
+  if (bn == 256) launch_cfg<256, 4, EPI>(ta, tb, a, grid, s);
+  else if (bn == 128) launch_cfg<128, 6, EPI>(ta, tb, a, grid, s);
+  else launch_cfg<64, 8, EPI>(ta, tb, a, grid, s);
+}
+
+GemmPlan plan_for(int64_t M, int64_t N, int64_t K, int sms) {
+  GemmPlan p;
+  const int64_t num_m = (M + BM - 1) / BM;
+  const int64_t kb_total = (K + BK - 1) / BK;
+  // Pick BN to balance waves across the SMs.
+  auto waves_eff = [&](int bn) {
+    const int64_t tiles = num_m * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    return (double)tiles / (double)(waves * sms);
+  };
+  p.bn = 256;
+  if (waves_eff(128) > waves_eff(256) * 1.15) p.bn = 128;
+  const int64_t tiles = num_m * ((N + p.bn - 1) / p.bn);
+  p.splits = 1;
+  if (tiles * 2 <= sms && kb_total >= 8) {
+    // few output tiles (decode): split K so every SM streams weights
+    const int64_t s = std::min<int64_t>(sms / tiles, kb_total / 4);
+    p.splits = (int)std::max<int64_t>(1, std::min<int64_t>(s, 16));
+  }
+  // every split gets at least one k-block
+  const int64_t per = (kb_total + p.splits - 1) / p.splits;
+  p.splits = (int)((kb_total + per - 1) / per);
+  return p;
+}
+
+}  // namespace
+
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) { return plan_for(M, N, K, num_sms()); }
+
+void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
+                 int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
+                 cudaStream_t s) {
+  if (M == 0 || N == 0) return;
+  if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm: K and N must be multiples of 8");
+  if (ldc % 8 != 0 || ((uint64_t)C & 15) != 0) throw std::runtime_error("gemm: C must be 16-byte aligned rows");
+  const int sms = num_sms();
+  GemmPlan p = plan_for(M, N, K, sms);
+  if (bn > 0) p.bn = bn;
+  if (splits > 0) p.splits = splits;
+  if (p.bn != 64 && p.bn != 128 && p.bn != 256) throw std::runtime_error("gemm: BN must be 64, 128 or 256");
+  GemmArgs a;
+  a.residual = static_cast<const __nv_bfloat16*>(residual);
+  a.ldc = ldc;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.num_m = (int)((M + BM - 1) / BM);
+  a.num_n = (int)((N + p.bn - 1) / p.bn);
+  a.kb_total = (int)((K + BK - 1) / BK);
+  a.splits = std::max(1, std::min(p.splits, a.kb_total));
+  a.kb_per_split = (a.kb_total + a.splits - 1) / a.splits;
+  a.splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  a.err = err;
+  a.timeout_ns = 2000000000ull;
+  const CUtensorMap ta = make_map(A, M, K, lda, BM);
+  const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);
+  const int units = a.num_m * a.num_n * a.splits;
+  const int grid = std::min(units, sms);
+  if (a.splits == 1) {
+    a.out = C;
+    if (residual) launch_bn<kEpiBf16AddResidual>(p.bn, ta, tb, a, grid, s);
+    else launch_bn<kEpiBf16>(p.bn, ta, tb, a, grid, s);
+  } else {
+    if (!workspace) throw std::runtime_error("gemm: split-K needs an fp32 workspace of splits*M*N elements");
+    if (N % 4 != 0) throw std::runtime_error("gemm: split-K needs N % 4 == 0");
+    a.out = workspace;
+    launch_bn<kEpiF32Partial>(p.bn, ta, tb, a, grid, s);
+    const int64_t MN = M * N;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
+    splitk_reduce_kernel<<<(int)blocks, threads, 0, s>>>(workspace, a.splits, MN, (int)N, (__nv_bfloat16*)C, ldc,
+                                                         a.residual);
+  }
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace mbx

@@ -1,0 +1,59 @@
+// Host-callable launchers of every sm_100a kernel in this package. Kernel
+// translation units include only CUDA headers; the torch-facing checks and
+// tensor plumbing live in bindings.cpp.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "ar/ar_ctx.h"
+
+namespace mbx {
+
+// ---- allreduce (ar/allreduce.cu) -------------------------------------------
+uint64_t ar_chunk_limit(const ArCtx& c, int algo);
+void ar_launch(const ArCtx& c, int algo, int dtype, const void* in, void* out, uint64_t nbytes, int max_blocks,
+               cudaStream_t stream);
+void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual, const void* weight, void* out, int M,
+                       int H, float eps, int max_blocks, cudaStream_t stream);
+void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nbytes, int max_blocks,
+                         cudaStream_t stream);
+void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream);
+void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, uint64_t nbytes, int max_blocks,
+                     cudaStream_t stream);
+void push_raw_launch(void* dst, const void* src, uint64_t nbytes, int grid_cap, cudaStream_t stream);
+
+// ---- elementwise (ops/elementwise.cu) ----------------------------------------
+void rmsnorm_launch(const void* x, void* residual, const void* w, void* out, int64_t M, int H, float eps,
+                    cudaStream_t s);
+void rope_and_cache_launch(const void* qkv, const int* pos, const float* cos_sin, const int64_t* slots, void* q_out,
+                           void* k_cache, void* v_cache, int64_t T, int nq, int nkv, int page, cudaStream_t s);
+void silu_mul_launch(const void* x, void* out, int64_t M, int I2, cudaStream_t s);
+void embedding_launch(const int* ids, const void* table, void* out, int64_t T, int H, int64_t start, int64_t rows,
+                      cudaStream_t s);
+void argmax_launch(const void* logits, bool bf16, int64_t ld, int64_t B, int V, int64_t offset, float* best_val,
+                   int64_t* best_idx, cudaStream_t s);
+void argmax_combine_launch(const float* vals, const int64_t* idxs, int W, int B, int64_t* out, cudaStream_t s);
+
+// ---- GEMM (gemm/gemm.cu) -----------------------------------------------------
+struct GemmPlan {
+  int bn = 256;
+  int splits = 1;
+};
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K);
+// C[M,N] (ldc) = A[M,K] (lda) * B[N,K]^T (ldb) (+ residual, same layout as C).
+// splits > 1 needs an fp32 workspace of splits*M*N elements.
+void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
+                 int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
+                 cudaStream_t s);
+
+// ---- attention (attn/attention.cu) -------------------------------------------
+void prefill_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
+                              const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
+                              int n_tiles, int nq, int nkv, float scale, cudaStream_t s);
+void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
+                             const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
+                             float* part_o, float* part_lse, float scale, cudaStream_t s);
+
+}  // namespace mbx
