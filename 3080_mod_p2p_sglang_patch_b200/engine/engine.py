@@ -1,0 +1,199 @@
+"""Offline serving engine: chunked prefill + CUDA-graph decode, greedy.
+
+``LLMEngine(cfg, tp=TPGroup|None, ...)`` owns one TP rank's weights, paged KV
+cache, scheduler and decode-graph runner. Every TP rank runs the same
+deterministic schedule, so all ranks take the same collective steps.
+
+Public API: ``generate(prompts, max_new_tokens)`` (token ids in, token ids
+out), ``add_request`` / ``step`` / ``run`` for streaming use, and
+``prefill_only`` for prompt-processing benchmarks (the reference's pp tok/s
+metric, tests/pp_bench.py: max_tokens=1).
+"""
+import time
+
+import torch
+
+from .. import ops
+from ..models import LlamaConfig, LlamaTP, LlamaWeights
+from .graph_runner import DecodeGraphRunner
+from .kv_cache import PAGE, PagedKVCache
+from .scheduler import Request, Scheduler
+
+
+class LLMEngine:
+    def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
+                 seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
+                 graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None):
+        self.cfg = cfg
+        self.tp = tp
+        self.tp_size = tp.world_size if tp is not None else 1
+        self.tp_rank = tp.rank if tp is not None else 0
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.max_batch = max_batch
+        self.max_seq = max_seq
+        self.chunk = chunk
+        self.weights = LlamaWeights(cfg, self.tp_rank, self.tp_size, self.device, seed=seed, full_init=full_init)
+        self.model = LlamaTP(cfg, self.weights, tp=tp, impl=impl)
+        nkv = cfg.kv_heads // self.tp_size
+        self.max_blocks_per_seq = (max_seq + PAGE - 1) // PAGE
+        if kv_blocks is None:
+            kv_blocks = max_batch * self.max_blocks_per_seq + 1
+        self.kv = PagedKVCache(cfg.layers, nkv, cfg.head_dim, kv_blocks, self.device)
+        self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq)
+        self.block_table = torch.zeros((max_batch, self.max_blocks_per_seq), dtype=torch.int32, device=self.device)
+        self._next_rid = 0
+        # scratch sized once (graph capture must not allocate)
+        self._reserve_scratch()
+        self.graphs = None
+        if use_graphs:
+            sizes = tuple(s for s in graph_sizes if s <= max_batch)
+            self.graphs = DecodeGraphRunner(self, sizes)
+
+    # ------------------------------------------------------------------ setup
+    def _reserve_scratch(self):
+        cfg, t = self.cfg, self.tp_size
+        C = None
+        try:
+            from .._ext import cuda_ext
+
+            C = cuda_ext()
+        except Exception:  # noqa: BLE001
+            return
+        H, F_, D = cfg.hidden, cfg.ffn // t, cfg.head_dim
+        shapes = [((cfg.heads + 2 * cfg.kv_heads) // t * D, H), (H, cfg.heads // t * D), (2 * F_, H), (H, F_),
+                  (cfg.vocab // t, H)]
+        need = 0
+        for M in (1, 8, 32, 64, self.max_batch):
+            for N, K in shapes:
+                bn, splits = C.gemm_plan(M, N, K)
+                if splits > 1:
+                    need = max(need, splits * M * N)
+        nq = cfg.heads // t
+        max_splits = 64
+        ops.reserve(self.device, gemm_elems=need, decode_o=self.max_batch * nq * max_splits * D,
+                    decode_lse=self.max_batch * nq * max_splits)
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, prompt, max_new_tokens: int) -> Request:
+        req = Request(self._next_rid, list(prompt), max_new_tokens, t_arrive=time.perf_counter())
+        self._next_rid += 1
+        self.sched.add(req)
+        return req
+
+    def _sync_block_row(self, req):
+        row = torch.zeros(self.max_blocks_per_seq, dtype=torch.int32)
+        row[: len(req.blocks)] = torch.tensor(req.blocks, dtype=torch.int32)
+        self.block_table[req.slot].copy_(row.to(self.device, non_blocking=True))
+        req._row_synced = True
+
+    # ------------------------------------------------------------------ execution
+    def _run_prefill(self, batch):
+        pieces = batch.pieces
+        for p in pieces:
+            if not getattr(p.req, "_row_synced", False):
+                self._sync_block_row(p.req)
+        ids, pos, slots, q_lens, kv_lens, rows, last = [], [], [], [], [], [], []
+        off = 0
+        for p in pieces:
+            req = p.req
+            ids.extend(req.prompt[p.start:p.start + p.n])
+            pos.extend(range(p.start, p.start + p.n))
+            slots.extend(self.kv.slots(req.blocks, p.start, p.n))
+            q_lens.append(p.n)
+            kv_lens.append(p.start + p.n)
+            rows.append(req.slot)
+            off += p.n
+            last.append(off - 1)
+        return self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, last)
+
+    def forward_prefill(self, ids, pos, slots, q_lens, kv_lens, rows, last):
+        """One prefill forward from host lists; returns next token per piece."""
+        dev = self.device
+        R = len(q_lens)
+        host = torch.tensor(ids + pos + q_lens + kv_lens + rows, dtype=torch.int32).pin_memory()
+        d = host.to(dev, non_blocking=True)
+        T = len(ids)
+        ids_d, pos_d = d[:T], d[T:2 * T]
+        kvl_d = d[2 * T + R:2 * T + 2 * R]
+        rows_d = d[2 * T + 2 * R:2 * T + 3 * R]
+        slots_d = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        cu = torch.zeros(R + 1, dtype=torch.int32)
+        cu[1:] = torch.tensor(q_lens, dtype=torch.int32).cumsum(0)
+        cu_d = cu.pin_memory().to(dev, non_blocking=True)
+        tiles = ops.prefill_tiles(q_lens).pin_memory().to(dev, non_blocking=True)
+        bt = self.block_table.index_select(0, rows_d.long())
+        last_d = torch.tensor(last, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        scale = self.model.scale
+
+        def attn(li, q, kc, vc):
+            return ops.prefill_attention(q, kc, vc, cu_d, kvl_d, bt, tiles, scale)
+
+        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d)
+
+    def decode_inputs(self, reqs):
+        ids = [r.output[-1] if r.output else r.prompt[-1] for r in reqs]
+        pos = [r.total_len - 1 for r in reqs]
+        kv_len = [r.total_len for r in reqs]
+        slots = [r.blocks[(r.total_len - 1) // PAGE] * PAGE + (r.total_len - 1) % PAGE for r in reqs]
+        rows = [r.slot for r in reqs]
+        return ids, pos, kv_len, slots, rows
+
+    def forward_decode_eager(self, ids_d, pos_d, kvl_d, slots_d, rows_d, splits=None):
+        B = ids_d.shape[0]
+        bt = self.block_table.index_select(0, rows_d.long())
+        nkv = self.cfg.kv_heads // self.tp_size
+        sp = splits or ops.decode_splits(B, nkv, self.max_seq)
+        scale = self.model.scale
+
+        def attn(li, q, kc, vc):
+            return ops.decode_attention(q, kc, vc, kvl_d, bt, scale, splits=sp)
+
+        last = torch.arange(B, device=self.device, dtype=torch.int64)
+        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last)
+
+    def _run_decode(self, batch):
+        for r in batch.reqs:
+            if not getattr(r, "_row_synced", False):
+                self._sync_block_row(r)
+        ids, pos, kv_len, slots, rows = self.decode_inputs(batch.reqs)
+        if self.graphs is not None and self.graphs.can_run(len(ids)):
+            return self.graphs.run(ids, pos, kv_len, slots, rows)
+        dev = self.device
+        B = len(ids)
+        host = torch.tensor(ids + pos + kv_len + rows, dtype=torch.int32).pin_memory()
+        d = host.to(dev, non_blocking=True)
+        slots_d = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        return self.forward_decode_eager(d[:B], d[B:2 * B], d[2 * B:3 * B], slots_d, d[3 * B:])
+
+    def step(self):
+        """Run one scheduled batch; returns the batch (or None when idle)."""
+        batch = self.sched.next_batch()
+        if batch is None:
+            return None
+        if batch.kind == "prefill":
+            nxt = self._run_prefill(batch).tolist()
+            now = time.perf_counter()
+            for p in batch.pieces:
+                if p.completes:
+                    p.req.t_first = now
+                    p.req.token_times.append(now)
+            self.sched.after_prefill(batch, nxt)
+        else:
+            nxt = self._run_decode(batch).tolist()
+            now = time.perf_counter()
+            for r in batch.reqs:
+                r.token_times.append(now)
+            self.sched.after_decode(batch, nxt)
+        return batch
+
+    def run(self):
+        while self.sched.has_work():
+            self.step()
+        done = sorted(self.sched.finished, key=lambda r: r.rid)
+        self.sched.finished = []
+        return done
+
+    def generate(self, prompts, max_new_tokens: int = 16):
+        reqs = [self.add_request(p, max_new_tokens) for p in prompts]
+        self.run()
+        return [r.output for r in reqs]

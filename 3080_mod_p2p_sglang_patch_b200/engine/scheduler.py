@@ -1,0 +1,139 @@
+"""Request state and the chunked-prefill scheduler.
+
+Policy (sglang's default): while any request still has prompt tokens to
+prefill, the next batch is a prefill chunk of up to ``chunk`` tokens, taken
+in arrival order (a long prompt spans several chunks; a chunk may hold the
+tail of one prompt and the head of the next). Otherwise all running requests
+decode one token. New requests are admitted while the running set is below
+``max_batch`` and the KV cache has room.
+"""
+import collections
+import dataclasses
+
+from .kv_cache import PAGE
+
+
+@dataclasses.dataclass
+class Request:
+    rid: int
+    prompt: list
+    max_new: int
+    output: list = dataclasses.field(default_factory=list)
+    blocks: list = dataclasses.field(default_factory=list)
+    computed: int = 0          # tokens whose K/V are in the cache
+    slot: int = -1             # row in the decode batch tables
+    done: bool = False
+    t_arrive: float = 0.0
+    t_first: float = 0.0
+    token_times: list = dataclasses.field(default_factory=list)
+
+    @property
+    def total_len(self):
+        return len(self.prompt) + len(self.output)
+
+    @property
+    def prefill_left(self):
+        return len(self.prompt) - self.computed if self.computed < len(self.prompt) else 0
+
+
+@dataclasses.dataclass
+class PrefillPiece:
+    req: Request
+    start: int
+    n: int
+
+    @property
+    def completes(self):
+        return self.start + self.n == len(self.req.prompt)
+
+
+@dataclasses.dataclass
+class Batch:
+    kind: str  # "prefill" or "decode"
+    pieces: list = None
+    reqs: list = None
+
+    @property
+    def num_tokens(self):
+        return sum(p.n for p in self.pieces) if self.kind == "prefill" else len(self.reqs)
+
+
+class Scheduler:
+    def __init__(self, chunk: int = 1024, max_batch: int = 64, allocator=None, max_seq: int = 16384):
+        self.chunk = chunk
+        self.max_batch = max_batch
+        self.allocator = allocator
+        self.max_seq = max_seq
+        self.waiting = collections.deque()
+        self.prefilling = []
+        self.running = []
+        self.finished = []
+        self._free_slots = list(range(max_batch - 1, -1, -1))
+
+    def add(self, req: Request):
+        if len(req.prompt) + req.max_new > self.max_seq:
+            raise ValueError(f"request {req.rid}: {len(req.prompt)}+{req.max_new} tokens exceed max_seq {self.max_seq}")
+        self.waiting.append(req)
+
+    def has_work(self):
+        return bool(self.waiting or self.prefilling or self.running)
+
+    def _admit(self):
+        while self.waiting and self._free_slots:
+            req = self.waiting[0]
+            need = (len(req.prompt) + req.max_new + PAGE - 1) // PAGE
+            if self.allocator is not None and self.allocator.free < need:
+                break
+            self.waiting.popleft()
+            if self.allocator is not None:
+                req.blocks = self.allocator.alloc(need)
+            req.slot = self._free_slots.pop()
+            self.prefilling.append(req)
+
+    def next_batch(self):
+        self._admit()
+        if self.prefilling:
+            budget = self.chunk
+            pieces = []
+            for req in self.prefilling:
+                if budget <= 0:
+                    break
+                n = min(req.prefill_left, budget)
+                if n <= 0:
+                    continue
+                pieces.append(PrefillPiece(req, req.computed, n))
+                budget -= n
+            return Batch("prefill", pieces=pieces)
+        if self.running:
+            return Batch("decode", reqs=list(self.running))
+        return None
+
+    def after_prefill(self, batch: Batch, next_tokens):
+        """next_tokens: list aligned with batch.pieces (only completing pieces matter)."""
+        for piece, tok in zip(batch.pieces, next_tokens):
+            req = piece.req
+            req.computed += piece.n
+            if piece.completes:
+                self.prefilling.remove(req)
+                req.output.append(int(tok))
+                if len(req.output) >= req.max_new:
+                    self._finish(req)
+                else:
+                    self.running.append(req)
+
+    def after_decode(self, batch: Batch, next_tokens):
+        for req, tok in zip(batch.reqs, next_tokens):
+            req.computed += 1
+            req.output.append(int(tok))
+            if len(req.output) >= req.max_new:
+                self.running.remove(req)
+                self._finish(req)
+
+    def _finish(self, req):
+        req.done = True
+        if self.allocator is not None and req.blocks:
+            self.allocator.release(req.blocks)
+            req.blocks = []
+        self._free_slots.append(req.slot)
+        req.slot = -1
+        self.finished.append(req)

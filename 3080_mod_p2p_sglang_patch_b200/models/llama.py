@@ -1,0 +1,199 @@
+"""Tensor-parallel Llama-style decoder on the package's sm_100a kernels.
+
+Per rank (TP degree t): vocab-parallel embedding [V/t, H]; per layer a
+column-parallel QKV [(nq+2nkv)/t*D, H] and gate_up [2F/t, H], row-parallel
+o_proj [H, nq/t*D] and down [H, F/t]; vocab-parallel LM head [V/t, H].
+Row-parallel outputs go through the communicator's fused
+allreduce + residual add + RMSNorm (one launch), the point where the
+reference's MailboxAR sits in sglang (RowParallelLinear ->
+tensor_model_parallel_all_reduce, the call stack of its hot path).
+
+``impl="native"``: tcgen05 GEMMs, own attention / norm / RoPE / SiLU kernels,
+MailboxAR collectives. ``impl="torch"``: the NCCL(+cuBLAS) TP baseline -
+F.linear (cuBLAS) GEMMs and NCCL allreduce, same attention/elementwise
+kernels, so the two builds differ exactly in GEMMs and collectives.
+"""
+import math
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .. import ops
+from .config import LlamaConfig
+
+
+def _randn(shape, std, gen, device):
+    return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+class LlamaWeights:
+    """Random-init N(0, std) weights of one TP rank.
+
+    ``full_init=True`` draws every full tensor from one seeded generator and
+    keeps this rank's shard (identical model at every TP degree, used by the
+    tests); otherwise each shard is drawn directly from a seed derived from
+    (seed, tensor, rank) (fast for 8B/70B)."""
+
+    def __init__(self, cfg: LlamaConfig, tp_rank: int, tp_size: int, device, seed: int = 0, full_init: bool = False):
+        cfg.check_tp(tp_size)
+        self.cfg = cfg
+        t, r = tp_size, tp_rank
+        H, D, F_ = cfg.hidden, cfg.head_dim, cfg.ffn
+        nq, nkv = cfg.heads // t, cfg.kv_heads // t
+        V = cfg.vocab // t
+        std = cfg.init_std
+        dev = torch.device(device)
+        counter = [0]
+
+        def gen_for():
+            counter[0] += 1
+            g = torch.Generator(device=dev)
+            g.manual_seed(seed * 1_000_003 + counter[0] * 7919 + (0 if full_init else r * 104_729))
+            return g
+
+        def col_parallel(full_rows_list, cols):
+            # rows of several full matrices, this rank's slice of each, concatenated
+            outs = []
+            for full_rows in full_rows_list:
+                g = gen_for()
+                per = full_rows // t
+                if full_init:
+                    full = _randn((full_rows, cols), std, g, dev)
+                    outs.append(full[r * per:(r + 1) * per])
+                else:
+                    outs.append(_randn((per, cols), std, g, dev))
+            return torch.cat(outs, 0).contiguous()
+
+        def row_parallel(rows, full_cols):
+            g = gen_for()
+            per = full_cols // t
+            if full_init:
+                full = _randn((rows, full_cols), std, g, dev)
+                return full[:, r * per:(r + 1) * per].contiguous()
+            return _randn((rows, per), std, g, dev)
+
+        self.embed = col_parallel([cfg.vocab], H)
+        self.layers = []
+        for _ in range(cfg.layers):
+            L = {}
+            L["ln1"] = torch.ones(H, dtype=torch.bfloat16, device=dev)
+            L["qkv"] = col_parallel([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], H)
+            L["o"] = row_parallel(H, cfg.heads * D)
+            L["ln2"] = torch.ones(H, dtype=torch.bfloat16, device=dev)
+            L["gate_up"] = col_parallel([F_, F_], H)
+            L["down"] = row_parallel(H, F_)
+            self.layers.append(L)
+        self.norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        self.lm_head = col_parallel([cfg.vocab], H)
+        self.vocab_start = r * V
+        self.nq, self.nkv = nq, nkv
+
+
+class LlamaTP:
+    """Forward passes of one TP rank over a paged KV cache.
+
+    ``tp``: a ``parallel.TPGroup`` (or None for one GPU).
+    """
+
+    def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, tp=None, impl: str = "native"):
+        self.cfg = cfg
+        self.w = weights
+        self.tp = tp
+        self.tp_size = tp.world_size if tp is not None else 1
+        self.impl = impl
+        self.device = weights.embed.device
+        self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, self.device)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    # ------------------------------------------------------------ building blocks
+    def _linear(self, x, w, out=None, residual=None):
+        if self.impl == "torch":
+            y = F.linear(x, w)
+            if residual is not None:
+                y = y + residual
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
+        return ops.gemm(x, w, out=out, residual=residual)
+
+    def _all_reduce(self, x):
+        if self.tp_size == 1:
+            return x
+        if self.impl == "torch":
+            dist.all_reduce(x, group=self.tp.group)
+            return x
+        return self.tp.all_reduce(x)
+
+    def _ar_norm(self, partial, residual, w, out=None):
+        """residual <- residual + allreduce(partial); returns rmsnorm(residual)."""
+        if self.tp_size == 1 or self.impl == "torch":
+            x = self._all_reduce(partial)
+            return ops.fused_add_rmsnorm(x, residual, w, self.cfg.eps, out=out)
+        return self.tp.all_reduce_rmsnorm(partial, residual, w, self.cfg.eps, out=out)
+
+    def _lm_argmax(self, x_last):
+        """Greedy next token from the vocab-parallel LM head."""
+        logits = self._linear(x_last, self.w.lm_head)
+        vals, idx = ops.argmax(logits, offset=self.w.vocab_start)
+        if self.tp_size == 1:
+            return idx
+        if self.impl == "torch":
+            gv = torch.empty((self.tp_size,) + vals.shape, dtype=vals.dtype, device=vals.device)
+            gi = torch.empty((self.tp_size,) + idx.shape, dtype=idx.dtype, device=idx.device)
+            dist.all_gather_into_tensor(gv, vals, group=self.tp.group)
+            dist.all_gather_into_tensor(gi, idx, group=self.tp.group)
+        else:
+            # pack (val, idx) as two int64 words per row so one all-gather carries both
+            B = vals.shape[0]
+            pack = torch.empty((B, 2), dtype=torch.int64, device=vals.device)
+            pack[:, 0] = vals.view(torch.int32).to(torch.int64)
+            pack[:, 1] = idx
+            g = self.tp.all_gather(pack)  # [tp, B, 2]
+            gv = g[:, :, 0].to(torch.int32).view(torch.float32)
+            gi = g[:, :, 1]
+        return ops.argmax_combine(gv.contiguous(), gi.contiguous())
+
+    # ------------------------------------------------------------ forward
+    def forward(self, ids, positions, slots, kv_caches, attn, last_idx, return_hidden=False):
+        """One forward over T tokens.
+
+        ids/positions int32 [T]; slots int64 [T] (KV write slots); kv_caches
+        [(k, v)] per layer; ``attn`` callable(layer, q, k_cache, v_cache) -> o
+        [T, nq, D] (prefill or decode attention); last_idx int64 [B] rows whose
+        next token is returned. Returns next-token ids int64 [B] (or the final
+        normalised hidden rows [B, H] with ``return_hidden``).
+        """
+        cfg, w = self.cfg, self.w
+        T = ids.shape[0]
+        nq, nkv, D = w.nq, w.nkv, cfg.head_dim
+        h = ops.embedding(ids, w.embed, start=w.vocab_start)
+        h = self._all_reduce(h)
+        residual = h
+        x = ops.rmsnorm(residual, w.layers[0]["ln1"], cfg.eps)
+        for li, L in enumerate(w.layers):
+            qkv = self._linear(x, L["qkv"])
+            kc, vc = kv_caches[li]
+            q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
+            o = attn(li, q, kc, vc)
+            if self.tp_size == 1 and self.impl == "native":
+                # residual add fused into the GEMM epilogue, in place
+                self._linear(o.view(T, nq * D), L["o"], out=residual, residual=residual)
+                x = ops.rmsnorm(residual, L["ln2"], cfg.eps)
+            else:
+                part = self._linear(o.view(T, nq * D), L["o"])
+                x = self._ar_norm(part, residual, L["ln2"])
+            gu = self._linear(x, L["gate_up"])
+            a = ops.silu_mul(gu)
+            nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
+            if self.tp_size == 1 and self.impl == "native":
+                self._linear(a, L["down"], out=residual, residual=residual)
+                x = ops.rmsnorm(residual, nxt, cfg.eps)
+            else:
+                part = self._linear(a, L["down"])
+                x = self._ar_norm(part, residual, nxt)
+        x_last = x.index_select(0, last_idx)
+        if return_hidden:
+            return x_last
+        return self._lm_argmax(x_last)

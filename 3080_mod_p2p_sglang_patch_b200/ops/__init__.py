@@ -11,6 +11,7 @@ import math
 import torch
 
 from .._ext import cuda_ext
+from ..utils import launches
 
 
 class _Workspace:
@@ -74,12 +75,14 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
     s = splits or plan_splits
     wbuf = ws.gemm(s * M * N) if s > 1 else None
     C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits)
+    launches.add(2 if s > 1 else 1)
     return out
 
 
 def rmsnorm(x, w, eps, out=None):
     out = torch.empty_like(x) if out is None else out
     cuda_ext().rmsnorm(x, w, out, eps)
+    launches.add(1)
     return out
 
 
@@ -87,6 +90,7 @@ def fused_add_rmsnorm(x, residual, w, eps, out=None):
     """residual <- bf16(x + residual); returns rmsnorm(residual) * w."""
     out = torch.empty_like(x) if out is None else out
     cuda_ext().fused_add_rmsnorm(x, residual, w, out, eps)
+    launches.add(1)
     return out
 
 
@@ -104,6 +108,7 @@ def rope_and_cache(qkv, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v
     if q_out is None:
         q_out = torch.empty((T, nq, 128), dtype=qkv.dtype, device=qkv.device)
     cuda_ext().rope_and_cache(qkv, positions, cos_sin, slots, q_out, k_cache, v_cache, nq, nkv, page)
+    launches.add(1)
     return q_out
 
 
@@ -111,6 +116,7 @@ def silu_mul(x, out=None):
     if out is None:
         out = torch.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=x.dtype, device=x.device)
     cuda_ext().silu_mul(x, out)
+    launches.add(1)
     return out
 
 
@@ -118,6 +124,7 @@ def embedding(ids, table, start=0, out=None):
     if out is None:
         out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device)
     cuda_ext().embedding(ids, table, out, start)
+    launches.add(1)
     return out
 
 
@@ -128,6 +135,7 @@ def argmax(logits, offset=0, vals=None, idx=None):
     if idx is None:
         idx = torch.empty(B, dtype=torch.int64, device=logits.device)
     cuda_ext().argmax(logits, offset, vals, idx)
+    launches.add(1)
     return vals, idx
 
 
@@ -135,6 +143,7 @@ def argmax_combine(vals, idx, out=None):
     if out is None:
         out = torch.empty(vals.shape[1], dtype=torch.int64, device=vals.device)
     cuda_ext().argmax_combine(vals, idx, out)
+    launches.add(1)
     return out
 
 
@@ -152,6 +161,7 @@ def prefill_attention(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles, sca
         out = torch.empty_like(q)
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     cuda_ext().prefill_attention(q, k_cache, v_cache, out, cu_q, kv_len, block_table, tiles, scale)
+    launches.add(1)
     return out
 
 
@@ -171,4 +181,5 @@ def decode_attention(q, k_cache, v_cache, kv_len, block_table, scale=None, split
     if splits > 1:
         po, pl = workspace(q.device).decode(B * nq * splits * 128, B * nq * splits)
     cuda_ext().decode_attention(q, k_cache, v_cache, out, kv_len, block_table, po, pl, splits, scale)
+    launches.add(2 if splits > 1 else 1)
     return out

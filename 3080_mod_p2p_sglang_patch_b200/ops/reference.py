@@ -33,8 +33,9 @@ def rope(x, positions, cos_sin):
 
 
 def silu_mul(x):
+    """silu(gate) rounded to bf16, times up (torch's bf16 evaluation order)."""
     g, u = x.float().chunk(2, dim=-1)
-    return F.silu(g) * u
+    return F.silu(g).to(torch.bfloat16).float() * u
 
 
 def gather_kv(cache, block_table_row, length, page=16):

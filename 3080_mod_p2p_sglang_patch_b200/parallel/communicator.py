@@ -32,6 +32,7 @@ import torch.distributed as dist
 
 from .._ext import cpu_ext, cuda_ext
 from ..config import CommConfig
+from ..utils import launches
 from . import bootstrap
 
 logger = logging.getLogger(__name__)
@@ -275,6 +276,7 @@ class MailboxAR:
         self._ar.allreduce(input.data_ptr(), out.data_ptr(), nbytes, DTYPE_IDS[input.dtype], a, self.cfg.max_blocks,
                            torch.cuda.current_stream(self.device).cuda_stream)
         self.counters[ALGO_NAMES[a]] += 1
+        launches.add(max(1, -(-nbytes // int(self._ar.chunk_limit(a)))))
         return out
 
     def all_reduce_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
@@ -293,6 +295,7 @@ class MailboxAR:
         self._ar.ar_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(), out.data_ptr(), M, H, eps, algo,
                             self.cfg.max_blocks, torch.cuda.current_stream(self.device).cuda_stream)
         self.counters["fused"] += 1
+        launches.add(1)
         return out
 
     def fused_rmsnorm_limit(self) -> int:
@@ -309,6 +312,7 @@ class MailboxAR:
         self._ar.allgather(x.data_ptr(), out.data_ptr(), x.numel() * x.element_size(), self.cfg.max_blocks,
                            torch.cuda.current_stream(self.device).cuda_stream)
         self.counters["allgather"] += 1
+        launches.add(1)
         return out
 
     # ------------------------------------------------------------------ graph

@@ -412,8 +412,10 @@ __global__ void __launch_bounds__(kArThreads) seg_submit_kernel(ArCtx c, const u
   if (threadIdx.x == 0) s_ok = true;
   __syncthreads();
   if (!poisoned(c)) {
-    // Slot reuse: every receiver must have acked seq - kSegSlots.
-    if (threadIdx.x < W && seq > (uint32_t)kSegSlots) {
+    // Slot reuse: every peer must have acked seq - kSegSlots. Only peers take
+    // part (the own contribution never goes through a slot), so no kernel
+    // waits on another kernel of the same GPU.
+    if (threadIdx.x < W && threadIdx.x != c.rank && seq > (uint32_t)kSegSlots) {
       const int r = threadIdx.x;
       if (!wait_flag_geq(seg_free(c.bufs[c.rank], slot, r), seq - kSegSlots, c.timeout_ns)) {
         record_error(c, kErrSegFree, blockIdx.x, r, 10, seq);
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(kArThreads) seg_submit_kernel(ArCtx c, const u
       for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
         const uint4 v = ld_nc_v4(in + i);
 #pragma unroll
-        for (int j = 0; j < W; ++j) {
+        for (int j = 1; j < W; ++j) {
           const int r = (c.rank + j) % W;
           st_v4(seg_data(c, c.bufs[r], slot, c.rank) + i * 16, v);
         }
@@ -443,7 +445,7 @@ __global__ void __launch_bounds__(kArThreads) seg_submit_kernel(ArCtx c, const u
     if (prev == gridDim.x - 1) {
       c.state[kStSegSubmitDone] = 0;
       if (!poisoned(c))
-        for (int r = 0; r < W; ++r) st_release_sys(seg_ready(c.bufs[r], slot, c.rank), seq);
+        for (int j = 1; j < W; ++j) st_release_sys(seg_ready(c.bufs[(c.rank + j) % W], slot, c.rank), seq);
       c.state[kStSegSubmit] = seq;
       __threadfence();
     }
@@ -459,7 +461,7 @@ __global__ void __launch_bounds__(kArThreads) seg_wait_kernel(ArCtx c, const uin
   if (threadIdx.x == 0) s_ok = true;
   __syncthreads();
   if (!poisoned(c)) {
-    if (threadIdx.x < W) {
+    if (threadIdx.x < W && threadIdx.x != c.rank) {
       const int r = threadIdx.x;
       if (!wait_flag_geq(seg_ready(c.bufs[c.rank], slot, r), seq, c.timeout_ns)) {
         record_error(c, kErrSegWait, blockIdx.x, r, 11, seq);
@@ -473,7 +475,7 @@ __global__ void __launch_bounds__(kArThreads) seg_wait_kernel(ArCtx c, const uin
         float acc[Pack<T>::N] = {};
 #pragma unroll
         for (int r = 0; r < W; ++r) {
-          // own contribution comes from the caller's local tensor (identical bits)
+          // rank order; the own contribution comes from the caller's tensor
           const uint4 v = (r == c.rank) ? ld_nc_v4(local + i) : ld_cg_v4(seg_data(c, c.bufs[c.rank], slot, r) + i * 16);
           unpack_add<T>(v, acc);
         }
@@ -488,9 +490,9 @@ __global__ void __launch_bounds__(kArThreads) seg_wait_kernel(ArCtx c, const uin
     if (prev == gridDim.x - 1) {
       c.state[kStSegWaitDone] = 0;
       c.state[kStSegWait] = seq;
-      // free the slot for every pusher
+      // free the slot for every pushing peer
       if (!poisoned(c))
-        for (int r = 0; r < W; ++r) st_release_sys(seg_free(c.bufs[r], slot, c.rank), seq);
+        for (int j = 1; j < W; ++j) st_release_sys(seg_free(c.bufs[(c.rank + j) % W], slot, c.rank), seq);
       __threadfence();
     }
   }

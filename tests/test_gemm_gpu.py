@@ -1,0 +1,60 @@
+"""tcgen05/TMEM GEMM vs a PyTorch fp32 reference (C = A @ B^T)."""
+import pytest
+import torch
+
+from conftest import sub
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    # (M, N, K, bn, splits)
+    (128, 256, 64, 256, 1),
+    (128, 128, 128, 128, 1),
+    (256, 512, 256, 0, 0),
+    (200, 384, 320, 128, 1),      # M / N tails
+    (1024, 4096, 4096, 0, 0),     # prefill o_proj at TP=1
+    (1000, 3072, 4096, 0, 0),     # qkv at TP=2 with a ragged M
+    (8, 6144, 4096, 0, 0),        # decode shape -> split-K
+    (64, 1792, 14336, 0, 0),      # down_proj at TP=8 decode
+    (1, 16032, 4096, 0, 0),       # lm_head shard, bs=1
+    (96, 2048, 4096, 64, 1),      # BN=64 path
+]
+
+
+@pytest.mark.parametrize("M,N,K,bn,splits", SHAPES)
+def test_gemm_matches_fp32(M, N, K, bn, splits):
+    ops = sub("ops")
+    torch.manual_seed(0)
+    a = (torch.randn(M, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+    out = ops.gemm(a, w, bn=bn, splits=splits)
+    torch.cuda.synchronize()
+    assert ops.gemm_error() == 0
+    ref = a.float() @ w.float().t()
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-2 * scale + 1e-2, f"max err {err} vs scale {scale}"
+
+
+def test_gemm_residual_epilogue():
+    ops = sub("ops")
+    torch.manual_seed(1)
+    M, N, K = 300, 1024, 512
+    a = (torch.randn(M, K, device="cuda") / 5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") / 5).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    out = ops.gemm(a, w, residual=r)
+    ref = (a.float() @ w.float().t()).to(torch.bfloat16).float() + r.float()
+    assert (out.float() - ref).abs().max().item() < 0.1
+
+
+def test_gemm_strided_views():
+    """Operands that are row slices of bigger tensors (ld > K)."""
+    ops = sub("ops")
+    torch.manual_seed(2)
+    big = (torch.randn(256, 1024, device="cuda") / 8).to(torch.bfloat16)
+    a = big[:, :512]
+    w = (torch.randn(384, 512, device="cuda") / 8).to(torch.bfloat16)
+    out = ops.gemm(a, w)
+    ref = a.float() @ w.float().t()
+    assert (out.float() - ref).abs().max().item() < 2e-2 * ref.abs().max().item() + 1e-2

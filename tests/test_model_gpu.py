@@ -1,0 +1,99 @@
+"""The TP Llama decoder on the native kernels vs a plain PyTorch fp32 forward
+of the same random weights (logit cosine / top-1 agreement), chunked prefill
+consistency, and CUDA-graph decode vs eager decode."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import sub
+
+pytestmark = pytest.mark.gpu
+
+
+def torch_forward(w, cfg, ids):
+    """fp32 reference forward of the full sequence (no cache); returns the
+    final normalised hidden states [T, H]."""
+    ref = sub("ops.reference")
+    T = len(ids)
+    D, nq, nkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+    cs = sub("ops").rope_cos_sin(cfg.max_pos, D, cfg.rope_theta, "cuda")
+    pos = torch.arange(T, device="cuda", dtype=torch.int32)
+    h = w.embed.float()[torch.tensor(ids, device="cuda")]
+    x = ref.rmsnorm(h, w.layers[0]["ln1"], cfg.eps)
+    res = h
+    for li, L in enumerate(w.layers):
+        qkv = x @ L["qkv"].float().t()
+        q = qkv[:, : nq * D].view(T, nq, D)
+        k = qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D)
+        v = qkv[:, (nq + nkv) * D:].view(T, nkv, D)
+        q, k = ref.rope(q, pos, cs), ref.rope(k, pos, cs)
+        o = ref.attention(q, k, v, causal_offset=0).reshape(T, nq * D)
+        res = res + o @ L["o"].float().t()
+        x = ref.rmsnorm(res, L["ln2"], cfg.eps)
+        gu = x @ L["gate_up"].float().t()
+        g, u = gu.chunk(2, -1)
+        res = res + (F.silu(g) * u) @ L["down"].float().t()
+        nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
+        x = ref.rmsnorm(res, nxt, cfg.eps)
+    return x
+
+
+def test_prefill_matches_torch_reference():
+    models, eng_mod = sub("models"), sub("engine")
+    cfg = models.LlamaConfig.tiny()
+    eng = eng_mod.LLMEngine(cfg, max_batch=4, max_seq=512, chunk=64, seed=3, use_graphs=False)
+    prompt = torch.randint(0, cfg.vocab, (150,), generator=torch.Generator().manual_seed(0)).tolist()
+    req = eng.add_request(prompt, 1)
+    eng.sched._admit()
+    eng._sync_block_row(req)
+    slots = eng.kv.slots(req.blocks, 0, len(prompt))
+    # native, chunked in pieces of 64 (+22), hidden state of the last token
+    hid = None
+    for s in range(0, len(prompt), 64):
+        n = min(64, len(prompt) - s)
+        dev = eng.device
+        ids = torch.tensor(prompt[s:s + n], dtype=torch.int32, device=dev)
+        pos = torch.arange(s, s + n, dtype=torch.int32, device=dev)
+        sl = torch.tensor(slots[s:s + n], dtype=torch.int64, device=dev)
+        cu = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        kvl = torch.tensor([s + n], dtype=torch.int32, device=dev)
+        bt = eng.block_table[req.slot:req.slot + 1]
+        tiles = sub("ops").prefill_tiles([n]).to(dev)
+        last = torch.tensor([n - 1], dtype=torch.int64, device=dev)
+        attn = lambda li, q, kc, vc: sub("ops").prefill_attention(q, kc, vc, cu, kvl, bt, tiles, eng.model.scale)
+        hid = eng.model.forward(ids, pos, sl, eng.kv.caches, attn, last, return_hidden=True)
+    want = torch_forward(eng.weights, cfg, prompt)[-1]
+    got = hid[0].float()
+    cos = F.cosine_similarity(got, want, dim=0).item()
+    assert cos > 0.995, cos
+    logits_got = got @ eng.weights.lm_head.float().t()
+    logits_want = want @ eng.weights.lm_head.float().t()
+    top = logits_want.topk(5).indices
+    assert logits_got.argmax().item() in top.tolist()
+
+
+def test_generate_graphs_match_eager():
+    models, eng_mod = sub("models"), sub("engine")
+    cfg = models.LlamaConfig.tiny()
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=torch.Generator().manual_seed(n)).tolist()
+               for n in (17, 64, 130)]
+    outs = []
+    for graphs in (False, True):
+        eng = eng_mod.LLMEngine(cfg, max_batch=8, max_seq=512, chunk=64, seed=5, use_graphs=graphs,
+                                graph_sizes=(1, 8))
+        outs.append(eng.generate(prompts, max_new_tokens=12))
+    assert outs[0] == outs[1]
+    assert all(len(o) == 12 for o in outs[0])
+
+
+def test_chunk_size_does_not_change_tokens():
+    models, eng_mod = sub("models"), sub("engine")
+    cfg = models.LlamaConfig.tiny()
+    prompts = [list(range(1, 200)), list(range(7, 90))]
+    res = []
+    for chunk in (32, 1024):
+        eng = eng_mod.LLMEngine(cfg, max_batch=4, max_seq=512, chunk=chunk, seed=9, use_graphs=False)
+        res.append(eng.generate(prompts, max_new_tokens=6))
+    assert res[0] == res[1]

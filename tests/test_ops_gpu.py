@@ -1,0 +1,74 @@
+"""Elementwise sm_100a kernels vs PyTorch fp32 references."""
+import pytest
+import torch
+
+from conftest import sub
+
+pytestmark = pytest.mark.gpu
+
+
+def test_rmsnorm_and_fused_add():
+    ops, ref = sub("ops"), sub("ops.reference")
+    torch.manual_seed(0)
+    for M, H in [(1, 4096), (37, 4096), (1024, 8192)]:
+        x = torch.randn(M, H, device="cuda").to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(H, device="cuda")).to(torch.bfloat16)
+        out = ops.rmsnorm(x, w, 1e-5)
+        assert (out.float() - ref.rmsnorm(x, w, 1e-5)).abs().max().item() < 3e-2
+        r = torch.randn(M, H, device="cuda").to(torch.bfloat16)
+        r0 = r.clone()
+        out2 = ops.fused_add_rmsnorm(x, r, w, 1e-5)
+        want, want_r = ref.fused_add_rmsnorm(x, r0, w, 1e-5)
+        assert torch.equal(r, want_r)
+        assert (out2.float() - want).abs().max().item() < 3e-2
+
+
+def test_silu_mul():
+    ops, ref = sub("ops"), sub("ops.reference")
+    x = torch.randn(77, 2 * 1792, device="cuda").to(torch.bfloat16)
+    assert (ops.silu_mul(x).float() - ref.silu_mul(x)).abs().max().item() < 3e-2
+
+
+def test_rope_and_paged_cache_write():
+    ops, ref = sub("ops"), sub("ops.reference")
+    torch.manual_seed(0)
+    T, nq, nkv, D, page = 50, 8, 2, 128, 16
+    cs = ops.rope_cos_sin(4096, D, 500000.0, "cuda")
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda").to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), device="cuda", dtype=torch.int32)
+    blocks = 8
+    kc = torch.zeros(blocks, nkv, page, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(blocks * page, device="cuda")[:T].to(torch.int64)
+    q = ops.rope_and_cache(qkv, pos, cs, nq, nkv, slots, kc, vc)
+    q_ref = ref.rope(qkv[:, : nq * D].view(T, nq, D), pos, cs)
+    k_ref = ref.rope(qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D), pos, cs)
+    v_ref = qkv[:, (nq + nkv) * D:].view(T, nkv, D)
+    assert (q.float() - q_ref).abs().max().item() < 3e-2
+    blk, off = slots // page, slots % page
+    assert (kc[blk, :, off, :].float() - k_ref).abs().max().item() < 3e-2
+    assert torch.equal(vc[blk, :, off, :], v_ref)
+
+
+def test_vocab_parallel_embedding():
+    ops = sub("ops")
+    table = torch.randn(1000, 256, device="cuda").to(torch.bfloat16)
+    ids = torch.tensor([0, 999, 1000, 1500, 2999, 5], device="cuda", dtype=torch.int32)
+    out = ops.embedding(ids, table, start=1000)  # shard holds ids [1000, 2000)
+    assert torch.equal(out[2], table[0]) and torch.equal(out[3], table[500])
+    assert out[0].abs().sum() == 0 and out[4].abs().sum() == 0
+
+
+def test_argmax_and_combine():
+    ops = sub("ops")
+    torch.manual_seed(3)
+    W, B, V = 4, 9, 5000
+    logits = torch.randn(W, B, V, device="cuda").to(torch.bfloat16)
+    vals, idxs = [], []
+    for r in range(W):
+        v, i = ops.argmax(logits[r], offset=r * V)
+        vals.append(v)
+        idxs.append(i)
+    best = ops.argmax_combine(torch.stack(vals), torch.stack(idxs))
+    full = logits.permute(1, 0, 2).reshape(B, W * V).float()
+    assert torch.equal(best, full.argmax(-1))
