@@ -45,6 +45,7 @@ ext_modules = [
             src("ops", "elementwise.cu"),
             src("gemm", "gemm.cu"),
             src("attn", "attention.cu"),
+            src("attn", "decode_noalloc.cu"),
         ],
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
