@@ -52,7 +52,7 @@ class CommConfig:
     # NVLS is preferred over two-shot at/above this many bytes
     nvls_min: int = 1 * MiB
     # grid cap of the allreduce kernels (blocks)
-    max_blocks: int = 64
+    max_blocks: int = 148
     # CPU transport: bytes per slot of the shared-memory mailbox
     cpu_slot_bytes: int = 32 * MiB
     cpu_timeout_ms: int = 30_000

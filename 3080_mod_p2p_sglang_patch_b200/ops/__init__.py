@@ -58,7 +58,8 @@ def reserve(device, gemm_elems=0, decode_o=0, decode_lse=0):
 
 
 def gemm_error(device=None) -> int:
-    """Non-zero if a GEMM's bounded wait gave up (sticky until cleared)."""
+    """Non-zero if a tcgen05 kernel's bounded wait gave up (GEMM or prefill
+    attention; sticky until cleared)."""
     return int(workspace(device or torch.cuda.current_device()).err.item())
 
 
@@ -147,20 +148,40 @@ def argmax_combine(vals, idx, out=None):
     return out
 
 
-def prefill_tiles(q_lens, bq: int = 64):
-    """(request, q offset) pairs of the 64-row query tiles of a ragged batch."""
+PREFILL_BQ = 128  # query rows per tile of the tcgen05 prefill kernel
+
+
+def prefill_tiles(q_lens, bq: int = PREFILL_BQ):
+    """(request, q offset) pairs of the query tiles of a ragged batch, the
+    tiles with the most keys first (causal: later tiles see more keys)."""
     tiles = []
     for r, n in enumerate(q_lens):
         for off in range(0, n, bq):
             tiles.append((r, off))
+    tiles.sort(key=lambda t: -t[1])
     return torch.tensor(tiles, dtype=torch.int32).reshape(-1, 2)
 
 
 def prefill_attention(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles, scale=None, out=None):
+    """Causal chunked-prefill attention over the paged cache, tcgen05/TMEM
+    kernel; ``tiles`` from ``prefill_tiles(q_lens)`` (128-row tiles)."""
     if out is None:
         out = torch.empty_like(q)
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
-    cuda_ext().prefill_attention(q, k_cache, v_cache, out, cu_q, kv_len, block_table, tiles, scale)
+    cuda_ext().prefill_attention_tc(q, k_cache, v_cache, out, cu_q, kv_len, block_table, tiles, scale,
+                                    workspace(q.device).err)
+    launches.add(1)
+    return out
+
+
+def prefill_attention_mma(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles64, scale=None, out=None):
+    """The same attention with legacy mma.sync (m16n8k16) tensor-core MMAs;
+    ``tiles64`` from ``prefill_tiles(q_lens, bq=64)``. Kept as the baseline
+    the tcgen05 kernel is measured against."""
+    if out is None:
+        out = torch.empty_like(q)
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    cuda_ext().prefill_attention(q, k_cache, v_cache, out, cu_q, kv_len, block_table, tiles64, scale)
     launches.add(1)
     return out
 

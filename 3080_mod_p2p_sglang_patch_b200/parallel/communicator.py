@@ -40,9 +40,9 @@ logger = logging.getLogger(__name__)
 # dtype ids shared with the kernels (reference numbering, mailbox_ar_ext.cu:123)
 DTYPE_IDS = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
-ALGO_AUTO, ALGO_ONESHOT_PUSH, ALGO_ONESHOT_PULL, ALGO_TWOSHOT, ALGO_NVLS = 0, 1, 2, 3, 4
+ALGO_AUTO, ALGO_ONESHOT_PUSH, ALGO_ONESHOT_PULL, ALGO_TWOSHOT, ALGO_NVLS, ALGO_TWOSHOT_PUSH = 0, 1, 2, 3, 4, 5
 ALGO_NAMES = {ALGO_ONESHOT_PUSH: "oneshot_push", ALGO_ONESHOT_PULL: "oneshot_pull", ALGO_TWOSHOT: "twoshot",
-              ALGO_NVLS: "nvls"}
+              ALGO_NVLS: "nvls", ALGO_TWOSHOT_PUSH: "twoshot_push"}
 ALGO_IDS = {v: k for k, v in ALGO_NAMES.items()}
 
 ERROR_NAMES = {3: "barrier/flag wait timed out", 4: "segment wait timed out", 5: "segment slot-free wait timed out",
@@ -77,8 +77,8 @@ class MailboxAR:
         self.max_size = int(max_size if max_size is not None else self.cfg.max_size)
         self.rank = dist.get_rank(group=group)
         self.world_size = dist.get_world_size(group=group)
-        self.counters = {"oneshot_push": 0, "oneshot_pull": 0, "twoshot": 0, "nvls": 0, "cpu": 0, "fallback": 0,
-                         "errors": 0, "fused": 0, "allgather": 0}
+        self.counters = {"oneshot_push": 0, "oneshot_pull": 0, "twoshot": 0, "twoshot_push": 0, "nvls": 0, "cpu": 0,
+                         "fallback": 0, "errors": 0, "fused": 0, "allgather": 0}
         self._buf = None
         self._ar = None
         self._cpu = None
@@ -216,7 +216,7 @@ class MailboxAR:
             return ALGO_ONESHOT_PUSH
         if self._buf is not None and self._buf.mc_ptr and nbytes >= self.cfg.nvls_min and self.world_size >= 4:
             return ALGO_NVLS
-        return ALGO_TWOSHOT
+        return ALGO_TWOSHOT_PUSH
 
     # ------------------------------------------------------------------ calls
     def _check_error(self):

@@ -82,7 +82,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--graph", action="store_true", help="also time CUDA-graph replays")
     ap.add_argument("--graph-replays", type=int, default=1000)
-    ap.add_argument("--algos", default="auto,oneshot_push,oneshot_pull,twoshot,nvls,nccl")
+    ap.add_argument("--algos", default="auto,oneshot_push,oneshot_pull,twoshot,twoshot_push,nvls,nccl")
     ap.add_argument("--reference", action="store_true")
     ap.add_argument("--max-bytes", type=int, default=256 << 20)
     ap.add_argument("--out", default=None)

@@ -28,7 +28,7 @@
 
 namespace mbx {
 
-enum Algo : int { kAuto = 0, kOneShotPush = 1, kOneShotPull = 2, kTwoShot = 3, kNvls = 4 };
+enum Algo : int { kAuto = 0, kOneShotPush = 1, kOneShotPull = 2, kTwoShot = 3, kNvls = 4, kTwoShotPush = 5 };
 
 constexpr int kArThreads = 512;
 
@@ -89,6 +89,7 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, co
     char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
     for (uint64_t i = i0; i < nvec; i += stride) st_v4(mine + i * 16, ld_nc_v4(in + i));
     if (block_barrier(c, 0, epoch, &s_ok)) {
+#pragma unroll 2
       for (uint64_t i = i0; i < nvec; i += stride) {
         uint4 v[W];
 #pragma unroll
@@ -159,6 +160,105 @@ done:
 }
 
 // --------------------------------------------------------------------------
+// Two-shot, push-push: every NVLink byte is a posted store.
+//   A: element i of chunk ch is stored into owner ch's slot[rank]
+//   B: the owner sums its W slots locally (rank order) and stores the result
+//      into every rank's result region (slot of chunk ch)
+//   C: each rank copies the result region to `out` (local reads)
+// Region A = W slots of cs vectors, region B = W chunks of cs vectors.
+// --------------------------------------------------------------------------
+constexpr int kU = 4;  // vectors in flight per thread per loop trip
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                     uint4* __restrict__ out, uint64_t nvec) {
+  __shared__ bool s_ok;
+  const uint32_t epoch = call_epoch(c);
+  if (!poisoned(c)) {
+    const uint64_t cs = (nvec + W - 1) / W;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t o0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+    // A: push every chunk's share to its owner
+#pragma unroll 1
+    for (int j = 0; j < W; ++j) {
+      const int ch = (c.rank + j) % W;
+      const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
+      char* dst = data_half(c.bufs[ch], epoch, c.half_bytes) + (uint64_t)c.rank * cs * 16;
+      for (uint64_t i = beg + o0; i < end; i += stride * kU) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint64_t k = i + u * stride;
+          if (k < end) v[u] = ld_nc_v4(in + k);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint64_t k = i + u * stride;
+          if (k < end) st_v4(dst + (k - beg) * 16, v[u]);
+        }
+      }
+    }
+    if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    {
+      // B: reduce the own chunk, broadcast the result
+      const uint64_t beg = c.rank * cs, end = min(nvec, beg + cs);
+      const uint64_t resoff = (uint64_t)W * cs * 16 + (uint64_t)c.rank * cs * 16;
+      for (uint64_t i = beg + o0; i < end; i += stride * kU) {
+        uint4 s4[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint64_t k = i + u * stride;
+          if (k < end) {
+            uint4 v[W];
+#pragma unroll
+            for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + ((uint64_t)r * cs + (k - beg)) * 16);
+            float acc[Pack<T>::N] = {};
+#pragma unroll
+            for (int r = 0; r < W; ++r) unpack_add<T>(v[r], acc);
+            s4[u] = pack_from<T>(acc);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const int r = (c.rank + j) % W;
+          char* dst = data_half(c.bufs[r], epoch, c.half_bytes) + resoff;
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const uint64_t k = i + u * stride;
+            if (k < end) st_v4(dst + (k - beg) * 16, s4[u]);
+          }
+        }
+      }
+    }
+    if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    {
+      // C: gather locally
+      const char* res = mine + (uint64_t)W * cs * 16;
+#pragma unroll 1
+      for (int ch = 0; ch < W; ++ch) {
+        const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
+        for (uint64_t i = beg + o0; i < end; i += stride * kU) {
+          uint4 v[kU];
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const uint64_t k = i + u * stride;
+            if (k < end) v[u] = ld_cg_v4(res + k * 16);
+          }
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const uint64_t k = i + u * stride;
+            if (k < end) out[k] = v[u];
+          }
+        }
+      }
+    }
+  }
+done:
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
 // NVLS: multimem.ld_reduce (switch-side sum, fp32 accumulation for 16-bit
 // types) + multimem.st broadcast of the owner's chunk.
 // --------------------------------------------------------------------------
@@ -219,9 +319,18 @@ __global__ void __launch_bounds__(kArThreads) ar_nvls_kernel(ArCtx c, const uint
     fence_proxy_alias();
     {
       const uint64_t beg = c.rank * cs, end = min(nvec, beg + cs);
-      for (uint64_t i = beg + o0; i < end; i += stride) {
-        const uint4 s = multimem_ld_reduce<T>(mc + i * 16);
-        multimem_st(mc + slot1 + i * 16, s);
+      for (uint64_t i = beg + o0; i < end; i += stride * kU) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint64_t k = i + u * stride;
+          if (k < end) v[u] = multimem_ld_reduce<T>(mc + k * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint64_t k = i + u * stride;
+          if (k < end) multimem_st(mc + slot1 + k * 16, v[u]);
+        }
       }
     }
     fence_proxy_alias();
@@ -578,6 +687,7 @@ uint64_t ar_chunk_limit(const ArCtx& c, int algo) {
     case kOneShotPull: return c.half_bytes & ~uint64_t(15);
     case kTwoShot:
     case kNvls: return (c.half_bytes / 2) & ~uint64_t(15);
+    case kTwoShotPush: return ((c.half_bytes / 2 - 16 * (uint64_t)c.world) / 16) * 16;
   }
   return 0;
 }
@@ -606,6 +716,7 @@ void ar_launch(const ArCtx& c, int algo, int dtype, const void* in, void* out, u
       const int g = ar_grid((nvec + W_ - 1) / W_, max_blocks);
       MBX_DISPATCH_T(dtype, MBX_DISPATCH_W(W_, {
         if (algo == kTwoShot) ar_twoshot_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+        else if (algo == kTwoShotPush) ar_twoshot_push_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
         else ar_nvls_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
       }));
     }

@@ -24,7 +24,7 @@ namespace mbx {
 
 
 constexpr int kMaxRanks = 8;
-constexpr int kMaxBlocks = 128;
+constexpr int kMaxBlocks = 256;
 constexpr int kPhases = 4;
 constexpr int kSegSlots = 3;
 constexpr int kTileFlagSlots = 4096;  // row-block flags for the fused GEMM epilogues

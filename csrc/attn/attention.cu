@@ -7,8 +7,9 @@
 //    O += PV with m16n8k16 bf16 tensor-core MMAs and an online softmax in
 //    fp32 (exp2 domain). Query i of a request with kv_len L and q_len Lq sits
 //    at position L - Lq + i and attends keys 0..that position.
-//  * decode_attention: one query per request; the request's keys are split
-//    across blocks (split-KV) for parallelism at small batch, each split
+//  * decode_attention: one query per request, GQA heads packed as the rows of
+//    one tensor-core tile so each KV page is read once; the request's keys are
+//    split across blocks (split-KV) for parallelism at small batch, each split
 //    writes a normalised partial output and its log-sum-exp, and a combine
 //    kernel merges the splits (LSE-weighted). A single split writes the
 //    output directly.
@@ -281,6 +282,13 @@ __global__ void __launch_bounds__(kAttnThreads) prefill_attention_kernel(Prefill
 }
 
 // ------------------------------------------------------------------- decode
+// One query token per request. The G = nq/nkv query heads that share a KV head
+// form the rows of one 16-row m16n8k16 tile (rows >= G are zero), so each KV
+// page is read once per (request, kv head). A block of 4 warps handles one
+// split of the request's keys; each warp streams its own pages (16 keys x 128
+// dims, 4 KB of K + 4 KB of V) through a 3-stage cp.async ring, computes
+// S = Q K^T and O += P V with tensor-core MMAs and keeps an online softmax;
+// the warps then merge (m, l, O) through shared memory.
 struct DecodeArgs {
   const __nv_bfloat16* q;   // [B, nq, D]
   const __nv_bfloat16* kc;
@@ -294,133 +302,200 @@ struct DecodeArgs {
   float scale_log2;
 };
 
-constexpr int kDecThreads = 128;
-constexpr int kMaxG = 8;
+constexpr int kDecWarps = 4;
+constexpr int kDecThreads = kDecWarps * 32;
+constexpr int kDecStages = 3;
+constexpr int kPageBytes = PAGE * D * 2;               // 4 KB
+constexpr int kDecStageBytes = 2 * kPageBytes;         // K + V page
+constexpr int kDecSmem = kDecWarps * kDecStages * kDecStageBytes;  // 96 KB
+constexpr int kMaxG = 16;
+
+MBX_DEVICE void load_page(uint32_t dst, const __nv_bfloat16* base, int lane) {
+  // 16 rows x 16 chunks of 16 B, 8 per lane, swizzled like the prefill tiles
+#pragma unroll
+  for (int i = 0; i < (PAGE * 16) / 32; ++i) {
+    const int idx = lane + i * 32;
+    const int row = idx >> 4, chunk = idx & 15;
+    cp_async16(dst + swz(row, chunk), base + row * D + chunk * 8);
+  }
+}
 
 __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(DecodeArgs a) {
-  __shared__ float sq[kMaxG][D];
-  __shared__ float sp[kMaxG][kDecThreads];
-  __shared__ float sred[kMaxG][4];
-  __shared__ float so[kMaxG][2][D];
+  extern __shared__ __align__(128) uint8_t dsm[];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = a.nq / a.nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
   const int L = a.kv_len[b];
-  const int chunk = ((L + a.splits - 1) / a.splits + PAGE - 1) / PAGE * PAGE;
-  const int k_begin = split * chunk, k_end = min(L, k_begin + chunk);
+  const int pages = (L + PAGE - 1) / PAGE;
+  const int per = (pages + a.splits - 1) / a.splits;
+  const int p_begin = split * per, p_end = min(pages, p_begin + per);
   const int* bt = a.block_table + (int64_t)b * a.max_blocks;
-  const int t = threadIdx.x;
-  for (int i = t; i < G * D; i += kDecThreads) {
-    const int h = i / D, d = i % D;
-    sq[h][d] = __bfloat162float(a.q[((int64_t)b * a.nq + kvh * G + h) * D + d]) * a.scale_log2;
+  const uint32_t ring = smem_addr(dsm) + warp * kDecStages * kDecStageBytes;
+
+  // Q fragments (16 rows = heads kvh*G .. +G-1; rows >= G zero), 8 k-steps
+  uint32_t qf[8][4];
+  {
+    const __nv_bfloat16* qb = a.q + ((int64_t)b * a.nq + kvh * G) * D;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int c0 = ks * 16 + 2 * t4;
+      qf[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * D + c0) : 0u;
+      qf[ks][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + c0) : 0u;
+      qf[ks][2] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * D + c0 + 8) : 0u;
+      qf[ks][3] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + c0 + 8) : 0u;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+
+  // pages of this warp: p_begin + warp, + kDecWarps, ...
+  auto page_src = [&](int p, const __nv_bfloat16* cache) {
+    return cache + (((int64_t)bt[p] * a.nkv + kvh) * PAGE) * D;
+  };
+  int issue = p_begin + warp;
+#pragma unroll
+  for (int st = 0; st < kDecStages - 1; ++st) {
+    if (issue < p_end) {
+      const uint32_t dst = ring + st * kDecStageBytes;
+      load_page(dst, page_src(issue, a.kc), lane);
+      load_page(dst + kPageBytes, page_src(issue, a.vc), lane);
+    }
+    cp_async_commit();
+    issue += kDecWarps;
+  }
+  int stage = 0;
+  for (int p = p_begin + warp; p < p_end; p += kDecWarps) {
+    {  // keep the ring full
+      const int st = (stage + kDecStages - 1) % kDecStages;
+      if (issue < p_end) {
+        const uint32_t dst = ring + st * kDecStageBytes;
+        load_page(dst, page_src(issue, a.kc), lane);
+        load_page(dst + kPageBytes, page_src(issue, a.vc), lane);
+      }
+      cp_async_commit();
+      issue += kDecWarps;
+    }
+    cp_async_wait<kDecStages - 1>();
+    __syncwarp();
+    const uint32_t sK = ring + stage * kDecStageBytes;
+    const uint32_t sV = sK + kPageBytes;
+    // S = Q K^T: 16 rows x 16 keys (2 n-tiles)
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int key = (lane & 7) + 8 * (lane >> 4);
+      const int chunk = ks * 2 + ((lane >> 3) & 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(sK + swz(key, chunk), b0, b1, b2, b3);
+      mma16816(s[0], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+      mma16816(s[1], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b2, b3);
+    }
+    const int key0 = p * PAGE;
+    float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key0 + j * 8 + 2 * t4 + (e & 1);
+        const float v = key < L ? s[j][e] * a.scale_log2 : -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    }
+    float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      corr[h] = (mx[h] == -INFINITY) ? 1.f : exp2f(m_r[h] - mx[h]);
+      m_r[h] = mx[h];
+    }
+    uint32_t pf[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float pv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mm = m_r[e >> 1];
+        pv[e] = (mm == -INFINITY) ? 0.f : exp2f(s[j][e] - mm);
+        rs[e >> 1] += pv[e];
+      }
+      pf[j * 2 + 0] = pack_bf16(pv[0], pv[1]);
+      pf[j * 2 + 1] = pack_bf16(pv[2], pv[3]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      l_r[h] = l_r[h] * corr[h] + rs[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= corr[0];
+      o[j][1] *= corr[0];
+      o[j][2] *= corr[1];
+      o[j][3] *= corr[1];
+    }
+    // O += P V (16 keys = one k-step), 8 pairs of dim n-tiles
+#pragma unroll
+    for (int jn = 0; jn < 8; ++jn) {
+      const int key = (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int chunk = jn * 2 + (lane >> 4);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(sV + swz(key, chunk), b0, b1, b2, b3);
+      mma16816(o[2 * jn], pf[0], pf[1], pf[2], pf[3], b0, b1);
+      mma16816(o[2 * jn + 1], pf[0], pf[1], pf[2], pf[3], b2, b3);
+    }
+    __syncwarp();
+    stage = (stage + 1) % kDecStages;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // merge the warps' states: smem [warp][16 rows][D] fp32 + m, l per row
+  float* so = reinterpret_cast<float*>(dsm);                 // 4 * 16 * 128 * 4 = 32 KB
+  float* sm = so + kDecWarps * 16 * D;                       // [warp][16]
+  float* sl = sm + kDecWarps * 16;                           // [warp][16]
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int col = j * 8 + 2 * t4;
+    so[(warp * 16 + g) * D + col] = o[j][0];
+    so[(warp * 16 + g) * D + col + 1] = o[j][1];
+    so[(warp * 16 + g + 8) * D + col] = o[j][2];
+    so[(warp * 16 + g + 8) * D + col + 1] = o[j][3];
+  }
+  if (t4 == 0) {
+    sm[warp * 16 + g] = m_r[0];
+    sm[warp * 16 + g + 8] = m_r[1];
+    sl[warp * 16 + g] = l_r[0];
+    sl[warp * 16 + g + 8] = l_r[1];
   }
   __syncthreads();
-  float m[kMaxG], l[kMaxG], acc[kMaxG][2];
+  for (int i = threadIdx.x; i < G * D; i += kDecThreads) {
+    const int row = i / D, d = i % D;
+    float mm = -INFINITY;
 #pragma unroll
-  for (int h = 0; h < kMaxG; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-    acc[h][0] = acc[h][1] = 0.f;
-  }
-  const int dp = t & 63, kpar = t >> 6;
-  for (int k0 = k_begin; k0 < k_end; k0 += kDecThreads) {
-    // scores: thread t <-> key k0 + t
-    const int key = k0 + t;
-    float sc[kMaxG];
+    for (int w = 0; w < kDecWarps; ++w) mm = fmaxf(mm, sm[w * 16 + row]);
+    float num = 0.f, den = 0.f;
 #pragma unroll
-    for (int h = 0; h < kMaxG; ++h) sc[h] = -INFINITY;
-    if (key < k_end) {
-      const int blk = bt[key / PAGE];
-      const uint4* kr = reinterpret_cast<const uint4*>(a.kc + (((int64_t)blk * a.nkv + kvh) * PAGE + key % PAGE) * D);
-#pragma unroll
-      for (int h = 0; h < kMaxG; ++h) sc[h] = 0.f;
-#pragma unroll 4
-      for (int c = 0; c < 16; ++c) {
-        float kv[8] = {};
-        unpack_add<__nv_bfloat16>(kr[c], kv);
-#pragma unroll
-        for (int h = 0; h < kMaxG; ++h) {
-          if (h < G) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sc[h] += sq[h][c * 8 + j] * kv[j];
-          }
-        }
-      }
+    for (int w = 0; w < kDecWarps; ++w) {
+      const float mw = sm[w * 16 + row];
+      const float e = (mw == -INFINITY) ? 0.f : exp2f(mw - mm);
+      num += e * so[(w * 16 + row) * D + d];
+      den += e * sl[w * 16 + row];
     }
-    // per-head max over the 128 keys
-#pragma unroll
-    for (int h = 0; h < kMaxG; ++h) {
-      if (h >= G) break;
-      float v = sc[h];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if ((t & 31) == 0) sred[h][t >> 5] = v;
-    }
-    __syncthreads();
-    float mnew[kMaxG];
-#pragma unroll
-    for (int h = 0; h < kMaxG; ++h) {
-      mnew[h] = m[h];
-      if (h < G) mnew[h] = fmaxf(fmaxf(fmaxf(sred[h][0], sred[h][1]), fmaxf(sred[h][2], sred[h][3])), m[h]);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int h = 0; h < kMaxG; ++h) {
-      if (h >= G) break;
-      const float p = (sc[h] == -INFINITY) ? 0.f : exp2f(sc[h] - mnew[h]);
-      sp[h][t] = p;
-      float v = p;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if ((t & 31) == 0) sred[h][t >> 5] = v;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int h = 0; h < kMaxG; ++h) {
-      if (h >= G) break;
-      const float corr = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mnew[h]);
-      l[h] = l[h] * corr + (sred[h][0] + sred[h][1] + sred[h][2] + sred[h][3]);
-      acc[h][0] *= corr;
-      acc[h][1] *= corr;
-      m[h] = mnew[h];
-    }
-    // PV: thread (dp, kpar) accumulates dims 2dp, 2dp+1 over keys of parity kpar
-    const int nk = min(kDecThreads, k_end - k0);
-    for (int j = kpar; j < nk; j += 2) {
-      const int key2 = k0 + j;
-      const int blk = bt[key2 / PAGE];
-      const __nv_bfloat162 vv = *reinterpret_cast<const __nv_bfloat162*>(
-          a.vc + (((int64_t)blk * a.nkv + kvh) * PAGE + key2 % PAGE) * D + 2 * dp);
-      const float2 vf = __bfloat1622float2(vv);
-#pragma unroll
-      for (int h = 0; h < kMaxG; ++h) {
-        if (h < G) {
-          acc[h][0] += sp[h][j] * vf.x;
-          acc[h][1] += sp[h][j] * vf.y;
-        }
-      }
-    }
-    __syncthreads();
-  }
-  // combine key parities
-#pragma unroll
-  for (int h = 0; h < kMaxG; ++h) {
-    if (h < G) {
-      so[h][kpar][2 * dp] = acc[h][0];
-      so[h][kpar][2 * dp + 1] = acc[h][1];
-    }
-  }
-  __syncthreads();
-  for (int i = t; i < G * D; i += kDecThreads) {
-    const int h = i / D, d = i % D;
-    const float v = so[h][0][d] + so[h][1][d];
-    const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
-    const int qh = kvh * G + h;
+    const int qh = kvh * G + row;
     if (a.splits == 1) {
-      a.o[((int64_t)b * a.nq + qh) * D + d] = __float2bfloat16(v * inv);
+      a.o[((int64_t)b * a.nq + qh) * D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
     } else {
-      a.part_o[(((int64_t)b * a.nq + qh) * a.splits + split) * D + d] = v * inv;
+      a.part_o[(((int64_t)b * a.nq + qh) * a.splits + split) * D + d] = den > 0.f ? num / den : 0.f;
       if (d == 0)
-        a.part_lse[((int64_t)b * a.nq + qh) * a.splits + split] = (l[h] > 0.f) ? m[h] + log2f(l[h]) : -INFINITY;
+        a.part_lse[((int64_t)b * a.nq + qh) * a.splits + split] = (den > 0.f) ? mm + log2f(den) : -INFINITY;
     }
   }
 }
@@ -476,7 +551,7 @@ void decode_attention_launch(const void* q, const void* kc, const void* vc, void
                              const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
                              float* part_o, float* part_lse, float scale, cudaStream_t s) {
   if (B == 0) return;
-  if (nq % nkv != 0 || nq / nkv > kMaxG) throw std::runtime_error("decode: group size must be <= 8");
+  if (nq % nkv != 0 || nq / nkv > kMaxG) throw std::runtime_error("decode: group size must be <= 16");
   DecodeArgs a;
   a.q = (const __nv_bfloat16*)q;
   a.kc = (const __nv_bfloat16*)kc;
@@ -492,8 +567,13 @@ void decode_attention_launch(const void* q, const void* kc, const void* vc, void
   a.part_o = part_o;
   a.part_lse = part_lse;
   if (a.splits > 1 && (!part_o || !part_lse)) throw std::runtime_error("decode: split-KV needs scratch buffers");
+  static bool attr = false;
+  if (!attr) {
+    MBX_CUDA_CHECK(cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem));
+    attr = true;
+  }
   dim3 grid(a.splits, nkv, B);
-  decode_attention_kernel<<<grid, kDecThreads, 0, s>>>(a);
+  decode_attention_kernel<<<grid, kDecThreads, kDecSmem, s>>>(a);
   MBX_CUDA_CHECK(cudaGetLastError());
   if (a.splits > 1) {
     decode_combine_kernel<<<B * nq, D, 0, s>>>(a.part_o, a.part_lse, a.splits, a.o);

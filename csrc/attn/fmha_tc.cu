@@ -1,0 +1,423 @@
+// Prefill attention on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA = 128 query rows of one q-head. For every 128-key tile of the
+// request's paged KV cache:
+//   S_j  = Q K_j^T      tcgen05.mma (M=128, N=128, K=128 head dims), fp32 in
+//                       TMEM, double-buffered (S_{j+1} overlaps softmax_j)
+//   P_j  = exp2(S_j*scale - m)   online softmax by 4 warps (one row per
+//                       thread, tcgen05.ld of the S row), written as bf16 to
+//                       shared memory in the canonical K-major 128B-swizzled
+//                       layout; the running output is rescaled in TMEM
+//                       (tcgen05.ld/st) when a row's max grows
+//   O   += P_j V_j      tcgen05.mma with V read MN-major (dims contiguous, as
+//                       stored in the cache), fp32 accumulator in TMEM
+// Warp roles (192 threads): warp 0 TMA producer (Q once; K/V pages of 16
+// keys x 64 dims per box, double-buffered stages), warp 1 TMEM allocator +
+// single-thread MMA issuer, warps 2-5 softmax + epilogue. No cluster
+// multicast. Causal masking / kv-length masking per element in softmax.
+// Every mbarrier wait is bounded; on timeout the CTA records an error, drains
+// its in-flight copies and MMAs, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <functional>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+
+#include "../gemm/tcgen05.cuh"
+#include "../kernels.h"
+
+namespace mbx {
+namespace {
+
+constexpr int D = 128;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int PAGE = 16;
+constexpr int kThreads = 192;
+constexpr int kTileBytes = BQ * D * 2;  // 32 KB: one [128 x 128] bf16 tile (two 16 KB column chunks)
+constexpr int kChunk = 16384;           // [128 rows x 64] bf16
+
+struct FmhaArgs {
+  __nv_bfloat16* o;         // [T, nq, D]
+  const int* cu_q;          // [R+1]
+  const int* kv_len;        // [R]
+  const int* block_table;   // [R, max_blocks]
+  const int2* tiles;        // (request, q offset), 128-row tiles
+  int max_blocks, nq, nkv;
+  float scale_log2;
+  uint32_t* err;
+  uint64_t timeout_ns;
+};
+
+struct Smem {
+  static constexpr int kQ = 0;
+  static constexpr int kK0 = kQ + kTileBytes;
+  static constexpr int kV0 = kK0 + 2 * kTileBytes;
+  static constexpr int kP = kV0 + 2 * kTileBytes;
+  static constexpr int kBar = kP + kTileBytes;
+  static constexpr int kTotal = kBar + 256 + 1024;
+};
+
+MBX_DEVICE void set_err(uint32_t* err, uint32_t code, volatile int* abort) {
+  *abort = 1;
+  if (err) atomicCAS(err, 0u, code);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, FmhaArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::kBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;
+  uint64_t* o_done = bars + 8;
+  uint64_t* mma_done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int2 tile = a.tiles[blockIdx.x];
+  const int r = tile.x, qoff = tile.y;
+  const int head = blockIdx.y;
+  const int kvh = head / (a.nq / a.nkv);
+  const int q_begin = a.cu_q[r], q_len = a.cu_q[r + 1] - q_begin;
+  const int L = a.kv_len[r];
+  const int pos0 = L - q_len;
+  const int rows_here = min(BQ, q_len - qoff);
+  const int kv_end = min(L, pos0 + qoff + rows_here);  // causal bound of the tile
+  const int n_tiles = (kv_end + BKV - 1) / BKV;
+  const int* bt = a.block_table + (int64_t)r * a.max_blocks;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&kv_full[i], 1);
+      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&s_full[i], 1);
+    }
+    tc::mbar_init(p_full, 4);
+    tc::mbar_init(o_done, 1);
+    tc::mbar_init(mma_done, 1);
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;         // S buffers: columns [0,128) and [128,256)
+  const uint32_t tO = tmem + 256;   // O: columns [256,384)
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (tc::elect_one()) {
+      tc::tma_prefetch_desc(&tmQ);
+      tc::tma_prefetch_desc(&tmK);
+      tc::tma_prefetch_desc(&tmV);
+      tc::mbar_arrive_expect_tx(q_full, kTileBytes);
+      for (int c = 0; c < 2; ++c)
+        tc::tma_load_3d(smem + Smem::kQ + c * kChunk, &tmQ, q_full, c * 64, head, q_begin + qoff);
+      const int last_page = (kv_end - 1) / PAGE;
+      int issued = 0;
+      for (int j = 0; j < n_tiles && !*abort; ++j, ++issued) {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, a.timeout_ns)) {
+          set_err(a.err, 11, abort);
+          break;
+        }
+        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        uint8_t* sk = smem + Smem::kK0 + s * kTileBytes;
+        uint8_t* sv = smem + Smem::kV0 + s * kTileBytes;
+#pragma unroll 1
+        for (int p = 0; p < BKV / PAGE; ++p) {
+          const int page = min(j * (BKV / PAGE) + p, last_page);  // clamp: masked keys read finite data
+          const int blk = bt[page];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tc::tma_load_4d(sk + c * kChunk + p * (PAGE * 128), &tmK, &kv_full[s], c * 64, 0, kvh, blk);
+            tc::tma_load_4d(sv + c * kChunk + p * (PAGE * 128), &tmV, &kv_full[s], c * 64, 0, kvh, blk);
+          }
+        }
+      }
+      // drain this thread's in-flight copies before the CTA can exit
+      volatile int never = 0;
+      tc::mbar_wait(q_full, 0, &never, 200000000ull);
+      for (int j = max(0, issued - 2); j < issued; ++j)
+        tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1, &never, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (tc::elect_one()) {
+      constexpr uint32_t idS = tc::idesc_bf16_f32_major(BQ, BKV, 0, 0);  // Q K-major, K K-major
+      constexpr uint32_t idO = tc::idesc_bf16_f32_major(BQ, D, 0, 1);    // P K-major, V MN-major
+      const uint32_t sQ = tc::smem_u32(smem + Smem::kQ);
+      const uint32_t sP = tc::smem_u32(smem + Smem::kP);
+      bool ok = tc::mbar_wait(q_full, 0, abort, a.timeout_ns);
+      if (!ok) set_err(a.err, 12, abort);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&kv_full[s], (j >> 1) & 1, abort, a.timeout_ns)) {
+          set_err(a.err, 12, abort);
+          return false;
+        }
+        tc::tc_fence_after();
+        const uint32_t sK = tc::smem_u32(smem + Smem::kK0 + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
+          tc::mma_bf16(tS + s * BKV, tc::sw128_desc(sQ + off, 16, 1024), tc::sw128_desc(sK + off, 16, 1024), idS,
+                       kk > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&s_full[s]);
+        return true;
+      };
+      if (ok && n_tiles > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        if (!tc::mbar_wait(p_full, j & 1, abort, a.timeout_ns)) {
+          set_err(a.err, 12, abort);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t sV = tc::smem_u32(smem + Smem::kV0 + (j & 1) * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint32_t poff = (kk >> 2) * kChunk + (kk & 3) * 32;  // P: keys along K, 2 chunks of 64
+          const uint32_t voff = kk * 16 * 128;                        // V: 16 key rows of 128 B per step
+          tc::mma_bf16(tO, tc::sw128_desc(sP + poff, 16, 1024), tc::sw128_desc(sV + voff, kChunk, 1024), idO,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&kv_empty[j & 1]);
+        tc::mma_commit(o_done);
+      }
+      tc::mma_commit(mma_done);
+      volatile int never = 0;
+      tc::mbar_wait(mma_done, 0, &never, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    const int q_pos = pos0 + qoff + row;
+    const float sc = a.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    uint8_t* sP = smem + Smem::kP;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (!tc::mbar_wait(&s_full[s], (j >> 1) & 1, abort, a.timeout_ns)) {
+        if (lane == 0) set_err(a.err, 13, abort);
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      uint32_t v[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t t[32];
+        tc::tmem_ld_32x32b_x32(tS + lane_addr + s * BKV + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[c * 32 + i] = t[i];
+      }
+      tc::tmem_ld_wait();
+      const int kv0 = j * BKV;
+      const int lim = min(q_pos + 1, kv_end) - kv0;  // keys [kv0, kv0+lim) are visible to this row
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < BKV; ++i) {
+        float x = __uint_as_float(v[i]) * sc;
+        x = (i < lim) ? x : -INFINITY;
+        v[i] = __float_as_uint(x);
+        mx = fmaxf(mx, x);
+      }
+      const float corr = (m == -INFINITY) ? 1.f : tc::ex2(m - mx);
+      float sum = 0.f;
+      uint32_t pk[BKV / 2];
+#pragma unroll
+      for (int i = 0; i < BKV; i += 2) {
+        const float p0 = (mx == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i]) - mx);
+        const float p1 = (mx == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i + 1]) - mx);
+        sum += p0 + p1;
+        __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+        pk[i / 2] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      l = l * corr + sum;
+      m = mx;
+      if (j > 0) {
+        // PV_{j-1} must be complete before O is rescaled and P is overwritten
+        if (!tc::mbar_wait(o_done, (j - 1) & 1, abort, a.timeout_ns)) {
+          if (lane == 0) set_err(a.err, 13, abort);
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        if (__any_sync(0xffffffffu, corr < 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t t[32];
+            tc::tmem_ld_32x32b_x32(tO + lane_addr + c * 32, t);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
+            tc::tmem_st_32x32b_x32(tO + lane_addr + c * 32, t);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      // P row -> shared memory, K-major 128B-swizzled (keys 0-63 in chunk 0, 64-127 in chunk 1)
+#pragma unroll
+      for (int c = 0; c < BKV / 8; ++c) {
+        const int kb = c >> 3, cc = c & 7;
+        uint8_t* dst = sP + kb * kChunk + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0) {
+      if (!tc::mbar_wait(o_done, (n_tiles - 1) & 1, abort, a.timeout_ns)) {
+        if (lane == 0) set_err(a.err, 13, abort);
+      } else {
+        tc::tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* dst = a.o + ((int64_t)(q_begin + qoff + row) * a.nq + head) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t t[32];
+          tc::tmem_ld_32x32b_x32(tO + lane_addr + c * 32, t);
+          tc::tmem_ld_wait();
+          if (row < rows_here) {
+            float f[8];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(t[g * 8 + i]) * inv;
+              *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = pack_from<__nv_bfloat16>(f);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled unavailable (no CUDA driver)");
+  return fn;
+}
+
+CUtensorMap encode(const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                   const cuuint32_t* box) {
+  if (((uint64_t)base & 15) != 0) throw std::runtime_error("fmha: tensor base must be 16-byte aligned");
+  CUtensorMap m;
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult res = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_bytes,
+                             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) throw std::runtime_error("fmha: cuTensorMapEncodeTiled failed " + std::to_string((int)res));
+  return m;
+}
+
+struct Key {
+  uint64_t p, a, b, c;
+  bool operator==(const Key& o) const { return p == o.p && a == o.a && b == o.b && c == o.c; }
+};
+struct KeyHash {
+  size_t operator()(const Key& k) const {
+    return (size_t)(k.p * 0x9E3779B97F4A7C15ull ^ (k.a << 1) ^ (k.b << 21) ^ (k.c << 41));
+  }
+};
+std::mutex g_mu;
+std::unordered_map<Key, CUtensorMap, KeyHash> g_maps;
+
+CUtensorMap cached(const Key& k, const std::function<CUtensorMap()>& make) {
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    auto it = g_maps.find(k);
+    if (it != g_maps.end()) return it->second;
+  }
+  CUtensorMap m = make();
+  std::lock_guard<std::mutex> g(g_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(k, m);
+  return m;
+}
+
+}  // namespace
+
+void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
+                                 const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
+                                 int n_tiles, int T, int nq, int nkv, int num_blocks, float scale, uint32_t* err,
+                                 cudaStream_t s) {
+  if (n_tiles == 0 || T == 0) return;
+  if (nq % nkv != 0) throw std::runtime_error("fmha: nq must be a multiple of nkv");
+  // Q: [T, nq, D] -> dims {D, nq, T}, box {64, 1, 128}
+  const CUtensorMap tq = cached(Key{(uint64_t)q, (uint64_t)T, (uint64_t)nq, 1}, [&] {
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)nq, (cuuint64_t)T};
+    cuuint64_t str[2] = {(cuuint64_t)D * 2, (cuuint64_t)nq * D * 2};
+    cuuint32_t box[3] = {64, 1, BQ};
+    return encode(q, 3, dims, str, box);
+  });
+  // K/V cache: [blocks, nkv, PAGE, D] -> dims {D, PAGE, nkv, blocks}, box {64, PAGE, 1, 1}
+  auto cache_map = [&](const void* base) {
+    return cached(Key{(uint64_t)base, (uint64_t)num_blocks, (uint64_t)nkv, 2}, [&] {
+      cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)PAGE, (cuuint64_t)nkv, (cuuint64_t)num_blocks};
+      cuuint64_t str[3] = {(cuuint64_t)D * 2, (cuuint64_t)PAGE * D * 2, (cuuint64_t)nkv * PAGE * D * 2};
+      cuuint32_t box[4] = {64, PAGE, 1, 1};
+      return encode(base, 4, dims, str, box);
+    });
+  };
+  const CUtensorMap tk = cache_map(kc);
+  const CUtensorMap tv = cache_map(vc);
+  FmhaArgs a;
+  a.o = static_cast<__nv_bfloat16*>(o);
+  a.cu_q = cu_q;
+  a.kv_len = kv_len;
+  a.block_table = block_table;
+  a.tiles = reinterpret_cast<const int2*>(tiles);
+  a.max_blocks = max_blocks;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = err;
+  a.timeout_ns = 2000000000ull;
+  static bool attr = false;
+  if (!attr) {
+    MBX_CUDA_CHECK(cudaFuncSetAttribute(fmha_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kTotal));
+    attr = true;
+  }
+  dim3 grid(n_tiles, nq);
+  fmha_tc_kernel<<<grid, kThreads, Smem::kTotal, s>>>(tq, tk, tv, a);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace mbx

@@ -232,6 +232,29 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
                            cur_stream());
 }
 
+void prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor out,
+                          torch::Tensor cu_q, torch::Tensor kv_len, torch::Tensor block_table, torch::Tensor tiles,
+                          double scale, torch::Tensor err) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_bf16(k_cache, "k_cache");
+  check_bf16(v_cache, "v_cache");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128, "q must be [T, nq, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.size(3) == 128,
+              "k_cache must be [blocks, nkv, 16, 128]");
+  for (auto* t : {&cu_q, &kv_len, &block_table, &tiles}) {
+    check_cuda(*t, "index tensor");
+    TORCH_CHECK(t->scalar_type() == torch::kInt32, "index tensors must be int32");
+  }
+  TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 2, "tiles must be [n, 2]");
+  TORCH_CHECK(err.scalar_type() == torch::kInt32 && err.is_cuda(), "err must be an int32 CUDA word");
+  prefill_attention_tc_launch(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+                              cu_q.data_ptr<int>(), kv_len.data_ptr<int>(), block_table.data_ptr<int>(),
+                              block_table.size(1), tiles.data_ptr<int>(), tiles.size(0), q.size(0), q.size(1),
+                              k_cache.size(1), k_cache.size(0), (float)scale,
+                              reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
+}
+
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor out,
                       torch::Tensor kv_len, torch::Tensor block_table, c10::optional<torch::Tensor> part_o,
                       c10::optional<torch::Tensor> part_lse, int64_t splits, double scale) {
@@ -340,5 +363,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("argmax_combine", &argmax_combine);
   m.def("prefill_attention", &prefill_attention);
+  m.def("prefill_attention_tc", &prefill_attention_tc);
   m.def("decode_attention", &decode_attention);
 }

@@ -52,6 +52,11 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 void prefill_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
                               const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
                               int n_tiles, int nq, int nkv, float scale, cudaStream_t s);
+// tcgen05/TMEM prefill attention (128-row query tiles, 128-key tiles).
+void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
+                                 const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
+                                 int n_tiles, int T, int nq, int nkv, int num_blocks, float scale, uint32_t* err,
+                                 cudaStream_t s);
 void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
                              const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
                              float* part_o, float* part_lse, float scale, cudaStream_t s);

@@ -46,6 +46,7 @@ ext_modules = [
             src("gemm", "gemm.cu"),
             src("attn", "attention.cu"),
             src("attn", "decode_noalloc.cu"),
+            src("attn", "fmha_tc.cu"),
         ],
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},

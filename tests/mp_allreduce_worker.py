@@ -36,7 +36,7 @@ def main():
     ar = comm_mod.MailboxAR(None, dev, config=cfg)
     assert not ar.disabled, "communicator did not come up"
     log(f"transport={ar.transport} world={world}")
-    algos = ["oneshot_push", "oneshot_pull", "twoshot"] + (["nvls"] if "nvls" in ar.transport else [])
+    algos = ["oneshot_push", "oneshot_pull", "twoshot", "twoshot_push"] + (["nvls"] if "nvls" in ar.transport else [])
 
     # 1. bit-exact world*x with identical inputs on every rank, varying sizes
     torch.manual_seed(1234)

@@ -22,20 +22,24 @@ def _paged(lengths, nkv, blocks_per_req, seed=0):
     return kc, vc, bt
 
 
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
 @pytest.mark.parametrize("nq,nkv", [(32, 8), (4, 1), (8, 1)])
-def test_prefill_chunked_ragged(nq, nkv):
+def test_prefill_chunked_ragged(nq, nkv, kernel):
     ops, ref = sub("ops"), sub("ops.reference")
-    kv_lens = [100, 264, 1024]
-    q_lens = [100, 64, 300]          # req 0 fresh, req 1/2 are later chunks
+    kv_lens = [100, 264, 1024, 777]
+    q_lens = [100, 64, 300, 257]     # req 0 fresh, req 1/2/3 are later chunks (unaligned offsets)
     kc, vc, bt = _paged(kv_lens, nkv, 64)
     T = sum(q_lens)
     q = torch.randn(T, nq, D, device="cuda").to(torch.bfloat16)
     cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32, device="cuda")
     kvl = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
-    tiles = ops.prefill_tiles(q_lens).cuda()
-    out = ops.prefill_attention(q, kc, vc, cu, kvl, bt, tiles)
+    if kernel == "tc":
+        out = ops.prefill_attention(q, kc, vc, cu, kvl, bt, ops.prefill_tiles(q_lens).cuda())
+    else:
+        out = ops.prefill_attention_mma(q, kc, vc, cu, kvl, bt, ops.prefill_tiles(q_lens, bq=64).cuda())
     torch.cuda.synchronize()
-    for r in range(3):
+    assert ops.gemm_error() == 0
+    for r in range(len(q_lens)):
         qs = q[cu[r]:cu[r + 1]]
         k = ref.gather_kv(kc, bt[r], kv_lens[r])
         v = ref.gather_kv(vc, bt[r], kv_lens[r])
