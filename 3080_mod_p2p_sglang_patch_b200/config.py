@@ -37,6 +37,9 @@ class CommConfig:
     max_size: int = 256 * MiB
     # one ping-pong data half of the symmetric buffer (two halves are mapped)
     half_bytes: int = 64 * MiB
+    # fused GEMM->allreduce path: one of its two halves (holds W partial slots
+    # plus the reduced rows: 2 * M * N * 2 bytes for an [M, N] bf16 output)
+    fuse_half_bytes: int = 40 * MiB
     # segmented (overlap) path: bytes per slot per source rank (0 disables)
     seg_slot_bytes: int = 8 * MiB
     # bound of every device-side wait (the reference uses ~1 s, mailbox_ar_ext.cu:5)
@@ -47,7 +50,7 @@ class CommConfig:
     nvls: bool = True
     # one-shot (push) is used up to this many bytes, per world size
     oneshot_max: dict = dataclasses.field(
-        default_factory=lambda: {2: 4 * MiB, 3: 1 * MiB, 4: 1 * MiB, 5: 512 << 10, 6: 512 << 10, 7: 512 << 10, 8: 512 << 10}
+        default_factory=lambda: {2: 32 * MiB, 3: 1 * MiB, 4: 1 * MiB, 5: 512 << 10, 6: 512 << 10, 7: 512 << 10, 8: 512 << 10}
     )
     # NVLS is preferred over two-shot at/above this many bytes
     nvls_min: int = 1 * MiB

@@ -181,6 +181,9 @@ class LlamaTP:
                 # residual add fused into the GEMM epilogue, in place
                 self._linear(o.view(T, nq * D), L["o"], out=residual, residual=residual)
                 x = ops.rmsnorm(residual, L["ln2"], cfg.eps)
+            elif self.impl == "native":
+                # fused row-parallel GEMM -> allreduce -> residual + RMSNorm
+                x = self.tp.gemm_all_reduce_rmsnorm(o.view(T, nq * D), L["o"], residual, L["ln2"], cfg.eps)
             else:
                 part = self._linear(o.view(T, nq * D), L["o"])
                 x = self._ar_norm(part, residual, L["ln2"])
@@ -190,6 +193,8 @@ class LlamaTP:
             if self.tp_size == 1 and self.impl == "native":
                 self._linear(a, L["down"], out=residual, residual=residual)
                 x = ops.rmsnorm(residual, nxt, cfg.eps)
+            elif self.impl == "native":
+                x = self.tp.gemm_all_reduce_rmsnorm(a, L["down"], residual, nxt, cfg.eps)
             else:
                 part = self._linear(a, L["down"])
                 x = self._ar_norm(part, residual, nxt)

@@ -127,7 +127,7 @@ class MailboxAR:
     def _buffer_bytes(self):
         C = cuda_ext()
         seg = C.SEG_SLOTS * C.MAX_RANKS * self.cfg.seg_slot_bytes
-        return C.SIG_BYTES + 2 * self.cfg.half_bytes + seg
+        return C.SIG_BYTES + 2 * self.cfg.half_bytes + 2 * self.cfg.fuse_half_bytes + seg
 
     def _setup_gpu(self):
         from .symm import SymmetricBuffer
@@ -140,7 +140,7 @@ class MailboxAR:
         self._status = C.host_mapped_alloc(4 * C.STATUS_WORDS)
         self._ar = C.ArComm(self.rank, self.world_size, list(self._buf.ptrs), int(self._buf.mc_ptr),
                             self._state.data_ptr(), self._status.dev, self._status.host, self.cfg.half_bytes,
-                            self.cfg.seg_slot_bytes, self.cfg.timeout_ns)
+                            self.cfg.seg_slot_bytes, self.cfg.timeout_ns, self.cfg.fuse_half_bytes)
         torch.cuda.synchronize(self.device)
         self.mbx = self._buf.local_ptr
         self.peer_mbx = self._buf.ptrs[(self.rank + 1) % self.world_size]
@@ -296,6 +296,31 @@ class MailboxAR:
                             self.cfg.max_blocks, torch.cuda.current_stream(self.device).cuda_stream)
         self.counters["fused"] += 1
         launches.add(1)
+        return out
+
+    def fused_gemm_fits(self, M: int, N: int) -> bool:
+        """Whether an [M, N] bf16 output fits the fused GEMM->allreduce buffer."""
+        if self._ar is None:
+            return False
+        Mo = -(-M // self.world_size)
+        return self.world_size * Mo * N * 2 + M * N * 2 <= self._ar.fused_capacity() and N % 8 == 0
+
+    def gemm_all_reduce_rmsnorm(self, a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                                norm_w: torch.Tensor, eps: float, out: torch.Tensor = None):
+        """Row-parallel GEMM fused with the allreduce: the GEMM epilogue stores
+        its partial output tiles straight into the owner ranks' symmetric
+        buffers (reduce-scatter overlapped with the remaining tiles), then one
+        launch reduces the owned rows, all-gathers them and applies
+        residual <- residual + sum, out = rmsnorm(residual) * norm_w."""
+        from .. import ops
+
+        M, N = a.shape[0], w.shape[0]
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+        self._check_error()
+        self._ar.gemm_ar_rmsnorm(a, w, residual, norm_w, out, eps, ops.workspace(a.device).err, self.cfg.max_blocks)
+        self.counters["fused"] += 1
+        launches.add(2)
         return out
 
     def fused_rmsnorm_limit(self) -> int:

@@ -60,6 +60,19 @@ class TPGroup:
         x = self.all_reduce(x)
         return ops.fused_add_rmsnorm(x, residual, weight, eps, out=out)
 
+    def gemm_all_reduce_rmsnorm(self, a, w, residual, norm_w, eps, out=None):
+        """Row-parallel linear + allreduce + residual add + RMSNorm: the fused
+        GEMM->collective kernel pair when the communicator is up and the
+        output fits its buffer, else GEMM then the fused allreduce+norm."""
+        from .. import ops
+
+        M, N = a.shape[0], w.shape[0]
+        ca = self.ca_comm
+        if self.world_size > 1 and ca is not None and not ca.disabled and ca.fused_gemm_fits(M, N):
+            return ca.gemm_all_reduce_rmsnorm(a, w, residual, norm_w, eps, out=out)
+        part = ops.gemm(a, w)
+        return self.all_reduce_rmsnorm(part, residual, norm_w, eps, out=out)
+
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         """[world, *x.shape]."""
         if self.world_size == 1:

@@ -495,6 +495,77 @@ done:
 }
 
 // --------------------------------------------------------------------------
+// Fused row-parallel GEMM -> allreduce -> residual + RMSNorm, second half.
+// The GEMM epilogue (gemm.cu, push-RS mode) has stored every rank's partial
+// rows into the owner's region A (W source slots of [Mo, N] bf16) and the last
+// CTA of each rank's GEMM released one flag per owner. Here each owner waits
+// for all W flags, sums its rows in rank order (fp32, one rounding), stores the
+// reduced rows into every rank's region B (all-gather by posted stores), and
+// after a block barrier every rank applies residual add + RMSNorm to all rows
+// from its local region B.
+// --------------------------------------------------------------------------
+MBX_DEVICE char* fuse_half(const ArCtx& c, char* base, uint32_t epoch) {
+  return base + c.fuse_off + (uint64_t)(epoch & 1u) * c.fuse_half_bytes;
+}
+MBX_DEVICE uint32_t* fuse_flag(char* base, int src) { return reinterpret_cast<uint32_t*>(base + kTileFlagOff) + src; }
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) fused_rs_norm_kernel(ArCtx c, int M, int N, int Mo, uint4* residual,
+                                                                   const uint4* __restrict__ w,
+                                                                   uint4* __restrict__ out, float eps) {
+  __shared__ bool s_ok;
+  __shared__ float red[32];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
+  const int nvec = N / 8;
+  if (!poisoned(c)) {
+    if (threadIdx.x == 0) s_ok = true;
+    __syncthreads();
+    if (threadIdx.x < W) {
+      if (!wait_flag_geq(fuse_flag(c.bufs[c.rank], threadIdx.x), epoch, c.timeout_ns)) {
+        record_error(c, kErrFuseWait, blockIdx.x, threadIdx.x, 4, epoch);
+        s_ok = false;
+      }
+    }
+    __syncthreads();
+    if (!s_ok) goto done;
+    {
+      char* mine = fuse_half(c, c.bufs[c.rank], epoch);
+      const uint64_t slot = (uint64_t)Mo * N * 2;
+      const uint64_t regB = (uint64_t)W * slot;
+      const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
+      for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+        const uint64_t lrow = row - r0;
+        for (int p = threadIdx.x; p < nvec; p += blockDim.x) {
+          uint4 v[W];
+#pragma unroll
+          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (lrow * nvec + p) * 16);
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
+          const uint4 sum = pack_from<__nv_bfloat16>(acc);
+#pragma unroll
+          for (int j = 0; j < W; ++j) {
+            char* dst = fuse_half(c, c.bufs[(c.rank + j) % W], epoch) + regB + ((uint64_t)row * nvec + p) * 16;
+            st_v4(dst, sum);
+          }
+        }
+      }
+      if (!block_barrier(c, 2, epoch, &s_ok)) goto done;
+      for (int o = 0; o < W; ++o) {
+        const int a0 = o * Mo, a1 = min(M, a0 + Mo);
+        for (int row = a0 + blockIdx.x; row < a1; row += gridDim.x) {
+          const uint64_t base = (uint64_t)row * nvec;
+          auto ld = [&](int p) { return ld_cg_v4(mine + regB + (base + p) * 16); };
+          residual_rmsnorm_row(ld, residual + base, w, out + base, nvec, N, eps, red);
+        }
+      }
+    }
+  }
+done:
+  finish_call(c, epoch, kStFuseEpoch, kStFuseDone);
+}
+
+// --------------------------------------------------------------------------
 // Segmented allreduce (overlap path). The reference pushes row segments with
 // the copy engine and flags a peer slot from the host-maintained seq
 // (sglang/mailbox_ar_ext.cu:233-342), which is not graph-replay safe. Here the
@@ -510,7 +581,7 @@ MBX_DEVICE uint32_t* seg_free(char* base, int slot, int src) {
   return reinterpret_cast<uint32_t*>(base + kSegFreeOff) + slot * kMaxRanks + src;
 }
 MBX_DEVICE char* seg_data(const ArCtx& c, char* base, int slot, int src) {
-  return base + kSigBytes + 2 * c.half_bytes + ((uint64_t)slot * kMaxRanks + src) * c.seg_slot_bytes;
+  return base + c.fuse_off + 2 * c.fuse_half_bytes + ((uint64_t)slot * kMaxRanks + src) * c.seg_slot_bytes;
 }
 
 template <int W>
@@ -754,6 +825,16 @@ void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nby
   const int W_ = c.world;
   MBX_DISPATCH_W(W_, ar_allgather_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(in),
                                                                            static_cast<uint4*>(out), nvec));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void fused_rs_norm_launch(const ArCtx& c, int M, int N, int Mo, void* residual, const void* weight, void* out,
+                          float eps, int max_blocks, cudaStream_t stream) {
+  const int g = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
+  const int W_ = c.world;
+  MBX_DISPATCH_W(W_, fused_rs_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
+                         c, M, N, Mo, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
+                         static_cast<uint4*>(out), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -10,6 +10,9 @@
 //       seg_free[slot][src]        u32 segment seq acked by the receiver
 //       tile_ready[slot][src]      u32 per-row-block flags of fused epilogues
 //   [kSigBytes, +2*half)  two ping-pong data halves (call epoch parity)
+//   [fuse_off, +2*fuse)   two ping-pong halves of the fused GEMM->allreduce
+//                         path (own epoch, so it never shares memory with
+//                         a plain allreduce that may overlap it across ranks)
 //   [.., + seg region)    segmented-allreduce slots
 //
 // The reference keeps a [flag][ack][pad] header plus two 24 MB halves in a
@@ -46,7 +49,8 @@ enum StateWord : int {
   kStSegSubmitDone = 5,  // blocks finished in the current submit
   kStSegWaitDone = 6,    // blocks finished in the current wait
   kStFuseEpoch = 7,      // fused GEMM-epilogue path epoch
-  kStFuseDone = 8,       // blocks finished in the current fused call
+  kStFuseDone = 8,       // blocks finished in the current fused reduce kernel
+  kStFuseGemmDone = 9,   // GEMM CTAs finished pushing in the current fused call
   kStWords = 16
 };
 
@@ -79,6 +83,8 @@ struct ArCtx {
   uint64_t timeout_ns;     // bound of every device-side wait
   uint64_t half_bytes;     // size of one ping-pong data half
   uint64_t seg_slot_bytes; // size of one segmented slot (per source rank)
+  uint64_t fuse_off;       // byte offset of the fused path's halves
+  uint64_t fuse_half_bytes;// size of one fused half (0 = fused path disabled)
   int rank;
   int world;
 };

@@ -32,7 +32,8 @@ void check_bf16(const torch::Tensor& t, const char* name) {
 class ArComm {
  public:
   ArComm(int rank, int world, std::vector<int64_t> bufs, int64_t mc, int64_t state, int64_t status_dev,
-         int64_t status_host, uint64_t half_bytes, uint64_t seg_slot_bytes, uint64_t timeout_ns)
+         int64_t status_host, uint64_t half_bytes, uint64_t seg_slot_bytes, uint64_t timeout_ns,
+         uint64_t fuse_half_bytes)
       : status_host_(reinterpret_cast<volatile uint32_t*>(status_host)) {
     TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)bufs.size() == world, "ArComm: bad world size");
     std::memset(&c_, 0, sizeof(c_));
@@ -43,6 +44,8 @@ class ArComm {
     c_.timeout_ns = timeout_ns;
     c_.half_bytes = half_bytes;
     c_.seg_slot_bytes = seg_slot_bytes;
+    c_.fuse_off = kSigBytes + 2 * half_bytes;
+    c_.fuse_half_bytes = fuse_half_bytes;
     c_.rank = rank;
     c_.world = world;
   }
@@ -67,6 +70,21 @@ class ArComm {
     seg_wait_launch(c_, dtype, reinterpret_cast<const void*>(local), reinterpret_cast<void*>(out), nbytes, max_blocks,
                     stream_of(stream));
   }
+  void gemm_ar_rmsnorm(torch::Tensor a, torch::Tensor w, torch::Tensor residual, torch::Tensor norm_w,
+                       torch::Tensor out, double eps, torch::Tensor err, int max_blocks) {
+    check_bf16(a, "a");
+    check_bf16(w, "w");
+    check_bf16(residual, "residual");
+    check_bf16(norm_w, "norm_w");
+    check_bf16(out, "out");
+    const int64_t M = a.size(0), K = a.size(1), N = w.size(0);
+    TORCH_CHECK(w.size(1) == K && residual.numel() == M * N && out.numel() == M * N && norm_w.numel() == N,
+                "gemm_ar_rmsnorm: shape mismatch");
+    gemm_ar_rmsnorm_launch(c_, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), M, N, K, residual.data_ptr(),
+                           norm_w.data_ptr(), out.data_ptr(), (float)eps,
+                           reinterpret_cast<uint32_t*>(err.data_ptr<int>()), max_blocks, cur_stream());
+  }
+  uint64_t fused_capacity() const { return c_.fuse_half_bytes; }
   uint64_t chunk_limit(int algo) const { return ar_chunk_limit(c_, algo); }
   std::vector<int64_t> status() const {
     std::vector<int64_t> v(kStatusWords);
@@ -318,9 +336,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("host_mapped_free", &host_mapped_free, py::arg("host"));
 
   py::class_<ArComm>(m, "ArComm")
-      .def(py::init<int, int, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, uint64_t, uint64_t, uint64_t>(),
+      .def(py::init<int, int, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, uint64_t, uint64_t, uint64_t,
+                    uint64_t>(),
            py::arg("rank"), py::arg("world"), py::arg("bufs"), py::arg("mc"), py::arg("state"), py::arg("status_dev"),
-           py::arg("status_host"), py::arg("half_bytes"), py::arg("seg_slot_bytes"), py::arg("timeout_ns"))
+           py::arg("status_host"), py::arg("half_bytes"), py::arg("seg_slot_bytes"), py::arg("timeout_ns"),
+           py::arg("fuse_half_bytes") = 0)
+      .def("gemm_ar_rmsnorm", &ArComm::gemm_ar_rmsnorm)
+      .def("fused_capacity", &ArComm::fused_capacity)
       .def("allreduce", &ArComm::allreduce, py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("dtype"),
            py::arg("algo"), py::arg("max_blocks"), py::arg("stream"))
       .def("ar_rmsnorm", &ArComm::ar_rmsnorm, py::arg("inp"), py::arg("residual"), py::arg("weight"), py::arg("out"),

@@ -37,7 +37,7 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 
-enum EpiMode : int { kEpiBf16 = 0, kEpiF32Partial = 1, kEpiBf16AddResidual = 2 };
+enum EpiMode : int { kEpiBf16 = 0, kEpiF32Partial = 1, kEpiBf16AddResidual = 2, kEpiPushRS = 3 };
 
 struct GemmArgs {
   void* out;             // bf16 C (ldc) or fp32 partials [splits][M][N]
@@ -47,6 +47,21 @@ struct GemmArgs {
   int num_m, num_n, splits, kb_per_split, kb_total;
   uint32_t* err;
   uint64_t timeout_ns;
+  // kEpiPushRS: row r of C goes to owner r / Mo's fused region A, slot `rank`
+  ArCtx ar;
+  int Mo;
+};
+
+MBX_DEVICE char* fused_half(const ArCtx& c, char* base, uint32_t epoch) {
+  return base + c.fuse_off + (uint64_t)(epoch & 1u) * c.fuse_half_bytes;
+}
+
+// TMEM columns per accumulator buffer (power of two >= BN, so both buffers
+// start on aligned columns and the allocation is a power of two).
+template <int BN>
+struct Tmem {
+  static constexpr int kAccStride = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int kCols = 2 * kAccStride;
 };
 
 template <int BN, int STAGES>
@@ -122,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_barrier_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, 2 * BN);
+    tc::tmem_alloc(tmem_slot, Tmem<BN>::kCols);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -181,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc::tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
+        const uint32_t d = tmem_base + acc * Tmem<BN>::kAccStride;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
@@ -215,6 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    const uint32_t fepoch =
+        EPI == kEpiPushRS ? *reinterpret_cast<volatile uint32_t*>(args.ar.state + kStFuseEpoch) + 1u : 0u;
     uint32_t t = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
       const int m = u % args.num_m;
@@ -233,12 +250,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
-        tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c0, r);
+        tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * Tmem<BN>::kAccStride + c0, r);
         tc::tmem_ld_wait();
         const int gcol = n * BN + c0;
         const int valid = min(32, args.N - gcol);
         if (row_ok && valid > 0) {
-          if (EPI == kEpiF32Partial) {
+          if (EPI == kEpiPushRS) {
+            const int owner = grow / args.Mo;
+            const int lrow = grow - owner * args.Mo;
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(
+                fused_half(args.ar, args.ar.bufs[owner], fepoch) +
+                ((uint64_t)(args.ar.rank * args.Mo + lrow) * args.N + gcol) * 2);
+            store_row_bf16(dst, r, valid, nullptr);
+          } else if (EPI == kEpiF32Partial) {
             float* dst = static_cast<float*>(args.out) + ((int64_t)ks * args.M + grow) * args.N + gcol;
 #pragma unroll
             for (int g = 0; g < 8; ++g)
@@ -256,12 +280,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
     }
+    if (EPI == kEpiPushRS) {
+      // This CTA's rows are stored; the last CTA of the grid tells every owner.
+      tc::named_bar_sync(1, kEpiWarps * 32);
+      if (warp == 2 && lane == 0 && !*abort) {
+        fence_acq_rel_sys();
+        const uint32_t prev = atomicAdd(args.ar.state + kStFuseGemmDone, 1u);
+        if (prev == gridDim.x - 1) {
+          fence_acq_rel_sys();
+          args.ar.state[kStFuseGemmDone] = 0;
+          for (int o = 0; o < args.ar.world; ++o)
+            st_release_sys(reinterpret_cast<uint32_t*>(args.ar.bufs[o] + kTileFlagOff) + args.ar.rank, fepoch);
+        }
+      }
+    }
   }
 
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == 1) tc::tmem_dealloc(tmem_base, 2 * BN);
+  if (warp == 1) tc::tmem_dealloc(tmem_base, Tmem<BN>::kCols);
 }
 
 // Sum split-K partials (fp32, in split order) into bf16 C, optional residual.
@@ -382,28 +420,45 @@ void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
 
 template <int EPI>
 void launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
-  if (bn == 256) launch_cfg<256, 4, EPI>(ta, tb, a, grid, s);
-  else if (bn == 128) launch_cfg<128, 6, EPI>(ta, tb, a, grid, s);
-  else launch_cfg<64, 8, EPI>(ta, tb, a, grid, s);
+  switch (bn) {
+    case 256: launch_cfg<256, 4, EPI>(ta, tb, a, grid, s); break;
+    case 224: launch_cfg<224, 5, EPI>(ta, tb, a, grid, s); break;
+    case 192: launch_cfg<192, 5, EPI>(ta, tb, a, grid, s); break;
+    case 160: launch_cfg<160, 5, EPI>(ta, tb, a, grid, s); break;
+    case 128: launch_cfg<128, 6, EPI>(ta, tb, a, grid, s); break;
+    default: launch_cfg<64, 8, EPI>(ta, tb, a, grid, s); break;
+  }
 }
 
 GemmPlan plan_for(int64_t M, int64_t N, int64_t K, int sms) {
   GemmPlan p;
   const int64_t num_m = (M + BM - 1) / BM;
   const int64_t kb_total = (K + BK - 1) / BK;
-  // Pick BN to balance waves across the SMs.
-  auto waves_eff = [&](int bn) {
+  // Tile width by estimated time: waves of the persistent grid x per-tile
+  // cost. Narrow tiles pay more shared-memory traffic per FLOP (A is
+  // re-read for every BN columns), which the factor models.
+  static const int kBN[] = {256, 224, 192, 160, 128};
+  static const double kCost[] = {1.00, 1.00, 1.02, 1.10, 1.25};
+  double best = 1e30;
+  for (int i = 0; i < 5; ++i) {
+    const int bn = kBN[i];
     const int64_t tiles = num_m * ((N + bn - 1) / bn);
     const int64_t waves = (tiles + sms - 1) / sms;
-    return (double)tiles / (double)(waves * sms);
-  };
-  p.bn = 256;
-  if (waves_eff(128) > waves_eff(256) * 1.15) p.bn = 128;
+    const double t = (double)waves * bn * kCost[i];
+    if (t < best * 0.999) {
+      best = t;
+      p.bn = bn;
+    }
+  }
   const int64_t tiles = num_m * ((N + p.bn - 1) / p.bn);
   p.splits = 1;
   if (tiles * 2 <= sms && kb_total >= 8) {
-    // few output tiles (decode): split K so every SM streams weights
-    const int64_t s = std::min<int64_t>(sms / tiles, kb_total / 4);
+    // few output tiles (decode, narrow TP shards): split K so every SM streams weights
+    if (p.bn > 128) {
+      p.bn = 128;
+    }
+    const int64_t t128 = num_m * ((N + 127) / 128);
+    const int64_t s = std::min<int64_t>(sms / std::max<int64_t>(1, t128), kb_total / 4);
     p.splits = (int)std::max<int64_t>(1, std::min<int64_t>(s, 16));
   }
   // every split gets at least one k-block
@@ -416,6 +471,43 @@ GemmPlan plan_for(int64_t M, int64_t N, int64_t K, int sms) {
 
 GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) { return plan_for(M, N, K, num_sms()); }
 
+void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
+                            int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
+                            uint32_t* err, int max_blocks, cudaStream_t s) {
+  if (M == 0) return;
+  if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm_ar: K and N must be multiples of 8");
+  const int W = c.world;
+  const int64_t Mo = (M + W - 1) / W;
+  const uint64_t need = (uint64_t)W * Mo * N * 2 + (uint64_t)M * N * 2;
+  if (c.fuse_half_bytes == 0 || need > c.fuse_half_bytes)
+    throw std::runtime_error("gemm_ar: message needs " + std::to_string(need) + " bytes of fused buffer, have " +
+                             std::to_string(c.fuse_half_bytes));
+  const int sms = num_sms();
+  GemmPlan p = plan_for(M, N, K, sms);
+  GemmArgs a;
+  a.out = nullptr;
+  a.residual = nullptr;
+  a.ldc = N;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.num_m = (int)((M + BM - 1) / BM);
+  a.num_n = (int)((N + p.bn - 1) / p.bn);
+  a.kb_total = (int)((K + BK - 1) / BK);
+  a.splits = 1;
+  a.kb_per_split = a.kb_total;
+  a.err = err;
+  a.timeout_ns = 2000000000ull;
+  a.ar = c;
+  a.Mo = (int)Mo;
+  const CUtensorMap ta = make_map(A, M, K, lda, BM);
+  const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);
+  const int units = a.num_m * a.num_n;
+  launch_bn<kEpiPushRS>(p.bn, ta, tb, a, std::min(units, sms), s);
+  MBX_CUDA_CHECK(cudaGetLastError());
+  fused_rs_norm_launch(c, (int)M, (int)N, (int)Mo, residual, norm_w, out, eps, max_blocks, s);
+}
+
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
                  cudaStream_t s) {
@@ -426,7 +518,8 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   GemmPlan p = plan_for(M, N, K, sms);
   if (bn > 0) p.bn = bn;
   if (splits > 0) p.splits = splits;
-  if (p.bn != 64 && p.bn != 128 && p.bn != 256) throw std::runtime_error("gemm: BN must be 64, 128 or 256");
+  if (p.bn != 64 && p.bn != 128 && p.bn != 160 && p.bn != 192 && p.bn != 224 && p.bn != 256)
+    throw std::runtime_error("gemm: BN must be one of 64, 128, 160, 192, 224, 256");
   GemmArgs a;
   a.residual = static_cast<const __nv_bfloat16*>(residual);
   a.ldc = ldc;

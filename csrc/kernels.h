@@ -19,6 +19,10 @@ void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual,
                        int H, float eps, int max_blocks, cudaStream_t stream);
 void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nbytes, int max_blocks,
                          cudaStream_t stream);
+// Second launch of the fused GEMM->allreduce->RMSNorm (reduce own rows,
+// all-gather, residual + norm). The first launch is gemm_ar_rmsnorm_launch.
+void fused_rs_norm_launch(const ArCtx& c, int M, int N, int Mo, void* residual, const void* weight, void* out,
+                          float eps, int max_blocks, cudaStream_t stream);
 void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream);
 void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, uint64_t nbytes, int max_blocks,
                      cudaStream_t stream);
@@ -47,6 +51,15 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K);
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
                  cudaStream_t s);
+
+// Row-parallel GEMM fused with allreduce + residual add + RMSNorm: the GEMM
+// epilogue stores its partial rows straight into the owner ranks' symmetric
+// buffers (reduce-scatter overlapped with the remaining tiles), then one
+// launch reduces, all-gathers and normalises. residual is updated in place;
+// out = rmsnorm(residual) * norm_w.
+void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
+                            int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
+                            uint32_t* err, int max_blocks, cudaStream_t s);
 
 // ---- attention (attn/attention.cu) -------------------------------------------
 void prefill_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,

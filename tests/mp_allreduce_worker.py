@@ -120,6 +120,31 @@ def main():
             assert (out.float() - want).abs().max().item() < 5e-2, f"fused norm M={M} algo={algo}"
     log("fused-rmsnorm OK")
 
+    # 5b. fused row-parallel GEMM -> allreduce -> residual + RMSNorm, interleaved
+    #     with plain allreduces (separate buffers/epochs must not interfere)
+    for it, (M, K, N) in enumerate([(1, 512, 4096), (64, 1024, 4096), (1024, 2048, 4096), (333, 512, 8192)] * 25):
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + it)
+        a = (torch.randn(M, K, device=dev, generator=g) / 8).to(torch.bfloat16)
+        wt = (torch.randn(N, K, device=dev, generator=g) / 8).to(torch.bfloat16)
+        gs = torch.Generator(device=dev).manual_seed(77 + it)  # same residual / norm weight on all ranks
+        res = torch.randn(M, N, device=dev, generator=gs).to(torch.bfloat16)
+        nw = (1 + 0.1 * torch.randn(N, device=dev, generator=gs)).to(torch.bfloat16)
+        r = res.clone()
+        out = ar.gemm_all_reduce_rmsnorm(a, wt, r, nw, 1e-5)
+        plain = ar.custom_all_reduce(torch.full((4096,), float(rank), dtype=torch.bfloat16, device=dev))
+        part = (a.float() @ wt.float().t()).to(torch.bfloat16).float()
+        dist.all_reduce(part)
+        want, want_r = ops_ref.fused_add_rmsnorm(part.to(torch.bfloat16), res, nw, 1e-5)
+        assert (r.float() - want_r.float()).abs().max().item() < 0.05, f"fused gemm residual it={it}"
+        assert (out.float() - want).abs().max().item() < 0.1, f"fused gemm out it={it}"
+        assert torch.all(plain == float(sum(range(world)))), f"plain AR after fused it={it}"
+        ga = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(ga, out)
+        assert all(torch.equal(ga[0], t) for t in ga), "fused output differs across ranks"
+    torch.cuda.synchronize()
+    assert ar.err() == 0, ar.status()
+    log("fused-gemm-allreduce OK")
+
     # 6. all-gather
     xg = torch.full((4096,), float(rank + 1), dtype=torch.bfloat16, device=dev)
     ag = ar.all_gather(xg)

@@ -18,6 +18,10 @@ SHAPES = [
     (64, 1792, 14336, 0, 0),      # down_proj at TP=8 decode
     (1, 16032, 4096, 0, 0),       # lm_head shard, bs=1
     (96, 2048, 4096, 64, 1),      # BN=64 path
+    (300, 960, 256, 160, 1),      # BN=160 with M/N tails
+    (1024, 6144, 1024, 192, 1),   # BN=192
+    (1024, 28672, 512, 224, 1),   # BN=224
+    (130, 448, 640, 224, 1),      # BN=224 with tails
 ]
 
 
