@@ -50,10 +50,10 @@ class CommConfig:
     nvls: bool = True
     # one-shot (push) is used up to this many bytes, per world size
     oneshot_max: dict = dataclasses.field(
-        default_factory=lambda: {2: 32 * MiB, 3: 1 * MiB, 4: 1 * MiB, 5: 512 << 10, 6: 512 << 10, 7: 512 << 10, 8: 512 << 10}
+        default_factory=lambda: {2: 32 * MiB, 3: 2 * MiB, 4: 2 * MiB, 5: 1 * MiB, 6: 1 * MiB, 7: 1 * MiB, 8: 1 * MiB}
     )
     # NVLS is preferred over two-shot at/above this many bytes
-    nvls_min: int = 1 * MiB
+    nvls_min: int = 64 * MiB
     # grid cap of the allreduce kernels (blocks)
     max_blocks: int = 148
     # CPU transport: bytes per slot of the shared-memory mailbox

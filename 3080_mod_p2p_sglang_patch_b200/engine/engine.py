@@ -15,7 +15,7 @@ import torch
 
 from .. import ops
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
-from .graph_runner import DecodeGraphRunner
+from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
 from .kv_cache import PAGE, PagedKVCache
 from .scheduler import Request, Scheduler
 
@@ -23,7 +23,7 @@ from .scheduler import Request, Scheduler
 class LLMEngine:
     def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
-                 graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None):
+                 graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False):
         self.cfg = cfg
         self.tp = tp
         self.tp_size = tp.world_size if tp is not None else 1
@@ -45,9 +45,12 @@ class LLMEngine:
         # scratch sized once (graph capture must not allocate)
         self._reserve_scratch()
         self.graphs = None
+        self.prefill_graph = None
         if use_graphs:
             sizes = tuple(s for s in graph_sizes if s <= max_batch)
             self.graphs = DecodeGraphRunner(self, sizes)
+        if prefill_graph:
+            self.prefill_graph = PrefillGraphRunner(self, chunk)
 
     # ------------------------------------------------------------------ setup
     def _reserve_scratch(self):
@@ -63,7 +66,7 @@ class LLMEngine:
         shapes = [((cfg.heads + 2 * cfg.kv_heads) // t * D, H), (H, cfg.heads // t * D), (2 * F_, H), (H, F_),
                   (cfg.vocab // t, H)]
         need = 0
-        for M in (1, 8, 32, 64, self.max_batch):
+        for M in (1, 8, 32, 64, self.max_batch, self.chunk):
             for N, K in shapes:
                 bn, splits = C.gemm_plan(M, N, K)
                 if splits > 1:
@@ -92,6 +95,17 @@ class LLMEngine:
         for p in pieces:
             if not getattr(p.req, "_row_synced", False):
                 self._sync_block_row(p.req)
+        if self.prefill_graph is not None and len(pieces) == 1 and pieces[0].n == self.chunk:
+            # a full single-request chunk: replay the captured chunk forward
+            p = pieces[0]
+            req = p.req
+            dev = self.device
+            host = torch.tensor(req.prompt[p.start:p.start + p.n] + list(range(p.start, p.start + p.n)),
+                                dtype=torch.int32).pin_memory()
+            d = host.to(dev, non_blocking=True)
+            slots_d = torch.tensor(self.kv.slots(req.blocks, p.start, p.n), dtype=torch.int64).pin_memory().to(
+                dev, non_blocking=True)
+            return self.prefill_graph.run(d[:p.n], d[p.n:], slots_d, p.start + p.n, self.block_table[req.slot])
         ids, pos, slots, q_lens, kv_lens, rows, last = [], [], [], [], [], [], []
         off = 0
         for p in pieces:
@@ -124,9 +138,10 @@ class LLMEngine:
         bt = self.block_table.index_select(0, rows_d.long())
         last_d = torch.tensor(last, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         scale = self.model.scale
+        splits = ops.prefill_splits(tiles.shape[0], self.cfg.heads // self.tp_size, max(kv_lens))
 
         def attn(li, q, kc, vc):
-            return ops.prefill_attention(q, kc, vc, cu_d, kvl_d, bt, tiles, scale)
+            return ops.prefill_attention(q, kc, vc, cu_d, kvl_d, bt, tiles, scale, splits=splits)
 
         return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d)
 

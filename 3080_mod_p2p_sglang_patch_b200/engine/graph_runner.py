@@ -11,6 +11,7 @@ re-registration (the reference's graph story, docs/principle.md:80-83).
 import torch
 
 from .. import ops
+from ..utils import launches
 from .kv_cache import PAGE
 
 
@@ -28,6 +29,7 @@ class DecodeGraphRunner:
         self.host_slots = torch.zeros(n, dtype=torch.int64).pin_memory()
         self.graphs = {}
         self.outputs = {}
+        self.kernels = {}
         self.pool = None
         self._captured = False
 
@@ -62,9 +64,11 @@ class DecodeGraphRunner:
                 g = torch.cuda.CUDAGraph()
                 comm = e.tp.ca_comm if e.tp is not None else None
                 ctx = comm.capture() if comm is not None else _null()
+                before = launches.get()
                 with ctx:
                     with torch.cuda.graph(g, pool=self.pool, stream=s):
                         out = e.forward_decode_eager(ids, pos, kvl, slots, rows, splits=splits)
+                self.kernels[bs] = launches.get() - before
                 if self.pool is None:
                     self.pool = g.pool()
                 self.graphs[bs] = g
@@ -89,6 +93,7 @@ class DecodeGraphRunner:
         self.in_i32.copy_(h, non_blocking=True)
         self.in_slots.copy_(self.host_slots, non_blocking=True)
         self.graphs[bs].replay()
+        launches.add(self.kernels.get(bs, 0))
         return self.outputs[bs][:B]
 
     def close(self):
@@ -102,3 +107,85 @@ class _null:
 
     def __exit__(self, *a):
         return False
+
+
+class PrefillGraphRunner:
+    """CUDA graph of one full prefill chunk (one request, T = chunk tokens).
+
+    At high TP a chunk's GPU work per rank is smaller than the host time to
+    launch its ~700 kernels one by one, so the whole chunk forward is captured
+    once and replayed with its inputs in static device buffers: token ids,
+    positions, cache slots, the request's kv length and block-table row. The
+    query-tile list and the split-KV factor are fixed at capture (the kernel
+    derives the causal bounds from the kv length at run time).
+    """
+
+    def __init__(self, engine, T: int):
+        self.e = engine
+        self.T = T
+        dev = engine.device
+        self.ids = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.slots = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.kvl = torch.full((1,), T, dtype=torch.int32, device=dev)
+        self.cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        self.bt = torch.zeros((1, engine.max_blocks_per_seq), dtype=torch.int32, device=dev)
+        self.tiles = ops.prefill_tiles([T]).to(dev)
+        self.last = torch.tensor([T - 1], dtype=torch.int64, device=dev)
+        nq = engine.cfg.heads // engine.tp_size
+        self.splits = ops.prefill_splits(self.tiles.shape[0], nq, engine.max_seq)
+        ops.workspace(dev).prefill(T * nq * self.splits * 128, T * nq * self.splits)
+        self.graph = None
+        self.out = None
+
+    def _forward(self):
+        e = self.e
+        scale = e.model.scale
+
+        def attn(li, q, kc, vc):
+            return ops.prefill_attention(q, kc, vc, self.cu, self.kvl, self.bt, self.tiles, scale, splits=self.splits)
+
+        return e.model.forward(self.ids, self.pos, self.slots, e.kv.caches, attn, self.last)
+
+    def capture(self):
+        e = self.e
+        # warm-up on the scratch block 0 (slots 0..T-1 of block 0.. would clobber
+        # real pages, so point every slot at the reserved block's first entry)
+        self.slots.zero_()
+        self.pos.copy_(torch.arange(self.T, dtype=torch.int32, device=e.device))
+        self.kvl.fill_(self.T)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(device=e.device)
+        s.wait_stream(torch.cuda.current_stream(e.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._forward()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            comm = e.tp.ca_comm if e.tp is not None else None
+            ctx = comm.capture() if comm is not None else _null()
+            before = launches.get()
+            with ctx:
+                with torch.cuda.graph(g, stream=s):
+                    self.out = self._forward()
+            self.kernels_per_replay = launches.get() - before
+        torch.cuda.current_stream(e.device).wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = g
+
+    def run(self, ids_d, pos_d, slots_d, kv_len: int, bt_row_d):
+        """Device tensors in, next token (int64 [1]) out."""
+        if self.graph is None:
+            self.capture()
+        self.ids.copy_(ids_d, non_blocking=True)
+        self.pos.copy_(pos_d, non_blocking=True)
+        self.slots.copy_(slots_d, non_blocking=True)
+        self.kvl.fill_(kv_len)
+        self.bt.copy_(bt_row_d.view(1, -1), non_blocking=True)
+        self.graph.replay()
+        launches.add(self.kernels_per_replay)
+        return self.out
+
+    def close(self):
+        self.graph = None
+        self.out = None

@@ -15,24 +15,37 @@ from ..utils import launches
 
 
 class _Workspace:
+    """Scratch buffers of one device. A buffer that must grow is replaced by
+    a new, larger one and the old one is kept alive (``_retired``): a CUDA graph
+    that captured the old address keeps valid memory."""
+
     def __init__(self, device):
         self.device = device
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
         self.dec_o = torch.empty(0, dtype=torch.float32, device=device)
         self.dec_lse = torch.empty(0, dtype=torch.float32, device=device)
+        self.pre_o = torch.empty(0, dtype=torch.float32, device=device)
+        self.pre_lse = torch.empty(0, dtype=torch.float32, device=device)
+        self._retired = []
+
+    def _grow(self, name, n, minimum):
+        buf = getattr(self, name)
+        if buf.numel() < n:
+            if buf.numel():
+                self._retired.append(buf)
+            buf = torch.empty(max(n, minimum), dtype=torch.float32, device=self.device)
+            setattr(self, name, buf)
+        return buf
 
     def gemm(self, n):
-        if self.gemm_ws.numel() < n:
-            self.gemm_ws = torch.empty(max(n, 1 << 22), dtype=torch.float32, device=self.device)
-        return self.gemm_ws
+        return self._grow("gemm_ws", n, 1 << 22)
 
     def decode(self, n_o, n_lse):
-        if self.dec_o.numel() < n_o:
-            self.dec_o = torch.empty(max(n_o, 1 << 20), dtype=torch.float32, device=self.device)
-        if self.dec_lse.numel() < n_lse:
-            self.dec_lse = torch.empty(max(n_lse, 1 << 14), dtype=torch.float32, device=self.device)
-        return self.dec_o, self.dec_lse
+        return self._grow("dec_o", n_o, 1 << 20), self._grow("dec_lse", n_lse, 1 << 14)
+
+    def prefill(self, n_o, n_lse):
+        return self._grow("pre_o", n_o, 1 << 20), self._grow("pre_lse", n_lse, 1 << 14)
 
 
 _WS = {}
@@ -162,15 +175,32 @@ def prefill_tiles(q_lens, bq: int = PREFILL_BQ):
     return torch.tensor(tiles, dtype=torch.int32).reshape(-1, 2)
 
 
-def prefill_attention(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles, scale=None, out=None):
+def prefill_splits(n_tiles: int, nq: int, max_kv: int, sms: int = 148) -> int:
+    """Split-KV factor for the prefill kernel: enough CTAs to cover the SMs
+    when a chunk has few query tiles x heads (high TP), at least 2 key tiles
+    (256 keys) per split."""
+    ctas = max(1, n_tiles * nq)
+    if ctas >= sms:
+        return 1
+    want = -(-sms // ctas)
+    return int(max(1, min(want, max_kv // 256, 16)))
+
+
+def prefill_attention(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles, scale=None, out=None, splits=1):
     """Causal chunked-prefill attention over the paged cache, tcgen05/TMEM
-    kernel; ``tiles`` from ``prefill_tiles(q_lens)`` (128-row tiles)."""
+    kernel; ``tiles`` from ``prefill_tiles(q_lens)`` (128-row tiles).
+    ``splits`` > 1 splits each query tile's keys across CTAs (see
+    ``prefill_splits``); the partials are merged by a combine kernel."""
     if out is None:
         out = torch.empty_like(q)
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    po = pl = None
+    if splits > 1:
+        T, nq, _ = q.shape
+        po, pl = workspace(q.device).prefill(T * nq * splits * 128, T * nq * splits)
     cuda_ext().prefill_attention_tc(q, k_cache, v_cache, out, cu_q, kv_len, block_table, tiles, scale,
-                                    workspace(q.device).err)
-    launches.add(1)
+                                    workspace(q.device).err, splits, po, pl)
+    launches.add(2 if splits > 1 else 1)
     return out
 
 
@@ -187,9 +217,10 @@ def prefill_attention_mma(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles6
 
 
 def decode_splits(batch: int, nkv: int, max_len: int, sms: int = 148) -> int:
-    """Split-KV factor so (batch x kv-heads x splits) fills the SMs."""
+    """Split-KV factor so (batch x kv-heads x splits) fills the SMs: at least
+    4 pages (64 keys, one page per warp) per split, at most 64 splits."""
     want = max(1, (2 * sms) // max(1, batch * nkv))
-    by_len = max(1, max_len // 256)
+    by_len = max(1, max_len // 64)
     return int(min(want, by_len, 64))
 
 

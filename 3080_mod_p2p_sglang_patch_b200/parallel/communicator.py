@@ -291,7 +291,7 @@ class MailboxAR:
             out = torch.empty_like(x)
         self._check_error()
         if algo is None:
-            algo = ALGO_ONESHOT_PUSH if nbytes <= self.cfg.oneshot_max.get(self.world_size, 0) else ALGO_TWOSHOT
+            algo = ALGO_ONESHOT_PUSH if nbytes <= self.cfg.oneshot_max.get(self.world_size, 0) else ALGO_TWOSHOT_PUSH
         self._ar.ar_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(), out.data_ptr(), M, H, eps, algo,
                             self.cfg.max_blocks, torch.cuda.current_stream(self.device).cuda_stream)
         self.counters["fused"] += 1
@@ -327,7 +327,8 @@ class MailboxAR:
         """Largest message (bytes) the fused allreduce+RMSNorm takes in one launch."""
         if self._ar is None:
             return 0
-        return int(self._ar.chunk_limit(ALGO_TWOSHOT))
+        # two-shot push needs W row slots plus the reduced rows in one half
+        return int(self.cfg.half_bytes // 2 - 16 * self.world_size * 8192)
 
     def all_gather(self, x: torch.Tensor, out: torch.Tensor = None):
         """out[r] = x of rank r (shape [world, *x.shape]), one launch."""

@@ -31,6 +31,7 @@ class TPGroup:
         self.world_size = dist.get_world_size(group) if self.initialized else 1
         self.device = device
         self.ca_comm = None
+        self.fused_gemm_ar = os.environ.get("MBX_FUSED_GEMM_AR", "0") == "1"
         if use_mailbox is None:
             use_mailbox = mailbox_enabled()
         if self.world_size > 1 and use_mailbox:
@@ -68,7 +69,11 @@ class TPGroup:
 
         M, N = a.shape[0], w.shape[0]
         ca = self.ca_comm
-        if self.world_size > 1 and ca is not None and not ca.disabled and ca.fused_gemm_fits(M, N):
+        # The fused pair (GEMM epilogue pushes its tiles) is opt-in: at chunk 1024
+        # these GEMMs are a single wave, so there are no later tiles to hide the
+        # pushes behind, and GEMM + one fused allreduce/norm launch measured faster.
+        if self.world_size > 1 and ca is not None and not ca.disabled and M > 64 and self.fused_gemm_ar \
+                and ca.fused_gemm_fits(M, N):
             return ca.gemm_all_reduce_rmsnorm(a, w, residual, norm_w, eps, out=out)
         part = ops.gemm(a, w)
         return self.all_reduce_rmsnorm(part, residual, norm_w, eps, out=out)

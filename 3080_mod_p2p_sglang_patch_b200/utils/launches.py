@@ -19,3 +19,11 @@ def get() -> int:
 def reset():
     global _count
     _count = 0
+
+
+def count_graph(fn, *args, **kwargs):
+    """Run fn once with counting on and return (result, launches it made):
+    used to know how many kernels a captured graph replays."""
+    before = get()
+    out = fn(*args, **kwargs)
+    return out, get() - before

@@ -49,6 +49,7 @@ def parse():
     p.add_argument("--prompt-len", type=int, default=4096)
     p.add_argument("--chunk", type=int, default=1024)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="launch every chunk's kernels eagerly")
     return p.parse_args()
 
 
@@ -79,7 +80,7 @@ def main():
     cfg = models.LlamaConfig.by_name(args.model)
     R, S, chunk = args.requests, args.prompt_len, args.chunk
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=R, max_seq=S + 16, chunk=chunk, seed=0, use_graphs=False,
-                            impl=args.impl)
+                            impl=args.impl, prefill_graph=not args.no_graph)
     g = torch.Generator().manual_seed(1234)
     prompts = torch.randint(0, cfg.vocab, (R, S), generator=g).tolist()
 
@@ -120,6 +121,9 @@ def main():
             "bt": eng.block_table.index_select(0, torch.tensor(rows, device=dev)),
             "tiles": ops.prefill_tiles(q_lens).to(dev),
             "last": torch.tensor(last, dtype=torch.int64, device=dev),
+            "splits": ops.prefill_splits(len(ops.prefill_tiles(q_lens)), cfg.heads // world, max(kv_lens)),
+            "graph": len(pieces) == 1 and q_lens[0] == chunk,
+            "kv_int": kv_lens[0],
         }
         staged.append(st)
     tokens_per_step = sum(sum(n for _, _, n, _, _ in pieces) for pieces in plan)
@@ -128,8 +132,13 @@ def main():
     def run_step():
         out = None
         for st in staged:
+            if eng.prefill_graph is not None and st["graph"]:
+                out = eng.prefill_graph.run(st["ids"], st["pos"], st["slots"], st["kv_int"], st["bt"][0])
+                continue
+
             def attn(li, q, kc, vc, st=st):
-                return ops.prefill_attention(q, kc, vc, st["cu"], st["kvl"], st["bt"], st["tiles"], scale)
+                return ops.prefill_attention(q, kc, vc, st["cu"], st["kvl"], st["bt"], st["tiles"], scale,
+                                             splits=st["splits"])
             out = eng.model.forward(st["ids"], st["pos"], st["slots"], eng.kv.caches, attn, st["last"])
         return out
 

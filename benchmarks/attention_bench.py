@@ -45,7 +45,8 @@ def main():
         tiles = ops.prefill_tiles([q_len]).cuda()
         tiles64 = ops.prefill_tiles([q_len], bq=64).cuda()
         flops = 4.0 * D * nq * (q_len * off + q_len * (q_len + 1) / 2)
-        for name, fn in (("tcgen05", lambda: ops.prefill_attention(q, kc, vc, cu, kvl, bt, tiles)),
+        sp = ops.prefill_splits(tiles.shape[0], nq, kv)
+        for name, fn in (("tcgen05", lambda: ops.prefill_attention(q, kc, vc, cu, kvl, bt, tiles, splits=sp)),
                          ("mma_sync", lambda: ops.prefill_attention_mma(q, kc, vc, cu, kvl, bt, tiles64))):
             t = timing.time_fn(fn, iters=args.iters)
             ms = t[len(t) // 2]

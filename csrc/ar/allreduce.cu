@@ -566,6 +566,75 @@ done:
 }
 
 // --------------------------------------------------------------------------
+// Allreduce + residual + RMSNorm, two-shot with posted stores only:
+//   A: every row is stored into its owner's region A slot[rank]
+//   B: the owner sums its rows (rank order, fp32, one rounding) and stores
+//      the reduced rows into every rank's region B
+//   C: every rank applies residual add + RMSNorm to all rows from region B
+// Rows are owned in contiguous blocks of Mo = ceil(M / W).
+// --------------------------------------------------------------------------
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                             uint4* residual,
+                                                                             const uint4* __restrict__ w,
+                                                                             uint4* __restrict__ out, int M, int H,
+                                                                             float eps) {
+  __shared__ bool s_ok;
+  __shared__ float red[32];
+  const uint32_t epoch = call_epoch(c);
+  const int hvec = H / 8;
+  const int Mo = (M + W - 1) / W;
+  if (!poisoned(c)) {
+    const uint64_t slot = (uint64_t)Mo * hvec * 16;
+    const uint64_t regB = (uint64_t)W * slot;
+    char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
+    // A: rows of owner o -> o's region A, slot `rank`; block b takes rows o*Mo + b + k*grid
+#pragma unroll 1
+    for (int j = 0; j < W; ++j) {
+      const int o = (c.rank + j) % W;
+      const int a0 = o * Mo, a1 = min(M, a0 + Mo);
+      char* dst = data_half(c.bufs[o], epoch, c.half_bytes) + (uint64_t)c.rank * slot;
+      for (int row = a0 + blockIdx.x; row < a1; row += gridDim.x) {
+        const uint64_t lrow = row - a0;
+        for (int p = threadIdx.x; p < hvec; p += blockDim.x)
+          st_v4(dst + (lrow * hvec + p) * 16, ld_nc_v4(in + (uint64_t)row * hvec + p));
+      }
+    }
+    if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    {
+      const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
+      for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+        const uint64_t lrow = row - r0;
+        for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
+          uint4 v[W];
+#pragma unroll
+          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (lrow * hvec + p) * 16);
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
+          const uint4 sum = pack_from<__nv_bfloat16>(acc);
+#pragma unroll
+          for (int j = 0; j < W; ++j)
+            st_v4(data_half(c.bufs[(c.rank + j) % W], epoch, c.half_bytes) + regB + ((uint64_t)row * hvec + p) * 16,
+                  sum);
+        }
+      }
+    }
+    if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    for (int o = 0; o < W; ++o) {
+      const int a0 = o * Mo, a1 = min(M, a0 + Mo);
+      for (int row = a0 + blockIdx.x; row < a1; row += gridDim.x) {
+        const uint64_t base = (uint64_t)row * hvec;
+        auto ld = [&](int p) { return ld_cg_v4(mine + regB + (base + p) * 16); };
+        residual_rmsnorm_row(ld, residual + base, w, out + base, hvec, H, eps, red);
+      }
+    }
+  }
+done:
+  finish_call(c, epoch);
+}
+
+// --------------------------------------------------------------------------
 // Segmented allreduce (overlap path). The reference pushes row segments with
 // the copy engine and flags a peer slot from the host-maintained seq
 // (sglang/mailbox_ar_ext.cu:233-342), which is not graph-replay safe. Here the
@@ -809,6 +878,12 @@ void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual,
   if (algo == kOneShotPush) {
     if (bytes > ar_chunk_limit(c, kOneShotPush)) throw std::runtime_error("ar_rmsnorm: message exceeds one-shot slot");
     MBX_DISPATCH_W(W_, ar_rmsnorm_oneshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+  } else if (algo == kTwoShotPush) {
+    const int Mo = (M + W_ - 1) / W_;
+    if ((uint64_t)W_ * Mo * H * 2 + bytes > c.half_bytes)
+      throw std::runtime_error("ar_rmsnorm: message exceeds the two-shot buffer");
+    const int gp = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
+    MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_push_kernel<W><<<gp, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
   } else {
     if (bytes > ar_chunk_limit(c, kTwoShot)) throw std::runtime_error("ar_rmsnorm: message exceeds two-shot slot");
     MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));

@@ -547,6 +547,13 @@ void prefill_attention_launch(const void* q, const void* kc, const void* vc, voi
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
+void attn_combine_launch(const float* part_o, const float* part_lse, int64_t rows, int splits, void* out,
+                         cudaStream_t s) {
+  if (rows == 0) return;
+  decode_combine_kernel<<<(unsigned)rows, D, 0, s>>>(part_o, part_lse, splits, static_cast<__nv_bfloat16*>(out));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
 void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
                              const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
                              float* part_o, float* part_lse, float scale, cudaStream_t s) {

@@ -11,9 +11,12 @@
 //                       (tcgen05.ld/st) when a row's max grows
 //   O   += P_j V_j      tcgen05.mma with V read MN-major (dims contiguous, as
 //                       stored in the cache), fp32 accumulator in TMEM
-// Warp roles (192 threads): warp 0 TMA producer (Q once; K/V pages of 16
+// Warp roles (320 threads): warp 0 TMA producer (Q once; K/V pages of 16
 // keys x 64 dims per box, double-buffered stages), warp 1 TMEM allocator +
-// single-thread MMA issuer, warps 2-5 softmax + epilogue. No cluster
+// single-thread MMA issuer, warps 2-9 softmax + epilogue, two threads per
+// row (each owns 64 of the 128 keys; row maxima exchanged through shared
+// memory), so two softmax warps share every SM sub-partition. The running
+// output is rescaled only when a row max grows by more than 2^8. No cluster
 // multicast. Causal masking / kv-length masking per element in softmax.
 // Every mbarrier wait is bounded; on timeout the CTA records an error, drains
 // its in-flight copies and MMAs, frees TMEM and exits.
@@ -36,7 +39,11 @@ constexpr int D = 128;
 constexpr int BQ = 128;
 constexpr int BKV = 128;
 constexpr int PAGE = 16;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two halves of each row)
+constexpr int kSoftWarps = 8;
+// Rescale the running output only when a row max grows by more than this
+// (log2 units): exponents stay <= 2^8, harmless in fp32/bf16.
+constexpr float kRescaleThreshold = 8.f;
 constexpr int kTileBytes = BQ * D * 2;  // 32 KB: one [128 x 128] bf16 tile (two 16 KB column chunks)
 constexpr int kChunk = 16384;           // [128 rows x 64] bf16
 
@@ -46,6 +53,9 @@ struct FmhaArgs {
   const int* kv_len;        // [R]
   const int* block_table;   // [R, max_blocks]
   const int2* tiles;        // (request, q offset), 128-row tiles
+  float* part_o;            // splits > 1: [T, nq, splits, D] normalised partial outputs
+  float* part_lse;          //             [T, nq, splits] log2-sum-exp
+  int splits;
   int max_blocks, nq, nkv;
   float scale_log2;
   uint32_t* err;
@@ -57,7 +67,8 @@ struct Smem {
   static constexpr int kK0 = kQ + kTileBytes;
   static constexpr int kV0 = kK0 + 2 * kTileBytes;
   static constexpr int kP = kV0 + 2 * kTileBytes;
-  static constexpr int kBar = kP + kTileBytes;
+  static constexpr int kRed = kP + kTileBytes;              // [2 parity][2 half][128 rows] fp32 row maxima
+  static constexpr int kBar = kRed + 2 * 2 * BQ * 4;
   static constexpr int kTotal = kBar + 256 + 1024;
 };
 
@@ -92,7 +103,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pos0 = L - q_len;
   const int rows_here = min(BQ, q_len - qoff);
   const int kv_end = min(L, pos0 + qoff + rows_here);  // causal bound of the tile
-  const int n_tiles = (kv_end + BKV - 1) / BKV;
+  const int n_all = (kv_end + BKV - 1) / BKV;
+  // split-KV: this CTA takes key tiles [t_begin, t_end) of the query tile
+  const int split = blockIdx.z;
+  const int per = (n_all + a.splits - 1) / a.splits;
+  const int t_begin = min(n_all, split * per);
+  const int t_end = min(n_all, t_begin + per);
+  const int n_tiles = t_end - t_begin;
   const int* bt = a.block_table + (int64_t)r * a.max_blocks;
 
   if (threadIdx.x == 0) {
@@ -102,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&kv_empty[i], 1);
       tc::mbar_init(&s_full[i], 1);
     }
-    tc::mbar_init(p_full, 4);
+    tc::mbar_init(p_full, kSoftWarps);
     tc::mbar_init(o_done, 1);
     tc::mbar_init(mma_done, 1);
     *abort = 0;
@@ -141,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sv = smem + Smem::kV0 + s * kTileBytes;
 #pragma unroll 1
         for (int p = 0; p < BKV / PAGE; ++p) {
-          const int page = min(j * (BKV / PAGE) + p, last_page);  // clamp: masked keys read finite data
+          const int page = min((t_begin + j) * (BKV / PAGE) + p, last_page);  // clamp: masked keys read finite data
           const int blk = bt[page];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -207,12 +224,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
+    // Warps 2-9: thread = (row, half); half h owns key columns [64h, 64h+64)
+    // of S and output columns [64h, 64h+64) of O.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
     const int q_pos = pos0 + qoff + row;
     const float sc = a.scale_log2;
-    float m = -INFINITY, l = 0.f;
+    float* red = reinterpret_cast<float*>(smem + Smem::kRed);  // [parity][half][row]
+    float m = -INFINITY, l = 0.f;                              // l: this half's partial sum
     uint8_t* sP = smem + Smem::kP;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
@@ -220,41 +241,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!tc::mbar_wait(&s_full[s], (j >> 1) & 1, abort, a.timeout_ns)) {
         if (lane == 0) set_err(a.err, 13, abort);
         ok = false;
+      }
+      // every softmax thread must reach the exchange barrier, even after a timeout
+      uint32_t v[64];
+      float mx = -INFINITY;
+      if (ok) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t t[32];
+          tc::tmem_ld_32x32b_x32(tS + lane_addr + s * BKV + half * 64 + c * 32, t);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[c * 32 + i] = t[i];
+        }
+        tc::tmem_ld_wait();
+        const int kv0 = (t_begin + j) * BKV + half * 64;
+        const int lim = min(q_pos + 1, kv_end) - kv0;  // visible keys of this half: [0, lim)
+        if (lim >= 64) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float x = __uint_as_float(v[i]) * sc;
+            v[i] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float x = (i < lim) ? __uint_as_float(v[i]) * sc : -INFINITY;
+            v[i] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+        }
+      }
+      red[(s * 2 + half) * BQ + row] = mx;
+      tc::named_bar_sync(1, kSoftWarps * 32);
+      if (!ok || *abort) {
+        ok = false;
         break;
       }
-      tc::tc_fence_after();
-      uint32_t v[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t t[32];
-        tc::tmem_ld_32x32b_x32(tS + lane_addr + s * BKV + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[c * 32 + i] = t[i];
-      }
-      tc::tmem_ld_wait();
-      const int kv0 = j * BKV;
-      const int lim = min(q_pos + 1, kv_end) - kv0;  // keys [kv0, kv0+lim) are visible to this row
-      float mx = m;
-#pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        float x = __uint_as_float(v[i]) * sc;
-        x = (i < lim) ? x : -INFINITY;
-        v[i] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
-      }
-      const float corr = (m == -INFINITY) ? 1.f : tc::ex2(m - mx);
+      mx = fmaxf(mx, red[(s * 2 + (half ^ 1)) * BQ + row]);
+      // conditional rescale: keep the stale max unless the new one is much larger
+      const bool grow = mx > m + kRescaleThreshold || m == -INFINITY;
+      const float m_new = grow ? mx : m;
+      const float corr = (m == -INFINITY || !grow) ? 1.f : tc::ex2(m - m_new);
       float sum = 0.f;
-      uint32_t pk[BKV / 2];
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < BKV; i += 2) {
-        const float p0 = (mx == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i]) - mx);
-        const float p1 = (mx == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i + 1]) - mx);
+      for (int i = 0; i < 64; i += 2) {
+        const float p0 = (m_new == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i]) - m_new);
+        const float p1 = (m_new == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i + 1]) - m_new);
         sum += p0 + p1;
-        __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-        pk[i / 2] = *reinterpret_cast<uint32_t*>(&h);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+        pk[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
       }
       l = l * corr + sum;
-      m = mx;
+      m = m_new;
       if (j > 0) {
         // PV_{j-1} must be complete before O is rescaled and P is overwritten
         if (!tc::mbar_wait(o_done, (j - 1) & 1, abort, a.timeout_ns)) {
@@ -263,54 +304,84 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc::tc_fence_after();
+        // P_{j-1} is no longer read: store P_j first (its registers die), then rescale O
+        // this half's 64 keys are exactly P chunk `half` (K-major, 128B-swizzled)
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint8_t* dst = sP + half * kChunk + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
+        }
         if (__any_sync(0xffffffffu, corr < 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t t[32];
-            tc::tmem_ld_32x32b_x32(tO + lane_addr + c * 32, t);
+            tc::tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, t);
             tc::tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
-            tc::tmem_st_32x32b_x32(tO + lane_addr + c * 32, t);
+            tc::tmem_st_32x32b_x32(tO + lane_addr + half * 64 + c * 32, t);
           }
           tc::tmem_st_wait();
         }
-      }
-      // P row -> shared memory, K-major 128B-swizzled (keys 0-63 in chunk 0, 64-127 in chunk 1)
+      } else {
+        // this half's 64 keys are exactly P chunk `half` (K-major, 128B-swizzled)
 #pragma unroll
-      for (int c = 0; c < BKV / 8; ++c) {
-        const int kb = c >> 3, cc = c & 7;
-        uint8_t* dst = sP + kb * kChunk + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+        for (int cc = 0; cc < 8; ++cc) {
+          uint8_t* dst = sP + half * kChunk + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
+        }
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(p_full);
     }
+    // row sum = sum of the two halves' partial sums (both applied the same corrections)
+    red[(2 + half) * BQ + row] = l;
+    tc::named_bar_sync(1, kSoftWarps * 32);
+    const float l_tot = l + red[(2 + (half ^ 1)) * BQ + row];
     if (ok && n_tiles > 0) {
       if (!tc::mbar_wait(o_done, (n_tiles - 1) & 1, abort, a.timeout_ns)) {
         if (lane == 0) set_err(a.err, 13, abort);
       } else {
         tc::tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        __nv_bfloat16* dst = a.o + ((int64_t)(q_begin + qoff + row) * a.nq + head) * D;
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        const int64_t tok = q_begin + qoff + row;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t t[32];
-          tc::tmem_ld_32x32b_x32(tO + lane_addr + c * 32, t);
+          tc::tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, t);
           tc::tmem_ld_wait();
+          const int col = half * 64 + c * 32;
           if (row < rows_here) {
-            float f[8];
+            if (a.splits == 1) {
+              __nv_bfloat16* dst = a.o + (tok * a.nq + head) * D + col;
+              float f[8];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
+              for (int g = 0; g < 4; ++g) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(t[g * 8 + i]) * inv;
-              *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = pack_from<__nv_bfloat16>(f);
+                for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(t[g * 8 + i]) * inv;
+                *reinterpret_cast<uint4*>(dst + g * 8) = pack_from<__nv_bfloat16>(f);
+              }
+            } else {
+              float* dst = a.part_o + ((tok * a.nq + head) * a.splits + split) * D + col;
+#pragma unroll
+              for (int g = 0; g < 8; ++g)
+                *reinterpret_cast<float4*>(dst + g * 4) =
+                    make_float4(__uint_as_float(t[g * 4]) * inv, __uint_as_float(t[g * 4 + 1]) * inv,
+                                __uint_as_float(t[g * 4 + 2]) * inv, __uint_as_float(t[g * 4 + 3]) * inv);
             }
           }
         }
+        if (a.splits > 1 && row < rows_here && half == 0)
+          a.part_lse[(tok * a.nq + head) * a.splits + split] = (l_tot > 0.f) ? m + log2f(l_tot) : -INFINITY;
       }
+    } else if (n_tiles == 0 && a.splits > 1 && row < rows_here) {
+      // empty split: contributes nothing to the combine
+      const int64_t tok = q_begin + qoff + row;
+      float* dst = a.part_o + ((tok * a.nq + head) * a.splits + split) * D + half * 64;
+      for (int d = 0; d < 64; d += 4) *reinterpret_cast<float4*>(dst + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (half == 0) a.part_lse[(tok * a.nq + head) * a.splits + split] = -INFINITY;
     }
   }
 
@@ -376,8 +447,8 @@ CUtensorMap cached(const Key& k, const std::function<CUtensorMap()>& make) {
 
 void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
                                  const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
-                                 int n_tiles, int T, int nq, int nkv, int num_blocks, float scale, uint32_t* err,
-                                 cudaStream_t s) {
+                                 int n_tiles, int T, int nq, int nkv, int num_blocks, float scale, int splits,
+                                 float* part_o, float* part_lse, uint32_t* err, cudaStream_t s) {
   if (n_tiles == 0 || T == 0) return;
   if (nq % nkv != 0) throw std::runtime_error("fmha: nq must be a multiple of nkv");
   // Q: [T, nq, D] -> dims {D, nq, T}, box {64, 1, 128}
@@ -410,14 +481,19 @@ void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, 
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
   a.timeout_ns = 2000000000ull;
+  a.splits = std::max(1, splits);
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  if (a.splits > 1 && (!part_o || !part_lse)) throw std::runtime_error("fmha: split-KV needs scratch buffers");
   static bool attr = false;
   if (!attr) {
     MBX_CUDA_CHECK(cudaFuncSetAttribute(fmha_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kTotal));
     attr = true;
   }
-  dim3 grid(n_tiles, nq);
+  dim3 grid(n_tiles, nq, a.splits);
   fmha_tc_kernel<<<grid, kThreads, Smem::kTotal, s>>>(tq, tk, tv, a);
   MBX_CUDA_CHECK(cudaGetLastError());
+  if (a.splits > 1) attn_combine_launch(part_o, part_lse, (int64_t)T * nq, a.splits, o, s);
 }
 
 }  // namespace mbx

@@ -252,7 +252,8 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
 
 void prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor out,
                           torch::Tensor cu_q, torch::Tensor kv_len, torch::Tensor block_table, torch::Tensor tiles,
-                          double scale, torch::Tensor err) {
+                          double scale, torch::Tensor err, int64_t splits, c10::optional<torch::Tensor> part_o,
+                          c10::optional<torch::Tensor> part_lse) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(k_cache, "k_cache");
@@ -266,10 +267,18 @@ void prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor 
   }
   TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 2, "tiles must be [n, 2]");
   TORCH_CHECK(err.scalar_type() == torch::kInt32 && err.is_cuda(), "err must be an int32 CUDA word");
+  float *po = nullptr, *pl = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV prefill needs scratch tensors");
+    TORCH_CHECK(part_o->numel() >= q.size(0) * q.size(1) * splits * 128 && part_lse->numel() >= q.size(0) * q.size(1) * splits,
+                "split-KV prefill scratch too small");
+    po = part_o->data_ptr<float>();
+    pl = part_lse->data_ptr<float>();
+  }
   prefill_attention_tc_launch(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
                               cu_q.data_ptr<int>(), kv_len.data_ptr<int>(), block_table.data_ptr<int>(),
                               block_table.size(1), tiles.data_ptr<int>(), tiles.size(0), q.size(0), q.size(1),
-                              k_cache.size(1), k_cache.size(0), (float)scale,
+                              k_cache.size(1), k_cache.size(0), (float)scale, (int)splits, po, pl,
                               reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
 }
 

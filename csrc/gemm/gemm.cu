@@ -37,7 +37,10 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 
-enum EpiMode : int { kEpiBf16 = 0, kEpiF32Partial = 1, kEpiBf16AddResidual = 2, kEpiPushRS = 3 };
+// kEpiSwapF32Partial: the kernel runs on swapped operands (A = weights
+// [N_w, K], B = activations [M_tok, K], tile rows = output features, tile
+// columns = tokens) and writes fp32 partials transposed to [split][token][feature].
+enum EpiMode : int { kEpiBf16 = 0, kEpiF32Partial = 1, kEpiBf16AddResidual = 2, kEpiPushRS = 3, kEpiSwapF32Partial = 4 };
 
 struct GemmArgs {
   void* out;             // bf16 C (ldc) or fp32 partials [splits][M][N]
@@ -255,7 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gcol = n * BN + c0;
         const int valid = min(32, args.N - gcol);
         if (row_ok && valid > 0) {
-          if (EPI == kEpiPushRS) {
+          if (EPI == kEpiSwapF32Partial) {
+            // row = output feature, columns = tokens: store column j of the tile as
+            // partial[ks][token][feature] (consecutive threads = consecutive features)
+            float* base = static_cast<float*>(args.out) + (int64_t)ks * args.N * args.M + grow;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < valid) base[(int64_t)(gcol + j) * args.M] = __uint_as_float(r[j]);
+          } else if (EPI == kEpiPushRS) {
             const int owner = grow / args.Mo;
             const int lrow = grow - owner * args.Mo;
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(
@@ -420,6 +430,11 @@ void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
 
 template <int EPI>
 void launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
+  if (EPI == kEpiSwapF32Partial) {
+    if (bn == 32) launch_cfg<32, 8, EPI>(ta, tb, a, grid, s);
+    else launch_cfg<64, 8, EPI>(ta, tb, a, grid, s);
+    return;
+  }
   switch (bn) {
     case 256: launch_cfg<256, 4, EPI>(ta, tb, a, grid, s); break;
     case 224: launch_cfg<224, 5, EPI>(ta, tb, a, grid, s); break;
@@ -467,9 +482,29 @@ GemmPlan plan_for(int64_t M, int64_t N, int64_t K, int sms) {
   return p;
 }
 
+// Decode shapes (M <= 64 tokens): operands swapped, tokens on the N side.
+GemmPlan swap_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  GemmPlan p;
+  p.bn = M <= 32 ? 32 : 64;
+  const int64_t kb_total = (K + BK - 1) / BK;
+  const int64_t num_f = (N + BM - 1) / BM;
+  const int64_t want = std::max<int64_t>(1, (sms + num_f - 1) / num_f);
+  int64_t sp = std::min<int64_t>(want, std::max<int64_t>(1, kb_total / 2));
+  sp = std::min<int64_t>(sp, 32);
+  const int64_t per = (kb_total + sp - 1) / sp;
+  p.splits = (int)((kb_total + per - 1) / per);
+  return p;
+}
+
 }  // namespace
 
-GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) { return plan_for(M, N, K, num_sms()); }
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
+  if (M <= 64 && N % 4 == 0) {
+    GemmPlan sp = swap_plan(M, N, K, num_sms());
+    if (sp.splits > 1) return sp;
+  }
+  return plan_for(M, N, K, num_sms());
+}
 
 void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
                             int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
@@ -512,6 +547,8 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
                  cudaStream_t s) {
   if (M == 0 || N == 0) return;
+  // explicit bn/splits requests keep the regular orientation (tests, tuning)
+  const bool swap_ok = bn <= 0 && splits <= 0 && N % 4 == 0;
   if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm: K and N must be multiples of 8");
   if (ldc % 8 != 0 || ((uint64_t)C & 15) != 0) throw std::runtime_error("gemm: C must be 16-byte aligned rows");
   const int sms = num_sms();
@@ -534,6 +571,33 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   a.splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
   a.err = err;
   a.timeout_ns = 2000000000ull;
+  const GemmPlan swp = swap_plan(M, N, K, sms);
+  if (M <= 64 && workspace != nullptr && swap_ok && swp.splits > 1) {
+    // Decode shapes: weights take the 128-row MMA side, the <= 64 tokens the
+    // N side (32 or 64), K split so every SM streams its share of the weights.
+    const int bnt = swp.bn;
+    const int64_t num_f = (N + BM - 1) / BM;
+    const int64_t sp = swp.splits;
+    const int64_t per = (a.kb_total + sp - 1) / sp;
+    GemmArgs sw = a;
+    sw.M = (int)N;  // kernel rows = features
+    sw.N = (int)M;  // kernel columns = tokens
+    sw.num_m = (int)num_f;
+    sw.num_n = 1;
+    sw.splits = (int)sp;
+    sw.kb_per_split = (int)per;
+    sw.out = workspace;
+    const CUtensorMap tw = make_map(B, N, K, ldb, BM);
+    const CUtensorMap tx = make_map(A, M, K, lda, bnt);
+    launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, sw, (int)std::min<int64_t>(num_f * sp, sms), s);
+    const int64_t MN = M * N;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
+    splitk_reduce_kernel<<<(int)std::max<int64_t>(1, blocks), threads, 0, s>>>(
+        workspace, (int)sp, MN, (int)N, (__nv_bfloat16*)C, ldc, a.residual);
+    MBX_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const CUtensorMap ta = make_map(A, M, K, lda, BM);
   const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);
   const int units = a.num_m * a.num_n * a.splits;

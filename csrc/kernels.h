@@ -66,10 +66,15 @@ void prefill_attention_launch(const void* q, const void* kc, const void* vc, voi
                               const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
                               int n_tiles, int nq, int nkv, float scale, cudaStream_t s);
 // tcgen05/TMEM prefill attention (128-row query tiles, 128-key tiles).
+// splits > 1 splits every query tile's keys across CTAs (partials in
+// part_o [T, nq, splits, 128] / part_lse [T, nq, splits], merged in place).
 void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
                                  const int* kv_len, const int* block_table, int max_blocks, const int* tiles,
-                                 int n_tiles, int T, int nq, int nkv, int num_blocks, float scale, uint32_t* err,
-                                 cudaStream_t s);
+                                 int n_tiles, int T, int nq, int nkv, int num_blocks, float scale, int splits,
+                                 float* part_o, float* part_lse, uint32_t* err, cudaStream_t s);
+// LSE-weighted merge of split partials: rows x splits x 128 -> bf16 rows x 128.
+void attn_combine_launch(const float* part_o, const float* part_lse, int64_t rows, int splits, void* out,
+                         cudaStream_t s);
 void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
                              const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
                              float* part_o, float* part_lse, float scale, cudaStream_t s);

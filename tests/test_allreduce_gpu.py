@@ -62,6 +62,8 @@ def test_multi_gpu_allreduce_suite():
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            os.path.join(ROOT, "tests", "mp_allreduce_worker.py")]
     p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=700)
-    tail = (p.stdout[-4000:] + "\n" + p.stderr[-4000:])
-    assert p.returncode == 0, tail
+    out = p.stdout + "\n" + p.stderr
+    err_at = out.find("WORKER-ERROR")
+    detail = out[err_at:err_at + 6000] if err_at >= 0 else out[-4000:]
+    assert p.returncode == 0, detail
     assert "ALLREDUCE-SUITE-PASS" in p.stdout, tail

@@ -22,7 +22,7 @@ def _paged(lengths, nkv, blocks_per_req, seed=0):
     return kc, vc, bt
 
 
-@pytest.mark.parametrize("kernel", ["tc", "mma"])
+@pytest.mark.parametrize("kernel", ["tc", "tc_split4", "mma"])
 @pytest.mark.parametrize("nq,nkv", [(32, 8), (4, 1), (8, 1)])
 def test_prefill_chunked_ragged(nq, nkv, kernel):
     ops, ref = sub("ops"), sub("ops.reference")
@@ -33,8 +33,9 @@ def test_prefill_chunked_ragged(nq, nkv, kernel):
     q = torch.randn(T, nq, D, device="cuda").to(torch.bfloat16)
     cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32, device="cuda")
     kvl = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
-    if kernel == "tc":
-        out = ops.prefill_attention(q, kc, vc, cu, kvl, bt, ops.prefill_tiles(q_lens).cuda())
+    if kernel.startswith("tc"):
+        sp = 4 if kernel == "tc_split4" else 1
+        out = ops.prefill_attention(q, kc, vc, cu, kvl, bt, ops.prefill_tiles(q_lens).cuda(), splits=sp)
     else:
         out = ops.prefill_attention_mma(q, kc, vc, cu, kvl, bt, ops.prefill_tiles(q_lens, bq=64).cuda())
     torch.cuda.synchronize()

@@ -22,6 +22,10 @@ SHAPES = [
     (1024, 6144, 1024, 192, 1),   # BN=192
     (1024, 28672, 512, 224, 1),   # BN=224
     (130, 448, 640, 224, 1),      # BN=224 with tails
+    (1, 768, 4096, 0, 0),         # swap-AB decode: TP=8 qkv, bs=1
+    (33, 3584, 4096, 0, 0),       # swap-AB, 33 tokens (N side 64)
+    (17, 4096, 512, 0, 0),        # swap-AB, short K
+    (64, 4096, 1792, 0, 0),       # swap-AB, bs=64 TP=8 down
 ]
 
 
@@ -38,6 +42,19 @@ def test_gemm_matches_fp32(M, N, K, bn, splits):
     err = (out.float() - ref).abs().max().item()
     scale = ref.abs().max().item()
     assert err <= 1e-2 * scale + 1e-2, f"max err {err} vs scale {scale}"
+
+
+def test_gemm_swap_residual():
+    """Decode-shaped GEMM (swap-AB path) with the residual add in the reduce."""
+    ops = sub("ops")
+    torch.manual_seed(4)
+    M, N, K = 5, 4096, 2048
+    a = (torch.randn(M, K, device="cuda") / 5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") / 5).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    out = ops.gemm(a, w, residual=r)
+    ref = (a.float() @ w.float().t()).to(torch.bfloat16).float() + r.float()
+    assert (out.float() - ref).abs().max().item() < 0.1
 
 
 def test_gemm_residual_epilogue():

@@ -97,3 +97,20 @@ def test_chunk_size_does_not_change_tokens():
         eng = eng_mod.LLMEngine(cfg, max_batch=4, max_seq=512, chunk=chunk, seed=9, use_graphs=False)
         res.append(eng.generate(prompts, max_new_tokens=6))
     assert res[0] == res[1]
+
+
+def test_prefill_graph_matches_eager():
+    """Full single-request chunks replayed from a captured graph give the same
+    tokens as the eager chunk forwards (partial last chunks stay eager)."""
+    models, eng_mod = sub("models"), sub("engine")
+    cfg = models.LlamaConfig.tiny()
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=torch.Generator().manual_seed(n)).tolist()
+               for n in (128, 200, 64)]
+    res = []
+    for pg in (False, True):
+        eng = eng_mod.LLMEngine(cfg, max_batch=4, max_seq=512, chunk=64, seed=13, use_graphs=False,
+                                prefill_graph=pg)
+        res.append(eng.generate(prompts, max_new_tokens=5))
+        if pg:
+            assert eng.prefill_graph.graph is not None
+    assert res[0] == res[1]
