@@ -49,7 +49,8 @@ def parse():
     p.add_argument("--prompt-len", type=int, default=4096)
     p.add_argument("--chunk", type=int, default=1024)
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--no-graph", action="store_true", help="launch every chunk's kernels eagerly")
+    p.add_argument("--no-graph", action="store_true", help="launch every chunk's kernels eagerly (the torch "
+                   "baseline always does: like sglang, it graphs decode only)")
     return p.parse_args()
 
 
@@ -80,7 +81,7 @@ def main():
     cfg = models.LlamaConfig.by_name(args.model)
     R, S, chunk = args.requests, args.prompt_len, args.chunk
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=R, max_seq=S + 16, chunk=chunk, seed=0, use_graphs=False,
-                            impl=args.impl, prefill_graph=not args.no_graph)
+                            impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graph))
     g = torch.Generator().manual_seed(1234)
     prompts = torch.randint(0, cfg.vocab, (R, S), generator=g).tolist()
 
@@ -199,6 +200,7 @@ def main():
                 "l2": "no flush: weights (16 GB) and KV cache (8 GB) exceed the 126 MB L2 every step",
                 "baseline_number": "1464 tok/s, reference docs/performance.md:43 (2x RTX 3080, 27B AWQ, TP=2)",
                 "transport": getattr(tp.ca_comm, "transport", None) if (tp and tp.ca_comm) else None,
+                "prefill_cuda_graph": eng.prefill_graph is not None,
             },
             "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")} if clocks else None,
             "e2e": e2e,
