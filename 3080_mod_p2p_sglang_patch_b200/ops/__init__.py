@@ -22,6 +22,8 @@ class _Workspace:
     def __init__(self, device):
         self.device = device
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        # split-K tile arrival counters (each reset by the tile's last CTA)
+        self.counters = torch.zeros(65536, dtype=torch.int32, device=device)
         self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
         self.dec_o = torch.empty(0, dtype=torch.float32, device=device)
         self.dec_lse = torch.empty(0, dtype=torch.float32, device=device)
@@ -88,7 +90,9 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
     plan_bn, plan_splits = C.gemm_plan(M, N, K)
     s = splits or plan_splits
     wbuf = ws.gemm(s * M * N) if s > 1 else None
-    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits)
+    # split-K partials are folded by a separate reduce kernel: the in-kernel
+    # reduction (pass ws.counters) measured no faster at 1 token and slower at 64
+    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, None)
     launches.add(2 if s > 1 else 1)
     return out
 
@@ -161,7 +165,7 @@ def argmax_combine(vals, idx, out=None):
     return out
 
 
-PREFILL_BQ = 128  # query rows per tile of the tcgen05 prefill kernel
+PREFILL_BQ = 256  # query rows per CTA of the tcgen05 prefill kernel (two 128-row tiles)
 
 
 def prefill_tiles(q_lens, bq: int = PREFILL_BQ):
@@ -176,14 +180,15 @@ def prefill_tiles(q_lens, bq: int = PREFILL_BQ):
 
 
 def prefill_splits(n_tiles: int, nq: int, max_kv: int, sms: int = 148) -> int:
-    """Split-KV factor for the prefill kernel: enough CTAs to cover the SMs
-    when a chunk has few query tiles x heads (high TP), at least 2 key tiles
-    (256 keys) per split."""
+    """Split-KV factor for the prefill kernel. Splitting costs a partial
+    write plus a combine pass, which only pays when fewer than half the SMs
+    would be busy (high TP: few heads per rank); then enough splits to cover
+    the SMs, at least 512 keys per split."""
     ctas = max(1, n_tiles * nq)
-    if ctas >= sms:
+    if 2 * ctas > sms:
         return 1
     want = -(-sms // ctas)
-    return int(max(1, min(want, max_kv // 256, 16)))
+    return int(max(1, min(want, max_kv // 512, 16)))
 
 
 def prefill_attention(q, k_cache, v_cache, cu_q, kv_len, block_table, tiles, scale=None, out=None, splits=1):

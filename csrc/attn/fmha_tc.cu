@@ -1,7 +1,10 @@
 // Prefill attention on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA = 128 query rows of one q-head. For every 128-key tile of the
-// request's paged KV cache:
+// One CTA = two 128-row query tiles (256 queries) of one q-head, each with
+// its own softmax warpgroup, sharing the K/V stages; the single MMA thread
+// interleaves both tiles' S and PV MMAs so the tensor core has independent
+// work while either softmax runs. For every 64-key tile of the request's
+// paged KV cache (per query tile):
 //   S_j  = Q K_j^T      tcgen05.mma (M=128, N=128, K=128 head dims), fp32 in
 //                       TMEM, double-buffered (S_{j+1} overlaps softmax_j)
 //   P_j  = exp2(S_j*scale - m)   online softmax by 4 warps (one row per
@@ -36,23 +39,27 @@ namespace mbx {
 namespace {
 
 constexpr int D = 128;
-constexpr int BQ = 128;
-constexpr int BKV = 128;
+constexpr int BQ = 128;             // rows per query tile
+constexpr int QT = 2;               // query tiles per CTA (ping-pong)
+constexpr int BKV = 64;             // keys per KV tile
+constexpr int NS = 3;               // K/V pipeline stages
 constexpr int PAGE = 16;
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two halves of each row)
-constexpr int kSoftWarps = 8;
+constexpr int kThreads = 320;       // warp 0 TMA, warp 1 MMA, warps 2-5 / 6-9 softmax of tile 0 / 1
+constexpr int kQBytes = BQ * D * 2;           // 32 KB, two 16 KB column chunks
+constexpr int kQChunk = BQ * 64 * 2;          // 16 KB
+constexpr int kKVBytes = BKV * D * 2;         // 16 KB, two 8 KB column chunks
+constexpr int kKVChunk = BKV * 64 * 2;        // 8 KB
+constexpr int kPBytes = BQ * BKV * 2;         // 16 KB: [128 rows x 64 keys], one 128B-wide chunk
 // Rescale the running output only when a row max grows by more than this
 // (log2 units): exponents stay <= 2^8, harmless in fp32/bf16.
 constexpr float kRescaleThreshold = 8.f;
-constexpr int kTileBytes = BQ * D * 2;  // 32 KB: one [128 x 128] bf16 tile (two 16 KB column chunks)
-constexpr int kChunk = 16384;           // [128 rows x 64] bf16
 
 struct FmhaArgs {
   __nv_bfloat16* o;         // [T, nq, D]
   const int* cu_q;          // [R+1]
   const int* kv_len;        // [R]
   const int* block_table;   // [R, max_blocks]
-  const int2* tiles;        // (request, q offset), 128-row tiles
+  const int2* tiles;        // (request, q offset): 256-row query-tile pairs
   float* part_o;            // splits > 1: [T, nq, splits, D] normalised partial outputs
   float* part_lse;          //             [T, nq, splits] log2-sum-exp
   int splits;
@@ -63,12 +70,11 @@ struct FmhaArgs {
 };
 
 struct Smem {
-  static constexpr int kQ = 0;
-  static constexpr int kK0 = kQ + kTileBytes;
-  static constexpr int kV0 = kK0 + 2 * kTileBytes;
-  static constexpr int kP = kV0 + 2 * kTileBytes;
-  static constexpr int kRed = kP + kTileBytes;              // [2 parity][2 half][128 rows] fp32 row maxima
-  static constexpr int kBar = kRed + 2 * 2 * BQ * 4;
+  static constexpr int kQ = 0;                          // [QT] query tiles
+  static constexpr int kK = kQ + QT * kQBytes;          // [NS] key tiles
+  static constexpr int kV = kK + NS * kKVBytes;         // [NS] value tiles
+  static constexpr int kP = kV + NS * kKVBytes;         // [QT] probability tiles
+  static constexpr int kBar = kP + QT * kPBytes;
   static constexpr int kTotal = kBar + 256 + 1024;
 };
 
@@ -84,13 +90,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::kBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_done = bars + 8;
-  uint64_t* mma_done = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* kv_full = bars + 1;          // [NS]
+  uint64_t* kv_empty = kv_full + NS;     // [NS]
+  uint64_t* s_full = kv_empty + NS;      // [QT][2]
+  uint64_t* p_full = s_full + 2 * QT;    // [QT]
+  uint64_t* o_done = p_full + QT;        // [QT]
+  uint64_t* mma_done = o_done + QT;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,26 +107,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_begin = a.cu_q[r], q_len = a.cu_q[r + 1] - q_begin;
   const int L = a.kv_len[r];
   const int pos0 = L - q_len;
-  const int rows_here = min(BQ, q_len - qoff);
-  const int kv_end = min(L, pos0 + qoff + rows_here);  // causal bound of the tile
-  const int n_all = (kv_end + BKV - 1) / BKV;
-  // split-KV: this CTA takes key tiles [t_begin, t_end) of the query tile
+  const int* bt = a.block_table + (int64_t)r * a.max_blocks;
+  // per query tile: valid rows, causal key bound, KV tiles needed
+  int rows_t[QT], kvend_t[QT], n_t[QT];
+#pragma unroll
+  for (int t = 0; t < QT; ++t) {
+    rows_t[t] = max(0, min(BQ, q_len - qoff - t * BQ));
+    kvend_t[t] = rows_t[t] > 0 ? min(L, pos0 + qoff + t * BQ + rows_t[t]) : 0;
+    n_t[t] = (kvend_t[t] + BKV - 1) / BKV;
+  }
+  const int n_all = max(n_t[0], n_t[1]);
+  const int kv_end_all = max(kvend_t[0], kvend_t[1]);
+  // split-KV: this CTA takes KV tiles [tb, te)
   const int split = blockIdx.z;
   const int per = (n_all + a.splits - 1) / a.splits;
-  const int t_begin = min(n_all, split * per);
-  const int t_end = min(n_all, t_begin + per);
-  const int n_tiles = t_end - t_begin;
-  const int* bt = a.block_table + (int64_t)r * a.max_blocks;
+  const int tb = min(n_all, split * per);
+  const int te = min(n_all, tb + per);
+  const int n_cta = te - tb;
+  int nt[QT];
+#pragma unroll
+  for (int t = 0; t < QT; ++t) nt[t] = max(0, min(te, n_t[t]) - tb);
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       tc::mbar_init(&kv_full[i], 1);
       tc::mbar_init(&kv_empty[i], 1);
-      tc::mbar_init(&s_full[i], 1);
     }
-    tc::mbar_init(p_full, kSoftWarps);
-    tc::mbar_init(o_done, 1);
+    for (int t = 0; t < QT; ++t) {
+      tc::mbar_init(&s_full[2 * t], 1);
+      tc::mbar_init(&s_full[2 * t + 1], 1);
+      tc::mbar_init(&p_full[t], 4);
+      tc::mbar_init(&o_done[t], 1);
+    }
     tc::mbar_init(mma_done, 1);
     *abort = 0;
     tc::fence_barrier_init();
@@ -133,8 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;         // S buffers: columns [0,128) and [128,256)
-  const uint32_t tO = tmem + 256;   // O: columns [256,384)
+  // TMEM columns: S[t][b] at (2t + b) * 64, O[t] at 256 + 128 t
+  auto tS = [&](int t, int b) { return tmem + (uint32_t)((2 * t + b) * BKV); };
+  auto tO = [&](int t) { return tmem + 256u + (uint32_t)(t * D); };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
@@ -142,81 +162,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tma_prefetch_desc(&tmQ);
       tc::tma_prefetch_desc(&tmK);
       tc::tma_prefetch_desc(&tmV);
-      tc::mbar_arrive_expect_tx(q_full, kTileBytes);
-      for (int c = 0; c < 2; ++c)
-        tc::tma_load_3d(smem + Smem::kQ + c * kChunk, &tmQ, q_full, c * 64, head, q_begin + qoff);
-      const int last_page = (kv_end - 1) / PAGE;
+      tc::mbar_arrive_expect_tx(q_full, QT * kQBytes);
+      for (int t = 0; t < QT; ++t)
+        for (int c = 0; c < 2; ++c)
+          tc::tma_load_3d(smem + Smem::kQ + t * kQBytes + c * kQChunk, &tmQ, q_full, c * 64, head,
+                          q_begin + qoff + t * BQ);
+      const int last_page = max(0, (kv_end_all - 1) / PAGE);
       int issued = 0;
-      for (int j = 0; j < n_tiles && !*abort; ++j, ++issued) {
-        const int s = j & 1;
-        if (!tc::mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, a.timeout_ns)) {
+      for (int j = 0; j < n_cta && !*abort; ++j, ++issued) {
+        const int s = j % NS;
+        if (!tc::mbar_wait(&kv_empty[s], ((j / NS) & 1) ^ 1, abort, a.timeout_ns)) {
           set_err(a.err, 11, abort);
           break;
         }
-        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
-        uint8_t* sk = smem + Smem::kK0 + s * kTileBytes;
-        uint8_t* sv = smem + Smem::kV0 + s * kTileBytes;
+        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
+        uint8_t* sk = smem + Smem::kK + s * kKVBytes;
+        uint8_t* sv = smem + Smem::kV + s * kKVBytes;
 #pragma unroll 1
         for (int p = 0; p < BKV / PAGE; ++p) {
-          const int page = min((t_begin + j) * (BKV / PAGE) + p, last_page);  // clamp: masked keys read finite data
+          const int page = min((tb + j) * (BKV / PAGE) + p, last_page);  // clamp: masked keys read finite data
           const int blk = bt[page];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            tc::tma_load_4d(sk + c * kChunk + p * (PAGE * 128), &tmK, &kv_full[s], c * 64, 0, kvh, blk);
-            tc::tma_load_4d(sv + c * kChunk + p * (PAGE * 128), &tmV, &kv_full[s], c * 64, 0, kvh, blk);
+            tc::tma_load_4d(sk + c * kKVChunk + p * (PAGE * 128), &tmK, &kv_full[s], c * 64, 0, kvh, blk);
+            tc::tma_load_4d(sv + c * kKVChunk + p * (PAGE * 128), &tmV, &kv_full[s], c * 64, 0, kvh, blk);
           }
         }
       }
-      // drain this thread's in-flight copies before the CTA can exit
       volatile int never = 0;
       tc::mbar_wait(q_full, 0, &never, 200000000ull);
-      for (int j = max(0, issued - 2); j < issued; ++j)
-        tc::mbar_wait(&kv_full[j & 1], (j >> 1) & 1, &never, 200000000ull);
+      for (int j = max(0, issued - NS); j < issued; ++j)
+        tc::mbar_wait(&kv_full[j % NS], (j / NS) & 1, &never, 200000000ull);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (tc::elect_one()) {
       constexpr uint32_t idS = tc::idesc_bf16_f32_major(BQ, BKV, 0, 0);  // Q K-major, K K-major
       constexpr uint32_t idO = tc::idesc_bf16_f32_major(BQ, D, 0, 1);    // P K-major, V MN-major
-      const uint32_t sQ = tc::smem_u32(smem + Smem::kQ);
-      const uint32_t sP = tc::smem_u32(smem + Smem::kP);
       bool ok = tc::mbar_wait(q_full, 0, abort, a.timeout_ns);
       if (!ok) set_err(a.err, 12, abort);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!tc::mbar_wait(&kv_full[s], (j >> 1) & 1, abort, a.timeout_ns)) {
+        const int s = j % NS;
+        if (!tc::mbar_wait(&kv_full[s], (j / NS) & 1, abort, a.timeout_ns)) {
           set_err(a.err, 12, abort);
           return false;
         }
         tc::tc_fence_after();
-        const uint32_t sK = tc::smem_u32(smem + Smem::kK0 + s * kTileBytes);
+        const uint32_t sK = tc::smem_u32(smem + Smem::kK + s * kKVBytes);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kChunk + (kk & 3) * 32;
-          tc::mma_bf16(tS + s * BKV, tc::sw128_desc(sQ + off, 16, 1024), tc::sw128_desc(sK + off, 16, 1024), idS,
-                       kk > 0 ? 1u : 0u);
+        for (int t = 0; t < QT; ++t) {
+          if (j >= nt[t]) continue;
+          const uint32_t sQ = tc::smem_u32(smem + Smem::kQ + t * kQBytes);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qoff_b = (kk >> 2) * kQChunk + (kk & 3) * 32;
+            const uint32_t koff_b = (kk >> 2) * kKVChunk + (kk & 3) * 32;
+            tc::mma_bf16(tS(t, j & 1), tc::sw128_desc(sQ + qoff_b, 16, 1024), tc::sw128_desc(sK + koff_b, 16, 1024),
+                         idS, kk > 0 ? 1u : 0u);
+          }
+          tc::mma_commit(&s_full[2 * t + (j & 1)]);
         }
-        tc::mma_commit(&s_full[s]);
         return true;
       };
-      if (ok && n_tiles > 0) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!tc::mbar_wait(p_full, j & 1, abort, a.timeout_ns)) {
-          set_err(a.err, 12, abort);
-          break;
-        }
-        tc::tc_fence_after();
-        const uint32_t sV = tc::smem_u32(smem + Smem::kV0 + (j & 1) * kTileBytes);
+      if (ok && n_cta > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_cta; ++j) {
+        if (j + 1 < n_cta && !issue_s(j + 1)) break;
+        const uint32_t sV = tc::smem_u32(smem + Smem::kV + (j % NS) * kKVBytes);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * kChunk + (kk & 3) * 32;  // P: keys along K, 2 chunks of 64
-          const uint32_t voff = kk * 16 * 128;                        // V: 16 key rows of 128 B per step
-          tc::mma_bf16(tO, tc::sw128_desc(sP + poff, 16, 1024), tc::sw128_desc(sV + voff, kChunk, 1024), idO,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+        for (int t = 0; t < QT; ++t) {
+          if (j >= nt[t]) continue;
+          if (!tc::mbar_wait(&p_full[t], j & 1, abort, a.timeout_ns)) {
+            set_err(a.err, 12, abort);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sP = tc::smem_u32(smem + Smem::kP + t * kPBytes);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            // P: keys along K within one 128B chunk; V: 16 key rows of 128 B per step, MN atoms 8 KB apart
+            tc::mma_bf16(tO(t), tc::sw128_desc(sP + kk * 32, 16, 1024), tc::sw128_desc(sV + kk * 16 * 128, kKVChunk, 1024),
+                         idO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&o_done[t]);
         }
-        tc::mma_commit(&kv_empty[j & 1]);
-        tc::mma_commit(o_done);
+        if (!ok) break;
+        tc::mma_commit(&kv_empty[j % NS]);
       }
       tc::mma_commit(mma_done);
       volatile int never = 0;
@@ -224,70 +255,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
-    // Warps 2-9: thread = (row, half); half h owns key columns [64h, 64h+64)
-    // of S and output columns [64h, 64h+64) of O.
+    // Warps 2-5 own query tile 0, warps 6-9 tile 1; one thread per row.
+    const int t = (warp - 2) >> 2;
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    const int q_pos = pos0 + qoff + row;
+    const int q_pos = pos0 + qoff + t * BQ + row;
     const float sc = a.scale_log2;
-    float* red = reinterpret_cast<float*>(smem + Smem::kRed);  // [parity][half][row]
-    float m = -INFINITY, l = 0.f;                              // l: this half's partial sum
-    uint8_t* sP = smem + Smem::kP;
+    const int my_n = nt[t];
+    float m = -INFINITY, l = 0.f;
+    uint8_t* sP = smem + Smem::kP + t * kPBytes;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int s = j & 1;
-      if (!tc::mbar_wait(&s_full[s], (j >> 1) & 1, abort, a.timeout_ns)) {
+    for (int j = 0; j < my_n; ++j) {
+      const int b = j & 1;
+      if (!tc::mbar_wait(&s_full[2 * t + b], (j >> 1) & 1, abort, a.timeout_ns)) {
         if (lane == 0) set_err(a.err, 13, abort);
-        ok = false;
-      }
-      // every softmax thread must reach the exchange barrier, even after a timeout
-      uint32_t v[64];
-      float mx = -INFINITY;
-      if (ok) {
-        tc::tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t t[32];
-          tc::tmem_ld_32x32b_x32(tS + lane_addr + s * BKV + half * 64 + c * 32, t);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[c * 32 + i] = t[i];
-        }
-        tc::tmem_ld_wait();
-        const int kv0 = (t_begin + j) * BKV + half * 64;
-        const int lim = min(q_pos + 1, kv_end) - kv0;  // visible keys of this half: [0, lim)
-        if (lim >= 64) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float x = __uint_as_float(v[i]) * sc;
-            v[i] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float x = (i < lim) ? __uint_as_float(v[i]) * sc : -INFINITY;
-            v[i] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
-        }
-      }
-      red[(s * 2 + half) * BQ + row] = mx;
-      tc::named_bar_sync(1, kSoftWarps * 32);
-      if (!ok || *abort) {
         ok = false;
         break;
       }
-      mx = fmaxf(mx, red[(s * 2 + (half ^ 1)) * BQ + row]);
-      // conditional rescale: keep the stale max unless the new one is much larger
-      const bool grow = mx > m + kRescaleThreshold || m == -INFINITY;
+      tc::tc_fence_after();
+      uint32_t v[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t tt[32];
+        tc::tmem_ld_32x32b_x32(tS(t, b) + lane_addr + c * 32, tt);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[c * 32 + i] = tt[i];
+      }
+      tc::tmem_ld_wait();
+      const int kv0 = (tb + j) * BKV;
+      const int lim = min(q_pos + 1, kvend_t[t]) - kv0;  // keys [kv0, kv0 + lim) are visible
+      float mx = -INFINITY;
+      if (lim >= BKV) {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i) {
+          const float x = __uint_as_float(v[i]) * sc;
+          v[i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i) {
+          const float x = (i < lim) ? __uint_as_float(v[i]) * sc : -INFINITY;
+          v[i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      const bool grow = mx > m + kRescaleThreshold || (m == -INFINITY && mx != -INFINITY);
       const float m_new = grow ? mx : m;
       const float corr = (m == -INFINITY || !grow) ? 1.f : tc::ex2(m - m_new);
       float sum = 0.f;
-      uint32_t pk[32];
+      uint32_t pk[BKV / 2];
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < BKV; i += 2) {
         const float p0 = (m_new == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i]) - m_new);
         const float p1 = (m_new == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i + 1]) - m_new);
         sum += p0 + p1;
@@ -297,91 +317,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       l = l * corr + sum;
       m = m_new;
       if (j > 0) {
-        // PV_{j-1} must be complete before O is rescaled and P is overwritten
-        if (!tc::mbar_wait(o_done, (j - 1) & 1, abort, a.timeout_ns)) {
+        // PV_{j-1} must be complete before P is overwritten and O is rescaled
+        if (!tc::mbar_wait(&o_done[t], (j - 1) & 1, abort, a.timeout_ns)) {
           if (lane == 0) set_err(a.err, 13, abort);
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        // P_{j-1} is no longer read: store P_j first (its registers die), then rescale O
-        // this half's 64 keys are exactly P chunk `half` (K-major, 128B-swizzled)
+      }
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint8_t* dst = sP + half * kChunk + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
+      for (int cc = 0; cc < BKV / 8; ++cc) {
+        uint8_t* dst = sP + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, corr < 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t tt[32];
+          tc::tmem_ld_32x32b_x32(tO(t) + lane_addr + c * 32, tt);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) tt[i] = __float_as_uint(__uint_as_float(tt[i]) * corr);
+          tc::tmem_st_32x32b_x32(tO(t) + lane_addr + c * 32, tt);
         }
-        if (__any_sync(0xffffffffu, corr < 1.f)) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t t[32];
-            tc::tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, t);
-            tc::tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * corr);
-            tc::tmem_st_32x32b_x32(tO + lane_addr + half * 64 + c * 32, t);
-          }
-          tc::tmem_st_wait();
-        }
-      } else {
-        // this half's 64 keys are exactly P chunk `half` (K-major, 128B-swizzled)
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint8_t* dst = sP + half * kChunk + (row >> 3) * 1024 + (row & 7) * 128 + ((cc ^ (row & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
-        }
+        tc::tmem_st_wait();
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(p_full);
+      if (lane == 0) tc::mbar_arrive(&p_full[t]);
     }
-    // row sum = sum of the two halves' partial sums (both applied the same corrections)
-    red[(2 + half) * BQ + row] = l;
-    tc::named_bar_sync(1, kSoftWarps * 32);
-    const float l_tot = l + red[(2 + (half ^ 1)) * BQ + row];
-    if (ok && n_tiles > 0) {
-      if (!tc::mbar_wait(o_done, (n_tiles - 1) & 1, abort, a.timeout_ns)) {
+    const int rows_here = rows_t[t];
+    const int64_t tok = q_begin + qoff + t * BQ + row;
+    if (ok && my_n > 0) {
+      if (!tc::mbar_wait(&o_done[t], (my_n - 1) & 1, abort, a.timeout_ns)) {
         if (lane == 0) set_err(a.err, 13, abort);
       } else {
         tc::tc_fence_after();
-        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-        const int64_t tok = q_begin + qoff + row;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t t[32];
-          tc::tmem_ld_32x32b_x32(tO + lane_addr + half * 64 + c * 32, t);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t tt[32];
+          tc::tmem_ld_32x32b_x32(tO(t) + lane_addr + c * 32, tt);
           tc::tmem_ld_wait();
-          const int col = half * 64 + c * 32;
           if (row < rows_here) {
             if (a.splits == 1) {
-              __nv_bfloat16* dst = a.o + (tok * a.nq + head) * D + col;
+              __nv_bfloat16* dst = a.o + (tok * a.nq + head) * D + c * 32;
               float f[8];
 #pragma unroll
               for (int g = 0; g < 4; ++g) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(t[g * 8 + i]) * inv;
+                for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(tt[g * 8 + i]) * inv;
                 *reinterpret_cast<uint4*>(dst + g * 8) = pack_from<__nv_bfloat16>(f);
               }
             } else {
-              float* dst = a.part_o + ((tok * a.nq + head) * a.splits + split) * D + col;
+              float* dst = a.part_o + ((tok * a.nq + head) * a.splits + split) * D + c * 32;
 #pragma unroll
               for (int g = 0; g < 8; ++g)
                 *reinterpret_cast<float4*>(dst + g * 4) =
-                    make_float4(__uint_as_float(t[g * 4]) * inv, __uint_as_float(t[g * 4 + 1]) * inv,
-                                __uint_as_float(t[g * 4 + 2]) * inv, __uint_as_float(t[g * 4 + 3]) * inv);
+                    make_float4(__uint_as_float(tt[g * 4]) * inv, __uint_as_float(tt[g * 4 + 1]) * inv,
+                                __uint_as_float(tt[g * 4 + 2]) * inv, __uint_as_float(tt[g * 4 + 3]) * inv);
             }
           }
         }
-        if (a.splits > 1 && row < rows_here && half == 0)
-          a.part_lse[(tok * a.nq + head) * a.splits + split] = (l_tot > 0.f) ? m + log2f(l_tot) : -INFINITY;
+        if (a.splits > 1 && row < rows_here)
+          a.part_lse[(tok * a.nq + head) * a.splits + split] = (l > 0.f) ? m + log2f(l) : -INFINITY;
       }
-    } else if (n_tiles == 0 && a.splits > 1 && row < rows_here) {
-      // empty split: contributes nothing to the combine
-      const int64_t tok = q_begin + qoff + row;
-      float* dst = a.part_o + ((tok * a.nq + head) * a.splits + split) * D + half * 64;
-      for (int d = 0; d < 64; d += 4) *reinterpret_cast<float4*>(dst + d) = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (half == 0) a.part_lse[(tok * a.nq + head) * a.splits + split] = -INFINITY;
+    } else if (ok && my_n == 0 && a.splits > 1 && row < rows_here) {
+      // this split holds no keys of the tile: contributes nothing to the combine
+      float* dst = a.part_o + ((tok * a.nq + head) * a.splits + split) * D;
+      for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(dst + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+      a.part_lse[(tok * a.nq + head) * a.splits + split] = -INFINITY;
     }
   }
 

@@ -195,7 +195,8 @@ void argmax_combine(torch::Tensor vals, torch::Tensor idxs, torch::Tensor out) {
 }
 
 void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, c10::optional<torch::Tensor> residual,
-          c10::optional<torch::Tensor> workspace, torch::Tensor err, int64_t bn, int64_t splits) {
+          c10::optional<torch::Tensor> workspace, torch::Tensor err, int64_t bn, int64_t splits,
+          c10::optional<torch::Tensor> counters) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == torch::kBFloat16 && B.scalar_type() == torch::kBFloat16 &&
                   C.scalar_type() == torch::kBFloat16,
@@ -219,9 +220,15 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, c10::optional<torch
     TORCH_CHECK(workspace->numel() >= need_splits * M * N, "gemm: workspace too small");
     ws = workspace->data_ptr<float>();
   }
+  uint32_t* cnt = nullptr;
+  if (counters.has_value()) {
+    TORCH_CHECK(counters->scalar_type() == torch::kInt32 && counters->is_cuda() && counters->numel() >= 65536,
+                "gemm: counters must be a zeroed int32 CUDA buffer of >= 65536 words");
+    cnt = reinterpret_cast<uint32_t*>(counters->data_ptr<int>());
+  }
   const at::cuda::CUDAGuard guard(A.device());
   gemm_launch(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), C.data_ptr(), C.stride(0), res, M, N, K, (int)bn,
-              (int)splits, ws, reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
+              (int)splits, ws, cnt, reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
 }
 
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K) {
@@ -384,7 +391,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       py::arg("dst"), py::arg("src"), py::arg("nbytes"), py::arg("stream"));
 
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("residual"), py::arg("workspace"),
-        py::arg("err"), py::arg("bn") = 0, py::arg("splits") = 0);
+        py::arg("err"), py::arg("bn") = 0, py::arg("splits") = 0, py::arg("counters") = c10::nullopt);
   m.def("gemm_plan", &gemm_plan_py, py::arg("M"), py::arg("N"), py::arg("K"));
   m.def("rmsnorm", &rmsnorm);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);

@@ -53,6 +53,11 @@ struct GemmArgs {
   // kEpiPushRS: row r of C goes to owner r / Mo's fused region A, slot `rank`
   ArCtx ar;
   int Mo;
+  // split-K: per-tile arrival counters (zeroed once; the last CTA of a tile
+  // resets its counter) and the final bf16 output of the in-kernel reduction
+  uint32_t* tile_counters;
+  __nv_bfloat16* final_out;
+  int64_t final_ld;
 };
 
 MBX_DEVICE char* fused_half(const ArCtx& c, char* base, uint32_t epoch) {
@@ -289,6 +294,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      if ((EPI == kEpiF32Partial || EPI == kEpiSwapF32Partial) && args.splits > 1 && args.tile_counters) {
+        // In-kernel split-K: the last CTA to finish a tile sums every split's
+        // partial (split order 0..S-1, deterministic) and writes bf16 output.
+        volatile uint32_t* s_last = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
+        tc::named_bar_sync(1, kEpiWarps * 32);
+        if (warp == 2 && lane == 0) {
+          __threadfence();
+          const int tile = m + n * args.num_m;
+          const uint32_t prev = atomicAdd(args.tile_counters + tile, 1u);
+          const bool last = prev == (uint32_t)(args.splits - 1);
+          if (last) {
+            args.tile_counters[tile] = 0;
+            __threadfence();
+          }
+          *s_last = last ? 1u : 0u;
+        }
+        tc::named_bar_sync(1, kEpiWarps * 32);
+        if (*s_last) {
+          const float* ws = static_cast<const float*>(args.out);
+          const int64_t plane = (int64_t)args.M * args.N;
+          if (EPI == kEpiSwapF32Partial) {
+            // row = feature `grow`, columns = tokens: C[token][feature]
+            if (row_ok) {
+              const int t_end = min(args.N, n * BN + BN);
+              for (int tk = n * BN; tk < t_end; ++tk) {
+                float acc2 = 0.f;
+                for (int sp = 0; sp < args.splits; ++sp)
+                  acc2 += __ldcg(ws + sp * plane + (int64_t)tk * args.M + grow);
+                __nv_bfloat16* dst = args.final_out + (int64_t)tk * args.final_ld + grow;
+                if (args.residual)
+                  acc2 = __bfloat162float(__float2bfloat16(acc2)) +
+                         __bfloat162float(args.residual[(int64_t)tk * args.final_ld + grow]);
+                *dst = __float2bfloat16(acc2);
+              }
+            }
+          } else if (row_ok) {
+            const int c_end = min(args.N, n * BN + BN);
+            for (int col = n * BN; col < c_end; col += 8) {
+              float f[8] = {};
+              for (int sp = 0; sp < args.splits; ++sp) {
+                const float4* src = reinterpret_cast<const float4*>(ws + sp * plane + (int64_t)grow * args.N + col);
+                const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
+                f[0] += lo.x; f[1] += lo.y; f[2] += lo.z; f[3] += lo.w;
+                f[4] += hi.x; f[5] += hi.y; f[6] += hi.z; f[7] += hi.w;
+              }
+              uint32_t rr[32];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) rr[j] = __float_as_uint(f[j]);
+              __nv_bfloat16* dst = args.final_out + (int64_t)grow * args.final_ld + col;
+              const __nv_bfloat16* res = args.residual ? args.residual + (int64_t)grow * args.final_ld + col : nullptr;
+              store_row_bf16(dst, rr, 8, res);
+            }
+          }
+        }
+      }
     }
     if (EPI == kEpiPushRS) {
       // This CTA's rows are stored; the last CTA of the grid tells every owner.
@@ -535,6 +595,9 @@ void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const vo
   a.timeout_ns = 2000000000ull;
   a.ar = c;
   a.Mo = (int)Mo;
+  a.tile_counters = nullptr;
+  a.final_out = nullptr;
+  a.final_ld = 0;
   const CUtensorMap ta = make_map(A, M, K, lda, BM);
   const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);
   const int units = a.num_m * a.num_n;
@@ -544,8 +607,8 @@ void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const vo
 }
 
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
-                 int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
-                 cudaStream_t s) {
+                 int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,
+                 uint32_t* err, cudaStream_t s) {
   if (M == 0 || N == 0) return;
   // explicit bn/splits requests keep the regular orientation (tests, tuning)
   const bool swap_ok = bn <= 0 && splits <= 0 && N % 4 == 0;
@@ -587,14 +650,26 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
     sw.splits = (int)sp;
     sw.kb_per_split = (int)per;
     sw.out = workspace;
+    sw.tile_counters = counters;
+    sw.final_out = static_cast<__nv_bfloat16*>(C);
+    sw.final_ld = ldc;
     const CUtensorMap tw = make_map(B, N, K, ldb, BM);
     const CUtensorMap tx = make_map(A, M, K, lda, bnt);
-    launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, sw, (int)std::min<int64_t>(num_f * sp, sms), s);
-    const int64_t MN = M * N;
-    const int threads = 256;
-    const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
-    splitk_reduce_kernel<<<(int)std::max<int64_t>(1, blocks), threads, 0, s>>>(
-        workspace, (int)sp, MN, (int)N, (__nv_bfloat16*)C, ldc, a.residual);
+    if (counters) {
+      launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, sw, (int)std::min<int64_t>(num_f * sp, sms), s);
+    } else {
+      sw.tile_counters = nullptr;
+      GemmArgs nofix = sw;
+      nofix.splits = (int)sp;
+      launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, nofix, (int)std::min<int64_t>(num_f * sp, sms), s);
+    }
+    if (!counters) {
+      const int64_t MN = M * N;
+      const int threads = 256;
+      const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
+      splitk_reduce_kernel<<<(int)std::max<int64_t>(1, blocks), threads, 0, s>>>(
+          workspace, (int)sp, MN, (int)N, (__nv_bfloat16*)C, ldc, a.residual);
+    }
     MBX_CUDA_CHECK(cudaGetLastError());
     return;
   }
@@ -610,12 +685,17 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
     if (!workspace) throw std::runtime_error("gemm: split-K needs an fp32 workspace of splits*M*N elements");
     if (N % 4 != 0) throw std::runtime_error("gemm: split-K needs N % 4 == 0");
     a.out = workspace;
+    a.tile_counters = counters;
+    a.final_out = static_cast<__nv_bfloat16*>(C);
+    a.final_ld = ldc;
     launch_bn<kEpiF32Partial>(p.bn, ta, tb, a, grid, s);
-    const int64_t MN = M * N;
-    const int threads = 256;
-    const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
-    splitk_reduce_kernel<<<(int)blocks, threads, 0, s>>>(workspace, a.splits, MN, (int)N, (__nv_bfloat16*)C, ldc,
-                                                         a.residual);
+    if (!counters) {
+      const int64_t MN = M * N;
+      const int threads = 256;
+      const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
+      splitk_reduce_kernel<<<(int)blocks, threads, 0, s>>>(workspace, a.splits, MN, (int)N, (__nv_bfloat16*)C, ldc,
+                                                           a.residual);
+    }
   }
   MBX_CUDA_CHECK(cudaGetLastError());
 }

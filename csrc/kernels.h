@@ -48,9 +48,11 @@ struct GemmPlan {
 GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K);
 // C[M,N] (ldc) = A[M,K] (lda) * B[N,K]^T (ldb) (+ residual, same layout as C).
 // splits > 1 needs an fp32 workspace of splits*M*N elements.
+// counters: zeroed uint32 per-tile arrival counters for the in-kernel split-K
+// reduction (nullptr: a separate reduce kernel folds the partials).
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
-                 int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* err,
-                 cudaStream_t s);
+                 int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,
+                 uint32_t* err, cudaStream_t s);
 
 // Row-parallel GEMM fused with allreduce + residual add + RMSNorm: the GEMM
 // epilogue stores its partial rows straight into the owner ranks' symmetric
