@@ -298,12 +298,22 @@ class MailboxAR:
         launches.add(1)
         return out
 
+    def fused_push_all(self, M: int, N: int) -> bool:
+        """Push every row to every rank (one exchange) for 2 ranks; push rows to
+        their owner (reduce-scatter + all-gather, less traffic) beyond."""
+        return self.world_size <= 2
+
     def fused_gemm_fits(self, M: int, N: int) -> bool:
         """Whether an [M, N] bf16 output fits the fused GEMM->allreduce buffer."""
-        if self._ar is None:
+        if self._ar is None or N % 8:
             return False
-        Mo = -(-M // self.world_size)
-        return self.world_size * Mo * N * 2 + M * N * 2 <= self._ar.fused_capacity() and N % 8 == 0
+        W = self.world_size
+        if self.fused_push_all(M, N):
+            need = W * M * N * 2
+        else:
+            Mo = -(-M // W)
+            need = W * Mo * N * 2 + M * N * 2
+        return need <= self._ar.fused_capacity()
 
     def gemm_all_reduce_rmsnorm(self, a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
                                 norm_w: torch.Tensor, eps: float, out: torch.Tensor = None):
@@ -318,7 +328,8 @@ class MailboxAR:
         if out is None:
             out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
         self._check_error()
-        self._ar.gemm_ar_rmsnorm(a, w, residual, norm_w, out, eps, ops.workspace(a.device).err, self.cfg.max_blocks)
+        self._ar.gemm_ar_rmsnorm(a, w, residual, norm_w, out, eps, ops.workspace(a.device).err, self.cfg.max_blocks,
+                                 self.fused_push_all(M, N))
         self.counters["fused"] += 1
         launches.add(2)
         return out

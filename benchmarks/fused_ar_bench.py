@@ -2,7 +2,7 @@
 the fused tcgen05 GEMM -> push-reduce-scatter -> reduce/all-gather/norm pair
 vs the same kernels unfused vs cuBLAS + NCCL (+ the same norm kernel).
 
-    torchrun --nproc-per-node N benchmarks/fused_ar_bench.py [--model 8b] [--m 1024,64,8,1]
+    torchrun --nproc-per-node N benchmarks/fused_ar_bench.py [--model 8b] [--rows 1024,64,8,1]
 
 CUDA events over --iters back-to-back calls, max over ranks. Reports us per
 call and the roofline of the fused pair: max(FLOPs / measured bf16 peak,
@@ -52,7 +52,7 @@ def timed(fn, iters):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="8b")
-    ap.add_argument("--m", default="1024,64,8,1")
+    ap.add_argument("--rows", default="1024,64,8,1", help="token counts M")
     ap.add_argument("--iters", type=int, default=50)
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -70,7 +70,7 @@ def main():
     for name, K in shapes.items():
         w = (torch.randn(H, K, device=dev) * 0.02).to(torch.bfloat16)
         nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
-        for M in [int(x) for x in args.m.split(",")]:
+        for M in [int(x) for x in args.rows.split(",")]:
             a = torch.randn(M, K, device=dev).to(torch.bfloat16)
             res = torch.zeros(M, H, device=dev, dtype=torch.bfloat16)
             out = torch.empty(M, H, device=dev, dtype=torch.bfloat16)

@@ -566,6 +566,52 @@ done:
 }
 
 // --------------------------------------------------------------------------
+// Fused GEMM -> allreduce, push-all variant (small worlds): the GEMM epilogue
+// stored every row of its partial output into every rank's slot[rank]
+// ([W][M][N] bf16) and released one flag per rank. Each rank waits for all W
+// flags, then sums the W partials of every row locally (rank order, fp32,
+// one rounding) and applies residual add + RMSNorm. No second exchange.
+// --------------------------------------------------------------------------
+template <int W>
+__global__ void __launch_bounds__(kArThreads) fused_allsum_norm_kernel(ArCtx c, int M, int N, uint4* residual,
+                                                                       const uint4* __restrict__ w,
+                                                                       uint4* __restrict__ out, float eps) {
+  __shared__ bool s_ok;
+  __shared__ float red[32];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
+  const int nvec = N / 8;
+  if (!poisoned(c)) {
+    if (threadIdx.x == 0) s_ok = true;
+    __syncthreads();
+    if (threadIdx.x < W) {
+      if (!wait_flag_geq(fuse_flag(c.bufs[c.rank], threadIdx.x), epoch, c.timeout_ns)) {
+        record_error(c, kErrFuseWait, blockIdx.x, threadIdx.x, 5, epoch);
+        s_ok = false;
+      }
+    }
+    __syncthreads();
+    if (s_ok) {
+      const char* mine = fuse_half(c, c.bufs[c.rank], epoch);
+      const uint64_t slot = (uint64_t)M * N * 2;
+      for (int row = blockIdx.x; row < M; row += gridDim.x) {
+        const uint64_t base = (uint64_t)row * nvec;
+        auto ld = [&](int p) {
+          uint4 v[W];
+#pragma unroll
+          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (base + p) * 16);
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
+          return pack_from<__nv_bfloat16>(acc);
+        };
+        residual_rmsnorm_row(ld, residual + base, w, out + base, nvec, N, eps, red);
+      }
+    }
+  }
+  finish_call(c, epoch, kStFuseEpoch, kStFuseDone);
+}
+
+// --------------------------------------------------------------------------
 // Allreduce + residual + RMSNorm, two-shot with posted stores only:
 //   A: every row is stored into its owner's region A slot[rank]
 //   B: the owner sums its rows (rank order, fp32, one rounding) and stores
@@ -909,6 +955,16 @@ void fused_rs_norm_launch(const ArCtx& c, int M, int N, int Mo, void* residual, 
   const int W_ = c.world;
   MBX_DISPATCH_W(W_, fused_rs_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
                          c, M, N, Mo, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
+                         static_cast<uint4*>(out), eps));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, const void* weight, void* out, float eps,
+                              int max_blocks, cudaStream_t stream) {
+  const int g = std::max(1, std::min(M, std::min(max_blocks, (int)kMaxBlocks)));
+  const int W_ = c.world;
+  MBX_DISPATCH_W(W_, fused_allsum_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
+                         c, M, N, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
                          static_cast<uint4*>(out), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
 }

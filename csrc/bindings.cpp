@@ -71,7 +71,7 @@ class ArComm {
                     stream_of(stream));
   }
   void gemm_ar_rmsnorm(torch::Tensor a, torch::Tensor w, torch::Tensor residual, torch::Tensor norm_w,
-                       torch::Tensor out, double eps, torch::Tensor err, int max_blocks) {
+                       torch::Tensor out, double eps, torch::Tensor err, int max_blocks, bool push_all) {
     check_bf16(a, "a");
     check_bf16(w, "w");
     check_bf16(residual, "residual");
@@ -82,7 +82,7 @@ class ArComm {
                 "gemm_ar_rmsnorm: shape mismatch");
     gemm_ar_rmsnorm_launch(c_, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), M, N, K, residual.data_ptr(),
                            norm_w.data_ptr(), out.data_ptr(), (float)eps,
-                           reinterpret_cast<uint32_t*>(err.data_ptr<int>()), max_blocks, cur_stream());
+                           reinterpret_cast<uint32_t*>(err.data_ptr<int>()), max_blocks, push_all, cur_stream());
   }
   uint64_t fused_capacity() const { return c_.fuse_half_bytes; }
   uint64_t chunk_limit(int algo) const { return ar_chunk_limit(c_, algo); }

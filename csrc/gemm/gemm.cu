@@ -50,9 +50,11 @@ struct GemmArgs {
   int num_m, num_n, splits, kb_per_split, kb_total;
   uint32_t* err;
   uint64_t timeout_ns;
-  // kEpiPushRS: row r of C goes to owner r / Mo's fused region A, slot `rank`
+  // kEpiPushRS: row r of C goes to owner r / Mo's fused region A, slot `rank`;
+  // with push_all every rank receives every row (slot `rank` of [M, N] slots)
   ArCtx ar;
   int Mo;
+  int push_all;
   // split-K: per-tile arrival counters (zeroed once; the last CTA of a tile
   // resets its counter) and the final bf16 output of the in-kernel reduction
   uint32_t* tile_counters;
@@ -72,13 +74,15 @@ struct Tmem {
   static constexpr int kCols = 2 * kAccStride;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kStaging = false>
 struct Smem {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOff = STAGES * kStageBytes;
-  static constexpr int kTotal = kBarOff + 256 + 1024;  // barriers + alignment slack
+  // push epilogue: per epilogue warp a [32 rows x 128 B] staging tile
+  static constexpr int kStageOut = kBarOff + 256;
+  static constexpr int kTotal = kStageOut + (kStaging ? 4 * 32 * 128 : 0) + 1024;  // + alignment slack
 };
 
 MBX_DEVICE void set_err(uint32_t* err, uint32_t code, volatile int* abort) {
@@ -115,7 +119,7 @@ template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmArgs args) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, EPI == kEpiPushRS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -262,21 +266,63 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_ld_wait();
         const int gcol = n * BN + c0;
         const int valid = min(32, args.N - gcol);
-        if (row_ok && valid > 0) {
-          if (EPI == kEpiSwapF32Partial) {
+        if (EPI == kEpiPushRS) {
+          // Stage this warp's 32 rows x 32 columns (bf16, 64 B per row) into a
+          // [32 x 128 B] tile (16-byte units XOR-swizzled by row); every second
+          // chunk, write 4 full 128-byte row segments per store instruction to
+          // the row owners' symmetric buffers (NVLink moves whole lines instead
+          // of 16-byte pieces of 32 different rows).
+          uint8_t* stg = smem + L::kStageOut + (warp - 2) * (32 * 128);
+          const int half64 = (c0 >> 5) & 1;
+          {
+            float f[8];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[g * 8 + j]);
+              const int unit = half64 * 4 + g;
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = pack_from<__nv_bfloat16>(f);
+            }
+          }
+          if (half64 == 1 || c0 + 32 >= BN) {
+            __syncwarp();
+            const int col0 = n * BN + (c0 & ~63);  // first column of the staged 64
+            const int unit = lane & 7;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int srow = k * 4 + (lane >> 3);
+              const int grow2 = m * BM + quad * 32 + srow;
+              const int col = col0 + unit * 8;
+              if (grow2 < args.M && col < args.N && (half64 == 1 || unit < 4)) {
+                const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
+                if (args.push_all) {
+                  const uint64_t off = ((uint64_t)args.ar.rank * args.M + grow2) * args.N + col;
+                  for (int j = 0; j < args.ar.world; ++j) {
+                    const int dst_rank = (args.ar.rank + j) % args.ar.world;
+                    *reinterpret_cast<uint4*>(fused_half(args.ar, args.ar.bufs[dst_rank], fepoch) + off * 2) = v;
+                  }
+                } else {
+                  const int owner = grow2 / args.Mo;
+                  const int lrow = grow2 - owner * args.Mo;
+                  char* dst = fused_half(args.ar, args.ar.bufs[owner], fepoch) +
+                              ((uint64_t)(args.ar.rank * args.Mo + lrow) * args.N + col) * 2;
+                  *reinterpret_cast<uint4*>(dst) = v;
+                }
+              }
+            }
+            __syncwarp();
+          }
+        }
+        if (EPI != kEpiPushRS && row_ok && valid > 0) {
+          if (EPI == kEpiPushRS) {
+            // staged below (coalesced 128-byte row segments)
+          } else if (EPI == kEpiSwapF32Partial) {
             // row = output feature, columns = tokens: store column j of the tile as
             // partial[ks][token][feature] (consecutive threads = consecutive features)
             float* base = static_cast<float*>(args.out) + (int64_t)ks * args.N * args.M + grow;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (j < valid) base[(int64_t)(gcol + j) * args.M] = __uint_as_float(r[j]);
-          } else if (EPI == kEpiPushRS) {
-            const int owner = grow / args.Mo;
-            const int lrow = grow - owner * args.Mo;
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(
-                fused_half(args.ar, args.ar.bufs[owner], fepoch) +
-                ((uint64_t)(args.ar.rank * args.Mo + lrow) * args.N + gcol) * 2);
-            store_row_bf16(dst, r, valid, nullptr);
           } else if (EPI == kEpiF32Partial) {
             float* dst = static_cast<float*>(args.out) + ((int64_t)ks * args.M + grow) * args.N + gcol;
 #pragma unroll
@@ -478,7 +524,7 @@ int num_sms() {
 
 template <int BN, int STAGES, int EPI>
 void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, EPI == kEpiPushRS>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -497,7 +543,7 @@ void launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   }
   switch (bn) {
     case 256: launch_cfg<256, 4, EPI>(ta, tb, a, grid, s); break;
-    case 224: launch_cfg<224, 5, EPI>(ta, tb, a, grid, s); break;
+    case 224: launch_cfg<224, EPI == kEpiPushRS ? 4 : 5, EPI>(ta, tb, a, grid, s); break;
     case 192: launch_cfg<192, 5, EPI>(ta, tb, a, grid, s); break;
     case 160: launch_cfg<160, 5, EPI>(ta, tb, a, grid, s); break;
     case 128: launch_cfg<128, 6, EPI>(ta, tb, a, grid, s); break;
@@ -568,12 +614,12 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
 
 void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
                             int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
-                            uint32_t* err, int max_blocks, cudaStream_t s) {
+                            uint32_t* err, int max_blocks, bool push_all, cudaStream_t s) {
   if (M == 0) return;
   if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm_ar: K and N must be multiples of 8");
   const int W = c.world;
   const int64_t Mo = (M + W - 1) / W;
-  const uint64_t need = (uint64_t)W * Mo * N * 2 + (uint64_t)M * N * 2;
+  const uint64_t need = push_all ? (uint64_t)W * M * N * 2 : (uint64_t)W * Mo * N * 2 + (uint64_t)M * N * 2;
   if (c.fuse_half_bytes == 0 || need > c.fuse_half_bytes)
     throw std::runtime_error("gemm_ar: message needs " + std::to_string(need) + " bytes of fused buffer, have " +
                              std::to_string(c.fuse_half_bytes));
@@ -595,6 +641,7 @@ void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const vo
   a.timeout_ns = 2000000000ull;
   a.ar = c;
   a.Mo = (int)Mo;
+  a.push_all = push_all ? 1 : 0;
   a.tile_counters = nullptr;
   a.final_out = nullptr;
   a.final_ld = 0;
@@ -603,7 +650,8 @@ void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const vo
   const int units = a.num_m * a.num_n;
   launch_bn<kEpiPushRS>(p.bn, ta, tb, a, std::min(units, sms), s);
   MBX_CUDA_CHECK(cudaGetLastError());
-  fused_rs_norm_launch(c, (int)M, (int)N, (int)Mo, residual, norm_w, out, eps, max_blocks, s);
+  if (push_all) fused_allsum_norm_launch(c, (int)M, (int)N, residual, norm_w, out, eps, max_blocks, s);
+  else fused_rs_norm_launch(c, (int)M, (int)N, (int)Mo, residual, norm_w, out, eps, max_blocks, s);
 }
 
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
@@ -655,14 +703,9 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
     sw.final_ld = ldc;
     const CUtensorMap tw = make_map(B, N, K, ldb, BM);
     const CUtensorMap tx = make_map(A, M, K, lda, bnt);
-    if (counters) {
-      launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, sw, (int)std::min<int64_t>(num_f * sp, sms), s);
-    } else {
-      sw.tile_counters = nullptr;
-      GemmArgs nofix = sw;
-      nofix.splits = (int)sp;
-      launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, nofix, (int)std::min<int64_t>(num_f * sp, sms), s);
-    }
+    // with counters the last CTA of each tile folds the partials in-kernel,
+    // otherwise the reduce kernel below does
+    launch_bn<kEpiSwapF32Partial>(bnt, tw, tx, sw, (int)std::min<int64_t>(num_f * sp, sms), s);
     if (!counters) {
       const int64_t MN = M * N;
       const int threads = 256;

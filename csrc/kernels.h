@@ -23,6 +23,9 @@ void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nby
 // all-gather, residual + norm). The first launch is gemm_ar_rmsnorm_launch.
 void fused_rs_norm_launch(const ArCtx& c, int M, int N, int Mo, void* residual, const void* weight, void* out,
                           float eps, int max_blocks, cudaStream_t stream);
+// Second launch of the push-all fused GEMM->allreduce->RMSNorm.
+void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, const void* weight, void* out, float eps,
+                              int max_blocks, cudaStream_t stream);
 void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream);
 void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, uint64_t nbytes, int max_blocks,
                      cudaStream_t stream);
@@ -59,9 +62,12 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 // buffers (reduce-scatter overlapped with the remaining tiles), then one
 // launch reduces, all-gathers and normalises. residual is updated in place;
 // out = rmsnorm(residual) * norm_w.
+// push_all: the epilogue stores every row to every rank (one exchange; best
+// for small worlds) instead of to the row's owner (reduce-scatter +
+// all-gather; less traffic for large worlds).
 void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
                             int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
-                            uint32_t* err, int max_blocks, cudaStream_t s);
+                            uint32_t* err, int max_blocks, bool push_all, cudaStream_t s);
 
 // ---- attention (attn/attention.cu) -------------------------------------------
 void prefill_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
