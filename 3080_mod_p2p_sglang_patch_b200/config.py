@@ -33,8 +33,16 @@ def mailbox_enabled() -> bool:
 class CommConfig:
     # largest message (bytes) handled by the communicator; above it the caller
     # falls back to NCCL. The kernels chunk through the buffer, so this is a
-    # policy limit, not a buffer limit.
-    max_size: int = 256 * MiB
+    # policy limit, not a buffer limit. None = per world size from
+    # ``max_size_by_world``: the size where NCCL's pipelined ring overtakes the
+    # in-house kernels on an 8xB200 NVSwitch box (measured with
+    # benchmarks/allreduce_sweep.py: TP=2 32 MB 80 us vs NCCL 85 us, 64 MB 160 vs
+    # 154; TP=8 64 MB 257 vs 274, 128 MB 515 vs 397).
+    max_size: int = None
+    max_size_by_world: dict = dataclasses.field(
+        default_factory=lambda: {2: 48 * MiB, 3: 64 * MiB, 4: 64 * MiB, 5: 96 * MiB, 6: 96 * MiB, 7: 96 * MiB,
+                                 8: 96 * MiB}
+    )
     # one ping-pong data half of the symmetric buffer (two halves are mapped)
     half_bytes: int = 64 * MiB
     # fused GEMM->allreduce path: one of its two halves (holds W partial slots
@@ -60,6 +68,11 @@ class CommConfig:
     cpu_slot_bytes: int = 32 * MiB
     cpu_timeout_ms: int = 30_000
     verbose: bool = False
+
+    def max_size_for(self, world: int) -> int:
+        if self.max_size is not None:
+            return int(self.max_size)
+        return int(self.max_size_by_world.get(world, 64 * MiB))
 
     @classmethod
     def from_env(cls) -> "CommConfig":

@@ -9,6 +9,7 @@ out), ``add_request`` / ``step`` / ``run`` for streaming use, and
 ``prefill_only`` for prompt-processing benchmarks (the reference's pp tok/s
 metric, tests/pp_bench.py: max_tokens=1).
 """
+import os
 import time
 
 import torch
@@ -23,7 +24,8 @@ from .scheduler import Request, Scheduler
 class LLMEngine:
     def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
-                 graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False):
+                 graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
+                 sp: bool = None):
         self.cfg = cfg
         self.tp = tp
         self.tp_size = tp.world_size if tp is not None else 1
@@ -34,6 +36,15 @@ class LLMEngine:
         self.chunk = chunk
         self.weights = LlamaWeights(cfg, self.tp_rank, self.tp_size, self.device, seed=seed, full_init=full_init)
         self.model = LlamaTP(cfg, self.weights, tp=tp, impl=impl)
+        # sequence parallel for prefill batches (TP > 1, native build);
+        # None = follow MBX_SP (default off)
+        if sp is None:
+            sp = os.environ.get("MBX_SP", "0") == "1"
+        self.sp = None
+        if sp and tp is not None and self.tp_size > 1 and impl == "native":
+            self.sp = tp.sp_setup(chunk, cfg.hidden)
+            if self.sp is not None:
+                self.model.enable_sp(self.sp)
         nkv = cfg.kv_heads // self.tp_size
         self.max_blocks_per_seq = (max_seq + PAGE - 1) // PAGE
         if kv_blocks is None:

@@ -105,6 +105,17 @@ class LlamaTP:
         self.device = weights.embed.device
         self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, self.device)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        # sequence parallel (parallel/sp.py): used for batches of at least
+        # ``sp_min_rows`` tokens that fit its buffers; None = off
+        self.sp = None
+        self.sp_min_rows = 256
+
+    def enable_sp(self, sp, min_rows: int = 256):
+        """Run large batches sequence-parallel (native TP build only)."""
+        if self.impl != "native" or self.tp_size == 1:
+            return
+        self.sp = sp
+        self.sp_min_rows = int(min_rows)
 
     # ------------------------------------------------------------ building blocks
     def _linear(self, x, w, out=None, residual=None):
@@ -167,6 +178,8 @@ class LlamaTP:
         """
         cfg, w = self.cfg, self.w
         T = ids.shape[0]
+        if self.sp is not None and T >= self.sp_min_rows and self.sp.fits(T):
+            return self._forward_sp(ids, positions, slots, kv_caches, attn, last_idx, return_hidden)
         nq, nkv, D = w.nq, w.nkv, cfg.head_dim
         h = ops.embedding(ids, w.embed, start=w.vocab_start)
         h = self._all_reduce(h)
@@ -199,6 +212,36 @@ class LlamaTP:
                 part = self._linear(a, L["down"])
                 x = self._ar_norm(part, residual, nxt)
         x_last = x.index_select(0, last_idx)
+        if return_hidden:
+            return x_last
+        return self._lm_argmax(x_last)
+
+    def _forward_sp(self, ids, positions, slots, kv_caches, attn, last_idx, return_hidden=False):
+        """Sequence-parallel forward: the residual stream is sharded by rows
+        (this rank owns ``sp.own_rows(T)``); row-parallel GEMMs reduce-scatter
+        from their epilogue, the owners normalise their rows and all-gather
+        them into the gather buffer the next column-parallel GEMM loads from.
+        Same math as ``forward`` (sums in rank order, one bf16 rounding)."""
+        cfg, w, sp = self.cfg, self.w, self.sp
+        T = ids.shape[0]
+        nq, nkv, D = w.nq, w.nkv, cfg.head_dim
+        h = ops.embedding(ids, w.embed, start=w.vocab_start)
+        sp.rs_push(h)
+        res = torch.zeros((sp.rows_per_rank(T), cfg.hidden), dtype=torch.bfloat16, device=ids.device)
+        sp.rs_norm_ag(T, res, w.layers[0]["ln1"], cfg.eps)
+        for li, L in enumerate(w.layers):
+            qkv = sp.gemm_ag(T, L["qkv"])
+            kc, vc = kv_caches[li]
+            q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
+            o = attn(li, q, kc, vc)
+            sp.gemm_rs(o.view(T, nq * D), L["o"])
+            sp.rs_norm_ag(T, res, L["ln2"], cfg.eps)
+            gu = sp.gemm_ag(T, L["gate_up"])
+            a = ops.silu_mul(gu)
+            sp.gemm_rs(a, L["down"])
+            nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
+            sp.rs_norm_ag(T, res, nxt, cfg.eps)
+        x_last = sp.gathered(T).index_select(0, last_idx)
         if return_hidden:
             return x_last
         return self._lm_argmax(x_last)

@@ -74,9 +74,9 @@ class MailboxAR:
         self.disabled = True
         self.group = group
         self.cfg = config or CommConfig.from_env()
-        self.max_size = int(max_size if max_size is not None else self.cfg.max_size)
         self.rank = dist.get_rank(group=group)
         self.world_size = dist.get_world_size(group=group)
+        self.max_size = int(max_size if max_size is not None else self.cfg.max_size_for(self.world_size))
         self.counters = {"oneshot_push": 0, "oneshot_pull": 0, "twoshot": 0, "twoshot_push": 0, "nvls": 0, "cpu": 0,
                          "fallback": 0, "errors": 0, "fused": 0, "allgather": 0}
         self._buf = None
@@ -85,6 +85,7 @@ class MailboxAR:
         self._status = None
         self._seg_seq = 0
         self._seg_stream = None
+        self.sp = None
         self.mbx = 0
         self.peer_mbx = 0
         if self.world_size < 2 or self.world_size > 8:
@@ -173,6 +174,12 @@ class MailboxAR:
         self.peer_mbx = 0
 
     def _teardown(self):
+        if self.sp is not None:
+            try:
+                self.sp.close()
+            except Exception:  # noqa: BLE001
+                pass
+            self.sp = None
         if self._buf is not None:
             try:
                 self._buf.close()
@@ -394,10 +401,31 @@ class MailboxAR:
         return self.err()
 
     # ------------------------------------------------------------------ status
+    def sp_setup(self, max_rows: int, hidden: int):
+        """Collective: allocate the sequence-parallel buffers for batches of up
+        to ``max_rows`` tokens of width ``hidden`` (see parallel/sp.py).
+        Returns the ``SequenceParallel`` object (also ``self.sp``), or None on
+        the CPU transport or when the communicator is off."""
+        if self.disabled or self._ar is None:
+            return None
+        if self.sp is not None and self.sp.max_rows >= max_rows and self.sp.hidden == hidden:
+            return self.sp
+        from .sp import SequenceParallel
+
+        if self.sp is not None:
+            torch.cuda.synchronize(self.device)
+            bootstrap.agree(True, self.group)
+            self.sp.close()
+        self.sp = SequenceParallel(self, max_rows, hidden)
+        return self.sp
+
     def err(self) -> int:
         """Sticky device error code (0 = ok), read from host-mapped memory."""
         if self._ar is not None:
-            return int(self._ar.error())
+            code = int(self._ar.error())
+            if code == 0 and self.sp is not None:
+                code = self.sp.err()
+            return code
         if self._cpu is not None:
             return int(self._cpu.error())
         return 0
@@ -426,6 +454,8 @@ class MailboxAR:
             self._state.zero_()
             self._ar.clear_status()
             torch.cuda.synchronize(self.device)
+            if self.sp is not None:
+                self.sp.reset()
         self._seg_seq = 0
         bootstrap.agree(True, self.group)
 

@@ -31,7 +31,13 @@ class TPGroup:
         self.world_size = dist.get_world_size(group) if self.initialized else 1
         self.device = device
         self.ca_comm = None
-        self.fused_gemm_ar = os.environ.get("MBX_FUSED_GEMM_AR", "0") == "1"
+        # Fused row-parallel GEMM -> allreduce: MBX_FUSED_GEMM_AR=1 forces it on,
+        # =0 off; by default on for two ranks, where the epilogue pushes every
+        # tile straight to both ranks (one exchange) and measured no slower than
+        # GEMM + fused allreduce/norm. With more ranks the owner-push variant
+        # needs a reduce-scatter then an all-gather and measured slower.
+        env = os.environ.get("MBX_FUSED_GEMM_AR")
+        self.fused_gemm_ar = (env == "1") if env in ("0", "1") else self.world_size == 2
         if use_mailbox is None:
             use_mailbox = mailbox_enabled()
         if self.world_size > 1 and use_mailbox:
@@ -69,14 +75,18 @@ class TPGroup:
 
         M, N = a.shape[0], w.shape[0]
         ca = self.ca_comm
-        # The fused pair (GEMM epilogue pushes its tiles) is opt-in: at chunk 1024
-        # these GEMMs are a single wave, so there are no later tiles to hide the
-        # pushes behind, and GEMM + one fused allreduce/norm launch measured faster.
         if self.world_size > 1 and ca is not None and not ca.disabled and M > 64 and self.fused_gemm_ar \
                 and ca.fused_gemm_fits(M, N):
             return ca.gemm_all_reduce_rmsnorm(a, w, residual, norm_w, eps, out=out)
         part = ops.gemm(a, w)
         return self.all_reduce_rmsnorm(part, residual, norm_w, eps, out=out)
+
+    def sp_setup(self, max_rows: int, hidden: int):
+        """Collective: sequence-parallel buffers on the communicator (None
+        without one; see parallel/sp.py)."""
+        if self.world_size == 1 or self.ca_comm is None:
+            return None
+        return self.ca_comm.sp_setup(max_rows, hidden)
 
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         """[world, *x.shape]."""

@@ -49,6 +49,8 @@ def parse():
     p.add_argument("--prompt-len", type=int, default=4096)
     p.add_argument("--chunk", type=int, default=1024)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--sp", type=int, default=None, choices=[0, 1],
+                   help="sequence-parallel prefill (1) or allreduce prefill (0); default: MBX_SP (off)")
     p.add_argument("--no-graph", action="store_true", help="launch every chunk's kernels eagerly (the torch "
                    "baseline always does: like sglang, it graphs decode only)")
     return p.parse_args()
@@ -81,7 +83,8 @@ def main():
     cfg = models.LlamaConfig.by_name(args.model)
     R, S, chunk = args.requests, args.prompt_len, args.chunk
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=R, max_seq=S + 16, chunk=chunk, seed=0, use_graphs=False,
-                            impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graph))
+                            impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graph),
+                            sp=(None if args.sp is None else bool(args.sp)) if args.impl == "native" else False)
     g = torch.Generator().manual_seed(1234)
     prompts = torch.randint(0, cfg.vocab, (R, S), generator=g).tolist()
 
@@ -201,6 +204,7 @@ def main():
                 "baseline_number": "1464 tok/s, reference docs/performance.md:43 (2x RTX 3080, 27B AWQ, TP=2)",
                 "transport": getattr(tp.ca_comm, "transport", None) if (tp and tp.ca_comm) else None,
                 "prefill_cuda_graph": eng.prefill_graph is not None,
+                "sequence_parallel": eng.sp is not None,
             },
             "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")} if clocks else None,
             "e2e": e2e,

@@ -86,6 +86,10 @@ def main():
     ap.add_argument("--reference", action="store_true")
     ap.add_argument("--max-bytes", type=int, default=256 << 20)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--sizes", default=None, help="comma-separated byte counts (default: the full sweep)")
+    ap.add_argument("--trace", action="store_true",
+                    help="also print block 0's phase timestamps (us from kernel start) of the last of 20 "
+                         "back-to-back calls, per rank")
     args = ap.parse_args()
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -95,7 +99,11 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     group = dist.group.WORLD
     comm_mod = importlib.import_module(f"{PKG}.parallel.communicator")
-    ar = comm_mod.MailboxAR(None, dev)
+    cfg_mod = importlib.import_module(f"{PKG}.config")
+    # explicit algorithms run in-house at every size; "auto" follows the
+    # product policy (in-house up to the per-world max_size, NCCL above)
+    policy_max = cfg_mod.CommConfig.from_env().max_size_for(world)
+    ar = comm_mod.MailboxAR(None, dev, max_size=max(args.max_bytes, 256 << 20))
     assert not ar.disabled
     algos = [a for a in args.algos.split(",") if a]
     if "nvls" in algos and "nvls" not in ar.transport:
@@ -118,7 +126,9 @@ def main():
             algos.append("reference_mailbox")
     out_f = open(args.out, "a") if (args.out and rank == 0) else None
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    for nbytes in sorted(set(s for s in SIZES if s <= args.max_bytes)):
+    sizes = [int(v) for v in args.sizes.split(",")] if args.sizes else SIZES
+    trace = torch.zeros(8, dtype=torch.int64, device=dev)
+    for nbytes in sorted(set(s for s in sizes if s <= args.max_bytes)):
         n = nbytes // 2
         x = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)
         o = torch.empty_like(x)
@@ -131,6 +141,9 @@ def main():
                 if nbytes > ref.max_size:
                     continue
                 fn = lambda: ref.custom_all_reduce(x)  # noqa: E731
+            elif algo == "auto" and nbytes > policy_max:
+                y = x.clone()
+                fn = lambda: dist.all_reduce(y, group=group)  # noqa: E731
             else:
                 a = None if algo == "auto" else algo
                 fn = lambda a=a: ar.custom_all_reduce(x, algo=a, out=o)  # noqa: E731
@@ -149,10 +162,27 @@ def main():
                     del gr
                 rec = {"bytes": nbytes, "impl": algo, "mode": mode, "tp": world, "us": ms * 1e3,
                        "busbw_gbs": busbw(nbytes, ms, world)}
+                if algo == "auto":
+                    rec["route"] = "nccl" if nbytes > policy_max else "mailbox"
                 if rank == 0:
                     print(json.dumps(rec), flush=True)
                     if out_f:
                         out_f.write(json.dumps(rec) + "\n")
+            if args.trace and algo not in ("nccl", "reference_mailbox") and not (algo == "auto" and nbytes > policy_max):
+                trace.zero_()
+                ar._ar.set_trace(trace.data_ptr())
+                torch.cuda.synchronize()
+                dist.barrier(group)
+                for _ in range(20):
+                    fn()
+                torch.cuda.synchronize()
+                ar._ar.set_trace(0)
+                allm = [None] * world
+                dist.all_gather_object(allm, trace.tolist(), group=group)
+                if rank == 0:
+                    t0 = min(m[0] for m in allm)
+                    print(json.dumps({"bytes": nbytes, "impl": algo, "trace_us": [
+                        [round((v - t0) / 1e3, 2) if v else None for v in m[:6]] for m in allm]}), flush=True)
         if ar.err():
             raise SystemExit(f"communicator error {ar.status()}")
     dist.barrier()

@@ -32,6 +32,8 @@ def main():
     ap.add_argument("--max-prompt", type=int, default=8192)
     ap.add_argument("--gen", type=int, default=512)
     ap.add_argument("--chunk", type=int, default=8192)
+    ap.add_argument("--sp", type=int, default=1, choices=[0, 1],
+                    help="sequence-parallel prefill (fused GEMM->reduce-scatter, all-gather->GEMM); native only")
     args = ap.parse_args()
     par = importlib.import_module(f"{PKG}.parallel")
     models = importlib.import_module(f"{PKG}.models")
@@ -41,7 +43,8 @@ def main():
     tp = par.TPGroup(None, dev, use_mailbox=(args.impl == "native")) if world > 1 else None
     cfg = models.LlamaConfig.by_name(args.model)
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=args.requests, max_seq=args.max_prompt + args.gen + 16,
-                            chunk=args.chunk, seed=0, use_graphs=True, impl=args.impl)
+                            chunk=args.chunk, seed=0, use_graphs=True, impl=args.impl,
+                            sp=bool(args.sp) and args.impl == "native")
     g = torch.Generator().manual_seed(11)
     lens = torch.randint(args.min_prompt, args.max_prompt + 1, (args.requests,), generator=g).tolist()
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in lens]
@@ -75,6 +78,7 @@ def main():
     if rank == 0:
         print(json.dumps({
             "metric": "mixed_serving", "model": cfg.name, "impl": args.impl, "tp": world, "requests": args.requests,
+            "sequence_parallel": eng.sp is not None,
             "prompt_tokens": pre_tok, "gen_tokens": args.requests * args.gen,
             "prefill_tok_s": pre_tok / (pre_ms * 1e-3),
             "decode_itl_p50_ms": dec[len(dec) // 2] if dec else None,

@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, co
                                                                      uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
+  trace_mark(c, 0);
   if (!poisoned(c)) {
     const uint64_t slot = c.half_bytes / W;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -59,7 +60,9 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, co
         st_v4(data_half(c.bufs[r], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
       }
     }
+    trace_mark(c, 1);
     if (block_barrier(c, 0, epoch, &s_ok)) {
+      trace_mark(c, 2);
       const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
       for (uint64_t i = i0; i < nvec; i += stride) {
         uint4 v[W];
@@ -72,6 +75,7 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, co
       }
     }
   }
+  trace_mark(c, 5);
   finish_call(c, epoch);
 }
 
@@ -174,6 +178,7 @@ __global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, co
                                                                      uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
+  trace_mark(c, 0);
   if (!poisoned(c)) {
     const uint64_t cs = (nvec + W - 1) / W;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -199,7 +204,9 @@ __global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, co
         }
       }
     }
+    trace_mark(c, 1);
     if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    trace_mark(c, 2);
     {
       // B: reduce the own chunk, broadcast the result
       const uint64_t beg = c.rank * cs, end = min(nvec, beg + cs);
@@ -231,7 +238,9 @@ __global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, co
         }
       }
     }
+    trace_mark(c, 3);
     if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    trace_mark(c, 4);
     {
       // C: gather locally
       const char* res = mine + (uint64_t)W * cs * 16;
@@ -255,12 +264,19 @@ __global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, co
     }
   }
 done:
+  trace_mark(c, 5);
   finish_call(c, epoch);
 }
 
 // --------------------------------------------------------------------------
 // NVLS: multimem.ld_reduce (switch-side sum, fp32 accumulation for 16-bit
 // types) + multimem.st broadcast of the owner's chunk.
+// The switch serves multicast loads and stores from/to every GPU's L2, the
+// same point of coherence as the local .cg loads and the unicast stores, so
+// the system-scope release/acquire barriers alone order the phases (no
+// fence.proxy.alias, which measured 3-30 us per barrier, growing with size).
+// Loads and stores of different warps overlap: the loads use a GPU's egress
+// (its memory is read by every owner), the stores its ingress.
 // --------------------------------------------------------------------------
 template <typename T>
 MBX_DEVICE uint4 multimem_ld_reduce(const void* mc);
@@ -296,13 +312,13 @@ MBX_DEVICE void multimem_st(void* mc, const uint4& v) {
                "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
-MBX_DEVICE void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
 template <typename T, int W>
 __global__ void __launch_bounds__(kArThreads) ar_nvls_kernel(ArCtx c, const uint4* __restrict__ in,
                                                              uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
+  trace_mark(c, 0);
   if (!poisoned(c)) {
     const uint64_t slot1 = c.half_bytes / 2;
     const uint64_t cs = (nvec + W - 1) / W;
@@ -314,9 +330,9 @@ __global__ void __launch_bounds__(kArThreads) ar_nvls_kernel(ArCtx c, const uint
       const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
       for (uint64_t i = beg + o0; i < end; i += stride) st_v4(mine + i * 16, ld_nc_v4(in + i));
     }
-    fence_proxy_alias();
+    trace_mark(c, 1);
     if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
-    fence_proxy_alias();
+    trace_mark(c, 2);
     {
       const uint64_t beg = c.rank * cs, end = min(nvec, beg + cs);
       for (uint64_t i = beg + o0; i < end; i += stride * kU) {
@@ -333,15 +349,16 @@ __global__ void __launch_bounds__(kArThreads) ar_nvls_kernel(ArCtx c, const uint
         }
       }
     }
-    fence_proxy_alias();
+    trace_mark(c, 3);
     if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
-    fence_proxy_alias();
+    trace_mark(c, 4);
     for (int ch = 0; ch < W; ++ch) {
       const uint64_t beg = ch * cs, end = min(nvec, beg + cs);
       for (uint64_t i = beg + o0; i < end; i += stride) out[i] = ld_cg_v4(mine + slot1 + i * 16);
     }
   }
 done:
+  trace_mark(c, 5);
   finish_call(c, epoch);
 }
 
@@ -366,9 +383,9 @@ MBX_DEVICE float block_sum(float v, float* red) {
 }
 
 // res/out for one row given the reduced bf16 row `ar` (read through `ld`).
-template <typename LoadAr>
-MBX_DEVICE void residual_rmsnorm_row(LoadAr ld, uint4* residual_row, const uint4* w_row, uint4* out_row,
-                                     int hvec, int H, float eps, float* red) {
+template <typename LoadAr, typename StoreOut>
+MBX_DEVICE void residual_rmsnorm_row_st(LoadAr ld, uint4* residual_row, const uint4* w_row, StoreOut st, int hvec,
+                                        int H, float eps, float* red) {
   float ss = 0.f;
   for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
     float a[8] = {};
@@ -393,8 +410,15 @@ MBX_DEVICE void residual_rmsnorm_row(LoadAr ld, uint4* residual_row, const uint4
     unpack_add<__nv_bfloat16>(w_row[p], wv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) q[k] = q[k] * rstd * wv[k];
-    out_row[p] = pack_from<__nv_bfloat16>(q);
+    st(p, pack_from<__nv_bfloat16>(q));
   }
+}
+
+template <typename LoadAr>
+MBX_DEVICE void residual_rmsnorm_row(LoadAr ld, uint4* residual_row, const uint4* w_row, uint4* out_row,
+                                     int hvec, int H, float eps, float* red) {
+  residual_rmsnorm_row_st(ld, residual_row, w_row, [&](int p, const uint4& v) { out_row[p] = v; }, hvec, H, eps,
+                          red);
 }
 
 template <int W>
@@ -611,6 +635,112 @@ __global__ void __launch_bounds__(kArThreads) fused_allsum_norm_kernel(ArCtx c, 
   finish_call(c, epoch, kStFuseEpoch, kStFuseDone);
 }
 
+// ==========================================================================
+// Sequence parallel. Rank r owns rows [r*Mo, r*Mo+Mo) of the residual stream.
+// Row-parallel GEMMs push each output row to its owner's reduce-scatter slot
+// (gemm_rs_launch, or sp_rs_push for a local tensor); sp_rs_norm_ag reduces
+// the owned rows, adds them to the residual shard, normalises them and pushes
+// the normed rows into every rank's gather buffer G, where the next
+// column-parallel GEMM's TMA producer loads an m-tile as soon as its owners'
+// flags are up (all-gather -> GEMM without a separate all-gather launch).
+// Buffers: the reduce-scatter slots live in the fused halves (epoch parity),
+// G is one fixed buffer: a rank only pushes into a peer's G after every rank's
+// previous row-parallel GEMM ran, which comes after that rank's last read of G.
+// ==========================================================================
+MBX_DEVICE uint32_t* ag_flag(char* base, int owner) {
+  return reinterpret_cast<uint32_t*>(base + kAgFlagOff) + owner;
+}
+
+// Once every block of the grid got here, release *flag_of(o) = epoch on every
+// rank o (the blocks' earlier stores, local or remote, are visible first).
+template <typename FlagOf>
+MBX_DEVICE void grid_done_release(const ArCtx& c, int counter_word, uint32_t epoch, FlagOf flag_of) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    const uint32_t prev = atomicAdd(c.state + counter_word, 1u);
+    if (prev == gridDim.x - 1) {
+      c.state[counter_word] = 0;
+      fence_acq_rel_sys();
+      for (int o = 0; o < c.world; ++o) st_release_sys(flag_of(o), epoch);
+    }
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) sp_rs_push_kernel(ArCtx c, const uint4* __restrict__ x, int M, int N,
+                                                                 int Mo) {
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
+  if (poisoned(c)) return;
+  const int nvec = N / 8;
+  const uint64_t total = (uint64_t)M * nvec;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int row = (int)(i / nvec);
+    const int p = (int)(i - (uint64_t)row * nvec);
+    const int owner = row / Mo;
+    const int lrow = row - owner * Mo;
+    char* dst = fuse_half(c, c.bufs[owner], epoch) + ((uint64_t)(c.rank * Mo + lrow) * nvec + p) * 16;
+    st_v4(dst, ld_nc_v4(x + i));
+  }
+  grid_done_release(c, kStFuseGemmDone, epoch, [&](int o) { return fuse_flag(c.bufs[o], c.rank); });
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) sp_rs_norm_ag_kernel(ArCtx c, int M, int N, int Mo, uint4* res_own,
+                                                                   const uint4* __restrict__ w, float eps) {
+  __shared__ bool s_ok;
+  __shared__ float red[32];
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
+  const int nvec = N / 8;
+  bool ok = false;
+  if (!poisoned(c)) {
+    if (threadIdx.x == 0) s_ok = true;
+    __syncthreads();
+    if (threadIdx.x < W) {
+      if (!wait_flag_geq(fuse_flag(c.bufs[c.rank], threadIdx.x), epoch, c.timeout_ns)) {
+        record_error(c, kErrFuseWait, blockIdx.x, threadIdx.x, 6, epoch);
+        s_ok = false;
+      }
+    }
+    __syncthreads();
+    ok = s_ok;
+    if (ok) {
+      const char* mine = fuse_half(c, c.bufs[c.rank], epoch);
+      const uint64_t slot = (uint64_t)Mo * N * 2;
+      const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
+      for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+        const uint64_t lrow = row - r0;
+        auto ld = [&](int p) {
+          uint4 v[W];
+#pragma unroll
+          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (lrow * nvec + p) * 16);
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
+          return pack_from<__nv_bfloat16>(acc);
+        };
+        auto st = [&](int p, const uint4& v) {
+#pragma unroll
+          for (int j = 0; j < W; ++j)
+            st_v4(c.bufs[(c.rank + j) % W] + c.sp_off + ((uint64_t)row * nvec + p) * 16, v);
+        };
+        residual_rmsnorm_row_st(ld, res_own + lrow * nvec, w, st, nvec, N, eps, red);
+      }
+    }
+  }
+  if (ok) grid_done_release(c, kStSpAgDone, epoch, [&](int o) { return ag_flag(c.bufs[o], c.rank); });
+  finish_call(c, epoch, kStFuseEpoch, kStFuseDone);
+}
+
+__global__ void sp_ag_wait_kernel(ArCtx c, int owners) {
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch);
+  if (poisoned(c)) return;
+  const int o = threadIdx.x;
+  if (o < owners && !wait_flag_geq(ag_flag(c.bufs[c.rank], o), epoch, c.timeout_ns))
+    record_error(c, kErrFuseWait, 0, o, 7, epoch);
+}
+
 // --------------------------------------------------------------------------
 // Allreduce + residual + RMSNorm, two-shot with posted stores only:
 //   A: every row is stored into its owner's region A slot[rank]
@@ -802,6 +932,7 @@ __global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const
                                                                   uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
+  trace_mark(c, 0);
   if (!poisoned(c)) {
     const uint64_t slot = c.half_bytes / W;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -814,7 +945,9 @@ __global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const
         st_v4(data_half(c.bufs[r], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
       }
     }
+    trace_mark(c, 1);
     if (block_barrier(c, 0, epoch, &s_ok)) {
+      trace_mark(c, 2);
       const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
       for (uint64_t i = i0; i < nvec; i += stride) {
 #pragma unroll
@@ -829,10 +962,76 @@ __global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const
 // Raw peer-store bench kernel (16-byte stores, capped grid): same role as the
 // reference's push microbench (sglang/mailbox_ar_ext.cu:201-221).
 // --------------------------------------------------------------------------
+// --------------------------------------------------------------------------
+// Raw transport kernels for the NVLink bandwidth benchmarks (the counterpart
+// of the reference's raw mailbox push bench, sglang/mailbox_ar_ext.cu:201-221):
+// SM stores into a peer (U vectors in flight per thread), SM loads from a
+// peer, NVLS multimem.ld_reduce from a multicast address (with or without
+// fp32 accumulation) and multimem.st to one.
+// --------------------------------------------------------------------------
+template <int U>
 __global__ void push_raw_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, uint64_t nvec) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride)
-    st_v4(dst + i, ld_nc_v4(src + i));
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i + u * stride < nvec) v[u] = ld_nc_v4(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i + u * stride < nvec) st_v4(dst + i + u * stride, v[u]);
+  }
+}
+
+__global__ void pull_raw_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, uint64_t nvec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride * kU) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i + u * stride < nvec) v[u] = ld_cg_v4(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i + u * stride < nvec) dst[i + u * stride] = v[u];
+  }
+}
+
+MBX_DEVICE uint4 multimem_ld_reduce_bf16_noacc(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
+template <bool kAcc>
+__global__ void mc_reduce_raw_kernel(uint4* __restrict__ dst, const char* mc, uint64_t nvec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride * kU) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i + u * stride < nvec)
+        v[u] = kAcc ? multimem_ld_reduce<__nv_bfloat16>(mc + (i + u * stride) * 16)
+                    : multimem_ld_reduce_bf16_noacc(mc + (i + u * stride) * 16);
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i + u * stride < nvec) dst[i + u * stride] = v[u];
+  }
+}
+
+__global__ void mc_store_raw_kernel(char* mc, const uint4* __restrict__ src, uint64_t nvec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride * kU) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i + u * stride < nvec) v[u] = ld_nc_v4(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i + u * stride < nvec) multimem_st(mc + (i + u * stride) * 16, v[u]);
+  }
 }
 
 // ==========================================================================
@@ -969,6 +1168,39 @@ void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, cons
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
+void sp_rs_push_launch(const ArCtx& c, const void* x, int M, int N, int max_blocks, cudaStream_t stream) {
+  if (M == 0) return;
+  if (N % 8 != 0) throw std::runtime_error("sp_rs_push: N must be a multiple of 8");
+  const int W_ = c.world;
+  const int Mo = (M + W_ - 1) / W_;
+  if ((uint64_t)W_ * Mo * N * 2 > c.fuse_half_bytes)
+    throw std::runtime_error("sp_rs_push: message exceeds the reduce-scatter buffer");
+  const int g = ar_grid((uint64_t)M * N / 8, max_blocks);
+  MBX_DISPATCH_W(W_, sp_rs_push_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(x), M, N, Mo));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void sp_rs_norm_ag_launch(const ArCtx& c, int M, int N, void* res_own, const void* w, float eps, int max_blocks,
+                          cudaStream_t stream) {
+  if (M == 0) return;
+  if (N % 8 != 0) throw std::runtime_error("sp_rs_norm_ag: N must be a multiple of 8");
+  const int W_ = c.world;
+  const int Mo = (M + W_ - 1) / W_;
+  if ((uint64_t)M * N * 2 > c.sp_bytes) throw std::runtime_error("sp_rs_norm_ag: rows exceed the gather buffer");
+  const int g = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
+  MBX_DISPATCH_W(W_, sp_rs_norm_ag_kernel<W><<<g, kArThreads, 0, stream>>>(
+                         c, M, N, Mo, static_cast<uint4*>(res_own), static_cast<const uint4*>(w), eps));
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void sp_ag_wait_launch(const ArCtx& c, int M, cudaStream_t stream) {
+  if (M == 0) return;
+  const int Mo = (M + c.world - 1) / c.world;
+  const int owners = std::min(c.world, (M + Mo - 1) / Mo);
+  sp_ag_wait_kernel<<<1, 32, 0, stream>>>(c, owners);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
 void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream) {
   if (nbytes % 16 != 0 || nbytes > c.seg_slot_bytes)
     throw std::runtime_error("submit_seg: segment must be a multiple of 16 bytes and <= slot size " +
@@ -992,14 +1224,25 @@ void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, ui
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
-void push_raw_launch(void* dst, const void* src, uint64_t nbytes, int grid_cap, cudaStream_t stream) {
-  if (nbytes % 16 != 0) throw std::runtime_error("push_raw: bytes must be a multiple of 16");
+void raw_transport_launch(int kind, void* dst, const void* src, uint64_t nbytes, int grid, int threads,
+                          cudaStream_t stream) {
+  if (nbytes % 16 != 0) throw std::runtime_error("raw transport: bytes must be a multiple of 16");
+  if (grid < 1 || grid > 65535 || threads < 32 || threads > 1024 || threads % 32)
+    throw std::runtime_error("raw transport: bad launch shape");
   const uint64_t nvec = nbytes / 16;
-  uint64_t g = (nvec + 255) / 256;
-  if (g < 1) g = 1;
-  if (g > 65535) g = 65535;
-  if (grid_cap > 0 && g > (uint64_t)grid_cap) g = grid_cap;
-  push_raw_kernel<<<(unsigned)g, 256, 0, stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), nvec);
+  auto d4 = static_cast<uint4*>(dst);
+  auto s4 = static_cast<const uint4*>(src);
+  switch (kind) {
+    case kRawPush1: push_raw_kernel<1><<<grid, threads, 0, stream>>>(d4, s4, nvec); break;
+    case kRawPush4: push_raw_kernel<4><<<grid, threads, 0, stream>>>(d4, s4, nvec); break;
+    case kRawPull4: pull_raw_kernel<<<grid, threads, 0, stream>>>(d4, s4, nvec); break;
+    case kRawMcReduce: mc_reduce_raw_kernel<true><<<grid, threads, 0, stream>>>(d4, static_cast<const char*>(src), nvec); break;
+    case kRawMcReduceNoAcc:
+      mc_reduce_raw_kernel<false><<<grid, threads, 0, stream>>>(d4, static_cast<const char*>(src), nvec);
+      break;
+    case kRawMcStore: mc_store_raw_kernel<<<grid, threads, 0, stream>>>(static_cast<char*>(dst), s4, nvec); break;
+    default: throw std::runtime_error("raw transport: unknown kind");
+  }
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -40,6 +40,12 @@ MBX_DEVICE void record_error(const ArCtx& c, uint32_t code, int block, int peer,
 // before the signalling thread's system-scope release, and the waiting
 // thread's acquire is ordered before the block's later loads by the trailing
 // __syncthreads. Returns false (after recording the error) on timeout.
+// Phase timestamp of block 0 (benchmarks only; c.trace is null otherwise).
+// Slot k holds %globaltimer at mark k of the last call.
+MBX_DEVICE void trace_mark(const ArCtx& c, int k) {
+  if (c.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) c.trace[k] = globaltimer_ns();
+}
+
 MBX_DEVICE bool block_barrier(const ArCtx& c, int phase, uint32_t epoch, bool* s_ok) {
   const int b = blockIdx.x;
   const int t = threadIdx.x;

@@ -36,6 +36,9 @@ constexpr size_t kSegReadyOff = kBarOff + sizeof(uint32_t) * kPhases * kMaxBlock
 constexpr size_t kSegFreeOff = kSegReadyOff + sizeof(uint32_t) * kSegSlots * kMaxRanks;
 constexpr size_t kTileFlagOff = kSegFreeOff + sizeof(uint32_t) * kSegSlots * kMaxRanks;
 constexpr size_t kSigBytes = 1 << 20;  // 1 MiB signal area (keeps data 1 MiB aligned)
+// Sequence-parallel all-gather flags: word `owner` = epoch of the last
+// all-gather whose rows from `owner` have landed in this rank's gather buffer.
+constexpr size_t kAgFlagOff = kTileFlagOff + sizeof(uint32_t) * 64;
 static_assert(kTileFlagOff + sizeof(uint32_t) * kTileFlagSlots * kMaxRanks <= kSigBytes,
               "signal area overflow");
 
@@ -51,6 +54,7 @@ enum StateWord : int {
   kStFuseEpoch = 7,      // fused GEMM-epilogue path epoch
   kStFuseDone = 8,       // blocks finished in the current fused reduce kernel
   kStFuseGemmDone = 9,   // GEMM CTAs finished pushing in the current fused call
+  kStSpAgDone = 10,      // blocks finished pushing in the current sequence-parallel all-gather
   kStWords = 16
 };
 
@@ -85,6 +89,9 @@ struct ArCtx {
   uint64_t seg_slot_bytes; // size of one segmented slot (per source rank)
   uint64_t fuse_off;       // byte offset of the fused path's halves
   uint64_t fuse_half_bytes;// size of one fused half (0 = fused path disabled)
+  uint64_t sp_off;         // byte offset of the sequence-parallel gather buffer G (0 = none)
+  uint64_t sp_bytes;       // its size
+  uint64_t* trace;         // optional device array of phase timestamps (block 0), or nullptr
   int rank;
   int world;
 };

@@ -500,20 +500,43 @@ __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(DecodeArg
   }
 }
 
-__global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
-                                      __nv_bfloat16* __restrict__ o) {
-  // one block per (b, head), D threads
-  const int64_t bh = blockIdx.x;
+// Split-KV combine: one warp per (row, head), lane l owns dims 4l..4l+3.
+// o = sum_s 2^(lse_s - max) o_s / sum_s 2^(lse_s - max); splits that saw no
+// key have lse = -inf and weight 0; a row with no key at all gets zeros.
+constexpr int kCombineRows = 8;  // warps (rows) per block
+__global__ void __launch_bounds__(32 * kCombineRows) decode_combine_kernel(const float* __restrict__ part_o,
+                                                                          const float* __restrict__ part_lse,
+                                                                          int splits, int64_t rows,
+                                                                          __nv_bfloat16* __restrict__ o) {
+  const int64_t bh = (int64_t)blockIdx.x * kCombineRows + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (bh >= rows) return;
   const float* lse = part_lse + bh * splits;
   float mx = -INFINITY;
-  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, lse[s]);
-  float den = 0.f, num = 0.f;
+  for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, lse[s]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float4* po = reinterpret_cast<const float4*>(part_o + bh * splits * D) + lane;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+#pragma unroll 4
   for (int s = 0; s < splits; ++s) {
-    const float w = (lse[s] == -INFINITY) ? 0.f : exp2f(lse[s] - mx);
+    const float ls = lse[s];
+    const float w = (ls == -INFINITY) ? 0.f : exp2f(ls - mx);
+    const float4 v = __ldg(po + s * (D / 4));
     den += w;
-    num += w * part_o[(bh * splits + s) * D + threadIdx.x];
+    acc.x += w * v.x;
+    acc.y += w * v.y;
+    acc.z += w * v.z;
+    acc.w += w * v.w;
   }
-  o[bh * D + threadIdx.x] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+  __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  uint2 packed;
+  packed.x = *reinterpret_cast<uint32_t*>(&lo);
+  packed.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(o + bh * D + lane * 4) = packed;
 }
 
 }  // namespace
@@ -550,7 +573,9 @@ void prefill_attention_launch(const void* q, const void* kc, const void* vc, voi
 void attn_combine_launch(const float* part_o, const float* part_lse, int64_t rows, int splits, void* out,
                          cudaStream_t s) {
   if (rows == 0) return;
-  decode_combine_kernel<<<(unsigned)rows, D, 0, s>>>(part_o, part_lse, splits, static_cast<__nv_bfloat16*>(out));
+  const unsigned blocks = (unsigned)((rows + kCombineRows - 1) / kCombineRows);
+  decode_combine_kernel<<<blocks, 32 * kCombineRows, 0, s>>>(part_o, part_lse, splits, rows,
+                                                             static_cast<__nv_bfloat16*>(out));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -583,7 +608,7 @@ void decode_attention_launch(const void* q, const void* kc, const void* vc, void
   decode_attention_kernel<<<grid, kDecThreads, kDecSmem, s>>>(a);
   MBX_CUDA_CHECK(cudaGetLastError());
   if (a.splits > 1) {
-    decode_combine_kernel<<<B * nq, D, 0, s>>>(a.part_o, a.part_lse, a.splits, a.o);
+    attn_combine_launch(a.part_o, a.part_lse, (int64_t)B * nq, a.splits, a.o, s);
     MBX_CUDA_CHECK(cudaGetLastError());
   }
 }

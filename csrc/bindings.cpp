@@ -33,7 +33,7 @@ class ArComm {
  public:
   ArComm(int rank, int world, std::vector<int64_t> bufs, int64_t mc, int64_t state, int64_t status_dev,
          int64_t status_host, uint64_t half_bytes, uint64_t seg_slot_bytes, uint64_t timeout_ns,
-         uint64_t fuse_half_bytes)
+         uint64_t fuse_half_bytes, uint64_t sp_bytes)
       : status_host_(reinterpret_cast<volatile uint32_t*>(status_host)) {
     TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)bufs.size() == world, "ArComm: bad world size");
     std::memset(&c_, 0, sizeof(c_));
@@ -46,6 +46,12 @@ class ArComm {
     c_.seg_slot_bytes = seg_slot_bytes;
     c_.fuse_off = kSigBytes + 2 * half_bytes;
     c_.fuse_half_bytes = fuse_half_bytes;
+    // buffer layout: [signals][2 AR halves][2 fused halves][segment slots][G]
+    c_.sp_off = sp_bytes ? kSigBytes + 2 * half_bytes + 2 * fuse_half_bytes +
+                               (uint64_t)kSegSlots * kMaxRanks * seg_slot_bytes
+                         : 0;
+    c_.sp_bytes = sp_bytes;
+    c_.trace = nullptr;
     c_.rank = rank;
     c_.world = world;
   }
@@ -85,6 +91,55 @@ class ArComm {
                            reinterpret_cast<uint32_t*>(err.data_ptr<int>()), max_blocks, push_all, cur_stream());
   }
   uint64_t fused_capacity() const { return c_.fuse_half_bytes; }
+
+  // ---- sequence parallel (rank r owns rows [r*Mo, r*Mo+Mo), Mo = ceil(M/world))
+  void gemm_rs(torch::Tensor a, torch::Tensor w, torch::Tensor err) {
+    check_bf16(a, "a");
+    check_bf16(w, "w");
+    TORCH_CHECK(w.size(1) == a.size(1), "gemm_rs: K mismatch");
+    gemm_rs_launch(c_, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), a.size(0), w.size(0), a.size(1),
+                   reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
+  }
+  void sp_rs_push(torch::Tensor x, int max_blocks) {
+    check_bf16(x, "x");
+    TORCH_CHECK(x.dim() == 2, "sp_rs_push: x must be [M, N]");
+    sp_rs_push_launch(c_, x.data_ptr(), (int)x.size(0), (int)x.size(1), max_blocks, cur_stream());
+  }
+  void sp_rs_norm_ag(int M, torch::Tensor res_own, torch::Tensor w, double eps, int max_blocks) {
+    check_bf16(res_own, "res_own");
+    check_bf16(w, "w");
+    const int N = (int)w.numel();
+    const int Mo = (M + c_.world - 1) / c_.world;
+    TORCH_CHECK(res_own.numel() >= (int64_t)Mo * N, "sp_rs_norm_ag: residual shard must hold Mo rows");
+    sp_rs_norm_ag_launch(c_, M, N, res_own.data_ptr(), w.data_ptr(), (float)eps, max_blocks, cur_stream());
+  }
+  // out[M, Nout] = G[M, K] * w[Nout, K]^T, loading each m-tile once its owners' rows landed.
+  void sp_gemm_ag(int M, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> workspace,
+                  torch::Tensor err) {
+    check_bf16(w, "w");
+    check_bf16(out, "out");
+    const int64_t N = w.size(0), K = w.size(1);
+    TORCH_CHECK(out.size(0) >= M && out.size(1) == N, "sp_gemm_ag: out must be [M, Nout]");
+    TORCH_CHECK((uint64_t)M * K * 2 <= c_.sp_bytes, "sp_gemm_ag: rows exceed the gather buffer");
+    float* ws = nullptr;
+    if (workspace.has_value()) {
+      const int64_t need_splits = gemm_plan(M, N, K).splits;
+      TORCH_CHECK(workspace->numel() >= need_splits * M * N, "sp_gemm_ag: workspace too small");
+      ws = workspace->data_ptr<float>();
+    }
+    GemmAgWait ag;
+    ag.flags = reinterpret_cast<const uint32_t*>(c_.bufs[c_.rank] + kAgFlagOff);
+    ag.epoch_word = c_.state + kStFuseEpoch;
+    ag.Mo = (M + c_.world - 1) / c_.world;
+    gemm_launch(c_.bufs[c_.rank] + c_.sp_off, K, w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0), nullptr, M,
+                N, K, 0, 0, ws, nullptr, reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream(), &ag);
+  }
+  void sp_ag_wait(int M) { sp_ag_wait_launch(c_, M, cur_stream()); }
+  int64_t sp_gather_ptr() const { return c_.sp_off ? reinterpret_cast<int64_t>(c_.bufs[c_.rank] + c_.sp_off) : 0; }
+  uint64_t sp_capacity() const { return c_.sp_bytes; }
+  // Device array of >= 8 uint64 that block 0 of every later allreduce call
+  // fills with %globaltimer phase marks (0 = off).
+  void set_trace(int64_t ptr) { c_.trace = reinterpret_cast<uint64_t*>(ptr); }
   uint64_t chunk_limit(int algo) const { return ar_chunk_limit(c_, algo); }
   std::vector<int64_t> status() const {
     std::vector<int64_t> v(kStatusWords);
@@ -353,12 +408,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   py::class_<ArComm>(m, "ArComm")
       .def(py::init<int, int, std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, uint64_t, uint64_t, uint64_t,
-                    uint64_t>(),
+                    uint64_t, uint64_t>(),
            py::arg("rank"), py::arg("world"), py::arg("bufs"), py::arg("mc"), py::arg("state"), py::arg("status_dev"),
            py::arg("status_host"), py::arg("half_bytes"), py::arg("seg_slot_bytes"), py::arg("timeout_ns"),
-           py::arg("fuse_half_bytes") = 0)
+           py::arg("fuse_half_bytes") = 0, py::arg("sp_bytes") = 0)
+      .def("gemm_rs", &ArComm::gemm_rs)
+      .def("sp_rs_push", &ArComm::sp_rs_push)
+      .def("sp_rs_norm_ag", &ArComm::sp_rs_norm_ag)
+      .def("sp_gemm_ag", &ArComm::sp_gemm_ag, py::arg("M"), py::arg("w"), py::arg("out"), py::arg("workspace"),
+           py::arg("err"))
+      .def("sp_ag_wait", &ArComm::sp_ag_wait)
+      .def("sp_gather_ptr", &ArComm::sp_gather_ptr)
+      .def("sp_capacity", &ArComm::sp_capacity)
       .def("gemm_ar_rmsnorm", &ArComm::gemm_ar_rmsnorm)
       .def("fused_capacity", &ArComm::fused_capacity)
+      .def("set_trace", &ArComm::set_trace)
       .def("allreduce", &ArComm::allreduce, py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("dtype"),
            py::arg("algo"), py::arg("max_blocks"), py::arg("stream"))
       .def("ar_rmsnorm", &ArComm::ar_rmsnorm, py::arg("inp"), py::arg("residual"), py::arg("weight"), py::arg("out"),
@@ -375,12 +439,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("clear_status", &ArComm::clear_status)
       .def("has_multicast", &ArComm::has_multicast);
   m.def(
-      "push_raw",
-      [](int64_t dst, int64_t src, uint64_t nbytes, int grid_cap, int64_t stream) {
-        push_raw_launch(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes, grid_cap,
-                        stream_of(stream));
+      "raw_transport",
+      [](int kind, int64_t dst, int64_t src, uint64_t nbytes, int grid, int threads, int64_t stream) {
+        raw_transport_launch(kind, reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes, grid,
+                             threads, stream_of(stream));
       },
-      py::arg("dst"), py::arg("src"), py::arg("nbytes"), py::arg("grid_cap"), py::arg("stream"));
+      py::arg("kind"), py::arg("dst"), py::arg("src"), py::arg("nbytes"), py::arg("grid"), py::arg("threads"),
+      py::arg("stream"));
   m.def(
       "ce_push",
       [](int64_t dst, int64_t src, uint64_t nbytes, int64_t stream) {

@@ -19,6 +19,8 @@
 // error word, drains its own in-flight TMA/MMA, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include <algorithm>
 #include <mutex>
 #include <stdexcept>
@@ -55,6 +57,12 @@ struct GemmArgs {
   ArCtx ar;
   int Mo;
   int push_all;
+  // Sequence-parallel all-gather consumer: before the first load of m-tile m
+  // the producer waits until every owner of its rows (row / ag_Mo) has
+  // released ag_flags[owner] >= *ag_epoch_word (nullptr = no wait).
+  const uint32_t* ag_flags;
+  const uint32_t* ag_epoch_word;
+  int ag_Mo;
   // split-K: per-tile arrival counters (zeroed once; the last CTA of a tile
   // resets its counter) and the final bf16 output of the in-kernel reduction
   uint32_t* tile_counters;
@@ -162,6 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tc::elect_one()) {
       tc::tma_prefetch_desc(&tmA);
       tc::tma_prefetch_desc(&tmB);
+      const uint32_t ag_epoch = args.ag_flags ? *reinterpret_cast<const volatile uint32_t*>(args.ag_epoch_word) : 0u;
+      int ready_m = -1;
       uint32_t it = 0;
       for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
         const int m = u % args.num_m;
@@ -170,6 +180,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ks = rest / args.num_n;
         const int kb0 = ks * args.kb_per_split;
         const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        if (args.ag_flags != nullptr && m != ready_m) {
+          // rows [m*BM, m*BM+BM) come from their owners' all-gather pushes
+          const int o0 = (m * BM) / args.ag_Mo;
+          const int o1 = (min(args.M, m * BM + BM) - 1) / args.ag_Mo;
+          bool ok = true;
+          for (int o = o0; o <= o1 && ok; ++o) ok = wait_flag_geq(args.ag_flags + o, ag_epoch, args.timeout_ns);
+          if (!ok) {
+            set_err(args.err, 4, abort);
+            break;
+          }
+          // the rows were written by peers' generic-proxy stores; TMA reads
+          // through the async proxy
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          ready_m = m;
+        }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -612,6 +637,40 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
   return plan_for(M, N, K, num_sms());
 }
 
+namespace {
+GemmArgs push_args(const ArCtx& c, int64_t M, int64_t N, int64_t K, int bn, int64_t Mo, bool push_all, uint32_t* err) {
+  GemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.ldc = N;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.num_m = (int)((M + BM - 1) / BM);
+  a.num_n = (int)((N + bn - 1) / bn);
+  a.kb_total = (int)((K + BK - 1) / BK);
+  a.splits = 1;
+  a.kb_per_split = a.kb_total;
+  a.err = err;
+  a.timeout_ns = 2000000000ull;
+  a.ar = c;
+  a.Mo = (int)Mo;
+  a.push_all = push_all ? 1 : 0;
+  return a;
+}
+
+void launch_push_gemm(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                      int64_t K, int64_t Mo, bool push_all, uint32_t* err, cudaStream_t s) {
+  const int sms = num_sms();
+  GemmPlan p = plan_for(M, N, K, sms);
+  GemmArgs a = push_args(c, M, N, K, p.bn, Mo, push_all, err);
+  const CUtensorMap ta = make_map(A, M, K, lda, BM);
+  const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);
+  const int units = a.num_m * a.num_n;
+  launch_bn<kEpiPushRS>(p.bn, ta, tb, a, std::min(units, sms), s);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+}  // namespace
+
 void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
                             int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
                             uint32_t* err, int max_blocks, bool push_all, cudaStream_t s) {
@@ -623,43 +682,29 @@ void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const vo
   if (c.fuse_half_bytes == 0 || need > c.fuse_half_bytes)
     throw std::runtime_error("gemm_ar: message needs " + std::to_string(need) + " bytes of fused buffer, have " +
                              std::to_string(c.fuse_half_bytes));
-  const int sms = num_sms();
-  GemmPlan p = plan_for(M, N, K, sms);
-  GemmArgs a;
-  a.out = nullptr;
-  a.residual = nullptr;
-  a.ldc = N;
-  a.M = (int)M;
-  a.N = (int)N;
-  a.K = (int)K;
-  a.num_m = (int)((M + BM - 1) / BM);
-  a.num_n = (int)((N + p.bn - 1) / p.bn);
-  a.kb_total = (int)((K + BK - 1) / BK);
-  a.splits = 1;
-  a.kb_per_split = a.kb_total;
-  a.err = err;
-  a.timeout_ns = 2000000000ull;
-  a.ar = c;
-  a.Mo = (int)Mo;
-  a.push_all = push_all ? 1 : 0;
-  a.tile_counters = nullptr;
-  a.final_out = nullptr;
-  a.final_ld = 0;
-  const CUtensorMap ta = make_map(A, M, K, lda, BM);
-  const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);
-  const int units = a.num_m * a.num_n;
-  launch_bn<kEpiPushRS>(p.bn, ta, tb, a, std::min(units, sms), s);
-  MBX_CUDA_CHECK(cudaGetLastError());
+  launch_push_gemm(c, A, lda, B, ldb, M, N, K, Mo, push_all, err, s);
   if (push_all) fused_allsum_norm_launch(c, (int)M, (int)N, residual, norm_w, out, eps, max_blocks, s);
   else fused_rs_norm_launch(c, (int)M, (int)N, (int)Mo, residual, norm_w, out, eps, max_blocks, s);
 }
 
+void gemm_rs_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                    int64_t K, uint32_t* err, cudaStream_t s) {
+  if (M == 0) return;
+  if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm_rs: K and N must be multiples of 8");
+  const int64_t Mo = (M + c.world - 1) / c.world;
+  if ((uint64_t)c.world * Mo * N * 2 > c.fuse_half_bytes)
+    throw std::runtime_error("gemm_rs: [" + std::to_string(M) + ", " + std::to_string(N) +
+                             "] exceeds the reduce-scatter buffer");
+  launch_push_gemm(c, A, lda, B, ldb, M, N, K, Mo, false, err, s);
+}
+
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,
-                 uint32_t* err, cudaStream_t s) {
+                 uint32_t* err, cudaStream_t s, const GemmAgWait* ag) {
   if (M == 0 || N == 0) return;
-  // explicit bn/splits requests keep the regular orientation (tests, tuning)
-  const bool swap_ok = bn <= 0 && splits <= 0 && N % 4 == 0;
+  // explicit bn/splits requests keep the regular orientation (tests, tuning);
+  // an all-gather consumer keeps it too (its rows arrive per m-tile)
+  const bool swap_ok = bn <= 0 && splits <= 0 && N % 4 == 0 && ag == nullptr;
   if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm: K and N must be multiples of 8");
   if (ldc % 8 != 0 || ((uint64_t)C & 15) != 0) throw std::runtime_error("gemm: C must be 16-byte aligned rows");
   const int sms = num_sms();
@@ -669,6 +714,12 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   if (p.bn != 64 && p.bn != 128 && p.bn != 160 && p.bn != 192 && p.bn != 224 && p.bn != 256)
     throw std::runtime_error("gemm: BN must be one of 64, 128, 160, 192, 224, 256");
   GemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  if (ag != nullptr) {
+    a.ag_flags = ag->flags;
+    a.ag_epoch_word = ag->epoch_word;
+    a.ag_Mo = ag->Mo;
+  }
   a.residual = static_cast<const __nv_bfloat16*>(residual);
   a.ldc = ldc;
   a.M = (int)M;

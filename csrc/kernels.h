@@ -29,7 +29,12 @@ void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, cons
 void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream);
 void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, uint64_t nbytes, int max_blocks,
                      cudaStream_t stream);
-void push_raw_launch(void* dst, const void* src, uint64_t nbytes, int grid_cap, cudaStream_t stream);
+// Raw NVLink transport kernels for bandwidth benchmarks. kMcReduce* read the
+// multicast address `src` and write local `dst`; kMcStore reads local `src`
+// and stores to the multicast address `dst`.
+enum RawKind { kRawPush1 = 0, kRawPush4 = 1, kRawPull4 = 2, kRawMcReduce = 3, kRawMcReduceNoAcc = 4, kRawMcStore = 5 };
+void raw_transport_launch(int kind, void* dst, const void* src, uint64_t nbytes, int grid, int threads,
+                          cudaStream_t stream);
 
 // ---- elementwise (ops/elementwise.cu) ----------------------------------------
 void rmsnorm_launch(const void* x, void* residual, const void* w, void* out, int64_t M, int H, float eps,
@@ -53,9 +58,16 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K);
 // splits > 1 needs an fp32 workspace of splits*M*N elements.
 // counters: zeroed uint32 per-tile arrival counters for the in-kernel split-K
 // reduction (nullptr: a separate reduce kernel folds the partials).
+// ag != nullptr: A is a sequence-parallel gather buffer; the producer waits
+// for the owners' all-gather flags of each m-tile before loading it.
+struct GemmAgWait {
+  const uint32_t* flags;       // this rank's all-gather flag words (one per owner)
+  const uint32_t* epoch_word;  // device word holding the epoch to wait for
+  int Mo;                      // rows per owner
+};
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,
-                 uint32_t* err, cudaStream_t s);
+                 uint32_t* err, cudaStream_t s, const GemmAgWait* ag = nullptr);
 
 // Row-parallel GEMM fused with allreduce + residual add + RMSNorm: the GEMM
 // epilogue stores its partial rows straight into the owner ranks' symmetric
@@ -68,6 +80,23 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
                             int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
                             uint32_t* err, int max_blocks, bool push_all, cudaStream_t s);
+
+// ---- sequence parallel (gemm/gemm.cu, ar/allreduce.cu) ---------------------
+// Rank r owns rows [r*Mo, r*Mo+Mo) of the residual stream, Mo = ceil(M/world).
+// GEMM -> reduce-scatter: the epilogue pushes every output row to its owner's
+// reduce-scatter slot (same buffers and flags as the fused allreduce path).
+void gemm_rs_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                    int64_t K, uint32_t* err, cudaStream_t s);
+// Reduce-scatter of a local [M, N] tensor (e.g. the vocab-parallel embedding).
+void sp_rs_push_launch(const ArCtx& c, const void* x, int M, int N, int max_blocks, cudaStream_t s);
+// Reduce the owned rows (rank order, fp32, one rounding), residual shard +=
+// them (bf16), normalise, and push the normed rows into every rank's gather
+// buffer G ([M, N] at c.sp_off); the last block releases the all-gather flags.
+void sp_rs_norm_ag_launch(const ArCtx& c, int M, int N, void* res_own, const void* w, float eps, int max_blocks,
+                          cudaStream_t s);
+// Wait (one tiny block) until every owner's rows of the last all-gather landed
+// in G, for consumers other than the all-gather GEMM.
+void sp_ag_wait_launch(const ArCtx& c, int M, cudaStream_t s);
 
 // ---- attention (attn/attention.cu) -------------------------------------------
 void prefill_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* cu_q,
