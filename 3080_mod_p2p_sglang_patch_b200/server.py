@@ -1,0 +1,303 @@
+"""OpenAI-compatible HTTP front end for the TP engine (the role of sglang's
+``launch_server`` in the reference's flow: ``SGLANG_MAILBOX_AR=1 ...
+launch_server --tp 2``, reference scripts/sglang-p2p.sh:162; its
+prompt-processing bench posts to ``/v1/chat/completions`` and reads
+``usage.prompt_tokens``, tests/pp_bench.py:21-29).
+
+    torchrun --nproc-per-node N -m 3080_mod_p2p_sglang_patch_b200.server --model 8b --port 8001
+
+One process per GPU. Rank 0 serves HTTP and owns the request queue; every
+rank runs the same engine loop in lockstep: at each iteration rank 0
+broadcasts the newly arrived requests over a gloo control group, every rank
+adds them in the same order and runs one engine step (the TP collectives of
+that step then line up across ranks). With ``SGLANG_MAILBOX_AR=1`` the TP
+allreduces go through MailboxAR, otherwise NCCL.
+
+Weights are random (no checkpoints offline), so text goes through a byte
+tokenizer: UTF-8 bytes are token ids 0..255, generated ids >= 256 decode to
+nothing. Token-id prompts (``"prompt": [ids]``) are accepted as well.
+Greedy decoding only (``temperature`` is ignored).
+"""
+import argparse
+import datetime
+import itertools
+import logging
+import queue
+import threading
+import time
+
+logger = logging.getLogger(__name__)
+
+
+class ByteTokenizer:
+    """UTF-8 bytes as token ids (ids >= 256 have no text)."""
+
+    def encode(self, text: str) -> list:
+        return list(text.encode("utf-8"))
+
+    def decode(self, ids) -> str:
+        return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
+
+
+class _Pending:
+    __slots__ = ("prompt", "max_new", "event", "output", "error")
+
+    def __init__(self, prompt, max_new):
+        self.prompt = prompt
+        self.max_new = max_new
+        self.event = threading.Event()
+        self.output = None
+        self.error = None
+
+
+class EngineServer:
+    """Lockstep request loop over the TP ranks.
+
+    ``engine`` needs ``add_request(prompt, max_new) -> request`` (with ``.rid``
+    and ``.output``), ``step()``, and ``sched`` with ``has_work()`` and a
+    ``finished`` list (``engine.LLMEngine`` has them). ``group`` is a gloo
+    process group spanning the TP ranks (None on one rank).
+    """
+
+    SHUTDOWN = "__shutdown__"
+
+    def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None):
+        self.engine = engine
+        self.group = group
+        self.rank = rank
+        self.world = world
+        self.max_prompt = max_prompt
+        self.q = queue.Queue()
+        self._by_rid = {}
+        self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0, "steps": 0}
+        self._stopped = threading.Event()
+
+    # ------------------------------------------------------------ rank 0 API
+    def submit(self, prompt: list, max_new: int, timeout: float = None) -> list:
+        """Called from HTTP threads on rank 0: blocks until the request is done
+        and returns the generated token ids."""
+        if self._stopped.is_set():
+            raise RuntimeError("server stopped")
+        if not prompt:
+            raise ValueError("empty prompt")
+        if self.max_prompt is not None and len(prompt) + max_new > self.max_prompt:
+            raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
+                             f"max sequence {self.max_prompt}")
+        p = _Pending(list(prompt), int(max_new))
+        self.q.put(p)
+        if not p.event.wait(timeout):
+            raise TimeoutError("request timed out")
+        if p.error is not None:
+            raise RuntimeError(p.error)
+        return p.output
+
+    def stop(self):
+        """Ask every rank's loop to exit after the current step (rank 0)."""
+        self.q.put(self.SHUTDOWN)
+
+    # ------------------------------------------------------------ every rank
+    def _next_commands(self, idle: bool):
+        """Rank 0: the requests that arrived since the last step (blocking
+        while the engine is idle); every rank: the same list."""
+        cmds = []
+        if self.rank == 0:
+            if idle:
+                cmds.append(self.q.get())  # nothing to run: wait for work
+            while True:
+                try:
+                    cmds.append(self.q.get_nowait())
+                except queue.Empty:
+                    break
+        if self.world > 1:
+            import torch.distributed as dist
+
+            payload = [[c if c == self.SHUTDOWN else (c.prompt, c.max_new) for c in cmds]]
+            dist.broadcast_object_list(payload, src=0, group=self.group)
+            if self.rank != 0:
+                cmds = [c if c == self.SHUTDOWN else _Pending(c[0], c[1]) for c in payload[0]]
+        return cmds
+
+    def serve_forever(self):
+        eng = self.engine
+        try:
+            while True:
+                idle = not eng.sched.has_work()
+                cmds = self._next_commands(idle)
+                stop = False
+                for c in cmds:
+                    if c == self.SHUTDOWN:
+                        stop = True
+                        continue
+                    req = eng.add_request(c.prompt, c.max_new)
+                    self._by_rid[req.rid] = c
+                    self.stats["requests"] += 1
+                    self.stats["prompt_tokens"] += len(c.prompt)
+                if stop:
+                    break
+                if eng.sched.has_work():
+                    eng.step()
+                    self.stats["steps"] += 1
+                done, eng.sched.finished = eng.sched.finished, []
+                for r in done:
+                    p = self._by_rid.pop(r.rid, None)
+                    if p is not None:
+                        p.output = list(r.output)
+                        self.stats["completion_tokens"] += len(r.output)
+                        p.event.set()
+        except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
+            for p in self._by_rid.values():
+                p.error = repr(e)
+                p.event.set()
+            raise
+        finally:
+            self._stopped.set()
+            for p in self._by_rid.values():
+                if not p.event.is_set():
+                    p.error = "server stopped"
+                    p.event.set()
+            while True:
+                try:
+                    c = self.q.get_nowait()
+                except queue.Empty:
+                    break
+                if c != self.SHUTDOWN:
+                    c.error = "server stopped"
+                    c.event.set()
+
+
+def build_app(server: EngineServer, model_name: str, tokenizer=None):
+    """FastAPI app with /health, /v1/models, /v1/completions and
+    /v1/chat/completions (non-streaming, greedy)."""
+    from fastapi import FastAPI, HTTPException
+    from fastapi.concurrency import run_in_threadpool
+
+    tok = tokenizer or ByteTokenizer()
+    app = FastAPI()
+    ids = itertools.count()
+
+    def _prompt_ids(p):
+        if isinstance(p, list) and all(isinstance(i, int) for i in p):
+            return p
+        if isinstance(p, str):
+            return tok.encode(p)
+        raise HTTPException(400, "prompt must be a string or a list of token ids")
+
+    def _run(prompt, max_tokens):
+        try:
+            return server.submit(prompt, max_tokens)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        except (RuntimeError, TimeoutError) as e:
+            raise HTTPException(503, str(e)) from e
+
+    def _usage(prompt, out):
+        return {"prompt_tokens": len(prompt), "completion_tokens": len(out), "total_tokens": len(prompt) + len(out)}
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok", **server.stats}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "mailbox-ar-b200"}]}
+
+    @app.post("/v1/completions")
+    async def completions(body: dict):
+        prompt = _prompt_ids(body.get("prompt", ""))
+        max_tokens = int(body.get("max_tokens", 16))
+        out = await run_in_threadpool(_run, prompt, max_tokens)
+        return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
+                "model": model_name,
+                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": "length"}],
+                "usage": _usage(prompt, out)}
+
+    @app.post("/v1/chat/completions")
+    async def chat(body: dict):
+        msgs = body.get("messages") or []
+        text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
+        prompt = tok.encode(text)
+        max_tokens = int(body.get("max_tokens", 16))
+        out = await run_in_threadpool(_run, prompt, max_tokens)
+        return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
+                "model": model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
+                             "token_ids": out, "finish_reason": "length"}],
+                "usage": _usage(prompt, out)}
+
+    return app
+
+
+def start_http(app, host: str, port: int):
+    """Run uvicorn in a daemon thread; returns (server, thread)."""
+    import uvicorn
+
+    config = uvicorn.Config(app, host=host, port=port, log_level="warning", lifespan="off")
+    srv = uvicorn.Server(config)
+    th = threading.Thread(target=srv.run, daemon=True, name="http")
+    th.start()
+    deadline = time.time() + 30
+    while not srv.started and th.is_alive() and time.time() < deadline:
+        time.sleep(0.02)
+    if not srv.started:
+        raise RuntimeError(f"HTTP server did not start on {host}:{port}")
+    return srv, th
+
+
+def main(argv=None):
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--model", default="8b", help="8b | 70b | tiny")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8001)
+    ap.add_argument("--max-batch", type=int, default=64)
+    ap.add_argument("--max-seq", type=int, default=16384)
+    ap.add_argument("--chunk", type=int, default=1024)
+    ap.add_argument("--impl", default="native", choices=["native", "torch"])
+    ap.add_argument("--no-graphs", action="store_true")
+    args = ap.parse_args(argv)
+    logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
+    pkg = __name__.rsplit(".", 1)[0]
+    par = importlib.import_module(f"{pkg}.parallel")
+    models = importlib.import_module(f"{pkg}.models")
+    eng_mod = importlib.import_module(f"{pkg}.engine")
+    rank, world, local = par.init_distributed(timeout_s=600)
+    dev = torch.device("cuda", local)
+    # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow
+    tp = par.TPGroup(None, dev, use_mailbox=None) if world > 1 else None
+    ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
+    cfg = models.LlamaConfig.by_name(args.model)
+    eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=args.max_batch, max_seq=args.max_seq, chunk=args.chunk, seed=0,
+                            use_graphs=not args.no_graphs, impl=args.impl,
+                            prefill_graph=(args.impl == "native" and not args.no_graphs))
+    server = EngineServer(eng, ctrl, rank, world, max_prompt=args.max_seq)
+    http = None
+    if rank == 0:
+        import signal
+
+        # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step
+        for sig in (signal.SIGINT, signal.SIGTERM):
+            signal.signal(sig, lambda *_: server.stop())
+        http, _ = start_http(build_app(server, cfg.name), args.host, args.port)
+        logger.info("serving %s at http://%s:%d (TP=%d, allreduce=%s)", cfg.name, args.host, args.port, world,
+                    "MailboxAR" if (tp is not None and tp.ca_comm is not None) else "NCCL")
+    try:
+        server.serve_forever()
+    except KeyboardInterrupt:
+        pass
+    finally:
+        if http is not None:
+            http.should_exit = True
+        if eng.graphs is not None:
+            eng.graphs.close()
+        if tp is not None:
+            tp.close()
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

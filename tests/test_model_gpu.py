@@ -137,3 +137,45 @@ def test_prefill_graph_matches_eager():
         if pg:
             assert eng.prefill_graph.graph is not None
     assert res[0] == res[1]
+
+
+def test_http_server_matches_generate():
+    """The OpenAI-style front end drives the real engine: token-id prompts
+    posted concurrently come back with the same greedy tokens as
+    ``generate`` on the same weights."""
+    requests = pytest.importorskip("requests")
+    import threading
+
+    from conftest import free_port
+
+    models, eng_mod, srv_mod = sub("models"), sub("engine"), sub("server")
+    cfg = models.LlamaConfig.tiny()
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=torch.Generator().manual_seed(n)).tolist()
+               for n in (40, 130, 7)]
+    want = eng_mod.LLMEngine(cfg, max_batch=4, max_seq=512, chunk=64, seed=21, use_graphs=False).generate(
+        prompts, max_new_tokens=6)
+    eng = eng_mod.LLMEngine(cfg, max_batch=4, max_seq=512, chunk=64, seed=21, use_graphs=False)
+    server = srv_mod.EngineServer(eng, max_prompt=512)
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, cfg.name), "127.0.0.1", port)
+    got = [None] * len(prompts)
+
+    def clients():
+        def one(i):
+            r = requests.post(f"http://127.0.0.1:{port}/v1/completions",
+                              json={"prompt": prompts[i], "max_tokens": 6}, timeout=120)
+            got[i] = r.json()["choices"][0]["token_ids"]
+
+        ths = [threading.Thread(target=one, args=(i,)) for i in range(len(prompts))]
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        server.stop()
+
+    threading.Thread(target=clients, daemon=True).start()
+    try:
+        server.serve_forever()  # CUDA work stays on this thread
+    finally:
+        http.should_exit = True
+    assert got == want

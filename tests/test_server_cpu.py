@@ -1,0 +1,151 @@
+"""HTTP front end and the lockstep request loop, on CPU with a stand-in
+engine (the real engine needs the GPU; tests/test_model_gpu.py covers it).
+
+The reference's clients post OpenAI-style requests and read
+``usage.prompt_tokens`` (tests/pp_bench.py:21-29); the same shapes are
+checked here, plus that every TP rank runs the same requests in the same
+order (two gloo ranks).
+"""
+import importlib
+import threading
+
+import pytest
+
+from _mp import run_ranks
+
+srv_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.server")
+
+
+class _Req:
+    def __init__(self, rid, prompt, max_new):
+        self.rid, self.prompt, self.max_new, self.output = rid, list(prompt), max_new, []
+
+
+class _Sched:
+    def __init__(self):
+        self.running, self.finished = [], []
+
+    def has_work(self):
+        return bool(self.running)
+
+
+class FakeEngine:
+    """One token per running request per step: (sum(prompt) + len(output)) % 1000."""
+
+    def __init__(self):
+        self.sched = _Sched()
+        self.n = 0
+        self.log = []
+
+    def add_request(self, prompt, max_new):
+        r = _Req(self.n, prompt, max_new)
+        self.n += 1
+        self.sched.running.append(r)
+        self.log.append((r.rid, tuple(prompt), max_new))
+        return r
+
+    def step(self):
+        for r in list(self.sched.running):
+            r.output.append((sum(r.prompt) + len(r.output)) % 1000)
+            if len(r.output) >= r.max_new:
+                self.sched.running.remove(r)
+                self.sched.finished.append(r)
+
+
+def expected(prompt, n):
+    return [(sum(prompt) + i) % 1000 for i in range(n)]
+
+
+def test_byte_tokenizer_roundtrip():
+    tok = srv_mod.ByteTokenizer()
+    text = "KV cache 页 16 ✓"
+    ids = tok.encode(text)
+    assert all(0 <= i < 256 for i in ids)
+    assert tok.decode(ids) == text
+    assert tok.decode(ids + [300, 4000]) == text  # ids >= 256 have no text
+
+
+def test_http_completions_and_chat():
+    requests = pytest.importorskip("requests")
+    from conftest import free_port
+
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    try:
+        base = f"http://127.0.0.1:{port}"
+        r = requests.post(base + "/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4}, timeout=30)
+        assert r.status_code == 200, r.text
+        j = r.json()
+        assert j["choices"][0]["token_ids"] == expected([5, 6, 7], 4)
+        assert j["usage"] == {"prompt_tokens": 3, "completion_tokens": 4, "total_tokens": 7}
+        # the reference's pp_bench request shape
+        body = {"model": "fake", "messages": [{"role": "user", "content": "hello"}], "max_tokens": 1,
+                "temperature": 0}
+        r = requests.post(base + "/v1/chat/completions", json=body, timeout=30)
+        assert r.status_code == 200, r.text
+        j = r.json()
+        prompt = srv_mod.ByteTokenizer().encode("<|user|>hello<|assistant|>")
+        assert j["usage"]["prompt_tokens"] == len(prompt)
+        assert j["choices"][0]["token_ids"] == expected(prompt, 1)
+        # concurrent requests all complete
+        outs = [None] * 8
+
+        def client(i):
+            outs[i] = requests.post(base + "/v1/completions", json={"prompt": [i + 1] * (i + 1), "max_tokens": i + 1},
+                                    timeout=30).json()["choices"][0]["token_ids"]
+
+        ths = [threading.Thread(target=client, args=(i,)) for i in range(8)]
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        for i in range(8):
+            assert outs[i] == expected([i + 1] * (i + 1), i + 1)
+        assert requests.post(base + "/v1/completions", json={"prompt": [], "max_tokens": 1}, timeout=30).status_code == 400
+        assert requests.post(base + "/v1/completions", json={"prompt": [1] * 4096, "max_tokens": 8},
+                             timeout=30).status_code == 400
+        h = requests.get(base + "/health", timeout=30).json()
+        assert h["status"] == "ok" and h["requests"] == 10
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+    assert not loop.is_alive()
+
+
+def _lockstep(rank, world):
+    import datetime
+
+    import torch.distributed as dist
+
+    ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, ctrl, rank, world)
+    results = {}
+    if rank == 0:
+        def clients():
+            ths = []
+            for i in range(6):
+                def one(i=i):
+                    results[i] = server.submit([i, i + 1], 3 + i % 3, timeout=60)
+                t = threading.Thread(target=one)
+                t.start()
+                ths.append(t)
+            for t in ths:
+                t.join()
+            server.stop()
+
+        threading.Thread(target=clients, daemon=True).start()
+    server.serve_forever()
+    return {"log": sorted(eng.log), "results": results}
+
+
+def test_lockstep_two_ranks():
+    res = run_ranks(_lockstep, 2)
+    assert res[0]["log"] == res[1]["log"] and len(res[0]["log"]) == 6
+    for i, out in res[0]["results"].items():
+        assert out == expected([i, i + 1], 3 + i % 3)
