@@ -323,7 +323,7 @@ class MailboxAR:
         return need <= self._ar.fused_capacity()
 
     def gemm_all_reduce_rmsnorm(self, a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
-                                norm_w: torch.Tensor, eps: float, out: torch.Tensor = None):
+                                norm_w: torch.Tensor, eps: float, out: torch.Tensor = None, push_all: bool = None):
         """Row-parallel GEMM fused with the allreduce: the GEMM epilogue stores
         its partial output tiles straight into the owner ranks' symmetric
         buffers (reduce-scatter overlapped with the remaining tiles), then one
@@ -335,8 +335,10 @@ class MailboxAR:
         if out is None:
             out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
         self._check_error()
+        if push_all is None:
+            push_all = self.fused_push_all(M, N)
         self._ar.gemm_ar_rmsnorm(a, w, residual, norm_w, out, eps, ops.workspace(a.device).err, self.cfg.max_blocks,
-                                 self.fused_push_all(M, N))
+                                 bool(push_all))
         self.counters["fused"] += 1
         launches.add(2)
         return out

@@ -6,8 +6,18 @@ Cases (a few hundred MB on the device at most):
   gemm   : tcgen05 GEMM, 8B gate_up at TP=1 (M=1024, N=28672, K=4096)
   fmha   : tcgen05 prefill attention, 1024 queries at context 4096, 32q/8kv heads
   decode : tensor-core decode attention, batch 64, context 4096, 32q/8kv heads
-Each kernel runs exactly once (plus nothing else from this package), so
-`ncu -k regex:<name> -c 1` captures it.
+  fused  : fused row-parallel GEMM -> allreduce -> residual + RMSNorm (push-all
+           epilogue + sum/norm launch), then the one-shot allreduce+RMSNorm,
+           8B o_proj shape (M=1024, N=4096, K=4096)
+  sp     : sequence-parallel GEMM -> reduce-scatter epilogue, owned-row
+           RMSNorm + all-gather push, all-gather -> GEMM (same shape)
+  elem   : RMSNorm [32768, 4096] and SiLU-mul [8192, 2 x 14336] (inputs > L2)
+The fused and sp cases run the multi-GPU kernels as a one-rank emulation
+(world = 1): the communicator context points at one local buffer laid out
+like the symmetric buffer, so every peer store lands in local memory. They
+show the kernels' tensor-core and memory behaviour; NVLink time is not in
+them. Each kernel runs exactly once (plus nothing else from this package),
+so `ncu -k regex:<name> -c 1` captures it.
 """
 import argparse
 import importlib
@@ -53,6 +63,45 @@ def main():
         kvl = torch.full((B,), L, dtype=torch.int32, device="cuda")
         ops.decode_attention(q, kc, vc, kvl, bt, splits=1)
         torch.cuda.synchronize()
+    if "fused" in which or "sp" in which:
+        C = importlib.import_module(f"{PKG}._ext").cuda_ext()
+        M, N, K = 1024, 4096, 4096
+        half, fuse_half, g_bytes = 16 << 20, 16 << 20, M * N * 2
+        size = C.SIG_BYTES + 2 * half + 2 * fuse_half + g_bytes
+        buf = torch.zeros(size, dtype=torch.uint8, device="cuda")
+        state = torch.zeros(C.STATE_WORDS, dtype=torch.int32, device="cuda")
+        status = C.host_mapped_alloc(4 * C.STATUS_WORDS)
+        ar = C.ArComm(0, 1, [buf.data_ptr()], 0, state.data_ptr(), status.dev, status.host, half, 0,
+                      2_000_000_000, fuse_half, g_bytes)
+        err = ops.workspace("cuda").err
+        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        res = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+        nw = torch.ones(N, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        stream = torch.cuda.current_stream().cuda_stream
+        if "fused" in which:
+            ar.gemm_ar_rmsnorm(a, w, res, nw, out, 1e-5, err, 148, True)
+            part = ops.gemm(a, w)
+            ar.ar_rmsnorm(part.data_ptr(), res.data_ptr(), nw.data_ptr(), out.data_ptr(), M, N, 1e-5, 1, 148, stream)
+            torch.cuda.synchronize()
+        if "sp" in which:
+            res_own = res.clone()
+            ar.gemm_rs(a, w, err)
+            ar.sp_rs_norm_ag(M, res_own, nw, 1e-5, 148)
+            ar.sp_gemm_ag(M, w, out, None, err)
+            torch.cuda.synchronize()
+        assert ar.error() == 0, ar.status()
+        C.host_mapped_free(status.host)
+    if "elem" in which:
+        x = torch.randn(32768, 4096, device="cuda").to(torch.bfloat16)
+        nw = torch.ones(4096, device="cuda", dtype=torch.bfloat16)
+        ops.rmsnorm(x, nw, 1e-5)
+        del x
+        gu = torch.randn(8192, 2 * 14336, device="cuda").to(torch.bfloat16)
+        ops.silu_mul(gu)
+        torch.cuda.synchronize()
+        del gu
     assert ops.gemm_error() == 0
     print("profile_kernels done")
 

@@ -383,42 +383,153 @@ MBX_DEVICE float block_sum(float v, float* red) {
 }
 
 // res/out for one row given the reduced bf16 row `ar` (read through `ld`).
-template <typename LoadAr, typename StoreOut>
-MBX_DEVICE void residual_rmsnorm_row_st(LoadAr ld, uint4* residual_row, const uint4* w_row, StoreOut st, int hvec,
-                                        int H, float eps, float* red) {
-  float ss = 0.f;
-  for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
-    float a[8] = {};
-    unpack_add<__nv_bfloat16>(ld(p), a);
-    // round the AR result to bf16 first (matches AR-then-add unfused order)
-    const uint4 arb = pack_from<__nv_bfloat16>(a);
-    float r[8] = {};
-    unpack_add<__nv_bfloat16>(arb, r);
-    unpack_add<__nv_bfloat16>(residual_row[p], r);
-    const uint4 rb = pack_from<__nv_bfloat16>(r);
-    residual_row[p] = rb;
-    float q[8] = {};
-    unpack_add<__nv_bfloat16>(rb, q);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) ss += q[k] * q[k];
+// Row kernels. Row l of a phase's range belongs to block l % gridDim.x (rows
+// b, b+g, b+2g, ...); every phase that reads rows another rank's block wrote
+// keeps this assignment, so the block-pairwise barriers between phases cover
+// every row. Inside a block, a normalisation phase works on one row with the
+// whole block (decode: few rows, lowest latency) or, when the block owns
+// several rows, on one row per warp (prefill: kRowWarps rows in flight, no
+// block-wide reductions).
+constexpr int kRowWarps = kArThreads / 32;
+
+struct RowCtx {
+  int t0, tstep;  // this thread's first 16-byte vector of the row and its stride
+  bool warp;      // one warp per row (warp reduction) or the whole block
+};
+
+// Rows b, b+g, ... below n owned by this block.
+MBX_DEVICE int block_rows(int n) {
+  return n > (int)blockIdx.x ? (n - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+}
+
+// fn(rc, k) for k in [0, count) (count uniform over the block).
+template <typename Fn>
+MBX_DEVICE void for_norm_rows(int count, Fn fn) {
+  if (count == 1) {
+    fn(RowCtx{(int)threadIdx.x, (int)blockDim.x, false}, 0);
+    return;
   }
-  const float tot = block_sum(ss, red);
-  const float rstd = rsqrtf(tot / (float)H + eps);
-  for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
-    float q[8] = {}, wv[8] = {};
-    unpack_add<__nv_bfloat16>(residual_row[p], q);
-    unpack_add<__nv_bfloat16>(w_row[p], wv);
+  for (int k = threadIdx.x >> 5; k < count; k += kRowWarps) fn(RowCtx{(int)(threadIdx.x & 31), 32, true}, k);
+}
+
+// Copy/reduce phases over the block's rows (row j = b + j*g of a range):
+// out(j, p, sum of the NV source vectors src(j, p, r)) for every vector p <
+// hvec, flattened over the block's threads. Each thread issues the loads of
+// KU vectors before it combines any (the load wrappers are ordered asm), so
+// about 8 loads are in flight per thread.
+template <int NV, typename Src, typename Out>
+MBX_DEVICE void reduce_block_vectors(int rows, int hvec, Src src, Out out) {
+  constexpr int KU = NV >= 8 ? 1 : (NV == 1 ? 4 : 8 / NV);
+  const int total = rows * hvec;
+  for (int i0 = threadIdx.x; i0 < total; i0 += blockDim.x * KU) {
+    uint4 v[KU][NV];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) q[k] = q[k] * rstd * wv[k];
-    st(p, pack_from<__nv_bfloat16>(q));
+    for (int u = 0; u < KU; ++u) {
+      const int i = i0 + u * (int)blockDim.x;
+      if (i < total) {
+        const int j = i / hvec, pv = i - j * hvec;
+#pragma unroll
+        for (int r = 0; r < NV; ++r) v[u][r] = src(j, pv, r);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int i = i0 + u * (int)blockDim.x;
+      if (i < total) {
+        const int j = i / hvec, pv = i - j * hvec;
+        if (NV == 1) {
+          out(j, pv, v[u][0]);
+        } else {
+          float acc[8] = {};
+#pragma unroll
+          for (int r = 0; r < NV; ++r) unpack_add<__nv_bfloat16>(v[u][r], acc);
+          out(j, pv, pack_from<__nv_bfloat16>(acc));
+        }
+      }
+    }
   }
 }
 
-template <typename LoadAr>
-MBX_DEVICE void residual_rmsnorm_row(LoadAr ld, uint4* residual_row, const uint4* w_row, uint4* out_row,
-                                     int hvec, int H, float eps, float* red) {
-  residual_rmsnorm_row_st(ld, residual_row, w_row, [&](int p, const uint4& v) { out_row[p] = v; }, hvec, H, eps,
-                          red);
+// res = bf16(bf16(sum_r src(p, r)) + residual) -> residual (in place);
+// st(p, bf16(res * rsqrt(mean(res^2) + eps) * w)). NV sources per vector,
+// summed in order r = 0..NV-1 in fp32 with one rounding; loads batched as in
+// reduce_block_vectors.
+template <int NV, typename Src, typename StoreOut>
+MBX_DEVICE void residual_rmsnorm_row(const RowCtx& rc, Src src, uint4* residual_row, const uint4* w_row,
+                                     StoreOut st, int hvec, int H, float eps, float* red) {
+  constexpr int KU = NV >= 8 ? 1 : (NV == 1 ? 4 : 8 / NV);
+  float ss = 0.f;
+  for (int p0 = rc.t0; p0 < hvec; p0 += rc.tstep * KU) {
+    uint4 v[KU][NV];
+    uint4 rv[KU];
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int pv = p0 + u * rc.tstep;
+      if (pv < hvec) {
+#pragma unroll
+        for (int r = 0; r < NV; ++r) v[u][r] = ld_cg_v4(src(pv, r));
+        rv[u] = residual_row[pv];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int pv = p0 + u * rc.tstep;
+      if (pv < hvec) {
+        float a[8] = {};
+#pragma unroll
+        for (int r = 0; r < NV; ++r) unpack_add<__nv_bfloat16>(v[u][r], a);
+        // round the AR result to bf16 first (matches AR-then-add unfused order)
+        const uint4 arb = pack_from<__nv_bfloat16>(a);
+        float q[8] = {};
+        unpack_add<__nv_bfloat16>(arb, q);
+        unpack_add<__nv_bfloat16>(rv[u], q);
+        const uint4 rb = pack_from<__nv_bfloat16>(q);
+        residual_row[pv] = rb;
+        float f[8] = {};
+        unpack_add<__nv_bfloat16>(rb, f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += f[k] * f[k];
+      }
+    }
+  }
+  const float tot = rc.warp ? warp_sum(ss) : block_sum(ss, red);
+  const float rstd = rsqrtf(tot / (float)H + eps);
+  constexpr int KU2 = 4;
+  for (int p0 = rc.t0; p0 < hvec; p0 += rc.tstep * KU2) {
+    uint4 rv[KU2], wv[KU2];
+#pragma unroll
+    for (int u = 0; u < KU2; ++u) {
+      const int pv = p0 + u * rc.tstep;
+      if (pv < hvec) {
+        rv[u] = residual_row[pv];
+        wv[u] = w_row[pv];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KU2; ++u) {
+      const int pv = p0 + u * rc.tstep;
+      if (pv < hvec) {
+        float q[8] = {}, ww[8] = {};
+        unpack_add<__nv_bfloat16>(rv[u], q);
+        unpack_add<__nv_bfloat16>(wv[u], ww);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q[k] = q[k] * rstd * ww[k];
+        st(pv, pack_from<__nv_bfloat16>(q));
+      }
+    }
+  }
+}
+
+// Norm rows of a per-owner layout: for every owner o (rows [o*Mo, o*Mo+Mo) of
+// M), this block's rows o*Mo + b + j*g; fn(rc, row).
+template <int NO, typename Fn>
+MBX_DEVICE void for_owner_norm_rows(int M, int Mo, Fn fn) {
+  const int per = block_rows(Mo);
+  for_norm_rows(NO * per, [&](const RowCtx& rc, int k) {
+    const int o = k / per, j = k - (k / per) * per;
+    const int row = o * Mo + (int)blockIdx.x + j * (int)gridDim.x;
+    if (row < min(M, o * Mo + Mo)) fn(rc, row);
+  });
 }
 
 template <int W>
@@ -432,33 +543,24 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_oneshot_kernel(ArCtx c,
   const int hvec = H / 8;
   if (!poisoned(c)) {
     const uint64_t slot = c.half_bytes / W;
-    for (int row = blockIdx.x; row < M; row += gridDim.x) {
-      for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
-        const uint64_t i = (uint64_t)row * hvec + p;
-        const uint4 v = ld_nc_v4(in + i);
+    const int nrows = block_rows(M);
+    const int b = blockIdx.x, g = gridDim.x;
+    reduce_block_vectors<1>(
+        nrows, hvec, [&](int j, int pv, int) { return ld_nc_v4(in + (uint64_t)(b + j * g) * hvec + pv); },
+        [&](int j, int pv, const uint4& v) {
+          const uint64_t i = (uint64_t)(b + j * g) * hvec + pv;
 #pragma unroll
-        for (int j = 0; j < W; ++j) {
-          const int r = (c.rank + j) % W;
-          st_v4(data_half(c.bufs[r], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
-        }
-      }
-    }
+          for (int t = 0; t < W; ++t)
+            st_v4(data_half(c.bufs[(c.rank + t) % W], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
+        });
     if (block_barrier(c, 0, epoch, &s_ok)) {
       const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
-      for (int row = blockIdx.x; row < M; row += gridDim.x) {
-        const uint64_t base = (uint64_t)row * hvec;
-        // Reduce into a bf16 pack directly (fp32 sum, one rounding).
-        auto ld_bf16 = [&](int p) {
-          uint4 v[W];
-#pragma unroll
-          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (base + p) * 16);
-          float acc[8] = {};
-#pragma unroll
-          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
-          return pack_from<__nv_bfloat16>(acc);
-        };
-        residual_rmsnorm_row(ld_bf16, residual + base, w, out + base, hvec, H, eps, red);
-      }
+      for_norm_rows(nrows, [&](const RowCtx& rc, int k) {
+        const uint64_t base = (uint64_t)(b + k * g) * hvec;
+        residual_rmsnorm_row<W>(
+            rc, [&](int pv, int r) { return mine + r * slot + (base + pv) * 16; }, residual + base, w,
+            [&](int pv, const uint4& v) { out[base + pv] = v; }, hvec, H, eps, red);
+      });
     }
   }
   finish_call(c, epoch);
@@ -476,43 +578,35 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_kernel(ArCtx c,
   if (!poisoned(c)) {
     const uint64_t slot1 = c.half_bytes / 2;
     const int rc = (M + W - 1) / W;
+    const int b = blockIdx.x, g = gridDim.x;
     char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
     for (int ch = 0; ch < W; ++ch) {
       const int beg = ch * rc, end = min(M, beg + rc);
-      for (int row = beg + blockIdx.x; row < end; row += gridDim.x)
-        for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
-          const uint64_t i = (uint64_t)row * hvec + p;
-          st_v4(mine + i * 16, ld_nc_v4(in + i));
-        }
+      reduce_block_vectors<1>(
+          block_rows(end - beg), hvec,
+          [&](int j, int pv, int) { return ld_nc_v4(in + (uint64_t)(beg + b + j * g) * hvec + pv); },
+          [&](int j, int pv, const uint4& v) { st_v4(mine + ((uint64_t)(beg + b + j * g) * hvec + pv) * 16, v); });
     }
     if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
     {
       const int beg = c.rank * rc, end = min(M, beg + rc);
-      for (int row = beg + blockIdx.x; row < end; row += gridDim.x)
-        for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
-          const uint64_t i = (uint64_t)row * hvec + p;
-          uint4 v[W];
-#pragma unroll
-          for (int j = 0; j < W; ++j) {
-            const int r = (c.rank + j) % W;
-            v[r] = ld_cg_v4(data_half(c.bufs[r], epoch, c.half_bytes) + i * 16);
-          }
-          float acc[8] = {};
-#pragma unroll
-          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
-          st_v4(mine + slot1 + i * 16, pack_from<__nv_bfloat16>(acc));
-        }
+      reduce_block_vectors<W>(
+          block_rows(end - beg), hvec,
+          [&](int j, int pv, int r) {
+            return ld_cg_v4(data_half(c.bufs[r], epoch, c.half_bytes) + ((uint64_t)(beg + b + j * g) * hvec + pv) * 16);
+          },
+          [&](int j, int pv, const uint4& sum) {
+            st_v4(mine + slot1 + ((uint64_t)(beg + b + j * g) * hvec + pv) * 16, sum);
+          });
     }
     if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
-    for (int ch = 0; ch < W; ++ch) {
-      const int beg = ch * rc, end = min(M, beg + rc);
-      const char* src = data_half(c.bufs[ch], epoch, c.half_bytes) + slot1;
-      for (int row = beg + blockIdx.x; row < end; row += gridDim.x) {
-        const uint64_t base = (uint64_t)row * hvec;
-        auto ld = [&](int p) { return ld_cg_v4(src + (base + p) * 16); };
-        residual_rmsnorm_row(ld, residual + base, w, out + base, hvec, H, eps, red);
-      }
-    }
+    for_owner_norm_rows<W>(M, rc, [&](const RowCtx& rx, int row) {
+      const char* src = data_half(c.bufs[row / rc], epoch, c.half_bytes) + slot1;
+      const uint64_t base = (uint64_t)row * hvec;
+      residual_rmsnorm_row<1>(
+          rx, [&](int pv, int) { return src + (base + pv) * 16; }, residual + base, w,
+          [&](int pv, const uint4& v) { out[base + pv] = v; }, hvec, H, eps, red);
+    });
   }
 done:
   finish_call(c, epoch);
@@ -557,32 +651,23 @@ __global__ void __launch_bounds__(kArThreads) fused_rs_norm_kernel(ArCtx c, int 
       const uint64_t slot = (uint64_t)Mo * N * 2;
       const uint64_t regB = (uint64_t)W * slot;
       const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
-      for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
-        const uint64_t lrow = row - r0;
-        for (int p = threadIdx.x; p < nvec; p += blockDim.x) {
-          uint4 v[W];
+      const int b = blockIdx.x, g = gridDim.x;
+      reduce_block_vectors<W>(
+          block_rows(r1 - r0), nvec,
+          [&](int j, int pv, int r) { return ld_cg_v4(mine + r * slot + ((uint64_t)(b + j * g) * nvec + pv) * 16); },
+          [&](int j, int pv, const uint4& sum) {
+            const uint64_t row = r0 + b + j * g;
 #pragma unroll
-          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (lrow * nvec + p) * 16);
-          float acc[8] = {};
-#pragma unroll
-          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
-          const uint4 sum = pack_from<__nv_bfloat16>(acc);
-#pragma unroll
-          for (int j = 0; j < W; ++j) {
-            char* dst = fuse_half(c, c.bufs[(c.rank + j) % W], epoch) + regB + ((uint64_t)row * nvec + p) * 16;
-            st_v4(dst, sum);
-          }
-        }
-      }
+            for (int t = 0; t < W; ++t)
+              st_v4(fuse_half(c, c.bufs[(c.rank + t) % W], epoch) + regB + (row * nvec + pv) * 16, sum);
+          });
       if (!block_barrier(c, 2, epoch, &s_ok)) goto done;
-      for (int o = 0; o < W; ++o) {
-        const int a0 = o * Mo, a1 = min(M, a0 + Mo);
-        for (int row = a0 + blockIdx.x; row < a1; row += gridDim.x) {
-          const uint64_t base = (uint64_t)row * nvec;
-          auto ld = [&](int p) { return ld_cg_v4(mine + regB + (base + p) * 16); };
-          residual_rmsnorm_row(ld, residual + base, w, out + base, nvec, N, eps, red);
-        }
-      }
+      for_owner_norm_rows<W>(M, Mo, [&](const RowCtx& rc, int row) {
+        const uint64_t base = (uint64_t)row * nvec;
+        residual_rmsnorm_row<1>(
+            rc, [&](int pv, int) { return mine + regB + (base + pv) * 16; }, residual + base, w,
+            [&](int pv, const uint4& v) { out[base + pv] = v; }, nvec, N, eps, red);
+      });
     }
   }
 done:
@@ -617,19 +702,13 @@ __global__ void __launch_bounds__(kArThreads) fused_allsum_norm_kernel(ArCtx c, 
     if (s_ok) {
       const char* mine = fuse_half(c, c.bufs[c.rank], epoch);
       const uint64_t slot = (uint64_t)M * N * 2;
-      for (int row = blockIdx.x; row < M; row += gridDim.x) {
-        const uint64_t base = (uint64_t)row * nvec;
-        auto ld = [&](int p) {
-          uint4 v[W];
-#pragma unroll
-          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (base + p) * 16);
-          float acc[8] = {};
-#pragma unroll
-          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
-          return pack_from<__nv_bfloat16>(acc);
-        };
-        residual_rmsnorm_row(ld, residual + base, w, out + base, nvec, N, eps, red);
-      }
+      const int b = blockIdx.x, g = gridDim.x;
+      for_norm_rows(block_rows(M), [&](const RowCtx& rc, int k) {
+        const uint64_t base = (uint64_t)(b + k * g) * nvec;
+        residual_rmsnorm_row<W>(
+            rc, [&](int pv, int r) { return mine + r * slot + (base + pv) * 16; }, residual + base, w,
+            [&](int pv, const uint4& v) { out[base + pv] = v; }, nvec, N, eps, red);
+      });
     }
   }
   finish_call(c, epoch, kStFuseEpoch, kStFuseDone);
@@ -709,24 +788,20 @@ __global__ void __launch_bounds__(kArThreads) sp_rs_norm_ag_kernel(ArCtx c, int 
       const char* mine = fuse_half(c, c.bufs[c.rank], epoch);
       const uint64_t slot = (uint64_t)Mo * N * 2;
       const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
-      for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
-        const uint64_t lrow = row - r0;
-        auto ld = [&](int p) {
-          uint4 v[W];
+      const int b = blockIdx.x, g = gridDim.x;
+      for_norm_rows(block_rows(r1 - r0), [&](const RowCtx& rc, int k) {
+        const int lrow = b + k * g;
+        const uint64_t row = r0 + lrow;
+        residual_rmsnorm_row<W>(
+            rc, [&](int pv, int r) { return mine + r * slot + ((uint64_t)lrow * nvec + pv) * 16; },
+            res_own + (uint64_t)lrow * nvec, w,
+            [&](int pv, const uint4& v) {
 #pragma unroll
-          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (lrow * nvec + p) * 16);
-          float acc[8] = {};
-#pragma unroll
-          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
-          return pack_from<__nv_bfloat16>(acc);
-        };
-        auto st = [&](int p, const uint4& v) {
-#pragma unroll
-          for (int j = 0; j < W; ++j)
-            st_v4(c.bufs[(c.rank + j) % W] + c.sp_off + ((uint64_t)row * nvec + p) * 16, v);
-        };
-        residual_rmsnorm_row_st(ld, res_own + lrow * nvec, w, st, nvec, N, eps, red);
-      }
+              for (int t = 0; t < W; ++t)
+                st_v4(c.bufs[(c.rank + t) % W] + c.sp_off + (row * nvec + pv) * 16, v);
+            },
+            nvec, N, eps, red);
+      });
     }
   }
   if (ok) grid_done_release(c, kStSpAgDone, epoch, [&](int o) { return ag_flag(c.bufs[o], c.rank); });
@@ -764,47 +839,40 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_push_kernel(ArC
     const uint64_t slot = (uint64_t)Mo * hvec * 16;
     const uint64_t regB = (uint64_t)W * slot;
     char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
-    // A: rows of owner o -> o's region A, slot `rank`; block b takes rows o*Mo + b + k*grid
+    const int b = blockIdx.x, g = gridDim.x;
+    // A: rows of owner o -> o's region A, slot `rank`; block b takes rows o*Mo + b + j*g
 #pragma unroll 1
-    for (int j = 0; j < W; ++j) {
-      const int o = (c.rank + j) % W;
+    for (int t = 0; t < W; ++t) {
+      const int o = (c.rank + t) % W;
       const int a0 = o * Mo, a1 = min(M, a0 + Mo);
       char* dst = data_half(c.bufs[o], epoch, c.half_bytes) + (uint64_t)c.rank * slot;
-      for (int row = a0 + blockIdx.x; row < a1; row += gridDim.x) {
-        const uint64_t lrow = row - a0;
-        for (int p = threadIdx.x; p < hvec; p += blockDim.x)
-          st_v4(dst + (lrow * hvec + p) * 16, ld_nc_v4(in + (uint64_t)row * hvec + p));
-      }
+      reduce_block_vectors<1>(
+          block_rows(a1 - a0), hvec,
+          [&](int j, int pv, int) { return ld_nc_v4(in + (uint64_t)(a0 + b + j * g) * hvec + pv); },
+          [&](int j, int pv, const uint4& v) { st_v4(dst + ((uint64_t)(b + j * g) * hvec + pv) * 16, v); });
     }
     if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
     {
+      // B: sum the own rows (rank order) and push the sums into every rank's region B
       const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
-      for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
-        const uint64_t lrow = row - r0;
-        for (int p = threadIdx.x; p < hvec; p += blockDim.x) {
-          uint4 v[W];
+      reduce_block_vectors<W>(
+          block_rows(r1 - r0), hvec,
+          [&](int j, int pv, int r) { return ld_cg_v4(mine + r * slot + ((uint64_t)(b + j * g) * hvec + pv) * 16); },
+          [&](int j, int pv, const uint4& sum) {
+            const uint64_t row = r0 + b + j * g;
 #pragma unroll
-          for (int r = 0; r < W; ++r) v[r] = ld_cg_v4(mine + r * slot + (lrow * hvec + p) * 16);
-          float acc[8] = {};
-#pragma unroll
-          for (int r = 0; r < W; ++r) unpack_add<__nv_bfloat16>(v[r], acc);
-          const uint4 sum = pack_from<__nv_bfloat16>(acc);
-#pragma unroll
-          for (int j = 0; j < W; ++j)
-            st_v4(data_half(c.bufs[(c.rank + j) % W], epoch, c.half_bytes) + regB + ((uint64_t)row * hvec + p) * 16,
-                  sum);
-        }
-      }
+            for (int t = 0; t < W; ++t)
+              st_v4(data_half(c.bufs[(c.rank + t) % W], epoch, c.half_bytes) + regB + (row * hvec + pv) * 16, sum);
+          });
     }
     if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
-    for (int o = 0; o < W; ++o) {
-      const int a0 = o * Mo, a1 = min(M, a0 + Mo);
-      for (int row = a0 + blockIdx.x; row < a1; row += gridDim.x) {
-        const uint64_t base = (uint64_t)row * hvec;
-        auto ld = [&](int p) { return ld_cg_v4(mine + regB + (base + p) * 16); };
-        residual_rmsnorm_row(ld, residual + base, w, out + base, hvec, H, eps, red);
-      }
-    }
+    // C: residual + norm of every row from the local region B
+    for_owner_norm_rows<W>(M, Mo, [&](const RowCtx& rc, int row) {
+      const uint64_t base = (uint64_t)row * hvec;
+      residual_rmsnorm_row<1>(
+          rc, [&](int pv, int) { return mine + regB + (base + pv) * 16; }, residual + base, w,
+          [&](int pv, const uint4& v) { out[base + pv] = v; }, hvec, H, eps, red);
+    });
   }
 done:
   finish_call(c, epoch);
@@ -1049,6 +1117,16 @@ __global__ void mc_store_raw_kernel(char* mc, const uint4* __restrict__ src, uin
     default: throw std::runtime_error("allreduce: unsupported world size " + std::to_string(W_)); \
   }
 
+// The fused GEMM/norm launches also take world 1: a single-GPU emulation in
+// which every push lands in the rank's own buffer (kernel profiling on one GPU).
+#define MBX_DISPATCH_W1(W_, ...)                                   \
+  if ((W_) == 1) {                                                 \
+    constexpr int W = 1;                                           \
+    __VA_ARGS__;                                                   \
+  } else {                                                         \
+    MBX_DISPATCH_W(W_, __VA_ARGS__)                                \
+  }
+
 #define MBX_DISPATCH_T(D_, ...)                                  \
   switch (D_) {                                                  \
     case kF32: { using T = float; __VA_ARGS__; } break;          \
@@ -1122,13 +1200,13 @@ void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual,
   auto o4 = static_cast<uint4*>(out);
   if (algo == kOneShotPush) {
     if (bytes > ar_chunk_limit(c, kOneShotPush)) throw std::runtime_error("ar_rmsnorm: message exceeds one-shot slot");
-    MBX_DISPATCH_W(W_, ar_rmsnorm_oneshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W1(W_, ar_rmsnorm_oneshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
   } else if (algo == kTwoShotPush) {
     const int Mo = (M + W_ - 1) / W_;
     if ((uint64_t)W_ * Mo * H * 2 + bytes > c.half_bytes)
       throw std::runtime_error("ar_rmsnorm: message exceeds the two-shot buffer");
     const int gp = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
-    MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_push_kernel<W><<<gp, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W1(W_, ar_rmsnorm_twoshot_push_kernel<W><<<gp, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
   } else {
     if (bytes > ar_chunk_limit(c, kTwoShot)) throw std::runtime_error("ar_rmsnorm: message exceeds two-shot slot");
     MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
@@ -1152,7 +1230,7 @@ void fused_rs_norm_launch(const ArCtx& c, int M, int N, int Mo, void* residual, 
                           float eps, int max_blocks, cudaStream_t stream) {
   const int g = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
   const int W_ = c.world;
-  MBX_DISPATCH_W(W_, fused_rs_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
+  MBX_DISPATCH_W1(W_, fused_rs_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
                          c, M, N, Mo, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
                          static_cast<uint4*>(out), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
@@ -1162,7 +1240,7 @@ void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, cons
                               int max_blocks, cudaStream_t stream) {
   const int g = std::max(1, std::min(M, std::min(max_blocks, (int)kMaxBlocks)));
   const int W_ = c.world;
-  MBX_DISPATCH_W(W_, fused_allsum_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
+  MBX_DISPATCH_W1(W_, fused_allsum_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
                          c, M, N, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
                          static_cast<uint4*>(out), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
@@ -1176,7 +1254,7 @@ void sp_rs_push_launch(const ArCtx& c, const void* x, int M, int N, int max_bloc
   if ((uint64_t)W_ * Mo * N * 2 > c.fuse_half_bytes)
     throw std::runtime_error("sp_rs_push: message exceeds the reduce-scatter buffer");
   const int g = ar_grid((uint64_t)M * N / 8, max_blocks);
-  MBX_DISPATCH_W(W_, sp_rs_push_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(x), M, N, Mo));
+  MBX_DISPATCH_W1(W_, sp_rs_push_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(x), M, N, Mo));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -1188,7 +1266,7 @@ void sp_rs_norm_ag_launch(const ArCtx& c, int M, int N, void* res_own, const voi
   const int Mo = (M + W_ - 1) / W_;
   if ((uint64_t)M * N * 2 > c.sp_bytes) throw std::runtime_error("sp_rs_norm_ag: rows exceed the gather buffer");
   const int g = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
-  MBX_DISPATCH_W(W_, sp_rs_norm_ag_kernel<W><<<g, kArThreads, 0, stream>>>(
+  MBX_DISPATCH_W1(W_, sp_rs_norm_ag_kernel<W><<<g, kArThreads, 0, stream>>>(
                          c, M, N, Mo, static_cast<uint4*>(res_own), static_cast<const uint4*>(w), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
 }

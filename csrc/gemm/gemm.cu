@@ -269,6 +269,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = quad * 32 + lane;
     const uint32_t fepoch =
         EPI == kEpiPushRS ? *reinterpret_cast<volatile uint32_t*>(args.ar.state + kStFuseEpoch) + 1u : 0u;
+    // push epilogue: destination bases fixed for the whole launch (push-all:
+    // this rank's slot in every rank's buffer, rank-staggered order)
+    char* dst_all[kMaxRanks];
+    if (EPI == kEpiPushRS) {
+#pragma unroll
+      for (int j = 0; j < kMaxRanks; ++j) {
+        const int r = (args.ar.rank + j) % max(1, args.ar.world);
+        dst_all[j] = (j < args.ar.world && args.push_all)
+                         ? fused_half(args.ar, args.ar.bufs[r], fepoch) + (uint64_t)args.ar.rank * args.M * args.N * 2
+                         : nullptr;
+      }
+    }
     uint32_t t = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
       const int m = u % args.num_m;
@@ -284,6 +296,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tc_fence_after();
       const int grow = m * BM + row_in_tile;
       const bool row_ok = grow < args.M;
+      // push epilogue: the 8 rows this lane flushes (row k*4 + lane/8 of the
+      // warp's 32), as byte offsets from dst_all[] (push-all) or as the
+      // owner's destination row (owner push); nullptr / ~0 = past M
+      char* prow[8];
+      uint64_t prow_off[8];
+      if (EPI == kEpiPushRS) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int grow2 = m * BM + quad * 32 + k * 4 + (lane >> 3);
+          prow[k] = nullptr;
+          prow_off[k] = ~0ull;
+          if (grow2 < args.M) {
+            if (args.push_all) {
+              prow_off[k] = (uint64_t)grow2 * args.N * 2;
+            } else {
+              const int owner = grow2 / args.Mo;
+              const int lrow = grow2 - owner * args.Mo;
+              prow[k] = fused_half(args.ar, args.ar.bufs[owner], fepoch) +
+                        (uint64_t)(args.ar.rank * args.Mo + lrow) * args.N * 2;
+            }
+          }
+        }
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -311,28 +346,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (half64 == 1 || c0 + 32 >= BN) {
             __syncwarp();
-            const int col0 = n * BN + (c0 & ~63);  // first column of the staged 64
             const int unit = lane & 7;
+            const int col = n * BN + (c0 & ~63) + unit * 8;  // this lane's 8 columns of the staged 64
+            const bool col_ok = col < args.N && (half64 == 1 || unit < 4);
+            const uint64_t col_b = (uint64_t)col * 2;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int srow = k * 4 + (lane >> 3);
-              const int grow2 = m * BM + quad * 32 + srow;
-              const int col = col0 + unit * 8;
-              if (grow2 < args.M && col < args.N && (half64 == 1 || unit < 4)) {
+              if (!col_ok) continue;
+              if (args.push_all) {
+                if (prow_off[k] == ~0ull) continue;
                 const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
-                if (args.push_all) {
-                  const uint64_t off = ((uint64_t)args.ar.rank * args.M + grow2) * args.N + col;
-                  for (int j = 0; j < args.ar.world; ++j) {
-                    const int dst_rank = (args.ar.rank + j) % args.ar.world;
-                    *reinterpret_cast<uint4*>(fused_half(args.ar, args.ar.bufs[dst_rank], fepoch) + off * 2) = v;
-                  }
-                } else {
-                  const int owner = grow2 / args.Mo;
-                  const int lrow = grow2 - owner * args.Mo;
-                  char* dst = fused_half(args.ar, args.ar.bufs[owner], fepoch) +
-                              ((uint64_t)(args.ar.rank * args.Mo + lrow) * args.N + col) * 2;
-                  *reinterpret_cast<uint4*>(dst) = v;
-                }
+                const uint64_t off = prow_off[k] + col_b;
+#pragma unroll
+                for (int j = 0; j < kMaxRanks; ++j)
+                  if (dst_all[j] != nullptr) *reinterpret_cast<uint4*>(dst_all[j] + off) = v;
+              } else {
+                if (prow[k] == nullptr) continue;
+                const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
+                *reinterpret_cast<uint4*>(prow[k] + col_b) = v;
               }
             }
             __syncwarp();

@@ -146,7 +146,9 @@ def main():
         res = torch.randn(M, N, device=dev, generator=gs).to(torch.bfloat16)
         nw = (1 + 0.1 * torch.randn(N, device=dev, generator=gs)).to(torch.bfloat16)
         r = res.clone()
-        out = ar.gemm_all_reduce_rmsnorm(a, wt, r, nw, 1e-5)
+        # alternate the two epilogue forms (push every row to every rank / to its owner)
+        pa = bool((it // 4) % 2) and world * M * N * 2 <= ar._ar.fused_capacity()
+        out = ar.gemm_all_reduce_rmsnorm(a, wt, r, nw, 1e-5, push_all=pa)
         plain = ar.custom_all_reduce(torch.full((4096,), float(rank), dtype=torch.bfloat16, device=dev))
         # reference: bf16 partials summed in fp32 in rank order (the kernel's order)
         part = (a.float() @ wt.float().t()).to(torch.bfloat16)
