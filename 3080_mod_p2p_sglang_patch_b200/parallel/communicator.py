@@ -33,7 +33,7 @@ import torch.distributed as dist
 from .._ext import cpu_ext, cuda_ext
 from ..config import CommConfig
 from ..utils import launches
-from . import bootstrap
+from . import bootstrap, faults
 
 logger = logging.getLogger(__name__)
 
@@ -102,6 +102,7 @@ class MailboxAR:
         attempt = -1
         for attempt in range(2):
             err = None
+            faults.set_attempt(attempt)
             try:
                 if device.type == "cuda":
                     self._setup_gpu()
@@ -154,6 +155,7 @@ class MailboxAR:
         err = None
         if self.rank == 0:
             try:
+                faults.check("cpu_open", self.rank)
                 self._cpu = ext.CpuMailbox(path, self.rank, self.world_size, self.cfg.cpu_slot_bytes, True,
                                            self.cfg.cpu_timeout_ms)
             except Exception as e:  # noqa: BLE001
@@ -162,6 +164,7 @@ class MailboxAR:
             raise RuntimeError(f"CPU mailbox creation failed ({err})")
         if self.rank != 0:
             try:
+                faults.check("cpu_open", self.rank)
                 self._cpu = ext.CpuMailbox(path, self.rank, self.world_size, self.cfg.cpu_slot_bytes, False,
                                            self.cfg.cpu_timeout_ms)
             except Exception as e:  # noqa: BLE001
@@ -459,6 +462,27 @@ class MailboxAR:
             if self.sp is not None:
                 self.sp.reset()
         self._seg_seq = 0
+        bootstrap.agree(True, self.group)
+
+    def debug_set_epoch(self, epoch: int):
+        """Collective, tests only: put every rank at allreduce epoch ``epoch``
+        with every barrier flag at the same value (the state after that many
+        calls), e.g. just below 2^32 to run the bounded waits across the wrap."""
+        if self.disabled:
+            return
+        bootstrap.agree(True, self.group)
+        e = int(epoch) & 0xFFFFFFFF
+        if self._cpu is not None:
+            self._cpu.set_epoch(e)
+        else:
+            from .symm import _raw_uint8
+
+            C = cuda_ext()
+            signed = e - (1 << 32) if e >= (1 << 31) else e
+            torch.cuda.synchronize(self.device)
+            _raw_uint8(self._buf.local_ptr, 4 * C.BAR_WORDS, self.device).view(torch.int32).fill_(signed)
+            self._state[0] = signed
+            torch.cuda.synchronize(self.device)
         bootstrap.agree(True, self.group)
 
     def check_health(self) -> bool:

@@ -20,7 +20,7 @@ import torch
 import torch.distributed as dist
 
 from .._ext import cuda_ext
-from . import bootstrap
+from . import bootstrap, faults
 
 logger = logging.getLogger(__name__)
 
@@ -92,6 +92,7 @@ class SymmetricBuffer:
         err = None
         mine = None
         try:
+            faults.check("symm_create", self.rank)
             mine = C.symm_create(self.dev, self.size)
             self._ids.append(mine.id)
         except Exception as e:  # noqa: BLE001
@@ -109,6 +110,7 @@ class SymmetricBuffer:
         self._mem_id = mine.id
         err = None
         try:
+            faults.check("symm_import", self.rank)
             for p, fd in sorted(fds.items()):
                 try:
                     a = C.symm_import(self.dev, fd, self.size)
@@ -148,6 +150,7 @@ class SymmetricBuffer:
         rfd = bootstrap.broadcast_fd(session, self.rank, self.world, fd, 0, self.group, timeout_ms, "mc")
         try:
             if self.rank != 0:
+                faults.check("mc_import", self.rank)
                 self._mc_id = C.mc_import(rfd, self.size)
             C.mc_add_device(self._mc_id, self.dev)
         except Exception as e:  # noqa: BLE001
@@ -182,6 +185,7 @@ class SymmetricBuffer:
         ptrs[self.rank] = self._ipc_tensor.data_ptr()
         err = None
         try:
+            faults.check("ipc_open", self.rank)
             for p in range(self.world):
                 if p != self.rank:
                     ptrs[p] = C.ipc_open(handles[p])

@@ -21,6 +21,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           },
           py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("dtype"))
       .def("reset", &mbx::CpuMailbox::reset)
+      .def("set_epoch", &mbx::CpuMailbox::set_epoch)
       .def("close", &mbx::CpuMailbox::close)
       .def("epoch", &mbx::CpuMailbox::epoch)
       .def("error", &mbx::CpuMailbox::error)

@@ -170,6 +170,11 @@ int CpuMailbox::allreduce(const void* in, void* out, size_t nbytes, int dtype) {
   return 0;
 }
 
+void CpuMailbox::set_epoch(uint32_t e) {
+  epoch_ = e;
+  for (int src = 0; src < world_; ++src) flag(rank_, src)->store(e, std::memory_order_release);
+}
+
 void CpuMailbox::reset() {
   epoch_ = 0;
   err_ = 0;

@@ -14,6 +14,10 @@ class CpuMailbox {
   // Returns 0, or a sticky error code (3 = timed out waiting for a peer's flag).
   int allreduce(const void* in, void* out, size_t nbytes, int dtype);
   void reset();
+  // Test support: put this rank at epoch `e` with every inbound flag at `e`
+  // (a consistent state, as if e calls had completed; used to run across the
+  // 2^32 wrap). Every rank must call it before the next allreduce.
+  void set_epoch(uint32_t e);
   void close();
   uint32_t epoch() const { return epoch_; }
   int error() const { return err_; }

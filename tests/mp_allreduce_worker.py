@@ -118,6 +118,18 @@ def main():
         assert bad == 0, f"hammer {algo} mismatches {bad}"
     log("hammer-per-algo OK")
 
+    # 4c. epoch wrap: start 40 calls below 2^32 and run every algorithm across it
+    ar.debug_set_epoch((1 << 32) - 40)
+    for it in range(80):
+        algo = algos[it % len(algos)]
+        v = (it % 251) + 1.0
+        t = torch.full(((1 << 20) // 2,), v, dtype=torch.bfloat16, device=dev)
+        out = ar.custom_all_reduce(t, algo=algo)
+        assert bool(torch.all(out.float() == world * v)), f"epoch wrap it={it} algo={algo}"
+    torch.cuda.synchronize()
+    assert ar.epoch() == 40, ar.epoch()  # one launch per 1 MB call: wrapped past 2^32
+    log("epoch-wrap OK")
+
     # 5. fused allreduce + residual + RMSNorm vs unfused
     ops_ref = importlib.import_module("3080_mod_p2p_sglang_patch_b200.ops.reference")
     for M, H in ((1, 4096), (64, 4096), (1024, 4096), (7, 8192)):
@@ -291,6 +303,25 @@ def main():
     assert ar.err() == 0, ar.status()
     log(f"engine sequence-parallel OK (min cosine {cos:.5f})")
     tp.close()
+
+    # 9. host-side fault injection in the GPU handshakes: one rank's local
+    #    failure gives every rank the same outcome, and the result is usable
+    for spec, want in (("symm_import@1", "ipc"), ("mc_import@1", "no-nvls")):
+        os.environ["MBX_INJECT_FAULT"] = spec
+        a2 = comm_mod.MailboxAR(None, dev, config=cfg)
+        os.environ.pop("MBX_INJECT_FAULT")
+        assert not a2.disabled, spec
+        if want == "ipc":
+            assert a2.transport.startswith("ipc"), (spec, a2.transport)
+        else:
+            assert "nvls" not in a2.transport, (spec, a2.transport)
+        tg = [None] * world
+        dist.all_gather_object(tg, a2.transport)
+        assert len(set(tg)) == 1, tg
+        t = torch.full((4096,), float(rank + 1), dtype=torch.bfloat16, device=dev)
+        assert torch.all(a2.custom_all_reduce(t).float() == sum(range(1, world + 1))), spec
+        a2.close()
+    log("fault-injection OK")
 
     dist.barrier()
     ar.close()

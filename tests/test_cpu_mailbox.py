@@ -103,3 +103,27 @@ def _gating(rank, world):
 def test_gating_matches_reference_rules():
     res = run_ranks(_gating, 2)
     assert res[0] == [True, False, False, False, False, True]
+
+
+def _wrap(rank, world):
+    import importlib
+
+    comm_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.parallel.communicator")
+    ar = comm_mod.MailboxAR(None, "cpu")
+    ar.debug_set_epoch((1 << 32) - 20)
+    bad = 0
+    for it in range(60):
+        v = float(it % 251 + 1)
+        out = ar.custom_all_reduce(torch.full((8192,), v * (rank + 1)))
+        bad += int(not bool(torch.all(out == v * sum(range(1, world + 1)))))
+    ep = ar.epoch()
+    ar.close()
+    return bad, ep
+
+
+def test_epoch_wraps_past_2_pow_32():
+    """60 rounds starting 20 below 2^32: the wrap-safe epoch compare keeps
+    every wait correct across the wrap (a plain >= would pass stale flags)."""
+    res = run_ranks(_wrap, 2)
+    for r in (0, 1):
+        assert res[r] == (0, 40), res

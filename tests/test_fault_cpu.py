@@ -53,3 +53,36 @@ def _bad_world(rank, world):
 def test_world_size_one_is_disabled():
     res = run_ranks(_bad_world, 2)
     assert res[0] is True
+
+
+def _inject(rank, world, spec):
+    import os
+    from importlib import import_module
+
+    os.environ["MBX_INJECT_FAULT"] = spec
+    comm_mod = import_module("3080_mod_p2p_sglang_patch_b200.parallel.communicator")
+    ar = comm_mod.MailboxAR(None, "cpu")
+    os.environ.pop("MBX_INJECT_FAULT")
+    x = torch.full((4096,), float(rank + 1))
+    out = ar.all_reduce(x)  # in-house when up, gloo fallback otherwise
+    res = (ar.disabled, getattr(ar, "_attempt", None), bool(torch.all(out == sum(range(1, world + 1)))))
+    ar.close()
+    return res
+
+
+def test_one_rank_open_failure_retries_on_every_rank():
+    """Rank 1 fails to map the mailbox at attempt 0 only: every rank retries
+    and comes up at attempt 1 (the consensus makes rank 0 drop its good
+    mapping too)."""
+    res = run_ranks(_inject, 2, args=("cpu_open@1#0",))
+    for r in (0, 1):
+        assert res[r] == (False, 1, True), res
+
+
+def test_persistent_failure_falls_back_to_nccl_on_every_rank():
+    """Rank 2 of 3 can never map the mailbox: all three ranks disable the
+    communicator (no hang, no split decision) and the allreduce still works
+    through the process-group fallback."""
+    res = run_ranks(_inject, 3, args=("cpu_open@2",))
+    for r in (0, 1, 2):
+        assert res[r][0] is True and res[r][2] is True, res
