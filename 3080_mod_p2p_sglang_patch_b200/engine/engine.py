@@ -15,6 +15,7 @@ import time
 import torch
 
 from .. import ops
+from ..utils import nvtx
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
 from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
 from .kv_cache import PAGE, PagedKVCache
@@ -25,7 +26,7 @@ class LLMEngine:
     def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
-                 sp: bool = None):
+                 sp: bool = None, weights=None):
         self.cfg = cfg
         self.tp = tp
         self.tp_size = tp.world_size if tp is not None else 1
@@ -34,7 +35,9 @@ class LLMEngine:
         self.max_batch = max_batch
         self.max_seq = max_seq
         self.chunk = chunk
-        self.weights = LlamaWeights(cfg, self.tp_rank, self.tp_size, self.device, seed=seed, full_init=full_init)
+        # random-init weights unless a checkpoint's shards are given (models.load_llama)
+        self.weights = weights if weights is not None else LlamaWeights(cfg, self.tp_rank, self.tp_size, self.device,
+                                                                        seed=seed, full_init=full_init)
         self.model = LlamaTP(cfg, self.weights, tp=tp, impl=impl)
         # sequence parallel for prefill batches (TP > 1, native build);
         # None = follow MBX_SP (default off)
@@ -62,6 +65,17 @@ class LLMEngine:
             self.graphs = DecodeGraphRunner(self, sizes)
         if prefill_graph:
             self.prefill_graph = PrefillGraphRunner(self, chunk)
+
+    @classmethod
+    def from_pretrained(cls, model_dir: str, tp=None, device=None, **kw):
+        """Engine over a Hugging Face Llama checkpoint directory (this rank's
+        shards only are read; see models/loader.py)."""
+        from ..models.loader import load_llama
+
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        cfg, w = load_llama(model_dir, tp.rank if tp is not None else 0, tp.world_size if tp is not None else 1, dev)
+        kw.setdefault("max_seq", min(cfg.max_pos, 8192))
+        return cls(cfg, tp=tp, device=dev, weights=w, **kw)
 
     # ------------------------------------------------------------------ setup
     def _reserve_scratch(self):
@@ -196,6 +210,10 @@ class LLMEngine:
         batch = self.sched.next_batch()
         if batch is None:
             return None
+        with nvtx.rng(f"{batch.kind} tokens={batch.num_tokens}"):
+            return self._step(batch)
+
+    def _step(self, batch):
         if batch.kind == "prefill":
             nxt = self._run_prefill(batch).tolist()
             now = time.perf_counter()

@@ -20,6 +20,9 @@ class LlamaConfig:
     eps: float = 1e-5
     max_pos: int = 16384
     init_std: float = 0.02
+    # RoPE frequency scaling as (key, value) pairs, e.g. Llama 3.1's
+    # (("rope_type", "llama3"), ("factor", 8.0), ...); empty = plain RoPE
+    rope_scaling: tuple = ()
 
     @classmethod
     def llama_8b(cls):

@@ -20,6 +20,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
+from ..utils import nvtx
 from .config import LlamaConfig
 
 
@@ -90,6 +91,48 @@ class LlamaWeights:
         self.nq, self.nkv = nq, nkv
 
 
+def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch):
+    """A LlamaWeights whose shards come from ``fetch(name, rows=None, cols=None)``
+    (full-tensor names as in Hugging Face Llama checkpoints, [out, in] layout;
+    ``rows`` / ``cols`` = (start, stop) slices), converted to bf16 on ``device``."""
+    cfg.check_tp(tp_size)
+    t, r = tp_size, tp_rank
+    H, D, F_ = cfg.hidden, cfg.head_dim, cfg.ffn
+    dev = torch.device(device)
+
+    def get(name, rows=None, cols=None):
+        return fetch(name, rows, cols).to(device=dev, dtype=torch.bfloat16).contiguous()
+
+    def rows_of(name, full_rows):
+        per = full_rows // t
+        return get(name, rows=(r * per, (r + 1) * per))
+
+    def cols_of(name, full_cols):
+        per = full_cols // t
+        return get(name, cols=(r * per, (r + 1) * per))
+
+    w = LlamaWeights.__new__(LlamaWeights)
+    w.cfg = cfg
+    w.embed = rows_of("model.embed_tokens.weight", cfg.vocab)
+    w.layers = []
+    for i in range(cfg.layers):
+        p = f"model.layers.{i}."
+        L = {"ln1": get(p + "input_layernorm.weight"), "ln2": get(p + "post_attention_layernorm.weight")}
+        L["qkv"] = torch.cat([rows_of(p + "self_attn.q_proj.weight", cfg.heads * D),
+                              rows_of(p + "self_attn.k_proj.weight", cfg.kv_heads * D),
+                              rows_of(p + "self_attn.v_proj.weight", cfg.kv_heads * D)], 0).contiguous()
+        L["o"] = cols_of(p + "self_attn.o_proj.weight", cfg.heads * D)
+        L["gate_up"] = torch.cat([rows_of(p + "mlp.gate_proj.weight", F_),
+                                  rows_of(p + "mlp.up_proj.weight", F_)], 0).contiguous()
+        L["down"] = cols_of(p + "mlp.down_proj.weight", F_)
+        w.layers.append(L)
+    w.norm = get("model.norm.weight")
+    w.lm_head = rows_of("lm_head.weight", cfg.vocab)
+    w.vocab_start = r * (cfg.vocab // t)
+    w.nq, w.nkv = cfg.heads // t, cfg.kv_heads // t
+    return w
+
+
 class LlamaTP:
     """Forward passes of one TP rank over a paged KV cache.
 
@@ -103,7 +146,8 @@ class LlamaTP:
         self.tp_size = tp.world_size if tp is not None else 1
         self.impl = impl
         self.device = weights.embed.device
-        self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, self.device)
+        self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, self.device,
+                                        dict(cfg.rope_scaling) if cfg.rope_scaling else None)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         # sequence parallel (parallel/sp.py): used for batches of at least
         # ``sp_min_rows`` tokens that fit its buffers; None = off
@@ -186,6 +230,8 @@ class LlamaTP:
         residual = h
         x = ops.rmsnorm(residual, w.layers[0]["ln1"], cfg.eps)
         for li, L in enumerate(w.layers):
+            if nvtx.ENABLED:
+                torch.cuda.nvtx.range_push(f"layer {li}")
             qkv = self._linear(x, L["qkv"])
             kc, vc = kv_caches[li]
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
@@ -211,6 +257,8 @@ class LlamaTP:
             else:
                 part = self._linear(a, L["down"])
                 x = self._ar_norm(part, residual, nxt)
+            if nvtx.ENABLED:
+                torch.cuda.nvtx.range_pop()
         x_last = x.index_select(0, last_idx)
         if return_hidden:
             return x_last

@@ -112,9 +112,23 @@ def fused_add_rmsnorm(x, residual, w, eps, out=None):
     return out
 
 
-def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
-    """[max_pos, head_dim] fp32 table: cos in the first half, sin in the second."""
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device, scaling=None) -> torch.Tensor:
+    """[max_pos, head_dim] fp32 table: cos in the first half, sin in the second.
+
+    ``scaling`` (dict) with ``rope_type == "llama3"`` applies Llama 3.1's
+    frequency rescaling: wavelengths above original_max_position /
+    low_freq_factor are divided by ``factor``, those below original /
+    high_freq_factor are kept, and the band between is interpolated linearly
+    in original / wavelength."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    if scaling and scaling.get("rope_type", scaling.get("type")) == "llama3":
+        factor = float(scaling["factor"])
+        lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+        orig = float(scaling.get("original_max_position_embeddings", 8192))
+        wavelen = 2 * math.pi / inv
+        smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        inv = torch.where(wavelen > orig / lo, inv / factor,
+                          torch.where(wavelen < orig / hi, inv, (1 - smooth) * inv / factor + smooth * inv))
     ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
     return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
 

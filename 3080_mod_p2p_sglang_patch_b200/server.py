@@ -13,10 +13,13 @@ adds them in the same order and runs one engine step (the TP collectives of
 that step then line up across ranks). With ``SGLANG_MAILBOX_AR=1`` the TP
 allreduces go through MailboxAR, otherwise NCCL.
 
-Weights are random (no checkpoints offline), so text goes through a byte
-tokenizer: UTF-8 bytes are token ids 0..255, generated ids >= 256 decode to
-nothing. Token-id prompts (``"prompt": [ids]``) are accepted as well.
-Greedy decoding only (``temperature`` is ignored).
+``--model-path DIR`` serves a Hugging Face Llama checkpoint (safetensors,
+each rank reads its shards) with the directory's tokenizer (through
+transformers, local files only) and its chat template. Without it the
+weights are random and text goes through a byte tokenizer: UTF-8 bytes are
+token ids 0..255, generated ids >= 256 decode to nothing. Token-id prompts
+(``"prompt": [ids]``) are accepted either way. Greedy decoding only
+(``temperature`` is ignored).
 """
 import argparse
 import datetime
@@ -37,6 +40,26 @@ class ByteTokenizer:
 
     def decode(self, ids) -> str:
         return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
+
+
+class HFTokenizer:
+    """A checkpoint directory's tokenizer (transformers, local files only)."""
+
+    def __init__(self, path: str):
+        from transformers import AutoTokenizer
+
+        self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+
+    def encode(self, text: str) -> list:
+        return self.tok.encode(text, add_special_tokens=True)
+
+    def decode(self, ids) -> str:
+        return self.tok.decode(ids, skip_special_tokens=True)
+
+    def chat(self, messages) -> list:
+        if getattr(self.tok, "chat_template", None):
+            return list(self.tok.apply_chat_template(messages, add_generation_prompt=True, tokenize=True))
+        return self.encode("".join(f"{m.get('role', 'user')}: {m.get('content', '')}\n" for m in messages))
 
 
 class _Pending:
@@ -214,8 +237,11 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     @app.post("/v1/chat/completions")
     async def chat(body: dict):
         msgs = body.get("messages") or []
-        text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
-        prompt = tok.encode(text)
+        if hasattr(tok, "chat"):
+            prompt = tok.chat(msgs)
+        else:
+            text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
+            prompt = tok.encode(text)
         max_tokens = int(body.get("max_tokens", 16))
         out = await run_in_threadpool(_run, prompt, max_tokens)
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
@@ -250,7 +276,8 @@ def main(argv=None):
     import torch.distributed as dist
 
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--model", default="8b", help="8b | 70b | tiny")
+    ap.add_argument("--model", default="8b", help="8b | 70b | tiny (random weights)")
+    ap.add_argument("--model-path", default=None, help="Hugging Face Llama checkpoint directory (safetensors)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8001)
     ap.add_argument("--max-batch", type=int, default=64)
@@ -269,10 +296,19 @@ def main(argv=None):
     # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow
     tp = par.TPGroup(None, dev, use_mailbox=None) if world > 1 else None
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
-    cfg = models.LlamaConfig.by_name(args.model)
-    eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=args.max_batch, max_seq=args.max_seq, chunk=args.chunk, seed=0,
-                            use_graphs=not args.no_graphs, impl=args.impl,
-                            prefill_graph=(args.impl == "native" and not args.no_graphs))
+    opts = dict(max_batch=args.max_batch, max_seq=args.max_seq, chunk=args.chunk, use_graphs=not args.no_graphs,
+                impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs))
+    tokenizer = None
+    if args.model_path:
+        eng = eng_mod.LLMEngine.from_pretrained(args.model_path, tp=tp, device=dev, **opts)
+        cfg = eng.cfg
+        try:
+            tokenizer = HFTokenizer(args.model_path)
+        except Exception as e:  # noqa: BLE001 - token-id prompts still work
+            logger.warning("no tokenizer in %s (%s); using the byte tokenizer", args.model_path, e)
+    else:
+        cfg = models.LlamaConfig.by_name(args.model)
+        eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, **opts)
     server = EngineServer(eng, ctrl, rank, world, max_prompt=args.max_seq)
     http = None
     if rank == 0:
@@ -281,7 +317,7 @@ def main(argv=None):
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step
         for sig in (signal.SIGINT, signal.SIGTERM):
             signal.signal(sig, lambda *_: server.stop())
-        http, _ = start_http(build_app(server, cfg.name), args.host, args.port)
+        http, _ = start_http(build_app(server, cfg.name, tokenizer), args.host, args.port)
         logger.info("serving %s at http://%s:%d (TP=%d, allreduce=%s)", cfg.name, args.host, args.port, world,
                     "MailboxAR" if (tp is not None and tp.ca_comm is not None) else "NCCL")
     try:

@@ -176,3 +176,82 @@ def test_http_server_matches_generate():
     finally:
         http.should_exit = True
     assert got == want
+
+
+def _engine_last_hidden(eng, prompt, chunk):
+    """Last token's final hidden state, prefilled chunk by chunk."""
+    ops = sub("ops")
+    req = eng.add_request(prompt, 1)
+    eng.sched._admit()
+    eng._sync_block_row(req)
+    slots = eng.kv.slots(req.blocks, 0, len(prompt))
+    dev = eng.device
+    hid = None
+    for s in range(0, len(prompt), chunk):
+        n = min(chunk, len(prompt) - s)
+        ids = torch.tensor(prompt[s:s + n], dtype=torch.int32, device=dev)
+        pos = torch.arange(s, s + n, dtype=torch.int32, device=dev)
+        sl = torch.tensor(slots[s:s + n], dtype=torch.int64, device=dev)
+        cu = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        kvl = torch.tensor([s + n], dtype=torch.int32, device=dev)
+        bt = eng.block_table[req.slot:req.slot + 1]
+        tiles = ops.prefill_tiles([n]).to(dev)
+        last = torch.tensor([n - 1], dtype=torch.int64, device=dev)
+        attn = lambda li, q, kc, vc: ops.prefill_attention(q, kc, vc, cu, kvl, bt, tiles, eng.model.scale)  # noqa
+        hid = eng.model.forward(ids, pos, sl, eng.kv.caches, attn, last, return_hidden=True)
+    return hid[0].float()
+
+
+def test_hf_checkpoint_engine_matches_reference(tmp_path):
+    """A Hugging Face-layout safetensors checkpoint (separate q/k/v and
+    gate/up projections, Llama 3.1 RoPE scaling, tied embeddings) loaded with
+    LLMEngine.from_pretrained gives the same last hidden state as an fp32
+    forward written directly over the checkpoint's tensors."""
+    import json
+
+    models, eng_mod, ops, ref = sub("models"), sub("engine"), sub("ops"), sub("ops.reference")
+    H, D, nq, nkv, Fd, V, NL = 512, 128, 8, 2, 1024, 4096, 2
+    scaling = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+               "original_max_position_embeddings": 64}
+    cfg_json = {"hidden_size": H, "num_hidden_layers": NL, "num_attention_heads": nq, "num_key_value_heads": nkv,
+                "head_dim": D, "intermediate_size": Fd, "vocab_size": V, "rope_theta": 500000.0,
+                "rms_norm_eps": 1e-5, "max_position_embeddings": 1024, "rope_scaling": scaling,
+                "tie_word_embeddings": True}
+    g = torch.Generator().manual_seed(1)
+    rnd = lambda *s: (torch.randn(*s, generator=g) * 0.05).to(torch.bfloat16)  # noqa: E731
+    one = lambda n: (1 + 0.1 * torch.randn(n, generator=g)).to(torch.bfloat16)  # noqa: E731
+    t = {"model.embed_tokens.weight": rnd(V, H) * 20, "model.norm.weight": one(H)}
+    for i in range(NL):
+        p = f"model.layers.{i}."
+        t.update({p + "input_layernorm.weight": one(H), p + "post_attention_layernorm.weight": one(H),
+                  p + "self_attn.q_proj.weight": rnd(nq * D, H), p + "self_attn.k_proj.weight": rnd(nkv * D, H),
+                  p + "self_attn.v_proj.weight": rnd(nkv * D, H), p + "self_attn.o_proj.weight": rnd(H, nq * D),
+                  p + "mlp.gate_proj.weight": rnd(Fd, H), p + "mlp.up_proj.weight": rnd(Fd, H),
+                  p + "mlp.down_proj.weight": rnd(H, Fd)})
+    models.write_safetensors(str(tmp_path / "model.safetensors"), t)
+    (tmp_path / "config.json").write_text(json.dumps(cfg_json))
+    eng = eng_mod.LLMEngine.from_pretrained(str(tmp_path), max_batch=2, max_seq=512, chunk=64, use_graphs=False)
+    prompt = torch.randint(0, V, (150,), generator=torch.Generator().manual_seed(2)).tolist()
+    got = _engine_last_hidden(eng, prompt, 64)
+
+    c = {k: v.cuda().float() for k, v in t.items()}
+    T = len(prompt)
+    cs = ops.rope_cos_sin(1024, D, 500000.0, "cuda", scaling)
+    pos = torch.arange(T, device="cuda", dtype=torch.int32)
+    res = c["model.embed_tokens.weight"][torch.tensor(prompt, device="cuda")]
+    for i in range(NL):
+        p = f"model.layers.{i}."
+        x = ref.rmsnorm(res, c[p + "input_layernorm.weight"], 1e-5)
+        q = (x @ c[p + "self_attn.q_proj.weight"].t()).view(T, nq, D)
+        k = (x @ c[p + "self_attn.k_proj.weight"].t()).view(T, nkv, D)
+        v = (x @ c[p + "self_attn.v_proj.weight"].t()).view(T, nkv, D)
+        q, k = ref.rope(q, pos, cs), ref.rope(k, pos, cs)
+        o = ref.attention(q, k, v, causal_offset=0).reshape(T, nq * D)
+        res = res + o @ c[p + "self_attn.o_proj.weight"].t()
+        x = ref.rmsnorm(res, c[p + "post_attention_layernorm.weight"], 1e-5)
+        a = F.silu(x @ c[p + "mlp.gate_proj.weight"].t()) * (x @ c[p + "mlp.up_proj.weight"].t())
+        res = res + a @ c[p + "mlp.down_proj.weight"].t()
+    want = ref.rmsnorm(res, c["model.norm.weight"], 1e-5)[-1]
+    assert F.cosine_similarity(got, want, dim=0).item() > 0.995
+    logits_want = want @ c["model.embed_tokens.weight"].t()  # tied LM head
+    assert (got @ c["model.embed_tokens.weight"].t()).argmax().item() in logits_want.topk(5).indices.tolist()
