@@ -16,6 +16,12 @@ both ways, as in an allreduce):
 
 CUDA events over --iters back-to-back launches, max over ranks; prints one
 JSON line per (kind, grid) with GB/s of payload per rank.
+
+--overlap (the reference's tests/gate8_ce_bench.py): the tcgen05 GEMM of
+its down_proj shape ([1024, 17408] x [17408, 5120]) alone, a peer push of
+the GEMM's output size alone (copy engine, or 16 CTAs of SM stores), the two
+serially, and the push on a side stream concurrent with the GEMM; reports
+the GEMM slowdown and the time the overlap saves.
 """
 import argparse
 import datetime
@@ -41,6 +47,7 @@ def main():
     ap.add_argument("--threads", type=int, default=512)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--kinds", default="sm_push1,sm_push4,sm_pull4,ce_push,nvls_reduce,nvls_reduce_noacc,nvls_store")
+    ap.add_argument("--overlap", action="store_true", help="GEMM / peer push overlap microbench only")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -70,6 +77,13 @@ def main():
             d, s_ = dst.data_ptr(), buf.mc_ptr + rank * S
         return lambda: C.raw_transport(k, d, s_, S, grid, args.threads, stream)
 
+    if args.overlap:
+        overlap(args, C, buf, rank, nxt, dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        buf.close()
+        dist.destroy_process_group()
+        return
     grids = [int(g) for g in args.grids.split(",")]
     for kind in args.kinds.split(","):
         if kind.startswith("nvls") and not buf.mc_ptr:
@@ -98,6 +112,60 @@ def main():
     dist.barrier()
     buf.close()
     dist.destroy_process_group()
+
+
+def overlap(args, C, buf, rank, nxt, dev):
+    ops = importlib.import_module(f"{PKG}.ops")
+    M, K, N = 1024, 17408, 5120
+    a = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    prev = torch.randn(M, N, device=dev).to(torch.bfloat16)  # the tile pushed while the next GEMM runs
+    nbytes = prev.numel() * 2
+    dst = buf.ptrs[nxt] + rank * nbytes
+    assert 2 * nbytes <= buf.size, "buffer too small"
+    side = torch.cuda.Stream(device=dev)
+    main = torch.cuda.current_stream(dev)
+
+    def gemm():
+        ops.gemm(a, w, out=y)
+
+    def push(kind, stream):
+        if kind == "ce":
+            C.ce_push(dst, prev.data_ptr(), nbytes, stream.cuda_stream)
+        else:
+            C.raw_transport(KINDS["sm_push4"], dst, prev.data_ptr(), nbytes, 16, 512, stream.cuda_stream)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(main)
+        for _ in range(args.iters):
+            fn()
+        e1.record(main)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.iters * 1e3], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def concurrent(kind):
+        side.wait_stream(main)
+        push(kind, side)
+        gemm()
+        main.wait_stream(side)
+
+    g = timed(gemm)
+    for kind in ("ce", "sm16"):
+        p_ = timed(lambda: push(kind, main))
+        serial = timed(lambda: (gemm(), push(kind, main)))
+        conc = timed(lambda: concurrent(kind))
+        if rank == 0:
+            print(json.dumps({"bench": "overlap", "push": kind, "tp": dist.get_world_size(), "gemm_us": g,
+                              "push_us": p_, "push_bytes": nbytes, "serial_us": serial, "concurrent_us": conc,
+                              "gemm_slowdown": conc / g, "overlap_saved_us": serial - conc}), flush=True)
 
 
 if __name__ == "__main__":
