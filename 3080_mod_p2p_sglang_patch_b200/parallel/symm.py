@@ -47,6 +47,8 @@ class SymmetricBuffer:
         self.dev = device.index if device.index is not None else torch.cuda.current_device()
         self.mc_ptr = 0
         self._mc_id = 0
+        self._mc_joined = False  # every rank's device was added to the multicast object
+        self._mc_bound = False  # this rank's buffer is bound to the multicast object
         self._ids = []
         self._ipc_ptrs = []
         self._ipc_tensor = None
@@ -84,7 +86,7 @@ class SymmetricBuffer:
                 self._setup_nvls(session, timeout_ms)
             except Exception as e:  # noqa: BLE001
                 logger.warning("[MailboxAR] NVLS multicast setup failed (%s); continuing without it", e)
-                self.mc_ptr = 0
+                self._release_mc()
 
     # ------------------------------------------------------------------ VMM
     def _setup_vmm(self, session, timeout_ms):
@@ -161,8 +163,10 @@ class SymmetricBuffer:
         # every device must be added before any memory is bound
         if not bootstrap.agree(err is None, self.group):
             raise RuntimeError(f"cuMulticastAddDevice failed ({err})")
+        self._mc_joined = True
         try:
             C.mc_bind(self._mc_id, self._mem_id, self.size)
+            self._mc_bound = True
         except Exception as e:  # noqa: BLE001
             err = e
         if not bootstrap.agree(err is None, self.group):
@@ -203,21 +207,31 @@ class SymmetricBuffer:
         _raw_uint8(self.local_ptr, nbytes, self.device).zero_()
         torch.cuda.synchronize(self.device)
 
-    def close(self):
+    def _release_mc(self):
+        """Drop this rank's multicast mapping, binding and handle, whatever
+        stage the setup reached (unbinding is only valid after a bind)."""
         C = self.C
-        if self.mc_ptr or self._mc_id:
+        if self._mc_bound:
             try:
                 C.mc_unbind(self._mc_id, self.dev, self.size)
             except Exception:  # noqa: BLE001
                 pass
-        self._free_vmm()
-        if self._mc_id:
+            self._mc_bound = False
+        if self._mc_id and self._mc_joined:
             try:
-                C.symm_free(self._mc_id)
+                C.symm_free(self._mc_id)  # unmaps the multicast range if mapped, releases the handle
             except Exception:  # noqa: BLE001
                 pass
-            self._mc_id = 0
+        # an object whose device set never completed is left to process exit
+        # (no driver call on a half-built multicast object)
+        self._mc_id = 0
+        self._mc_joined = False
         self.mc_ptr = 0
+
+    def close(self):
+        C = self.C
+        self._release_mc()
+        self._free_vmm()
         for p in self._ipc_ptrs:
             try:
                 C.ipc_close(p)
