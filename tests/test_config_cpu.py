@@ -1,0 +1,61 @@
+"""Flags and configuration: the reference's SGLANG_MAILBOX_AR switch and
+sglang hook (sglang/README.md:14-31), env overrides, the per-world NCCL
+fallback size, and the fault-injection rule parser."""
+import importlib
+
+cfg_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.config")
+integ = importlib.import_module("3080_mod_p2p_sglang_patch_b200.parallel.sglang_integration")
+faults = importlib.import_module("3080_mod_p2p_sglang_patch_b200.parallel.faults")
+
+
+def test_sglang_flag_selects_the_communicator(monkeypatch):
+    monkeypatch.delenv("SGLANG_MAILBOX_AR", raising=False)
+    assert integ.dispatch_custom_allreduce("nccl-default") == "nccl-default"
+    for v in ("1", "true", "on"):
+        monkeypatch.setenv("SGLANG_MAILBOX_AR", v)
+        assert integ.dispatch_custom_allreduce() is integ.MailboxAR
+    monkeypatch.setenv("SGLANG_MAILBOX_AR", "0")
+    assert integ.dispatch_custom_allreduce() is None
+
+
+def test_env_overrides(monkeypatch):
+    monkeypatch.setenv("MBX_MAX_SIZE", str(8 << 20))
+    monkeypatch.setenv("MBX_TIMEOUT_MS", "250")
+    monkeypatch.setenv("MBX_NVLS", "0")
+    monkeypatch.setenv("SGLANG_MAILBOX_AR_VERBOSE", "1")
+    c = cfg_mod.CommConfig.from_env()
+    assert c.max_size_for(8) == 8 << 20 and c.timeout_ns == 250_000_000 and c.nvls is False and c.verbose
+    monkeypatch.delenv("MBX_NVLS")
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")  # NVLS off for NCCL means off here too
+    assert cfg_mod.CommConfig.from_env().nvls is False
+
+
+def test_per_world_fallback_size(monkeypatch):
+    for k in ("MBX_MAX_SIZE", "NCCL_NVLS_ENABLE"):
+        monkeypatch.delenv(k, raising=False)
+    c = cfg_mod.CommConfig.from_env()
+    MiB = 1 << 20
+    assert c.max_size_for(2) == 48 * MiB and c.max_size_for(4) == 64 * MiB and c.max_size_for(8) == 96 * MiB
+    # the reference's own limit is smaller: everything it handled in-house stays in-house here
+    assert all(c.max_size_for(w) >= cfg_mod.REFERENCE_MAX_SIZE for w in range(2, 9))
+
+
+def test_fault_rules(monkeypatch):
+    monkeypatch.setenv("MBX_INJECT_FAULT", "cpu_open@1#0, symm_import@0")
+    faults.set_attempt(0)
+    faults.check("cpu_open", 0)  # other rank: no fault
+    try:
+        faults.check("cpu_open", 1)
+        raise AssertionError("expected an injected fault")
+    except faults.InjectedFault:
+        pass
+    faults.set_attempt(1)
+    faults.check("cpu_open", 1)  # only attempt 0
+    try:
+        faults.check("symm_import", 0)  # every attempt
+        raise AssertionError("expected an injected fault")
+    except faults.InjectedFault:
+        pass
+    monkeypatch.delenv("MBX_INJECT_FAULT")
+    faults.check("symm_import", 0)
+    faults.set_attempt(0)

@@ -1,0 +1,105 @@
+"""Chunked-prefill scheduler, block allocator and KV slot mapping on CPU.
+
+The policy under test is sglang's default, which the reference relies on
+for its chunk-1024/2048 prefill measurements (docs/performance.md:29-49):
+prefill chunks first, in arrival order, a chunk may span the tail of one
+prompt and the head of the next; otherwise every running request decodes.
+"""
+import importlib
+
+import pytest
+
+sched_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine.scheduler")
+kv_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine.kv_cache")
+PAGE = kv_mod.PAGE
+
+
+def _req(rid, n, max_new):
+    return sched_mod.Request(rid=rid, prompt=list(range(n)), max_new=max_new)
+
+
+def _drive(s, tok=7):
+    """Run the scheduler to completion with a constant next token; returns
+    the batch sequence as (kind, [(rid, start, n)] or [rids])."""
+    trace = []
+    while s.has_work():
+        b = s.next_batch()
+        if b.kind == "prefill":
+            trace.append(("prefill", [(p.req.rid, p.start, p.n) for p in b.pieces]))
+            s.after_prefill(b, [tok] * len(b.pieces))
+        else:
+            trace.append(("decode", [r.rid for r in b.reqs]))
+            s.after_decode(b, [tok] * len(b.reqs))
+    return trace
+
+
+def test_chunks_span_prompts_in_arrival_order():
+    s = sched_mod.Scheduler(chunk=100, max_batch=8)
+    for rid, n in enumerate((150, 30, 70)):
+        s.add(_req(rid, n, 2))
+    trace = _drive(s)
+    assert trace[0] == ("prefill", [(0, 0, 100)])
+    assert trace[1] == ("prefill", [(0, 100, 50), (1, 0, 30), (2, 0, 20)])
+    assert trace[2] == ("prefill", [(2, 20, 50)])
+    # every prompt done: one decode step for all three (max_new=2: 1 token from prefill + 1 decode)
+    assert trace[3] == ("decode", [0, 1, 2])
+    assert len(trace) == 4
+    assert [len(r.output) for r in sorted(s.finished, key=lambda r: r.rid)] == [2, 2, 2]
+
+
+def test_prefill_has_priority_over_decode():
+    s = sched_mod.Scheduler(chunk=64, max_batch=8)
+    s.add(_req(0, 10, 5))
+    b = s.next_batch()
+    s.after_prefill(b, [1])
+    assert s.next_batch().kind == "decode"
+    s.add(_req(1, 100, 2))  # arrives while request 0 decodes
+    b = s.next_batch()
+    assert b.kind == "prefill" and b.pieces[0].req.rid == 1 and b.pieces[0].n == 64
+
+
+def test_admission_limited_by_batch_slots_and_kv_blocks():
+    alloc = kv_mod.BlockAllocator(num_blocks=1 + 10)  # block 0 reserved
+    s = sched_mod.Scheduler(chunk=1000, max_batch=2, allocator=alloc)
+    for rid in range(3):
+        s.add(_req(rid, 40, 8))  # 48 tokens -> 3 blocks each
+    b = s.next_batch()
+    assert [p.req.rid for p in b.pieces] == [0, 1]  # only 2 batch slots
+    assert alloc.free == 10 - 6
+    s.after_prefill(b, [1, 1])
+    trace = _drive(s)
+    assert any(k == "prefill" and pieces[0][0] == 2 for k, pieces in trace)  # admitted once a slot freed
+    assert alloc.free == 10 and len(s.finished) == 3
+    # blocks never overlap between requests alive at the same time, and block 0 is never handed out
+    alloc2 = kv_mod.BlockAllocator(num_blocks=9)
+    got = [alloc2.alloc(4), alloc2.alloc(4)]
+    assert 0 not in got[0] + got[1] and len(set(got[0] + got[1])) == 8
+    with pytest.raises(MemoryError):
+        alloc2.alloc(1)
+
+
+def test_kv_memory_admission_waits_instead_of_failing():
+    alloc = kv_mod.BlockAllocator(num_blocks=1 + 4)
+    s = sched_mod.Scheduler(chunk=1000, max_batch=8, allocator=alloc)
+    s.add(_req(0, 50, 14))  # 64 tokens = 4 blocks: the whole cache
+    s.add(_req(1, 10, 2))
+    b = s.next_batch()
+    assert [p.req.rid for p in b.pieces] == [0]
+    s.after_prefill(b, [1])
+    assert s.next_batch().kind == "decode"  # request 1 waits for blocks
+    _drive(s)
+    assert sorted(r.rid for r in s.finished) == [0, 1] and alloc.free == 4
+
+
+def test_request_longer_than_max_seq_is_rejected():
+    s = sched_mod.Scheduler(chunk=64, max_batch=2, max_seq=100)
+    with pytest.raises(ValueError):
+        s.add(_req(0, 90, 20))
+
+
+def test_slots_map_positions_to_pages():
+    blocks = [5, 9, 2]
+    slots = kv_mod.PagedKVCache.slots(None, blocks, 14, 5)
+    assert slots == [5 * PAGE + 14, 5 * PAGE + 15, 9 * PAGE + 0, 9 * PAGE + 1, 9 * PAGE + 2]
+    assert kv_mod.PagedKVCache.blocks_for(33) == 3
+    assert kv_mod.PagedKVCache.bytes_per_token(32, 8, 128) == 32 * 2 * 8 * 128 * 2
