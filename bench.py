@@ -29,7 +29,7 @@ sys.path.insert(0, ROOT)
 PKG = "3080_mod_p2p_sglang_patch_b200"
 
 # published reference prefill number at chunk 1024 (2x RTX 3080, Qwen3.8-27B
-# AWQ, TP=2, 40K prompt): docs/performance.md:43 -> BASELINE.md
+# AWQ, TP=2, 40K prompt): reference docs/performance.md:43
 BASELINE_PREFILL_TOKS = 1464.0
 
 REFERENCE_UNAVAILABLE = (
