@@ -19,6 +19,7 @@
 // error word, drains its own in-flight TMA/MMA, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include <algorithm>
@@ -579,6 +580,207 @@ int num_sms() {
   return n;
 }
 
+// ==========================================================================
+// CTA-pair GEMM (cta_group::2): a cluster of two CTAs computes one 256 x BN
+// tile. CTA r stages rows [256m + 128r, +128) of A and rows [BN n + BN/2 r,
+// +BN/2) of B in its own shared memory; the leader (r = 0) issues M=256
+// tcgen05.mma over both CTAs' tiles, so each SM streams half of B per k-step
+// instead of all of it (the per-SM operand traffic drops from 48 KB to 32 KB
+// per 64-deep k-block at BN = 256). Accumulator rows land in each CTA's own
+// TMEM; each CTA's epilogue stores its 128 rows. Plain / residual epilogues.
+// Barriers: full[s] lives in the leader (both CTAs' loads count on it; the
+// leader expects both CTAs' bytes), empty[s] and tfull[acc] in both CTAs (the
+// MMA commit arrives on both), tempty[acc] in the leader (both CTAs'
+// epilogue warps arrive). Every wait is bounded; the only unbounded waits are
+// the two cluster barriers, at the start and at the end, which every thread
+// of both CTAs reaches on every path.
+// ==========================================================================
+template <int BN, int STAGES>
+struct Smem2 {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = (BN / 2) * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kTotal = kBarOff + 256 + 1024;
+};
+
+template <int BN, int STAGES, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         GemmArgs args) {
+  using L = Smem2<BN, STAGES>;
+  static_assert(BN % 32 == 0 && BN <= 256, "pair tile width");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;   // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint64_t* mma_done = tempty + 2;    // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m2 = (args.M + 2 * BM - 1) / (2 * BM);
+  const int units = num_m2 * args.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull[a], 1);
+      tc::mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    tc::mbar_init(mma_done, 1);
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tmem_slot, Tmem<BN>::kCols);
+    tc::tmem_relinquish_pair();
+  }
+  tc::tc_fence_before();
+  __syncwarp();
+  tc::cluster_sync();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (tc::elect_one()) {
+      tc::tma_prefetch_desc(&tmA);
+      tc::tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      for (int u = pair; u < units && !*abort; u += npairs) {
+        const int m = u % num_m2;
+        const int n = u / num_m2;
+        for (int kb = 0; kb < args.kb_total; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(&empty[s], ph ^ 1, abort, args.timeout_ns)) {
+            set_err(args.err, 5, abort);
+            break;
+          }
+          uint8_t* sa = smem + s * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+          tc::tma_load_2d_pair(sa, &tmA, &full[s], kb * BK, m * 2 * BM + (int)rank * BM);
+          tc::tma_load_2d_pair(sb, &tmB, &full[s], kb * BK, n * BN + (int)rank * (BN / 2));
+        }
+      }
+      if (rank == 0) {
+        // Drain: the last (up to STAGES) stages' loads of both CTAs have landed
+        // (the leader's full barriers count both) before the final cluster
+        // barrier lets either CTA exit.
+        const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
+        for (uint32_t j = first; j < it; ++j) {
+          volatile int never = 0;
+          tc::mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &never, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (rank == 0 && tc::elect_one()) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(2 * BM, BN);
+      uint32_t it = 0, t = 0;
+      for (int u = pair; u < units && !*abort; u += npairs, ++t) {
+        const int acc = t & 1;
+        const uint32_t aph = (t >> 1) & 1;
+        if (!tc::mbar_wait(&tempty[acc], aph ^ 1, abort, args.timeout_ns)) {
+          set_err(args.err, 6, abort);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d = tmem_base + acc * Tmem<BN>::kAccStride;
+        bool ok = true;
+        for (int kb = 0; kb < args.kb_total; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!tc::mbar_wait(&full[s], ph, abort, args.timeout_ns)) {
+            set_err(args.err, 6, abort);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = tc::smem_u32(smem + s * L::kStageBytes);
+          const uint64_t da = tc::sw128_kmajor_desc(sa);
+          const uint64_t db = tc::sw128_kmajor_desc(sa + L::kABytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) tc::mma_bf16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc::mma_commit_pair(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        tc::mma_commit_pair(&tfull[acc], 0x3);
+      }
+      // every issued MMA completes before the pair's TMEM is released
+      tc::mma_commit_pair(mma_done, 0x1);
+      volatile int never = 0;
+      tc::mbar_wait(mma_done, 0, &never, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    uint32_t t = 0;
+    for (int u = pair; u < units; u += npairs, ++t) {
+      const int m = u % num_m2;
+      const int n = u / num_m2;
+      const int acc = t & 1;
+      const uint32_t aph = (t >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[acc], aph, abort, args.timeout_ns)) {
+        if (lane == 0) set_err(args.err, 7, abort);
+        break;
+      }
+      tc::tc_fence_after();
+      const int grow = m * 2 * BM + (int)rank * BM + quad * 32 + lane;
+      const bool row_ok = grow < args.M;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * Tmem<BN>::kAccStride + c0, r);
+        tc::tmem_ld_wait();
+        const int gcol = n * BN + c0;
+        const int valid = min(32, args.N - gcol);
+        if (row_ok && valid > 0) {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.out) + (int64_t)grow * args.ldc + gcol;
+          const __nv_bfloat16* res =
+              EPI == kEpiBf16AddResidual ? args.residual + (int64_t)grow * args.ldc + gcol : nullptr;
+          store_row_bf16(dst, r, valid, res);
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) tc::mbar_arrive(&tempty[acc]);
+        else tc::mbar_arrive_remote(&tempty[acc], 0);
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncwarp();
+  tc::cluster_sync();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc_pair(tmem_base, Tmem<BN>::kCols);
+}
+
+template <int BN, int STAGES, int EPI>
+void launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
+  using L = Smem2<BN, STAGES>;
+  auto kern = gemm2_tcgen05_kernel<BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    MBX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, a);
+}
+
 template <int BN, int STAGES, int EPI>
 void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
   using L = Smem<BN, STAGES, EPI == kEpiPushRS>;
@@ -730,6 +932,15 @@ void gemm_rs_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, i
   launch_push_gemm(c, A, lda, B, ldb, M, N, K, Mo, false, err, s);
 }
 
+// CTA-pair GEMM for large M: MBX_GEMM_2CTA=1 turns it on (default off).
+static bool pair_gemm_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MBX_GEMM_2CTA");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,
                  uint32_t* err, cudaStream_t s, const GemmAgWait* ag) {
@@ -796,6 +1007,22 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
       splitk_reduce_kernel<<<(int)std::max<int64_t>(1, blocks), threads, 0, s>>>(
           workspace, (int)sp, MN, (int)N, (__nv_bfloat16*)C, ldc, a.residual);
     }
+    MBX_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
+  if (ag == nullptr && bn <= 0 && splits <= 0 && pair_gemm_enabled() && M >= 2 * BM && N % 8 == 0) {
+    // CTA-pair tiles (256 x 256): same grid of SMs, half of B per SM per k-step
+    GemmArgs pa = a;
+    pa.splits = 1;
+    pa.kb_per_split = pa.kb_total;
+    pa.num_n = (int)((N + 255) / 256);
+    pa.out = C;
+    const CUtensorMap ta2 = make_map(A, M, K, lda, BM);
+    const CUtensorMap tb2 = make_map(B, N, K, ldb, 128);
+    const int units2 = (int)((M + 2 * BM - 1) / (2 * BM)) * pa.num_n;
+    const int grid2 = 2 * std::min(units2, sms / 2);
+    if (residual) launch_pair_cfg<256, 6, kEpiBf16AddResidual>(ta2, tb2, pa, grid2, s);
+    else launch_pair_cfg<256, 6, kEpiBf16>(ta2, tb2, pa, grid2, s);
     MBX_CUDA_CHECK(cudaGetLastError());
     return;
   }

@@ -79,3 +79,41 @@ def test_gemm_strided_views():
     out = ops.gemm(a, w)
     ref = a.float() @ w.float().t()
     assert (out.float() - ref).abs().max().item() < 2e-2 * ref.abs().max().item() + 1e-2
+
+
+_PAIR_SCRIPT = r"""
+import importlib, torch
+ops = importlib.import_module("3080_mod_p2p_sglang_patch_b200.ops")
+ref = importlib.import_module("3080_mod_p2p_sglang_patch_b200.ops.reference")
+torch.manual_seed(0)
+worst = 0.0
+for (M, N, K, res) in [(256, 4096, 4096, False), (1024, 3072, 512, True), (589, 1000, 2048, False),
+                       (2048, 6144, 4096, True), (1024, 28672, 1024, False), (300, 256, 64, True)]:
+    a = (torch.randn(M, K, device="cuda") / 8).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") / 8).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda").to(torch.bfloat16) if res else None
+    got = ops.gemm(a, w, residual=r).float()
+    want = a.float() @ w.float().t()
+    if res:
+        want = want.to(torch.bfloat16).float() + r.float()
+    err = ((got - want).abs() / (want.abs() + 1.0)).max().item()
+    worst = max(worst, err)
+    assert err < 2e-2, (M, N, K, res, err)
+assert ops.gemm_error() == 0
+print("PAIR-OK", worst)
+"""
+
+
+def test_cta_pair_gemm_matches_reference():
+    """The CTA-pair (cta_group::2) GEMM, selected with MBX_GEMM_2CTA=1 (read
+    once per process, so it runs in a child), against the fp32 reference on
+    ragged and multi-wave shapes, plain and residual epilogues."""
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, MBX_GEMM_2CTA="1")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    p = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT], env=env, cwd=root, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0 and "PAIR-OK" in p.stdout, p.stdout[-2000:] + p.stderr[-4000:]
