@@ -932,13 +932,38 @@ void gemm_rs_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, i
   launch_push_gemm(c, A, lda, B, ldb, M, N, K, Mo, false, err, s);
 }
 
-// CTA-pair GEMM for large M: MBX_GEMM_2CTA=1 turns it on (default off).
-static bool pair_gemm_enabled() {
-  static const bool on = [] {
+// CTA-pair GEMM selection: MBX_GEMM_2CTA=0 never, =1 whenever M >= 256,
+// unset: when its wave cost is lower. A 256x256 pair tile occupies two SMs
+// and, per SM, costs 0.85 of a 128x256 single-CTA tile (measured on the 8B
+// shapes: down_proj K=14336 98.3 -> 80.7 us, o_proj K=4096 36.9 -> 32.8 us);
+// its coarser tiles lose where they fill the pairs worse than the single-CTA
+// plan fills the SMs (qkv N=6144: 53.2 vs 51.2 us). This rule picks the
+// faster kernel on all eight measured 8B TP=1/2 shapes.
+static int pair_gemm_mode() {
+  static const int mode = [] {
     const char* v = std::getenv("MBX_GEMM_2CTA");
-    return v != nullptr && v[0] == '1';
+    if (v == nullptr || v[0] == '\0') return -1;
+    return v[0] == '1' ? 1 : 0;
   }();
-  return on;
+  return mode;
+}
+
+static bool use_pair_gemm(int64_t M, int64_t N, const GemmPlan& p, int sms) {
+  const int mode = pair_gemm_mode();
+  if (mode == 0 || M < 2 * BM || p.splits > 1) return false;
+  if (mode == 1) return true;
+  static const int kBN[] = {256, 224, 192, 160, 128};
+  static const double kCost[] = {1.00, 1.00, 1.02, 1.10, 1.25};
+  double c1 = 0.0;
+  for (int i = 0; i < 5; ++i)
+    if (kBN[i] == p.bn) c1 = kCost[i];
+  if (c1 == 0.0) return false;
+  const int64_t tiles1 = ((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn);
+  const double t1 = (double)((tiles1 + sms - 1) / sms) * p.bn * c1;
+  const int64_t pairs = ((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+  const int64_t slots = std::max(1, sms / 2);
+  const double t2 = (double)((pairs + slots - 1) / slots) * 256 * 0.85;
+  return t2 < t1;
 }
 
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
@@ -1010,7 +1035,7 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
     MBX_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  if (ag == nullptr && bn <= 0 && splits <= 0 && pair_gemm_enabled() && M >= 2 * BM && N % 8 == 0) {
+  if (ag == nullptr && bn <= 0 && splits <= 0 && N % 8 == 0 && use_pair_gemm(M, N, p, sms)) {
     // CTA-pair tiles (256 x 256): same grid of SMs, half of B per SM per k-step
     GemmArgs pa = a;
     pa.splits = 1;
