@@ -5,6 +5,7 @@ contiguous 4 KB page per (block, kv head), the unit the attention kernels
 stream. Block 0 is reserved as a scratch page for padded decode rows.
 (The reference relies on sglang's paged cache; it ships none.)
 """
+import numpy as np
 import torch
 
 PAGE = 16
@@ -47,7 +48,7 @@ class PagedKVCache:
 
     def slots(self, blocks, start: int, n: int):
         """Cache slots (block*PAGE + offset) of token positions [start, start+n)."""
-        out = []
-        for p in range(start, start + n):
-            out.append(blocks[p // PAGE] * PAGE + p % PAGE)
-        return out
+        if n <= 0:
+            return []
+        pos = np.arange(start, start + n, dtype=np.int64)
+        return (np.asarray(blocks, dtype=np.int64)[pos // PAGE] * PAGE + pos % PAGE).tolist()
