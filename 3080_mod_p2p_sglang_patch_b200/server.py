@@ -24,6 +24,7 @@ token ids 0..255, generated ids >= 256 decode to nothing. Token-id prompts
 import argparse
 import datetime
 import itertools
+import json
 import logging
 import queue
 import threading
@@ -63,14 +64,24 @@ class HFTokenizer:
 
 
 class _Pending:
-    __slots__ = ("prompt", "max_new", "event", "output", "error")
+    __slots__ = ("prompt", "max_new", "event", "output", "error", "stream", "req", "sent")
 
-    def __init__(self, prompt, max_new):
+    def __init__(self, prompt, max_new, stream=False):
         self.prompt = prompt
         self.max_new = max_new
         self.event = threading.Event()
         self.output = None
         self.error = None
+        # streaming: new token ids are put here as they are generated, then None
+        self.stream = queue.Queue() if stream else None
+        self.req = None  # the engine request (rank 0)
+        self.sent = 0    # tokens already streamed
+
+    def finish(self, output=None, error=None):
+        self.output, self.error = output, error
+        if self.stream is not None:
+            self.stream.put(None)
+        self.event.set()
 
 
 class EngineServer:
@@ -99,20 +110,42 @@ class EngineServer:
     def submit(self, prompt: list, max_new: int, timeout: float = None) -> list:
         """Called from HTTP threads on rank 0: blocks until the request is done
         and returns the generated token ids."""
-        if self._stopped.is_set():
-            raise RuntimeError("server stopped")
-        if not prompt:
-            raise ValueError("empty prompt")
-        if self.max_prompt is not None and len(prompt) + max_new > self.max_prompt:
-            raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
-                             f"max sequence {self.max_prompt}")
-        p = _Pending(list(prompt), int(max_new))
-        self.q.put(p)
+        p = self._enqueue(prompt, max_new, stream=False)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if p.error is not None:
             raise RuntimeError(p.error)
         return p.output
+
+    def submit_stream(self, prompt: list, max_new: int, timeout: float = None):
+        """Like ``submit`` but yields lists of new token ids as the engine
+        produces them (rank 0, from an HTTP thread)."""
+        p = self._enqueue(prompt, max_new, stream=True)
+        while True:
+            try:
+                item = p.stream.get(timeout=timeout)
+            except queue.Empty:
+                raise TimeoutError("request timed out") from None
+            if item is None:
+                break
+            yield item
+        if p.error is not None:
+            raise RuntimeError(p.error)
+
+    def _enqueue_check(self, prompt, max_new):
+        if not prompt:
+            raise ValueError("empty prompt")
+        if self.max_prompt is not None and len(prompt) + max_new > self.max_prompt:
+            raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
+                             f"max sequence {self.max_prompt}")
+
+    def _enqueue(self, prompt, max_new, stream):
+        if self._stopped.is_set():
+            raise RuntimeError("server stopped")
+        self._enqueue_check(prompt, max_new)
+        p = _Pending(list(prompt), int(max_new), stream=stream)
+        self.q.put(p)
+        return p
 
     def stop(self):
         """Ask every rank's loop to exit after the current step (rank 0)."""
@@ -152,6 +185,7 @@ class EngineServer:
                         stop = True
                         continue
                     req = eng.add_request(c.prompt, c.max_new)
+                    c.req = req
                     self._by_rid[req.rid] = c
                     self.stats["requests"] += 1
                     self.stats["prompt_tokens"] += len(c.prompt)
@@ -160,39 +194,41 @@ class EngineServer:
                 if eng.sched.has_work():
                     eng.step()
                     self.stats["steps"] += 1
+                if self.rank == 0:
+                    for p in self._by_rid.values():  # stream tokens as they appear
+                        if p.stream is not None and p.req is not None and len(p.req.output) > p.sent:
+                            p.stream.put(list(p.req.output[p.sent:]))
+                            p.sent = len(p.req.output)
                 done, eng.sched.finished = eng.sched.finished, []
                 for r in done:
                     p = self._by_rid.pop(r.rid, None)
                     if p is not None:
-                        p.output = list(r.output)
                         self.stats["completion_tokens"] += len(r.output)
-                        p.event.set()
+                        p.finish(output=list(r.output))
         except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
             for p in self._by_rid.values():
-                p.error = repr(e)
-                p.event.set()
+                p.finish(error=repr(e))
             raise
         finally:
             self._stopped.set()
             for p in self._by_rid.values():
                 if not p.event.is_set():
-                    p.error = "server stopped"
-                    p.event.set()
+                    p.finish(error="server stopped")
             while True:
                 try:
                     c = self.q.get_nowait()
                 except queue.Empty:
                     break
                 if c != self.SHUTDOWN:
-                    c.error = "server stopped"
-                    c.event.set()
+                    c.finish(error="server stopped")
 
 
 def build_app(server: EngineServer, model_name: str, tokenizer=None):
     """FastAPI app with /health, /v1/models, /v1/completions and
     /v1/chat/completions (non-streaming, greedy)."""
     from fastapi import FastAPI, HTTPException
-    from fastapi.concurrency import run_in_threadpool
+    from fastapi.concurrency import iterate_in_threadpool, run_in_threadpool
+    from fastapi.responses import StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
     app = FastAPI()
@@ -216,6 +252,28 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     def _usage(prompt, out):
         return {"prompt_tokens": len(prompt), "completion_tokens": len(out), "total_tokens": len(prompt) + len(out)}
 
+    def _check(prompt, max_tokens):
+        try:
+            server._enqueue_check(prompt, max_tokens)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+
+    def _sse(prompt, max_tokens, chunk_of):
+        """Server-sent events: one chunk per engine step's new tokens, a last
+        chunk with finish_reason and usage, then [DONE]."""
+        def gen():
+            out = []
+            try:
+                for toks in server.submit_stream(prompt, max_tokens):
+                    out += toks
+                    yield "data: " + json.dumps(chunk_of(toks, None, None)) + "\n\n"
+                yield "data: " + json.dumps(chunk_of([], "length", _usage(prompt, out))) + "\n\n"
+            except (RuntimeError, TimeoutError) as e:
+                yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(iterate_in_threadpool(gen()), media_type="text/event-stream")
+
     @app.get("/health")
     def health():
         return {"status": "ok", **server.stats}
@@ -228,6 +286,13 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     async def completions(body: dict):
         prompt = _prompt_ids(body.get("prompt", ""))
         max_tokens = int(body.get("max_tokens", 16))
+        if body.get("stream"):
+            _check(prompt, max_tokens)
+            cid, created = f"cmpl-{next(ids)}", int(time.time())
+            return _sse(prompt, max_tokens, lambda toks, fin, usage: {
+                "id": cid, "object": "text_completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "text": tok.decode(toks), "token_ids": toks, "finish_reason": fin}],
+                **({"usage": usage} if usage else {})})
         out = await run_in_threadpool(_run, prompt, max_tokens)
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
                 "model": model_name,
@@ -243,6 +308,14 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
             text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
             prompt = tok.encode(text)
         max_tokens = int(body.get("max_tokens", 16))
+        if body.get("stream"):
+            _check(prompt, max_tokens)
+            cid, created = f"chatcmpl-{next(ids)}", int(time.time())
+            return _sse(prompt, max_tokens, lambda toks, fin, usage: {
+                "id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
+                "choices": [{"index": 0, "delta": {"content": tok.decode(toks)} if toks else {},
+                             "token_ids": toks, "finish_reason": fin}],
+                **({"usage": usage} if usage else {})})
         out = await run_in_threadpool(_run, prompt, max_tokens)
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
                 "model": model_name,

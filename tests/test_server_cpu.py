@@ -117,6 +117,46 @@ def test_http_completions_and_chat():
     assert not loop.is_alive()
 
 
+def test_streaming_completions():
+    """stream=true: server-sent events carry the tokens step by step, then
+    a chunk with finish_reason and usage, then [DONE]."""
+    requests = pytest.importorskip("requests")
+    import json
+
+    from conftest import free_port
+
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    try:
+        base = f"http://127.0.0.1:{port}"
+        for path, body in (("/v1/completions", {"prompt": [3, 4], "max_tokens": 5, "stream": True}),
+                           ("/v1/chat/completions", {"messages": [{"role": "user", "content": "x"}],
+                                                     "max_tokens": 5, "stream": True})):
+            r = requests.post(base + path, json=body, timeout=30, stream=True)
+            assert r.status_code == 200 and r.headers["content-type"].startswith("text/event-stream")
+            events = [ln[len("data: "):] for ln in r.iter_lines(decode_unicode=True) if ln.startswith("data: ")]
+            assert events[-1] == "[DONE]"
+            chunks = [json.loads(e) for e in events[:-1]]
+            toks = [t for c in chunks for t in c["choices"][0]["token_ids"]]
+            prompt = [3, 4] if path == "/v1/completions" else \
+                srv_mod.ByteTokenizer().encode("<|user|>x<|assistant|>")
+            assert toks == expected(prompt, 5)
+            assert len(chunks) >= 3  # tokens arrive over several engine steps
+            assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+            assert chunks[-1]["usage"]["completion_tokens"] == 5
+        bad = requests.post(base + "/v1/completions", json={"prompt": [], "max_tokens": 1, "stream": True},
+                            timeout=30)
+        assert bad.status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+
+
 def _lockstep(rank, world):
     import datetime
 
