@@ -102,8 +102,11 @@ class LLMEngine:
                     decode_lse=self.max_batch * nq * max_splits)
 
     # ------------------------------------------------------------------ requests
-    def add_request(self, prompt, max_new_tokens: int) -> Request:
-        req = Request(self._next_rid, list(prompt), max_new_tokens, t_arrive=time.perf_counter())
+    def add_request(self, prompt, max_new_tokens: int, stop_ids=()) -> Request:
+        """Queue a prompt (token ids); generation ends after ``max_new_tokens``
+        or after any token in ``stop_ids`` (kept in the output)."""
+        req = Request(self._next_rid, list(prompt), max_new_tokens, t_arrive=time.perf_counter(),
+                      stop_ids=tuple(int(t) for t in stop_ids))
         self._next_rid += 1
         self.sched.add(req)
         return req
@@ -237,7 +240,7 @@ class LLMEngine:
         self.sched.finished = []
         return done
 
-    def generate(self, prompts, max_new_tokens: int = 16):
-        reqs = [self.add_request(p, max_new_tokens) for p in prompts]
+    def generate(self, prompts, max_new_tokens: int = 16, stop_ids=()):
+        reqs = [self.add_request(p, max_new_tokens, stop_ids) for p in prompts]
         self.run()
         return [r.output for r in reqs]

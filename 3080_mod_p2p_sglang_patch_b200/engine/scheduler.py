@@ -26,6 +26,10 @@ class Request:
     t_arrive: float = 0.0
     t_first: float = 0.0
     token_times: list = dataclasses.field(default_factory=list)
+    # generation also ends after any of these token ids (e.g. the model's EOS);
+    # the stop token is kept in the output
+    stop_ids: tuple = ()
+    finish_reason: str = None  # "length" or "stop" once done
 
     @property
     def total_len(self):
@@ -116,7 +120,7 @@ class Scheduler:
             if piece.completes:
                 self.prefilling.remove(req)
                 req.output.append(int(tok))
-                if len(req.output) >= req.max_new:
+                if self._done(req):
                     self._finish(req)
                 else:
                     self.running.append(req)
@@ -125,9 +129,19 @@ class Scheduler:
         for req, tok in zip(batch.reqs, next_tokens):
             req.computed += 1
             req.output.append(int(tok))
-            if len(req.output) >= req.max_new:
+            if self._done(req):
                 self.running.remove(req)
                 self._finish(req)
+
+    @staticmethod
+    def _done(req):
+        if req.stop_ids and req.output[-1] in req.stop_ids:
+            req.finish_reason = "stop"
+            return True
+        if len(req.output) >= req.max_new:
+            req.finish_reason = "length"
+            return True
+        return False
 
     def _finish(self, req):
         req.done = True

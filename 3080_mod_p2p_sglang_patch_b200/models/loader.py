@@ -122,3 +122,16 @@ def load_llama(model_dir: str, tp_rank: int = 0, tp_size: int = 1, device="cuda"
         raise ValueError(f"{model_dir}: head_dim {cfg.head_dim}; the attention kernels need 128")
     ck = _Checkpoint(model_dir)
     return cfg, _shard_weights(cfg, tp_rank, tp_size, device, ck.fetch)
+
+
+def stop_token_ids(model_dir: str) -> tuple:
+    """End-of-sequence token ids of a checkpoint: ``eos_token_id`` (an int or a
+    list) from generation_config.json, else from config.json; () if none."""
+    for name in ("generation_config.json", "config.json"):
+        path = os.path.join(model_dir, name)
+        if os.path.isfile(path):
+            with open(path) as f:
+                eos = json.load(f).get("eos_token_id")
+            if eos is not None:
+                return tuple(int(e) for e in (eos if isinstance(eos, list) else [eos]))
+    return ()

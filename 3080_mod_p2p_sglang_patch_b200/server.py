@@ -64,11 +64,13 @@ class HFTokenizer:
 
 
 class _Pending:
-    __slots__ = ("prompt", "max_new", "event", "output", "error", "stream", "req", "sent")
+    __slots__ = ("prompt", "max_new", "stop_ids", "event", "output", "error", "stream", "req", "sent", "reason")
 
-    def __init__(self, prompt, max_new, stream=False):
+    def __init__(self, prompt, max_new, stream=False, stop_ids=()):
         self.prompt = prompt
         self.max_new = max_new
+        self.stop_ids = tuple(stop_ids)
+        self.reason = "length"
         self.event = threading.Event()
         self.output = None
         self.error = None
@@ -95,8 +97,9 @@ class EngineServer:
 
     SHUTDOWN = "__shutdown__"
 
-    def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None):
+    def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None, stop_ids=()):
         self.engine = engine
+        self.stop_ids = tuple(stop_ids)  # default stop tokens (e.g. the checkpoint's EOS)
         self.group = group
         self.rank = rank
         self.world = world
@@ -107,20 +110,22 @@ class EngineServer:
         self._stopped = threading.Event()
 
     # ------------------------------------------------------------ rank 0 API
-    def submit(self, prompt: list, max_new: int, timeout: float = None) -> list:
+    def submit(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, with_reason=False):
         """Called from HTTP threads on rank 0: blocks until the request is done
-        and returns the generated token ids."""
-        p = self._enqueue(prompt, max_new, stream=False)
+        and returns the generated token ids (and the finish reason, "length" or
+        "stop", with ``with_reason``). ``stop_ids`` None = the server default."""
+        p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if p.error is not None:
             raise RuntimeError(p.error)
-        return p.output
+        return (p.output, p.reason) if with_reason else p.output
 
-    def submit_stream(self, prompt: list, max_new: int, timeout: float = None):
+    def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None):
         """Like ``submit`` but yields lists of new token ids as the engine
-        produces them (rank 0, from an HTTP thread)."""
-        p = self._enqueue(prompt, max_new, stream=True)
+        produces them (rank 0, from an HTTP thread); the finish reason is
+        appended to ``reason_out`` (a list) at the end."""
+        p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids)
         while True:
             try:
                 item = p.stream.get(timeout=timeout)
@@ -131,6 +136,8 @@ class EngineServer:
             yield item
         if p.error is not None:
             raise RuntimeError(p.error)
+        if reason_out is not None:
+            reason_out.append(p.reason)
 
     def _enqueue_check(self, prompt, max_new):
         if not prompt:
@@ -139,11 +146,12 @@ class EngineServer:
             raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
                              f"max sequence {self.max_prompt}")
 
-    def _enqueue(self, prompt, max_new, stream):
+    def _enqueue(self, prompt, max_new, stream, stop_ids=None):
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
-        p = _Pending(list(prompt), int(max_new), stream=stream)
+        p = _Pending(list(prompt), int(max_new), stream=stream,
+                     stop_ids=self.stop_ids if stop_ids is None else stop_ids)
         self.q.put(p)
         return p
 
@@ -167,10 +175,10 @@ class EngineServer:
         if self.world > 1:
             import torch.distributed as dist
 
-            payload = [[c if c == self.SHUTDOWN else (c.prompt, c.max_new) for c in cmds]]
+            payload = [[c if c == self.SHUTDOWN else (c.prompt, c.max_new, c.stop_ids) for c in cmds]]
             dist.broadcast_object_list(payload, src=0, group=self.group)
             if self.rank != 0:
-                cmds = [c if c == self.SHUTDOWN else _Pending(c[0], c[1]) for c in payload[0]]
+                cmds = [c if c == self.SHUTDOWN else _Pending(c[0], c[1], stop_ids=c[2]) for c in payload[0]]
         return cmds
 
     def serve_forever(self):
@@ -184,7 +192,7 @@ class EngineServer:
                     if c == self.SHUTDOWN:
                         stop = True
                         continue
-                    req = eng.add_request(c.prompt, c.max_new)
+                    req = eng.add_request(c.prompt, c.max_new, c.stop_ids)
                     c.req = req
                     self._by_rid[req.rid] = c
                     self.stats["requests"] += 1
@@ -204,6 +212,7 @@ class EngineServer:
                     p = self._by_rid.pop(r.rid, None)
                     if p is not None:
                         self.stats["completion_tokens"] += len(r.output)
+                        p.reason = getattr(r, "finish_reason", None) or "length"
                         p.finish(output=list(r.output))
         except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
             for p in self._by_rid.values():
@@ -241,9 +250,13 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
             return tok.encode(p)
         raise HTTPException(400, "prompt must be a string or a list of token ids")
 
-    def _run(prompt, max_tokens):
+    def _stop(body):
+        ids_ = body.get("stop_token_ids")
+        return None if ids_ is None else [int(t) for t in ids_]
+
+    def _run(prompt, max_tokens, stop=None):
         try:
-            return server.submit(prompt, max_tokens)
+            return server.submit(prompt, max_tokens, stop_ids=stop, with_reason=True)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         except (RuntimeError, TimeoutError) as e:
@@ -258,16 +271,17 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
 
-    def _sse(prompt, max_tokens, chunk_of):
+    def _sse(prompt, max_tokens, chunk_of, stop=None):
         """Server-sent events: one chunk per engine step's new tokens, a last
         chunk with finish_reason and usage, then [DONE]."""
         def gen():
-            out = []
+            out, reason = [], []
             try:
-                for toks in server.submit_stream(prompt, max_tokens):
+                for toks in server.submit_stream(prompt, max_tokens, stop_ids=stop, reason_out=reason):
                     out += toks
                     yield "data: " + json.dumps(chunk_of(toks, None, None)) + "\n\n"
-                yield "data: " + json.dumps(chunk_of([], "length", _usage(prompt, out))) + "\n\n"
+                fin = reason[0] if reason else "length"
+                yield "data: " + json.dumps(chunk_of([], fin, _usage(prompt, out))) + "\n\n"
             except (RuntimeError, TimeoutError) as e:
                 yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
             yield "data: [DONE]\n\n"
@@ -286,17 +300,18 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     async def completions(body: dict):
         prompt = _prompt_ids(body.get("prompt", ""))
         max_tokens = int(body.get("max_tokens", 16))
+        stop = _stop(body)
         if body.get("stream"):
             _check(prompt, max_tokens)
             cid, created = f"cmpl-{next(ids)}", int(time.time())
             return _sse(prompt, max_tokens, lambda toks, fin, usage: {
                 "id": cid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": 0, "text": tok.decode(toks), "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})})
-        out = await run_in_threadpool(_run, prompt, max_tokens)
+                **({"usage": usage} if usage else {})}, stop)
+        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop)
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
                 "model": model_name,
-                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": "length"}],
+                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": fin}],
                 "usage": _usage(prompt, out)}
 
     @app.post("/v1/chat/completions")
@@ -308,6 +323,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
             text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
             prompt = tok.encode(text)
         max_tokens = int(body.get("max_tokens", 16))
+        stop = _stop(body)
         if body.get("stream"):
             _check(prompt, max_tokens)
             cid, created = f"chatcmpl-{next(ids)}", int(time.time())
@@ -315,12 +331,12 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 "id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                 "choices": [{"index": 0, "delta": {"content": tok.decode(toks)} if toks else {},
                              "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})})
-        out = await run_in_threadpool(_run, prompt, max_tokens)
+                **({"usage": usage} if usage else {})}, stop)
+        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop)
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
                 "model": model_name,
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
-                             "token_ids": out, "finish_reason": "length"}],
+                             "token_ids": out, "finish_reason": fin}],
                 "usage": _usage(prompt, out)}
 
     return app
@@ -382,7 +398,8 @@ def main(argv=None):
     else:
         cfg = models.LlamaConfig.by_name(args.model)
         eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, **opts)
-    server = EngineServer(eng, ctrl, rank, world, max_prompt=args.max_seq)
+    stop = models.stop_token_ids(args.model_path) if args.model_path else ()
+    server = EngineServer(eng, ctrl, rank, world, max_prompt=args.max_seq, stop_ids=stop)
     http = None
     if rank == 0:
         import signal

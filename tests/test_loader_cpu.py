@@ -105,3 +105,11 @@ def test_llama3_rope_scaling_bands():
     assert torch.allclose(ang_s[-4:], ang_b[-4:] / 8.0, rtol=1e-4)  # low frequencies / factor
     mid = (ang_s / ang_b)[4:-4]
     assert bool(((mid <= 1.0 + 1e-6) & (mid >= 1 / 8.0 - 1e-6)).all())
+
+
+def test_stop_token_ids_from_checkpoint(tmp_path):
+    (tmp_path / "config.json").write_text(json.dumps({"eos_token_id": 2}))
+    assert models.stop_token_ids(str(tmp_path)) == (2,)
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [128001, 128009]}))
+    assert models.stop_token_ids(str(tmp_path)) == (128001, 128009)  # generation config wins
+    assert models.stop_token_ids(str(tmp_path / "missing")) == ()

@@ -103,3 +103,25 @@ def test_slots_map_positions_to_pages():
     assert slots == [5 * PAGE + 14, 5 * PAGE + 15, 9 * PAGE + 0, 9 * PAGE + 1, 9 * PAGE + 2]
     assert kv_mod.PagedKVCache.blocks_for(33) == 3
     assert kv_mod.PagedKVCache.bytes_per_token(32, 8, 128) == 32 * 2 * 8 * 128 * 2
+
+
+def test_stop_token_ends_generation():
+    s = sched_mod.Scheduler(chunk=64, max_batch=4)
+    a = sched_mod.Request(rid=0, prompt=[1, 2, 3], max_new=10, stop_ids=(99,))
+    b = sched_mod.Request(rid=1, prompt=[4, 5], max_new=3)
+    s.add(a)
+    s.add(b)
+    batch = s.next_batch()
+    s.after_prefill(batch, [7, 7])
+    toks = iter([[8, 8], [99, 9]])
+    while s.has_work():
+        batch = s.next_batch()
+        s.after_decode(batch, next(toks)[:len(batch.reqs)])
+    assert a.output == [7, 8, 99] and a.finish_reason == "stop"     # stops on (and keeps) the stop id
+    assert b.output == [7, 8, 9] and b.finish_reason == "length"
+    # a stop id produced by the prefill itself ends the request at once
+    s2 = sched_mod.Scheduler(chunk=64, max_batch=4)
+    c = sched_mod.Request(rid=2, prompt=[1], max_new=5, stop_ids=(7,))
+    s2.add(c)
+    s2.after_prefill(s2.next_batch(), [7])
+    assert not s2.has_work() and c.output == [7] and c.finish_reason == "stop"

@@ -37,8 +37,9 @@ class FakeEngine:
         self.n = 0
         self.log = []
 
-    def add_request(self, prompt, max_new):
+    def add_request(self, prompt, max_new, stop_ids=()):
         r = _Req(self.n, prompt, max_new)
+        r.stop_ids = tuple(stop_ids)
         self.n += 1
         self.sched.running.append(r)
         self.log.append((r.rid, tuple(prompt), max_new))
@@ -47,7 +48,9 @@ class FakeEngine:
     def step(self):
         for r in list(self.sched.running):
             r.output.append((sum(r.prompt) + len(r.output)) % 1000)
-            if len(r.output) >= r.max_new:
+            r.finish_reason = "stop" if r.output[-1] in r.stop_ids else \
+                ("length" if len(r.output) >= r.max_new else None)
+            if r.finish_reason:
                 self.sched.running.remove(r)
                 self.sched.finished.append(r)
 
@@ -108,8 +111,12 @@ def test_http_completions_and_chat():
         assert requests.post(base + "/v1/completions", json={"prompt": [], "max_tokens": 1}, timeout=30).status_code == 400
         assert requests.post(base + "/v1/completions", json={"prompt": [1] * 4096, "max_tokens": 8},
                              timeout=30).status_code == 400
+        # stop_token_ids: prompt [10] generates 10, 11, 12, ...; stop at 12
+        j = requests.post(base + "/v1/completions", json={"prompt": [10], "max_tokens": 8, "stop_token_ids": [12]},
+                          timeout=30).json()
+        assert j["choices"][0]["token_ids"] == [10, 11, 12] and j["choices"][0]["finish_reason"] == "stop"
         h = requests.get(base + "/health", timeout=30).json()
-        assert h["status"] == "ok" and h["requests"] == 10
+        assert h["status"] == "ok" and h["requests"] == 11
     finally:
         server.stop()
         loop.join(timeout=30)
