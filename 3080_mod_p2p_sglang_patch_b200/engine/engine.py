@@ -19,6 +19,7 @@ from ..utils import nvtx
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
 from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
 from .kv_cache import PAGE, PagedKVCache
+from .sampling import GREEDY, sample
 from .scheduler import Request, Scheduler
 
 
@@ -54,6 +55,9 @@ class LLMEngine:
             kv_blocks = max_batch * self.max_blocks_per_seq + 1
         self.kv = PagedKVCache(cfg.layers, nkv, cfg.head_dim, kv_blocks, self.device)
         self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq)
+        # draws of unseeded sampled requests (same seed on every TP rank)
+        self._rng = torch.Generator(device=self.device)
+        self._rng.manual_seed(int(seed) + 1_000_003)
         self.block_table = torch.zeros((max_batch, self.max_blocks_per_seq), dtype=torch.int32, device=self.device)
         self._next_rid = 0
         # scratch sized once (graph capture must not allocate)
@@ -65,6 +69,19 @@ class LLMEngine:
             self.graphs = DecodeGraphRunner(self, sizes)
         if prefill_graph:
             self.prefill_graph = PrefillGraphRunner(self, chunk)
+
+    def _sample_tokens(self, hidden, reqs, draw=None):
+        """Next tokens for rows of final hidden states (one per request).
+        ``draw[i]`` False: row i's token is not used (a prefill piece that
+        does not end its prompt), so it is taken greedily and no generator
+        advances."""
+        logits = self.model.full_logits(hidden)
+        params, gens = [], []
+        for i, r in enumerate(reqs):
+            use = r.sampled and (draw is None or draw[i])
+            params.append(r.sampling if use else GREEDY)
+            gens.append((r.rng if r.rng is not None else self._rng) if use else None)
+        return sample(logits, params, gens)
 
     @classmethod
     def from_pretrained(cls, model_dir: str, tp=None, device=None, **kw):
@@ -102,11 +119,17 @@ class LLMEngine:
                     decode_lse=self.max_batch * nq * max_splits)
 
     # ------------------------------------------------------------------ requests
-    def add_request(self, prompt, max_new_tokens: int, stop_ids=()) -> Request:
+    def add_request(self, prompt, max_new_tokens: int, stop_ids=(), sampling=None) -> Request:
         """Queue a prompt (token ids); generation ends after ``max_new_tokens``
-        or after any token in ``stop_ids`` (kept in the output)."""
+        or after any token in ``stop_ids`` (kept in the output). ``sampling``:
+        a SamplingParams (None = greedy); a seeded one draws from its own
+        generator, an unseeded one from the engine's (seeded identically on
+        every TP rank, so all ranks draw the same tokens)."""
         req = Request(self._next_rid, list(prompt), max_new_tokens, t_arrive=time.perf_counter(),
-                      stop_ids=tuple(int(t) for t in stop_ids))
+                      stop_ids=tuple(int(t) for t in stop_ids), sampling=sampling)
+        if sampling is not None and not sampling.greedy and sampling.seed is not None:
+            req.rng = torch.Generator(device=self.device)
+            req.rng.manual_seed(int(sampling.seed))
         self._next_rid += 1
         self.sched.add(req)
         return req
@@ -123,7 +146,8 @@ class LLMEngine:
         for p in pieces:
             if not getattr(p.req, "_row_synced", False):
                 self._sync_block_row(p.req)
-        if self.prefill_graph is not None and len(pieces) == 1 and pieces[0].n == self.chunk:
+        sampled = any(p.completes and p.req.sampled for p in pieces)
+        if self.prefill_graph is not None and len(pieces) == 1 and pieces[0].n == self.chunk and not sampled:
             # a full single-request chunk: replay the captured chunk forward
             p = pieces[0]
             req = p.req
@@ -146,10 +170,14 @@ class LLMEngine:
             rows.append(req.slot)
             off += p.n
             last.append(off - 1)
+        if sampled:
+            hidden = self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, last, return_hidden=True)
+            return self._sample_tokens(hidden, [p.req for p in pieces], [p.completes for p in pieces])
         return self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, last)
 
-    def forward_prefill(self, ids, pos, slots, q_lens, kv_lens, rows, last):
-        """One prefill forward from host lists; returns next token per piece."""
+    def forward_prefill(self, ids, pos, slots, q_lens, kv_lens, rows, last, return_hidden=False):
+        """One prefill forward from host lists; returns next token per piece
+        (or the pieces' final hidden rows with ``return_hidden``)."""
         dev = self.device
         R = len(q_lens)
         host = torch.tensor(ids + pos + q_lens + kv_lens + rows, dtype=torch.int32).pin_memory()
@@ -171,7 +199,7 @@ class LLMEngine:
         def attn(li, q, kc, vc):
             return ops.prefill_attention(q, kc, vc, cu_d, kvl_d, bt, tiles, scale, splits=splits)
 
-        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d)
+        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d, return_hidden=return_hidden)
 
     def decode_inputs(self, reqs):
         ids = [r.output[-1] if r.output else r.prompt[-1] for r in reqs]
@@ -181,7 +209,7 @@ class LLMEngine:
         rows = [r.slot for r in reqs]
         return ids, pos, kv_len, slots, rows
 
-    def forward_decode_eager(self, ids_d, pos_d, kvl_d, slots_d, rows_d, splits=None):
+    def forward_decode_eager(self, ids_d, pos_d, kvl_d, slots_d, rows_d, splits=None, return_hidden=False):
         B = ids_d.shape[0]
         bt = self.block_table.index_select(0, rows_d.long())
         nkv = self.cfg.kv_heads // self.tp_size
@@ -192,20 +220,25 @@ class LLMEngine:
             return ops.decode_attention(q, kc, vc, kvl_d, bt, scale, splits=sp)
 
         last = torch.arange(B, device=self.device, dtype=torch.int64)
-        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last)
+        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last, return_hidden=return_hidden)
 
     def _run_decode(self, batch):
         for r in batch.reqs:
             if not getattr(r, "_row_synced", False):
                 self._sync_block_row(r)
         ids, pos, kv_len, slots, rows = self.decode_inputs(batch.reqs)
-        if self.graphs is not None and self.graphs.can_run(len(ids)):
+        sampled = any(r.sampled for r in batch.reqs)
+        if self.graphs is not None and self.graphs.can_run(len(ids)) and not sampled:
             return self.graphs.run(ids, pos, kv_len, slots, rows)
         dev = self.device
         B = len(ids)
         host = torch.tensor(ids + pos + kv_len + rows, dtype=torch.int32).pin_memory()
         d = host.to(dev, non_blocking=True)
         slots_d = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        if sampled:
+            hidden = self.forward_decode_eager(d[:B], d[B:2 * B], d[2 * B:3 * B], slots_d, d[3 * B:],
+                                               return_hidden=True)
+            return self._sample_tokens(hidden, batch.reqs)
         return self.forward_decode_eager(d[:B], d[B:2 * B], d[2 * B:3 * B], slots_d, d[3 * B:])
 
     def step(self):
@@ -240,7 +273,7 @@ class LLMEngine:
         self.sched.finished = []
         return done
 
-    def generate(self, prompts, max_new_tokens: int = 16, stop_ids=()):
-        reqs = [self.add_request(p, max_new_tokens, stop_ids) for p in prompts]
+    def generate(self, prompts, max_new_tokens: int = 16, stop_ids=(), sampling=None):
+        reqs = [self.add_request(p, max_new_tokens, stop_ids, sampling) for p in prompts]
         self.run()
         return [r.output for r in reqs]

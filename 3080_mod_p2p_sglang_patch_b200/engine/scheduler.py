@@ -30,6 +30,12 @@ class Request:
     # the stop token is kept in the output
     stop_ids: tuple = ()
     finish_reason: str = None  # "length" or "stop" once done
+    sampling: object = None    # engine.sampling.SamplingParams (None = greedy)
+    rng: object = None         # torch.Generator of a seeded sampled request
+
+    @property
+    def sampled(self):
+        return self.sampling is not None and not self.sampling.greedy
 
     @property
     def total_len(self):

@@ -188,6 +188,20 @@ class LlamaTP:
             return ops.fused_add_rmsnorm(x, residual, w, self.cfg.eps, out=out)
         return self.tp.all_reduce_rmsnorm(partial, residual, w, self.cfg.eps, out=out)
 
+    def full_logits(self, x_last):
+        """fp32 logits [B, V] over the whole vocabulary, identical on every
+        rank (the LM-head shards all-gathered in rank order)."""
+        logits = self._linear(x_last, self.w.lm_head)
+        if self.tp_size == 1:
+            return logits.float()
+        B = logits.shape[0]
+        if self.impl == "torch":
+            g = torch.empty((self.tp_size,) + tuple(logits.shape), dtype=logits.dtype, device=logits.device)
+            dist.all_gather_into_tensor(g, logits.contiguous(), group=self.tp.group)
+        else:
+            g = self.tp.all_gather(logits.contiguous())  # [tp, B, V/tp]
+        return g.permute(1, 0, 2).reshape(B, -1).float()
+
     def _lm_argmax(self, x_last):
         """Greedy next token from the vocab-parallel LM head."""
         logits = self._linear(x_last, self.w.lm_head)

@@ -64,12 +64,14 @@ class HFTokenizer:
 
 
 class _Pending:
-    __slots__ = ("prompt", "max_new", "stop_ids", "event", "output", "error", "stream", "req", "sent", "reason")
+    __slots__ = ("prompt", "max_new", "stop_ids", "sampling", "event", "output", "error", "stream", "req", "sent",
+                 "reason")
 
-    def __init__(self, prompt, max_new, stream=False, stop_ids=()):
+    def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None):
         self.prompt = prompt
         self.max_new = max_new
         self.stop_ids = tuple(stop_ids)
+        self.sampling = sampling  # (temperature, top_k, top_p, seed) or None
         self.reason = "length"
         self.event = threading.Event()
         self.output = None
@@ -110,22 +112,24 @@ class EngineServer:
         self._stopped = threading.Event()
 
     # ------------------------------------------------------------ rank 0 API
-    def submit(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, with_reason=False):
+    def submit(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, with_reason=False,
+               sampling=None):
         """Called from HTTP threads on rank 0: blocks until the request is done
         and returns the generated token ids (and the finish reason, "length" or
         "stop", with ``with_reason``). ``stop_ids`` None = the server default."""
-        p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids)
+        p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if p.error is not None:
             raise RuntimeError(p.error)
         return (p.output, p.reason) if with_reason else p.output
 
-    def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None):
+    def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None,
+                      sampling=None):
         """Like ``submit`` but yields lists of new token ids as the engine
         produces them (rank 0, from an HTTP thread); the finish reason is
         appended to ``reason_out`` (a list) at the end."""
-        p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids)
+        p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids, sampling=sampling)
         while True:
             try:
                 item = p.stream.get(timeout=timeout)
@@ -146,12 +150,12 @@ class EngineServer:
             raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
                              f"max sequence {self.max_prompt}")
 
-    def _enqueue(self, prompt, max_new, stream, stop_ids=None):
+    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None):
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
         p = _Pending(list(prompt), int(max_new), stream=stream,
-                     stop_ids=self.stop_ids if stop_ids is None else stop_ids)
+                     stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling)
         self.q.put(p)
         return p
 
@@ -175,10 +179,11 @@ class EngineServer:
         if self.world > 1:
             import torch.distributed as dist
 
-            payload = [[c if c == self.SHUTDOWN else (c.prompt, c.max_new, c.stop_ids) for c in cmds]]
+            payload = [[c if c == self.SHUTDOWN else (c.prompt, c.max_new, c.stop_ids, c.sampling) for c in cmds]]
             dist.broadcast_object_list(payload, src=0, group=self.group)
             if self.rank != 0:
-                cmds = [c if c == self.SHUTDOWN else _Pending(c[0], c[1], stop_ids=c[2]) for c in payload[0]]
+                cmds = [c if c == self.SHUTDOWN else _Pending(c[0], c[1], stop_ids=c[2], sampling=c[3])
+                        for c in payload[0]]
         return cmds
 
     def serve_forever(self):
@@ -192,7 +197,12 @@ class EngineServer:
                     if c == self.SHUTDOWN:
                         stop = True
                         continue
-                    req = eng.add_request(c.prompt, c.max_new, c.stop_ids)
+                    if c.sampling is None:
+                        req = eng.add_request(c.prompt, c.max_new, c.stop_ids)
+                    else:
+                        from .engine.sampling import SamplingParams
+
+                        req = eng.add_request(c.prompt, c.max_new, c.stop_ids, SamplingParams(*c.sampling))
                     c.req = req
                     self._by_rid[req.rid] = c
                     self.stats["requests"] += 1
@@ -254,9 +264,18 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         ids_ = body.get("stop_token_ids")
         return None if ids_ is None else [int(t) for t in ids_]
 
-    def _run(prompt, max_tokens, stop=None):
+    def _sampling(body):
+        """(temperature, top_k, top_p, seed), or None for greedy."""
+        t = float(body.get("temperature") or 0.0)
+        if t <= 0.0:
+            return None
+        seed = body.get("seed")
+        return (t, int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
+                None if seed is None else int(seed))
+
+    def _run(prompt, max_tokens, stop=None, sampling=None):
         try:
-            return server.submit(prompt, max_tokens, stop_ids=stop, with_reason=True)
+            return server.submit(prompt, max_tokens, stop_ids=stop, with_reason=True, sampling=sampling)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         except (RuntimeError, TimeoutError) as e:
@@ -271,13 +290,14 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
 
-    def _sse(prompt, max_tokens, chunk_of, stop=None):
+    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None):
         """Server-sent events: one chunk per engine step's new tokens, a last
         chunk with finish_reason and usage, then [DONE]."""
         def gen():
             out, reason = [], []
             try:
-                for toks in server.submit_stream(prompt, max_tokens, stop_ids=stop, reason_out=reason):
+                for toks in server.submit_stream(prompt, max_tokens, stop_ids=stop, reason_out=reason,
+                                                 sampling=sampling):
                     out += toks
                     yield "data: " + json.dumps(chunk_of(toks, None, None)) + "\n\n"
                 fin = reason[0] if reason else "length"
@@ -307,8 +327,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
             return _sse(prompt, max_tokens, lambda toks, fin, usage: {
                 "id": cid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": 0, "text": tok.decode(toks), "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})}, stop)
-        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop)
+                **({"usage": usage} if usage else {})}, stop, _sampling(body))
+        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body))
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
                 "model": model_name,
                 "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": fin}],
@@ -331,8 +351,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 "id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                 "choices": [{"index": 0, "delta": {"content": tok.decode(toks)} if toks else {},
                              "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})}, stop)
-        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop)
+                **({"usage": usage} if usage else {})}, stop, _sampling(body))
+        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body))
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
                 "model": model_name,
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},

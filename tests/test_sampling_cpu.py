@@ -1,0 +1,44 @@
+"""Sampling: greedy equivalence, top-k / top-p supports, the temperature
+distribution, and seeded reproducibility (CPU tensors)."""
+import importlib
+
+import torch
+
+smp = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine.sampling")
+P = smp.SamplingParams
+
+
+def test_greedy_and_top1_are_argmax():
+    x = torch.randn(4, 100, generator=torch.Generator().manual_seed(0))
+    want = x.argmax(-1)
+    assert torch.equal(smp.sample(x, [P()] * 4), want)
+    assert torch.equal(smp.sample(x, [P(temperature=1.0, top_k=1)] * 4), want)
+
+
+def test_top_k_and_top_p_restrict_the_support():
+    x = torch.tensor([[5.0, 4.0, 3.0, 0.0, -1.0, -2.0]])
+    g = torch.Generator().manual_seed(1)
+    seen_k = {int(smp.sample(x, [P(temperature=5.0, top_k=3)], [g])[0]) for _ in range(300)}
+    assert seen_k == {0, 1, 2}
+    # probs at T=1: ~[0.66, 0.24, 0.09, ...]: top_p=0.8 keeps exactly the first two
+    seen_p = {int(smp.sample(x, [P(temperature=1.0, top_p=0.8)], [g])[0]) for _ in range(300)}
+    assert seen_p == {0, 1}
+    # a tiny top_p always keeps the top token
+    assert {int(smp.sample(x, [P(temperature=1.0, top_p=1e-6)], [g])[0]) for _ in range(50)} == {0}
+
+
+def test_temperature_matches_softmax_frequencies():
+    x = torch.tensor([[1.0, 0.0, -1.0]])
+    g = torch.Generator().manual_seed(2)
+    n = 6000
+    counts = torch.zeros(3)
+    for _ in range(n):
+        counts[smp.sample(x, [P(temperature=2.0)], [g])[0]] += 1
+    want = torch.softmax(x[0] / 2.0, 0)
+    assert torch.allclose(counts / n, want, atol=0.025), (counts / n, want)
+
+
+def test_seeded_draws_reproduce():
+    x = torch.randn(1, 1000, generator=torch.Generator().manual_seed(3))
+    a = [int(smp.sample(x, [P(temperature=1.0)], [torch.Generator().manual_seed(7)])[0]) for _ in range(5)]
+    assert len(set(a)) == 1

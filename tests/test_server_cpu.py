@@ -36,10 +36,13 @@ class FakeEngine:
         self.sched = _Sched()
         self.n = 0
         self.log = []
+        self.sampling_seen = []
 
-    def add_request(self, prompt, max_new, stop_ids=()):
+    def add_request(self, prompt, max_new, stop_ids=(), sampling=None):
         r = _Req(self.n, prompt, max_new)
         r.stop_ids = tuple(stop_ids)
+        r.sampling = sampling
+        self.sampling_seen.append(sampling)
         self.n += 1
         self.sched.running.append(r)
         self.log.append((r.rid, tuple(prompt), max_new))
@@ -115,8 +118,14 @@ def test_http_completions_and_chat():
         j = requests.post(base + "/v1/completions", json={"prompt": [10], "max_tokens": 8, "stop_token_ids": [12]},
                           timeout=30).json()
         assert j["choices"][0]["token_ids"] == [10, 11, 12] and j["choices"][0]["finish_reason"] == "stop"
+        # sampling fields reach the engine as SamplingParams
+        requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 1, "temperature": 0.7,
+                                                      "top_p": 0.9, "top_k": 40, "seed": 5}, timeout=30)
+        sp = eng.sampling_seen[-1]
+        assert (sp.temperature, sp.top_k, sp.top_p, sp.seed) == (0.7, 40, 0.9, 5)
+        assert eng.sampling_seen[0] is None  # greedy requests stay greedy
         h = requests.get(base + "/health", timeout=30).json()
-        assert h["status"] == "ok" and h["requests"] == 11
+        assert h["status"] == "ok" and h["requests"] == 12
     finally:
         server.stop()
         loop.join(timeout=30)
