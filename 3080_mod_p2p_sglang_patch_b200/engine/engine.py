@@ -18,7 +18,7 @@ from .. import ops
 from ..utils import nvtx
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
 from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
-from .kv_cache import PAGE, PagedKVCache
+from .kv_cache import PAGE, PagedKVCache, PrefixCache
 from .sampling import GREEDY, sample
 from .scheduler import Request, Scheduler
 
@@ -27,7 +27,7 @@ class LLMEngine:
     def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
-                 sp: bool = None, weights=None):
+                 sp: bool = None, weights=None, prefix_cache: bool = False):
         self.cfg = cfg
         self.tp = tp
         self.tp_size = tp.world_size if tp is not None else 1
@@ -54,7 +54,9 @@ class LLMEngine:
         if kv_blocks is None:
             kv_blocks = max_batch * self.max_blocks_per_seq + 1
         self.kv = PagedKVCache(cfg.layers, nkv, cfg.head_dim, kv_blocks, self.device)
-        self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq)
+        # prefix caching: off by default (benchmarks must not reuse work)
+        self.prefix_cache = PrefixCache(self.kv.alloc) if prefix_cache else None
+        self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq, prefix_cache=self.prefix_cache)
         # draws of unseeded sampled requests (same seed on every TP rank)
         self._rng = torch.Generator(device=self.device)
         self._rng.manual_seed(int(seed) + 1_000_003)

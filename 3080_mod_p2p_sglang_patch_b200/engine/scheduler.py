@@ -30,6 +30,7 @@ class Request:
     # the stop token is kept in the output
     stop_ids: tuple = ()
     finish_reason: str = None  # "length" or "stop" once done
+    cached_pages: int = 0      # leading prompt pages served by the prefix cache
     sampling: object = None    # engine.sampling.SamplingParams (None = greedy)
     rng: object = None         # torch.Generator of a seeded sampled request
 
@@ -69,11 +70,14 @@ class Batch:
 
 
 class Scheduler:
-    def __init__(self, chunk: int = 1024, max_batch: int = 64, allocator=None, max_seq: int = 16384):
+    def __init__(self, chunk: int = 1024, max_batch: int = 64, allocator=None, max_seq: int = 16384,
+                 prefix_cache=None):
         self.chunk = chunk
         self.max_batch = max_batch
         self.allocator = allocator
         self.max_seq = max_seq
+        # kv_cache.PrefixCache (needs the allocator) or None
+        self.prefix_cache = prefix_cache
         self.waiting = collections.deque()
         self.prefilling = []
         self.running = []
@@ -89,13 +93,25 @@ class Scheduler:
         return bool(self.waiting or self.prefilling or self.running)
 
     def _admit(self):
+        pc = self.prefix_cache
         while self.waiting and self._free_slots:
             req = self.waiting[0]
             need = (len(req.prompt) + req.max_new + PAGE - 1) // PAGE
-            if self.allocator is not None and self.allocator.free < need:
-                break
-            self.waiting.popleft()
+            matched = []
+            if pc is not None:
+                # full pages before the last prompt token (that one is always computed)
+                matched = pc.match(req.prompt, (len(req.prompt) - 1) // PAGE)
             if self.allocator is not None:
+                room = self.allocator.free + (pc.evictable if pc is not None else 0)
+                if room < need - len(matched):
+                    break
+            self.waiting.popleft()
+            if pc is not None:
+                pc.acquire(matched)
+                req.blocks = matched + pc.alloc_blocks(need - len(matched))
+                req.computed = len(matched) * PAGE
+                req.cached_pages = len(matched)
+            elif self.allocator is not None:
                 req.blocks = self.allocator.alloc(need)
             req.slot = self._free_slots.pop()
             self.prefilling.append(req)
@@ -125,6 +141,9 @@ class Scheduler:
             req.computed += piece.n
             if piece.completes:
                 self.prefilling.remove(req)
+                if self.prefix_cache is not None:
+                    # the prompt's full pages now hold valid K/V: share them
+                    self.prefix_cache.insert(req.prompt, req.blocks, req.cached_pages, len(req.prompt) // PAGE)
                 req.output.append(int(tok))
                 if self._done(req):
                     self._finish(req)
@@ -151,8 +170,11 @@ class Scheduler:
 
     def _finish(self, req):
         req.done = True
-        if self.allocator is not None and req.blocks:
-            self.allocator.release(req.blocks)
+        if req.blocks:
+            if self.prefix_cache is not None:
+                self.prefix_cache.release(req.blocks)
+            elif self.allocator is not None:
+                self.allocator.release(req.blocks)
             req.blocks = []
         self._free_slots.append(req.slot)
         req.slot = -1

@@ -394,6 +394,7 @@ def main(argv=None):
     ap.add_argument("--chunk", type=int, default=1024)
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
     args = ap.parse_args(argv)
     logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
     pkg = __name__.rsplit(".", 1)[0]
@@ -406,7 +407,8 @@ def main(argv=None):
     tp = par.TPGroup(None, dev, use_mailbox=None) if world > 1 else None
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
     opts = dict(max_batch=args.max_batch, max_seq=args.max_seq, chunk=args.chunk, use_graphs=not args.no_graphs,
-                impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs))
+                impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
+                prefix_cache=args.prefix_cache)
     tokenizer = None
     if args.model_path:
         eng = eng_mod.LLMEngine.from_pretrained(args.model_path, tp=tp, device=dev, **opts)

@@ -125,3 +125,79 @@ def test_stop_token_ends_generation():
     s2.add(c)
     s2.after_prefill(s2.next_batch(), [7])
     assert not s2.has_work() and c.output == [7] and c.finish_reason == "stop"
+
+
+def _pc_sched(num_blocks=64, chunk=1000, max_batch=8):
+    alloc = kv_mod.BlockAllocator(num_blocks=num_blocks)
+    pc = kv_mod.PrefixCache(alloc)
+    return sched_mod.Scheduler(chunk=chunk, max_batch=max_batch, allocator=alloc, prefix_cache=pc), pc, alloc
+
+
+def _run_one(s, req, tok=7):
+    s.add(req)
+    while s.has_work():
+        b = s.next_batch()
+        if b.kind == "prefill":
+            s.after_prefill(b, [tok] * len(b.pieces))
+        else:
+            s.after_decode(b, [tok] * len(b.reqs))
+
+
+def test_prefix_cache_shares_full_pages_of_a_common_prefix():
+    s, pc, alloc = _pc_sched()
+    common = list(range(100, 140))                      # 40 tokens: 2 full pages + 8
+    a = sched_mod.Request(rid=0, prompt=common + [1, 2, 3], max_new=2)
+    s.add(a)
+    first = s.next_batch()
+    a_blocks = list(a.blocks)
+    s.after_prefill(first, [7])
+    while s.has_work():
+        s.after_decode(s.next_batch(), [7])
+    free_after_a = alloc.free
+    assert pc.evictable == 2                            # a's 2 full prompt pages stay cached
+    b = sched_mod.Request(rid=1, prompt=common + [9] * 30, max_new=2)
+    s.add(b)
+    batch = s.next_batch()
+    assert b.cached_pages == 2 and b.computed == 32     # prefill starts after the shared pages
+    assert batch.pieces[0].start == 32 and batch.pieces[0].n == len(b.prompt) - 32
+    assert b.blocks[:2] == a_blocks[:2]                 # the same physical pages
+    assert pc.evictable == 0 and pc.hits == 2           # referenced again
+    s.after_prefill(batch, [5])
+    while s.has_work():
+        s.after_decode(s.next_batch(), [5])
+    # b registered its own 2 further full pages (common + 30 = 70 tokens -> 4 full pages)
+    assert pc.evictable == 4 and alloc.free == free_after_a - 2
+
+
+def test_prefix_cache_never_shares_the_page_of_the_last_token():
+    s, pc, _ = _pc_sched()
+    p = list(range(32))                                 # exactly 2 full pages
+    _run_one(s, sched_mod.Request(rid=0, prompt=p, max_new=1))
+    again = sched_mod.Request(rid=1, prompt=p, max_new=1)
+    s.add(again)
+    b = s.next_batch()
+    assert again.cached_pages == 1 and b.pieces[0].start == 16 and b.pieces[0].n == 16
+
+
+def test_prefix_cache_evicts_lru_pages_when_memory_is_short():
+    s, pc, alloc = _pc_sched(num_blocks=1 + 6)
+    _run_one(s, sched_mod.Request(rid=0, prompt=list(range(48)), max_new=1))   # 3 full pages cached
+    assert pc.evictable == 3 and alloc.free == 3
+    big = sched_mod.Request(rid=1, prompt=list(range(1000, 1080)), max_new=1)  # needs 6 blocks
+    _run_one(s, big)
+    assert big.done and big.cached_pages == 0
+    assert sorted(pc.ref.values()) == [0] * len(pc.ref)  # nothing referenced after both finished
+
+
+def test_prefix_cache_checks_tokens_not_just_hashes():
+    s, pc, _ = _pc_sched()
+    p = list(range(40))
+    _run_one(s, sched_mod.Request(rid=0, prompt=p, max_new=1))
+    # poison the table entry's stored tokens: a hash hit with different tokens must miss
+    key = next(iter(pc.table))
+    blk, page = pc.table[key]
+    pc.table[key] = (blk, tuple(t + 1 for t in page))
+    r = sched_mod.Request(rid=1, prompt=p, max_new=1)
+    s.add(r)
+    s.next_batch()
+    assert r.cached_pages == 0
