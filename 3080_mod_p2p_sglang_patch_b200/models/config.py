@@ -23,6 +23,8 @@ class LlamaConfig:
     # RoPE frequency scaling as (key, value) pairs, e.g. Llama 3.1's
     # (("rope_type", "llama3"), ("factor", 8.0), ...); empty = plain RoPE
     rope_scaling: tuple = ()
+    # per-head RMSNorm of q and k before RoPE (Qwen3); weights q_norm / k_norm [head_dim]
+    qk_norm: bool = False
 
     @classmethod
     def llama_8b(cls):

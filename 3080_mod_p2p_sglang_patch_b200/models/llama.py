@@ -118,6 +118,9 @@ def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch):
     for i in range(cfg.layers):
         p = f"model.layers.{i}."
         L = {"ln1": get(p + "input_layernorm.weight"), "ln2": get(p + "post_attention_layernorm.weight")}
+        if cfg.qk_norm:  # per-head norms: [head_dim], the same on every rank
+            L["q_norm"] = get(p + "self_attn.q_norm.weight")
+            L["k_norm"] = get(p + "self_attn.k_norm.weight")
         L["qkv"] = torch.cat([rows_of(p + "self_attn.q_proj.weight", cfg.heads * D),
                               rows_of(p + "self_attn.k_proj.weight", cfg.kv_heads * D),
                               rows_of(p + "self_attn.v_proj.weight", cfg.kv_heads * D)], 0).contiguous()
@@ -188,6 +191,16 @@ class LlamaTP:
             return ops.fused_add_rmsnorm(x, residual, w, self.cfg.eps, out=out)
         return self.tp.all_reduce_rmsnorm(partial, residual, w, self.cfg.eps, out=out)
 
+    def _qk_norm(self, qkv, L, nq, nkv, D):
+        """Qwen3: RMSNorm over each head's D values of q and k, in place in the
+        fused qkv output (before RoPE). fp32 statistics, bf16 result."""
+        T = qkv.shape[0]
+        for lo, n, wgt in ((0, nq, L["q_norm"]), (nq * D, nkv, L["k_norm"])):
+            x = qkv[:, lo:lo + n * D].view(T, n, D)
+            xf = x.float()
+            y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * wgt.float()
+            x.copy_(y.to(qkv.dtype))
+
     def full_logits(self, x_last):
         """fp32 logits [B, V] over the whole vocabulary, identical on every
         rank (the LM-head shards all-gathered in rank order)."""
@@ -247,6 +260,8 @@ class LlamaTP:
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_push(f"layer {li}")
             qkv = self._linear(x, L["qkv"])
+            if cfg.qk_norm:
+                self._qk_norm(qkv, L, nq, nkv, D)
             kc, vc = kv_caches[li]
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
             o = attn(li, q, kc, vc)
@@ -293,6 +308,8 @@ class LlamaTP:
         sp.rs_norm_ag(T, res, w.layers[0]["ln1"], cfg.eps)
         for li, L in enumerate(w.layers):
             qkv = sp.gemm_ag(T, L["qkv"])
+            if cfg.qk_norm:
+                self._qk_norm(qkv, L, nq, nkv, D)
             kc, vc = kv_caches[li]
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
             o = attn(li, q, kc, vc)

@@ -79,8 +79,17 @@ def write_safetensors(path: str, tensors: dict, metadata: dict = None):
             f.write(raw)
 
 
+SUPPORTED_ARCHS = ("LlamaForCausalLM", "Qwen3ForCausalLM")
+
+
 def config_from_hf(d: dict, name: str = None) -> LlamaConfig:
-    """LlamaConfig from a Hugging Face ``config.json`` dict (LlamaForCausalLM)."""
+    """LlamaConfig from a Hugging Face ``config.json`` dict: LlamaForCausalLM,
+    or Qwen3ForCausalLM (the same decoder plus per-head q/k RMSNorm)."""
+    arch = (d.get("architectures") or ["LlamaForCausalLM"])[0]
+    if arch not in SUPPORTED_ARCHS:
+        raise ValueError(f"unsupported architecture {arch} (supported: {', '.join(SUPPORTED_ARCHS)})")
+    if d.get("attention_bias") or d.get("mlp_bias"):
+        raise ValueError("projection biases are not supported")
     heads = int(d["num_attention_heads"])
     hidden = int(d["hidden_size"])
     scaling = d.get("rope_scaling") or {}
@@ -92,6 +101,7 @@ def config_from_hf(d: dict, name: str = None) -> LlamaConfig:
         vocab=int(d["vocab_size"]), rope_theta=float(d.get("rope_theta", 10000.0)),
         eps=float(d.get("rms_norm_eps", 1e-5)), max_pos=int(d.get("max_position_embeddings", 8192)),
         rope_scaling=tuple(sorted((str(k), v) for k, v in scaling.items())),
+        qk_norm=arch == "Qwen3ForCausalLM",
     )
 
 

@@ -113,3 +113,43 @@ def test_stop_token_ids_from_checkpoint(tmp_path):
     (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [128001, 128009]}))
     assert models.stop_token_ids(str(tmp_path)) == (128001, 128009)  # generation config wins
     assert models.stop_token_ids(str(tmp_path / "missing")) == ()
+
+
+def test_qwen3_checkpoint_qk_norm(tmp_path):
+    """Qwen3ForCausalLM: the Llama decoder plus per-head q/k RMSNorm; the norm
+    weights are loaded on every rank and applied to the fused qkv in place."""
+    cfg_json = dict(HF_CFG, architectures=["Qwen3ForCausalLM"], rope_scaling=None, tie_word_embeddings=True)
+    t = _checkpoint(tmp_path, tied=True)
+    g = torch.Generator().manual_seed(5)
+    extra = {}
+    for i in range(2):
+        extra[f"model.layers.{i}.self_attn.q_norm.weight"] = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+        extra[f"model.layers.{i}.self_attn.k_norm.weight"] = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    models.write_safetensors(str(tmp_path / "model-00003.safetensors"), extra)
+    (tmp_path / "config.json").write_text(json.dumps(cfg_json))
+    cfg, w = models.load_llama(str(tmp_path), 1, 2, "cpu")
+    assert cfg.qk_norm and torch.equal(w.layers[1]["q_norm"], extra["model.layers.1.self_attn.q_norm.weight"])
+    model = models.LlamaTP(cfg, w, tp=None, impl="native")
+    nq, nkv, D = w.nq, w.nkv, 128
+    qkv = torch.randn(5, (nq + 2 * nkv) * D, generator=g).to(torch.bfloat16)
+    before = qkv.clone()
+    model._qk_norm(qkv, w.layers[1], nq, nkv, D)
+
+    def rms(x, wt):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg.eps) * wt.float()).to(torch.bfloat16)
+
+    q = before[:, :nq * D].view(5, nq, D)
+    k = before[:, nq * D:(nq + nkv) * D].view(5, nkv, D)
+    assert torch.equal(qkv[:, :nq * D].view(5, nq, D), rms(q, w.layers[1]["q_norm"]))
+    assert torch.equal(qkv[:, nq * D:(nq + nkv) * D].view(5, nkv, D), rms(k, w.layers[1]["k_norm"]))
+    assert torch.equal(qkv[:, (nq + nkv) * D:], before[:, (nq + nkv) * D:])  # v untouched
+
+
+def test_unsupported_architecture_is_rejected():
+    import pytest
+
+    with pytest.raises(ValueError):
+        models.config_from_hf(dict(HF_CFG, architectures=["MixtralForCausalLM"]))
+    with pytest.raises(ValueError):
+        models.config_from_hf(dict(HF_CFG, attention_bias=True))
