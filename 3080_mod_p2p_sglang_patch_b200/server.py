@@ -22,6 +22,7 @@ token ids 0..255, generated ids >= 256 decode to nothing. Token-id prompts
 (``temperature`` is ignored).
 """
 import argparse
+import collections
 import datetime
 import itertools
 import json
@@ -109,6 +110,9 @@ class EngineServer:
         self.q = queue.Queue()
         self._by_rid = {}
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0, "steps": 0}
+        # latency samples of finished requests (seconds): time to first token, inter-token gaps
+        self.ttft = collections.deque(maxlen=4096)
+        self.itl = collections.deque(maxlen=65536)
         self._stopped = threading.Event()
 
     # ------------------------------------------------------------ rank 0 API
@@ -222,6 +226,10 @@ class EngineServer:
                     p = self._by_rid.pop(r.rid, None)
                     if p is not None:
                         self.stats["completion_tokens"] += len(r.output)
+                        times = getattr(r, "token_times", None) or []
+                        if times and getattr(r, "t_arrive", 0):
+                            self.ttft.append(times[0] - r.t_arrive)
+                            self.itl.extend(b - a for a, b in zip(times, times[1:]))
                         p.reason = getattr(r, "finish_reason", None) or "length"
                         p.finish(output=list(r.output))
         except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
@@ -312,6 +320,15 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     def health():
         return {"status": "ok", **server.stats}
 
+    @app.get("/metrics")
+    def metrics():
+        """Prometheus text format: request / token / step counters, latency
+        quantiles, and the communicator's calls per path (one-shot, two-shot,
+        NVLS, fused, NCCL fallback, errors) when the engine runs on MailboxAR."""
+        from fastapi.responses import PlainTextResponse
+
+        return PlainTextResponse(render_metrics(server), media_type="text/plain; version=0.0.4")
+
     @app.get("/v1/models")
     def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "mailbox-ar-b200"}]}
@@ -360,6 +377,47 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 "usage": _usage(prompt, out)}
 
     return app
+
+
+def _quantiles(xs, qs=(0.5, 0.9, 0.99)):
+    v = sorted(xs)
+    return {q: v[min(len(v) - 1, int(q * len(v)))] for q in qs} if v else {}
+
+
+def render_metrics(server: "EngineServer") -> str:
+    """The server's metrics in Prometheus text exposition format."""
+    lines = []
+
+    def metric(name, kind, help_, samples):
+        lines.append(f"# HELP {name} {help_}")
+        lines.append(f"# TYPE {name} {kind}")
+        for labels, value in samples:
+            lab = "{" + ",".join(f'{k}="{v}"' for k, v in labels.items()) + "}" if labels else ""
+            lines.append(f"{name}{lab} {value}")
+
+    st = server.stats
+    metric("mbx_requests_total", "counter", "Requests admitted.", [({}, st["requests"])])
+    metric("mbx_prompt_tokens_total", "counter", "Prompt tokens admitted.", [({}, st["prompt_tokens"])])
+    metric("mbx_generation_tokens_total", "counter", "Tokens generated by finished requests.",
+           [({}, st["completion_tokens"])])
+    metric("mbx_engine_steps_total", "counter", "Engine steps (prefill chunks and decode batches).",
+           [({}, st["steps"])])
+    for name, xs, help_ in (("mbx_time_to_first_token_seconds", server.ttft, "Time to first token."),
+                            ("mbx_inter_token_latency_seconds", server.itl, "Gap between generated tokens.")):
+        metric(name, "summary", help_, [({"quantile": q}, v) for q, v in _quantiles(xs).items()] +
+               [({"stat": "count"}, len(xs))])
+    eng = server.engine
+    tp = getattr(eng, "tp", None)
+    comm = getattr(tp, "ca_comm", None) if tp is not None else None
+    if comm is not None:
+        metric("mbx_allreduce_calls_total", "counter", "In-house collective calls by path.",
+               [({"path": k}, v) for k, v in sorted(comm.counters.items())])
+        metric("mbx_communicator_error", "gauge", "Sticky device error code (0 = ok).", [({}, comm.err())])
+    pc = getattr(eng, "prefix_cache", None)
+    if pc is not None:
+        metric("mbx_prefix_cache_hit_pages_total", "counter", "KV pages served from the prefix cache.",
+               [({}, pc.hits)])
+    return "\n".join(lines) + "\n"
 
 
 def start_http(app, host: str, port: int):

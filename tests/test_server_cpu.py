@@ -18,7 +18,10 @@ srv_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.server")
 
 class _Req:
     def __init__(self, rid, prompt, max_new):
+        import time as _t
+
         self.rid, self.prompt, self.max_new, self.output = rid, list(prompt), max_new, []
+        self.t_arrive, self.token_times = _t.perf_counter(), []
 
 
 class _Sched:
@@ -49,8 +52,11 @@ class FakeEngine:
         return r
 
     def step(self):
+        import time as _t
+
         for r in list(self.sched.running):
             r.output.append((sum(r.prompt) + len(r.output)) % 1000)
+            r.token_times.append(_t.perf_counter())
             r.finish_reason = "stop" if r.output[-1] in r.stop_ids else \
                 ("length" if len(r.output) >= r.max_new else None)
             if r.finish_reason:
@@ -126,6 +132,12 @@ def test_http_completions_and_chat():
         assert eng.sampling_seen[0] is None  # greedy requests stay greedy
         h = requests.get(base + "/health", timeout=30).json()
         assert h["status"] == "ok" and h["requests"] == 12
+        m = requests.get(base + "/metrics", timeout=30)
+        assert m.status_code == 200 and m.headers["content-type"].startswith("text/plain")
+        lines = m.text.splitlines()
+        assert "mbx_requests_total 12" in lines
+        assert any(ln.startswith('mbx_inter_token_latency_seconds{quantile="0.5"}') for ln in lines)
+        assert any(ln.startswith("# TYPE mbx_generation_tokens_total counter") for ln in lines)
     finally:
         server.stop()
         loop.join(timeout=30)
