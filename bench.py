@@ -205,6 +205,8 @@ def main():
                 "transport": getattr(tp.ca_comm, "transport", None) if (tp and tp.ca_comm) else None,
                 "prefill_cuda_graph": eng.prefill_graph is not None,
                 "sequence_parallel": eng.sp is not None,
+                "gemm_cta_pair": {"0": "off", "1": "on"}.get(os.environ.get("MBX_GEMM_2CTA", ""), "by wave cost"),
+                "fused_gemm_allreduce": bool(tp is not None and tp.fused_gemm_ar),
             },
             "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")} if clocks else None,
             "e2e": e2e,
