@@ -11,6 +11,12 @@ A safetensors file is a little-endian u64 header length, a JSON header
 raw tensor bytes. ``SafeTensors`` maps the file with numpy and slices rows or
 columns before converting, so a rank reads only its shard of each tensor.
 ``write_safetensors`` writes the same format (tests, exports).
+
+AWQ int4 checkpoints (the reference's served model is one: Qwen3.8-27B-AWQ,
+docs/performance.md:3-5) load too: each quantized linear is dequantized to
+bf16 as its TP shard is read, on the target device, and then runs on the
+same bf16 tensor-core GEMMs as any other checkpoint (a 27B model is 54 GB in
+bf16, well inside one B200's HBM).
 """
 import glob
 import json
@@ -22,8 +28,9 @@ import torch
 
 from .config import LlamaConfig
 
-_DT = {"BF16": (np.uint16, torch.bfloat16), "F16": (np.float16, torch.float16), "F32": (np.float32, torch.float32)}
-_DT_NAME = {torch.bfloat16: "BF16", torch.float16: "F16", torch.float32: "F32"}
+_DT = {"BF16": (np.uint16, torch.bfloat16), "F16": (np.float16, torch.float16), "F32": (np.float32, torch.float32),
+       "I32": (np.int32, torch.int32)}
+_DT_NAME = {torch.bfloat16: "BF16", torch.float16: "F16", torch.float32: "F32", torch.int32: "I32"}
 
 
 class SafeTensors:
@@ -121,16 +128,120 @@ class _Checkpoint:
         return self.where[name].get(name, rows, cols)
 
 
+# AWQ "gemm" packing (AutoAWQ's format, which Hugging Face's AwqConfig reads):
+# for a linear with K inputs and N outputs, ``qweight`` is int32 [K, N/8],
+# ``qzeros`` int32 [K/G, N/8] and ``scales`` fp16 [K/G, N] for group size G.
+# Bits 4i..4i+3 of a packed word hold output column 8c + _AWQ_ORDER[i], and
+# W[k, n] = (q[k, n] - z[k // G, n]) * s[k // G, n].
+_AWQ_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
+
+
+def awq_unpack(packed: torch.Tensor) -> torch.Tensor:
+    """int32 [R, C] packed in AWQ order -> int32 [R, 8C] values 0..15, columns
+    in natural order."""
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32, device=packed.device)
+    nib = (packed.unsqueeze(-1) >> shifts) & 0xF     # nib[..., i] = bits 4i..4i+3
+    out = torch.empty_like(nib)
+    out[..., list(_AWQ_ORDER)] = nib                  # column _AWQ_ORDER[i] <- nibble i
+    return out.reshape(packed.shape[0], -1)
+
+
+def awq_pack(q: torch.Tensor) -> torch.Tensor:
+    """Inverse of ``awq_unpack``: values 0..15 [R, 8C] -> int32 [R, C]."""
+    R, N = q.shape
+    q = q.to(torch.int64).reshape(R, N // 8, 8)
+    packed = torch.zeros(R, N // 8, dtype=torch.int64, device=q.device)
+    for i, col in enumerate(_AWQ_ORDER):
+        packed |= q[..., col] << (4 * i)
+    return torch.where(packed >= 2 ** 31, packed - 2 ** 32, packed).to(torch.int32)
+
+
+def awq_dequant(qweight, qzeros, scales, group: int) -> torch.Tensor:
+    """fp32 [N, K] (Hugging Face [out, in] layout) from AWQ tensors."""
+    q = awq_unpack(qweight)
+    z = awq_unpack(qzeros).repeat_interleave(group, 0)
+    s = scales.float().repeat_interleave(group, 0)
+    return ((q - z).float() * s).t()
+
+
+def awq_quantize(w: torch.Tensor, group: int = 128):
+    """Round-to-nearest asymmetric int4 of an [N, K] weight in AWQ layout:
+    (qweight, qzeros, scales fp16). Used to write AWQ-format test checkpoints;
+    it does not search activation-aware scales."""
+    wt = w.float().t()                                   # [K, N]
+    K, N = wt.shape
+    g = wt.reshape(K // group, group, N)
+    lo, hi = g.amin(1), g.amax(1)
+    s = ((hi - lo) / 15).clamp_min(1e-6).half()          # fp16, like the checkpoints
+    sf = s.float()
+    z = torch.round(-lo / sf).clamp(0, 15)
+    q = torch.round(g / sf.unsqueeze(1) + z.unsqueeze(1)).clamp(0, 15).reshape(K, N)
+    return awq_pack(q.to(torch.int32)), awq_pack(z.to(torch.int32)), s
+
+
+def awq_group_size(qc: dict) -> int:
+    """Group size of a ``quantization_config`` this loader accepts (AWQ,
+    4-bit, zero point, gemm packing); -1 = one group per input row range."""
+    method = str(qc.get("quant_method", "")).lower()
+    if method != "awq":
+        raise ValueError(f"unsupported quantization {method or qc} (supported: awq)")
+    if int(qc.get("bits", qc.get("w_bit", 4))) != 4 or not qc.get("zero_point", True):
+        raise ValueError("AWQ checkpoints must be 4-bit with zero points")
+    if str(qc.get("version", "gemm")).lower() != "gemm":
+        raise ValueError(f"AWQ packing {qc.get('version')} is not supported (supported: gemm)")
+    return int(qc.get("group_size", qc.get("q_group_size", 128)))
+
+
+class _AwqCheckpoint(_Checkpoint):
+    """A checkpoint whose linears may be AWQ-quantized: ``fetch`` of
+    ``<prefix>.weight`` returns that shard dequantized when only
+    ``<prefix>.qweight`` / ``qzeros`` / ``scales`` are stored. Unquantized
+    modules (embeddings, norms, ``modules_to_not_convert``) read as usual."""
+
+    def __init__(self, model_dir: str, group: int, device):
+        super().__init__(model_dir)
+        self.group = group
+        self.device = torch.device(device)
+
+    def fetch(self, name, rows=None, cols=None):
+        base = name[:-len(".weight")] if name.endswith(".weight") else None
+        if base is None or name in self.where or base + ".qweight" not in self.where:
+            return super().fetch(name, rows, cols)
+        qw = self.where[base + ".qweight"]
+        K = qw.entries[base + ".qweight"]["shape"][0]
+        G = K if self.group <= 0 else self.group
+        # HF rows are output columns of the packed tensors; HF cols are their input rows
+        out_cols = pk_cols = None
+        if rows is not None:
+            if rows[0] % 8 or rows[1] % 8:
+                raise ValueError(f"{name}: output shard {rows} is not a multiple of 8 (AWQ packing)")
+            out_cols, pk_cols = rows, (rows[0] // 8, rows[1] // 8)
+        in_rows = grp_rows = None
+        if cols is not None:
+            if cols[0] % G or cols[1] % G:
+                raise ValueError(f"{name}: input shard {cols} is not a multiple of the AWQ group {G}")
+            in_rows, grp_rows = cols, (cols[0] // G, cols[1] // G)
+
+        def part(suffix, r, c):
+            return self.where[base + suffix].get(base + suffix, r, c).to(self.device)
+
+        return awq_dequant(part(".qweight", in_rows, pk_cols), part(".qzeros", grp_rows, pk_cols),
+                           part(".scales", grp_rows, out_cols), G)
+
+
 def load_llama(model_dir: str, tp_rank: int = 0, tp_size: int = 1, device="cuda"):
     """(LlamaConfig, LlamaWeights) of this TP rank from a Hugging Face Llama
-    directory. Head dim 128 (the attention kernels' width) is required."""
+    directory (bf16 / fp16 / fp32, or AWQ int4 dequantized to bf16). Head dim
+    128 (the attention kernels' width) is required."""
     from .llama import _shard_weights
 
     with open(os.path.join(model_dir, "config.json")) as f:
-        cfg = config_from_hf(json.load(f), name=os.path.basename(os.path.normpath(model_dir)))
+        hf = json.load(f)
+    cfg = config_from_hf(hf, name=os.path.basename(os.path.normpath(model_dir)))
     if cfg.head_dim != 128:
         raise ValueError(f"{model_dir}: head_dim {cfg.head_dim}; the attention kernels need 128")
-    ck = _Checkpoint(model_dir)
+    qc = hf.get("quantization_config")
+    ck = _AwqCheckpoint(model_dir, awq_group_size(qc), device) if qc else _Checkpoint(model_dir)
     return cfg, _shard_weights(cfg, tp_rank, tp_size, device, ck.fetch)
 
 

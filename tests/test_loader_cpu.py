@@ -153,3 +153,113 @@ def test_unsupported_architecture_is_rejected():
         models.config_from_hf(dict(HF_CFG, architectures=["MixtralForCausalLM"]))
     with pytest.raises(ValueError):
         models.config_from_hf(dict(HF_CFG, attention_bias=True))
+
+
+# ---------------------------------------------------------------- AWQ int4
+
+def _nibbles_by_hand(word: int):
+    """Output column -> value of one AWQ-packed int32, decoded bit by bit:
+    nibble i sits at bits 4i..4i+3 and holds column (0, 2, 4, 6, 1, 3, 5, 7)[i]."""
+    word &= 0xFFFFFFFF
+    order = (0, 2, 4, 6, 1, 3, 5, 7)
+    cols = [0] * 8
+    for i in range(8):
+        cols[order[i]] = (word >> (4 * i)) & 0xF
+    return cols
+
+
+def test_awq_packing_golden_and_roundtrip():
+    p = models.awq_pack(torch.arange(8, dtype=torch.int32).view(1, 8))
+    assert p.dtype == torch.int32 and p.item() == 0x75316420
+    g = torch.Generator().manual_seed(1)
+    q = torch.randint(0, 16, (5, 64), generator=g, dtype=torch.int32)
+    packed = models.awq_pack(q)
+    assert bool((packed < 0).any())                       # high nibbles >= 8 wrap to negative words
+    assert torch.equal(models.awq_unpack(packed), q)
+    for r in range(5):
+        for c in range(8):
+            assert _nibbles_by_hand(int(packed[r, c])) == q[r, 8 * c:8 * c + 8].tolist()
+
+
+def test_awq_dequant_matches_the_formula_and_bounds_the_error():
+    g = torch.Generator().manual_seed(2)
+    N, K, G = 48, 256, 64
+    w = torch.randn(N, K, generator=g)
+    qw, qz, s = models.awq_quantize(w, G)
+    assert qw.shape == (K, N // 8) and qz.shape == (K // G, N // 8) and s.shape == (K // G, N)
+    assert s.dtype == torch.float16
+    deq = models.awq_dequant(qw, qz, s, G)
+    assert deq.shape == (N, K)
+    # independent decode of one element per group
+    for n, k in ((0, 0), (17, 100), (47, 255), (9, 64)):
+        q = _nibbles_by_hand(int(qw[k, n // 8]))[n % 8]
+        z = _nibbles_by_hand(int(qz[k // G, n // 8]))[n % 8]
+        assert deq[n, k].item() == (q - z) * s[k // G, n].float().item()
+    step = s.float().repeat_interleave(G, 0).t()          # [N, K] quantization step
+    assert bool(((deq - w).abs() <= step * 0.5 + 1e-3).all())
+
+
+def _awq_checkpoint(tmp_path, group):
+    """The bf16 test checkpoint with every decoder linear but layer 0's v_proj
+    stored AWQ-quantized (that one stays bf16, as ``modules_to_not_convert``
+    would leave it). Returns the fp32 weights the loader must produce."""
+    t = _checkpoint(tmp_path)
+    want, out = {}, {}
+    for name, v in t.items():
+        quant = ".layers." in name and name.endswith("_proj.weight") and name != \
+            "model.layers.0.self_attn.v_proj.weight"
+        if not quant:
+            out[name] = v
+            want[name] = v.float()
+            continue
+        base = name[:-len(".weight")]
+        qw, qz, s = models.awq_quantize(v, group)
+        out[base + ".qweight"], out[base + ".qzeros"], out[base + ".scales"] = qw, qz, s
+        want[name] = models.awq_dequant(qw, qz, s, group)
+    for f in tmp_path.glob("*.safetensors"):
+        f.unlink()
+    models.write_safetensors(str(tmp_path / "model.safetensors"), out)
+    cfg = dict(HF_CFG, quantization_config={"quant_method": "awq", "bits": 4, "group_size": group,
+                                            "zero_point": True, "version": "gemm",
+                                            "modules_to_not_convert": ["model.layers.0.self_attn.v_proj"]})
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    return want
+
+
+def test_awq_checkpoint_loads_dequantized_tp_shards(tmp_path):
+    want = _awq_checkpoint(tmp_path, group=64)
+    D = 128
+    bf = lambda x: x.to(torch.bfloat16)  # noqa: E731
+    for tp in (1, 2):
+        for r in range(tp):
+            _, w = models.load_llama(str(tmp_path), r, tp, "cpu")
+            nq, nkv, F = 4 // tp, 2 // tp, 384 // tp
+            for i in (0, 1):
+                L, p = w.layers[i], f"model.layers.{i}."
+                want_qkv = torch.cat([want[p + "self_attn.q_proj.weight"][r * nq * D:(r + 1) * nq * D],
+                                      want[p + "self_attn.k_proj.weight"][r * nkv * D:(r + 1) * nkv * D],
+                                      want[p + "self_attn.v_proj.weight"][r * nkv * D:(r + 1) * nkv * D]])
+                assert torch.equal(L["qkv"], bf(want_qkv))
+                assert torch.equal(L["o"], bf(want[p + "self_attn.o_proj.weight"][:, r * nq * D:(r + 1) * nq * D]))
+                want_gu = torch.cat([want[p + "mlp.gate_proj.weight"][r * F:(r + 1) * F],
+                                     want[p + "mlp.up_proj.weight"][r * F:(r + 1) * F]])
+                assert torch.equal(L["gate_up"], bf(want_gu))
+                assert torch.equal(L["down"], bf(want[p + "mlp.down_proj.weight"][:, r * F:(r + 1) * F]))
+                assert all(v.dtype == torch.bfloat16 and v.is_contiguous() for v in L.values())
+            V = 512 // tp
+            assert torch.equal(w.embed, bf(want["model.embed_tokens.weight"][r * V:(r + 1) * V]))
+
+
+def test_awq_rejects_unsupported_configs_and_misaligned_shards(tmp_path):
+    import pytest
+    loader = importlib.import_module("3080_mod_p2p_sglang_patch_b200.models.loader")
+    assert loader.awq_group_size({"quant_method": "awq", "bits": 4, "group_size": 128}) == 128
+    for qc in ({"quant_method": "gptq", "bits": 4}, {"quant_method": "awq", "bits": 8},
+               {"quant_method": "awq", "bits": 4, "version": "gemv"},
+               {"quant_method": "awq", "bits": 4, "zero_point": False}):
+        with pytest.raises(ValueError):
+            loader.awq_group_size(qc)
+    _awq_checkpoint(tmp_path, group=128)
+    models.load_llama(str(tmp_path), 0, 1, "cpu")          # whole tensors: any group size works
+    with pytest.raises(ValueError, match="group"):
+        models.load_llama(str(tmp_path), 1, 2, "cpu")      # down_proj shard of 192 inputs vs group 128

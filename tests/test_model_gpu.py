@@ -255,3 +255,43 @@ def test_hf_checkpoint_engine_matches_reference(tmp_path):
     assert F.cosine_similarity(got, want, dim=0).item() > 0.995
     logits_want = want @ c["model.embed_tokens.weight"].t()  # tied LM head
     assert (got @ c["model.embed_tokens.weight"].t()).argmax().item() in logits_want.topk(5).indices.tolist()
+
+
+@pytest.mark.gpu
+def test_awq_checkpoint_dequantizes_on_device(tmp_path):
+    """An AWQ int4 checkpoint (the reference's served model format) loads with
+    each shard dequantized on the GPU: the bf16 shards equal the CPU
+    dequantization bit for bit, and the engine serves from them."""
+    import json
+
+    models, eng_mod = sub("models"), sub("engine")
+    H, D, nq, nkv, Fd, V, NL, G = 512, 128, 8, 2, 1024, 4096, 2, 128
+    cfg_json = {"architectures": ["LlamaForCausalLM"], "hidden_size": H, "num_hidden_layers": NL,
+                "num_attention_heads": nq, "num_key_value_heads": nkv, "head_dim": D, "intermediate_size": Fd,
+                "vocab_size": V, "rope_theta": 500000.0, "rms_norm_eps": 1e-5, "max_position_embeddings": 1024,
+                "quantization_config": {"quant_method": "awq", "bits": 4, "group_size": G, "zero_point": True,
+                                        "version": "gemm"}}
+    g = torch.Generator().manual_seed(3)
+    rnd = lambda *s: (torch.randn(*s, generator=g) * 0.05).to(torch.float16)  # noqa: E731
+    t = {"model.embed_tokens.weight": rnd(V, H) * 20, "model.norm.weight": torch.ones(H, dtype=torch.float16),
+         "lm_head.weight": rnd(V, H)}
+    shapes = {"self_attn.q_proj": (nq * D, H), "self_attn.k_proj": (nkv * D, H), "self_attn.v_proj": (nkv * D, H),
+              "self_attn.o_proj": (H, nq * D), "mlp.gate_proj": (Fd, H), "mlp.up_proj": (Fd, H),
+              "mlp.down_proj": (H, Fd)}
+    for i in range(NL):
+        p = f"model.layers.{i}."
+        t[p + "input_layernorm.weight"] = torch.ones(H, dtype=torch.float16)
+        t[p + "post_attention_layernorm.weight"] = torch.ones(H, dtype=torch.float16)
+        for name, shape in shapes.items():
+            qw, qz, s = models.awq_quantize(rnd(*shape), G)
+            t[p + name + ".qweight"], t[p + name + ".qzeros"], t[p + name + ".scales"] = qw, qz, s
+    models.write_safetensors(str(tmp_path / "model.safetensors"), t)
+    (tmp_path / "config.json").write_text(json.dumps(cfg_json))
+    _, w_gpu = models.load_llama(str(tmp_path), 0, 1, "cuda")
+    _, w_cpu = models.load_llama(str(tmp_path), 0, 1, "cpu")
+    for L_g, L_c in zip(w_gpu.layers, w_cpu.layers):
+        for k in ("qkv", "o", "gate_up", "down"):
+            assert L_g[k].is_cuda and torch.equal(L_g[k].cpu(), L_c[k]), k
+    eng = eng_mod.LLMEngine.from_pretrained(str(tmp_path), max_batch=2, max_seq=512, chunk=64, use_graphs=False)
+    out = eng.generate([list(range(1, 40))], max_new_tokens=4)[0]
+    assert len(out) == 4 and all(0 <= x < V for x in out)
