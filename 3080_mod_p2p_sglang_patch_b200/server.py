@@ -4,22 +4,30 @@ launch_server --tp 2``, reference scripts/sglang-p2p.sh:162; its
 prompt-processing bench posts to ``/v1/chat/completions`` and reads
 ``usage.prompt_tokens``, tests/pp_bench.py:21-29).
 
+    SGLANG_MAILBOX_AR=1 python -m 3080_mod_p2p_sglang_patch_b200.server --model /path/to/ckpt --tp 2
     torchrun --nproc-per-node N -m 3080_mod_p2p_sglang_patch_b200.server --model 8b --port 8001
 
-One process per GPU. Rank 0 serves HTTP and owns the request queue; every
-rank runs the same engine loop in lockstep: at each iteration rank 0
-broadcasts the newly arrived requests over a gloo control group, every rank
-adds them in the same order and runs one engine step (the TP collectives of
-that step then line up across ranks). With ``SGLANG_MAILBOX_AR=1`` the TP
-allreduces go through MailboxAR, otherwise NCCL.
+One process per GPU. ``--tp N`` outside torchrun starts the N ranks itself
+(torch.distributed.run on 127.0.0.1); under torchrun the ranks are
+torchrun's. sglang's spellings of the common flags are accepted
+(``--tp-size``, ``--chunked-prefill-size``, ``--context-length``,
+``--max-running-requests``, ``--disable-cuda-graph``).
 
-``--model-path DIR`` serves a Hugging Face Llama checkpoint (safetensors,
-each rank reads its shards) with the directory's tokenizer (through
-transformers, local files only) and its chat template. Without it the
-weights are random and text goes through a byte tokenizer: UTF-8 bytes are
-token ids 0..255, generated ids >= 256 decode to nothing. Token-id prompts
-(``"prompt": [ids]``) are accepted either way. Greedy decoding only
-(``temperature`` is ignored).
+Rank 0 serves HTTP and owns the request queue; every rank runs the same
+engine loop in lockstep: at each iteration rank 0 broadcasts the newly
+arrived requests over a gloo control group, every rank adds them in the same
+order and runs one engine step (the TP collectives of that step then line up
+across ranks). With ``SGLANG_MAILBOX_AR=1`` the TP allreduces go through
+MailboxAR, otherwise NCCL.
+
+``--model DIR`` (or ``--model-path DIR``) serves a Hugging Face checkpoint
+(safetensors, each rank reads its shards) with the directory's tokenizer
+(through transformers, local files only) and its chat template. ``--model
+8b|70b|tiny`` runs random weights, and text goes through a byte tokenizer:
+UTF-8 bytes are token ids 0..255, generated ids >= 256 decode to nothing.
+Token-id prompts (``"prompt": [ids]``) are accepted either way. Decoding is
+greedy unless a request sets ``temperature`` (with ``top_p``, ``top_k``,
+``seed``).
 """
 import argparse
 import collections
@@ -27,7 +35,11 @@ import datetime
 import itertools
 import json
 import logging
+import os
 import queue
+import signal
+import subprocess
+import sys
 import threading
 import time
 
@@ -436,29 +448,100 @@ def start_http(app, host: str, port: int):
     return srv, th
 
 
+RANDOM_MODELS = ("8b", "70b", "tiny")
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--model", default="8b",
+                    help="a Hugging Face checkpoint directory, or 8b | 70b | tiny (random weights)")
+    ap.add_argument("--model-path", default=None, help="Hugging Face checkpoint directory (safetensors)")
+    ap.add_argument("--tp", "--tp-size", dest="tp", type=int, default=None,
+                    help="tensor-parallel ranks (one GPU each); started here unless launched by torchrun")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8001)
+    ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
+    ap.add_argument("--max-seq", "--context-length", dest="max_seq", type=int, default=16384)
+    ap.add_argument("--chunk", "--chunked-prefill-size", dest="chunk", type=int, default=1024)
+    ap.add_argument("--impl", default="native", choices=["native", "torch"])
+    ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
+    ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
+    return ap
+
+
+def resolve_model(args):
+    """(random-weights name or None, checkpoint directory or None) from
+    ``--model`` / ``--model-path``: ``--model`` names a directory or one of
+    the random-weight configs."""
+    if args.model_path:
+        return None, args.model_path
+    if os.path.isdir(args.model):
+        return None, args.model
+    if args.model in RANDOM_MODELS:
+        return args.model, None
+    raise SystemExit(f"--model {args.model!r}: not a directory and not one of {', '.join(RANDOM_MODELS)}")
+
+
+def relaunch_command(argv, tp: int, port: int):
+    """The torch.distributed.run command that starts ``tp`` ranks of this
+    server with ``argv`` minus its ``--tp`` / ``--tp-size`` option."""
+    rest, skip = [], False
+    for a in argv:
+        if skip:
+            skip = False
+        elif a in ("--tp", "--tp-size"):
+            skip = True
+        elif not a.startswith(("--tp=", "--tp-size=")):
+            rest.append(a)
+    return [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={tp}",
+            "--master-addr=127.0.0.1", f"--master-port={port}", "-m", f"{_package()}.server", *rest]
+
+
+def _package() -> str:
+    return __package__ or __name__.rsplit(".", 1)[0]
+
+
+def _free_port() -> int:
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run_ranks(cmd) -> int:
+    """Run the per-rank launcher in the foreground; SIGTERM / SIGINT to this
+    process reach it (rank 0 then stops every rank at the same step)."""
+    proc = subprocess.Popen(cmd)
+    for sig in (signal.SIGINT, signal.SIGTERM):
+        signal.signal(sig, lambda signum, _: proc.send_signal(signum))
+    return proc.wait()
+
+
 def main(argv=None):
     import importlib
+
+    argv = list(sys.argv[1:] if argv is None else argv)
+    args = build_parser().parse_args(argv)
+    name, model_path = resolve_model(args)
+    in_torchrun = "WORLD_SIZE" in os.environ
+    if args.tp is not None and args.tp < 1:
+        raise SystemExit("--tp must be >= 1")
+    if in_torchrun and args.tp is not None and args.tp != int(os.environ["WORLD_SIZE"]):
+        raise SystemExit(f"--tp {args.tp} but torchrun started {os.environ['WORLD_SIZE']} ranks")
+    if not in_torchrun and (args.tp or 1) > 1:
+        raise SystemExit(_run_ranks(relaunch_command(argv, args.tp, _free_port())))
 
     import torch
     import torch.distributed as dist
 
-    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--model", default="8b", help="8b | 70b | tiny (random weights)")
-    ap.add_argument("--model-path", default=None, help="Hugging Face Llama checkpoint directory (safetensors)")
-    ap.add_argument("--host", default="127.0.0.1")
-    ap.add_argument("--port", type=int, default=8001)
-    ap.add_argument("--max-batch", type=int, default=64)
-    ap.add_argument("--max-seq", type=int, default=16384)
-    ap.add_argument("--chunk", type=int, default=1024)
-    ap.add_argument("--impl", default="native", choices=["native", "torch"])
-    ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
-    args = ap.parse_args(argv)
-    logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
-    pkg = __name__.rsplit(".", 1)[0]
+    pkg = _package()
     par = importlib.import_module(f"{pkg}.parallel")
     models = importlib.import_module(f"{pkg}.models")
     eng_mod = importlib.import_module(f"{pkg}.engine")
+    if not torch.cuda.is_available():
+        raise SystemExit("the server needs a CUDA GPU per rank (none visible)")
+    logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
     rank, world, local = par.init_distributed(timeout_s=600)
     dev = torch.device("cuda", local)
     # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow
@@ -468,22 +551,20 @@ def main(argv=None):
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
                 prefix_cache=args.prefix_cache)
     tokenizer = None
-    if args.model_path:
-        eng = eng_mod.LLMEngine.from_pretrained(args.model_path, tp=tp, device=dev, **opts)
+    if model_path:
+        eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, **opts)
         cfg = eng.cfg
         try:
-            tokenizer = HFTokenizer(args.model_path)
+            tokenizer = HFTokenizer(model_path)
         except Exception as e:  # noqa: BLE001 - token-id prompts still work
-            logger.warning("no tokenizer in %s (%s); using the byte tokenizer", args.model_path, e)
+            logger.warning("no tokenizer in %s (%s); using the byte tokenizer", model_path, e)
     else:
-        cfg = models.LlamaConfig.by_name(args.model)
+        cfg = models.LlamaConfig.by_name(name)
         eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, **opts)
-    stop = models.stop_token_ids(args.model_path) if args.model_path else ()
+    stop = models.stop_token_ids(model_path) if model_path else ()
     server = EngineServer(eng, ctrl, rank, world, max_prompt=args.max_seq, stop_ids=stop)
     http = None
     if rank == 0:
-        import signal
-
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step
         for sig in (signal.SIGINT, signal.SIGTERM):
             signal.signal(sig, lambda *_: server.stop())

@@ -7,12 +7,16 @@ checked here, plus that every TP rank runs the same requests in the same
 order (two gloo ranks).
 """
 import importlib
+import os
+import subprocess
+import sys
 import threading
 
 import pytest
 
 from _mp import run_ranks
 
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 srv_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.server")
 
 
@@ -217,3 +221,41 @@ def test_lockstep_two_ranks():
     assert res[0]["log"] == res[1]["log"] and len(res[0]["log"]) == 6
     for i, out in res[0]["results"].items():
         assert out == expected([i, i + 1], 3 + i % 3)
+
+
+def test_cli_accepts_sglang_flag_spellings_and_model_dirs(tmp_path):
+    p = srv_mod.build_parser()
+    a = p.parse_args(["--model", str(tmp_path), "--tp-size", "2", "--chunked-prefill-size", "2048",
+                      "--context-length", "8192", "--max-running-requests", "32", "--disable-cuda-graph"])
+    assert (a.tp, a.chunk, a.max_seq, a.max_batch, a.no_graphs) == (2, 2048, 8192, 32, True)
+    assert srv_mod.resolve_model(a) == (None, str(tmp_path))            # a directory is a checkpoint
+    assert srv_mod.resolve_model(p.parse_args(["--model", "tiny"])) == ("tiny", None)
+    assert srv_mod.resolve_model(p.parse_args(["--model-path", "/ck", "--model", "8b"])) == (None, "/ck")
+    with pytest.raises(SystemExit):
+        srv_mod.resolve_model(p.parse_args(["--model", str(tmp_path / "missing")]))
+
+
+def test_tp_flag_relaunches_one_rank_per_gpu():
+    for argv in (["--model", "tiny", "--tp", "4", "--port", "9"], ["--tp=4", "--model", "tiny", "--port", "9"],
+                 ["--model", "tiny", "--tp-size", "4", "--port", "9"]):
+        cmd = srv_mod.relaunch_command(argv, 4, 29555)
+        assert cmd[1:3] == ["-m", "torch.distributed.run"]
+        assert "--nproc-per-node=4" in cmd and "--master-addr=127.0.0.1" in cmd and "--master-port=29555" in cmd
+        i = cmd.index("3080_mod_p2p_sglang_patch_b200.server")
+        assert cmd[i - 1] == "-m" and sorted(cmd[i + 1:]) == sorted(["--model", "tiny", "--port", "9"])
+
+
+def test_module_entry_point_runs_as_main():
+    """``python -m <pkg>.server`` resolves the package's modules (``__name__``
+    is ``__main__`` there); without a GPU it stops with a message, not a
+    traceback."""
+    env = dict(os.environ)
+    env.pop("WORLD_SIZE", None)
+    env["CUDA_VISIBLE_DEVICES"] = ""
+    env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
+    r = subprocess.run([sys.executable, "-m", "3080_mod_p2p_sglang_patch_b200.server", "--model", "tiny"],
+                       capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
+    assert r.returncode == 1 and "needs a CUDA GPU" in r.stderr and "Traceback" not in r.stderr, r.stderr[-2000:]
+    r = subprocess.run([sys.executable, "-m", "3080_mod_p2p_sglang_patch_b200.server", "--model", "nope"],
+                       capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
+    assert r.returncode == 1 and "not a directory" in r.stderr
