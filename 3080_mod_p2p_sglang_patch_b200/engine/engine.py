@@ -15,6 +15,7 @@ import time
 import torch
 
 from .. import ops
+from ..ops import oracle
 from ..utils import nvtx
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
 from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
@@ -28,8 +29,11 @@ class LLMEngine:
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
                  sp: bool = None, weights=None, prefix_cache: bool = False):
+        if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
+            use_graphs, prefill_graph = False, False
         self.cfg = cfg
         self.tp = tp
+        self.impl = impl
         self.tp_size = tp.world_size if tp is not None else 1
         self.tp_rank = tp.rank if tp is not None else 0
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -97,7 +101,15 @@ class LLMEngine:
         return cls(cfg, tp=tp, device=dev, weights=w, **kw)
 
     # ------------------------------------------------------------------ setup
+    def _h2d(self, host: torch.Tensor) -> torch.Tensor:
+        """A host tensor on the engine's device (pinned, asynchronous on CUDA)."""
+        if self.device.type != "cuda":
+            return host.to(self.device)
+        return host.pin_memory().to(self.device, non_blocking=True)
+
     def _reserve_scratch(self):
+        if self.impl == "oracle" or self.device.type != "cuda":
+            return
         cfg, t = self.cfg, self.tp_size
         C = None
         try:
@@ -153,12 +165,9 @@ class LLMEngine:
             # a full single-request chunk: replay the captured chunk forward
             p = pieces[0]
             req = p.req
-            dev = self.device
-            host = torch.tensor(req.prompt[p.start:p.start + p.n] + list(range(p.start, p.start + p.n)),
-                                dtype=torch.int32).pin_memory()
-            d = host.to(dev, non_blocking=True)
-            slots_d = torch.tensor(self.kv.slots(req.blocks, p.start, p.n), dtype=torch.int64).pin_memory().to(
-                dev, non_blocking=True)
+            d = self._h2d(torch.tensor(req.prompt[p.start:p.start + p.n] + list(range(p.start, p.start + p.n)),
+                                       dtype=torch.int32))
+            slots_d = self._h2d(torch.tensor(self.kv.slots(req.blocks, p.start, p.n), dtype=torch.int64))
             return self.prefill_graph.run(d[:p.n], d[p.n:], slots_d, p.start + p.n, self.block_table[req.slot])
         ids, pos, slots, q_lens, kv_lens, rows, last = [], [], [], [], [], [], []
         off = 0
@@ -180,21 +189,25 @@ class LLMEngine:
     def forward_prefill(self, ids, pos, slots, q_lens, kv_lens, rows, last, return_hidden=False):
         """One prefill forward from host lists; returns next token per piece
         (or the pieces' final hidden rows with ``return_hidden``)."""
-        dev = self.device
         R = len(q_lens)
-        host = torch.tensor(ids + pos + q_lens + kv_lens + rows, dtype=torch.int32).pin_memory()
-        d = host.to(dev, non_blocking=True)
+        d = self._h2d(torch.tensor(ids + pos + q_lens + kv_lens + rows, dtype=torch.int32))
         T = len(ids)
         ids_d, pos_d = d[:T], d[T:2 * T]
         kvl_d = d[2 * T + R:2 * T + 2 * R]
         rows_d = d[2 * T + 2 * R:2 * T + 3 * R]
-        slots_d = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        slots_d = self._h2d(torch.tensor(slots, dtype=torch.int64))
+        bt = self.block_table.index_select(0, rows_d.long())
+        last_d = self._h2d(torch.tensor(last, dtype=torch.int64))
+        if self.impl == "oracle":
+            def attn(li, q, kc, vc):
+                return oracle.paged_attention(q, kc, vc, q_lens, kv_lens, bt)
+
+            return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d,
+                                      return_hidden=return_hidden)
         cu = torch.zeros(R + 1, dtype=torch.int32)
         cu[1:] = torch.tensor(q_lens, dtype=torch.int32).cumsum(0)
-        cu_d = cu.pin_memory().to(dev, non_blocking=True)
-        tiles = ops.prefill_tiles(q_lens).pin_memory().to(dev, non_blocking=True)
-        bt = self.block_table.index_select(0, rows_d.long())
-        last_d = torch.tensor(last, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        cu_d = self._h2d(cu)
+        tiles = self._h2d(ops.prefill_tiles(q_lens))
         scale = self.model.scale
         splits = ops.prefill_splits(tiles.shape[0], self.cfg.heads // self.tp_size, max(kv_lens))
 
@@ -214,12 +227,18 @@ class LLMEngine:
     def forward_decode_eager(self, ids_d, pos_d, kvl_d, slots_d, rows_d, splits=None, return_hidden=False):
         B = ids_d.shape[0]
         bt = self.block_table.index_select(0, rows_d.long())
-        nkv = self.cfg.kv_heads // self.tp_size
-        sp = splits or ops.decode_splits(B, nkv, self.max_seq)
-        scale = self.model.scale
+        if self.impl == "oracle":
+            kv_lens = kvl_d.tolist()
 
-        def attn(li, q, kc, vc):
-            return ops.decode_attention(q, kc, vc, kvl_d, bt, scale, splits=sp)
+            def attn(li, q, kc, vc):
+                return oracle.paged_attention(q, kc, vc, [1] * B, kv_lens, bt)
+        else:
+            nkv = self.cfg.kv_heads // self.tp_size
+            sp = splits or ops.decode_splits(B, nkv, self.max_seq)
+            scale = self.model.scale
+
+            def attn(li, q, kc, vc):
+                return ops.decode_attention(q, kc, vc, kvl_d, bt, scale, splits=sp)
 
         last = torch.arange(B, device=self.device, dtype=torch.int64)
         return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last, return_hidden=return_hidden)
@@ -232,11 +251,9 @@ class LLMEngine:
         sampled = any(r.sampled for r in batch.reqs)
         if self.graphs is not None and self.graphs.can_run(len(ids)) and not sampled:
             return self.graphs.run(ids, pos, kv_len, slots, rows)
-        dev = self.device
         B = len(ids)
-        host = torch.tensor(ids + pos + kv_len + rows, dtype=torch.int32).pin_memory()
-        d = host.to(dev, non_blocking=True)
-        slots_d = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        d = self._h2d(torch.tensor(ids + pos + kv_len + rows, dtype=torch.int32))
+        slots_d = self._h2d(torch.tensor(slots, dtype=torch.int64))
         if sampled:
             hidden = self.forward_decode_eager(d[:B], d[B:2 * B], d[2 * B:3 * B], slots_d, d[3 * B:],
                                                return_hidden=True)

@@ -12,6 +12,9 @@ tensor_model_parallel_all_reduce, the call stack of its hot path).
 MailboxAR collectives. ``impl="torch"``: the NCCL(+cuBLAS) TP baseline -
 F.linear (cuBLAS) GEMMs and NCCL allreduce, same attention/elementwise
 kernels, so the two builds differ exactly in GEMMs and collectives.
+``impl="oracle"``: every kernel restated in fp32 PyTorch (``ops.oracle``)
+and plain torch.distributed collectives, on any device (CPU with gloo): the
+whole-model oracle of the tests, not a serving path.
 """
 import math
 
@@ -20,6 +23,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
+from ..ops import oracle
 from ..utils import nvtx
 from .config import LlamaConfig
 
@@ -84,6 +88,9 @@ class LlamaWeights:
             L["ln2"] = torch.ones(H, dtype=torch.bfloat16, device=dev)
             L["gate_up"] = col_parallel([F_, F_], H)
             L["down"] = row_parallel(H, F_)
+            if cfg.qk_norm:  # Qwen3 per-head q/k norms, identity at init
+                L["q_norm"] = torch.ones(D, dtype=torch.bfloat16, device=dev)
+                L["k_norm"] = torch.ones(D, dtype=torch.bfloat16, device=dev)
             self.layers.append(L)
         self.norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
         self.lm_head = col_parallel([cfg.vocab], H)
@@ -147,7 +154,12 @@ class LlamaTP:
         self.w = weights
         self.tp = tp
         self.tp_size = tp.world_size if tp is not None else 1
+        if impl not in ("native", "torch", "oracle"):
+            raise ValueError(f"impl {impl!r}: native | torch | oracle")
         self.impl = impl
+        # the elementwise / attention-side kernels: the CUDA ones, or their
+        # fp32 restatements for the oracle
+        self.k = oracle if impl == "oracle" else ops
         self.device = weights.embed.device
         self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, self.device,
                                         dict(cfg.rope_scaling) if cfg.rope_scaling else None)
@@ -166,6 +178,8 @@ class LlamaTP:
 
     # ------------------------------------------------------------ building blocks
     def _linear(self, x, w, out=None, residual=None):
+        if self.impl == "oracle":
+            return oracle.gemm(x, w, out=out, residual=residual)
         if self.impl == "torch":
             y = F.linear(x, w)
             if residual is not None:
@@ -179,6 +193,10 @@ class LlamaTP:
     def _all_reduce(self, x):
         if self.tp_size == 1:
             return x
+        if self.impl == "oracle":  # fp32 sum, one rounding (gloo has no bf16 sum on every build)
+            y = x.float()
+            dist.all_reduce(y, group=self.tp.group)
+            return x.copy_(y)
         if self.impl == "torch":
             dist.all_reduce(x, group=self.tp.group)
             return x
@@ -186,9 +204,9 @@ class LlamaTP:
 
     def _ar_norm(self, partial, residual, w, out=None):
         """residual <- residual + allreduce(partial); returns rmsnorm(residual)."""
-        if self.tp_size == 1 or self.impl == "torch":
+        if self.tp_size == 1 or self.impl != "native":
             x = self._all_reduce(partial)
-            return ops.fused_add_rmsnorm(x, residual, w, self.cfg.eps, out=out)
+            return self.k.fused_add_rmsnorm(x, residual, w, self.cfg.eps, out=out)
         return self.tp.all_reduce_rmsnorm(partial, residual, w, self.cfg.eps, out=out)
 
     def _qk_norm(self, qkv, L, nq, nkv, D):
@@ -208,7 +226,11 @@ class LlamaTP:
         if self.tp_size == 1:
             return logits.float()
         B = logits.shape[0]
-        if self.impl == "torch":
+        if self.impl == "oracle":
+            parts = [torch.empty_like(logits) for _ in range(self.tp_size)]
+            dist.all_gather(parts, logits.contiguous(), group=self.tp.group)
+            g = torch.stack(parts)
+        elif self.impl == "torch":
             g = torch.empty((self.tp_size,) + tuple(logits.shape), dtype=logits.dtype, device=logits.device)
             dist.all_gather_into_tensor(g, logits.contiguous(), group=self.tp.group)
         else:
@@ -218,9 +240,15 @@ class LlamaTP:
     def _lm_argmax(self, x_last):
         """Greedy next token from the vocab-parallel LM head."""
         logits = self._linear(x_last, self.w.lm_head)
-        vals, idx = ops.argmax(logits, offset=self.w.vocab_start)
+        vals, idx = self.k.argmax(logits, offset=self.w.vocab_start)
         if self.tp_size == 1:
             return idx
+        if self.impl == "oracle":
+            gv = [torch.empty_like(vals) for _ in range(self.tp_size)]
+            gi = [torch.empty_like(idx) for _ in range(self.tp_size)]
+            dist.all_gather(gv, vals, group=self.tp.group)
+            dist.all_gather(gi, idx, group=self.tp.group)
+            return oracle.argmax_combine(torch.stack(gv), torch.stack(gi))
         if self.impl == "torch":
             gv = torch.empty((self.tp_size,) + vals.shape, dtype=vals.dtype, device=vals.device)
             gi = torch.empty((self.tp_size,) + idx.shape, dtype=idx.dtype, device=idx.device)
@@ -252,10 +280,10 @@ class LlamaTP:
         if self.sp is not None and T >= self.sp_min_rows and self.sp.fits(T):
             return self._forward_sp(ids, positions, slots, kv_caches, attn, last_idx, return_hidden)
         nq, nkv, D = w.nq, w.nkv, cfg.head_dim
-        h = ops.embedding(ids, w.embed, start=w.vocab_start)
+        h = self.k.embedding(ids, w.embed, start=w.vocab_start)
         h = self._all_reduce(h)
         residual = h
-        x = ops.rmsnorm(residual, w.layers[0]["ln1"], cfg.eps)
+        x = self.k.rmsnorm(residual, w.layers[0]["ln1"], cfg.eps)
         for li, L in enumerate(w.layers):
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_push(f"layer {li}")
@@ -263,7 +291,7 @@ class LlamaTP:
             if cfg.qk_norm:
                 self._qk_norm(qkv, L, nq, nkv, D)
             kc, vc = kv_caches[li]
-            q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
+            q = self.k.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
             o = attn(li, q, kc, vc)
             if self.tp_size == 1 and self.impl == "native":
                 # residual add fused into the GEMM epilogue, in place
@@ -276,7 +304,7 @@ class LlamaTP:
                 part = self._linear(o.view(T, nq * D), L["o"])
                 x = self._ar_norm(part, residual, L["ln2"])
             gu = self._linear(x, L["gate_up"])
-            a = ops.silu_mul(gu)
+            a = self.k.silu_mul(gu)
             nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
             if self.tp_size == 1 and self.impl == "native":
                 self._linear(a, L["down"], out=residual, residual=residual)

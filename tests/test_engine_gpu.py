@@ -1,0 +1,95 @@
+"""The native engine (tcgen05 GEMMs, own attention and elementwise kernels,
+CUDA-graph decode) on the paths the CPU engine tests cover with the oracle
+model: greedy batches, prefix-cache hits, seeded sampling mixed with greedy
+requests, and the Qwen3 q/k norm. Each is checked against the dense fp32
+forward of ``test_engine_cpu`` over the same weights copied to the host."""
+import importlib
+import types
+
+import pytest
+import torch
+
+from test_engine_cpu import CFG, _cos, _dense, _prompt_hidden
+
+pytestmark = pytest.mark.gpu
+
+PKG = "3080_mod_p2p_sglang_patch_b200"
+models = importlib.import_module(f"{PKG}.models")
+eng_mod = importlib.import_module(f"{PKG}.engine")
+# the native attention rounds P to bf16 before the PV product; logits move more than the oracle's
+TOL = 0.1
+
+
+def _engine(cfg=CFG, **kw):
+    kw.setdefault("max_batch", 4)
+    kw.setdefault("max_seq", 512)
+    kw.setdefault("chunk", 64)
+    return eng_mod.LLMEngine(cfg, device="cuda", full_init=True, seed=0, **kw)
+
+
+def _host(w):
+    return types.SimpleNamespace(embed=w.embed.cpu(), norm=w.norm.cpu(), lm_head=w.lm_head.cpu(),
+                                 layers=[{k: v.cpu() for k, v in L.items()} for L in w.layers])
+
+
+def _near_argmax(cfg, w, prompt, out, tol=TOL):
+    seq = list(prompt)
+    for t in out:
+        _, logits = _dense(cfg, w, seq)
+        assert logits[-1][t] >= logits[-1].max() - tol, (len(seq) - len(prompt), t, int(logits[-1].argmax()))
+        seq.append(t)
+
+
+def test_native_engine_greedy_and_prefix_cache_follow_the_dense_forward():
+    eng = _engine(prefix_cache=True)
+    w = _host(eng.weights)
+    g = torch.Generator().manual_seed(11)
+    common = torch.randint(0, CFG.vocab, (48,), generator=g).tolist()
+    a = common + torch.randint(0, CFG.vocab, (30,), generator=g).tolist()
+    b = common + torch.randint(0, CFG.vocab, (9,), generator=g).tolist()
+    c = torch.randint(0, CFG.vocab, (100,), generator=g).tolist()
+    out_a, out_c = eng.generate([a, c], max_new_tokens=6)
+    req_b = eng.add_request(b, 6)
+    eng.run()
+    assert req_b.cached_pages == 3 and eng.prefix_cache.hits == 3
+    for p, o in ((a, out_a), (c, out_c), (b, req_b.output)):
+        assert len(o) == 6
+        _near_argmax(CFG, w, p, o)
+
+
+def test_native_engine_sampling_is_seeded_and_within_top_k():
+    SP = eng_mod.SamplingParams
+    g = torch.Generator().manual_seed(12)
+    p1, p2 = (torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (40, 70))
+    greedy_alone = _engine().generate([p2], max_new_tokens=5)[0]
+
+    def run(seed):
+        eng = _engine()
+        r1 = eng.add_request(p1, 8, sampling=SP(temperature=1.5, top_k=40, seed=seed))
+        r2 = eng.add_request(p2, 5)
+        eng.run()
+        return r1.output, r2.output, eng
+
+    s_a, greedy_mixed, eng = run(21)
+    s_b, _, _ = run(21)
+    assert s_a == s_b and len(s_a) == 8
+    assert greedy_mixed == greedy_alone
+    w = _host(eng.weights)
+    seq = list(p1)
+    for t in s_a:
+        _, logits = _dense(CFG, w, seq)
+        assert t in set(torch.topk(logits[-1], 40 + 4).indices.tolist())
+        seq.append(t)
+
+
+def test_native_qwen3_forward_matches_dense():
+    cfg = models.LlamaConfig(**{**CFG.__dict__, "name": "qwen3-tiny", "qk_norm": True})
+    eng = _engine(cfg, use_graphs=False)
+    g = torch.Generator().manual_seed(13)
+    for L in eng.weights.layers:
+        L["q_norm"].copy_((1 + 0.3 * torch.randn(cfg.head_dim, generator=g)).to(torch.bfloat16))
+        L["k_norm"].copy_((1 + 0.3 * torch.randn(cfg.head_dim, generator=g)).to(torch.bfloat16))
+    prompt = torch.randint(0, cfg.vocab, (90,), generator=g).tolist()
+    want, _ = _dense(cfg, _host(eng.weights), prompt)
+    got = _prompt_hidden(eng, prompt, 64).cpu()
+    assert _cos(got, want[-1]) > 0.995
