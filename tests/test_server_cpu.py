@@ -259,3 +259,36 @@ def test_module_entry_point_runs_as_main():
     r = subprocess.run([sys.executable, "-m", "3080_mod_p2p_sglang_patch_b200.server", "--model", "nope"],
                        capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
     assert r.returncode == 1 and "not a directory" in r.stderr
+
+
+def test_pp_bench_against_the_server(capsys):
+    """benchmarks/pp_bench.py (the reference's prefill benchmark method:
+    max_tokens=1, usage.prompt_tokens / wall) against the HTTP front end."""
+    import importlib.util
+
+    from conftest import free_port
+
+    spec = importlib.util.spec_from_file_location("pp_bench", os.path.join(ROOT, "benchmarks", "pp_bench.py"))
+    pp = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(pp)
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    try:
+        res = pp.main(["--url", f"http://127.0.0.1:{port}", "--sizes", "300,120", "--warmup", "50"])
+        assert [v["prompt_tokens"] for v in res.values()] == [300, 120]
+        assert all(v["pp_tok_s"] > 0 for v in res.values())
+        prompts = [p for _, p, _ in eng.log]
+        assert len(prompts) == 3 and len({p[:4] for p in prompts}) == 3   # salted: no shared prefix
+        assert all(m == 1 for _, _, m in eng.log)                          # max_tokens=1
+        out = capsys.readouterr().out
+        assert "SUMMARY " in out
+        pp.main(["--url", f"http://127.0.0.1:{port}", "--sizes", "200", "--warmup", "20", "--text"])
+        assert len(eng.log) == 5
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
