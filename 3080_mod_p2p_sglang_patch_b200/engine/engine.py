@@ -28,7 +28,7 @@ class LLMEngine:
     def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
-                 sp: bool = None, weights=None, prefix_cache: bool = False):
+                 sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None):
         if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
             use_graphs, prefill_graph = False, False
         self.cfg = cfg
@@ -57,6 +57,16 @@ class LLMEngine:
         self.max_blocks_per_seq = (max_seq + PAGE - 1) // PAGE
         if kv_blocks is None:
             kv_blocks = max_batch * self.max_blocks_per_seq + 1
+            if mem_fraction is not None and self.device.type == "cuda":
+                # weights + KV cache within mem_fraction of the device (the rest:
+                # activations, workspaces, CUDA graphs)
+                free, total = torch.cuda.mem_get_info(self.device)
+                block_bytes = PagedKVCache.bytes_per_token(cfg.layers, nkv, cfg.head_dim) * PAGE
+                fit = PagedKVCache.blocks_for_memory(total, free, mem_fraction, block_bytes)
+                if fit < self.max_blocks_per_seq:
+                    raise ValueError(f"mem_fraction {mem_fraction}: the KV cache would hold {fit * PAGE} tokens, "
+                                     f"fewer than max_seq {max_seq}")
+                kv_blocks = min(kv_blocks, fit + 1)
         self.kv = PagedKVCache(cfg.layers, nkv, cfg.head_dim, kv_blocks, self.device)
         # prefix caching: off by default (benchmarks must not reuse work)
         self.prefix_cache = PrefixCache(self.kv.alloc) if prefix_cache else None
@@ -99,6 +109,12 @@ class LLMEngine:
         cfg, w = load_llama(model_dir, tp.rank if tp is not None else 0, tp.world_size if tp is not None else 1, dev)
         kw.setdefault("max_seq", min(cfg.max_pos, 8192))
         return cls(cfg, tp=tp, device=dev, weights=w, **kw)
+
+    @property
+    def max_request_tokens(self) -> int:
+        """Longest prompt + max_new_tokens one request may have: max_seq, or
+        less if the KV cache is smaller than that."""
+        return min(self.max_seq, self.kv.alloc.capacity * PAGE)
 
     # ------------------------------------------------------------------ setup
     def _h2d(self, host: torch.Tensor) -> torch.Tensor:

@@ -16,11 +16,17 @@ PAGE = 16
 class BlockAllocator:
     def __init__(self, num_blocks: int, reserved: int = 1):
         self.num_blocks = num_blocks
+        self.reserved = reserved
         self._free = list(range(num_blocks - 1, reserved - 1, -1))
 
     @property
     def free(self) -> int:
         return len(self._free)
+
+    @property
+    def capacity(self) -> int:
+        """Blocks that can ever be handed out (all but the reserved ones)."""
+        return self.num_blocks - self.reserved
 
     def alloc(self, n: int):
         if n > len(self._free):
@@ -136,6 +142,14 @@ class PagedKVCache:
     @staticmethod
     def bytes_per_token(layers, kv_heads, head_dim, dtype_bytes=2):
         return layers * 2 * kv_heads * head_dim * dtype_bytes
+
+    @staticmethod
+    def blocks_for_memory(total_bytes: int, free_bytes: int, fraction: float, block_bytes: int) -> int:
+        """Blocks that fit when weights plus KV cache may use ``fraction`` of
+        the device's memory (sglang's ``--mem-fraction-static``): the budget
+        is fraction x total minus what is already in use."""
+        budget = fraction * total_bytes - (total_bytes - free_bytes)
+        return max(0, int(budget // block_bytes))
 
     def slots(self, blocks, start: int, n: int):
         """Cache slots (block*PAGE + offset) of token positions [start, start+n)."""

@@ -85,8 +85,13 @@ class Scheduler:
         self._free_slots = list(range(max_batch - 1, -1, -1))
 
     def add(self, req: Request):
-        if len(req.prompt) + req.max_new > self.max_seq:
+        n = len(req.prompt) + req.max_new
+        if n > self.max_seq:
             raise ValueError(f"request {req.rid}: {len(req.prompt)}+{req.max_new} tokens exceed max_seq {self.max_seq}")
+        if self.allocator is not None and (n + PAGE - 1) // PAGE > self.allocator.capacity:
+            # it would wait for room forever
+            raise ValueError(f"request {req.rid}: {n} tokens exceed the KV cache "
+                             f"({self.allocator.capacity * PAGE} tokens)")
         self.waiting.append(req)
 
     def has_work(self):

@@ -136,6 +136,8 @@ class EngineServer:
         p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
+        if isinstance(p.error, ValueError):  # the engine rejected the request itself
+            raise p.error
         if p.error is not None:
             raise RuntimeError(p.error)
         return (p.output, p.reason) if with_reason else p.output
@@ -162,9 +164,13 @@ class EngineServer:
     def _enqueue_check(self, prompt, max_new):
         if not prompt:
             raise ValueError("empty prompt")
-        if self.max_prompt is not None and len(prompt) + max_new > self.max_prompt:
+        limit = self.max_prompt
+        cap = getattr(self.engine, "max_request_tokens", None)
+        if isinstance(cap, int):
+            limit = cap if limit is None else min(limit, cap)
+        if limit is not None and len(prompt) + max_new > limit:
             raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
-                             f"max sequence {self.max_prompt}")
+                             f"max sequence {limit}")
 
     def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None):
         if self._stopped.is_set():
@@ -213,12 +219,18 @@ class EngineServer:
                     if c == self.SHUTDOWN:
                         stop = True
                         continue
-                    if c.sampling is None:
-                        req = eng.add_request(c.prompt, c.max_new, c.stop_ids)
-                    else:
-                        from .engine.sampling import SamplingParams
+                    try:
+                        if c.sampling is None:
+                            req = eng.add_request(c.prompt, c.max_new, c.stop_ids)
+                        else:
+                            from .engine.sampling import SamplingParams
 
-                        req = eng.add_request(c.prompt, c.max_new, c.stop_ids, SamplingParams(*c.sampling))
+                            req = eng.add_request(c.prompt, c.max_new, c.stop_ids, SamplingParams(*c.sampling))
+                    except ValueError as e:
+                        # rejected on every rank alike (same command, same engine
+                        # state): fail this request only
+                        c.finish(error=e)
+                        continue
                     c.req = req
                     self._by_rid[req.rid] = c
                     self.stats["requests"] += 1
@@ -466,6 +478,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
     ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
     ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
+    ap.add_argument("--mem-fraction-static", dest="mem_fraction", type=float, default=None,
+                    help="size the KV cache so weights + cache use this fraction of GPU memory "
+                         "(default: room for max-batch requests of max-seq tokens)")
     return ap
 
 
@@ -549,7 +564,7 @@ def main(argv=None):
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
     opts = dict(max_batch=args.max_batch, max_seq=args.max_seq, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
-                prefix_cache=args.prefix_cache)
+                prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction)
     tokenizer = None
     if model_path:
         eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, **opts)

@@ -7,6 +7,7 @@ directly over the weights (no cache, no chunks, no pages)."""
 import importlib
 import threading
 
+import pytest
 import torch
 import torch.nn.functional as F
 
@@ -239,3 +240,11 @@ def test_lockstep_server_with_real_engines_on_two_ranks():
         want = solo.generate([list(range(10 + i, 50 + 7 * i))], max_new_tokens=3 + i % 2)[0]
         if out != want:   # batching order may move a near-tie; otherwise exact
             _assert_near_argmax(CFG, solo.weights, list(range(10 + i, 50 + 7 * i)), out)
+
+
+def test_small_kv_cache_limits_request_length():
+    eng = _engine(kv_blocks=1 + 6)                           # 96 tokens of cache
+    assert eng.max_request_tokens == 96
+    with pytest.raises(ValueError, match="KV cache"):
+        eng.add_request(list(range(90)), 10)
+    assert eng.generate([list(range(80))], max_new_tokens=4)[0]   # fits: served

@@ -3,6 +3,7 @@ mapping, TP sharding into the engine's layout), on CPU tensors."""
 import importlib
 import json
 
+import pytest
 import torch
 
 models = importlib.import_module("3080_mod_p2p_sglang_patch_b200.models")
@@ -147,7 +148,6 @@ def test_qwen3_checkpoint_qk_norm(tmp_path):
 
 
 def test_unsupported_architecture_is_rejected():
-    import pytest
 
     with pytest.raises(ValueError):
         models.config_from_hf(dict(HF_CFG, architectures=["MixtralForCausalLM"]))
@@ -251,7 +251,6 @@ def test_awq_checkpoint_loads_dequantized_tp_shards(tmp_path):
 
 
 def test_awq_rejects_unsupported_configs_and_misaligned_shards(tmp_path):
-    import pytest
     loader = importlib.import_module("3080_mod_p2p_sglang_patch_b200.models.loader")
     assert loader.awq_group_size({"quant_method": "awq", "bits": 4, "group_size": 128}) == 128
     for qc in ({"quant_method": "gptq", "bits": 4}, {"quant_method": "awq", "bits": 8},

@@ -201,3 +201,23 @@ def test_prefix_cache_checks_tokens_not_just_hashes():
     s.add(r)
     s.next_batch()
     assert r.cached_pages == 0
+
+
+def test_request_larger_than_the_whole_kv_cache_is_rejected_not_queued():
+    alloc = kv_mod.BlockAllocator(num_blocks=1 + 4)          # 64 tokens of cache
+    s = sched_mod.Scheduler(chunk=64, max_batch=2, allocator=alloc, max_seq=1000)
+    assert alloc.capacity == 4
+    with pytest.raises(ValueError, match="KV cache"):
+        s.add(_req(0, 60, 20))                               # 80 tokens: it would wait forever
+    s.add(_req(1, 50, 14))                                   # exactly 64 tokens fits
+    assert len(s.waiting) == 1
+
+
+def test_kv_blocks_for_a_memory_fraction():
+    GB = 1 << 30
+    block = kv_mod.PagedKVCache.bytes_per_token(32, 8, 128) * PAGE       # 8B at TP=1: 2 MiB per page
+    assert block == 2 << 20
+    # 180 GB device, 16 GB already used by weights, weights + cache within 90 %
+    n = kv_mod.PagedKVCache.blocks_for_memory(180 * GB, 164 * GB, 0.9, block)
+    assert n == int((0.9 * 180 * GB - 16 * GB) // block)
+    assert kv_mod.PagedKVCache.blocks_for_memory(180 * GB, 10 * GB, 0.9, block) == 0   # nothing left

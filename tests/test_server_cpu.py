@@ -292,3 +292,41 @@ def test_pp_bench_against_the_server(capsys):
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+class _PickyEngine(FakeEngine):
+    """Rejects prompts that start with 999 the way the engine rejects a
+    request its KV cache can never hold."""
+
+    max_request_tokens = 64
+
+    def add_request(self, prompt, max_new, stop_ids=(), sampling=None):
+        if prompt and prompt[0] == 999:
+            raise ValueError("too large for the KV cache")
+        return super().add_request(prompt, max_new, stop_ids, sampling)
+
+
+def test_engine_rejection_fails_one_request_and_the_server_keeps_serving():
+    import requests
+
+    from conftest import free_port
+
+    eng = _PickyEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    url = f"http://127.0.0.1:{port}/v1/completions"
+    try:
+        r = requests.post(url, json={"prompt": [999, 1, 2], "max_tokens": 2}, timeout=60)
+        assert r.status_code == 400 and "KV cache" in r.text
+        r = requests.post(url, json={"prompt": list(range(1, 70)), "max_tokens": 2}, timeout=60)
+        assert r.status_code == 400                       # beyond max_request_tokens: refused up front
+        r = requests.post(url, json={"prompt": [5, 6], "max_tokens": 3}, timeout=60)
+        assert r.status_code == 200 and r.json()["choices"][0]["token_ids"] == expected([5, 6], 3)
+        assert loop.is_alive()
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
