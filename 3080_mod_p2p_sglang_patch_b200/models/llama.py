@@ -209,15 +209,12 @@ class LlamaTP:
             return self.k.fused_add_rmsnorm(x, residual, w, self.cfg.eps, out=out)
         return self.tp.all_reduce_rmsnorm(partial, residual, w, self.cfg.eps, out=out)
 
-    def _qk_norm(self, qkv, L, nq, nkv, D):
-        """Qwen3: RMSNorm over each head's D values of q and k, in place in the
-        fused qkv output (before RoPE). fp32 statistics, bf16 result."""
-        T = qkv.shape[0]
-        for lo, n, wgt in ((0, nq, L["q_norm"]), (nq * D, nkv, L["k_norm"])):
-            x = qkv[:, lo:lo + n * D].view(T, n, D)
-            xf = x.float()
-            y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * wgt.float()
-            x.copy_(y.to(qkv.dtype))
+    def _qk_norm_args(self, L):
+        """Qwen3's per-head q/k RMSNorm, applied by the RoPE kernel in the same
+        launch (empty for Llama)."""
+        if not self.cfg.qk_norm:
+            return {}
+        return {"q_norm": L["q_norm"], "k_norm": L["k_norm"], "eps": self.cfg.eps}
 
     def full_logits(self, x_last):
         """fp32 logits [B, V] over the whole vocabulary, identical on every
@@ -288,10 +285,8 @@ class LlamaTP:
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_push(f"layer {li}")
             qkv = self._linear(x, L["qkv"])
-            if cfg.qk_norm:
-                self._qk_norm(qkv, L, nq, nkv, D)
             kc, vc = kv_caches[li]
-            q = self.k.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
+            q = self.k.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc, **self._qk_norm_args(L))
             o = attn(li, q, kc, vc)
             if self.tp_size == 1 and self.impl == "native":
                 # residual add fused into the GEMM epilogue, in place
@@ -336,10 +331,8 @@ class LlamaTP:
         sp.rs_norm_ag(T, res, w.layers[0]["ln1"], cfg.eps)
         for li, L in enumerate(w.layers):
             qkv = sp.gemm_ag(T, L["qkv"])
-            if cfg.qk_norm:
-                self._qk_norm(qkv, L, nq, nkv, D)
             kc, vc = kv_caches[li]
-            q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc)
+            q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc, **self._qk_norm_args(L))
             o = attn(li, q, kc, vc)
             sp.gemm_rs(o.view(T, nq * D), L["o"])
             sp.rs_norm_ag(T, res, L["ln2"], cfg.eps)

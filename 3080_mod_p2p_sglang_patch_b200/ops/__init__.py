@@ -133,13 +133,17 @@ def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device, scaling=None
     return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
 
 
-def rope_and_cache(qkv, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v_cache=None, q_out=None, page=16):
+def rope_and_cache(qkv, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v_cache=None, q_out=None, page=16,
+                   q_norm=None, k_norm=None, eps=0.0):
     """Rotate q/k (neox), write rotated q to q_out [T, nq, 128] and k/v to the
-    paged cache at ``slots`` (int64 block*page+offset)."""
+    paged cache at ``slots`` (int64 block*page+offset). ``q_norm`` /
+    ``k_norm`` (bf16 [128]): Qwen3's per-head RMSNorm of q and k (epsilon
+    ``eps``) before the rotation, in the same launch."""
     T = qkv.shape[0]
     if q_out is None:
         q_out = torch.empty((T, nq, 128), dtype=qkv.dtype, device=qkv.device)
-    cuda_ext().rope_and_cache(qkv, positions, cos_sin, slots, q_out, k_cache, v_cache, nq, nkv, page)
+    cuda_ext().rope_and_cache(qkv, positions, cos_sin, slots, q_out, k_cache, v_cache, nq, nkv, page, q_norm, k_norm,
+                              float(eps))
     launches.add(1)
     return q_out
 

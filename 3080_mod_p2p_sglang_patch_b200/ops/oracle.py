@@ -42,13 +42,18 @@ def fused_add_rmsnorm(x, residual, w, eps, out=None):
     return _emit(y, x.dtype, out)
 
 
-def rope_and_cache(qkv, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v_cache=None, q_out=None, page=16):
+def rope_and_cache(qkv, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v_cache=None, q_out=None, page=16,
+                   q_norm=None, k_norm=None, eps=0.0):
     """Rotate q/k of the fused [T, (nq + 2 nkv) D] projection (neox halves),
-    store k/v at the paged ``slots`` (block * page + offset); returns q."""
+    store k/v at the paged ``slots`` (block * page + offset); returns q.
+    ``q_norm`` / ``k_norm``: per-head RMSNorm of q and k first (Qwen3), kept
+    in fp32 into the rotation."""
     T = qkv.shape[0]
     D = cos_sin.shape[1]
     q = qkv[:, :nq * D].view(T, nq, D)
     k = qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D)
+    if q_norm is not None:
+        q, k = ref.rmsnorm(q, q_norm, eps), ref.rmsnorm(k, k_norm, eps)
     v = qkv[:, (nq + nkv) * D:(nq + 2 * nkv) * D].view(T, nkv, D)
     qr = ref.rope(q, positions, cos_sin).to(qkv.dtype)
     if slots is not None:

@@ -181,7 +181,8 @@ void fused_add_rmsnorm(torch::Tensor x, torch::Tensor residual, torch::Tensor w,
 
 void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
                     c10::optional<torch::Tensor> slots, torch::Tensor q_out, c10::optional<torch::Tensor> k_cache,
-                    c10::optional<torch::Tensor> v_cache, int64_t nq, int64_t nkv, int64_t page) {
+                    c10::optional<torch::Tensor> v_cache, int64_t nq, int64_t nkv, int64_t page,
+                    c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double eps) {
   check_bf16(qkv, "qkv");
   check_bf16(q_out, "q_out");
   check_cuda(positions, "positions");
@@ -206,8 +207,19 @@ void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor co
     kc = k_cache->data_ptr();
     vc = v_cache->data_ptr();
   }
+  const void *qn = nullptr, *kn = nullptr;
+  TORCH_CHECK(q_norm.has_value() == k_norm.has_value(), "q_norm and k_norm go together");
+  if (q_norm.has_value()) {
+    check_bf16(*q_norm, "q_norm");
+    check_bf16(*k_norm, "k_norm");
+    TORCH_CHECK(q_norm->numel() == 128 && k_norm->numel() == 128 && q_norm->is_contiguous() &&
+                    k_norm->is_contiguous() && qkv.is_contiguous(),
+                "q_norm / k_norm must be contiguous [128] (and qkv contiguous)");
+    qn = q_norm->data_ptr();
+    kn = k_norm->data_ptr();
+  }
   rope_and_cache_launch(qkv.data_ptr(), positions.data_ptr<int>(), cos_sin.data_ptr<float>(), sp, q_out.data_ptr(), kc,
-                        vc, T, (int)nq, (int)nkv, (int)page, cur_stream());
+                        vc, T, (int)nq, (int)nkv, (int)page, cur_stream(), qn, kn, (float)eps);
 }
 
 void silu_mul(torch::Tensor x, torch::Tensor out) {

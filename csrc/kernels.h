@@ -39,8 +39,11 @@ void raw_transport_launch(int kind, void* dst, const void* src, uint64_t nbytes,
 // ---- elementwise (ops/elementwise.cu) ----------------------------------------
 void rmsnorm_launch(const void* x, void* residual, const void* w, void* out, int64_t M, int H, float eps,
                     cudaStream_t s);
+// q_norm / k_norm (bf16 [128], both or neither): Qwen3's per-head RMSNorm of
+// q and k, applied before the rotation in the same launch.
 void rope_and_cache_launch(const void* qkv, const int* pos, const float* cos_sin, const int64_t* slots, void* q_out,
-                           void* k_cache, void* v_cache, int64_t T, int nq, int nkv, int page, cudaStream_t s);
+                           void* k_cache, void* v_cache, int64_t T, int nq, int nkv, int page, cudaStream_t s,
+                           const void* q_norm = nullptr, const void* k_norm = nullptr, float eps = 0.f);
 void silu_mul_launch(const void* x, void* out, int64_t M, int I2, cudaStream_t s);
 void embedding_launch(const int* ids, const void* table, void* out, int64_t T, int H, int64_t start, int64_t rows,
                       cudaStream_t s);

@@ -113,6 +113,56 @@ __global__ void rope_and_cache_kernel(const __nv_bfloat16* __restrict__ qkv, con
   }
 }
 
+// Qwen3: per-head RMSNorm of q and k (weights q_norm / k_norm [D], fp32
+// statistics, one rounding after the rotation) fused in front of the NeoX
+// rotation, then the stores of rope_and_cache_kernel. One warp per head:
+// lane l holds elements 2l, 2l+1 and their rotation partners 2l+64, 2l+65, so
+// a head's sum of squares is one warp reduction and the rotation stays in the
+// lane. v is copied unnormalised (the model norms q and k only).
+__global__ void rope_qknorm_cache_kernel(const __nv_bfloat16* __restrict__ qkv, const int* __restrict__ pos,
+                                         const float* __restrict__ cos_sin, const int64_t* __restrict__ slots,
+                                         const __nv_bfloat16* __restrict__ q_norm,
+                                         const __nv_bfloat16* __restrict__ k_norm, float eps,
+                                         __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
+                                         __nv_bfloat16* __restrict__ v_cache, int nq, int nkv, int page) {
+  constexpr int D = 128, H2 = 64;
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const float* cs = cos_sin + (int64_t)pos[t] * D;  // [cos(H2) | sin(H2)]
+  const __nv_bfloat16* row = qkv + (int64_t)t * (nq + 2 * nkv) * D;
+  const int64_t slot = slots ? slots[t] : -1;
+  const int64_t blk = slot >= 0 ? slot / page : 0, off = slot >= 0 ? slot % page : 0;
+  const int j = 2 * lane;
+  const float c0 = cs[j], c1 = cs[j + 1], s0 = cs[H2 + j], s1 = cs[H2 + j + 1];
+  // k heads only feed the cache: without slots the warps stop after the q heads
+  const int heads = slot >= 0 ? nq + nkv : nq;
+  for (int h = warp; h < heads; h += nwarps) {
+    const __nv_bfloat16* src = row + h * D;
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + H2 + j));
+    float ss = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss * (1.f / D) + eps);
+    const __nv_bfloat16* w = h < nq ? q_norm : k_norm;
+    const float a0 = a.x * r * __bfloat162float(w[j]), a1 = a.y * r * __bfloat162float(w[j + 1]);
+    const float b0 = b.x * r * __bfloat162float(w[H2 + j]), b1 = b.y * r * __bfloat162float(w[H2 + j + 1]);
+    __nv_bfloat16* dst = h < nq ? q_out + ((int64_t)t * nq + h) * D
+                                : k_cache + ((blk * nkv + (h - nq)) * page + off) * D;
+    *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(a0 * c0 - b0 * s0, a1 * c1 - b1 * s1);
+    *reinterpret_cast<__nv_bfloat162*>(dst + H2 + j) = __floats2bfloat162_rn(b0 * c0 + a0 * s0, b1 * c1 + a1 * s1);
+  }
+  if (slot >= 0) {
+    const uint4* vsrc = reinterpret_cast<const uint4*>(row + (nq + nkv) * D);
+    constexpr int PV = D / 8;
+    for (int i = threadIdx.x; i < nkv * PV; i += blockDim.x) {
+      const int kh = i / PV, jj = i % PV;
+      uint4* dst = reinterpret_cast<uint4*>(v_cache + ((blk * nkv + kh) * page + off) * D);
+      dst[jj] = vsrc[kh * PV + jj];
+    }
+  }
+}
+
 // out[m, j] = silu(x[m, j]) * x[m, I + j]
 __global__ void silu_mul_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, int ivec) {
   const int64_t row = blockIdx.y;
@@ -231,11 +281,18 @@ void rmsnorm_launch(const void* x, void* residual, const void* w, void* out, int
 }
 
 void rope_and_cache_launch(const void* qkv, const int* pos, const float* cos_sin, const int64_t* slots, void* q_out,
-                           void* k_cache, void* v_cache, int64_t T, int nq, int nkv, int page, cudaStream_t s) {
+                           void* k_cache, void* v_cache, int64_t T, int nq, int nkv, int page, cudaStream_t s,
+                           const void* q_norm, const void* k_norm, float eps) {
   if (T == 0) return;
-  rope_and_cache_kernel<128><<<(unsigned)T, 256, 0, s>>>(
-      (const __nv_bfloat16*)qkv, pos, cos_sin, slots, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache,
-      (__nv_bfloat16*)v_cache, nq, nkv, page);
+  if (q_norm != nullptr) {
+    rope_qknorm_cache_kernel<<<(unsigned)T, 256, 0, s>>>(
+        (const __nv_bfloat16*)qkv, pos, cos_sin, slots, (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm,
+        eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, nq, nkv, page);
+  } else {
+    rope_and_cache_kernel<128><<<(unsigned)T, 256, 0, s>>>(
+        (const __nv_bfloat16*)qkv, pos, cos_sin, slots, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache,
+        (__nv_bfloat16*)v_cache, nq, nkv, page);
+  }
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -130,21 +130,30 @@ def test_qwen3_checkpoint_qk_norm(tmp_path):
     (tmp_path / "config.json").write_text(json.dumps(cfg_json))
     cfg, w = models.load_llama(str(tmp_path), 1, 2, "cpu")
     assert cfg.qk_norm and torch.equal(w.layers[1]["q_norm"], extra["model.layers.1.self_attn.q_norm.weight"])
-    model = models.LlamaTP(cfg, w, tp=None, impl="native")
+    model = models.LlamaTP(cfg, w, tp=None, impl="oracle")
     nq, nkv, D = w.nq, w.nkv, 128
+    args = model._qk_norm_args(w.layers[1])
+    assert args["q_norm"] is w.layers[1]["q_norm"] and args["k_norm"] is w.layers[1]["k_norm"]
+    # the RoPE step applies the norm: q and cached k are rope(rmsnorm(head)), v is copied as is
     qkv = torch.randn(5, (nq + 2 * nkv) * D, generator=g).to(torch.bfloat16)
-    before = qkv.clone()
-    model._qk_norm(qkv, w.layers[1], nq, nkv, D)
+    pos = torch.arange(5, dtype=torch.int32)
+    cs = ops.rope_cos_sin(64, D, cfg.rope_theta, "cpu")
+    kc = torch.zeros(2, nkv, 16, D, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.arange(16, 21, dtype=torch.int64)
+    q = model.k.rope_and_cache(qkv, pos, cs, nq, nkv, slots, kc, vc, **args)
 
     def rms(x, wt):
         xf = x.float()
-        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg.eps) * wt.float()).to(torch.bfloat16)
+        return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + cfg.eps) * wt.float()
 
-    q = before[:, :nq * D].view(5, nq, D)
-    k = before[:, nq * D:(nq + nkv) * D].view(5, nkv, D)
-    assert torch.equal(qkv[:, :nq * D].view(5, nq, D), rms(q, w.layers[1]["q_norm"]))
-    assert torch.equal(qkv[:, nq * D:(nq + nkv) * D].view(5, nkv, D), rms(k, w.layers[1]["k_norm"]))
-    assert torch.equal(qkv[:, (nq + nkv) * D:], before[:, (nq + nkv) * D:])  # v untouched
+    ref = importlib.import_module("3080_mod_p2p_sglang_patch_b200.ops.reference")
+    want_q = ref.rope(rms(qkv[:, :nq * D].view(5, nq, D), w.layers[1]["q_norm"]), pos, cs).to(torch.bfloat16)
+    want_k = ref.rope(rms(qkv[:, nq * D:(nq + nkv) * D].view(5, nkv, D), w.layers[1]["k_norm"]), pos, cs)
+    assert torch.equal(q, want_q)
+    assert torch.equal(kc[1, :, :5, :].permute(1, 0, 2), want_k.to(torch.bfloat16))
+    assert torch.equal(vc[1, :, :5, :].permute(1, 0, 2), qkv[:, (nq + nkv) * D:].view(5, nkv, D))
+    assert "q_norm" not in models.LlamaTP(models.config_from_hf(HF_CFG), w, impl="oracle")._qk_norm_args(w.layers[1])
 
 
 def test_unsupported_architecture_is_rejected():

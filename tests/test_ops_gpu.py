@@ -50,6 +50,33 @@ def test_rope_and_paged_cache_write():
     assert torch.equal(vc[blk, :, off, :], v_ref)
 
 
+def test_rope_with_qk_norm_and_paged_cache_write():
+    """Qwen3's per-head q/k RMSNorm fused into the RoPE + cache-write kernel,
+    against the fp32 reference: rope(rmsnorm(head) * w); v copied as is."""
+    ops, ref = sub("ops"), sub("ops.reference")
+    torch.manual_seed(1)
+    T, nq, nkv, D, page, eps = 37, 16, 4, 128, 16, 1e-6
+    cs = ops.rope_cos_sin(4096, D, 1000000.0, "cuda")
+    qkv = (3 * torch.randn(T, (nq + 2 * nkv) * D, device="cuda")).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), device="cuda", dtype=torch.int32)
+    qw = (1 + 0.3 * torch.randn(D, device="cuda")).to(torch.bfloat16)
+    kw = (1 + 0.3 * torch.randn(D, device="cuda")).to(torch.bfloat16)
+    blocks = 6
+    kc = torch.zeros(blocks, nkv, page, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(blocks * page, device="cuda")[:T].to(torch.int64)
+    q = ops.rope_and_cache(qkv, pos, cs, nq, nkv, slots, kc, vc, q_norm=qw, k_norm=kw, eps=eps)
+    q_ref = ref.rope(ref.rmsnorm(qkv[:, :nq * D].view(T, nq, D), qw, eps), pos, cs)
+    k_ref = ref.rope(ref.rmsnorm(qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D), kw, eps), pos, cs)
+    assert (q.float() - q_ref).abs().max().item() < 3e-2
+    blk, off = slots // page, slots % page
+    assert (kc[blk, :, off, :].float() - k_ref).abs().max().item() < 3e-2
+    assert torch.equal(vc[blk, :, off, :], qkv[:, (nq + nkv) * D:].view(T, nkv, D))
+    # without slots (no cache given) the kernel produces the same q
+    q2 = ops.rope_and_cache(qkv, pos, cs, nq, nkv, q_norm=qw, k_norm=kw, eps=eps)
+    assert torch.equal(q2, q)
+
+
 def test_vocab_parallel_embedding():
     ops = sub("ops")
     table = torch.randn(1000, 256, device="cuda").to(torch.bfloat16)
