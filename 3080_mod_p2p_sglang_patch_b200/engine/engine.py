@@ -31,6 +31,9 @@ class LLMEngine:
                  sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None):
         if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
             use_graphs, prefill_graph = False, False
+        if max_seq > cfg.max_pos:
+            # positions index the RoPE table, which has max_pos rows
+            raise ValueError(f"max_seq {max_seq} exceeds the model's {cfg.max_pos} positions")
         self.cfg = cfg
         self.tp = tp
         self.impl = impl

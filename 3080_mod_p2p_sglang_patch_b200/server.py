@@ -473,7 +473,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8001)
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
-    ap.add_argument("--max-seq", "--context-length", dest="max_seq", type=int, default=16384)
+    ap.add_argument("--max-seq", "--context-length", dest="max_seq", type=int, default=None,
+                    help="longest prompt + generation (default: the model's positions, at most 16384 with "
+                         "random weights, 8192 with a checkpoint)")
     ap.add_argument("--chunk", "--chunked-prefill-size", dest="chunk", type=int, default=1024)
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
     ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
@@ -562,9 +564,11 @@ def main(argv=None):
     # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow
     tp = par.TPGroup(None, dev, use_mailbox=None) if world > 1 else None
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
-    opts = dict(max_batch=args.max_batch, max_seq=args.max_seq, chunk=args.chunk, use_graphs=not args.no_graphs,
+    opts = dict(max_batch=args.max_batch, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
                 prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction)
+    if args.max_seq is not None:
+        opts["max_seq"] = args.max_seq
     tokenizer = None
     if model_path:
         eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, **opts)
@@ -575,9 +579,10 @@ def main(argv=None):
             logger.warning("no tokenizer in %s (%s); using the byte tokenizer", model_path, e)
     else:
         cfg = models.LlamaConfig.by_name(name)
+        opts.setdefault("max_seq", min(16384, cfg.max_pos))
         eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, **opts)
     stop = models.stop_token_ids(model_path) if model_path else ()
-    server = EngineServer(eng, ctrl, rank, world, max_prompt=args.max_seq, stop_ids=stop)
+    server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop)
     http = None
     if rank == 0:
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step

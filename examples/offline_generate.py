@@ -36,7 +36,7 @@ def main():
     dev = torch.device("cuda", local)
     tp = par.TPGroup(None, dev) if world > 1 else None  # MailboxAR when SGLANG_MAILBOX_AR=1, else NCCL
     if args.model_path:
-        eng = eng_mod.LLMEngine.from_pretrained(args.model_path, tp=tp, device=dev, max_batch=4, max_seq=4096)
+        eng = eng_mod.LLMEngine.from_pretrained(args.model_path, tp=tp, device=dev, max_batch=4)
         tok = server.HFTokenizer(args.model_path)
         stop = models.stop_token_ids(args.model_path)
     else:

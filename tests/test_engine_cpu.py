@@ -248,3 +248,11 @@ def test_small_kv_cache_limits_request_length():
     with pytest.raises(ValueError, match="KV cache"):
         eng.add_request(list(range(90)), 10)
     assert eng.generate([list(range(80))], max_new_tokens=4)[0]   # fits: served
+
+
+def test_max_seq_beyond_the_models_positions_is_refused():
+    """Positions index the RoPE table (max_pos rows): an engine that could
+    be asked for later positions must not start."""
+    with pytest.raises(ValueError, match="positions"):
+        _engine(max_seq=CFG.max_pos + 1)
+    assert _engine(max_seq=CFG.max_pos).max_seq == CFG.max_pos
