@@ -158,7 +158,10 @@ class LLMEngine:
         a SamplingParams (None = greedy); a seeded one draws from its own
         generator, an unseeded one from the engine's (seeded identically on
         every TP rank, so all ranks draw the same tokens)."""
-        req = Request(self._next_rid, list(prompt), max_new_tokens, t_arrive=time.perf_counter(),
+        prompt = list(prompt)
+        if prompt and (min(prompt) < 0 or max(prompt) >= self.cfg.vocab):
+            raise ValueError(f"prompt token ids must lie in [0, {self.cfg.vocab})")
+        req = Request(self._next_rid, prompt, max_new_tokens, t_arrive=time.perf_counter(),
                       stop_ids=tuple(int(t) for t in stop_ids), sampling=sampling)
         if sampling is not None and not sampling.greedy and sampling.seed is not None:
             req.rng = torch.Generator(device=self.device)

@@ -85,6 +85,8 @@ class Scheduler:
         self._free_slots = list(range(max_batch - 1, -1, -1))
 
     def add(self, req: Request):
+        if not req.prompt or req.max_new < 1:
+            raise ValueError(f"request {req.rid}: needs a prompt and max_new >= 1")
         n = len(req.prompt) + req.max_new
         if n > self.max_seq:
             raise ValueError(f"request {req.rid}: {len(req.prompt)}+{req.max_new} tokens exceed max_seq {self.max_seq}")

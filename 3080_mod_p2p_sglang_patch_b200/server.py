@@ -164,6 +164,11 @@ class EngineServer:
     def _enqueue_check(self, prompt, max_new):
         if not prompt:
             raise ValueError("empty prompt")
+        if max_new < 1:
+            raise ValueError("max_tokens must be at least 1")
+        vocab = getattr(getattr(self.engine, "cfg", None), "vocab", None)
+        if isinstance(vocab, int) and (min(prompt) < 0 or max(prompt) >= vocab):
+            raise ValueError(f"prompt token ids must lie in [0, {vocab})")
         limit = self.max_prompt
         cap = getattr(self.engine, "max_request_tokens", None)
         if isinstance(cap, int):

@@ -256,3 +256,11 @@ def test_max_seq_beyond_the_models_positions_is_refused():
     with pytest.raises(ValueError, match="positions"):
         _engine(max_seq=CFG.max_pos + 1)
     assert _engine(max_seq=CFG.max_pos).max_seq == CFG.max_pos
+
+
+def test_out_of_vocabulary_prompt_ids_are_refused():
+    eng = _engine()
+    for bad in ([1, CFG.vocab], [-1, 5]):
+        with pytest.raises(ValueError, match="token ids"):
+            eng.add_request(bad, 2)
+    assert not eng.sched.has_work()

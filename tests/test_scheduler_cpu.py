@@ -221,3 +221,10 @@ def test_kv_blocks_for_a_memory_fraction():
     n = kv_mod.PagedKVCache.blocks_for_memory(180 * GB, 164 * GB, 0.9, block)
     assert n == int((0.9 * 180 * GB - 16 * GB) // block)
     assert kv_mod.PagedKVCache.blocks_for_memory(180 * GB, 10 * GB, 0.9, block) == 0   # nothing left
+
+
+def test_request_needs_a_prompt_and_a_positive_budget():
+    s = sched_mod.Scheduler(chunk=64, max_batch=2)
+    for prompt, max_new in (([], 4), ([1, 2], 0), ([1, 2], -3)):
+        with pytest.raises(ValueError):
+            s.add(sched_mod.Request(rid=0, prompt=prompt, max_new=max_new))

@@ -323,6 +323,11 @@ def test_engine_rejection_fails_one_request_and_the_server_keeps_serving():
         assert r.status_code == 400 and "KV cache" in r.text
         r = requests.post(url, json={"prompt": list(range(1, 70)), "max_tokens": 2}, timeout=60)
         assert r.status_code == 400                       # beyond max_request_tokens: refused up front
+        r = requests.post(url, json={"prompt": [5, 6], "max_tokens": 0}, timeout=60)
+        assert r.status_code == 400                       # nothing to generate
+        eng.cfg = type("Cfg", (), {"vocab": 100})()
+        r = requests.post(url, json={"prompt": [5, 100], "max_tokens": 2}, timeout=60)
+        assert r.status_code == 400 and "token ids" in r.text
         r = requests.post(url, json={"prompt": [5, 6], "max_tokens": 3}, timeout=60)
         assert r.status_code == 200 and r.json()["choices"][0]["token_ids"] == expected([5, 6], 3)
         assert loop.is_alive()
