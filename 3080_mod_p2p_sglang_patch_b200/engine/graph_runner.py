@@ -27,6 +27,9 @@ class DecodeGraphRunner:
         self.in_slots = torch.zeros(n, dtype=torch.int64, device=dev)
         self.host_i32 = torch.zeros(4 * n, dtype=torch.int32).pin_memory()
         self.host_slots = torch.zeros(n, dtype=torch.int64).pin_memory()
+        # completion of the last host->device copy out of the pinned buffers:
+        # they are rewritten only after it (copies are asynchronous)
+        self._copied = None
         self.graphs = {}
         self.outputs = {}
         self.kernels = {}
@@ -85,6 +88,8 @@ class DecodeGraphRunner:
         n = self.max_bs
         h = self.host_i32
         pad = bs - B
+        if self._copied is not None:
+            self._copied.synchronize()
         h[0:bs] = torch.tensor(ids + [0] * pad, dtype=torch.int32)
         h[n:n + bs] = torch.tensor(pos + [0] * pad, dtype=torch.int32)
         h[2 * n:2 * n + bs] = torch.tensor(kv_len + [1] * pad, dtype=torch.int32)
@@ -92,6 +97,9 @@ class DecodeGraphRunner:
         self.host_slots[:bs] = torch.tensor(slots + [0] * pad, dtype=torch.int64)
         self.in_i32.copy_(h, non_blocking=True)
         self.in_slots.copy_(self.host_slots, non_blocking=True)
+        if self._copied is None:
+            self._copied = torch.cuda.Event()
+        self._copied.record()
         self.graphs[bs].replay()
         launches.add(self.kernels.get(bs, 0))
         return self.outputs[bs][:B]
