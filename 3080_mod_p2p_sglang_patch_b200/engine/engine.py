@@ -292,7 +292,14 @@ class LLMEngine:
 
     def _step(self, batch):
         if batch.kind == "prefill":
-            nxt = self._run_prefill(batch).tolist()
+            out = self._run_prefill(batch)
+            if any(p.completes for p in batch.pieces):
+                nxt = out.tolist()
+            else:
+                # no prompt ends in this chunk, so no token is used: skip the
+                # device->host read (a sync), and the host prepares the next
+                # chunk while this one runs
+                nxt = [0] * len(batch.pieces)
             now = time.perf_counter()
             for p in batch.pieces:
                 if p.completes:

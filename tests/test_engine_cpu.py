@@ -264,3 +264,24 @@ def test_out_of_vocabulary_prompt_ids_are_refused():
         with pytest.raises(ValueError, match="token ids"):
             eng.add_request(bad, 2)
     assert not eng.sched.has_work()
+
+
+def test_prefill_chunks_that_end_no_prompt_are_not_read_back():
+    """Only a chunk that completes a prompt produces a used token; the engine
+    reads back (synchronises on) those chunks only."""
+    eng = _engine(chunk=32)
+    reads = []
+    run = eng._run_prefill
+
+    class _Spy:
+        def __init__(self, t, batch):
+            self.t, self.batch = t, batch
+
+        def tolist(self):
+            reads.append([p.completes for p in self.batch.pieces])
+            return self.t.tolist()
+
+    eng._run_prefill = lambda batch: _Spy(run(batch), batch)
+    out = eng.generate([list(range(1, 101))], max_new_tokens=2)[0]   # 100 tokens: 4 chunks of 32
+    assert len(reads) == 1 and reads[0] == [True] and len(out) == 2
+    _assert_near_argmax(CFG, eng.weights, list(range(1, 101)), out)
