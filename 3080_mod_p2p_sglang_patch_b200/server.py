@@ -475,6 +475,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--model-path", default=None, help="Hugging Face checkpoint directory (safetensors)")
     ap.add_argument("--tp", "--tp-size", dest="tp", type=int, default=None,
                     help="tensor-parallel ranks (one GPU each); started here unless launched by torchrun")
+    ap.add_argument("--dp", "--dp-size", dest="dp", type=int, default=1,
+                    help="data-parallel replicas, each a TP group on its own GPUs, behind one router")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8001)
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
@@ -504,19 +506,45 @@ def resolve_model(args):
     raise SystemExit(f"--model {args.model!r}: not a directory and not one of {', '.join(RANDOM_MODELS)}")
 
 
-def relaunch_command(argv, tp: int, port: int):
-    """The torch.distributed.run command that starts ``tp`` ranks of this
-    server with ``argv`` minus its ``--tp`` / ``--tp-size`` option."""
+def _strip_options(argv, names):
+    """``argv`` without the options in ``names`` (``--x v`` and ``--x=v``)."""
     rest, skip = [], False
     for a in argv:
         if skip:
             skip = False
-        elif a in ("--tp", "--tp-size"):
+        elif a in names:
             skip = True
-        elif not a.startswith(("--tp=", "--tp-size=")):
+        elif not a.startswith(tuple(n + "=" for n in names)):
             rest.append(a)
+    return rest
+
+
+def relaunch_command(argv, tp: int, port: int):
+    """The torch.distributed.run command that starts ``tp`` ranks of this
+    server with ``argv`` minus its ``--tp`` / ``--tp-size`` option."""
+    rest = _strip_options(argv, ("--tp", "--tp-size"))
     return [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={tp}",
             "--master-addr=127.0.0.1", f"--master-port={port}", "-m", f"{_package()}.server", *rest]
+
+
+def replica_commands(argv, tp: int, dp: int, port: int, visible=None):
+    """(environment overrides, command) of each data-parallel replica:
+    replica i serves on 127.0.0.1:port + 1 + i over GPUs [i*tp, (i+1)*tp) of
+    ``visible`` (the devices this process may use)."""
+    gpus = list(visible) if visible is not None else [str(g) for g in range(tp * dp)]
+    if len(gpus) < tp * dp:
+        raise SystemExit(f"--dp {dp} x --tp {tp} needs {tp * dp} GPUs, {len(gpus)} visible")
+    rest = _strip_options(argv, ("--dp", "--dp-size", "--port", "--host", "--tp", "--tp-size"))
+    out = []
+    for i in range(dp):
+        env = {"CUDA_VISIBLE_DEVICES": ",".join(gpus[i * tp:(i + 1) * tp])}
+        args_i = rest + ["--host", "127.0.0.1", "--port", str(port + 1 + i)]
+        if tp > 1:
+            cmd = relaunch_command(args_i, tp, _free_port())
+        else:
+            cmd = [sys.executable, "-m", f"{_package()}.server", *args_i]
+        out.append((env, cmd))
+    return out
 
 
 def _package() -> str:
@@ -540,6 +568,31 @@ def _run_ranks(cmd) -> int:
     return proc.wait()
 
 
+def _run_replicas(argv, args) -> int:
+    """``--dp N``: N replicas (each its own TP group and GPUs) plus the
+    data-parallel router on --host:--port in this process."""
+    from .router import Router, build_router_app
+
+    tp = args.tp or 1
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    visible = [v for v in vis.split(",") if v] if vis else None
+    if visible is None:
+        import torch
+
+        visible = [str(g) for g in range(torch.cuda.device_count())]
+    procs = []
+    for env, cmd in replica_commands(argv, tp, args.dp, args.port, visible):
+        procs.append(subprocess.Popen(cmd, env={**os.environ, **env}))
+    for sig in (signal.SIGINT, signal.SIGTERM):
+        signal.signal(sig, lambda signum, _: [p.send_signal(signum) for p in procs])
+    router = Router([f"http://127.0.0.1:{args.port + 1 + i}" for i in range(args.dp)])
+    http, _ = start_http(build_router_app(router), args.host, args.port)
+    logger.info("data-parallel router at http://%s:%d over %d replicas of TP=%d", args.host, args.port, args.dp, tp)
+    codes = [p.wait() for p in procs]
+    http.should_exit = True
+    return max(codes, key=abs)
+
+
 def main(argv=None):
     import importlib
 
@@ -551,6 +604,13 @@ def main(argv=None):
         raise SystemExit("--tp must be >= 1")
     if in_torchrun and args.tp is not None and args.tp != int(os.environ["WORLD_SIZE"]):
         raise SystemExit(f"--tp {args.tp} but torchrun started {os.environ['WORLD_SIZE']} ranks")
+    if args.dp < 1:
+        raise SystemExit("--dp must be >= 1")
+    if args.dp > 1:
+        if in_torchrun:
+            raise SystemExit("--dp starts its own replicas: launch it without torchrun")
+        logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
+        raise SystemExit(_run_replicas(argv, args))
     if not in_torchrun and (args.tp or 1) > 1:
         raise SystemExit(_run_ranks(relaunch_command(argv, args.tp, _free_port())))
 
