@@ -213,12 +213,17 @@ def _lockstep(rank, world):
 
         threading.Thread(target=clients, daemon=True).start()
     server.serve_forever()
-    return {"log": sorted(eng.log), "results": results}
+    return {"log": sorted(eng.log), "results": results, "stats": dict(server.stats)}
 
 
 def test_lockstep_two_ranks():
     res = run_ranks(_lockstep, 2)
     assert res[0]["log"] == res[1]["log"] and len(res[0]["log"]) == 6
+    # busy steps exchanged the command count over shared memory; gloo carried
+    # only payloads and idle waits (same sequence on both ranks)
+    st0, st1 = res[0]["stats"], res[1]["stats"]
+    assert st0["control_shm"] > 0 and st0["control_shm"] == st1["control_shm"]
+    assert st0["control_gloo"] == st1["control_gloo"] and st0["control_gloo"] <= 6 + 2
     for i, out in res[0]["results"].items():
         assert out == expected([i, i + 1], 3 + i % 3)
 
