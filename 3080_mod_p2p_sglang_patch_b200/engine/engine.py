@@ -239,11 +239,16 @@ class LLMEngine:
         return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d, return_hidden=return_hidden)
 
     def decode_inputs(self, reqs):
-        ids = [r.output[-1] if r.output else r.prompt[-1] for r in reqs]
-        pos = [r.total_len - 1 for r in reqs]
-        kv_len = [r.total_len for r in reqs]
-        slots = [r.blocks[(r.total_len - 1) // PAGE] * PAGE + (r.total_len - 1) % PAGE for r in reqs]
-        rows = [r.slot for r in reqs]
+        """(last token, position, kv length, cache slot, table row) per request."""
+        ids, pos, kv_len, slots, rows = [], [], [], [], []
+        for r in reqs:  # one pass: this runs every decode step
+            out = r.output
+            n = len(r.prompt) + len(out)
+            ids.append(out[-1] if out else r.prompt[-1])
+            pos.append(n - 1)
+            kv_len.append(n)
+            slots.append(r.blocks[(n - 1) // PAGE] * PAGE + (n - 1) % PAGE)
+            rows.append(r.slot)
         return ids, pos, kv_len, slots, rows
 
     def forward_decode_eager(self, ids_d, pos_d, kvl_d, slots_d, rows_d, splits=None, return_hidden=False):

@@ -131,7 +131,6 @@ def test_sampling_is_seeded_and_leaves_greedy_requests_alone():
     SP = eng_mod.SamplingParams
     g = torch.Generator().manual_seed(4)
     p1, p2 = (torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (40, 25))
-    greedy_alone = _engine().generate([p2], max_new_tokens=5)[0]
 
     def run(seed):
         eng = _engine()
@@ -144,7 +143,9 @@ def test_sampling_is_seeded_and_leaves_greedy_requests_alone():
     s7b, _, _ = run(7)
     s8, _, _ = run(8)
     assert s7a == s7b and s7a != s8 and len(s7a) == 8
-    assert greedy_mixed == greedy_alone
+    # the greedy request stays greedy next to a sampled one (batches and chunks
+    # differ from a solo run, so compare with the dense argmax, not token for token)
+    _assert_near_argmax(CFG, eng.weights, p2, greedy_mixed)
     seq = list(p1)
     for t in s7a:                                          # every draw is inside the top 40
         _, logits = _dense(CFG, eng.weights, seq)

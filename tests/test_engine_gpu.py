@@ -61,7 +61,6 @@ def test_native_engine_sampling_is_seeded_and_within_top_k():
     SP = eng_mod.SamplingParams
     g = torch.Generator().manual_seed(12)
     p1, p2 = (torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (40, 70))
-    greedy_alone = _engine().generate([p2], max_new_tokens=5)[0]
 
     def run(seed):
         eng = _engine()
@@ -73,8 +72,9 @@ def test_native_engine_sampling_is_seeded_and_within_top_k():
     s_a, greedy_mixed, eng = run(21)
     s_b, _, _ = run(21)
     assert s_a == s_b and len(s_a) == 8
-    assert greedy_mixed == greedy_alone
     w = _host(eng.weights)
+    # greedy next to a sampled request: the dense argmax (batching differs from a solo run)
+    _near_argmax(CFG, w, p2, greedy_mixed)
     seq = list(p1)
     for t in s_a:
         _, logits = _dense(CFG, w, seq)
