@@ -68,9 +68,10 @@ def test_rope_with_qk_norm_and_paged_cache_write():
     q = ops.rope_and_cache(qkv, pos, cs, nq, nkv, slots, kc, vc, q_norm=qw, k_norm=kw, eps=eps)
     q_ref = ref.rope(ref.rmsnorm(qkv[:, :nq * D].view(T, nq, D), qw, eps), pos, cs)
     k_ref = ref.rope(ref.rmsnorm(qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D), kw, eps), pos, cs)
-    assert (q.float() - q_ref).abs().max().item() < 3e-2
+    # one bf16 rounding of values up to ~10: compare relative to the magnitude
+    assert torch.allclose(q.float(), q_ref, rtol=1 / 128, atol=1e-2)
     blk, off = slots // page, slots % page
-    assert (kc[blk, :, off, :].float() - k_ref).abs().max().item() < 3e-2
+    assert torch.allclose(kc[blk, :, off, :].float(), k_ref, rtol=1 / 128, atol=1e-2)
     assert torch.equal(vc[blk, :, off, :], qkv[:, (nq + nkv) * D:].view(T, nkv, D))
     # without slots (no cache given) the kernel produces the same q
     q2 = ops.rope_and_cache(qkv, pos, cs, nq, nkv, q_norm=qw, k_norm=kw, eps=eps)
