@@ -25,6 +25,8 @@ class LlamaConfig:
     rope_scaling: tuple = ()
     # per-head RMSNorm of q and k before RoPE (Qwen3); weights q_norm / k_norm [head_dim]
     qk_norm: bool = False
+    # biases on the q, k and v projections (Qwen2); weight qkv_bias [(nq + 2 nkv) head_dim]
+    qkv_bias: bool = False
 
     @classmethod
     def llama_8b(cls):

@@ -91,6 +91,8 @@ class LlamaWeights:
             if cfg.qk_norm:  # Qwen3 per-head q/k norms, identity at init
                 L["q_norm"] = torch.ones(D, dtype=torch.bfloat16, device=dev)
                 L["k_norm"] = torch.ones(D, dtype=torch.bfloat16, device=dev)
+            if cfg.qkv_bias:  # Qwen2 q/k/v biases, this rank's rows
+                L["qkv_bias"] = col_parallel([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], 1).view(-1)
             self.layers.append(L)
         self.norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
         self.lm_head = col_parallel([cfg.vocab], H)
@@ -131,6 +133,10 @@ def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch):
         L["qkv"] = torch.cat([rows_of(p + "self_attn.q_proj.weight", cfg.heads * D),
                               rows_of(p + "self_attn.k_proj.weight", cfg.kv_heads * D),
                               rows_of(p + "self_attn.v_proj.weight", cfg.kv_heads * D)], 0).contiguous()
+        if cfg.qkv_bias:  # Qwen2: sharded like the projections' rows
+            L["qkv_bias"] = torch.cat([rows_of(p + "self_attn.q_proj.bias", cfg.heads * D),
+                                       rows_of(p + "self_attn.k_proj.bias", cfg.kv_heads * D),
+                                       rows_of(p + "self_attn.v_proj.bias", cfg.kv_heads * D)], 0).contiguous()
         L["o"] = cols_of(p + "self_attn.o_proj.weight", cfg.heads * D)
         L["gate_up"] = torch.cat([rows_of(p + "mlp.gate_proj.weight", F_),
                                   rows_of(p + "mlp.up_proj.weight", F_)], 0).contiguous()
@@ -285,6 +291,8 @@ class LlamaTP:
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_push(f"layer {li}")
             qkv = self._linear(x, L["qkv"])
+            if cfg.qkv_bias:
+                qkv += L["qkv_bias"]
             kc, vc = kv_caches[li]
             q = self.k.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc, **self._qk_norm_args(L))
             o = attn(li, q, kc, vc)
@@ -331,6 +339,8 @@ class LlamaTP:
         sp.rs_norm_ag(T, res, w.layers[0]["ln1"], cfg.eps)
         for li, L in enumerate(w.layers):
             qkv = sp.gemm_ag(T, L["qkv"])
+            if cfg.qkv_bias:
+                qkv += L["qkv_bias"]
             kc, vc = kv_caches[li]
             q = ops.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc, **self._qk_norm_args(L))
             o = attn(li, q, kc, vc)

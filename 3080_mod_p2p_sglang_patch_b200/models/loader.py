@@ -86,29 +86,42 @@ def write_safetensors(path: str, tensors: dict, metadata: dict = None):
             f.write(raw)
 
 
-SUPPORTED_ARCHS = ("LlamaForCausalLM", "Qwen3ForCausalLM")
+SUPPORTED_ARCHS = ("LlamaForCausalLM", "Qwen3ForCausalLM", "Qwen2ForCausalLM", "MistralForCausalLM")
 
 
 def config_from_hf(d: dict, name: str = None) -> LlamaConfig:
-    """LlamaConfig from a Hugging Face ``config.json`` dict: LlamaForCausalLM,
-    or Qwen3ForCausalLM (the same decoder plus per-head q/k RMSNorm)."""
+    """LlamaConfig from a Hugging Face ``config.json`` dict. Supported: the
+    Llama decoder (LlamaForCausalLM, MistralForCausalLM), Qwen3ForCausalLM
+    (plus per-head q/k RMSNorm) and Qwen2ForCausalLM (plus q/k/v biases).
+
+    A sliding attention window (Mistral's ``sliding_window``, Qwen2's with
+    ``use_sliding_window``) caps the positions at the window: every sequence
+    the engine admits then fits inside it, where sliding and full attention
+    are the same."""
     arch = (d.get("architectures") or ["LlamaForCausalLM"])[0]
     if arch not in SUPPORTED_ARCHS:
         raise ValueError(f"unsupported architecture {arch} (supported: {', '.join(SUPPORTED_ARCHS)})")
-    if d.get("attention_bias") or d.get("mlp_bias"):
-        raise ValueError("projection biases are not supported")
+    if d.get("mlp_bias") or (d.get("attention_bias") and arch != "Qwen2ForCausalLM"):
+        raise ValueError("projection biases are not supported (only Qwen2's q/k/v biases)")
     heads = int(d["num_attention_heads"])
     hidden = int(d["hidden_size"])
     scaling = d.get("rope_scaling") or {}
+    max_pos = int(d.get("max_position_embeddings", 8192))
+    window = None
+    if arch == "MistralForCausalLM" or d.get("use_sliding_window"):
+        window = d.get("sliding_window")
+    if window:
+        max_pos = min(max_pos, int(window))
     return LlamaConfig(
         name=name or d.get("_name_or_path") or d.get("model_type", "llama"),
         hidden=hidden, layers=int(d["num_hidden_layers"]), heads=heads,
         kv_heads=int(d.get("num_key_value_heads", heads)),
         head_dim=int(d.get("head_dim") or hidden // heads), ffn=int(d["intermediate_size"]),
         vocab=int(d["vocab_size"]), rope_theta=float(d.get("rope_theta", 10000.0)),
-        eps=float(d.get("rms_norm_eps", 1e-5)), max_pos=int(d.get("max_position_embeddings", 8192)),
+        eps=float(d.get("rms_norm_eps", 1e-5)), max_pos=max_pos,
         rope_scaling=tuple(sorted((str(k), v) for k, v in scaling.items())),
         qk_norm=arch == "Qwen3ForCausalLM",
+        qkv_bias=arch == "Qwen2ForCausalLM",
     )
 
 

@@ -42,6 +42,8 @@ def _dense(cfg, w, tokens):
     for L in w.layers:
         x = ref.rmsnorm(res, L["ln1"], eps)
         qkv = x @ L["qkv"].float().t()
+        if cfg.qkv_bias:
+            qkv = qkv + L["qkv_bias"].float()
         q = qkv[:, :nq * D].view(T, nq, D)
         k = qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D)
         v = qkv[:, (nq + nkv) * D:].view(T, nkv, D)
@@ -176,6 +178,20 @@ def test_qwen3_qk_norm_forward_matches_dense():
     got = _prompt_hidden(eng, prompt, 64)
     assert _cos(got, want[-1]) > 0.999
     plain, _ = _dense(CFG, eng.weights, prompt)             # the norm does change the result
+    assert _cos(plain[-1], want[-1]) < 0.99
+
+
+def test_qwen2_qkv_bias_forward_matches_dense():
+    cfg = models.LlamaConfig(**{**CFG.__dict__, "name": "qwen2-tiny", "qkv_bias": True})
+    eng = _engine(cfg)
+    g = torch.Generator().manual_seed(8)
+    for L in eng.weights.layers:                            # biases large enough to matter
+        L["qkv_bias"].copy_((0.5 * torch.randn(L["qkv_bias"].numel(), generator=g)).to(torch.bfloat16))
+    prompt = torch.randint(0, cfg.vocab, (90,), generator=g).tolist()
+    want, _ = _dense(cfg, eng.weights, prompt)
+    got = _prompt_hidden(eng, prompt, 64)
+    assert _cos(got, want[-1]) > 0.999
+    plain, _ = _dense(CFG, eng.weights, prompt)             # without the biases the answer differs
     assert _cos(plain[-1], want[-1]) < 0.99
 
 

@@ -96,3 +96,15 @@ def test_native_qwen3_forward_matches_dense():
     want, _ = _dense(cfg, _host(eng.weights), prompt)
     got = _prompt_hidden(eng, prompt, 64).cpu()
     assert _cos(got, want[-1]) > 0.995
+
+
+def test_native_qwen2_qkv_bias_forward_matches_dense():
+    cfg = models.LlamaConfig(**{**CFG.__dict__, "name": "qwen2-tiny", "qkv_bias": True})
+    eng = _engine(cfg, use_graphs=False)
+    g = torch.Generator().manual_seed(14)
+    for L in eng.weights.layers:
+        L["qkv_bias"].copy_((0.5 * torch.randn(L["qkv_bias"].numel(), generator=g)).to(torch.bfloat16))
+    prompt = torch.randint(0, cfg.vocab, (90,), generator=g).tolist()
+    want, _ = _dense(cfg, _host(eng.weights), prompt)
+    got = _prompt_hidden(eng, prompt, 64).cpu()
+    assert _cos(got, want[-1]) > 0.995

@@ -156,6 +156,38 @@ def test_qwen3_checkpoint_qk_norm(tmp_path):
     assert "q_norm" not in models.LlamaTP(models.config_from_hf(HF_CFG), w, impl="oracle")._qk_norm_args(w.layers[1])
 
 
+def test_qwen2_biases_and_sliding_windows(tmp_path):
+    """Qwen2ForCausalLM: q/k/v biases sharded like the projections' rows;
+    MistralForCausalLM: the sliding window caps the positions; a Llama
+    checkpoint with attention biases (o_proj too) is refused."""
+    cfg_json = dict(HF_CFG, architectures=["Qwen2ForCausalLM"], rope_scaling=None)
+    t = _checkpoint(tmp_path)
+    g = torch.Generator().manual_seed(9)
+    extra = {}
+    for i in range(2):
+        for proj, rows in (("q_proj", 4 * 128), ("k_proj", 2 * 128), ("v_proj", 2 * 128)):
+            extra[f"model.layers.{i}.self_attn.{proj}.bias"] = torch.randn(rows, generator=g).to(torch.bfloat16)
+    models.write_safetensors(str(tmp_path / "model-00003.safetensors"), extra)
+    (tmp_path / "config.json").write_text(json.dumps(cfg_json))
+    for r in range(2):
+        cfg, w = models.load_llama(str(tmp_path), r, 2, "cpu")
+        assert cfg.qkv_bias and not cfg.qk_norm
+        p = "model.layers.1.self_attn."
+        want = torch.cat([extra[p + "q_proj.bias"][r * 256:(r + 1) * 256], extra[p + "k_proj.bias"][r * 128:(r + 1) * 128],
+                          extra[p + "v_proj.bias"][r * 128:(r + 1) * 128]])
+        assert torch.equal(w.layers[1]["qkv_bias"], want)
+        assert torch.equal(w.layers[1]["qkv"][:256], t[p + "q_proj.weight"][r * 256:(r + 1) * 256])
+    mis = models.config_from_hf(dict(HF_CFG, architectures=["MistralForCausalLM"], sliding_window=512))
+    assert mis.max_pos == 512 and not mis.qkv_bias
+    assert models.config_from_hf(dict(HF_CFG, architectures=["MistralForCausalLM"], sliding_window=None)).max_pos == 1024
+    q2 = models.config_from_hf(dict(HF_CFG, architectures=["Qwen2ForCausalLM"], use_sliding_window=True,
+                                    sliding_window=256))
+    assert q2.max_pos == 256
+    assert models.config_from_hf(dict(HF_CFG, architectures=["Qwen2ForCausalLM"], sliding_window=256)).max_pos == 1024
+    with pytest.raises(ValueError, match="biases"):
+        models.config_from_hf(dict(HF_CFG, attention_bias=True))
+
+
 def test_unsupported_architecture_is_rejected():
 
     with pytest.raises(ValueError):
