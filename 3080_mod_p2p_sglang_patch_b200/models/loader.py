@@ -106,6 +106,11 @@ def config_from_hf(d: dict, name: str = None) -> LlamaConfig:
     heads = int(d["num_attention_heads"])
     hidden = int(d["hidden_size"])
     scaling = d.get("rope_scaling") or {}
+    from ..ops import ROPE_SCALINGS
+
+    kind = scaling.get("rope_type", scaling.get("type")) if scaling else None
+    if kind not in ROPE_SCALINGS:
+        raise ValueError(f"rope scaling {kind!r} is not supported (supported: linear, llama3)")
     max_pos = int(d.get("max_position_embeddings", 8192))
     window = None
     if arch == "MistralForCausalLM" or d.get("use_sliding_window"):

@@ -112,8 +112,15 @@ def fused_add_rmsnorm(x, residual, w, eps, out=None):
     return out
 
 
+# rope_scaling types rope_cos_sin implements (None / "default": plain RoPE)
+ROPE_SCALINGS = (None, "default", "linear", "llama3")
+
+
 def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device, scaling=None) -> torch.Tensor:
     """[max_pos, head_dim] fp32 table: cos in the first half, sin in the second.
+
+    ``scaling`` (dict) with ``rope_type == "linear"`` divides every frequency
+    by ``factor`` (position interpolation); other types raise.
 
     ``scaling`` (dict) with ``rope_type == "llama3"`` applies Llama 3.1's
     frequency rescaling: wavelengths above original_max_position /
@@ -121,7 +128,12 @@ def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device, scaling=None
     high_freq_factor are kept, and the band between is interpolated linearly
     in original / wavelength."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
-    if scaling and scaling.get("rope_type", scaling.get("type")) == "llama3":
+    kind = scaling.get("rope_type", scaling.get("type")) if scaling else None
+    if kind not in ROPE_SCALINGS:
+        raise ValueError(f"rope scaling {kind!r} is not supported (supported: {', '.join(map(str, ROPE_SCALINGS))})")
+    if kind == "linear":  # position interpolation: every frequency divided by the factor
+        inv = inv / float(scaling["factor"])
+    if kind == "llama3":
         factor = float(scaling["factor"])
         lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
         orig = float(scaling.get("original_max_position_embeddings", 8192))

@@ -303,3 +303,20 @@ def test_awq_rejects_unsupported_configs_and_misaligned_shards(tmp_path):
     models.load_llama(str(tmp_path), 0, 1, "cpu")          # whole tensors: any group size works
     with pytest.raises(ValueError, match="group"):
         models.load_llama(str(tmp_path), 1, 2, "cpu")      # down_proj shard of 192 inputs vs group 128
+
+
+def test_rope_scaling_types():
+    """linear scaling divides every frequency by the factor; scalings the
+    table does not implement are refused when the config is read."""
+    base = ops.rope_cos_sin(8, 128, 10000.0, "cpu")
+    lin = ops.rope_cos_sin(8, 128, 10000.0, "cpu", {"rope_type": "linear", "factor": 4.0})
+    ang_b = torch.atan2(base[1, 64:], base[1, :64])
+    ang_l = torch.atan2(lin[1, 64:], lin[1, :64])
+    assert torch.allclose(ang_l, ang_b / 4.0, rtol=1e-5, atol=1e-7)
+    assert torch.equal(ops.rope_cos_sin(8, 128, 10000.0, "cpu", {"rope_type": "default"}), base)
+    for kind in ("yarn", "dynamic", "longrope"):
+        with pytest.raises(ValueError, match="rope scaling"):
+            models.config_from_hf(dict(HF_CFG, rope_scaling={"rope_type": kind, "factor": 4.0}))
+        with pytest.raises(ValueError, match="rope scaling"):
+            ops.rope_cos_sin(8, 128, 10000.0, "cpu", {"type": kind, "factor": 4.0})
+    assert dict(models.config_from_hf(dict(HF_CFG, rope_scaling={"type": "linear", "factor": 2.0})).rope_scaling)
