@@ -103,6 +103,9 @@ def config_from_hf(d: dict, name: str = None) -> LlamaConfig:
         raise ValueError(f"unsupported architecture {arch} (supported: {', '.join(SUPPORTED_ARCHS)})")
     if d.get("mlp_bias") or (d.get("attention_bias") and arch != "Qwen2ForCausalLM"):
         raise ValueError("projection biases are not supported (only Qwen2's q/k/v biases)")
+    act = d.get("hidden_act", "silu")
+    if act != "silu":  # the MLP kernel is SiLU(gate) * up
+        raise ValueError(f"activation {act!r} is not supported (supported: silu)")
     heads = int(d["num_attention_heads"])
     hidden = int(d["hidden_size"])
     scaling = d.get("rope_scaling") or {}

@@ -320,3 +320,9 @@ def test_rope_scaling_types():
         with pytest.raises(ValueError, match="rope scaling"):
             ops.rope_cos_sin(8, 128, 10000.0, "cpu", {"type": kind, "factor": 4.0})
     assert dict(models.config_from_hf(dict(HF_CFG, rope_scaling={"type": "linear", "factor": 2.0})).rope_scaling)
+
+
+def test_non_silu_activation_is_refused():
+    with pytest.raises(ValueError, match="activation"):
+        models.config_from_hf(dict(HF_CFG, hidden_act="gelu_pytorch_tanh"))
+    assert models.config_from_hf(dict(HF_CFG, hidden_act="silu")).ffn == 384
