@@ -20,7 +20,7 @@ from ..utils import nvtx
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
 from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
 from .kv_cache import PAGE, PagedKVCache, PrefixCache
-from .sampling import GREEDY, sample
+from .sampling import GREEDY, SamplingParams, sample
 from .scheduler import Request, Scheduler
 
 
@@ -37,6 +37,10 @@ class LLMEngine:
         self.cfg = cfg
         self.tp = tp
         self.impl = impl
+        # text API (generate_text): the checkpoint's tokenizer and stop ids when
+        # loaded with from_pretrained, else bytes and none
+        self.tokenizer = None
+        self.default_stop_ids = ()
         self.tp_size = tp.world_size if tp is not None else 1
         self.tp_rank = tp.rank if tp is not None else 0
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -108,10 +112,19 @@ class LLMEngine:
         shards only are read; see models/loader.py)."""
         from ..models.loader import load_llama
 
+        from ..models.loader import stop_token_ids
+        from .tokenizer import HFTokenizer
+
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         cfg, w = load_llama(model_dir, tp.rank if tp is not None else 0, tp.world_size if tp is not None else 1, dev)
         kw.setdefault("max_seq", min(cfg.max_pos, 8192))
-        return cls(cfg, tp=tp, device=dev, weights=w, **kw)
+        eng = cls(cfg, tp=tp, device=dev, weights=w, **kw)
+        try:
+            eng.tokenizer = HFTokenizer(model_dir)
+        except Exception:  # noqa: BLE001 - token-id APIs still work without one
+            eng.tokenizer = None
+        eng.default_stop_ids = stop_token_ids(model_dir)
+        return eng
 
     @property
     def max_request_tokens(self) -> int:
@@ -330,3 +343,30 @@ class LLMEngine:
         reqs = [self.add_request(p, max_new_tokens, stop_ids, sampling) for p in prompts]
         self.run()
         return [r.output for r in reqs]
+
+    def generate_text(self, prompts, sampling_params: dict = None):
+        """Offline generation over text, in the shape of sglang's offline
+        engine: ``prompts`` is a string or a list of strings;
+        ``sampling_params`` a dict of ``max_new_tokens`` (16), ``temperature``
+        (0: greedy), ``top_k``, ``top_p``, ``seed`` and ``stop_token_ids``
+        (default: the checkpoint's EOS ids). Returns one ``{"text",
+        "token_ids", "finish_reason"}`` per prompt (a single dict for a single
+        string)."""
+        from .tokenizer import ByteTokenizer
+
+        tok = self.tokenizer or ByteTokenizer()
+        sp = dict(sampling_params or {})
+        max_new = int(sp.pop("max_new_tokens", 16))
+        stop = sp.pop("stop_token_ids", None)
+        stop = self.default_stop_ids if stop is None else tuple(stop)
+        temp = float(sp.pop("temperature", 0.0))
+        top_k, top_p, seed = int(sp.pop("top_k", 0)), float(sp.pop("top_p", 1.0)), sp.pop("seed", None)
+        if sp:
+            raise ValueError(f"unknown sampling params: {', '.join(sorted(sp))}")
+        sampling = SamplingParams(temp, top_k, top_p, seed) if temp > 0 else None
+        single = isinstance(prompts, str)
+        reqs = [self.add_request(tok.encode(p), max_new, stop, sampling) for p in ([prompts] if single else prompts)]
+        self.run()
+        out = [{"text": tok.decode(r.output), "token_ids": list(r.output), "finish_reason": r.finish_reason}
+               for r in reqs]
+        return out[0] if single else out

@@ -43,37 +43,9 @@ import sys
 import threading
 import time
 
+from .engine.tokenizer import ByteTokenizer, HFTokenizer  # noqa: F401 - re-exported
+
 logger = logging.getLogger(__name__)
-
-
-class ByteTokenizer:
-    """UTF-8 bytes as token ids (ids >= 256 have no text)."""
-
-    def encode(self, text: str) -> list:
-        return list(text.encode("utf-8"))
-
-    def decode(self, ids) -> str:
-        return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
-
-
-class HFTokenizer:
-    """A checkpoint directory's tokenizer (transformers, local files only)."""
-
-    def __init__(self, path: str):
-        from transformers import AutoTokenizer
-
-        self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
-
-    def encode(self, text: str) -> list:
-        return self.tok.encode(text, add_special_tokens=True)
-
-    def decode(self, ids) -> str:
-        return self.tok.decode(ids, skip_special_tokens=True)
-
-    def chat(self, messages) -> list:
-        if getattr(self.tok, "chat_template", None):
-            return list(self.tok.apply_chat_template(messages, add_generation_prompt=True, tokenize=True))
-        return self.encode("".join(f"{m.get('role', 'user')}: {m.get('content', '')}\n" for m in messages))
 
 
 class _Pending:
@@ -674,15 +646,14 @@ def main(argv=None):
     if model_path:
         eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, **opts)
         cfg = eng.cfg
-        try:
-            tokenizer = HFTokenizer(model_path)
-        except Exception as e:  # noqa: BLE001 - token-id prompts still work
-            logger.warning("no tokenizer in %s (%s); using the byte tokenizer", model_path, e)
+        tokenizer = eng.tokenizer
+        if tokenizer is None:  # token-id prompts still work
+            logger.warning("no tokenizer in %s; using the byte tokenizer", model_path)
     else:
         cfg = models.LlamaConfig.by_name(name)
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
         eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, **opts)
-    stop = models.stop_token_ids(model_path) if model_path else ()
+    stop = eng.default_stop_ids
     server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop)
     http = None
     if rank == 0:

@@ -302,3 +302,22 @@ def test_prefill_chunks_that_end_no_prompt_are_not_read_back():
     out = eng.generate([list(range(1, 101))], max_new_tokens=2)[0]   # 100 tokens: 4 chunks of 32
     assert len(reads) == 1 and reads[0] == [True] and len(out) == 2
     _assert_near_argmax(CFG, eng.weights, list(range(1, 101)), out)
+
+
+def test_text_api_in_the_shape_of_sglangs_offline_engine():
+    eng = _engine()
+    one = eng.generate_text("Hello, B200", {"max_new_tokens": 4})
+    assert set(one) == {"text", "token_ids", "finish_reason"}
+    assert len(one["token_ids"]) == 4 and one["finish_reason"] == "length" and isinstance(one["text"], str)
+    # the same prompt as token ids gives the same tokens (byte tokenizer without a checkpoint)
+    assert _engine().generate([list("Hello, B200".encode())], max_new_tokens=4)[0] == one["token_ids"]
+    sp = {"max_new_tokens": 5, "temperature": 1.3, "top_k": 30, "seed": 11}
+    a = _engine().generate_text(["x", "yz"], sp)
+    b = _engine().generate_text(["x", "yz"], sp)
+    assert [r["token_ids"] for r in a] == [r["token_ids"] for r in b] and len(a) == 2
+    stop = one["token_ids"][1]
+    k = one["token_ids"].index(stop)
+    cut = _engine().generate_text("Hello, B200", {"max_new_tokens": 4, "stop_token_ids": [stop]})
+    assert cut["token_ids"] == one["token_ids"][:k + 1] and cut["finish_reason"] == "stop"
+    with pytest.raises(ValueError, match="unknown sampling"):
+        eng.generate_text("x", {"max_tokens": 3})
