@@ -20,7 +20,7 @@ PKG = "3080_mod_p2p_sglang_patch_b200"
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="tiny", help="8b | 70b | tiny (random weights)")
-    ap.add_argument("--model-path", default=None, help="Hugging Face Llama / Qwen3 safetensors directory")
+    ap.add_argument("--model-path", default=None, help="Hugging Face checkpoint directory (Llama, Mistral, Qwen2/3)")
     ap.add_argument("--prompt", default="Hello from B200")
     ap.add_argument("--max-new", type=int, default=16)
     ap.add_argument("--temperature", type=float, default=0.0)
@@ -31,23 +31,17 @@ def main():
     par = importlib.import_module(f"{PKG}.parallel")
     models = importlib.import_module(f"{PKG}.models")
     eng_mod = importlib.import_module(f"{PKG}.engine")
-    server = importlib.import_module(f"{PKG}.server")
     rank, world, local = par.init_distributed()
     dev = torch.device("cuda", local)
     tp = par.TPGroup(None, dev) if world > 1 else None  # MailboxAR when SGLANG_MAILBOX_AR=1, else NCCL
     if args.model_path:
         eng = eng_mod.LLMEngine.from_pretrained(args.model_path, tp=tp, device=dev, max_batch=4)
-        tok = server.HFTokenizer(args.model_path)
-        stop = models.stop_token_ids(args.model_path)
     else:
         eng = eng_mod.LLMEngine(models.LlamaConfig.by_name(args.model), tp=tp, device=dev, max_batch=4, max_seq=4096)
-        tok, stop = server.ByteTokenizer(), ()
-    sampling = None
-    if args.temperature > 0:
-        sampling = eng_mod.SamplingParams(args.temperature, args.top_k, args.top_p, args.seed)
-    out = eng.generate([tok.encode(args.prompt)], max_new_tokens=args.max_new, stop_ids=stop, sampling=sampling)[0]
+    out = eng.generate_text(args.prompt, {"max_new_tokens": args.max_new, "temperature": args.temperature,
+                                          "top_k": args.top_k, "top_p": args.top_p, "seed": args.seed})
     if rank == 0:
-        print({"token_ids": out, "text": tok.decode(out)})
+        print(out)
     if eng.graphs is not None:
         eng.graphs.close()
     if tp is not None:
