@@ -183,6 +183,12 @@ class LLMEngine:
         self.sched.add(req)
         return req
 
+    def abort(self, rid: int) -> bool:
+        """End request ``rid`` between steps (finish_reason "abort"); its KV
+        pages and batch slot are freed. Every TP rank must abort the same
+        request at the same step."""
+        return self.sched.abort(rid)
+
     def _sync_block_row(self, req):
         row = torch.zeros(self.max_blocks_per_seq, dtype=torch.int32)
         row[: len(req.blocks)] = torch.tensor(req.blocks, dtype=torch.int32)

@@ -175,6 +175,26 @@ class Scheduler:
             return True
         return False
 
+    def abort(self, rid: int) -> bool:
+        """End request ``rid`` now, wherever it is (queued, prefilling or
+        decoding): its pages and batch slot are released and it moves to
+        ``finished`` with finish_reason "abort" and the tokens it has. Call
+        between steps. False if no live request has that id."""
+        for req in self.waiting:
+            if req.rid == rid:
+                self.waiting.remove(req)
+                req.done, req.finish_reason = True, "abort"
+                self.finished.append(req)
+                return True
+        for queue in (self.prefilling, self.running):
+            for req in queue:
+                if req.rid == rid:
+                    queue.remove(req)
+                    req.finish_reason = "abort"
+                    self._finish(req)
+                    return True
+        return False
+
     def _finish(self, req):
         req.done = True
         if req.blocks:

@@ -50,13 +50,20 @@ logger = logging.getLogger(__name__)
 
 class _Pending:
     __slots__ = ("prompt", "max_new", "stop_ids", "sampling", "event", "output", "error", "stream", "req", "sent",
-                 "reason")
+                 "reason", "sid", "stop_strs", "detok", "checked", "stop_hit", "abort_sent")
 
-    def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None):
+    def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None, sid=-1, stop_strs=(), detok=None):
         self.prompt = prompt
         self.max_new = max_new
         self.stop_ids = tuple(stop_ids)
         self.sampling = sampling  # (temperature, top_k, top_p, seed) or None
+        self.sid = sid            # server-wide request id: the same on every rank
+        # stop strings (rank 0): checked on the decoded output after each step
+        self.stop_strs = tuple(stop_strs)
+        self.detok = detok        # token ids -> text
+        self.checked = 0          # output tokens already checked for stop strings
+        self.stop_hit = False
+        self.abort_sent = False
         self.reason = "length"
         self.event = threading.Event()
         self.output = None
@@ -93,6 +100,8 @@ class EngineServer:
         self.max_prompt = max_prompt
         self.q = queue.Queue()
         self._by_rid = {}
+        self._sids = itertools.count()   # rank 0 numbers requests; the id travels with them
+        self._rid_of_sid = {}            # live requests, every rank
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0, "steps": 0,
                       "control_shm": 0, "control_gloo": 0}  # control-plane exchanges by channel
         # latency samples of finished requests (seconds): time to first token, inter-token gaps
@@ -123,12 +132,18 @@ class EngineServer:
         return None if ar.disabled else (ar, torch.zeros(4, dtype=torch.float32))
 
     # ------------------------------------------------------------ rank 0 API
+    ABORT = "__abort__"
+
     def submit(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, with_reason=False,
-               sampling=None):
+               sampling=None, stop_strs=(), detok=None):
         """Called from HTTP threads on rank 0: blocks until the request is done
-        and returns the generated token ids (and the finish reason, "length" or
-        "stop", with ``with_reason``). ``stop_ids`` None = the server default."""
-        p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling)
+        and returns the generated token ids (and the finish reason, "length",
+        "stop" or "abort", with ``with_reason``). ``stop_ids`` None = the server
+        default. ``stop_strs``: generation also ends once ``detok(tokens)``
+        contains one of them; the tokens are then cut to the shortest prefix
+        whose text contains it."""
+        p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
+                          detok=detok)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if isinstance(p.error, ValueError):  # the engine rejected the request itself
@@ -138,23 +153,36 @@ class EngineServer:
         return (p.output, p.reason) if with_reason else p.output
 
     def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None,
-                      sampling=None):
+                      sampling=None, stop_strs=(), detok=None):
         """Like ``submit`` but yields lists of new token ids as the engine
         produces them (rank 0, from an HTTP thread); the finish reason is
-        appended to ``reason_out`` (a list) at the end."""
-        p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids, sampling=sampling)
-        while True:
-            try:
-                item = p.stream.get(timeout=timeout)
-            except queue.Empty:
-                raise TimeoutError("request timed out") from None
-            if item is None:
-                break
-            yield item
+        appended to ``reason_out`` (a list) at the end. Closing the generator
+        early (a client that went away) aborts the request."""
+        p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
+                          detok=detok)
+        try:
+            while True:
+                try:
+                    item = p.stream.get(timeout=timeout)
+                except queue.Empty:
+                    raise TimeoutError("request timed out") from None
+                if item is None:
+                    break
+                yield item
+        finally:
+            if not p.event.is_set():
+                self.abort(p)
         if p.error is not None:
             raise RuntimeError(p.error)
         if reason_out is not None:
             reason_out.append(p.reason)
+
+    def abort(self, p):
+        """End a submitted request early (rank 0, any thread): every rank drops
+        it at the same step; its waiter gets the tokens so far."""
+        if not p.abort_sent and not p.event.is_set():
+            p.abort_sent = True
+            self.q.put((self.ABORT, p.sid))
 
     def _enqueue_check(self, prompt, max_new):
         if not prompt:
@@ -172,12 +200,16 @@ class EngineServer:
             raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
                              f"max sequence {limit}")
 
-    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None):
+    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None, stop_strs=(), detok=None):
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
+        stop_strs = tuple(x for x in stop_strs if x)
+        if stop_strs and detok is None:
+            raise ValueError("stop strings need a detokenizer")
         p = _Pending(list(prompt), int(max_new), stream=stream,
-                     stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling)
+                     stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling,
+                     sid=next(self._sids), stop_strs=stop_strs, detok=detok)
         self.q.put(p)
         return p
 
@@ -211,11 +243,12 @@ class EngineServer:
                 if int(ar.all_reduce(cnt)[0].item()) == 0:
                     return cmds  # nothing new (rank 0's list is empty too)
             self.stats["control_gloo"] += 1
-            payload = [[c if c == self.SHUTDOWN else (c.prompt, c.max_new, c.stop_ids, c.sampling) for c in cmds]]
+            payload = [[c if not isinstance(c, _Pending) else (c.sid, c.prompt, c.max_new, c.stop_ids, c.sampling)
+                        for c in cmds]]
             dist.broadcast_object_list(payload, src=0, group=self.group)
             if self.rank != 0:
-                cmds = [c if c == self.SHUTDOWN else _Pending(c[0], c[1], stop_ids=c[2], sampling=c[3])
-                        for c in payload[0]]
+                cmds = [c if c == self.SHUTDOWN or c[0] == self.ABORT else
+                        _Pending(c[1], c[2], stop_ids=c[3], sampling=c[4], sid=c[0]) for c in payload[0]]
         return cmds
 
     def serve_forever(self):
@@ -228,6 +261,11 @@ class EngineServer:
                 for c in cmds:
                     if c == self.SHUTDOWN:
                         stop = True
+                        continue
+                    if isinstance(c, tuple):  # (ABORT, sid): the same request on every rank
+                        rid = self._rid_of_sid.get(c[1])
+                        if rid is not None:
+                            eng.abort(rid)
                         continue
                     try:
                         if c.sampling is None:
@@ -243,6 +281,7 @@ class EngineServer:
                         continue
                     c.req = req
                     self._by_rid[req.rid] = c
+                    self._rid_of_sid[c.sid] = req.rid
                     self.stats["requests"] += 1
                     self.stats["prompt_tokens"] += len(c.prompt)
                 if stop:
@@ -255,17 +294,28 @@ class EngineServer:
                         if p.stream is not None and p.req is not None and len(p.req.output) > p.sent:
                             p.stream.put(list(p.req.output[p.sent:]))
                             p.sent = len(p.req.output)
+                        if p.stop_strs and p.req is not None and len(p.req.output) > p.checked:
+                            p.checked = len(p.req.output)
+                            if _find_stop(p.detok(p.req.output), p.stop_strs) >= 0:
+                                p.stop_hit = True
+                                self.abort(p)  # every rank drops it next step
                 done, eng.sched.finished = eng.sched.finished, []
                 for r in done:
                     p = self._by_rid.pop(r.rid, None)
                     if p is not None:
+                        self._rid_of_sid.pop(p.sid, None)
                         self.stats["completion_tokens"] += len(r.output)
                         times = getattr(r, "token_times", None) or []
                         if times and getattr(r, "t_arrive", 0):
                             self.ttft.append(times[0] - r.t_arrive)
                             self.itl.extend(b - a for a, b in zip(times, times[1:]))
+                        out = list(r.output)
                         p.reason = getattr(r, "finish_reason", None) or "length"
-                        p.finish(output=list(r.output))
+                        if p.stop_strs and p.detok is not None:
+                            k = _stop_prefix(out, p.stop_strs, p.detok)
+                            if k is not None:
+                                out, p.reason = out[:k], "stop"
+                        p.finish(output=out)
         except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
             for p in self._by_rid.values():
                 p.finish(error=repr(e))
@@ -287,9 +337,39 @@ class EngineServer:
                     c.finish(error="server stopped")
 
 
+def _find_stop(text: str, stops) -> int:
+    """Index of the earliest stop string in ``text``, or -1."""
+    hits = [i for i in (text.find(x) for x in stops) if i >= 0]
+    return min(hits) if hits else -1
+
+
+def _held_back(text: str, stops) -> int:
+    """Characters at the end of ``text`` that could begin a stop string (a
+    stream holds them until the next tokens decide)."""
+    hold = 0
+    for x in stops:
+        for k in range(min(len(x) - 1, len(text)), hold, -1):
+            if text.endswith(x[:k]):
+                hold = k
+                break
+    return hold
+
+
+def _stop_prefix(tokens, stops, detok):
+    """Length of the shortest token prefix whose text contains a stop string
+    (None if the whole output holds none)."""
+    if _find_stop(detok(tokens), stops) < 0:
+        return None
+    k = len(tokens)
+    while k > 1 and _find_stop(detok(tokens[:k - 1]), stops) >= 0:
+        k -= 1
+    return k
+
+
 def build_app(server: EngineServer, model_name: str, tokenizer=None):
-    """FastAPI app with /health, /v1/models, /v1/completions and
-    /v1/chat/completions (non-streaming, greedy)."""
+    """FastAPI app with /health, /metrics, /v1/models, /v1/completions and
+    /v1/chat/completions (plain or streamed; greedy or sampled; stop token
+    ids and stop strings)."""
     from fastapi import FastAPI, HTTPException
     from fastapi.concurrency import iterate_in_threadpool, run_in_threadpool
     from fastapi.responses import StreamingResponse
@@ -309,6 +389,23 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         ids_ = body.get("stop_token_ids")
         return None if ids_ is None else [int(t) for t in ids_]
 
+    def _stop_strs(body):
+        """OpenAI ``stop``: a string or a list of strings."""
+        st = body.get("stop")
+        if st is None:
+            return ()
+        if isinstance(st, str):
+            return (st,)
+        if isinstance(st, list) and all(isinstance(x, str) for x in st):
+            return tuple(st)
+        raise HTTPException(400, "stop must be a string or a list of strings")
+
+    def _text(out, stops):
+        """Decoded text, ending before the first stop string."""
+        text = tok.decode(out)
+        i = _find_stop(text, stops) if stops else -1
+        return text if i < 0 else text[:i]
+
     def _sampling(body):
         """(temperature, top_k, top_p, seed), or None for greedy."""
         t = float(body.get("temperature") or 0.0)
@@ -318,9 +415,10 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         return (t, int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
                 None if seed is None else int(seed))
 
-    def _run(prompt, max_tokens, stop=None, sampling=None):
+    def _run(prompt, max_tokens, stop=None, sampling=None, stops=()):
         try:
-            return server.submit(prompt, max_tokens, stop_ids=stop, with_reason=True, sampling=sampling)
+            return server.submit(prompt, max_tokens, stop_ids=stop, with_reason=True, sampling=sampling,
+                                 stop_strs=stops, detok=tok.decode)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         except (RuntimeError, TimeoutError) as e:
@@ -335,18 +433,36 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
 
-    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None):
-        """Server-sent events: one chunk per engine step's new tokens, a last
-        chunk with finish_reason and usage, then [DONE]."""
+    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None, stops=()):
+        """Server-sent events: one chunk per engine step's new tokens (the text
+        delta of the decoded output, cut before a stop string), a last chunk
+        with finish_reason and usage, then [DONE]. A client that disconnects
+        closes the generator, which aborts the request."""
         def gen():
-            out, reason = [], []
+            out, reason, sent = [], [], ""
+            fin = None
             try:
-                for toks in server.submit_stream(prompt, max_tokens, stop_ids=stop, reason_out=reason,
-                                                 sampling=sampling):
-                    out += toks
-                    yield "data: " + json.dumps(chunk_of(toks, None, None)) + "\n\n"
-                fin = reason[0] if reason else "length"
-                yield "data: " + json.dumps(chunk_of([], fin, _usage(prompt, out))) + "\n\n"
+                stream = server.submit_stream(prompt, max_tokens, stop_ids=stop, reason_out=reason,
+                                              sampling=sampling, stop_strs=stops, detok=tok.decode)
+                try:
+                    for toks in stream:
+                        out += toks
+                        hit = bool(stops) and _find_stop(tok.decode(out), stops) >= 0
+                        text = _text(out, stops)
+                        if stops and not hit:
+                            text = text[:len(text) - _held_back(text, stops)]
+                        delta, sent = text[len(sent):], text
+                        yield "data: " + json.dumps(chunk_of(toks, delta, None, None)) + "\n\n"
+                        if hit:
+                            fin = "stop"  # the server loop drops the request on every rank
+                            break
+                finally:
+                    stream.close()
+                fin = fin or (reason[0] if reason else "length")
+                if fin == "stop" and stops:
+                    out = out[:_stop_prefix(out, stops, tok.decode) or len(out)]
+                rest = _text(out, stops)[len(sent):]  # text held back for a stop string that never came
+                yield "data: " + json.dumps(chunk_of([], rest, fin, _usage(prompt, out))) + "\n\n"
             except (RuntimeError, TimeoutError) as e:
                 yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
             yield "data: [DONE]\n\n"
@@ -374,18 +490,18 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     async def completions(body: dict):
         prompt = _prompt_ids(body.get("prompt", ""))
         max_tokens = int(body.get("max_tokens", 16))
-        stop = _stop(body)
+        stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
             _check(prompt, max_tokens)
             cid, created = f"cmpl-{next(ids)}", int(time.time())
-            return _sse(prompt, max_tokens, lambda toks, fin, usage: {
+            return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
                 "id": cid, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "text": tok.decode(toks), "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})}, stop, _sampling(body))
-        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body))
+                "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": fin}],
+                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
+        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops)
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
                 "model": model_name,
-                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": fin}],
+                "choices": [{"index": 0, "text": _text(out, stops), "token_ids": out, "finish_reason": fin}],
                 "usage": _usage(prompt, out)}
 
     @app.post("/v1/chat/completions")
@@ -397,19 +513,19 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
             text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
             prompt = tok.encode(text)
         max_tokens = int(body.get("max_tokens", 16))
-        stop = _stop(body)
+        stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
             _check(prompt, max_tokens)
             cid, created = f"chatcmpl-{next(ids)}", int(time.time())
-            return _sse(prompt, max_tokens, lambda toks, fin, usage: {
+            return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
                 "id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
-                "choices": [{"index": 0, "delta": {"content": tok.decode(toks)} if toks else {},
+                "choices": [{"index": 0, "delta": {"content": text} if (toks or text) else {},
                              "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})}, stop, _sampling(body))
-        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body))
+                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
+        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops)
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
                 "model": model_name,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": _text(out, stops)},
                              "token_ids": out, "finish_reason": fin}],
                 "usage": _usage(prompt, out)}
 

@@ -321,3 +321,18 @@ def test_text_api_in_the_shape_of_sglangs_offline_engine():
     assert cut["token_ids"] == one["token_ids"][:k + 1] and cut["finish_reason"] == "stop"
     with pytest.raises(ValueError, match="unknown sampling"):
         eng.generate_text("x", {"max_tokens": 3})
+
+
+def test_abort_mid_decode_frees_the_request_and_spares_the_others():
+    eng = _engine()
+    g = torch.Generator().manual_seed(15)
+    pa, pb = (torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (30, 50))
+    a = eng.add_request(pa, 20)
+    b = eng.add_request(pb, 6)
+    while len(a.output) < 3:
+        eng.step()
+    assert eng.abort(a.rid) and a.finish_reason == "abort" and len(a.output) == 3
+    eng.run()
+    assert b.finish_reason == "length" and len(b.output) == 6
+    _assert_near_argmax(CFG, eng.weights, pb, b.output)
+    assert eng.kv.alloc.free == eng.kv.alloc.num_blocks - 1 and not eng.abort(a.rid)

@@ -228,3 +228,25 @@ def test_request_needs_a_prompt_and_a_positive_budget():
     for prompt, max_new in (([], 4), ([1, 2], 0), ([1, 2], -3)):
         with pytest.raises(ValueError):
             s.add(sched_mod.Request(rid=0, prompt=prompt, max_new=max_new))
+
+
+def test_abort_frees_pages_and_slots_wherever_the_request_is():
+    alloc = kv_mod.BlockAllocator(num_blocks=1 + 40)
+    pc = kv_mod.PrefixCache(alloc)
+    s = sched_mod.Scheduler(chunk=32, max_batch=2, allocator=alloc, prefix_cache=pc)
+    reqs = [_req(i, 40, 8) for i in range(3)]
+    for r in reqs:
+        s.add(r)
+    b = s.next_batch()                               # 0 and 1 admitted (2 slots), 2 waits
+    assert [p.req.rid for p in b.pieces] == [0] and len(s.waiting) == 1
+    s.after_prefill(b, [7])
+    assert s.abort(2) and reqs[2].finish_reason == "abort" and reqs[2].output == []   # from the queue
+    assert s.abort(1) and reqs[1].blocks == [] and reqs[1].slot == -1                 # mid-prefill
+    while reqs[0].computed < 40:
+        s.after_prefill(s.next_batch(), [7])
+    s.after_decode(s.next_batch(), [5])
+    assert s.abort(0) and reqs[0].output == [7, 5] and reqs[0].finish_reason == "abort"  # decoding
+    assert not s.has_work() and not s.abort(0)
+    assert sorted(r.rid for r in s.finished) == [0, 1, 2]
+    assert alloc.free + pc.evictable == 40                                           # every page back
+    assert sorted(s._free_slots) == [0, 1]

@@ -44,6 +44,8 @@ class FakeEngine:
         self.n = 0
         self.log = []
         self.sampling_seen = []
+        self.aborted = []   # (rid, steps taken when it was aborted)
+        self.steps = 0
 
     def add_request(self, prompt, max_new, stop_ids=(), sampling=None):
         r = _Req(self.n, prompt, max_new)
@@ -55,9 +57,20 @@ class FakeEngine:
         self.log.append((r.rid, tuple(prompt), max_new))
         return r
 
+    def abort(self, rid):
+        for r in list(self.sched.running):
+            if r.rid == rid:
+                self.sched.running.remove(r)
+                r.finish_reason = "abort"
+                self.sched.finished.append(r)
+                self.aborted.append((rid, self.steps))
+                return True
+        return False
+
     def step(self):
         import time as _t
 
+        self.steps += 1
         for r in list(self.sched.running):
             r.output.append((sum(r.prompt) + len(r.output)) % 1000)
             r.token_times.append(_t.perf_counter())
@@ -336,6 +349,147 @@ def test_engine_rejection_fails_one_request_and_the_server_keeps_serving():
         r = requests.post(url, json={"prompt": [5, 6], "max_tokens": 3}, timeout=60)
         assert r.status_code == 200 and r.json()["choices"][0]["token_ids"] == expected([5, 6], 3)
         assert loop.is_alive()
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+
+
+def _serve(eng):
+    from conftest import free_port
+
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    return server, loop, http, f"http://127.0.0.1:{port}"
+
+
+def test_stop_strings_end_generation_and_cut_the_text():
+    """OpenAI ``stop``: the fake engine emits ids 100, 101, ... = bytes
+    'd', 'e', 'f', 'g', ...; stop "fg" ends the request once "fg" appears,
+    on the engine too (aborted, not run to max_tokens)."""
+    import json as _json
+
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 12, "stop": ["zz", "fg"]},
+                          timeout=60).json()
+        ch = r["choices"][0]
+        assert ch["text"] == "de" and ch["finish_reason"] == "stop" and ch["token_ids"] == [100, 101, 102, 103]
+        assert eng.aborted and eng.aborted[0][1] < 12                     # the engine stopped early
+        # streamed: the text deltas add up to the cut text
+        with requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 12, "stop": "fg",
+                                                            "stream": True}, stream=True, timeout=60) as resp:
+            chunks = [_json.loads(ln[6:]) for ln in resp.iter_lines(decode_unicode=True)
+                      if ln.startswith("data: ") and ln != "data: [DONE]"]
+        assert "".join(c["choices"][0]["text"] for c in chunks) == "de"
+        assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+        # chat: same rules
+        r = requests.post(base + "/v1/chat/completions",
+                          json={"messages": [{"role": "user", "content": "d"}], "max_tokens": 6, "stop": "\x00"},
+                          timeout=60).json()
+        assert r["choices"][0]["finish_reason"] == "length"                 # no stop string in the output
+        bad = requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 2, "stop": [3]}, timeout=60)
+        assert bad.status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+
+
+class _SlowEngine(FakeEngine):
+    """5 ms per step: a long request is still running when its client leaves."""
+
+    def step(self):
+        import time as _t
+
+        _t.sleep(0.005)
+        super().step()
+
+
+def test_closing_a_stream_aborts_the_request():
+    eng = _SlowEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    try:
+        g = server.submit_stream([1, 2, 3], 1000, timeout=60)
+        assert next(g)                      # the request is running
+        g.close()                           # the client went away
+        import time as _t
+        deadline = _t.time() + 10
+        while not eng.aborted and _t.time() < deadline:
+            _t.sleep(0.01)
+        assert eng.aborted and not eng.sched.running
+        assert eng.steps < 1000                     # it did not run to max_tokens
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+
+
+def _lockstep_stop(rank, world):
+    import datetime
+
+    import torch.distributed as dist
+
+    ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, ctrl, rank, world)
+    results = {}
+    if rank == 0:
+        def clients():
+            tok = srv_mod.ByteTokenizer()
+            a = threading.Thread(target=lambda: results.update(
+                a=server.submit([100], 40, timeout=60, with_reason=True, stop_strs=("fg",), detok=tok.decode)))
+            b = threading.Thread(target=lambda: results.update(b=server.submit([5, 6], 8, timeout=60,
+                                                                              with_reason=True)))
+            a.start()
+            b.start()
+            a.join()
+            b.join()
+            server.stop()
+
+        threading.Thread(target=clients, daemon=True).start()
+    server.serve_forever()
+    return {"aborted": eng.aborted, "results": results, "steps": eng.steps}
+
+
+def test_stop_string_abort_is_lockstep_on_two_ranks():
+    res = run_ranks(_lockstep_stop, 2)
+    assert res[0]["aborted"] == res[1]["aborted"] and len(res[0]["aborted"]) == 1   # same request, same step
+    assert res[0]["steps"] == res[1]["steps"]
+    assert res[0]["results"]["a"] == ([100, 101, 102, 103], "stop")
+    assert res[0]["results"]["b"] == (expected([5, 6], 8), "length")
+
+
+def test_stream_holds_back_a_possible_stop_string_then_releases_it():
+    """Text that may begin a stop string is held until the next tokens
+    decide: stop "fz" never completes, so "f" is sent later, not lost."""
+    import json as _json
+
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        for path, body, get in (
+                ("/v1/completions", {"prompt": [100]}, lambda c: c["choices"][0]["text"]),
+                ("/v1/chat/completions", {"messages": [{"role": "user", "content": "d"}]},
+                 lambda c: c["choices"][0].get("delta", {}).get("content", ""))):
+            with requests.post(base + path, json={**body, "max_tokens": 3, "stop": ["fz"], "stream": True},
+                               stream=True, timeout=60) as resp:
+                chunks = [_json.loads(ln[6:]) for ln in resp.iter_lines(decode_unicode=True)
+                          if ln.startswith("data: ") and ln != "data: [DONE]"]
+            assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+            if path == "/v1/completions":
+                assert "".join(get(c) for c in chunks) == "def"
+                assert [get(c) for c in chunks[:3]] == ["d", "e", ""]   # "f" held: it may start "fz"
+            assert get(chunks[-1]) != "" or path != "/v1/completions"
     finally:
         server.stop()
         loop.join(timeout=30)
