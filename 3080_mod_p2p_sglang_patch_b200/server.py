@@ -512,7 +512,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         else:
             text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
             prompt = tok.encode(text)
-        max_tokens = int(body.get("max_tokens", 16))
+        max_tokens = int(body.get("max_completion_tokens") or body.get("max_tokens") or 16)
         stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
             _check(prompt, max_tokens)
@@ -528,6 +528,57 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": _text(out, stops)},
                              "token_ids": out, "finish_reason": fin}],
                 "usage": _usage(prompt, out)}
+
+    @app.post("/generate")
+    async def generate(body: dict):
+        """sglang's native API: ``text`` (or ``input_ids``) and a
+        ``sampling_params`` dict (max_new_tokens, temperature, top_k, top_p,
+        seed, stop, stop_token_ids). Returns ``text``, ``output_ids`` and
+        ``meta_info`` (prompt / completion tokens, finish_reason); with
+        ``stream`` the same objects, cumulative, as server-sent events."""
+        if body.get("input_ids") is not None:
+            prompt = _prompt_ids(body["input_ids"])
+        else:
+            prompt = _prompt_ids(body.get("text", ""))
+        sp = dict(body.get("sampling_params") or {})
+        max_new = int(sp.get("max_new_tokens", 128))
+        stop, stops = _stop(sp), _stop_strs(sp)
+        sampling = _sampling(sp)
+
+        def result(out, fin):
+            return {"text": _text(out, stops), "output_ids": out,
+                    "meta_info": {"prompt_tokens": len(prompt), "completion_tokens": len(out),
+                                  "finish_reason": {"type": fin}}}
+
+        if body.get("stream"):
+            _check(prompt, max_new)
+
+            def gen():
+                out, reason = [], []
+                try:
+                    stream = server.submit_stream(prompt, max_new, stop_ids=stop, reason_out=reason,
+                                                  sampling=sampling, stop_strs=stops, detok=tok.decode)
+                    fin = None
+                    try:
+                        for toks in stream:
+                            out += toks
+                            if stops and _find_stop(tok.decode(out), stops) >= 0:
+                                fin = "stop"
+                                break
+                            yield "data: " + json.dumps(result(out, None)) + "\n\n"
+                    finally:
+                        stream.close()
+                    fin = fin or (reason[0] if reason else "length")
+                    if fin == "stop" and stops:
+                        out = out[:_stop_prefix(out, stops, tok.decode) or len(out)]
+                    yield "data: " + json.dumps(result(out, fin)) + "\n\n"
+                except (RuntimeError, TimeoutError) as e:
+                    yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
+                yield "data: [DONE]\n\n"
+
+            return StreamingResponse(iterate_in_threadpool(gen()), media_type="text/event-stream")
+        out, fin = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops)
+        return result(out, fin)
 
     return app
 

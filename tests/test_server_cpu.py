@@ -494,3 +494,34 @@ def test_stream_holds_back_a_possible_stop_string_then_releases_it():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_sglang_native_generate_endpoint():
+    import json as _json
+
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/generate", json={"input_ids": [100], "sampling_params": {
+            "max_new_tokens": 12, "stop": "fg"}}, timeout=60).json()
+        assert r["text"] == "de" and r["output_ids"] == [100, 101, 102, 103]
+        assert r["meta_info"] == {"prompt_tokens": 1, "completion_tokens": 4, "finish_reason": {"type": "stop"}}
+        r = requests.post(base + "/generate", json={"text": "ab", "sampling_params": {"max_new_tokens": 3}},
+                          timeout=60).json()
+        assert r["output_ids"] == expected(list(b"ab"), 3) and r["meta_info"]["finish_reason"]["type"] == "length"
+        with requests.post(base + "/generate", json={"input_ids": [5], "sampling_params": {"max_new_tokens": 4},
+                                                     "stream": True}, stream=True, timeout=60) as resp:
+            objs = [_json.loads(ln[6:]) for ln in resp.iter_lines(decode_unicode=True)
+                    if ln.startswith("data: ") and ln != "data: [DONE]"]
+        assert objs[-1]["output_ids"] == expected([5], 4) and objs[-1]["meta_info"]["finish_reason"]["type"] == "length"
+        assert all(len(a["output_ids"]) <= len(b["output_ids"]) for a, b in zip(objs, objs[1:]))   # cumulative
+        # chat accepts the newer max_completion_tokens spelling
+        c = requests.post(base + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                               "max_completion_tokens": 2}, timeout=60).json()
+        assert c["usage"]["completion_tokens"] == 2
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
