@@ -138,6 +138,10 @@ def build_router_app(router: Router):
     async def chat(body: dict):
         return await forward("/v1/chat/completions", body)
 
+    @app.post("/generate")
+    async def generate(body: dict):
+        return await forward("/generate", body)
+
     @app.get("/v1/models")
     def models():
         for i in range(len(router.backends)):

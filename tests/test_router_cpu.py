@@ -75,6 +75,9 @@ def test_router_over_two_replicas():
         assert 'mbx_requests_total{replica="0"}' in m and 'mbx_requests_total{replica="1"}' in m
         assert 'mbx_router_requests_total{replica="1"}' in m
         assert requests.get(base + "/v1/models", timeout=30).json()["data"][0]["id"] == "fake"
+        g = requests.post(base + "/generate", json={"input_ids": [3], "sampling_params": {"max_new_tokens": 2}},
+                          timeout=60).json()
+        assert g["output_ids"] == expected([3], 2)
         # one replica goes down: requests fail over to the other
         _stop(reps[1])
         time.sleep(0.5)
