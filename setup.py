@@ -56,7 +56,7 @@ ext_modules = [
 setup(
     name="mailbox-ar-b200",
     version="0.1.0",
-    packages=[PKG],
+    packages=[PKG, "mailbox_ar_b200"],
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -59,3 +59,16 @@ def test_fault_rules(monkeypatch):
     monkeypatch.delenv("MBX_INJECT_FAULT")
     faults.check("symm_import", 0)
     faults.set_attempt(0)
+
+
+def test_importable_alias_resolves_to_the_same_modules():
+    """``mailbox_ar_b200.X`` is the package under an importable name: the
+    same module objects (one copy of the extensions and their state)."""
+    import mailbox_ar_b200.engine as e
+    from mailbox_ar_b200.parallel import MailboxAR
+
+    real = importlib.import_module("3080_mod_p2p_sglang_patch_b200")
+    assert e is importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine")
+    assert MailboxAR is integ.MailboxAR
+    import mailbox_ar_b200
+    assert mailbox_ar_b200.engine is real.engine
