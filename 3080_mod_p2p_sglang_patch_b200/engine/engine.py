@@ -104,7 +104,20 @@ class LLMEngine:
             use = r.sampled and (draw is None or draw[i])
             params.append(r.sampling if use else GREEDY)
             gens.append((r.rng if r.rng is not None else self._rng) if use else None)
-        return sample(logits, params, gens)
+        tokens = sample(logits, params, gens)
+        want = [i for i, r in enumerate(reqs) if r.logprobs is not None and (draw is None or draw[i])]
+        if want:
+            # logprobs of the model's own distribution (before temperature / top-k / top-p)
+            rows = torch.tensor(want, device=logits.device)
+            lp = torch.log_softmax(logits.index_select(0, rows).float(), dim=-1)
+            chosen = lp.gather(1, tokens.index_select(0, rows)[:, None])[:, 0].tolist()
+            k = max(reqs[i].logprobs for i in want)
+            top_v, top_i = torch.topk(lp, k, dim=-1) if k > 0 else (lp[:, :0], lp[:, :0].long())
+            top_v, top_i = top_v.tolist(), top_i.tolist()
+            for j, i in enumerate(want):
+                n = reqs[i].logprobs
+                reqs[i].token_logprobs.append((chosen[j], list(zip(top_i[j][:n], top_v[j][:n]))))
+        return tokens
 
     @classmethod
     def from_pretrained(cls, model_dir: str, tp=None, device=None, **kw):
@@ -165,17 +178,21 @@ class LLMEngine:
                     decode_lse=self.max_batch * nq * max_splits)
 
     # ------------------------------------------------------------------ requests
-    def add_request(self, prompt, max_new_tokens: int, stop_ids=(), sampling=None) -> Request:
+    def add_request(self, prompt, max_new_tokens: int, stop_ids=(), sampling=None, logprobs: int = None) -> Request:
         """Queue a prompt (token ids); generation ends after ``max_new_tokens``
         or after any token in ``stop_ids`` (kept in the output). ``sampling``:
         a SamplingParams (None = greedy); a seeded one draws from its own
         generator, an unseeded one from the engine's (seeded identically on
-        every TP rank, so all ranks draw the same tokens)."""
+        every TP rank, so all ranks draw the same tokens). ``logprobs`` k:
+        record each generated token's logprob and the k most likely
+        alternatives in ``request.token_logprobs`` (such requests run eagerly,
+        with full logits)."""
         prompt = list(prompt)
         if prompt and (min(prompt) < 0 or max(prompt) >= self.cfg.vocab):
             raise ValueError(f"prompt token ids must lie in [0, {self.cfg.vocab})")
         req = Request(self._next_rid, prompt, max_new_tokens, t_arrive=time.perf_counter(),
-                      stop_ids=tuple(int(t) for t in stop_ids), sampling=sampling)
+                      stop_ids=tuple(int(t) for t in stop_ids), sampling=sampling,
+                      logprobs=None if logprobs is None else int(logprobs))
         if sampling is not None and not sampling.greedy and sampling.seed is not None:
             req.rng = torch.Generator(device=self.device)
             req.rng.manual_seed(int(sampling.seed))
@@ -201,7 +218,7 @@ class LLMEngine:
         for p in pieces:
             if not getattr(p.req, "_row_synced", False):
                 self._sync_block_row(p.req)
-        sampled = any(p.completes and p.req.sampled for p in pieces)
+        sampled = any(p.completes and p.req.needs_logits for p in pieces)
         if self.prefill_graph is not None and len(pieces) == 1 and pieces[0].n == self.chunk and not sampled:
             # a full single-request chunk: replay the captured chunk forward
             p = pieces[0]
@@ -294,7 +311,7 @@ class LLMEngine:
             if not getattr(r, "_row_synced", False):
                 self._sync_block_row(r)
         ids, pos, kv_len, slots, rows = self.decode_inputs(batch.reqs)
-        sampled = any(r.sampled for r in batch.reqs)
+        sampled = any(r.needs_logits for r in batch.reqs)
         if self.graphs is not None and self.graphs.can_run(len(ids)) and not sampled:
             return self.graphs.run(ids, pos, kv_len, slots, rows)
         B = len(ids)
@@ -350,14 +367,16 @@ class LLMEngine:
         self.run()
         return [r.output for r in reqs]
 
-    def generate_text(self, prompts, sampling_params: dict = None):
+    def generate_text(self, prompts, sampling_params: dict = None, return_logprob: bool = False,
+                      top_logprobs_num: int = 0):
         """Offline generation over text, in the shape of sglang's offline
         engine: ``prompts`` is a string or a list of strings;
         ``sampling_params`` a dict of ``max_new_tokens`` (16), ``temperature``
         (0: greedy), ``top_k``, ``top_p``, ``seed`` and ``stop_token_ids``
         (default: the checkpoint's EOS ids). Returns one ``{"text",
         "token_ids", "finish_reason"}`` per prompt (a single dict for a single
-        string)."""
+        string). ``return_logprob`` adds ``"logprobs"``: per generated token
+        (id, logprob, [(id, logprob)] of the ``top_logprobs_num`` most likely)."""
         from .tokenizer import ByteTokenizer
 
         tok = self.tokenizer or ByteTokenizer()
@@ -371,8 +390,14 @@ class LLMEngine:
             raise ValueError(f"unknown sampling params: {', '.join(sorted(sp))}")
         sampling = SamplingParams(temp, top_k, top_p, seed) if temp > 0 else None
         single = isinstance(prompts, str)
-        reqs = [self.add_request(tok.encode(p), max_new, stop, sampling) for p in ([prompts] if single else prompts)]
+        lp = int(top_logprobs_num) if return_logprob else None
+        reqs = [self.add_request(tok.encode(p), max_new, stop, sampling, logprobs=lp)
+                for p in ([prompts] if single else prompts)]
         self.run()
-        out = [{"text": tok.decode(r.output), "token_ids": list(r.output), "finish_reason": r.finish_reason}
-               for r in reqs]
+        out = []
+        for r in reqs:
+            o = {"text": tok.decode(r.output), "token_ids": list(r.output), "finish_reason": r.finish_reason}
+            if return_logprob:
+                o["logprobs"] = [(t, c, top) for t, (c, top) in zip(r.output, r.token_logprobs)]
+            out.append(o)
         return out[0] if single else out

@@ -33,10 +33,20 @@ class Request:
     cached_pages: int = 0      # leading prompt pages served by the prefix cache
     sampling: object = None    # engine.sampling.SamplingParams (None = greedy)
     rng: object = None         # torch.Generator of a seeded sampled request
+    # log-probabilities of the generated tokens: None = off, k >= 0 = each
+    # token's logprob plus the k most likely alternatives
+    logprobs: int = None
+    # per generated token: (logprob, [(token id, logprob), ...] top-k)
+    token_logprobs: list = dataclasses.field(default_factory=list)
 
     @property
     def sampled(self):
         return self.sampling is not None and not self.sampling.greedy
+
+    @property
+    def needs_logits(self):
+        """Full logits are needed: a sampled request, or one that returns logprobs."""
+        return self.sampled or self.logprobs is not None
 
     @property
     def total_len(self):

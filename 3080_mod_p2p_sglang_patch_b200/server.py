@@ -50,9 +50,11 @@ logger = logging.getLogger(__name__)
 
 class _Pending:
     __slots__ = ("prompt", "max_new", "stop_ids", "sampling", "event", "output", "error", "stream", "req", "sent",
-                 "reason", "sid", "stop_strs", "detok", "checked", "stop_hit", "abort_sent")
+                 "reason", "sid", "stop_strs", "detok", "checked", "stop_hit", "abort_sent", "logprobs",
+                 "token_logprobs")
 
-    def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None, sid=-1, stop_strs=(), detok=None):
+    def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None, sid=-1, stop_strs=(), detok=None,
+                 logprobs=None):
         self.prompt = prompt
         self.max_new = max_new
         self.stop_ids = tuple(stop_ids)
@@ -64,6 +66,8 @@ class _Pending:
         self.checked = 0          # output tokens already checked for stop strings
         self.stop_hit = False
         self.abort_sent = False
+        self.logprobs = logprobs        # None, or k: per-token logprob + k alternatives
+        self.token_logprobs = []
         self.reason = "length"
         self.event = threading.Event()
         self.output = None
@@ -142,15 +146,22 @@ class EngineServer:
         default. ``stop_strs``: generation also ends once ``detok(tokens)``
         contains one of them; the tokens are then cut to the shortest prefix
         whose text contains it."""
+        p = self._submit_pending(prompt, max_new, timeout, stop_ids, sampling, stop_strs, detok)
+        return (p.output, p.reason) if with_reason else p.output
+
+    def _submit_pending(self, prompt, max_new, timeout=None, stop_ids=None, sampling=None, stop_strs=(), detok=None,
+                        logprobs=None):
+        """``submit`` returning the finished request record (output, reason,
+        token_logprobs)."""
         p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
-                          detok=detok)
+                          detok=detok, logprobs=logprobs)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if isinstance(p.error, ValueError):  # the engine rejected the request itself
             raise p.error
         if p.error is not None:
             raise RuntimeError(p.error)
-        return (p.output, p.reason) if with_reason else p.output
+        return p
 
     def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None,
                       sampling=None, stop_strs=(), detok=None):
@@ -200,7 +211,7 @@ class EngineServer:
             raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
                              f"max sequence {limit}")
 
-    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None, stop_strs=(), detok=None):
+    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None, stop_strs=(), detok=None, logprobs=None):
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
@@ -209,7 +220,7 @@ class EngineServer:
             raise ValueError("stop strings need a detokenizer")
         p = _Pending(list(prompt), int(max_new), stream=stream,
                      stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling,
-                     sid=next(self._sids), stop_strs=stop_strs, detok=detok)
+                     sid=next(self._sids), stop_strs=stop_strs, detok=detok, logprobs=logprobs)
         self.q.put(p)
         return p
 
@@ -243,12 +254,13 @@ class EngineServer:
                 if int(ar.all_reduce(cnt)[0].item()) == 0:
                     return cmds  # nothing new (rank 0's list is empty too)
             self.stats["control_gloo"] += 1
-            payload = [[c if not isinstance(c, _Pending) else (c.sid, c.prompt, c.max_new, c.stop_ids, c.sampling)
-                        for c in cmds]]
+            payload = [[c if not isinstance(c, _Pending) else
+                        (c.sid, c.prompt, c.max_new, c.stop_ids, c.sampling, c.logprobs) for c in cmds]]
             dist.broadcast_object_list(payload, src=0, group=self.group)
             if self.rank != 0:
                 cmds = [c if c == self.SHUTDOWN or c[0] == self.ABORT else
-                        _Pending(c[1], c[2], stop_ids=c[3], sampling=c[4], sid=c[0]) for c in payload[0]]
+                        _Pending(c[1], c[2], stop_ids=c[3], sampling=c[4], sid=c[0], logprobs=c[5])
+                        for c in payload[0]]
         return cmds
 
     def serve_forever(self):
@@ -268,12 +280,14 @@ class EngineServer:
                             eng.abort(rid)
                         continue
                     try:
+                        extra = {} if c.logprobs is None else {"logprobs": c.logprobs}
                         if c.sampling is None:
-                            req = eng.add_request(c.prompt, c.max_new, c.stop_ids)
+                            req = eng.add_request(c.prompt, c.max_new, c.stop_ids, **extra)
                         else:
                             from .engine.sampling import SamplingParams
 
-                            req = eng.add_request(c.prompt, c.max_new, c.stop_ids, SamplingParams(*c.sampling))
+                            req = eng.add_request(c.prompt, c.max_new, c.stop_ids, SamplingParams(*c.sampling),
+                                                  **extra)
                     except ValueError as e:
                         # rejected on every rank alike (same command, same engine
                         # state): fail this request only
@@ -315,6 +329,7 @@ class EngineServer:
                             k = _stop_prefix(out, p.stop_strs, p.detok)
                             if k is not None:
                                 out, p.reason = out[:k], "stop"
+                        p.token_logprobs = list(getattr(r, "token_logprobs", None) or [])[:len(out)]
                         p.finish(output=out)
         except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
             for p in self._by_rid.values():
@@ -415,14 +430,38 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         return (t, int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
                 None if seed is None else int(seed))
 
-    def _run(prompt, max_tokens, stop=None, sampling=None, stops=()):
+    def _run(prompt, max_tokens, stop=None, sampling=None, stops=(), logprobs=None):
+        """(output ids, finish reason, per-token logprobs)."""
         try:
-            return server.submit(prompt, max_tokens, stop_ids=stop, with_reason=True, sampling=sampling,
-                                 stop_strs=stops, detok=tok.decode)
+            p = server._submit_pending(prompt, max_tokens, stop_ids=stop, sampling=sampling, stop_strs=stops,
+                                       detok=tok.decode, logprobs=logprobs)
+            return p.output, p.reason, p.token_logprobs
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         except (RuntimeError, TimeoutError) as e:
             raise HTTPException(503, str(e)) from e
+
+    def _tok_str(t):
+        return tok.decode([t])
+
+    def _completion_logprobs(out, lps):
+        """OpenAI completions ``logprobs``: tokens, token_logprobs,
+        top_logprobs (token text -> logprob), text_offset."""
+        toks = [_tok_str(t) for t in out]
+        offs, o = [], 0
+        for t in toks:
+            offs.append(o)
+            o += len(t)
+        return {"tokens": toks, "token_logprobs": [lp for lp, _ in lps],
+                "top_logprobs": [{_tok_str(i): v for i, v in top} for _, top in lps], "text_offset": offs}
+
+    def _chat_logprobs(out, lps):
+        """OpenAI chat ``logprobs``: content = [{token, logprob, bytes, top_logprobs}]."""
+        def item(t, lp):
+            s_ = _tok_str(t)
+            return {"token": s_, "logprob": lp, "bytes": list(s_.encode("utf-8"))}
+        return {"content": [{**item(t, lp), "top_logprobs": [item(i, v) for i, v in top]}
+                            for t, (lp, top) in zip(out, lps)]}
 
     def _usage(prompt, out):
         return {"prompt_tokens": len(prompt), "completion_tokens": len(out), "total_tokens": len(prompt) + len(out)}
@@ -498,10 +537,13 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 "id": cid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": fin}],
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
-        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops)
+        lp = body.get("logprobs")
+        lp = None if lp is None or lp is False else int(lp)
+        out, fin, lps = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp)
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
                 "model": model_name,
-                "choices": [{"index": 0, "text": _text(out, stops), "token_ids": out, "finish_reason": fin}],
+                "choices": [{"index": 0, "text": _text(out, stops), "token_ids": out, "finish_reason": fin,
+                             "logprobs": _completion_logprobs(out, lps) if lp is not None else None}],
                 "usage": _usage(prompt, out)}
 
     @app.post("/v1/chat/completions")
@@ -522,11 +564,13 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 "choices": [{"index": 0, "delta": {"content": text} if (toks or text) else {},
                              "token_ids": toks, "finish_reason": fin}],
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
-        out, fin = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops)
+        lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
+        out, fin, lps = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp)
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
                 "model": model_name,
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": _text(out, stops)},
-                             "token_ids": out, "finish_reason": fin}],
+                             "token_ids": out, "finish_reason": fin,
+                             "logprobs": _chat_logprobs(out, lps) if lp is not None else None}],
                 "usage": _usage(prompt, out)}
 
     @app.post("/generate")
@@ -577,7 +621,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(iterate_in_threadpool(gen()), media_type="text/event-stream")
-        out, fin = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops)
+        out, fin, _ = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops)
         return result(out, fin)
 
     return app

@@ -336,3 +336,66 @@ def test_abort_mid_decode_frees_the_request_and_spares_the_others():
     assert b.finish_reason == "length" and len(b.output) == 6
     _assert_near_argmax(CFG, eng.weights, pb, b.output)
     assert eng.kv.alloc.free == eng.kv.alloc.num_blocks - 1 and not eng.abort(a.rid)
+
+
+def test_logprobs_of_generated_tokens():
+    eng = _engine()
+    g = torch.Generator().manual_seed(16)
+    p1, p2 = (torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (33, 20))
+    a = eng.add_request(p1, 4, logprobs=3)                       # greedy, with logprobs
+    b = eng.add_request(p2, 4, sampling=eng_mod.SamplingParams(1.0, 20, 1.0, 5), logprobs=0)
+    c = eng.add_request(p2, 4)                                   # neither: unaffected
+    eng.run()
+    assert len(a.token_logprobs) == 4 and len(b.token_logprobs) == 4 and c.token_logprobs == []
+    for t, (lp, top) in zip(a.output, a.token_logprobs):
+        assert len(top) == 3 and top[0] == (t, lp)              # greedy: the chosen token is the top one
+        assert lp <= 0 and [v for _, v in top] == sorted((v for _, v in top), reverse=True)
+    seq = list(p1)
+    for t, (lp, _) in zip(a.output, a.token_logprobs):        # against the dense fp32 distribution
+        _, logits = _dense(CFG, eng.weights, seq)
+        assert abs(lp - float(torch.log_softmax(logits[-1], -1)[t])) < 0.05
+        seq.append(t)
+    assert all(top == [] and lp <= 0 for lp, top in b.token_logprobs)
+    _assert_near_argmax(CFG, eng.weights, p2, c.output)
+    r = _engine().generate_text("hi", {"max_new_tokens": 2}, return_logprob=True, top_logprobs_num=2)
+    assert [x[0] for x in r["logprobs"]] == r["token_ids"] and all(len(x[2]) == 2 for x in r["logprobs"])
+
+
+def _serve_logprobs_worker(rank, world):
+    import datetime
+
+    import torch.distributed as dist
+
+    par = importlib.import_module(f"{PKG}.parallel")
+    srv_mod = importlib.import_module(f"{PKG}.server")
+    tp = par.TPGroup(None, "cpu", use_mailbox=False)
+    ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
+    eng = eng_mod.LLMEngine(CFG, tp=tp, impl="oracle", device="cpu", full_init=True, seed=0, max_batch=4,
+                            max_seq=512, chunk=64)
+    server = srv_mod.EngineServer(eng, ctrl, rank, world, max_prompt=512)
+    out = {}
+    if rank == 0:
+        def client():
+            p = server._submit_pending(list(range(20, 60)), 3, timeout=120, logprobs=2)
+            q = server._submit_pending(list(range(5, 25)), 3, timeout=120)
+            out.update(lp=(p.output, p.token_logprobs), plain=q.output)
+            server.stop()
+
+        threading.Thread(target=client, daemon=True).start()
+    done = []
+    orig = eng.sched._finish
+
+    def spy(req):  # every rank records what it finished, with the logprobs
+        done.append((req.rid, list(req.output), [round(x, 5) for x, _ in req.token_logprobs]))
+        orig(req)
+
+    eng.sched._finish = spy
+    server.serve_forever()
+    return {"out": out, "done": done}
+
+
+def test_logprobs_through_the_two_rank_lockstep_server():
+    res = run_ranks(_serve_logprobs_worker, 2, timeout=300)
+    assert res[0]["done"] == res[1]["done"] and len(res[0]["done"]) == 2   # same tokens and logprobs on both
+    toks, lps = res[0]["out"]["lp"]
+    assert len(lps) == len(toks) == 3 and all(top[0][0] == t for t, (_, top) in zip(toks, lps))

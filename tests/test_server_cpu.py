@@ -47,10 +47,11 @@ class FakeEngine:
         self.aborted = []   # (rid, steps taken when it was aborted)
         self.steps = 0
 
-    def add_request(self, prompt, max_new, stop_ids=(), sampling=None):
+    def add_request(self, prompt, max_new, stop_ids=(), sampling=None, logprobs=None):
         r = _Req(self.n, prompt, max_new)
         r.stop_ids = tuple(stop_ids)
         r.sampling = sampling
+        r.logprobs, r.token_logprobs = logprobs, []
         self.sampling_seen.append(sampling)
         self.n += 1
         self.sched.running.append(r)
@@ -73,6 +74,9 @@ class FakeEngine:
         self.steps += 1
         for r in list(self.sched.running):
             r.output.append((sum(r.prompt) + len(r.output)) % 1000)
+            if r.logprobs is not None:  # a fixed distribution: the token, then its successor
+                t = r.output[-1]
+                r.token_logprobs.append((-0.25, [(t, -0.25), (t + 1, -2.0)][:r.logprobs]))
             r.token_times.append(_t.perf_counter())
             r.finish_reason = "stop" if r.output[-1] in r.stop_ids else \
                 ("length" if len(r.output) >= r.max_new else None)
@@ -318,10 +322,10 @@ class _PickyEngine(FakeEngine):
 
     max_request_tokens = 64
 
-    def add_request(self, prompt, max_new, stop_ids=(), sampling=None):
+    def add_request(self, prompt, max_new, stop_ids=(), sampling=None, **kw):
         if prompt and prompt[0] == 999:
             raise ValueError("too large for the KV cache")
-        return super().add_request(prompt, max_new, stop_ids, sampling)
+        return super().add_request(prompt, max_new, stop_ids, sampling, **kw)
 
 
 def test_engine_rejection_fails_one_request_and_the_server_keeps_serving():
@@ -521,6 +525,35 @@ def test_sglang_native_generate_endpoint():
         c = requests.post(base + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
                                                                "max_completion_tokens": 2}, timeout=60).json()
         assert c["usage"]["completion_tokens"] == 2
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+
+
+def test_openai_logprobs_formats():
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 3, "logprobs": 2},
+                          timeout=60).json()
+        lp = r["choices"][0]["logprobs"]
+        assert lp["tokens"] == ["d", "e", "f"] and lp["token_logprobs"] == [-0.25] * 3
+        assert lp["top_logprobs"][0] == {"d": -0.25, "e": -2.0} and lp["text_offset"] == [0, 1, 2]
+        r = requests.post(base + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                               "max_tokens": 2, "logprobs": True, "top_logprobs": 1},
+                          timeout=60).json()
+        content = r["choices"][0]["logprobs"]["content"]
+        assert len(content) == 2 and content[0]["logprob"] == -0.25 and len(content[0]["top_logprobs"]) == 1
+        assert content[0]["bytes"] == list(content[0]["token"].encode())
+        r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 2}, timeout=60).json()
+        assert r["choices"][0]["logprobs"] is None
+        # with a stop string the logprobs are cut with the tokens
+        r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 9, "logprobs": 0,
+                                                          "stop": "fg"}, timeout=60).json()
+        assert len(r["choices"][0]["logprobs"]["tokens"]) == len(r["choices"][0]["token_ids"]) == 4
     finally:
         server.stop()
         loop.join(timeout=30)
