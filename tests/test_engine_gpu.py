@@ -108,3 +108,18 @@ def test_native_qwen2_qkv_bias_forward_matches_dense():
     want, _ = _dense(cfg, _host(eng.weights), prompt)
     got = _prompt_hidden(eng, prompt, 64).cpu()
     assert _cos(got, want[-1]) > 0.995
+
+
+def test_native_engine_logprobs_match_the_dense_distribution():
+    eng = _engine()
+    g = torch.Generator().manual_seed(15)
+    p = torch.randint(0, CFG.vocab, (45,), generator=g).tolist()
+    r = eng.add_request(p, 4, logprobs=3)
+    eng.run()
+    w = _host(eng.weights)
+    seq = list(p)
+    for t, (lp, top) in zip(r.output, r.token_logprobs):
+        assert top[0] == (t, lp) and len(top) == 3
+        _, logits = _dense(CFG, w, seq)
+        assert abs(lp - float(torch.log_softmax(logits[-1], -1)[t])) < TOL
+        seq.append(t)
