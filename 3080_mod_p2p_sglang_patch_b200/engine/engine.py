@@ -98,7 +98,9 @@ class LLMEngine:
         ``draw[i]`` False: row i's token is not used (a prefill piece that
         does not end its prompt), so it is taken greedily and no generator
         advances."""
-        logits = self.model.full_logits(hidden)
+        return self._sample_from_logits(self.model.full_logits(hidden), reqs, draw)
+
+    def _sample_from_logits(self, logits, reqs, draw=None):
         params, gens = [], []
         for i, r in enumerate(reqs):
             use = r.sampled and (draw is None or draw[i])
@@ -178,7 +180,8 @@ class LLMEngine:
                     decode_lse=self.max_batch * nq * max_splits)
 
     # ------------------------------------------------------------------ requests
-    def add_request(self, prompt, max_new_tokens: int, stop_ids=(), sampling=None, logprobs: int = None) -> Request:
+    def add_request(self, prompt, max_new_tokens: int, stop_ids=(), sampling=None, logprobs: int = None,
+                    prompt_logprobs: bool = False) -> Request:
         """Queue a prompt (token ids); generation ends after ``max_new_tokens``
         or after any token in ``stop_ids`` (kept in the output). ``sampling``:
         a SamplingParams (None = greedy); a seeded one draws from its own
@@ -186,13 +189,15 @@ class LLMEngine:
         every TP rank, so all ranks draw the same tokens). ``logprobs`` k:
         record each generated token's logprob and the k most likely
         alternatives in ``request.token_logprobs`` (such requests run eagerly,
-        with full logits)."""
+        with full logits). ``prompt_logprobs``: also score the prompt, into
+        ``request.prompt_token_logprobs`` (None for the first token; its
+        prefill skips the prefix cache)."""
         prompt = list(prompt)
         if prompt and (min(prompt) < 0 or max(prompt) >= self.cfg.vocab):
             raise ValueError(f"prompt token ids must lie in [0, {self.cfg.vocab})")
         req = Request(self._next_rid, prompt, max_new_tokens, t_arrive=time.perf_counter(),
                       stop_ids=tuple(int(t) for t in stop_ids), sampling=sampling,
-                      logprobs=None if logprobs is None else int(logprobs))
+                      logprobs=None if logprobs is None else int(logprobs), prompt_logprobs=bool(prompt_logprobs))
         if sampling is not None and not sampling.greedy and sampling.seed is not None:
             req.rng = torch.Generator(device=self.device)
             req.rng.manual_seed(int(sampling.seed))
@@ -218,7 +223,8 @@ class LLMEngine:
         for p in pieces:
             if not getattr(p.req, "_row_synced", False):
                 self._sync_block_row(p.req)
-        sampled = any(p.completes and p.req.needs_logits for p in pieces)
+        sampled = any(p.completes and p.req.needs_logits for p in pieces) or \
+            any(p.req.prompt_logprobs for p in pieces)
         if self.prefill_graph is not None and len(pieces) == 1 and pieces[0].n == self.chunk and not sampled:
             # a full single-request chunk: replay the captured chunk forward
             p = pieces[0]
@@ -239,10 +245,53 @@ class LLMEngine:
             rows.append(req.slot)
             off += p.n
             last.append(off - 1)
+        if any(p.req.prompt_logprobs for p in pieces):
+            return self._prefill_scoring(pieces, ids, pos, slots, q_lens, kv_lens, rows)
         if sampled:
             hidden = self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, last, return_hidden=True)
             return self._sample_tokens(hidden, [p.req for p in pieces], [p.completes for p in pieces])
         return self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, last)
+
+    def _prefill_scoring(self, pieces, ids, pos, slots, q_lens, kv_lens, rows):
+        """A prefill batch holding a request that scores its prompt: hidden
+        states of every row of such pieces (the last row of the others), full
+        logits, the prompt tokens' logprobs recorded on their requests, then
+        the next token per piece from its last row."""
+        want, last_of = [], []
+        off = 0
+        for p in pieces:
+            if p.req.prompt_logprobs:
+                want.extend(range(off, off + p.n))
+            else:
+                want.append(off + p.n - 1)
+            last_of.append(len(want) - 1)
+            off += p.n
+        hidden = self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, want, return_hidden=True)
+        logits = self.model.full_logits(hidden)
+        row = 0
+        for p in pieces:
+            req = p.req
+            if req.prompt_logprobs:
+                lp = torch.log_softmax(logits[row:row + p.n].float(), dim=-1)
+                if p.start == 0:
+                    req.prompt_token_logprobs.append(None)  # the first token has no context
+                n_next = min(p.n, len(req.prompt) - 1 - p.start)  # positions whose next token is in the prompt
+                if n_next > 0:
+                    nxt = torch.tensor(req.prompt[p.start + 1:p.start + 1 + n_next], device=lp.device)
+                    vals = lp[:n_next].gather(1, nxt[:, None])[:, 0].tolist()
+                    k = req.logprobs or 0
+                    if k > 0:
+                        tv, ti = torch.topk(lp[:n_next], k, dim=-1)
+                        tops = [list(zip(a, b)) for a, b in zip(ti.tolist(), tv.tolist())]
+                    else:
+                        tops = [[] for _ in vals]
+                    req.prompt_token_logprobs.extend(zip(vals, tops))
+                row += p.n
+            else:
+                row += 1
+        sel = torch.tensor(last_of, device=logits.device)
+        return self._sample_from_logits(logits.index_select(0, sel), [p.req for p in pieces],
+                                        [p.completes for p in pieces])
 
     def forward_prefill(self, ids, pos, slots, q_lens, kv_lens, rows, last, return_hidden=False):
         """One prefill forward from host lists; returns next token per piece

@@ -38,6 +38,10 @@ class Request:
     logprobs: int = None
     # per generated token: (logprob, [(token id, logprob), ...] top-k)
     token_logprobs: list = dataclasses.field(default_factory=list)
+    # logprobs of the prompt's own tokens (scoring; "echo"): one entry per
+    # prompt token, None for the first (it has no context)
+    prompt_logprobs: bool = False
+    prompt_token_logprobs: list = dataclasses.field(default_factory=list)
 
     @property
     def sampled(self):
@@ -46,7 +50,7 @@ class Request:
     @property
     def needs_logits(self):
         """Full logits are needed: a sampled request, or one that returns logprobs."""
-        return self.sampled or self.logprobs is not None
+        return self.sampled or self.logprobs is not None or self.prompt_logprobs
 
     @property
     def total_len(self):
@@ -115,7 +119,7 @@ class Scheduler:
             req = self.waiting[0]
             need = (len(req.prompt) + req.max_new + PAGE - 1) // PAGE
             matched = []
-            if pc is not None:
+            if pc is not None and not req.prompt_logprobs:  # scoring needs every position computed
                 # full pages before the last prompt token (that one is always computed)
                 matched = pc.match(req.prompt, (len(req.prompt) - 1) // PAGE)
             if self.allocator is not None:

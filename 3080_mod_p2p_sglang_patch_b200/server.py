@@ -51,10 +51,10 @@ logger = logging.getLogger(__name__)
 class _Pending:
     __slots__ = ("prompt", "max_new", "stop_ids", "sampling", "event", "output", "error", "stream", "req", "sent",
                  "reason", "sid", "stop_strs", "detok", "checked", "stop_hit", "abort_sent", "logprobs",
-                 "token_logprobs")
+                 "token_logprobs", "prompt_logprobs", "prompt_token_logprobs")
 
     def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None, sid=-1, stop_strs=(), detok=None,
-                 logprobs=None):
+                 logprobs=None, prompt_logprobs=False):
         self.prompt = prompt
         self.max_new = max_new
         self.stop_ids = tuple(stop_ids)
@@ -68,6 +68,8 @@ class _Pending:
         self.abort_sent = False
         self.logprobs = logprobs        # None, or k: per-token logprob + k alternatives
         self.token_logprobs = []
+        self.prompt_logprobs = bool(prompt_logprobs)  # also score the prompt (echo)
+        self.prompt_token_logprobs = []
         self.reason = "length"
         self.event = threading.Event()
         self.output = None
@@ -150,11 +152,11 @@ class EngineServer:
         return (p.output, p.reason) if with_reason else p.output
 
     def _submit_pending(self, prompt, max_new, timeout=None, stop_ids=None, sampling=None, stop_strs=(), detok=None,
-                        logprobs=None):
+                        logprobs=None, prompt_logprobs=False):
         """``submit`` returning the finished request record (output, reason,
-        token_logprobs)."""
+        token_logprobs, prompt_token_logprobs)."""
         p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
-                          detok=detok, logprobs=logprobs)
+                          detok=detok, logprobs=logprobs, prompt_logprobs=prompt_logprobs)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if isinstance(p.error, ValueError):  # the engine rejected the request itself
@@ -211,7 +213,8 @@ class EngineServer:
             raise ValueError(f"prompt + max_tokens = {len(prompt) + max_new} exceeds the engine's "
                              f"max sequence {limit}")
 
-    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None, stop_strs=(), detok=None, logprobs=None):
+    def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None, stop_strs=(), detok=None, logprobs=None,
+                 prompt_logprobs=False):
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
@@ -220,7 +223,8 @@ class EngineServer:
             raise ValueError("stop strings need a detokenizer")
         p = _Pending(list(prompt), int(max_new), stream=stream,
                      stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling,
-                     sid=next(self._sids), stop_strs=stop_strs, detok=detok, logprobs=logprobs)
+                     sid=next(self._sids), stop_strs=stop_strs, detok=detok, logprobs=logprobs,
+                     prompt_logprobs=prompt_logprobs)
         self.q.put(p)
         return p
 
@@ -255,12 +259,13 @@ class EngineServer:
                     return cmds  # nothing new (rank 0's list is empty too)
             self.stats["control_gloo"] += 1
             payload = [[c if not isinstance(c, _Pending) else
-                        (c.sid, c.prompt, c.max_new, c.stop_ids, c.sampling, c.logprobs) for c in cmds]]
+                        (c.sid, c.prompt, c.max_new, c.stop_ids, c.sampling, c.logprobs, c.prompt_logprobs)
+                        for c in cmds]]
             dist.broadcast_object_list(payload, src=0, group=self.group)
             if self.rank != 0:
                 cmds = [c if c == self.SHUTDOWN or c[0] == self.ABORT else
-                        _Pending(c[1], c[2], stop_ids=c[3], sampling=c[4], sid=c[0], logprobs=c[5])
-                        for c in payload[0]]
+                        _Pending(c[1], c[2], stop_ids=c[3], sampling=c[4], sid=c[0], logprobs=c[5],
+                                 prompt_logprobs=c[6]) for c in payload[0]]
         return cmds
 
     def serve_forever(self):
@@ -281,6 +286,8 @@ class EngineServer:
                         continue
                     try:
                         extra = {} if c.logprobs is None else {"logprobs": c.logprobs}
+                        if c.prompt_logprobs:
+                            extra["prompt_logprobs"] = True
                         if c.sampling is None:
                             req = eng.add_request(c.prompt, c.max_new, c.stop_ids, **extra)
                         else:
@@ -330,6 +337,7 @@ class EngineServer:
                             if k is not None:
                                 out, p.reason = out[:k], "stop"
                         p.token_logprobs = list(getattr(r, "token_logprobs", None) or [])[:len(out)]
+                        p.prompt_token_logprobs = list(getattr(r, "prompt_token_logprobs", None) or [])
                         p.finish(output=out)
         except BaseException as e:  # noqa: BLE001 - fail every waiter, then re-raise
             for p in self._by_rid.values():
@@ -430,12 +438,12 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         return (t, int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
                 None if seed is None else int(seed))
 
-    def _run(prompt, max_tokens, stop=None, sampling=None, stops=(), logprobs=None):
-        """(output ids, finish reason, per-token logprobs)."""
+    def _run(prompt, max_tokens, stop=None, sampling=None, stops=(), logprobs=None, prompt_logprobs=False):
+        """(output ids, finish reason, per-token logprobs, prompt logprobs)."""
         try:
             p = server._submit_pending(prompt, max_tokens, stop_ids=stop, sampling=sampling, stop_strs=stops,
-                                       detok=tok.decode, logprobs=logprobs)
-            return p.output, p.reason, p.token_logprobs
+                                       detok=tok.decode, logprobs=logprobs, prompt_logprobs=prompt_logprobs)
+            return p.output, p.reason, p.token_logprobs, p.prompt_token_logprobs
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         except (RuntimeError, TimeoutError) as e:
@@ -446,14 +454,16 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
 
     def _completion_logprobs(out, lps):
         """OpenAI completions ``logprobs``: tokens, token_logprobs,
-        top_logprobs (token text -> logprob), text_offset."""
+        top_logprobs (token text -> logprob), text_offset. An entry of None
+        (the first echoed prompt token) has no logprob."""
         toks = [_tok_str(t) for t in out]
         offs, o = [], 0
         for t in toks:
             offs.append(o)
             o += len(t)
-        return {"tokens": toks, "token_logprobs": [lp for lp, _ in lps],
-                "top_logprobs": [{_tok_str(i): v for i, v in top} for _, top in lps], "text_offset": offs}
+        return {"tokens": toks, "token_logprobs": [None if e is None else e[0] for e in lps],
+                "top_logprobs": [None if e is None else {_tok_str(i): v for i, v in e[1]} for e in lps],
+                "text_offset": offs}
 
     def _chat_logprobs(out, lps):
         """OpenAI chat ``logprobs``: content = [{token, logprob, bytes, top_logprobs}]."""
@@ -529,6 +539,10 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
     async def completions(body: dict):
         prompt = _prompt_ids(body.get("prompt", ""))
         max_tokens = int(body.get("max_tokens", 16))
+        echo = bool(body.get("echo"))
+        score_only = echo and max_tokens == 0  # scoring: the prompt's logprobs, nothing generated
+        if score_only:
+            max_tokens = 1
         stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
             _check(prompt, max_tokens)
@@ -539,11 +553,19 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
         lp = body.get("logprobs")
         lp = None if lp is None or lp is False else int(lp)
-        out, fin, lps = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp)
+        out, fin, lps, plps = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp,
+                                                      echo and lp is not None)
+        if score_only:
+            out, lps, fin = [], [], "length"
+        text = _text(out, stops)
+        logprobs = None
+        if lp is not None:
+            logprobs = _completion_logprobs((prompt if echo else []) + out, (plps if echo else []) + lps)
+        if echo:
+            text = tok.decode(prompt) + text
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
                 "model": model_name,
-                "choices": [{"index": 0, "text": _text(out, stops), "token_ids": out, "finish_reason": fin,
-                             "logprobs": _completion_logprobs(out, lps) if lp is not None else None}],
+                "choices": [{"index": 0, "text": text, "token_ids": out, "finish_reason": fin, "logprobs": logprobs}],
                 "usage": _usage(prompt, out)}
 
     @app.post("/v1/chat/completions")
@@ -565,7 +587,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                              "token_ids": toks, "finish_reason": fin}],
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
         lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
-        out, fin, lps = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp)
+        out, fin, lps, _ = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp)
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
                 "model": model_name,
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": _text(out, stops)},
@@ -588,11 +610,29 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         max_new = int(sp.get("max_new_tokens", 128))
         stop, stops = _stop(sp), _stop_strs(sp)
         sampling = _sampling(sp)
+        want_lp = bool(body.get("return_logprob"))
+        top_n = int(body.get("top_logprobs_num") or 0)
+        start = body.get("logprob_start_len")
+        score_prompt = want_lp and start is not None and int(start) >= 0
 
-        def result(out, fin):
-            return {"text": _text(out, stops), "output_ids": out,
-                    "meta_info": {"prompt_tokens": len(prompt), "completion_tokens": len(out),
-                                  "finish_reason": {"type": fin}}}
+        def _lp_list(toks, lps):
+            """sglang's [logprob, token id, None] triples (and top-n lists)."""
+            vals = [[None if e is None else e[0], t, None] for t, e in zip(toks, lps)]
+            tops = [None if e is None else [[v, i, None] for i, v in e[1]] for e in lps]
+            return vals, tops
+
+        def result(out, fin, lps=(), plps=()):
+            meta = {"prompt_tokens": len(prompt), "completion_tokens": len(out), "finish_reason": {"type": fin}}
+            if want_lp:
+                meta["output_token_logprobs"], tops = _lp_list(out, lps)
+                if top_n:
+                    meta["output_top_logprobs"] = tops
+                if score_prompt:
+                    k = int(start)
+                    meta["input_token_logprobs"], itops = _lp_list(prompt[k:], list(plps)[k:])
+                    if top_n:
+                        meta["input_top_logprobs"] = itops
+            return {"text": _text(out, stops), "output_ids": out, "meta_info": meta}
 
         if body.get("stream"):
             _check(prompt, max_new)
@@ -621,8 +661,9 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(iterate_in_threadpool(gen()), media_type="text/event-stream")
-        out, fin, _ = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops)
-        return result(out, fin)
+        out, fin, lps, plps = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops,
+                                                      top_n if want_lp else None, score_prompt)
+        return result(out, fin, lps, plps)
 
     return app
 

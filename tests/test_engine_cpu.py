@@ -399,3 +399,26 @@ def test_logprobs_through_the_two_rank_lockstep_server():
     assert res[0]["done"] == res[1]["done"] and len(res[0]["done"]) == 2   # same tokens and logprobs on both
     toks, lps = res[0]["out"]["lp"]
     assert len(lps) == len(toks) == 3 and all(top[0][0] == t for t, (_, top) in zip(toks, lps))
+
+
+def test_prompt_logprobs_score_every_prompt_token():
+    eng = _engine(chunk=32, prefix_cache=True)
+    g = torch.Generator().manual_seed(17)
+    prompt = torch.randint(0, CFG.vocab, (70,), generator=g).tolist()        # three chunks
+    warm = eng.add_request(prompt[:40] + [1, 2], 2)                          # fills the prefix cache
+    eng.run()
+    r = eng.add_request(prompt, 3, logprobs=2, prompt_logprobs=True)
+    plain = eng.add_request(prompt[:20], 3)                                   # shares the batch, unaffected
+    eng.run()
+    assert r.cached_pages == 0                                                # scoring skips the cache
+    assert len(r.prompt_token_logprobs) == len(prompt) and r.prompt_token_logprobs[0] is None
+    _, logits = _dense(CFG, eng.weights, prompt)
+    lp = torch.log_softmax(logits, dim=-1)
+    for j in range(1, len(prompt)):                                           # logprob of token j given 0..j-1
+        v, top = r.prompt_token_logprobs[j]
+        assert abs(v - float(lp[j - 1, prompt[j]])) < 0.05
+        assert len(top) == 2 and top[0][1] >= top[1][1]
+    assert len(r.token_logprobs) == len(r.output) == 3
+    _assert_near_argmax(CFG, eng.weights, prompt, r.output)
+    _assert_near_argmax(CFG, eng.weights, prompt[:20], plain.output)
+    assert warm.output and eng.kv.alloc.free + eng.prefix_cache.evictable == eng.kv.alloc.num_blocks - 1

@@ -123,3 +123,16 @@ def test_native_engine_logprobs_match_the_dense_distribution():
         _, logits = _dense(CFG, w, seq)
         assert abs(lp - float(torch.log_softmax(logits[-1], -1)[t])) < TOL
         seq.append(t)
+
+
+def test_native_prompt_logprobs_match_the_dense_distribution():
+    eng = _engine(chunk=32)
+    g = torch.Generator().manual_seed(16)
+    prompt = torch.randint(0, CFG.vocab, (70,), generator=g).tolist()
+    r = eng.add_request(prompt, 2, prompt_logprobs=True)
+    eng.run()
+    assert len(r.prompt_token_logprobs) == len(prompt) and r.prompt_token_logprobs[0] is None
+    _, logits = _dense(CFG, _host(eng.weights), prompt)
+    lp = torch.log_softmax(logits, dim=-1)
+    err = max(abs(r.prompt_token_logprobs[j][0] - float(lp[j - 1, prompt[j]])) for j in range(1, len(prompt)))
+    assert err < TOL

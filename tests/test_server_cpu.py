@@ -47,11 +47,13 @@ class FakeEngine:
         self.aborted = []   # (rid, steps taken when it was aborted)
         self.steps = 0
 
-    def add_request(self, prompt, max_new, stop_ids=(), sampling=None, logprobs=None):
+    def add_request(self, prompt, max_new, stop_ids=(), sampling=None, logprobs=None, prompt_logprobs=False):
         r = _Req(self.n, prompt, max_new)
         r.stop_ids = tuple(stop_ids)
         r.sampling = sampling
         r.logprobs, r.token_logprobs = logprobs, []
+        # scoring: every prompt token after the first at -1.0
+        r.prompt_token_logprobs = [None] + [(-1.0, [])] * (len(prompt) - 1) if prompt_logprobs else []
         self.sampling_seen.append(sampling)
         self.n += 1
         self.sched.running.append(r)
@@ -554,6 +556,39 @@ def test_openai_logprobs_formats():
         r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 9, "logprobs": 0,
                                                           "stop": "fg"}, timeout=60).json()
         assert len(r["choices"][0]["logprobs"]["tokens"]) == len(r["choices"][0]["token_ids"]) == 4
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+
+
+def test_echo_scores_the_prompt():
+    """``echo`` with ``logprobs``: the prompt's tokens and logprobs come first
+    (None for the first token); ``max_tokens`` 0 scores without generating.
+    sglang's /generate returns the same through ``return_logprob``."""
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/v1/completions", json={"prompt": [97, 98, 99], "max_tokens": 0, "echo": True,
+                                                          "logprobs": 0}, timeout=60).json()
+        ch = r["choices"][0]
+        assert ch["text"] == "abc" and ch["token_ids"] == []
+        assert ch["logprobs"]["tokens"] == ["a", "b", "c"] and ch["logprobs"]["token_logprobs"] == [None, -1.0, -1.0]
+        assert ch["logprobs"]["top_logprobs"][0] is None
+        r = requests.post(base + "/v1/completions", json={"prompt": [97, 98], "max_tokens": 2, "echo": True,
+                                                          "logprobs": 1}, timeout=60).json()
+        lp = r["choices"][0]["logprobs"]
+        assert lp["tokens"][:2] == ["a", "b"] and len(lp["tokens"]) == 4
+        assert lp["token_logprobs"] == [None, -1.0, -0.25, -0.25]
+        assert r["choices"][0]["text"].startswith("ab")
+        g = requests.post(base + "/generate", json={"input_ids": [97, 98, 99], "sampling_params": {
+            "max_new_tokens": 2}, "return_logprob": True, "logprob_start_len": 0, "top_logprobs_num": 1},
+            timeout=60).json()
+        m = g["meta_info"]
+        assert m["input_token_logprobs"] == [[None, 97, None], [-1.0, 98, None], [-1.0, 99, None]]
+        assert [x[1] for x in m["output_token_logprobs"]] == g["output_ids"] and len(m["output_top_logprobs"]) == 2
     finally:
         server.stop()
         loop.join(timeout=30)
