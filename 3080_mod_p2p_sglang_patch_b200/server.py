@@ -473,6 +473,31 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         return {"content": [{**item(t, lp), "top_logprobs": [item(i, v) for i, v in top]}
                             for t, (lp, top) in zip(out, lps)]}
 
+    def _n(body):
+        n = int(body.get("n") or 1)
+        if n < 1 or n > 16:
+            raise HTTPException(400, "n must lie in 1..16")
+        if n > 1 and body.get("stream"):
+            raise HTTPException(400, "n > 1 is not supported with stream")
+        return n
+
+    async def _run_n(n, prompt, max_tokens, stop, sampling, stops, lp, plp=False):
+        """n independent requests for one prompt (choice i draws with seed + i
+        when the request is seeded); each result as ``_run`` returns it."""
+        import asyncio
+
+        def samp(i):
+            if sampling is None or sampling[3] is None:
+                return sampling
+            return sampling[:3] + (sampling[3] + i,)
+
+        return await asyncio.gather(*[run_in_threadpool(_run, prompt, max_tokens, stop, samp(i), stops, lp, plp)
+                                      for i in range(n)])
+
+    def _usage_n(prompt, outs):
+        c = sum(len(o) for o in outs)
+        return {"prompt_tokens": len(prompt), "completion_tokens": c, "total_tokens": len(prompt) + c}
+
     def _usage(prompt, out):
         return {"prompt_tokens": len(prompt), "completion_tokens": len(out), "total_tokens": len(prompt) + len(out)}
 
@@ -545,6 +570,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
             max_tokens = 1
         stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
+            _n(body)
             _check(prompt, max_tokens)
             cid, created = f"cmpl-{next(ids)}", int(time.time())
             return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
@@ -553,20 +579,21 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
         lp = body.get("logprobs")
         lp = None if lp is None or lp is False else int(lp)
-        out, fin, lps, plps = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp,
-                                                      echo and lp is not None)
-        if score_only:
-            out, lps, fin = [], [], "length"
-        text = _text(out, stops)
-        logprobs = None
-        if lp is not None:
-            logprobs = _completion_logprobs((prompt if echo else []) + out, (plps if echo else []) + lps)
-        if echo:
-            text = tok.decode(prompt) + text
+        runs = await _run_n(_n(body), prompt, max_tokens, stop, _sampling(body), stops, lp, echo and lp is not None)
+        choices, outs = [], []
+        for i, (out, fin, lps, plps) in enumerate(runs):
+            if score_only:
+                out, lps, fin = [], [], "length"
+            text = _text(out, stops)
+            logprobs = None
+            if lp is not None:
+                logprobs = _completion_logprobs((prompt if echo else []) + out, (plps if echo else []) + lps)
+            if echo:
+                text = tok.decode(prompt) + text
+            choices.append({"index": i, "text": text, "token_ids": out, "finish_reason": fin, "logprobs": logprobs})
+            outs.append(out)
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
-                "model": model_name,
-                "choices": [{"index": 0, "text": text, "token_ids": out, "finish_reason": fin, "logprobs": logprobs}],
-                "usage": _usage(prompt, out)}
+                "model": model_name, "choices": choices, "usage": _usage_n(prompt, outs)}
 
     @app.post("/v1/chat/completions")
     async def chat(body: dict):
@@ -579,6 +606,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
         max_tokens = int(body.get("max_completion_tokens") or body.get("max_tokens") or 16)
         stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
+            _n(body)
             _check(prompt, max_tokens)
             cid, created = f"chatcmpl-{next(ids)}", int(time.time())
             return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
@@ -587,13 +615,12 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None):
                              "token_ids": toks, "finish_reason": fin}],
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
         lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
-        out, fin, lps, _ = await run_in_threadpool(_run, prompt, max_tokens, stop, _sampling(body), stops, lp)
+        runs = await _run_n(_n(body), prompt, max_tokens, stop, _sampling(body), stops, lp)
+        choices = [{"index": i, "message": {"role": "assistant", "content": _text(out, stops)}, "token_ids": out,
+                    "finish_reason": fin, "logprobs": _chat_logprobs(out, lps) if lp is not None else None}
+                   for i, (out, fin, lps, _) in enumerate(runs)]
         return {"id": f"chatcmpl-{next(ids)}", "object": "chat.completion", "created": int(time.time()),
-                "model": model_name,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": _text(out, stops)},
-                             "token_ids": out, "finish_reason": fin,
-                             "logprobs": _chat_logprobs(out, lps) if lp is not None else None}],
-                "usage": _usage(prompt, out)}
+                "model": model_name, "choices": choices, "usage": _usage_n(prompt, [r[0] for r in runs])}
 
     @app.post("/generate")
     async def generate(body: dict):

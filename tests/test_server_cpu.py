@@ -593,3 +593,25 @@ def test_echo_scores_the_prompt():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_n_choices_per_request():
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/v1/completions", json={"prompt": [7, 8], "max_tokens": 3, "n": 3,
+                                                          "temperature": 0.9, "seed": 40}, timeout=60).json()
+        assert [c["index"] for c in r["choices"]] == [0, 1, 2] and r["usage"]["completion_tokens"] == 9
+        assert sorted(s_.seed for s_ in eng.sampling_seen[-3:]) == [40, 41, 42]   # choice i draws with seed + i
+        c = requests.post(base + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                               "max_tokens": 2, "n": 2}, timeout=60).json()
+        assert len(c["choices"]) == 2 and c["usage"]["completion_tokens"] == 4
+        bad = requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 2, "n": 2, "stream": True},
+                            timeout=60)
+        assert bad.status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
