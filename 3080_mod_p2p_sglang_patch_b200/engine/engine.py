@@ -123,15 +123,19 @@ class LLMEngine:
 
     @classmethod
     def from_pretrained(cls, model_dir: str, tp=None, device=None, **kw):
-        """Engine over a Hugging Face Llama checkpoint directory (this rank's
-        shards only are read; see models/loader.py)."""
+        """Engine over a Hugging Face checkpoint directory (this rank's shards
+        only are read; see models/loader.py). ``int4_weights=True`` keeps an
+        AWQ checkpoint's linears packed (int4 GEMV for decode batches, a
+        per-layer bf16 expansion for prefill) instead of expanding them once."""
         from ..models.loader import load_llama
 
         from ..models.loader import stop_token_ids
         from .tokenizer import HFTokenizer
 
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        cfg, w = load_llama(model_dir, tp.rank if tp is not None else 0, tp.world_size if tp is not None else 1, dev)
+        int4 = bool(kw.pop("int4_weights", False))
+        cfg, w = load_llama(model_dir, tp.rank if tp is not None else 0, tp.world_size if tp is not None else 1, dev,
+                            int4=int4)
         kw.setdefault("max_seq", min(cfg.max_pos, 8192))
         eng = cls(cfg, tp=tp, device=dev, weights=w, **kw)
         try:
@@ -176,8 +180,15 @@ class LLMEngine:
                     need = max(need, splits * M * N)
         nq = cfg.heads // t
         max_splits = 64
+        awq_ws = awq_w = 0
+        for L in self.weights.layers[:1]:  # every layer has the same shapes
+            for w in L.values():
+                if isinstance(w, ops.Int4Weight):
+                    N_, K_ = w.shape
+                    awq_ws = max(awq_ws, (K_ // w.group) * ops.AWQ_GEMV_MAX_ROWS * N_)
+                    awq_w = max(awq_w, N_ * K_)
         ops.reserve(self.device, gemm_elems=need, decode_o=self.max_batch * nq * max_splits * D,
-                    decode_lse=self.max_batch * nq * max_splits)
+                    decode_lse=self.max_batch * nq * max_splits, awq_ws=awq_ws, awq_w=awq_w)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt, max_new_tokens: int, stop_ids=(), sampling=None, logprobs: int = None,

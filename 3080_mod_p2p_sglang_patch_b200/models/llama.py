@@ -100,10 +100,13 @@ class LlamaWeights:
         self.nq, self.nkv = nq, nkv
 
 
-def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch):
+def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch, linear=None):
     """A LlamaWeights whose shards come from ``fetch(name, rows=None, cols=None)``
     (full-tensor names as in Hugging Face Llama checkpoints, [out, in] layout;
-    ``rows`` / ``cols`` = (start, stop) slices), converted to bf16 on ``device``."""
+    ``rows`` / ``cols`` = (start, stop) slices), converted to bf16 on ``device``.
+    ``linear`` (same signature): a decoder linear's shard as an
+    ``ops.Int4Weight``, or None to read it through ``fetch`` (int4 checkpoints
+    kept packed)."""
     cfg.check_tp(tp_size)
     t, r = tp_size, tp_rank
     H, D, F_ = cfg.hidden, cfg.head_dim, cfg.ffn
@@ -120,6 +123,20 @@ def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch):
         per = full_cols // t
         return get(name, cols=(r * per, (r + 1) * per))
 
+    def packed(names_rows):
+        """Int4 shards of several column-parallel parts, concatenated; None
+        unless every part is stored quantized."""
+        if linear is None:
+            return None
+        parts = [linear(n, rows=(r * (f // t), (r + 1) * (f // t))) for n, f in names_rows]
+        return ops.Int4Weight.cat(parts) if all(p is not None for p in parts) else None
+
+    def packed_cols(name, full_cols):
+        if linear is None:
+            return None
+        per = full_cols // t
+        return linear(name, cols=(r * per, (r + 1) * per))
+
     w = LlamaWeights.__new__(LlamaWeights)
     w.cfg = cfg
     w.embed = rows_of("model.embed_tokens.weight", cfg.vocab)
@@ -130,17 +147,25 @@ def _shard_weights(cfg: LlamaConfig, tp_rank: int, tp_size: int, device, fetch):
         if cfg.qk_norm:  # per-head norms: [head_dim], the same on every rank
             L["q_norm"] = get(p + "self_attn.q_norm.weight")
             L["k_norm"] = get(p + "self_attn.k_norm.weight")
-        L["qkv"] = torch.cat([rows_of(p + "self_attn.q_proj.weight", cfg.heads * D),
-                              rows_of(p + "self_attn.k_proj.weight", cfg.kv_heads * D),
-                              rows_of(p + "self_attn.v_proj.weight", cfg.kv_heads * D)], 0).contiguous()
+        qkv_parts = [(p + "self_attn.q_proj.weight", cfg.heads * D), (p + "self_attn.k_proj.weight", cfg.kv_heads * D),
+                     (p + "self_attn.v_proj.weight", cfg.kv_heads * D)]
+        L["qkv"] = packed(qkv_parts)
+        if L["qkv"] is None:
+            L["qkv"] = torch.cat([rows_of(n, f) for n, f in qkv_parts], 0).contiguous()
         if cfg.qkv_bias:  # Qwen2: sharded like the projections' rows
             L["qkv_bias"] = torch.cat([rows_of(p + "self_attn.q_proj.bias", cfg.heads * D),
                                        rows_of(p + "self_attn.k_proj.bias", cfg.kv_heads * D),
                                        rows_of(p + "self_attn.v_proj.bias", cfg.kv_heads * D)], 0).contiguous()
-        L["o"] = cols_of(p + "self_attn.o_proj.weight", cfg.heads * D)
-        L["gate_up"] = torch.cat([rows_of(p + "mlp.gate_proj.weight", F_),
-                                  rows_of(p + "mlp.up_proj.weight", F_)], 0).contiguous()
-        L["down"] = cols_of(p + "mlp.down_proj.weight", F_)
+        L["o"] = packed_cols(p + "self_attn.o_proj.weight", cfg.heads * D)
+        if L["o"] is None:
+            L["o"] = cols_of(p + "self_attn.o_proj.weight", cfg.heads * D)
+        gu_parts = [(p + "mlp.gate_proj.weight", F_), (p + "mlp.up_proj.weight", F_)]
+        L["gate_up"] = packed(gu_parts)
+        if L["gate_up"] is None:
+            L["gate_up"] = torch.cat([rows_of(n, f) for n, f in gu_parts], 0).contiguous()
+        L["down"] = packed_cols(p + "mlp.down_proj.weight", F_)
+        if L["down"] is None:
+            L["down"] = cols_of(p + "mlp.down_proj.weight", F_)
         w.layers.append(L)
     w.norm = get("model.norm.weight")
     w.lm_head = rows_of("lm_head.weight", cfg.vocab)
@@ -170,20 +195,29 @@ class LlamaTP:
         self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, self.device,
                                         dict(cfg.rope_scaling) if cfg.rope_scaling else None)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        # AWQ int4 layers (ops.Int4Weight): their GEMMs are not fused with the
+        # collectives that follow them
+        self.int4 = any(isinstance(v, ops.Int4Weight) for L in weights.layers for v in L.values())
         # sequence parallel (parallel/sp.py): used for batches of at least
         # ``sp_min_rows`` tokens that fit its buffers; None = off
         self.sp = None
         self.sp_min_rows = 256
 
     def enable_sp(self, sp, min_rows: int = 256):
-        """Run large batches sequence-parallel (native TP build only)."""
-        if self.impl != "native" or self.tp_size == 1:
+        """Run large batches sequence-parallel (native TP build, bf16 weights)."""
+        if self.impl != "native" or self.tp_size == 1 or self.int4:
             return
         self.sp = sp
         self.sp_min_rows = int(min_rows)
 
     # ------------------------------------------------------------ building blocks
     def _linear(self, x, w, out=None, residual=None):
+        if isinstance(w, ops.Int4Weight):  # AWQ int4 kept packed
+            if self.impl == "oracle":
+                return oracle.awq_gemm(x, w, out=out, residual=residual)
+            if self.impl != "native":
+                raise ValueError("int4 weights run on the native build only")
+            return ops.awq_gemm(x, w, out=out, residual=residual)
         if self.impl == "oracle":
             return oracle.gemm(x, w, out=out, residual=residual)
         if self.impl == "torch":
@@ -300,7 +334,7 @@ class LlamaTP:
                 # residual add fused into the GEMM epilogue, in place
                 self._linear(o.view(T, nq * D), L["o"], out=residual, residual=residual)
                 x = ops.rmsnorm(residual, L["ln2"], cfg.eps)
-            elif self.impl == "native":
+            elif self.impl == "native" and not isinstance(L["o"], ops.Int4Weight):
                 # fused row-parallel GEMM -> allreduce -> residual + RMSNorm
                 x = self.tp.gemm_all_reduce_rmsnorm(o.view(T, nq * D), L["o"], residual, L["ln2"], cfg.eps)
             else:
@@ -312,7 +346,7 @@ class LlamaTP:
             if self.tp_size == 1 and self.impl == "native":
                 self._linear(a, L["down"], out=residual, residual=residual)
                 x = ops.rmsnorm(residual, nxt, cfg.eps)
-            elif self.impl == "native":
+            elif self.impl == "native" and not isinstance(L["down"], ops.Int4Weight):
                 x = self.tp.gemm_all_reduce_rmsnorm(a, L["down"], residual, nxt, cfg.eps)
             else:
                 part = self._linear(a, L["down"])

@@ -224,10 +224,31 @@ class _AwqCheckpoint(_Checkpoint):
         self.group = group
         self.device = torch.device(device)
 
-    def fetch(self, name, rows=None, cols=None):
+    def _quantized(self, name):
         base = name[:-len(".weight")] if name.endswith(".weight") else None
         if base is None or name in self.where or base + ".qweight" not in self.where:
+            return None
+        return base
+
+    def fetch(self, name, rows=None, cols=None):
+        if self._quantized(name) is None:
             return super().fetch(name, rows, cols)
+        qw, qz, sc, G = self._parts(name, rows, cols)
+        return awq_dequant(qw, qz, sc, G)
+
+    def fetch_int4(self, name, rows=None, cols=None):
+        """The shard kept packed, as an ``ops.Int4Weight`` on the device
+        (None for a module stored unquantized)."""
+        from ..ops import Int4Weight
+
+        if self._quantized(name) is None:
+            return None
+        qw, qz, sc, G = self._parts(name, rows, cols)
+        return Int4Weight(qw.contiguous(), qz.contiguous(), sc.to(torch.float16).contiguous(), G)
+
+    def _parts(self, name, rows=None, cols=None):
+        """(qweight, qzeros, scales, group) of a shard, on the device."""
+        base = self._quantized(name)
         qw = self.where[base + ".qweight"]
         K = qw.entries[base + ".qweight"]["shape"][0]
         G = K if self.group <= 0 else self.group
@@ -246,14 +267,15 @@ class _AwqCheckpoint(_Checkpoint):
         def part(suffix, r, c):
             return self.where[base + suffix].get(base + suffix, r, c).to(self.device)
 
-        return awq_dequant(part(".qweight", in_rows, pk_cols), part(".qzeros", grp_rows, pk_cols),
-                           part(".scales", grp_rows, out_cols), G)
+        return (part(".qweight", in_rows, pk_cols), part(".qzeros", grp_rows, pk_cols),
+                part(".scales", grp_rows, out_cols), G)
 
 
-def load_llama(model_dir: str, tp_rank: int = 0, tp_size: int = 1, device="cuda"):
+def load_llama(model_dir: str, tp_rank: int = 0, tp_size: int = 1, device="cuda", int4: bool = False):
     """(LlamaConfig, LlamaWeights) of this TP rank from a Hugging Face Llama
-    directory (bf16 / fp16 / fp32, or AWQ int4 dequantized to bf16). Head dim
-    128 (the attention kernels' width) is required."""
+    directory (bf16 / fp16 / fp32, or AWQ int4: dequantized to bf16, or with
+    ``int4`` kept packed as ``ops.Int4Weight`` for the int4 GEMV / dequant
+    path). Head dim 128 (the attention kernels' width) is required."""
     from .llama import _shard_weights
 
     with open(os.path.join(model_dir, "config.json")) as f:
@@ -263,7 +285,8 @@ def load_llama(model_dir: str, tp_rank: int = 0, tp_size: int = 1, device="cuda"
         raise ValueError(f"{model_dir}: head_dim {cfg.head_dim}; the attention kernels need 128")
     qc = hf.get("quantization_config")
     ck = _AwqCheckpoint(model_dir, awq_group_size(qc), device) if qc else _Checkpoint(model_dir)
-    return cfg, _shard_weights(cfg, tp_rank, tp_size, device, ck.fetch)
+    linear = ck.fetch_int4 if (int4 and qc) else None
+    return cfg, _shard_weights(cfg, tp_rank, tp_size, device, ck.fetch, linear)
 
 
 def stop_token_ids(model_dir: str) -> tuple:

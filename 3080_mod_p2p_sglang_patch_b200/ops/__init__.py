@@ -6,6 +6,7 @@ decode split-KV partials, the GEMM error word) comes from a per-device
 workspace that is allocated once and reused, so CUDA-graph capture never
 allocates.
 """
+import dataclasses
 import math
 
 import torch
@@ -29,14 +30,16 @@ class _Workspace:
         self.dec_lse = torch.empty(0, dtype=torch.float32, device=device)
         self.pre_o = torch.empty(0, dtype=torch.float32, device=device)
         self.pre_lse = torch.empty(0, dtype=torch.float32, device=device)
+        self.awq_ws = torch.empty(0, dtype=torch.float32, device=device)    # int4 GEMV partial sums
+        self.awq_w = torch.empty(0, dtype=torch.bfloat16, device=device)    # one layer dequantized
         self._retired = []
 
-    def _grow(self, name, n, minimum):
+    def _grow(self, name, n, minimum, dtype=torch.float32):
         buf = getattr(self, name)
         if buf.numel() < n:
             if buf.numel():
                 self._retired.append(buf)
-            buf = torch.empty(max(n, minimum), dtype=torch.float32, device=self.device)
+            buf = torch.empty(max(n, minimum), dtype=dtype, device=self.device)
             setattr(self, name, buf)
         return buf
 
@@ -48,6 +51,9 @@ class _Workspace:
 
     def prefill(self, n_o, n_lse):
         return self._grow("pre_o", n_o, 1 << 20), self._grow("pre_lse", n_lse, 1 << 14)
+
+    def awq(self, n_ws=0, n_w=0):
+        return self._grow("awq_ws", n_ws, 1 << 16), self._grow("awq_w", n_w, 1 << 16, torch.bfloat16)
 
 
 _WS = {}
@@ -63,13 +69,15 @@ def workspace(device) -> _Workspace:
     return ws
 
 
-def reserve(device, gemm_elems=0, decode_o=0, decode_lse=0):
+def reserve(device, gemm_elems=0, decode_o=0, decode_lse=0, awq_ws=0, awq_w=0):
     """Pre-size the scratch buffers (call before CUDA-graph capture)."""
     ws = workspace(device)
     if gemm_elems:
         ws.gemm(gemm_elems)
     if decode_o or decode_lse:
         ws.decode(decode_o, decode_lse)
+    if awq_ws or awq_w:
+        ws.awq(awq_ws, awq_w)
 
 
 def gemm_error(device=None) -> int:
@@ -94,6 +102,69 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
     # reduction (pass ws.counters) measured no faster at 1 token and slower at 64
     C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, None)
     launches.add(2 if s > 1 else 1)
+    return out
+
+
+@dataclasses.dataclass
+class Int4Weight:
+    """A linear layer's weight kept as AWQ int4 (``gemm`` packing): qweight
+    int32 [K, N/8], qzeros int32 [K/G, N/8], scales fp16 [K/G, N]. ``shape``
+    is the dense weight's [N, K], as for a bf16 weight."""
+    qweight: torch.Tensor
+    qzeros: torch.Tensor
+    scales: torch.Tensor
+    group: int
+
+    @property
+    def shape(self):
+        return (self.qweight.shape[1] * 8, self.qweight.shape[0])
+
+    @property
+    def device(self):
+        return self.qweight.device
+
+    @staticmethod
+    def cat(parts):
+        """Concatenated along the output dimension (fused qkv / gate_up)."""
+        g = {p.group for p in parts}
+        if len(g) != 1:
+            raise ValueError("int4 weights with different group sizes")
+        return Int4Weight(torch.cat([p.qweight for p in parts], 1).contiguous(),
+                          torch.cat([p.qzeros for p in parts], 1).contiguous(),
+                          torch.cat([p.scales for p in parts], 1).contiguous(), g.pop())
+
+
+AWQ_GEMV_MAX_ROWS = 8
+
+
+def awq_gemm(a: torch.Tensor, w: Int4Weight, out: torch.Tensor = None, residual: torch.Tensor = None):
+    """out[M, N] = a @ W^T (+ residual) for an int4 weight: the int4 GEMV
+    (CUDA cores) up to 8 rows, else the layer dequantized to bf16 into a
+    reused scratch buffer and the tcgen05 GEMM."""
+    C = cuda_ext()
+    M = a.shape[0]
+    N, K = w.shape
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    ws = workspace(a.device)
+    if M <= AWQ_GEMV_MAX_ROWS and w.group <= 256:
+        part, _ = ws.awq(n_ws=(K // w.group) * M * N)
+        C.awq_gemv(a, w.qweight, w.qzeros, w.scales, w.group, part, out, residual)
+        launches.add(2)
+        return out
+    _, wbuf = ws.awq(n_w=N * K)
+    dense = wbuf[:N * K].view(N, K)
+    C.awq_dequant(w.qweight, w.qzeros, w.scales, w.group, dense)
+    launches.add(1)
+    return gemm(a, dense, out=out, residual=residual)
+
+
+def awq_dequant(w: Int4Weight) -> torch.Tensor:
+    """bf16 [N, K] copy of an int4 weight (a new tensor)."""
+    N, K = w.shape
+    out = torch.empty((N, K), dtype=torch.bfloat16, device=w.device)
+    cuda_ext().awq_dequant(w.qweight, w.qzeros, w.scales, w.group, out)
+    launches.add(1)
     return out
 
 

@@ -31,6 +31,15 @@ def gemm(a, w, out=None, residual=None, bn: int = 0, splits: int = 0):
     return _emit(ref.gemm(a, w, residual), BF16, out)
 
 
+def awq_gemm(a, w, out=None, residual=None):
+    """``ops.awq_gemm``: the int4 weight dequantized in fp32, then ``gemm``'s
+    rounding."""
+    from ..models.loader import awq_dequant
+
+    dense = awq_dequant(w.qweight, w.qzeros, w.scales, w.group)
+    return _emit(ref.gemm(a, dense, residual), BF16, out)
+
+
 def rmsnorm(x, w, eps, out=None):
     return _emit(ref.rmsnorm(x, w, eps), x.dtype, out)
 

@@ -774,6 +774,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
     ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
     ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
+    ap.add_argument("--int4-weights", action="store_true",
+                    help="keep an AWQ checkpoint's linears packed as int4 (int4 GEMV for decode) instead of "
+                         "expanding them to bf16 at load")
     ap.add_argument("--mem-fraction-static", dest="mem_fraction", type=float, default=None,
                     help="size the KV cache so weights + cache use this fraction of GPU memory "
                          "(default: room for max-batch requests of max-seq tokens)")
@@ -923,7 +926,8 @@ def main(argv=None):
         opts["max_seq"] = args.max_seq
     tokenizer = None
     if model_path:
-        eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, **opts)
+        eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, int4_weights=args.int4_weights,
+                                                **opts)
         cfg = eng.cfg
         tokenizer = eng.tokenizer
         if tokenizer is None:  # token-id prompts still work

@@ -222,6 +222,57 @@ void rope_and_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor co
                         vc, T, (int)nq, (int)nkv, (int)page, cur_stream(), qn, kn, (float)eps);
 }
 
+void check_awq(const torch::Tensor& qweight, const torch::Tensor& qzeros, const torch::Tensor& scales, int64_t G,
+               int64_t& K, int64_t& N) {
+  check_cuda(qweight, "qweight");
+  check_cuda(qzeros, "qzeros");
+  check_cuda(scales, "scales");
+  TORCH_CHECK(qweight.scalar_type() == torch::kInt32 && qzeros.scalar_type() == torch::kInt32 &&
+                  scales.scalar_type() == torch::kHalf,
+              "awq: qweight / qzeros int32, scales fp16");
+  TORCH_CHECK(qweight.is_contiguous() && qzeros.is_contiguous() && scales.is_contiguous(), "awq: contiguous tensors");
+  K = qweight.size(0);
+  N = qweight.size(1) * 8;
+  TORCH_CHECK(G > 0 && K % G == 0 && qzeros.size(0) == K / G && qzeros.size(1) == N / 8 && scales.size(0) == K / G &&
+                  scales.size(1) == N,
+              "awq: shapes of qweight [K, N/8], qzeros [K/G, N/8], scales [K/G, N]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(scales.data_ptr()) % 16 == 0, "awq: scales must be 16-byte aligned");
+}
+
+void awq_gemv(torch::Tensor x, torch::Tensor qweight, torch::Tensor qzeros, torch::Tensor scales, int64_t G,
+              torch::Tensor ws, torch::Tensor out, c10::optional<torch::Tensor> residual) {
+  int64_t K, N;
+  check_awq(qweight, qzeros, scales, G, K, N);
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  TORCH_CHECK(G <= 256, "awq_gemv: group size above 256");
+  TORCH_CHECK(x.dim() == 2 && x.size(1) == K && x.stride(1) == 1, "awq_gemv: x must be [M, K] with unit stride");
+  const int64_t M = x.size(0);
+  TORCH_CHECK(M >= 1 && M <= kAwqGemvMaxRows, "awq_gemv: 1..8 rows");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "awq_gemv: out [M, N]");
+  TORCH_CHECK(ws.scalar_type() == torch::kFloat32 && ws.is_contiguous() && ws.numel() >= (K / G) * M * N,
+              "awq_gemv: fp32 workspace of (K/G) * M * N");
+  const void* res = nullptr;
+  if (residual.has_value()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->sizes() == out.sizes() && residual->strides() == out.strides(),
+                "awq_gemv: residual laid out like out");
+    res = residual->data_ptr();
+  }
+  AwqGemvArgs a{x.data_ptr(), x.stride(0), qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
+                ws.data_ptr<float>(), res, out.data_ptr(), out.stride(0), (int)M, (int)K, (int)N, (int)G};
+  awq_gemv_launch(a, cur_stream());
+}
+
+void awq_dequant(torch::Tensor qweight, torch::Tensor qzeros, torch::Tensor scales, int64_t G, torch::Tensor out) {
+  int64_t K, N;
+  check_awq(qweight, qzeros, scales, G, K, N);
+  check_bf16(out, "out");
+  TORCH_CHECK(out.is_contiguous() && out.numel() >= N * K, "awq_dequant: out must hold bf16 [N, K]");
+  awq_dequant_launch(qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), out.data_ptr(), (int)K, (int)N,
+                     (int)G, cur_stream());
+}
+
 void silu_mul(torch::Tensor x, torch::Tensor out) {
   check_bf16(x, "x");
   check_bf16(out, "out");
@@ -474,6 +525,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("rope_and_cache", &rope_and_cache);
+  m.def("awq_gemv", &awq_gemv);
+  m.def("awq_dequant", &awq_dequant);
   m.def("silu_mul", &silu_mul);
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);

@@ -36,6 +36,26 @@ enum RawKind { kRawPush1 = 0, kRawPush4 = 1, kRawPull4 = 2, kRawMcReduce = 3, kR
 void raw_transport_launch(int kind, void* dst, const void* src, uint64_t nbytes, int grid, int threads,
                           cudaStream_t stream);
 
+// ---- AWQ int4 weights (quant/awq.cu) ------------------------------------------
+constexpr int kAwqGemvMaxRows = 8;
+struct AwqGemvArgs {
+  const void* x;          // bf16 [M, K], row stride ldx
+  int64_t ldx;
+  const void* qweight;    // int32 [K, N/8]
+  const void* qzeros;     // int32 [K/G, N/8]
+  const void* scales;     // fp16 [K/G, N], 16-byte aligned
+  float* ws;              // fp32 [K/G, M, N]: per-group partial sums
+  const void* residual;   // bf16 [M, N] (row stride ldo) or nullptr
+  void* out;              // bf16 [M, N], row stride ldo; may alias residual
+  int64_t ldo;
+  int M, K, N, G;
+};
+// out = x @ W^T (+ residual) for M <= 8 rows, W dequantized on the fly.
+void awq_gemv_launch(const AwqGemvArgs& a, cudaStream_t s);
+// bf16 [N, K] (row-major, the GEMM's weight layout) from the packed tensors.
+void awq_dequant_launch(const void* qweight, const void* qzeros, const void* scales, void* out, int K, int N, int G,
+                        cudaStream_t s);
+
 // ---- elementwise (ops/elementwise.cu) ----------------------------------------
 void rmsnorm_launch(const void* x, void* residual, const void* w, void* out, int64_t M, int H, float eps,
                     cudaStream_t s);

@@ -2,7 +2,7 @@
 
 * ``_cpu``: host-only C++ runtime (CPU mailbox allreduce engine, FD exchange).
 * ``_C``:   CUDA for sm_100a only (symmetric memory, allreduce kernels,
-            tcgen05 GEMM, attention, elementwise ops).
+            tcgen05 GEMM, attention, elementwise ops, AWQ int4 GEMV/dequant).
 
 Usage: ``python setup.py build_ext --inplace`` (``__graft_entry__.build`` does
 this). The arch is passed explicitly as ``-gencode arch=compute_100a,
@@ -47,6 +47,7 @@ ext_modules = [
             src("attn", "attention.cu"),
             src("attn", "decode_noalloc.cu"),
             src("attn", "fmha_tc.cu"),
+            src("quant", "awq.cu"),
         ],
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},

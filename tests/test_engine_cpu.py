@@ -422,3 +422,35 @@ def test_prompt_logprobs_score_every_prompt_token():
     _assert_near_argmax(CFG, eng.weights, prompt, r.output)
     _assert_near_argmax(CFG, eng.weights, prompt[:20], plain.output)
     assert warm.output and eng.kv.alloc.free + eng.prefix_cache.evictable == eng.kv.alloc.num_blocks - 1
+
+
+def _int4_weights(cfg, group=64):
+    """The oracle engine's random weights with every decoder linear quantized
+    to AWQ int4 (packed), plus the dense fp32 weights they stand for."""
+    loader = importlib.import_module(f"{PKG}.models.loader")
+    w = models.LlamaWeights(cfg, 0, 1, "cpu", seed=0, full_init=True)
+    dense = models.LlamaWeights(cfg, 0, 1, "cpu", seed=0, full_init=True)
+    for L, Ld in zip(w.layers, dense.layers):
+        for k in ("qkv", "o", "gate_up", "down"):
+            qw, qz, s = models.awq_quantize(L[k], group)
+            L[k] = ops.Int4Weight(qw, qz, s, group)
+            Ld[k] = loader.awq_dequant(qw, qz, s, group)      # fp32
+    return w, dense
+
+
+def test_int4_weights_through_the_engine():
+    w, dense = _int4_weights(CFG)
+    eng = eng_mod.LLMEngine(CFG, impl="oracle", device="cpu", weights=w, max_batch=4, max_seq=512, chunk=32)
+    assert eng.model.int4
+    g = torch.Generator().manual_seed(18)
+    prompts = [torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (50, 7)]
+    outs = eng.generate(prompts, max_new_tokens=5)
+    for p, o in zip(prompts, outs):
+        _assert_near_argmax(CFG, dense, p, o)
+    got = _prompt_hidden(_engine_with(w), prompts[0], 32)
+    want, _ = _dense(CFG, dense, prompts[0])
+    assert _cos(got, want[-1]) > 0.999
+
+
+def _engine_with(weights):
+    return eng_mod.LLMEngine(CFG, impl="oracle", device="cpu", weights=weights, max_batch=4, max_seq=512, chunk=32)

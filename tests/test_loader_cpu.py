@@ -326,3 +326,24 @@ def test_non_silu_activation_is_refused():
     with pytest.raises(ValueError, match="activation"):
         models.config_from_hf(dict(HF_CFG, hidden_act="gelu_pytorch_tanh"))
     assert models.config_from_hf(dict(HF_CFG, hidden_act="silu")).ffn == 384
+
+
+def test_awq_int4_shards_stay_packed_and_match_the_bf16_load(tmp_path):
+    """``load_llama(..., int4=True)``: the decoder linears stay AWQ-packed
+    (``ops.Int4Weight``), sharded like the bf16 weights; expanding a shard
+    gives exactly the bf16 shard the dequantizing load produces."""
+    loader = importlib.import_module("3080_mod_p2p_sglang_patch_b200.models.loader")
+    _awq_checkpoint(tmp_path, group=64)
+    for tp in (1, 2):
+        for r in range(tp):
+            _, wq = models.load_llama(str(tmp_path), r, tp, "cpu", int4=True)
+            _, wb = models.load_llama(str(tmp_path), r, tp, "cpu")
+            for i in (0, 1):
+                for k in ("qkv", "o", "gate_up", "down"):
+                    a, b = wq.layers[i][k], wb.layers[i][k]
+                    if i == 0 and k == "qkv":   # layer 0's v_proj is stored unquantized: stays bf16
+                        assert isinstance(a, torch.Tensor) and torch.equal(a, b)
+                        continue
+                    assert isinstance(a, ops.Int4Weight) and a.shape == tuple(b.shape), (i, k)
+                    dense = loader.awq_dequant(a.qweight, a.qzeros, a.scales, a.group).to(torch.bfloat16)
+                    assert torch.equal(dense, b), (tp, r, i, k)

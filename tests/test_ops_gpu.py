@@ -100,3 +100,33 @@ def test_argmax_and_combine():
     best = ops.argmax_combine(torch.stack(vals), torch.stack(idxs))
     full = logits.permute(1, 0, 2).reshape(B, W * V).float()
     assert torch.equal(best, full.argmax(-1))
+
+
+def test_awq_int4_gemv_and_dequant():
+    """AWQ int4 kernels against PyTorch: the dequantizer bit for bit (same
+    fp32 product, one rounding), the GEMV (1..8 rows, with and without a
+    residual) against x @ W^T in fp32."""
+    ops, models = sub("ops"), sub("models")
+    loader = sub("models.loader")
+    torch.manual_seed(7)
+    for N, K, G in ((512, 1024, 128), (1544, 512, 64), (64, 2048, 128)):
+        wf = torch.randn(N, K) * 0.05
+        qw, qz, s = models.awq_quantize(wf, G)
+        w = ops.Int4Weight(qw.cuda(), qz.cuda(), s.cuda(), G)
+        ref_w = loader.awq_dequant(qw, qz, s, G)                 # fp32 [N, K]
+        assert torch.equal(ops.awq_dequant(w).cpu(), ref_w.to(torch.bfloat16))
+        for M in (1, 3, 8):
+            x = torch.randn(M, K).to(torch.bfloat16)
+            want = x.float() @ ref_w.t()
+            got = ops.awq_gemm(x.cuda(), w).float().cpu()
+            tol = 2e-2 * want.abs().max().item() + 1e-2
+            assert (got - want).abs().max().item() < tol, (N, K, G, M)
+            res = torch.randn(M, N).to(torch.bfloat16)
+            out = res.clone().cuda()
+            ops.awq_gemm(x.cuda(), w, out=out, residual=out)       # in place, like the residual epilogue
+            assert (out.float().cpu() - (want + res.float())).abs().max().item() < tol + 2e-2
+        # more rows than the GEMV takes: the dequant + tcgen05 GEMM path
+        x = torch.randn(40, K).to(torch.bfloat16)
+        got = ops.awq_gemm(x.cuda(), w).float().cpu()
+        want = x.float() @ ref_w.to(torch.bfloat16).float().t()
+        assert (got - want).abs().max().item() < 2e-2 * want.abs().max().item() + 1e-2
