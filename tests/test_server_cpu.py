@@ -615,3 +615,26 @@ def test_n_choices_per_request():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_serving_bench_against_the_server():
+    """benchmarks/bench_serving.py: streamed requests under a concurrency cap
+    and a Poisson arrival rate, timed by the client."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_serving", os.path.join(ROOT, "benchmarks", "bench_serving.py"))
+    bs = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bs)
+    eng = _SlowEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        res = bs.main(["--url", base, "--num-requests", "12", "--concurrency", "4", "--request-rate", "50",
+                       "--input-len", "5:20", "--output-len", "6"])
+        assert res["completed"] == 12 and res["errors"] == 0
+        assert res["output_tok_s"] > 0 and res["ttft_ms"]["p50"] > 0 and res["itl_ms"]["p50"] > 0
+        assert res["latency_ms"]["p99"] >= res["latency_ms"]["p50"] >= res["ttft_ms"]["p50"]
+        assert len(eng.log) == 12 and all(m == 6 for _, _, m in eng.log)
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
