@@ -1,4 +1,4 @@
-"""Model configurations of the served decoder.
+"""Model configurations of the served decoder: Llama-style 8B and 70B, and a tiny one.
 
 The reference serves Qwen3.8-27B-AWQ through sglang (docs/performance.md:3-5);
 it ships no model code. These are the Llama-style dense shapes the B200 build

@@ -1,5 +1,5 @@
 """Headline benchmark: tensor-parallel prefill tokens/s of the Llama-style 8B
-decoder (BASELINE config 3: hidden 4096, 32 layers, 32q/8kv heads, FFN 14336,
+decoder (hidden 4096, 32 layers, 32q/8kv heads, FFN 14336,
 vocab 128256, bf16, random-init weights N(0, 0.02); 16 requests x 4096
 uniform-random token ids, chunked prefill with chunk 1024), TP = --gpus.
 
@@ -30,7 +30,7 @@ PKG = "3080_mod_p2p_sglang_patch_b200"
 
 # published reference prefill number at chunk 1024 (2x RTX 3080, Qwen3.8-27B
 # AWQ, TP=2, 40K prompt): reference docs/performance.md:43
-BASELINE_PREFILL_TOKS = 1464.0
+REFERENCE_PUBLISHED_PREFILL_TOKS = 1464.0
 
 REFERENCE_UNAVAILABLE = (
     "the reference (ackerx/3080_mod_p2p_sglang_patch) is an allreduce plugin for sglang 0.5.19 with no model, "
@@ -193,7 +193,7 @@ def main():
             "ms_per_step": ms_per_step,
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": value / BASELINE_PREFILL_TOKS,
+            "vs_baseline": value / REFERENCE_PUBLISHED_PREFILL_TOKS,
             "dtype": "bf16",
             "data": "synthetic (uniform-random token ids, random-init weights N(0,0.02))",
             "impl": args.impl,

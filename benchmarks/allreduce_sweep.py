@@ -1,4 +1,4 @@
-"""Allreduce size sweep (BASELINE config 2), one rank per GPU under torchrun:
+"""Allreduce size sweep, one rank per GPU under torchrun:
 
     torchrun --nproc-per-node N benchmarks/allreduce_sweep.py [--graph] [--algos ...] [--reference]
 

@@ -1,4 +1,4 @@
-"""CUDA-graph decode ITL (BASELINE config 4): Llama-style 8B at TP = world
+"""CUDA-graph decode ITL: Llama-style 8B at TP = world
 size, batch sizes {1, 8, 32, 64}, every request with a 4096-token
 uniform-random-id context prefilled into the paged KV cache (page 16, bf16),
 then 256 tokens generated greedily.

@@ -1,4 +1,4 @@
-"""Mixed serving (BASELINE config 5): 70B-class decoder at TP = world size,
+"""Mixed serving: 70B-class decoder at TP = world size,
 64 requests with uniform-random prompt lengths in [512, 8192] and 512
 generated tokens each, served by the engine's own scheduler (chunked prefill
 first, CUDA-graph decode batches otherwise).

@@ -1,4 +1,4 @@
-"""the mailbox lockstep protocol on CPU/gloo ranks.
+"""The mailbox lockstep protocol on CPU/gloo ranks.
 
 Two (and four) processes run the communicator's CPU transport (native shared-
 memory engine, csrc/cpu/mailbox_cpu.cpp) on fp32 and bf16 tensors of shape
