@@ -28,7 +28,8 @@ class LLMEngine:
     def __init__(self, cfg: LlamaConfig, tp=None, max_batch: int = 64, max_seq: int = 8192, chunk: int = 1024,
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
-                 sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None):
+                 sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None,
+                 mixed_chunk: bool = False):
         if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
             use_graphs, prefill_graph = False, False
         if max_seq > cfg.max_pos:
@@ -77,7 +78,8 @@ class LLMEngine:
         self.kv = PagedKVCache(cfg.layers, nkv, cfg.head_dim, kv_blocks, self.device)
         # prefix caching: off by default (benchmarks must not reuse work)
         self.prefix_cache = PrefixCache(self.kv.alloc) if prefix_cache else None
-        self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq, prefix_cache=self.prefix_cache)
+        self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq, prefix_cache=self.prefix_cache,
+                               mixed=mixed_chunk)
         # draws of unseeded sampled requests (same seed on every TP rank)
         self._rng = torch.Generator(device=self.device)
         self._rng.manual_seed(int(seed) + 1_000_003)
@@ -235,20 +237,19 @@ class LLMEngine:
             if not getattr(p.req, "_row_synced", False):
                 self._sync_block_row(p.req)
         sampled = any(p.completes and p.req.needs_logits for p in pieces) or \
-            any(p.req.prompt_logprobs for p in pieces)
+            any(p.req.prompt_logprobs and not p.decode for p in pieces)
         if self.prefill_graph is not None and len(pieces) == 1 and pieces[0].n == self.chunk and not sampled:
             # a full single-request chunk: replay the captured chunk forward
             p = pieces[0]
             req = p.req
-            d = self._h2d(torch.tensor(req.prompt[p.start:p.start + p.n] + list(range(p.start, p.start + p.n)),
-                                       dtype=torch.int32))
+            d = self._h2d(torch.tensor(p.tokens() + list(range(p.start, p.start + p.n)), dtype=torch.int32))
             slots_d = self._h2d(torch.tensor(self.kv.slots(req.blocks, p.start, p.n), dtype=torch.int64))
             return self.prefill_graph.run(d[:p.n], d[p.n:], slots_d, p.start + p.n, self.block_table[req.slot])
         ids, pos, slots, q_lens, kv_lens, rows, last = [], [], [], [], [], [], []
         off = 0
         for p in pieces:
             req = p.req
-            ids.extend(req.prompt[p.start:p.start + p.n])
+            ids.extend(p.tokens())
             pos.extend(range(p.start, p.start + p.n))
             slots.extend(self.kv.slots(req.blocks, p.start, p.n))
             q_lens.append(p.n)
@@ -256,7 +257,7 @@ class LLMEngine:
             rows.append(req.slot)
             off += p.n
             last.append(off - 1)
-        if any(p.req.prompt_logprobs for p in pieces):
+        if any(p.req.prompt_logprobs and not p.decode for p in pieces):
             return self._prefill_scoring(pieces, ids, pos, slots, q_lens, kv_lens, rows)
         if sampled:
             hidden = self.forward_prefill(ids, pos, slots, q_lens, kv_lens, rows, last, return_hidden=True)
@@ -271,7 +272,7 @@ class LLMEngine:
         want, last_of = [], []
         off = 0
         for p in pieces:
-            if p.req.prompt_logprobs:
+            if p.req.prompt_logprobs and not p.decode:
                 want.extend(range(off, off + p.n))
             else:
                 want.append(off + p.n - 1)
@@ -282,7 +283,7 @@ class LLMEngine:
         row = 0
         for p in pieces:
             req = p.req
-            if req.prompt_logprobs:
+            if req.prompt_logprobs and not p.decode:
                 lp = torch.log_softmax(logits[row:row + p.n].float(), dim=-1)
                 if p.start == 0:
                     req.prompt_token_logprobs.append(None)  # the first token has no context
@@ -404,7 +405,8 @@ class LLMEngine:
             now = time.perf_counter()
             for p in batch.pieces:
                 if p.completes:
-                    p.req.t_first = now
+                    if not p.decode:
+                        p.req.t_first = now
                     p.req.token_times.append(now)
             self.sched.after_prefill(batch, nxt)
         else:

@@ -66,10 +66,19 @@ class PrefillPiece:
     req: Request
     start: int
     n: int
+    # a running request's decode step carried by a prefill batch (mixed
+    # chunks): one token, its last output, at position total_len - 1
+    decode: bool = False
 
     @property
     def completes(self):
-        return self.start + self.n == len(self.req.prompt)
+        """The piece's last row yields a token that is used."""
+        return self.decode or self.start + self.n == len(self.req.prompt)
+
+    def tokens(self):
+        if self.decode:
+            return [self.req.output[-1]]
+        return self.req.prompt[self.start:self.start + self.n]
 
 
 @dataclasses.dataclass
@@ -85,8 +94,12 @@ class Batch:
 
 class Scheduler:
     def __init__(self, chunk: int = 1024, max_batch: int = 64, allocator=None, max_seq: int = 16384,
-                 prefix_cache=None):
+                 prefix_cache=None, mixed: bool = False):
         self.chunk = chunk
+        # mixed chunks (sglang's --enable-mixed-chunk): a prefill batch also
+        # carries one decode token of every running request, so decoding does
+        # not pause while long prompts prefill
+        self.mixed = mixed
         self.max_batch = max_batch
         self.allocator = allocator
         self.max_seq = max_seq
@@ -150,6 +163,8 @@ class Scheduler:
                     continue
                 pieces.append(PrefillPiece(req, req.computed, n))
                 budget -= n
+            if self.mixed:
+                pieces.extend(PrefillPiece(r, r.total_len - 1, 1, decode=True) for r in self.running)
             return Batch("prefill", pieces=pieces)
         if self.running:
             return Batch("decode", reqs=list(self.running))
@@ -160,6 +175,12 @@ class Scheduler:
         for piece, tok in zip(batch.pieces, next_tokens):
             req = piece.req
             req.computed += piece.n
+            if piece.decode:  # a running request's decode step
+                req.output.append(int(tok))
+                if self._done(req):
+                    self.running.remove(req)
+                    self._finish(req)
+                continue
             if piece.completes:
                 self.prefilling.remove(req)
                 if self.prefix_cache is not None:

@@ -774,6 +774,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
     ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
     ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
+    ap.add_argument("--enable-mixed-chunk", dest="mixed_chunk", action="store_true",
+                    help="prefill batches also carry the running requests' decode tokens")
     ap.add_argument("--int4-weights", action="store_true",
                     help="keep an AWQ checkpoint's linears packed as int4 (int4 GEMV for decode) instead of "
                          "expanding them to bf16 at load")
@@ -921,7 +923,7 @@ def main(argv=None):
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
     opts = dict(max_batch=args.max_batch, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
-                prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction)
+                prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction, mixed_chunk=args.mixed_chunk)
     if args.max_seq is not None:
         opts["max_seq"] = args.max_seq
     tokenizer = None

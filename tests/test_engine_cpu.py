@@ -454,3 +454,22 @@ def test_int4_weights_through_the_engine():
 
 def _engine_with(weights):
     return eng_mod.LLMEngine(CFG, impl="oracle", device="cpu", weights=weights, max_batch=4, max_seq=512, chunk=32)
+
+
+def test_mixed_chunks_keep_decoding_during_a_long_prefill():
+    eng = _engine(chunk=32, mixed_chunk=True)
+    g = torch.Generator().manual_seed(20)
+    pa = torch.randint(0, CFG.vocab, (20,), generator=g).tolist()
+    pb = torch.randint(0, CFG.vocab, (120,), generator=g).tolist()
+    a = eng.add_request(pa, 8)
+    eng.step()                                               # a's prefill: one token
+    b = eng.add_request(pb, 3)
+    steps = 0
+    while b.computed < len(pb):
+        eng.step()
+        steps += 1
+    assert steps == 4 and len(a.output) == 1 + 4             # a advanced in every chunk of b
+    eng.run()
+    _assert_near_argmax(CFG, eng.weights, pa, a.output)
+    _assert_near_argmax(CFG, eng.weights, pb, b.output)
+    assert eng.kv.alloc.free == eng.kv.alloc.num_blocks - 1

@@ -161,3 +161,19 @@ def test_native_engine_with_int4_weights():
     outs = eng.generate(many, max_new_tokens=3)                          # bs 10: dequant + GEMM
     for p, o in zip(many, outs):
         _near_argmax(CFG, dense, p, o)
+
+
+def test_native_mixed_chunks():
+    """Prefill batches that also carry running requests' decode tokens (one-row
+    pieces in the tcgen05 prefill attention)."""
+    eng = _engine(chunk=64, mixed_chunk=True, max_batch=8)
+    g = torch.Generator().manual_seed(21)
+    short = [torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (15, 33, 9)]
+    reqs = [eng.add_request(p, 8) for p in short]
+    eng.step()
+    long_p = torch.randint(0, CFG.vocab, (300,), generator=g).tolist()
+    lr = eng.add_request(long_p, 3)
+    eng.run()
+    w = _host(eng.weights)
+    for p, r in zip(short + [long_p], reqs + [lr]):
+        _near_argmax(CFG, w, p, r.output)

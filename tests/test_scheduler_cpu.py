@@ -250,3 +250,27 @@ def test_abort_frees_pages_and_slots_wherever_the_request_is():
     assert sorted(r.rid for r in s.finished) == [0, 1, 2]
     assert alloc.free + pc.evictable == 40                                           # every page back
     assert sorted(s._free_slots) == [0, 1]
+
+
+def test_mixed_chunks_carry_decode_tokens_while_prompts_prefill():
+    s = sched_mod.Scheduler(chunk=16, max_batch=4, mixed=True)
+    a = sched_mod.Request(rid=0, prompt=[1] * 5, max_new=6)
+    s.add(a)
+    s.after_prefill(s.next_batch(), [7])                     # a is decoding now
+    b = sched_mod.Request(rid=1, prompt=[2] * 40, max_new=2)
+    s.add(b)
+    kinds = []
+    while b.computed < 40:
+        batch = s.next_batch()
+        assert batch.kind == "prefill"
+        dec = [p for p in batch.pieces if p.decode]
+        kinds.append(len(dec))
+        assert all(p.req is a and p.n == 1 and p.start == a.total_len - 1 and p.tokens() == [a.output[-1]]
+                   for p in dec)
+        s.after_prefill(batch, [8] * len(batch.pieces))
+    assert kinds == [1, 1, 1]                                # a decoded in each of b's three chunks
+    assert a.output == [7, 8, 8, 8] and a.computed == 5 + 3
+    while s.has_work():
+        batch = s.next_batch()
+        s.after_decode(batch, [9] * len(batch.reqs))
+    assert a.output == [7, 8, 8, 8, 9, 9] and b.output == [8, 9]
