@@ -13,14 +13,14 @@ import time
 import requests
 
 
-def main():
+def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--url", default="http://127.0.0.1:8001")
     ap.add_argument("--prompt", default="Explain NVLink in one sentence.")
     ap.add_argument("--max-tokens", type=int, default=32)
     ap.add_argument("--temperature", type=float, default=0.0)
     ap.add_argument("--stream", action="store_true")
-    args = ap.parse_args()
+    args = ap.parse_args(argv)
     body = {"messages": [{"role": "user", "content": args.prompt}], "max_tokens": args.max_tokens,
             "temperature": args.temperature, "stream": args.stream}
     if args.stream:

@@ -638,3 +638,22 @@ def test_serving_bench_against_the_server():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_example_client_against_the_server(capsys):
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("client", os.path.join(ROOT, "examples", "client.py"))
+    client = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(client)
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        client.main(["--url", base, "--prompt", "hi", "--max-tokens", "4"])
+        client.main(["--url", base, "--prompt", "hi", "--max-tokens", "4", "--stream"])
+        out = capsys.readouterr().out
+        assert "tok/s" in out and "prompt=" in out
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
