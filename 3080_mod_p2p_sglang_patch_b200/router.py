@@ -48,7 +48,7 @@ class Router:
         with self._lock:
             self.inflight[i] -= 1
 
-    def post(self, path: str, body: dict):
+    def post(self, path: str, body: dict, headers: dict = None):
         """Forward a non-streaming request: (status, json body, replica)."""
         import requests
 
@@ -56,7 +56,7 @@ class Router:
         for i in self.order():
             self._acquire(i)
             try:
-                r = requests.post(self.backends[i] + path, json=body, timeout=self.timeout)
+                r = requests.post(self.backends[i] + path, json=body, timeout=self.timeout, headers=headers)
                 return r.status_code, r.json(), i
             except requests.ConnectionError as e:  # replica down: try the next one
                 with self._lock:
@@ -66,7 +66,7 @@ class Router:
                 self._release(i)
         raise ConnectionError(f"no replica reachable ({last})")
 
-    def stream(self, path: str, body: dict):
+    def stream(self, path: str, body: dict, headers: dict = None):
         """Forward a streaming request; yields the replica's server-sent-event
         lines (each ending in a blank line) as they arrive."""
         import requests
@@ -76,7 +76,8 @@ class Router:
             self._acquire(i)
             try:
                 try:
-                    r = requests.post(self.backends[i] + path, json=body, timeout=self.timeout, stream=True)
+                    r = requests.post(self.backends[i] + path, json=body, timeout=self.timeout, stream=True,
+                                      headers=headers)
                 except requests.ConnectionError as e:
                     with self._lock:
                         self.failed[i] += 1
@@ -92,10 +93,10 @@ class Router:
         yield "data: " + json.dumps({"error": {"message": f"no replica reachable ({last})"}}) + "\n\n"
         yield "data: [DONE]\n\n"
 
-    def get(self, i: int, path: str):
+    def get(self, i: int, path: str, headers: dict = None):
         import requests
 
-        return requests.get(self.backends[i] + path, timeout=30)
+        return requests.get(self.backends[i] + path, timeout=30, headers=headers)
 
 
 def _relabel(text: str, replica: int) -> list:
@@ -114,39 +115,45 @@ def _relabel(text: str, replica: int) -> list:
 
 
 def build_router_app(router: Router):
-    from fastapi import FastAPI, HTTPException
+    from fastapi import FastAPI, HTTPException, Request
     from fastapi.concurrency import iterate_in_threadpool, run_in_threadpool
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     app = FastAPI()
 
-    async def forward(path, body):
+    def _auth(request):
+        """The client's credentials travel to the replica, which checks them."""
+        a = request.headers.get("authorization")
+        return {"Authorization": a} if a else None
+
+    async def forward(path, body, request):
         if body.get("stream"):
-            return StreamingResponse(iterate_in_threadpool(router.stream(path, body)),
+            return StreamingResponse(iterate_in_threadpool(router.stream(path, body, _auth(request))),
                                      media_type="text/event-stream")
         try:
-            status, data, _ = await run_in_threadpool(router.post, path, body)
+            status, data, _ = await run_in_threadpool(router.post, path, body, _auth(request))
         except ConnectionError as e:
             raise HTTPException(503, str(e)) from e
         return JSONResponse(data, status_code=status)
 
     @app.post("/v1/completions")
-    async def completions(body: dict):
-        return await forward("/v1/completions", body)
+    async def completions(body: dict, request: Request):
+        return await forward("/v1/completions", body, request)
 
     @app.post("/v1/chat/completions")
-    async def chat(body: dict):
-        return await forward("/v1/chat/completions", body)
+    async def chat(body: dict, request: Request):
+        return await forward("/v1/chat/completions", body, request)
 
     @app.post("/generate")
-    async def generate(body: dict):
-        return await forward("/generate", body)
+    async def generate(body: dict, request: Request):
+        return await forward("/generate", body, request)
 
     @app.get("/v1/models")
-    def models():
+    def models(request: Request):
         for i in range(len(router.backends)):
             try:
-                return router.get(i, "/v1/models").json()
+                r = router.get(i, "/v1/models", _auth(request))
+                return JSONResponse(r.json(), status_code=r.status_code)
             except Exception:  # noqa: BLE001 - try the next replica
                 continue
         raise HTTPException(503, "no replica reachable")

@@ -389,17 +389,30 @@ def _stop_prefix(tokens, stops, detok):
     return k
 
 
-def build_app(server: EngineServer, model_name: str, tokenizer=None):
-    """FastAPI app with /health, /metrics, /v1/models, /v1/completions and
-    /v1/chat/completions (plain or streamed; greedy or sampled; stop token
-    ids and stop strings)."""
-    from fastapi import FastAPI, HTTPException
+def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: str = None):
+    """FastAPI app with /health, /metrics, /v1/models, /v1/completions,
+    /v1/chat/completions and /generate (plain or streamed; greedy or
+    sampled; stop token ids and stop strings). ``api_key``: requests to the
+    model endpoints need ``Authorization: Bearer <api_key>`` (/health and
+    /metrics stay open for probes)."""
+    import hmac
+
+    from fastapi import FastAPI, HTTPException, Request
     from fastapi.concurrency import iterate_in_threadpool, run_in_threadpool
-    from fastapi.responses import StreamingResponse
+    from fastapi.responses import JSONResponse, StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
     app = FastAPI()
     ids = itertools.count()
+
+    if api_key:
+        @app.middleware("http")
+        async def _auth(request: Request, call_next):
+            if request.url.path not in ("/health", "/metrics"):
+                got = request.headers.get("authorization", "")
+                if not hmac.compare_digest(got.encode(), f"Bearer {api_key}".encode()):
+                    return JSONResponse({"error": {"message": "invalid or missing API key"}}, status_code=401)
+            return await call_next(request)
 
     def _prompt_ids(p):
         if isinstance(p, list) and all(isinstance(i, int) for i in p):
@@ -766,6 +779,8 @@ def build_parser() -> argparse.ArgumentParser:
                     help="data-parallel replicas, each a TP group on its own GPUs, behind one router")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8001)
+    ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on the model endpoints")
+    ap.add_argument("--served-model-name", default=None, help="model id reported by /v1/models")
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
     ap.add_argument("--max-seq", "--context-length", dest="max_seq", type=int, default=None,
                     help="longest prompt + generation (default: the model's positions, at most 16384 with "
@@ -945,7 +960,8 @@ def main(argv=None):
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step
         for sig in (signal.SIGINT, signal.SIGTERM):
             signal.signal(sig, lambda *_: server.stop())
-        http, _ = start_http(build_app(server, cfg.name, tokenizer), args.host, args.port)
+        http, _ = start_http(build_app(server, args.served_model_name or cfg.name, tokenizer, api_key=args.api_key),
+                             args.host, args.port)
         logger.info("serving %s at http://%s:%d (TP=%d, allreduce=%s)", cfg.name, args.host, args.port, world,
                     "MailboxAR" if (tp is not None and tp.ca_comm is not None) else "NCCL")
     try:

@@ -104,3 +104,30 @@ def test_replica_commands_partition_gpus_and_ports():
     assert all("torch.distributed.run" not in cmd for _, cmd in single)
     with pytest.raises(SystemExit):
         srv_mod.replica_commands([], 2, 4, 8001, ["0", "1", "2"])
+
+
+def test_router_passes_the_api_key_to_replicas():
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    rep_http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake", api_key="k1"), "127.0.0.1", port)
+    router = rt_mod.Router([f"http://127.0.0.1:{port}"])
+    rport = free_port()
+    http, _ = srv_mod.start_http(rt_mod.build_router_app(router), "127.0.0.1", rport)
+    base = f"http://127.0.0.1:{rport}"
+    try:
+        body = {"prompt": [3, 4], "max_tokens": 2}
+        assert requests.post(base + "/v1/completions", json=body, timeout=30).status_code == 401
+        r = requests.post(base + "/v1/completions", json=body, headers={"Authorization": "Bearer k1"}, timeout=30)
+        assert r.status_code == 200 and r.json()["choices"][0]["token_ids"] == expected([3, 4], 2)
+        with requests.post(base + "/v1/completions", json={**body, "stream": True}, stream=True, timeout=30,
+                           headers={"Authorization": "Bearer k1"}) as s:
+            assert any(ln == "data: [DONE]" for ln in s.iter_lines(decode_unicode=True))
+        assert requests.get(base + "/v1/models", headers={"Authorization": "Bearer k1"}, timeout=30).status_code == 200
+    finally:
+        http.should_exit = True
+        rep_http.should_exit = True
+        server.stop()
+        loop.join(timeout=30)

@@ -657,3 +657,30 @@ def test_example_client_against_the_server(capsys):
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_api_key_guards_the_model_endpoints():
+    import requests
+
+    from conftest import free_port
+
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "served-name", api_key="s3cret"), "127.0.0.1", port)
+    base = f"http://127.0.0.1:{port}"
+    try:
+        body = {"prompt": [1, 2], "max_tokens": 2}
+        assert requests.post(base + "/v1/completions", json=body, timeout=30).status_code == 401
+        assert requests.post(base + "/v1/completions", json=body, timeout=30,
+                             headers={"Authorization": "Bearer wrong"}).status_code == 401
+        ok = requests.post(base + "/v1/completions", json=body, timeout=30, headers={"Authorization": "Bearer s3cret"})
+        assert ok.status_code == 200 and ok.json()["model"] == "served-name"
+        assert requests.get(base + "/health", timeout=30).status_code == 200      # probes stay open
+        assert requests.get(base + "/v1/models", timeout=30).status_code == 401
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
