@@ -558,6 +558,14 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
 
     @app.get("/health")
     def health():
+        """200 while serving; 503 once the server stopped or the communicator
+        holds a device error (a timed-out peer wait), so a load balancer or the
+        data-parallel router can see it."""
+        tp = getattr(server.engine, "tp", None)
+        comm = getattr(tp, "ca_comm", None) if tp is not None else None
+        err = comm.err() if comm is not None else 0
+        if server._stopped.is_set() or err:
+            return JSONResponse({"status": "unhealthy", "communicator_error": err, **server.stats}, status_code=503)
         return {"status": "ok", **server.stats}
 
     @app.get("/metrics")

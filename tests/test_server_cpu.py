@@ -684,3 +684,29 @@ def test_api_key_guards_the_model_endpoints():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_health_reports_a_communicator_error():
+    import requests
+
+    class _Comm:
+        code = 0
+
+        def err(self):
+            return self.code
+
+        counters = {}
+
+    eng = FakeEngine()
+    comm = _Comm()
+    eng.tp = type("TP", (), {"ca_comm": comm})()
+    server, loop, http, base = _serve(eng)
+    try:
+        assert requests.get(base + "/health", timeout=30).status_code == 200
+        comm.code = 3                                   # a device wait timed out
+        h = requests.get(base + "/health", timeout=30)
+        assert h.status_code == 503 and h.json()["communicator_error"] == 3
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
