@@ -317,7 +317,10 @@ class EngineServer:
                             p.sent = len(p.req.output)
                         if p.stop_strs and p.req is not None and len(p.req.output) > p.checked:
                             p.checked = len(p.req.output)
-                            if _find_stop(p.detok(p.req.output), p.stop_strs) >= 0:
+                            # a new match ends in the newest tokens: decode a tail
+                            # window, not the whole output, every step
+                            win = max(16, 4 * max(len(x) for x in p.stop_strs))
+                            if _find_stop(p.detok(p.req.output[-win:]), p.stop_strs) >= 0:
                                 p.stop_hit = True
                                 self.abort(p)  # every rank drops it next step
                 done, eng.sched.finished = eng.sched.finished, []
