@@ -584,9 +584,19 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
     def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "mailbox-ar-b200"}]}
 
+    def _prompt_batch(p):
+        """OpenAI ``prompt``: a string, a token-id list, or a list of either
+        (several prompts in one request)."""
+        if isinstance(p, list) and p and all(isinstance(x, (str, list)) for x in p):
+            return [_prompt_ids(x) for x in p]
+        return [_prompt_ids(p)]
+
     @app.post("/v1/completions")
     async def completions(body: dict):
-        prompt = _prompt_ids(body.get("prompt", ""))
+        import asyncio
+
+        prompts = _prompt_batch(body.get("prompt", ""))
+        prompt = prompts[0]
         max_tokens = int(body.get("max_tokens", 16))
         echo = bool(body.get("echo"))
         score_only = echo and max_tokens == 0  # scoring: the prompt's logprobs, nothing generated
@@ -595,6 +605,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
             _n(body)
+            if len(prompts) > 1:
+                raise HTTPException(400, "several prompts are not supported with stream")
             _check(prompt, max_tokens)
             cid, created = f"cmpl-{next(ids)}", int(time.time())
             return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
@@ -603,21 +615,30 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                 **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
         lp = body.get("logprobs")
         lp = None if lp is None or lp is False else int(lp)
-        runs = await _run_n(_n(body), prompt, max_tokens, stop, _sampling(body), stops, lp, echo and lp is not None)
+        n = _n(body)
+        for pr in prompts:  # refuse the whole request before running any of it
+            _check(pr, max_tokens)
+        per_prompt = await asyncio.gather(*[_run_n(n, pr, max_tokens, stop, _sampling(body), stops, lp,
+                                                   echo and lp is not None) for pr in prompts])
         choices, outs = [], []
-        for i, (out, fin, lps, plps) in enumerate(runs):
-            if score_only:
-                out, lps, fin = [], [], "length"
-            text = _text(out, stops)
-            logprobs = None
-            if lp is not None:
-                logprobs = _completion_logprobs((prompt if echo else []) + out, (plps if echo else []) + lps)
-            if echo:
-                text = tok.decode(prompt) + text
-            choices.append({"index": i, "text": text, "token_ids": out, "finish_reason": fin, "logprobs": logprobs})
-            outs.append(out)
+        for pr, runs in zip(prompts, per_prompt):   # choices: prompt-major, then n
+            for out, fin, lps, plps in runs:
+                if score_only:
+                    out, lps, fin = [], [], "length"
+                text = _text(out, stops)
+                logprobs = None
+                if lp is not None:
+                    logprobs = _completion_logprobs((pr if echo else []) + out, (plps if echo else []) + lps)
+                if echo:
+                    text = tok.decode(pr) + text
+                choices.append({"index": len(choices), "text": text, "token_ids": out, "finish_reason": fin,
+                                "logprobs": logprobs})
+                outs.append(out)
+        usage = _usage_n(prompt, outs)
+        usage["prompt_tokens"] = sum(len(pr) for pr in prompts) * n
+        usage["total_tokens"] = usage["prompt_tokens"] + usage["completion_tokens"]
         return {"id": f"cmpl-{next(ids)}", "object": "text_completion", "created": int(time.time()),
-                "model": model_name, "choices": choices, "usage": _usage_n(prompt, outs)}
+                "model": model_name, "choices": choices, "usage": usage}
 
     @app.post("/v1/chat/completions")
     async def chat(body: dict):

@@ -710,3 +710,29 @@ def test_health_reports_a_communicator_error():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_several_prompts_in_one_completion_request():
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/v1/completions", json={"prompt": [[1, 2], [10], "a"], "max_tokens": 2, "n": 2},
+                          timeout=60).json()
+        got = [c["token_ids"] for c in r["choices"]]
+        want = [expected(p, 2) for p in ([1, 2], [1, 2], [10], [10], [97], [97])]
+        assert got == want and [c["index"] for c in r["choices"]] == list(range(6))
+        assert r["usage"]["prompt_tokens"] == (2 + 1 + 1) * 2 and r["usage"]["completion_tokens"] == 12
+        # lm-eval style scoring of several texts at once
+        r = requests.post(base + "/v1/completions", json={"prompt": ["ab", "cd"], "max_tokens": 0, "echo": True,
+                                                          "logprobs": 0}, timeout=60).json()
+        assert [c["text"] for c in r["choices"]] == ["ab", "cd"]
+        assert [c["logprobs"]["token_logprobs"] for c in r["choices"]] == [[None, -1.0], [None, -1.0]]
+        bad = requests.post(base + "/v1/completions", json={"prompt": [[1], [2] * 5000], "max_tokens": 2},
+                            timeout=60)
+        assert bad.status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
