@@ -6,8 +6,31 @@ tokenizer through transformers (local files only), with its chat template.
 """
 
 
+def render_chat(template: str, messages) -> str:
+    """A Jinja chat template (the format of Hugging Face ``chat_template``)
+    rendered for ``messages`` with the generation prompt appended, in a
+    sandboxed environment."""
+    from jinja2.sandbox import ImmutableSandboxedEnvironment
+
+    env = ImmutableSandboxedEnvironment(trim_blocks=True, lstrip_blocks=True)
+    return env.from_string(template).render(messages=messages, add_generation_prompt=True)
+
+
+def load_chat_template(arg: str) -> str:
+    """``--chat-template``: a file path, else the template text itself."""
+    import os
+
+    if os.path.isfile(arg):
+        with open(arg) as f:
+            return f.read()
+    return arg
+
+
 class ByteTokenizer:
     """UTF-8 bytes as token ids (ids >= 256 have no text)."""
+
+    def __init__(self, chat_template: str = None):
+        self.chat_template = chat_template
 
     def encode(self, text: str) -> list:
         return list(text.encode("utf-8"))
@@ -15,14 +38,22 @@ class ByteTokenizer:
     def decode(self, ids) -> str:
         return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
 
+    def chat(self, messages) -> list:
+        if self.chat_template:
+            return self.encode(render_chat(self.chat_template, messages))
+        text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in messages) + "<|assistant|>"
+        return self.encode(text)
+
 
 class HFTokenizer:
     """A checkpoint directory's tokenizer (transformers, local files only)."""
 
-    def __init__(self, path: str):
+    def __init__(self, path: str, chat_template: str = None):
         from transformers import AutoTokenizer
 
         self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+        if chat_template:  # replaces the checkpoint's own template
+            self.tok.chat_template = chat_template
 
     def encode(self, text: str) -> list:
         return self.tok.encode(text, add_special_tokens=True)

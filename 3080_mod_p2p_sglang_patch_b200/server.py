@@ -43,7 +43,7 @@ import sys
 import threading
 import time
 
-from .engine.tokenizer import ByteTokenizer, HFTokenizer  # noqa: F401 - re-exported
+from .engine.tokenizer import ByteTokenizer, HFTokenizer, load_chat_template  # noqa: F401 - re-exported
 
 logger = logging.getLogger(__name__)
 
@@ -643,11 +643,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
     @app.post("/v1/chat/completions")
     async def chat(body: dict):
         msgs = body.get("messages") or []
-        if hasattr(tok, "chat"):
-            prompt = tok.chat(msgs)
-        else:
-            text = "".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}" for m in msgs) + "<|assistant|>"
-            prompt = tok.encode(text)
+        prompt = tok.chat(msgs)
         max_tokens = int(body.get("max_completion_tokens") or body.get("max_tokens") or 16)
         stop, stops = _stop(body), _stop_strs(body)
         if body.get("stream"):
@@ -813,6 +809,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--port", type=int, default=8001)
     ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on the model endpoints")
     ap.add_argument("--served-model-name", default=None, help="model id reported by /v1/models")
+    ap.add_argument("--chat-template", default=None,
+                    help="Jinja chat template (a file, or the template text) instead of the checkpoint's own")
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
     ap.add_argument("--max-seq", "--context-length", dest="max_seq", type=int, default=None,
                     help="longest prompt + generation (default: the model's positions, at most 16384 with "
@@ -981,6 +979,8 @@ def main(argv=None):
         tokenizer = eng.tokenizer
         if tokenizer is None:  # token-id prompts still work
             logger.warning("no tokenizer in %s; using the byte tokenizer", model_path)
+        elif args.chat_template:
+            tokenizer.tok.chat_template = load_chat_template(args.chat_template)
     else:
         cfg = models.LlamaConfig.by_name(name)
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
@@ -992,6 +992,8 @@ def main(argv=None):
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step
         for sig in (signal.SIGINT, signal.SIGTERM):
             signal.signal(sig, lambda *_: server.stop())
+        if tokenizer is None:
+            tokenizer = ByteTokenizer(load_chat_template(args.chat_template) if args.chat_template else None)
         http, _ = start_http(build_app(server, args.served_model_name or cfg.name, tokenizer, api_key=args.api_key),
                              args.host, args.port)
         logger.info("serving %s at http://%s:%d (TP=%d, allreduce=%s)", cfg.name, args.host, args.port, world,

@@ -736,3 +736,28 @@ def test_several_prompts_in_one_completion_request():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_chat_template_override():
+    import requests
+
+    from conftest import free_port
+
+    tpl = "{% for m in messages %}[{{ m.role }}]{{ m.content }}{% endfor %}{% if add_generation_prompt %}>{% endif %}"
+    tok = srv_mod.ByteTokenizer(srv_mod.load_chat_template(tpl))
+    assert tok.chat([{"role": "user", "content": "hi"}]) == list(b"[user]hi>")
+    assert srv_mod.ByteTokenizer().chat([{"role": "user", "content": "x"}]) == list(b"<|user|>x<|assistant|>")
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake", tok), "127.0.0.1", port)
+    try:
+        requests.post(f"http://127.0.0.1:{port}/v1/chat/completions",
+                      json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 1}, timeout=30)
+        assert eng.log[-1][1] == tuple(b"[user]hi>")
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
