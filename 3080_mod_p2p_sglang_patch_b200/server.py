@@ -816,7 +816,11 @@ def build_parser() -> argparse.ArgumentParser:
                     help="longest prompt + generation (default: the model's positions, at most 16384 with "
                          "random weights, 8192 with a checkpoint)")
     ap.add_argument("--chunk", "--chunked-prefill-size", dest="chunk", type=int, default=1024)
-    ap.add_argument("--impl", default="native", choices=["native", "torch"])
+    ap.add_argument("--impl", default="native", choices=["native", "torch", "oracle"],
+                    help="native: the sm_100a kernels; torch: cuBLAS + NCCL baseline; oracle: fp32 PyTorch "
+                         "restatement (with --device cpu: no GPU, for API development and tests)")
+    ap.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
+                    help="cpu needs --impl oracle; ranks then talk over gloo")
     ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
     ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
     ap.add_argument("--enable-mixed-chunk", dest="mixed_chunk", action="store_true",
@@ -958,13 +962,17 @@ def main(argv=None):
     par = importlib.import_module(f"{pkg}.parallel")
     models = importlib.import_module(f"{pkg}.models")
     eng_mod = importlib.import_module(f"{pkg}.engine")
-    if not torch.cuda.is_available():
+    on_cpu = args.device == "cpu"
+    if on_cpu and args.impl != "oracle":
+        raise SystemExit("--device cpu runs the oracle model only (--impl oracle)")
+    if not on_cpu and not torch.cuda.is_available():
         raise SystemExit("the server needs a CUDA GPU per rank (none visible)")
     logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
-    rank, world, local = par.init_distributed(timeout_s=600)
-    dev = torch.device("cuda", local)
-    # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow
-    tp = par.TPGroup(None, dev, use_mailbox=None) if world > 1 else None
+    rank, world, local = par.init_distributed(backend="gloo" if on_cpu else None, timeout_s=600)
+    dev = torch.device("cpu") if on_cpu else torch.device("cuda", local)
+    # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow (the
+    # oracle takes plain torch.distributed collectives)
+    tp = par.TPGroup(None, dev, use_mailbox=False if args.impl == "oracle" else None) if world > 1 else None
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
     opts = dict(max_batch=args.max_batch, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
@@ -984,7 +992,7 @@ def main(argv=None):
     else:
         cfg = models.LlamaConfig.by_name(name)
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
-        eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, **opts)
+        eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, device=dev, **opts)
     stop = eng.default_stop_ids
     server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop)
     http = None

@@ -761,3 +761,49 @@ def test_chat_template_override():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_server_entry_point_end_to_end_on_cpu():
+    """``python -m <pkg>.server --tp 2`` for real: the launcher starts two
+    ranks under torch.distributed.run, each builds the oracle engine on CPU
+    (gloo collectives), rank 0 serves HTTP; SIGTERM stops every rank."""
+    import signal as _signal
+    import time as _t
+
+    import requests
+
+    from conftest import free_port
+
+    port = free_port()
+    env = dict(os.environ)
+    for k in ("WORLD_SIZE", "RANK", "LOCAL_RANK", "MASTER_PORT"):
+        env.pop(k, None)
+    env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
+    cmd = [sys.executable, "-m", "3080_mod_p2p_sglang_patch_b200.server", "--model", "tiny", "--impl", "oracle",
+           "--device", "cpu", "--tp", "2", "--port", str(port), "--max-batch", "4", "--max-seq", "512",
+           "--chunk", "64"]
+    proc = subprocess.Popen(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                            start_new_session=True)
+    base = f"http://127.0.0.1:{port}"
+    try:
+        deadline = _t.time() + 240
+        while _t.time() < deadline:
+            try:
+                if requests.get(base + "/health", timeout=2).status_code == 200:
+                    break
+            except requests.ConnectionError:
+                pass
+            assert proc.poll() is None, proc.stdout.read().decode()[-3000:]
+            _t.sleep(0.5)
+        r = requests.post(base + "/v1/completions", json={"prompt": "hello", "max_tokens": 4}, timeout=120)
+        assert r.status_code == 200 and len(r.json()["choices"][0]["token_ids"]) == 4
+        c = requests.post(base + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                               "max_tokens": 3, "temperature": 0.7, "seed": 1},
+                          timeout=120)
+        assert c.status_code == 200 and c.json()["usage"]["completion_tokens"] == 3
+        proc.send_signal(_signal.SIGTERM)
+        proc.wait(timeout=90)
+    finally:
+        if proc.poll() is None:
+            os.killpg(proc.pid, _signal.SIGKILL)   # the process group this test started
+            proc.wait(timeout=30)
