@@ -917,7 +917,9 @@ def _run_replicas(argv, args) -> int:
     tp = args.tp or 1
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     visible = [v for v in vis.split(",") if v] if vis else None
-    if visible is None:
+    if args.device == "cpu":  # no GPUs to partition
+        visible = [""] * (tp * args.dp)
+    elif visible is None:
         import torch
 
         visible = [str(g) for g in range(torch.cuda.device_count())]

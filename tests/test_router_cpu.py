@@ -131,3 +131,47 @@ def test_router_passes_the_api_key_to_replicas():
         rep_http.should_exit = True
         server.stop()
         loop.join(timeout=30)
+
+
+def test_dp_entry_point_end_to_end_on_cpu():
+    """``server --dp 2`` for real: two oracle replicas on CPU behind the router."""
+    import os
+    import signal as _signal
+    import subprocess
+    import sys
+
+    port = free_port()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ)
+    for k in ("WORLD_SIZE", "RANK", "LOCAL_RANK", "MASTER_PORT"):
+        env.pop(k, None)
+    env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
+    cmd = [sys.executable, "-m", "3080_mod_p2p_sglang_patch_b200.server", "--model", "tiny", "--impl", "oracle",
+           "--device", "cpu", "--dp", "2", "--port", str(port), "--max-batch", "4", "--max-seq", "512"]
+    proc = subprocess.Popen(cmd, env=env, cwd=root, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                            start_new_session=True)
+    base = f"http://127.0.0.1:{port}"
+    try:
+        deadline = time.time() + 240
+        while time.time() < deadline:
+            try:
+                if requests.get(base + "/health", timeout=2).status_code == 200:
+                    break
+            except requests.ConnectionError:
+                pass
+            assert proc.poll() is None, proc.stdout.read().decode()[-3000:]
+            time.sleep(0.5)
+        outs = []
+        for i in range(4):
+            r = requests.post(base + "/v1/completions", json={"prompt": [5 + i, 6], "max_tokens": 3}, timeout=120)
+            assert r.status_code == 200
+            outs.append(r.json()["choices"][0]["token_ids"])
+        m = requests.get(base + "/metrics", timeout=30).text
+        assert 'mbx_router_requests_total{replica="0"}' in m and 'mbx_router_requests_total{replica="1"}' in m
+        assert all(len(o) == 3 for o in outs)
+        proc.send_signal(_signal.SIGTERM)
+        proc.wait(timeout=90)
+    finally:
+        if proc.poll() is None:
+            os.killpg(proc.pid, _signal.SIGKILL)   # the process group this test started
+            proc.wait(timeout=30)
