@@ -12,7 +12,6 @@ import torch
 
 from .. import ops
 from ..utils import launches
-from .kv_cache import PAGE
 
 
 class DecodeGraphRunner:

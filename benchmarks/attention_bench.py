@@ -10,7 +10,6 @@ median of iterations; FLOPs count causal work only.
 import argparse
 import importlib
 import json
-import math
 import os
 import sys
 

@@ -1,5 +1,4 @@
 """Paged prefill (chunked, causal) and split-KV decode attention vs fp32."""
-import math
 
 import pytest
 import torch

@@ -1,7 +1,6 @@
 """The TP Llama decoder on the native kernels vs a plain PyTorch fp32 forward
 of the same random weights (logit cosine / top-1 agreement), chunked prefill
 consistency, and CUDA-graph decode vs eager decode."""
-import math
 
 import pytest
 import torch
