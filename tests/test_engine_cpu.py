@@ -473,3 +473,17 @@ def test_mixed_chunks_keep_decoding_during_a_long_prefill():
     _assert_near_argmax(CFG, eng.weights, pa, a.output)
     _assert_near_argmax(CFG, eng.weights, pb, b.output)
     assert eng.kv.alloc.free == eng.kv.alloc.num_blocks - 1
+
+
+def test_perplexity_tool_on_the_oracle():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("perplexity", os.path.join(root, "benchmarks", "perplexity.py"))
+    ppl = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ppl)
+    res = ppl.main(["--model", "tiny", "--tokens", "300", "--window", "100", "--chunk", "64", "--impl", "oracle",
+                    "--device", "cpu", "--compare", "oracle"])
+    assert res["tokens"] == 297 and 1 < res["ppl"] < float("inf")      # 3 windows, first token of each excluded
+    assert res["mean_abs_logprob_diff"] == 0.0 and res["ppl_compare"] == res["ppl"]
