@@ -177,3 +177,18 @@ def test_native_mixed_chunks():
     w = _host(eng.weights)
     for p, r in zip(short + [long_p], reqs + [lr]):
         _near_argmax(CFG, w, p, r.output)
+
+
+def test_native_and_oracle_score_text_alike():
+    """Whole-model numerics: the native build and the fp32 oracle on the same
+    weights give nearly the same per-token logprobs over 1500 scored tokens."""
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("perplexity", os.path.join(root, "benchmarks", "perplexity.py"))
+    ppl = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ppl)
+    res = ppl.main(["--model", "tiny", "--tokens", "1500", "--window", "500", "--chunk", "128", "--impl", "native",
+                    "--device", "cuda", "--compare", "oracle"])
+    assert res["mean_abs_logprob_diff"] < 0.05 and abs(res["ppl"] / res["ppl_compare"] - 1) < 0.05
