@@ -29,7 +29,7 @@ class LLMEngine:
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
                  sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None,
-                 mixed_chunk: bool = False):
+                 mixed_chunk: bool = False, schedule_policy: str = "fcfs"):
         if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
             use_graphs, prefill_graph = False, False
         if max_seq > cfg.max_pos:
@@ -79,7 +79,7 @@ class LLMEngine:
         # prefix caching: off by default (benchmarks must not reuse work)
         self.prefix_cache = PrefixCache(self.kv.alloc) if prefix_cache else None
         self.sched = Scheduler(chunk, max_batch, self.kv.alloc, max_seq, prefix_cache=self.prefix_cache,
-                               mixed=mixed_chunk)
+                               mixed=mixed_chunk, policy=schedule_policy)
         # draws of unseeded sampled requests (same seed on every TP rank)
         self._rng = torch.Generator(device=self.device)
         self._rng.manual_seed(int(seed) + 1_000_003)

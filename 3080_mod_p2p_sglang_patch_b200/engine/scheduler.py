@@ -93,8 +93,16 @@ class Batch:
 
 
 class Scheduler:
+    POLICIES = ("fcfs", "lpm")
+
     def __init__(self, chunk: int = 1024, max_batch: int = 64, allocator=None, max_seq: int = 16384,
-                 prefix_cache=None, mixed: bool = False):
+                 prefix_cache=None, mixed: bool = False, policy: str = "fcfs"):
+        if policy not in self.POLICIES:
+            raise ValueError(f"schedule policy {policy!r}: {' | '.join(self.POLICIES)}")
+        # admission order of waiting requests: "fcfs" (arrival) or "lpm" (the
+        # longest cached prompt prefix first, ties by arrival; with a prefix
+        # cache, as sglang's default)
+        self.policy = policy
         self.chunk = chunk
         # mixed chunks (sglang's --enable-mixed-chunk): a prefill batch also
         # carries one decode token of every running request, so decoding does
@@ -128,6 +136,11 @@ class Scheduler:
 
     def _admit(self):
         pc = self.prefix_cache
+        if self.policy == "lpm" and pc is not None and len(self.waiting) > 1:
+            # stable sort: equal matches keep their arrival order
+            hits = {id(r): (0 if r.prompt_logprobs else len(pc.match(r.prompt, (len(r.prompt) - 1) // PAGE)))
+                    for r in self.waiting}
+            self.waiting = collections.deque(sorted(self.waiting, key=lambda r: -hits[id(r)]))
         while self.waiting and self._free_slots:
             req = self.waiting[0]
             need = (len(req.prompt) + req.max_new + PAGE - 1) // PAGE

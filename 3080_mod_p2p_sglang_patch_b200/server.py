@@ -823,6 +823,9 @@ def build_parser() -> argparse.ArgumentParser:
                     help="cpu needs --impl oracle; ranks then talk over gloo")
     ap.add_argument("--no-graphs", "--disable-cuda-graph", dest="no_graphs", action="store_true")
     ap.add_argument("--prefix-cache", action="store_true", help="share the KV pages of common prompt prefixes")
+    ap.add_argument("--schedule-policy", default=None, choices=["fcfs", "lpm"],
+                    help="admission order: arrival (fcfs) or longest cached prefix first (lpm; the default with "
+                         "--prefix-cache)")
     ap.add_argument("--enable-mixed-chunk", dest="mixed_chunk", action="store_true",
                     help="prefill batches also carry the running requests' decode tokens")
     ap.add_argument("--int4-weights", action="store_true",
@@ -978,7 +981,8 @@ def main(argv=None):
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
     opts = dict(max_batch=args.max_batch, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
-                prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction, mixed_chunk=args.mixed_chunk)
+                prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction, mixed_chunk=args.mixed_chunk,
+                schedule_policy=args.schedule_policy or ("lpm" if args.prefix_cache else "fcfs"))
     if args.max_seq is not None:
         opts["max_seq"] = args.max_seq
     tokenizer = None

@@ -274,3 +274,22 @@ def test_mixed_chunks_carry_decode_tokens_while_prompts_prefill():
         batch = s.next_batch()
         s.after_decode(batch, [9] * len(batch.reqs))
     assert a.output == [7, 8, 8, 8, 9, 9] and b.output == [8, 9]
+
+
+def test_lpm_admits_the_longest_cached_prefix_first():
+    s, pc, alloc = _pc_sched(num_blocks=64, chunk=1000, max_batch=1)
+    s.policy = "lpm"
+    shared = list(range(500, 548))                                   # 3 full pages
+    _run_one(s, sched_mod.Request(rid=0, prompt=shared + [1], max_new=1))
+    cold = sched_mod.Request(rid=1, prompt=list(range(2000, 2040)), max_new=1)
+    warm = sched_mod.Request(rid=2, prompt=shared + [7, 8], max_new=1)
+    s.add(cold)
+    s.add(warm)
+    b = s.next_batch()                                               # one slot: lpm picks the cache hit
+    assert b.pieces[0].req is warm and warm.cached_pages == 3
+    fcfs, _, _ = _pc_sched(num_blocks=64, chunk=1000, max_batch=1)
+    fcfs.add(sched_mod.Request(rid=3, prompt=[1] * 20, max_new=1))
+    fcfs.add(sched_mod.Request(rid=4, prompt=[2] * 20, max_new=1))
+    assert fcfs.next_batch().pieces[0].req.rid == 3                  # arrival order by default
+    with pytest.raises(ValueError):
+        sched_mod.Scheduler(policy="random")
