@@ -20,7 +20,7 @@ from ..utils import nvtx
 from ..models import LlamaConfig, LlamaTP, LlamaWeights
 from .graph_runner import DecodeGraphRunner, PrefillGraphRunner
 from .kv_cache import PAGE, PagedKVCache, PrefixCache
-from .sampling import GREEDY, SamplingParams, sample
+from .sampling import GREEDY, SamplingParams, adjust_logits, sample
 from .scheduler import Request, Scheduler
 
 
@@ -103,17 +103,21 @@ class LLMEngine:
         return self._sample_from_logits(self.model.full_logits(hidden), reqs, draw)
 
     def _sample_from_logits(self, logits, reqs, draw=None):
+        raw = logits
+        if any(r.sampling is not None and r.sampling.adjusts for r in reqs):
+            logits = adjust_logits(logits, [r.sampling for r in reqs], [r.prompt for r in reqs],
+                                   [r.output for r in reqs], [r.stop_ids for r in reqs])
         params, gens = [], []
         for i, r in enumerate(reqs):
             use = r.sampled and (draw is None or draw[i])
-            params.append(r.sampling if use else GREEDY)
+            params.append(r.sampling if use else GREEDY)  # adjustments are already in the logits
             gens.append((r.rng if r.rng is not None else self._rng) if use else None)
         tokens = sample(logits, params, gens)
         want = [i for i, r in enumerate(reqs) if r.logprobs is not None and (draw is None or draw[i])]
         if want:
-            # logprobs of the model's own distribution (before temperature / top-k / top-p)
-            rows = torch.tensor(want, device=logits.device)
-            lp = torch.log_softmax(logits.index_select(0, rows).float(), dim=-1)
+            # logprobs of the model's own distribution (before penalties, temperature, top-k / top-p)
+            rows = torch.tensor(want, device=raw.device)
+            lp = torch.log_softmax(raw.index_select(0, rows).float(), dim=-1)
             chosen = lp.gather(1, tokens.index_select(0, rows)[:, None])[:, 0].tolist()
             k = max(reqs[i].logprobs for i in want)
             top_v, top_i = torch.topk(lp, k, dim=-1) if k > 0 else (lp[:, :0], lp[:, :0].long())
@@ -434,8 +438,10 @@ class LLMEngine:
         """Offline generation over text, in the shape of sglang's offline
         engine: ``prompts`` is a string or a list of strings;
         ``sampling_params`` a dict of ``max_new_tokens`` (16), ``temperature``
-        (0: greedy), ``top_k``, ``top_p``, ``seed`` and ``stop_token_ids``
-        (default: the checkpoint's EOS ids). Returns one ``{"text",
+        (0: greedy), ``top_k``, ``top_p``, ``seed``, ``stop_token_ids``
+        (default: the checkpoint's EOS ids), ``presence_penalty``,
+        ``frequency_penalty``, ``repetition_penalty``, ``logit_bias`` ({id:
+        bias}) and ``min_new_tokens``. Returns one ``{"text",
         "token_ids", "finish_reason"}`` per prompt (a single dict for a single
         string). ``return_logprob`` adds ``"logprobs"``: per generated token
         (id, logprob, [(id, logprob)] of the ``top_logprobs_num`` most likely)."""
@@ -448,9 +454,16 @@ class LLMEngine:
         stop = self.default_stop_ids if stop is None else tuple(stop)
         temp = float(sp.pop("temperature", 0.0))
         top_k, top_p, seed = int(sp.pop("top_k", 0)), float(sp.pop("top_p", 1.0)), sp.pop("seed", None)
+        adj = dict(presence_penalty=float(sp.pop("presence_penalty", 0.0)),
+                   frequency_penalty=float(sp.pop("frequency_penalty", 0.0)),
+                   repetition_penalty=float(sp.pop("repetition_penalty", 1.0)),
+                   logit_bias=tuple(sorted((int(k), float(v)) for k, v in dict(sp.pop("logit_bias", {})).items())),
+                   min_new_tokens=int(sp.pop("min_new_tokens", 0)))
         if sp:
             raise ValueError(f"unknown sampling params: {', '.join(sorted(sp))}")
-        sampling = SamplingParams(temp, top_k, top_p, seed) if temp > 0 else None
+        sampling = SamplingParams(max(temp, 0.0), top_k, top_p, seed, **adj)
+        if not sampling.adjusts and temp <= 0:
+            sampling = None
         single = isinstance(prompts, str)
         lp = int(top_logprobs_num) if return_logprob else None
         reqs = [self.add_request(tok.encode(p), max_new, stop, sampling, logprobs=lp)

@@ -50,7 +50,8 @@ class Request:
     @property
     def needs_logits(self):
         """Full logits are needed: a sampled request, or one that returns logprobs."""
-        return self.sampled or self.logprobs is not None or self.prompt_logprobs
+        return (self.sampled or self.logprobs is not None or self.prompt_logprobs or
+                (self.sampling is not None and self.sampling.adjusts))
 
     @property
     def total_len(self):

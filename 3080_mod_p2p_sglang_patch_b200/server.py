@@ -446,13 +446,24 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         return text if i < 0 else text[:i]
 
     def _sampling(body):
-        """(temperature, top_k, top_p, seed), or None for greedy."""
+        """The fields of engine.sampling.SamplingParams, in order (temperature,
+        top_k, top_p, seed, presence / frequency / repetition penalties,
+        logit_bias, min tokens), or None for plain greedy decoding."""
         t = float(body.get("temperature") or 0.0)
-        if t <= 0.0:
+        try:
+            bias = tuple(sorted((int(k), float(v)) for k, v in (body.get("logit_bias") or {}).items()))
+        except (TypeError, ValueError, AttributeError) as e:
+            raise HTTPException(400, "logit_bias must map token ids to numbers") from e
+        adj = (float(body.get("presence_penalty") or 0.0), float(body.get("frequency_penalty") or 0.0),
+               float(body.get("repetition_penalty") or 1.0), bias,
+               int(body.get("min_tokens") or body.get("min_new_tokens") or 0))
+        if adj[2] <= 0:
+            raise HTTPException(400, "repetition_penalty must be positive")
+        if t <= 0.0 and adj == (0.0, 0.0, 1.0, (), 0):
             return None
         seed = body.get("seed")
-        return (t, int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
-                None if seed is None else int(seed))
+        return (max(t, 0.0), int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
+                None if seed is None else int(seed)) + adj
 
     def _run(prompt, max_tokens, stop=None, sampling=None, stops=(), logprobs=None, prompt_logprobs=False):
         """(output ids, finish reason, per-token logprobs, prompt logprobs)."""
@@ -505,7 +516,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         def samp(i):
             if sampling is None or sampling[3] is None:
                 return sampling
-            return sampling[:3] + (sampling[3] + i,)
+            return sampling[:3] + (sampling[3] + i,) + sampling[4:]
 
         return await asyncio.gather(*[run_in_threadpool(_run, prompt, max_tokens, stop, samp(i), stops, lp, plp)
                                       for i in range(n)])

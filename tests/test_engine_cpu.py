@@ -487,3 +487,19 @@ def test_perplexity_tool_on_the_oracle():
                     "--device", "cpu", "--compare", "oracle"])
     assert res["tokens"] == 297 and 1 < res["ppl"] < float("inf")      # 3 windows, first token of each excluded
     assert res["mean_abs_logprob_diff"] == 0.0 and res["ppl_compare"] == res["ppl"]
+
+
+def test_penalties_bias_and_min_tokens_through_the_engine():
+    prompt = list(range(300, 330))
+    forced = _engine().generate_text("x", {"max_new_tokens": 4, "logit_bias": {77: 100.0}})
+    assert forced["token_ids"] == [77] * 4                                   # greedy over biased logits
+    plain = _engine().generate([prompt], max_new_tokens=8)[0]
+    eng = _engine()
+    r = eng.add_request(prompt, 8, sampling=eng_mod.SamplingParams(frequency_penalty=100.0))
+    eng.run()
+    assert len(set(r.output)) == 8                                           # a used token is never picked again
+    first = plain[0]
+    eng = _engine()
+    held = eng.add_request(prompt, 5, stop_ids=(first,), sampling=eng_mod.SamplingParams(min_new_tokens=3))
+    eng.run()
+    assert len(held.output) >= 3 and first not in held.output[:3]            # the stop id could not end it early

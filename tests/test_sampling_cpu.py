@@ -42,3 +42,20 @@ def test_seeded_draws_reproduce():
     x = torch.randn(1, 1000, generator=torch.Generator().manual_seed(3))
     a = [int(smp.sample(x, [P(temperature=1.0)], [torch.Generator().manual_seed(7)])[0]) for _ in range(5)]
     assert len(set(a)) == 1
+
+
+def test_logit_adjustments():
+    samp = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine.sampling")
+    SP = samp.SamplingParams
+    logits = torch.tensor([[2.0, -1.0, 0.5, 3.0, 0.0],
+                           [1.0, 1.0, 1.0, 1.0, 1.0],
+                           [0.0, 0.0, 0.0, 0.0, 9.0]])
+    params = [SP(repetition_penalty=2.0), SP(presence_penalty=0.5, frequency_penalty=0.25, logit_bias=((4, 3.0),)),
+              SP(min_new_tokens=3)]
+    out = samp.adjust_logits(logits, params, prompts=[[0, 1], [], []], outputs=[[3], [2, 2, 0], [7]],
+                             stop_ids=[(), (), (4,)])
+    assert torch.equal(out[0], torch.tensor([1.0, -2.0, 0.5, 1.5, 0.0]))     # seen: 0, 1, 3 (> 0 halved, < 0 doubled)
+    assert torch.allclose(out[1], torch.tensor([1 - 0.5 - 0.25, 1.0, 1 - 0.5 - 0.5, 1.0, 4.0]))
+    assert out[2, 4] == float("-inf") and out[2, :4].eq(0).all()            # the stop id waits for 3 tokens
+    assert torch.equal(logits[0], torch.tensor([2.0, -1.0, 0.5, 3.0, 0.0]))  # the input is left as it was
+    assert SP().adjusts is False and SP(min_new_tokens=1).adjusts and SP(temperature=0.5).adjusts is False

@@ -807,3 +807,27 @@ def test_server_entry_point_end_to_end_on_cpu():
         if proc.poll() is None:
             os.killpg(proc.pid, _signal.SIGKILL)   # the process group this test started
             proc.wait(timeout=30)
+
+
+def test_sampling_adjustments_reach_the_engine():
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        r = requests.post(base + "/v1/completions", json={
+            "prompt": [1, 2], "max_tokens": 2, "presence_penalty": 0.5, "frequency_penalty": 0.25,
+            "repetition_penalty": 1.1, "logit_bias": {"7": 5, "3": -100}, "min_tokens": 2}, timeout=30)
+        assert r.status_code == 200
+        sp = eng.sampling_seen[-1]
+        assert (sp.temperature, sp.presence_penalty, sp.frequency_penalty, sp.repetition_penalty) == (0.0, 0.5, 0.25, 1.1)
+        assert sp.logit_bias == ((3, -100.0), (7, 5.0)) and sp.min_new_tokens == 2
+        requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 1}, timeout=30)
+        assert eng.sampling_seen[-1] is None                                # plain greedy: no adjustments
+        bad = requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 1,
+                                                            "logit_bias": {"x": 1}}, timeout=30)
+        assert bad.status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
