@@ -503,3 +503,63 @@ def test_penalties_bias_and_min_tokens_through_the_engine():
     held = eng.add_request(prompt, 5, stop_ids=(first,), sampling=eng_mod.SamplingParams(min_new_tokens=3))
     eng.run()
     assert len(held.output) >= 3 and first not in held.output[:3]            # the stop id could not end it early
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_engine_fuzz_mixed_features_and_aborts(seed):
+    """Random requests over shared prefixes with every per-request feature,
+    random aborts between steps, random chunking / mixed chunks / policy;
+    afterwards every request ended properly and every page and slot is back."""
+    import random
+
+    rnd = random.Random(seed)
+    eng = _engine(chunk=rnd.choice([16, 32, 48]), max_batch=rnd.choice([2, 3, 4]), prefix_cache=True,
+                  mixed_chunk=rnd.random() < 0.5, schedule_policy=rnd.choice(["fcfs", "lpm"]))
+    SP = eng_mod.SamplingParams
+    prefixes = [[rnd.randrange(1, CFG.vocab) for _ in range(rnd.choice([16, 32, 40]))] for _ in range(3)]
+    reqs = []
+
+    def submit():
+        prompt = rnd.choice(prefixes)[:rnd.randrange(8, 41)] + [rnd.randrange(1, CFG.vocab)
+                                                                 for _ in range(rnd.randrange(1, 30))]
+        kind = rnd.random()
+        kw = {}
+        if kind < 0.25:
+            kw["sampling"] = SP(temperature=1.0, top_k=20, seed=rnd.randrange(100))
+        elif kind < 0.4:
+            kw["sampling"] = SP(frequency_penalty=1.0, logit_bias=((5, 2.0),), min_new_tokens=2)
+        if rnd.random() < 0.3:
+            kw["logprobs"] = rnd.choice([0, 2])
+        if rnd.random() < 0.15:
+            kw["prompt_logprobs"] = True
+        if rnd.random() < 0.2:
+            kw["stop_ids"] = tuple(rnd.randrange(1, CFG.vocab) for _ in range(50))
+        reqs.append(eng.add_request(prompt, rnd.randrange(1, 7), **kw))
+
+    for _ in range(6):
+        submit()
+    steps = 0
+    while eng.sched.has_work():
+        eng.step()
+        steps += 1
+        if rnd.random() < 0.3 and len(reqs) < 14:
+            submit()
+        if rnd.random() < 0.1:
+            live = [r for r in reqs if not r.done]
+            if live:
+                eng.abort(rnd.choice(live).rid)
+        assert steps < 500
+    eng.run()
+    for r in reqs:
+        assert r.done and r.finish_reason in ("length", "stop", "abort"), r.rid
+        assert len(r.output) <= r.max_new
+        if r.finish_reason == "length":
+            assert len(r.output) == r.max_new
+        if r.logprobs is not None and r.finish_reason != "abort":
+            assert len(r.token_logprobs) == len(r.output)
+        if r.prompt_logprobs and r.finish_reason != "abort":
+            assert len(r.prompt_token_logprobs) == len(r.prompt)
+    pc, alloc = eng.prefix_cache, eng.kv.alloc
+    assert alloc.free + pc.evictable == alloc.capacity
+    assert all(v == 0 for v in pc.ref.values())
+    assert sorted(eng.sched._free_slots) == list(range(eng.max_batch))
