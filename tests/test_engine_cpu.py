@@ -563,3 +563,66 @@ def test_engine_fuzz_mixed_features_and_aborts(seed):
     assert alloc.free + pc.evictable == alloc.capacity
     assert all(v == 0 for v in pc.ref.values())
     assert sorted(eng.sched._free_slots) == list(range(eng.max_batch))
+
+
+def _lockstep_fuzz_worker(rank, world, seed):
+    import datetime
+    import random
+
+    import torch.distributed as dist
+
+    par = importlib.import_module(f"{PKG}.parallel")
+    srv_mod = importlib.import_module(f"{PKG}.server")
+    tp = par.TPGroup(None, "cpu", use_mailbox=False)
+    ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+    eng = eng_mod.LLMEngine(CFG, tp=tp, impl="oracle", device="cpu", full_init=True, seed=0, max_batch=3,
+                            max_seq=256, chunk=32, prefix_cache=True, mixed_chunk=True)
+    server = srv_mod.EngineServer(eng, ctrl, rank, world, max_prompt=256)
+    done = []
+    orig = eng.sched._finish
+
+    def spy(req):
+        done.append((req.rid, tuple(req.output), req.finish_reason))
+        orig(req)
+
+    eng.sched._finish = spy
+    if rank == 0:
+        def clients():
+            rnd = random.Random(seed)
+            tok = srv_mod.ByteTokenizer()
+            threads = []
+            for i in range(10):
+                prompt = [rnd.randrange(1, 256) for _ in range(rnd.randrange(5, 60))]
+                kind = rnd.random()
+
+                def go(prompt=prompt, kind=kind, i=i):
+                    if kind < 0.3:   # a stream whose client leaves after its first tokens
+                        g = server.submit_stream(prompt, 20, timeout=120)
+                        next(g)
+                        g.close()
+                    elif kind < 0.5:
+                        server.submit(prompt, 8, timeout=120, stop_strs=("a",), detok=tok.decode)
+                    elif kind < 0.7:
+                        server.submit(prompt, 6, timeout=120, sampling=(0.9, 10, 1.0, i))
+                    else:
+                        server._submit_pending(prompt, 4, timeout=120, logprobs=1)
+                threads.append(threading.Thread(target=go))
+                threads[-1].start()
+            for t in threads:
+                t.join()
+            server.stop()
+
+        threading.Thread(target=clients, daemon=True).start()
+    server.serve_forever()
+    return {"done": sorted(done), "free": eng.kv.alloc.free + eng.prefix_cache.evictable,
+            "cap": eng.kv.alloc.capacity}
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_lockstep_server_fuzz_two_ranks(seed):
+    """Concurrent clients with streams that disconnect, stop strings, sampling
+    and logprobs against two lockstep ranks: both ranks finish the same
+    requests with the same tokens, and every page comes back."""
+    res = run_ranks(_lockstep_fuzz_worker, 2, args=(seed,), timeout=300)
+    assert res[0]["done"] == res[1]["done"] and len(res[0]["done"]) == 10
+    assert all(r["free"] == r["cap"] for r in res.values())
