@@ -97,8 +97,11 @@ class EngineServer:
 
     SHUTDOWN = "__shutdown__"
 
-    def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None, stop_ids=()):
+    def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None, stop_ids=(),
+                 log_requests: bool = False):
         self.engine = engine
+        # rank 0 logs one JSON line per finished request (id, tokens, reason, latencies)
+        self.log_requests = log_requests
         self.stop_ids = tuple(stop_ids)  # default stop tokens (e.g. the checkpoint's EOS)
         self.group = group
         self.rank = rank
@@ -333,6 +336,13 @@ class EngineServer:
                         if times and getattr(r, "t_arrive", 0):
                             self.ttft.append(times[0] - r.t_arrive)
                             self.itl.extend(b - a for a, b in zip(times, times[1:]))
+                        if self.log_requests and self.rank == 0:
+                            t0 = getattr(r, "t_arrive", 0) or 0
+                            logger.info("request %s", json.dumps({
+                                "id": p.sid, "prompt_tokens": len(p.prompt), "output_tokens": len(r.output),
+                                "finish_reason": getattr(r, "finish_reason", None),
+                                "ttft_ms": round((times[0] - t0) * 1e3, 3) if times and t0 else None,
+                                "e2e_ms": round((time.perf_counter() - t0) * 1e3, 3) if t0 else None}))
                         out = list(r.output)
                         p.reason = getattr(r, "finish_reason", None) or "length"
                         if p.stop_strs and p.detok is not None:
@@ -820,6 +830,7 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--port", type=int, default=8001)
     ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on the model endpoints")
     ap.add_argument("--served-model-name", default=None, help="model id reported by /v1/models")
+    ap.add_argument("--log-requests", action="store_true", help="one JSON log line per finished request")
     ap.add_argument("--chat-template", default=None,
                     help="Jinja chat template (a file, or the template text) instead of the checkpoint's own")
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
@@ -1011,7 +1022,8 @@ def main(argv=None):
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
         eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, device=dev, **opts)
     stop = eng.default_stop_ids
-    server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop)
+    server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop,
+                          log_requests=args.log_requests)
     http = None
     if rank == 0:
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step

@@ -831,3 +831,23 @@ def test_sampling_adjustments_reach_the_engine():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_request_log_lines(caplog):
+    import json as _json
+    import logging
+
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096, log_requests=True)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    try:
+        with caplog.at_level(logging.INFO, logger=srv_mod.__name__):
+            server.submit([1, 2, 3], 4, timeout=30)
+        lines = [r.getMessage() for r in caplog.records if r.getMessage().startswith("request ")]
+        rec = _json.loads(lines[-1][len("request "):])
+        assert rec["prompt_tokens"] == 3 and rec["output_tokens"] == 4 and rec["finish_reason"] == "length"
+        assert rec["e2e_ms"] >= rec["ttft_ms"] >= 0
+    finally:
+        server.stop()
+        loop.join(timeout=30)
