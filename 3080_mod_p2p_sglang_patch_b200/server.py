@@ -831,6 +831,19 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on the model endpoints")
     ap.add_argument("--served-model-name", default=None, help="model id reported by /v1/models")
     ap.add_argument("--log-requests", action="store_true", help="one JSON log line per finished request")
+    # sglang launch flags with the same meaning here
+    ap.add_argument("--dtype", default="auto", choices=["auto", "bfloat16", "bf16"],
+                    help="compute dtype: bf16 (auto)")
+    ap.add_argument("--kv-cache-dtype", default="auto", choices=["auto", "bfloat16", "bf16"],
+                    help="KV cache dtype: bf16 (auto)")
+    ap.add_argument("--quantization", default=None, choices=["awq", "awq_marlin"],
+                    help="AWQ checkpoints: keep the int4 weights packed (same as --int4-weights)")
+    ap.add_argument("--random-seed", "--seed", dest="seed", type=int, default=0,
+                    help="random weights and unseeded sampling draws")
+    ap.add_argument("--log-level", default="info", choices=["debug", "info", "warning", "error"])
+    ap.add_argument("--max-total-tokens", type=int, default=None, help="KV cache capacity in tokens")
+    ap.add_argument("--disable-radix-cache", action="store_true",
+                    help="no prefix sharing (the default unless --prefix-cache)")
     ap.add_argument("--chat-template", default=None,
                     help="Jinja chat template (a file, or the template text) instead of the checkpoint's own")
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
@@ -994,7 +1007,11 @@ def main(argv=None):
         raise SystemExit("--device cpu runs the oracle model only (--impl oracle)")
     if not on_cpu and not torch.cuda.is_available():
         raise SystemExit("the server needs a CUDA GPU per rank (none visible)")
-    logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
+    logging.basicConfig(level=getattr(logging, args.log_level.upper()), format="%(asctime)s %(name)s %(message)s")
+    if args.quantization in ("awq", "awq_marlin"):
+        args.int4_weights = True
+    if args.disable_radix_cache:
+        args.prefix_cache = False
     rank, world, local = par.init_distributed(backend="gloo" if on_cpu else None, timeout_s=600)
     dev = torch.device("cpu") if on_cpu else torch.device("cuda", local)
     # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow (the
@@ -1007,6 +1024,9 @@ def main(argv=None):
                 schedule_policy=args.schedule_policy or ("lpm" if args.prefix_cache else "fcfs"))
     if args.max_seq is not None:
         opts["max_seq"] = args.max_seq
+    if args.max_total_tokens:
+        opts["kv_blocks"] = -(-args.max_total_tokens // 16) + 1  # pages of 16 tokens + the reserved page
+    opts["seed"] = args.seed
     tokenizer = None
     if model_path:
         eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, int4_weights=args.int4_weights,
@@ -1020,7 +1040,7 @@ def main(argv=None):
     else:
         cfg = models.LlamaConfig.by_name(name)
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
-        eng = eng_mod.LLMEngine(cfg, tp=tp, seed=0, device=dev, **opts)
+        eng = eng_mod.LLMEngine(cfg, tp=tp, device=dev, **opts)
     stop = eng.default_stop_ids
     server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop,
                           log_requests=args.log_requests)

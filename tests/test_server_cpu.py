@@ -851,3 +851,15 @@ def test_request_log_lines(caplog):
     finally:
         server.stop()
         loop.join(timeout=30)
+
+
+def test_more_sglang_launch_flags_parse():
+    p = srv_mod.build_parser()
+    a = p.parse_args(["--model", "tiny", "--dtype", "bfloat16", "--kv-cache-dtype", "auto", "--quantization", "awq",
+                      "--random-seed", "7", "--log-level", "warning", "--max-total-tokens", "100000",
+                      "--disable-radix-cache", "--log-requests"])
+    assert (a.quantization, a.seed, a.log_level, a.max_total_tokens, a.disable_radix_cache, a.log_requests) == \
+        ("awq", 7, "warning", 100000, True, True)
+    import pytest as _pt
+    with _pt.raises(SystemExit):
+        p.parse_args(["--kv-cache-dtype", "fp8_e5m2"])      # not supported: refused, not ignored
