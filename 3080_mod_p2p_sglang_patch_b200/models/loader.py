@@ -200,6 +200,20 @@ def awq_quantize(w: torch.Tensor, group: int = 128):
     return awq_pack(q.to(torch.int32)), awq_pack(z.to(torch.int32)), s
 
 
+def quantize_weights_int4(weights, group: int = 128):
+    """Pack every decoder linear of ``weights`` (a LlamaWeights of any TP
+    shard, on any device) as AWQ int4 in place (round-to-nearest per group),
+    giving ``ops.Int4Weight`` linears: the int4 path measured on random
+    weights. Returns ``weights``."""
+    from ..ops import Int4Weight
+
+    for L in weights.layers:
+        for k in ("qkv", "o", "gate_up", "down"):
+            qw, qz, s = awq_quantize(L[k], group)
+            L[k] = Int4Weight(qw, qz, s, group)
+    return weights
+
+
 def awq_group_size(qc: dict) -> int:
     """Group size of a ``quantization_config`` this loader accepts (AWQ,
     4-bit, zero point, gemm packing); -1 = one group per input row range."""

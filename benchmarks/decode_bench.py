@@ -26,6 +26,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="8b")
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
+    ap.add_argument("--int4", action="store_true", help="random weights packed as AWQ int4 (native only)")
     ap.add_argument("--batches", default="1,8,32,64")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--gen", type=int, default=256)
@@ -40,8 +41,13 @@ def main():
     cfg = models.LlamaConfig.by_name(args.model)
     batches = [int(b) for b in args.batches.split(",")]
     max_bs = max(batches)
+    weights = None
+    if args.int4:  # the random weights packed as AWQ int4 (int4 GEMV decode)
+        weights = models.LlamaWeights(cfg, tp.rank if tp else 0, world, dev, seed=0)
+        models.quantize_weights_int4(weights)
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=max_bs, max_seq=args.ctx + args.gen + 16, chunk=8192, seed=0,
-                            use_graphs=True, impl=args.impl, graph_sizes=tuple(sorted(set(batches))))
+                            use_graphs=True, impl=args.impl, graph_sizes=tuple(sorted(set(batches))),
+                            weights=weights, device=dev)
     g = torch.Generator().manual_seed(7)
     for bs in batches:
         prompts = torch.randint(0, cfg.vocab, (bs, args.ctx), generator=g).tolist()
@@ -78,6 +84,7 @@ def main():
         mean = sum(ts) / len(ts)
         if rank == 0:
             print(json.dumps({"metric": "decode_itl", "model": cfg.name, "impl": args.impl, "tp": world, "batch": bs,
+                              "int4_weights": args.int4,
                               "ctx": args.ctx, "gen": args.gen, "itl_p50_ms": p50, "itl_p99_ms": p99,
                               "decode_tok_s": bs / (mean * 1e-3), "steps": steps}), flush=True)
     if eng.graphs is not None:

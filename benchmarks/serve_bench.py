@@ -27,6 +27,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="70b")
     ap.add_argument("--impl", default="native", choices=["native", "torch"])
+    ap.add_argument("--int4", action="store_true", help="random weights packed as AWQ int4 (native only)")
+    ap.add_argument("--mixed-chunk", action="store_true", help="prefill batches carry decode tokens")
     ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--min-prompt", type=int, default=512)
     ap.add_argument("--max-prompt", type=int, default=8192)
@@ -42,9 +44,14 @@ def main():
     dev = torch.device("cuda", local)
     tp = par.TPGroup(None, dev, use_mailbox=(args.impl == "native")) if world > 1 else None
     cfg = models.LlamaConfig.by_name(args.model)
+    weights = None
+    if args.int4:  # the random weights packed as AWQ int4 (int4 GEMV decode, per-layer expansion for prefill)
+        weights = models.LlamaWeights(cfg, tp.rank if tp else 0, world, dev, seed=0)
+        models.quantize_weights_int4(weights)
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=args.requests, max_seq=args.max_prompt + args.gen + 16,
                             chunk=args.chunk, seed=0, use_graphs=True, impl=args.impl,
-                            sp=bool(args.sp) and args.impl == "native")
+                            sp=bool(args.sp) and args.impl == "native" and not args.int4,
+                            mixed_chunk=args.mixed_chunk, weights=weights, device=dev)
     g = torch.Generator().manual_seed(11)
     lens = torch.randint(args.min_prompt, args.max_prompt + 1, (args.requests,), generator=g).tolist()
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in lens]
@@ -78,6 +85,7 @@ def main():
     if rank == 0:
         print(json.dumps({
             "metric": "mixed_serving", "model": cfg.name, "impl": args.impl, "tp": world, "requests": args.requests,
+            "int4_weights": args.int4, "mixed_chunk": args.mixed_chunk,
             "sequence_parallel": eng.sp is not None,
             "prompt_tokens": pre_tok, "gen_tokens": args.requests * args.gen,
             "prefill_tok_s": pre_tok / (pre_ms * 1e-3),

@@ -347,3 +347,16 @@ def test_awq_int4_shards_stay_packed_and_match_the_bf16_load(tmp_path):
                     assert isinstance(a, ops.Int4Weight) and a.shape == tuple(b.shape), (i, k)
                     dense = loader.awq_dequant(a.qweight, a.qzeros, a.scales, a.group).to(torch.bfloat16)
                     assert torch.equal(dense, b), (tp, r, i, k)
+
+
+def test_quantize_random_weights_to_int4():
+    cfg = models.LlamaConfig.tiny()
+    w = models.LlamaWeights(cfg, 0, 1, "cpu", seed=0, full_init=True)
+    ref = {k: w.layers[0][k].float().clone() for k in ("qkv", "o", "gate_up", "down")}
+    models.quantize_weights_int4(w, group=128)
+    loader = importlib.import_module("3080_mod_p2p_sglang_patch_b200.models.loader")
+    for k, dense in ref.items():
+        q = w.layers[0][k]
+        assert isinstance(q, ops.Int4Weight) and q.shape == tuple(dense.shape)
+        err = (loader.awq_dequant(q.qweight, q.qzeros, q.scales, q.group) - dense).abs().max().item()
+        assert err <= dense.abs().max().item() / 15 + 1e-3            # within one quantization step
