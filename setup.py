@@ -10,7 +10,7 @@ code=sm_100a``, which also stops torch from adding its own arch list.
 """
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 PKG = "3080_mod_p2p_sglang_patch_b200"
@@ -57,7 +57,7 @@ ext_modules = [
 setup(
     name="mailbox-ar-b200",
     version="0.1.0",
-    packages=[PKG, "mailbox_ar_b200"],
+    packages=find_packages(include=[PKG, PKG + ".*", "mailbox_ar_b200"]),
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

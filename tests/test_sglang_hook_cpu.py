@@ -63,3 +63,16 @@ def test_sglang_group_coordinator_flow_on_two_ranks():
         assert o["declined_returns_none"] is True
         assert o["in_capture"] == "custom"
         assert o["closed"] is True and o["off"] == "default"
+
+
+def test_dropin_module_exports_the_communicator():
+    """The file a user copies into sglang's device_communicators/ exports this
+    package's MailboxAR under the reference's module name."""
+    import importlib.util
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        PKG, "integrations", "sglang", "mailbox_all_reduce.py")
+    spec = importlib.util.spec_from_file_location("mailbox_all_reduce", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.MailboxAR is importlib.import_module(f"{PKG}.parallel").MailboxAR
