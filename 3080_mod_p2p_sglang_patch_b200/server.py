@@ -48,10 +48,14 @@ from .engine.tokenizer import ByteTokenizer, HFTokenizer, load_chat_template  # 
 logger = logging.getLogger(__name__)
 
 
+class Overloaded(RuntimeError):
+    """The server holds its maximum of queued and running requests."""
+
+
 class _Pending:
     __slots__ = ("prompt", "max_new", "stop_ids", "sampling", "event", "output", "error", "stream", "req", "sent",
                  "reason", "sid", "stop_strs", "detok", "checked", "stop_hit", "abort_sent", "logprobs",
-                 "token_logprobs", "prompt_logprobs", "prompt_token_logprobs")
+                 "token_logprobs", "prompt_logprobs", "prompt_token_logprobs", "on_finish")
 
     def __init__(self, prompt, max_new, stream=False, stop_ids=(), sampling=None, sid=-1, stop_strs=(), detok=None,
                  logprobs=None, prompt_logprobs=False):
@@ -70,6 +74,7 @@ class _Pending:
         self.token_logprobs = []
         self.prompt_logprobs = bool(prompt_logprobs)  # also score the prompt (echo)
         self.prompt_token_logprobs = []
+        self.on_finish = None     # rank 0: releases the request's place in the overload count
         self.reason = "length"
         self.event = threading.Event()
         self.output = None
@@ -80,6 +85,9 @@ class _Pending:
         self.sent = 0    # tokens already streamed
 
     def finish(self, output=None, error=None):
+        if self.on_finish is not None:
+            self.on_finish()
+            self.on_finish = None
         self.output, self.error = output, error
         if self.stream is not None:
             self.stream.put(None)
@@ -98,8 +106,13 @@ class EngineServer:
     SHUTDOWN = "__shutdown__"
 
     def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None, stop_ids=(),
-                 log_requests: bool = False):
+                 log_requests: bool = False, max_queued: int = None):
         self.engine = engine
+        # overload: new requests are refused (HTTP 503) while this many are
+        # queued or running; None = no bound
+        self.max_queued = max_queued
+        self._live = 0                   # submitted and not finished (rank 0)
+        self._live_lock = threading.Lock()
         # rank 0 logs one JSON line per finished request (id, tokens, reason, latencies)
         self.log_requests = log_requests
         self.stop_ids = tuple(stop_ids)  # default stop tokens (e.g. the checkpoint's EOS)
@@ -193,6 +206,14 @@ class EngineServer:
         if reason_out is not None:
             reason_out.append(p.reason)
 
+    def overloaded(self) -> bool:
+        with self._live_lock:
+            return self.max_queued is not None and self._live >= self.max_queued
+
+    def _release_live(self):
+        with self._live_lock:
+            self._live -= 1
+
     def abort(self, p):
         """End a submitted request early (rank 0, any thread): every rank drops
         it at the same step; its waiter gets the tokens so far."""
@@ -221,6 +242,10 @@ class EngineServer:
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
+        with self._live_lock:
+            if self.max_queued is not None and self._live >= self.max_queued:
+                raise Overloaded(f"{self._live} requests in flight (limit {self.max_queued})")
+            self._live += 1
         stop_strs = tuple(x for x in stop_strs if x)
         if stop_strs and detok is None:
             raise ValueError("stop strings need a detokenizer")
@@ -228,6 +253,7 @@ class EngineServer:
                      stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling,
                      sid=next(self._sids), stop_strs=stop_strs, detok=detok, logprobs=logprobs,
                      prompt_logprobs=prompt_logprobs)
+        p.on_finish = self._release_live
         self.q.put(p)
         return p
 
@@ -543,6 +569,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
             server._enqueue_check(prompt, max_tokens)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
+        if server.overloaded():  # before a stream starts: a status code, not an error event
+            raise HTTPException(503, "server overloaded")
 
     def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None, stops=()):
         """Server-sent events: one chunk per engine step's new tokens (the text
@@ -831,6 +859,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on the model endpoints")
     ap.add_argument("--served-model-name", default=None, help="model id reported by /v1/models")
     ap.add_argument("--log-requests", action="store_true", help="one JSON log line per finished request")
+    ap.add_argument("--max-queued-requests", type=int, default=None,
+                    help="refuse new requests (HTTP 503) while this many are queued or running")
     # sglang launch flags with the same meaning here
     ap.add_argument("--dtype", default="auto", choices=["auto", "bfloat16", "bf16"],
                     help="compute dtype: bf16 (auto)")
@@ -1043,7 +1073,7 @@ def main(argv=None):
         eng = eng_mod.LLMEngine(cfg, tp=tp, device=dev, **opts)
     stop = eng.default_stop_ids
     server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop,
-                          log_requests=args.log_requests)
+                          log_requests=args.log_requests, max_queued=args.max_queued_requests)
     http = None
     if rank == 0:
         # Ctrl-C / SIGTERM on rank 0: every rank leaves the loop at the same step

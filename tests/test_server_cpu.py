@@ -863,3 +863,39 @@ def test_more_sglang_launch_flags_parse():
     import pytest as _pt
     with _pt.raises(SystemExit):
         p.parse_args(["--kv-cache-dtype", "fp8_e5m2"])      # not supported: refused, not ignored
+
+
+def test_overload_bound_refuses_with_503_and_recovers():
+    import requests
+
+    from conftest import free_port
+
+    eng = _SlowEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096, max_queued=2)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    url = f"http://127.0.0.1:{port}/v1/completions"
+    try:
+        results = []
+        ths = [threading.Thread(target=lambda: results.append(
+            requests.post(url, json={"prompt": [1], "max_tokens": 60}, timeout=60).status_code)) for _ in range(2)]
+        for t in ths:
+            t.start()
+        import time as _t
+        deadline = _t.time() + 10
+        while server._live < 2 and _t.time() < deadline:
+            _t.sleep(0.01)
+        r = requests.post(url, json={"prompt": [2], "max_tokens": 2}, timeout=60)
+        assert r.status_code == 503                                   # two in flight: refused
+        s = requests.post(url, json={"prompt": [2], "max_tokens": 2, "stream": True}, timeout=60)
+        assert s.status_code == 503                                   # a stream is refused up front too
+        for t in ths:
+            t.join()
+        assert results == [200, 200] and server._live == 0
+        assert requests.post(url, json={"prompt": [3], "max_tokens": 2}, timeout=60).status_code == 200
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
