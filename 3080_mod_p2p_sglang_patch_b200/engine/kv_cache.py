@@ -90,6 +90,18 @@ class PrefixCache:
             self.ref[b] += 1
         self.hits += len(blocks)
 
+    def flush(self) -> int:
+        """Evict every unreferenced cached page (sglang's flush_cache); pages
+        live requests hold stay. Returns the pages freed."""
+        n = 0
+        while self.lru:
+            b, _ = self.lru.popitem(last=False)
+            del self.table[self.key_of.pop(b)]
+            del self.ref[b]
+            self.alloc.release([b])
+            n += 1
+        return n
+
     def alloc_blocks(self, n: int):
         """n free blocks, evicting unreferenced cached pages (oldest first) if needed."""
         while self.alloc.free < n and self.lru:

@@ -104,6 +104,7 @@ class EngineServer:
     """
 
     SHUTDOWN = "__shutdown__"
+    FLUSH = "__flush_cache__"
 
     def __init__(self, engine, group=None, rank: int = 0, world: int = 1, max_prompt: int = None, stop_ids=(),
                  log_requests: bool = False, max_queued: int = None):
@@ -214,6 +215,10 @@ class EngineServer:
         with self._live_lock:
             self._live -= 1
 
+    def flush_cache(self):
+        """Drop the prefix cache's unreferenced pages on every rank (rank 0)."""
+        self.q.put(self.FLUSH)
+
     def abort(self, p):
         """End a submitted request early (rank 0, any thread): every rank drops
         it at the same step; its waiter gets the tokens so far."""
@@ -292,7 +297,7 @@ class EngineServer:
                         for c in cmds]]
             dist.broadcast_object_list(payload, src=0, group=self.group)
             if self.rank != 0:
-                cmds = [c if c == self.SHUTDOWN or c[0] == self.ABORT else
+                cmds = [c if isinstance(c, str) or c[0] == self.ABORT else
                         _Pending(c[1], c[2], stop_ids=c[3], sampling=c[4], sid=c[0], logprobs=c[5],
                                  prompt_logprobs=c[6]) for c in payload[0]]
         return cmds
@@ -307,6 +312,11 @@ class EngineServer:
                 for c in cmds:
                     if c == self.SHUTDOWN:
                         stop = True
+                        continue
+                    if c == self.FLUSH:  # every rank, same step
+                        pc = getattr(eng, "prefix_cache", None)
+                        if pc is not None:
+                            pc.flush()
                         continue
                     if isinstance(c, tuple):  # (ABORT, sid): the same request on every rank
                         rid = self._rid_of_sid.get(c[1])
@@ -395,7 +405,7 @@ class EngineServer:
                     c = self.q.get_nowait()
                 except queue.Empty:
                     break
-                if c != self.SHUTDOWN:
+                if isinstance(c, _Pending):
                     c.finish(error="server stopped")
 
 
@@ -628,6 +638,35 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         from fastapi.responses import PlainTextResponse
 
         return PlainTextResponse(render_metrics(server), media_type="text/plain; version=0.0.4")
+
+    @app.post("/flush_cache")
+    def flush_cache():
+        server.flush_cache()
+        return {"status": "ok"}
+
+    @app.get("/get_model_info")
+    def model_info():
+        eng = server.engine
+        cfg = getattr(eng, "cfg", None)
+        return {"model_path": model_name, "is_generation": True,
+                "max_seq": getattr(eng, "max_seq", None), "tp_size": server.world,
+                "vocab_size": getattr(cfg, "vocab", None)}
+
+    @app.get("/get_server_info")
+    def server_info():
+        eng = server.engine
+        return {"tp_size": server.world, "max_batch": getattr(eng, "max_batch", None),
+                "chunk": getattr(eng, "chunk", None), "impl": getattr(eng, "impl", None),
+                "prefix_cache": getattr(eng, "prefix_cache", None) is not None,
+                "max_queued_requests": server.max_queued, **server.stats}
+
+    @app.post("/tokenize")
+    def tokenize(body: dict):
+        return {"tokens": tok.encode(str(body.get("text", "")))}
+
+    @app.post("/detokenize")
+    def detokenize(body: dict):
+        return {"text": tok.decode([int(t) for t in body.get("tokens") or []])}
 
     @app.get("/v1/models")
     def models():

@@ -626,3 +626,40 @@ def test_lockstep_server_fuzz_two_ranks(seed):
     res = run_ranks(_lockstep_fuzz_worker, 2, args=(seed,), timeout=300)
     assert res[0]["done"] == res[1]["done"] and len(res[0]["done"]) == 10
     assert all(r["free"] == r["cap"] for r in res.values())
+
+
+def _flush_worker(rank, world):
+    import datetime
+
+    import torch.distributed as dist
+
+    par = importlib.import_module(f"{PKG}.parallel")
+    srv_mod = importlib.import_module(f"{PKG}.server")
+    tp = par.TPGroup(None, "cpu", use_mailbox=False)
+    ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
+    eng = eng_mod.LLMEngine(CFG, tp=tp, impl="oracle", device="cpu", full_init=True, seed=0, max_batch=2,
+                            max_seq=256, chunk=64, prefix_cache=True)
+    server = srv_mod.EngineServer(eng, ctrl, rank, world, max_prompt=256)
+    seen = {}
+    if rank == 0:
+        def client():
+            server.submit(list(range(10, 60)), 2, timeout=60)            # leaves 3 cached pages
+            server.flush_cache()
+            server.submit([1, 2, 3], 1, timeout=60)                     # a step after the flush
+            server.stop()
+
+        threading.Thread(target=client, daemon=True).start()
+    orig = eng.prefix_cache.flush
+
+    def spy():
+        seen["flushed"] = orig()
+        return seen["flushed"]
+
+    eng.prefix_cache.flush = spy
+    server.serve_forever()
+    return {"flushed": seen.get("flushed"), "evictable": eng.prefix_cache.evictable}
+
+
+def test_flush_cache_reaches_every_rank():
+    res = run_ranks(_flush_worker, 2)
+    assert res[0] == res[1] and res[0]["flushed"] == 3

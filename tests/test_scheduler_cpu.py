@@ -293,3 +293,17 @@ def test_lpm_admits_the_longest_cached_prefix_first():
     assert fcfs.next_batch().pieces[0].req.rid == 3                  # arrival order by default
     with pytest.raises(ValueError):
         sched_mod.Scheduler(policy="random")
+
+
+def test_prefix_cache_flush_keeps_pages_in_use():
+    s, pc, alloc = _pc_sched(num_blocks=64)
+    _run_one(s, sched_mod.Request(rid=0, prompt=list(range(48)), max_new=1))     # 3 cached, unreferenced
+    held = sched_mod.Request(rid=1, prompt=list(range(1000, 1040)), max_new=4)
+    s.add(held)
+    s.after_prefill(s.next_batch(), [1])                                       # 2 more cached, referenced
+    assert pc.evictable == 3
+    assert pc.flush() == 3 and pc.evictable == 0
+    assert len(pc.table) == 2 and all(v == 1 for v in pc.ref.values())         # the live request's pages stay
+    while s.has_work():
+        s.after_decode(s.next_batch(), [1])
+    assert alloc.free + pc.evictable == alloc.capacity

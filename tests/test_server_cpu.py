@@ -899,3 +899,22 @@ def test_overload_bound_refuses_with_503_and_recovers():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_admin_endpoints():
+    import requests
+
+    eng = FakeEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        assert requests.post(base + "/tokenize", json={"text": "hi"}, timeout=30).json() == {"tokens": [104, 105]}
+        assert requests.post(base + "/detokenize", json={"tokens": [104, 105]}, timeout=30).json() == {"text": "hi"}
+        assert requests.get(base + "/get_model_info", timeout=30).json()["model_path"] == "fake"
+        assert requests.get(base + "/get_server_info", timeout=30).json()["tp_size"] == 1
+        assert requests.post(base + "/flush_cache", timeout=30).json() == {"status": "ok"}
+        r = requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 2}, timeout=30)
+        assert r.status_code == 200                                             # still serving after the flush
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
