@@ -148,6 +148,49 @@ def build_router_app(router: Router):
     async def generate(body: dict, request: Request):
         return await forward("/generate", body, request)
 
+    @app.post("/flush_cache")
+    def flush_cache(request: Request):
+        """Every replica drops its unreferenced prefix pages."""
+        import requests
+
+        out = []
+        for i, b in enumerate(router.backends):
+            try:
+                r = requests.post(b + "/flush_cache", timeout=30, headers=_auth(request))
+                out.append({"url": b, "status_code": r.status_code})
+            except requests.ConnectionError as e:
+                out.append({"url": b, "error": str(e)})
+        ok = all(x.get("status_code") == 200 for x in out)
+        return JSONResponse({"status": "ok" if ok else "partial", "replicas": out}, status_code=200 if ok else 503)
+
+    def _any(method, path, request, body=None):
+        """A read-only call answered by the first replica that answers."""
+        import requests
+
+        for b in router.backends:
+            try:
+                r = requests.request(method, b + path, json=body, timeout=30, headers=_auth(request))
+                return JSONResponse(r.json(), status_code=r.status_code)
+            except requests.ConnectionError:
+                continue
+        raise HTTPException(503, "no replica reachable")
+
+    @app.get("/get_model_info")
+    def model_info(request: Request):
+        return _any("GET", "/get_model_info", request)
+
+    @app.get("/get_server_info")
+    def server_info(request: Request):
+        return _any("GET", "/get_server_info", request)
+
+    @app.post("/tokenize")
+    def tokenize(body: dict, request: Request):
+        return _any("POST", "/tokenize", request, body)
+
+    @app.post("/detokenize")
+    def detokenize(body: dict, request: Request):
+        return _any("POST", "/detokenize", request, body)
+
     @app.get("/v1/models")
     def models(request: Request):
         for i in range(len(router.backends)):

@@ -78,6 +78,9 @@ def test_router_over_two_replicas():
         g = requests.post(base + "/generate", json={"input_ids": [3], "sampling_params": {"max_new_tokens": 2}},
                           timeout=60).json()
         assert g["output_ids"] == expected([3], 2)
+        assert requests.post(base + "/flush_cache", timeout=30).json()["status"] == "ok"
+        assert requests.post(base + "/tokenize", json={"text": "a"}, timeout=30).json() == {"tokens": [97]}
+        assert requests.get(base + "/get_model_info", timeout=30).json()["model_path"] == "fake"
         # one replica goes down: requests fail over to the other
         _stop(reps[1])
         time.sleep(0.5)
