@@ -1,13 +1,21 @@
-"""Offline serving engine: chunked prefill + CUDA-graph decode, greedy.
+"""Offline serving engine: chunked prefill (optionally with decode tokens
+mixed in) and CUDA-graph decode.
 
 ``LLMEngine(cfg, tp=TPGroup|None, ...)`` owns one TP rank's weights, paged KV
-cache, scheduler and decode-graph runner. Every TP rank runs the same
-deterministic schedule, so all ranks take the same collective steps.
+cache (optionally shared prefixes), scheduler and graph runners. Every TP
+rank runs the same deterministic schedule, so all ranks take the same
+collective steps.
 
-Public API: ``generate(prompts, max_new_tokens)`` (token ids in, token ids
-out), ``add_request`` / ``step`` / ``run`` for streaming use, and
-``prefill_only`` for prompt-processing benchmarks (the reference's pp tok/s
-metric, tests/pp_bench.py: max_tokens=1).
+Public API:
+
+* ``generate(prompts, max_new_tokens, stop_ids, sampling)``: token ids in,
+  token ids out. With ``max_new_tokens=1`` it is the prefill measurement of
+  the reference's prompt-processing bench (tests/pp_bench.py).
+* ``generate_text(prompts, sampling_params)``: text in the shape of sglang's
+  offline engine.
+* ``add_request`` / ``step`` / ``run`` / ``abort`` for streaming use. Requests
+  can ask for sampling, logit adjustments, logprobs or prompt scoring.
+* ``from_pretrained(dir, ...)`` for Hugging Face checkpoints.
 """
 import os
 import time
@@ -133,9 +141,7 @@ class LLMEngine:
         only are read; see models/loader.py). ``int4_weights=True`` keeps an
         AWQ checkpoint's linears packed (int4 GEMV for decode batches, a
         per-layer bf16 expansion for prefill) instead of expanding them once."""
-        from ..models.loader import load_llama
-
-        from ..models.loader import stop_token_ids
+        from ..models.loader import load_llama, stop_token_ids
         from .tokenizer import HFTokenizer
 
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
