@@ -1,10 +1,13 @@
-"""Token sampling: greedy, temperature, top-k, top-p (nucleus), seeded.
+"""Token selection: greedy, temperature, top-k, top-p (nucleus), seeded; and
+the logit adjustments applied before it (presence / frequency / repetition
+penalties, logit bias, minimum tokens before a stop id).
 
-Greedy requests keep the fused path (vocab-parallel argmax, in the decode
-CUDA graphs). A batch with any sampled request instead produces full logits
-(the LM-head shards all-gathered across the TP ranks, so every rank holds
-the same values) and calls ``sample``; every rank draws with the same seeded
-generator, so all ranks pick the same token without another exchange.
+Plain greedy requests keep the fused path (vocab-parallel argmax, in the
+decode CUDA graphs). A batch with any request that samples, adjusts logits or
+asks for logprobs instead produces full logits (the LM-head shards
+all-gathered across the TP ranks, so every rank holds the same values),
+applies ``adjust_logits`` and calls ``sample``; every rank draws with the same
+seeded generator, so all ranks pick the same token without another exchange.
 """
 import dataclasses
 

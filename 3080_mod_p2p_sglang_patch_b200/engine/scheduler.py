@@ -2,10 +2,13 @@
 
 Policy (sglang's default): while any request still has prompt tokens to
 prefill, the next batch is a prefill chunk of up to ``chunk`` tokens, taken
-in arrival order (a long prompt spans several chunks; a chunk may hold the
+in admission order (a long prompt spans several chunks; a chunk may hold the
 tail of one prompt and the head of the next). Otherwise all running requests
-decode one token. New requests are admitted while the running set is below
-``max_batch`` and the KV cache has room.
+decode one token. With ``mixed`` a prefill batch also carries one decode
+token of every running request. New requests are admitted while the running
+set is below ``max_batch`` and the KV cache has room, in arrival order
+("fcfs") or longest cached prefix first ("lpm"). ``abort`` ends a request
+between steps.
 """
 import collections
 import dataclasses
