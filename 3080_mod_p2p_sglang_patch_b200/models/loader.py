@@ -1,5 +1,6 @@
-"""Hugging Face Llama checkpoints (``config.json`` + ``*.safetensors``) onto
-this engine's tensor-parallel shards.
+"""Hugging Face checkpoints of the Llama decoder family (Llama, Mistral,
+Qwen2, Qwen3: ``config.json`` + ``*.safetensors``) onto this engine's
+tensor-parallel shards.
 
 The reference serves real checkpoints through sglang's loader
 (docs/performance.md:3-5); this is the B200 build's equivalent for the
