@@ -134,6 +134,72 @@ def config_from_hf(d: dict, name: str = None) -> LlamaConfig:
     )
 
 
+def config_to_hf(cfg: LlamaConfig) -> dict:
+    """The Hugging Face ``config.json`` of a LlamaConfig (inverse of
+    ``config_from_hf``)."""
+    arch = "Qwen3ForCausalLM" if cfg.qk_norm else "Qwen2ForCausalLM" if cfg.qkv_bias else "LlamaForCausalLM"
+    d = {"architectures": [arch], "model_type": arch[:-len("ForCausalLM")].lower(), "hidden_size": cfg.hidden,
+         "num_hidden_layers": cfg.layers, "num_attention_heads": cfg.heads, "num_key_value_heads": cfg.kv_heads,
+         "head_dim": cfg.head_dim, "intermediate_size": cfg.ffn, "vocab_size": cfg.vocab,
+         "rope_theta": cfg.rope_theta, "rms_norm_eps": cfg.eps, "max_position_embeddings": cfg.max_pos,
+         "hidden_act": "silu", "tie_word_embeddings": False, "torch_dtype": "bfloat16"}
+    if cfg.rope_scaling:
+        d["rope_scaling"] = dict(cfg.rope_scaling)
+    return d
+
+
+def save_llama(model_dir: str, cfg: LlamaConfig, weights, shard_bytes: int = 4 << 30):
+    """Write TP-1 bf16 ``weights`` as a Hugging Face checkpoint: config.json
+    and safetensors files of at most ``shard_bytes`` each, fused qkv /
+    gate_up split back into their projections. ``load_llama`` reads it back
+    at any TP degree."""
+    from ..ops import Int4Weight
+
+    if weights.vocab_start != 0 or weights.embed.shape[0] != cfg.vocab:
+        raise ValueError("save_llama needs the whole (TP-1) model")
+    os.makedirs(model_dir, exist_ok=True)
+    D = cfg.head_dim
+    nq, nkv = cfg.heads * D, cfg.kv_heads * D
+    t = {"model.embed_tokens.weight": weights.embed, "model.norm.weight": weights.norm,
+         "lm_head.weight": weights.lm_head}
+    for i, L in enumerate(weights.layers):
+        if any(isinstance(v, Int4Weight) for v in L.values()):
+            raise ValueError("save_llama writes bf16 weights (int4 layers found)")
+        p = f"model.layers.{i}."
+        t[p + "input_layernorm.weight"] = L["ln1"]
+        t[p + "post_attention_layernorm.weight"] = L["ln2"]
+        q, k, v = L["qkv"][:nq], L["qkv"][nq:nq + nkv], L["qkv"][nq + nkv:]
+        t[p + "self_attn.q_proj.weight"], t[p + "self_attn.k_proj.weight"], t[p + "self_attn.v_proj.weight"] = q, k, v
+        t[p + "self_attn.o_proj.weight"] = L["o"]
+        F_ = cfg.ffn
+        t[p + "mlp.gate_proj.weight"], t[p + "mlp.up_proj.weight"] = L["gate_up"][:F_], L["gate_up"][F_:]
+        t[p + "mlp.down_proj.weight"] = L["down"]
+        if cfg.qk_norm:
+            t[p + "self_attn.q_norm.weight"], t[p + "self_attn.k_norm.weight"] = L["q_norm"], L["k_norm"]
+        if cfg.qkv_bias:
+            b = L["qkv_bias"]
+            t[p + "self_attn.q_proj.bias"], t[p + "self_attn.k_proj.bias"] = b[:nq], b[nq:nq + nkv]
+            t[p + "self_attn.v_proj.bias"] = b[nq + nkv:]
+    shards, cur, size = [], {}, 0
+    for name, ten in t.items():
+        nb = ten.numel() * ten.element_size()
+        if cur and size + nb > shard_bytes:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[name] = ten
+        size += nb
+    shards.append(cur)
+    index = {}
+    for j, sh in enumerate(shards):
+        fname = f"model-{j + 1:05d}-of-{len(shards):05d}.safetensors"
+        write_safetensors(os.path.join(model_dir, fname), sh, {"format": "pt"})
+        index.update({k: fname for k in sh})
+    with open(os.path.join(model_dir, "config.json"), "w") as f:
+        json.dump(config_to_hf(cfg), f, indent=2)
+    with open(os.path.join(model_dir, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {}, "weight_map": index}, f, indent=2)
+
+
 class _Checkpoint:
     def __init__(self, model_dir: str):
         files = sorted(glob.glob(os.path.join(model_dir, "*.safetensors")))

@@ -360,3 +360,24 @@ def test_quantize_random_weights_to_int4():
         assert isinstance(q, ops.Int4Weight) and q.shape == tuple(dense.shape)
         err = (loader.awq_dequant(q.qweight, q.qzeros, q.scales, q.group) - dense).abs().max().item()
         assert err <= dense.abs().max().item() / 15 + 1e-3            # within one quantization step
+
+
+def test_save_and_reload_round_trip(tmp_path):
+    """save_llama writes a Hugging Face checkpoint (split projections, sharded
+    files) that load_llama reads back exactly, at TP 1 and 2, for the Llama,
+    Qwen2 and Qwen3 variants."""
+    base = models.LlamaConfig.tiny()
+    for extra in ({}, {"qkv_bias": True}, {"qk_norm": True}):
+        cfg = models.LlamaConfig(**{**base.__dict__, **extra, "name": "rt"})
+        w = models.LlamaWeights(cfg, 0, 1, "cpu", seed=3, full_init=True)
+        d = tmp_path / ("m" + "".join(extra))
+        models.save_llama(str(d), cfg, w, shard_bytes=2 << 20)
+        assert len(list(d.glob("*.safetensors"))) > 1                        # sharded
+        cfg2, w1 = models.load_llama(str(d), 0, 1, "cpu")
+        assert (cfg2.qk_norm, cfg2.qkv_bias, cfg2.hidden, cfg2.vocab) == (cfg.qk_norm, cfg.qkv_bias, 512, 4096)
+        for L, L1 in zip(w.layers, w1.layers):
+            assert L.keys() == L1.keys() and all(torch.equal(L[k], L1[k]) for k in L)
+        assert torch.equal(w.embed, w1.embed) and torch.equal(w.lm_head, w1.lm_head)
+        w2 = models.LlamaWeights(cfg, 1, 2, "cpu", seed=3, full_init=True)   # rank 1 of TP=2, drawn directly
+        _, r1 = models.load_llama(str(d), 1, 2, "cpu")
+        assert all(torch.equal(a[k], b[k]) for a, b in zip(w2.layers, r1.layers) for k in a)
