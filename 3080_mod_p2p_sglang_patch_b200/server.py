@@ -911,6 +911,10 @@ def build_parser() -> argparse.ArgumentParser:
                     help="random weights and unseeded sampling draws")
     ap.add_argument("--log-level", default="info", choices=["debug", "info", "warning", "error"])
     ap.add_argument("--max-total-tokens", type=int, default=None, help="KV cache capacity in tokens")
+    ap.add_argument("--cuda-graph-bs", type=int, nargs="+", default=None,
+                    help="decode batch sizes captured as CUDA graphs (default 1 8 32 64)")
+    ap.add_argument("--cuda-graph-max-bs", type=int, default=None,
+                    help="largest decode batch captured as a CUDA graph")
     ap.add_argument("--disable-radix-cache", action="store_true",
                     help="no prefix sharing (the default unless --prefix-cache)")
     ap.add_argument("--chat-template", default=None,
@@ -1096,6 +1100,10 @@ def main(argv=None):
     if args.max_total_tokens:
         opts["kv_blocks"] = -(-args.max_total_tokens // 16) + 1  # pages of 16 tokens + the reserved page
     opts["seed"] = args.seed
+    sizes = tuple(args.cuda_graph_bs) if args.cuda_graph_bs else (1, 8, 32, 64)
+    if args.cuda_graph_max_bs:
+        sizes = tuple(sorted({x for x in sizes if x <= args.cuda_graph_max_bs} | {args.cuda_graph_max_bs}))
+    opts["graph_sizes"] = sizes
     tokenizer = None
     if model_path:
         eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, int4_weights=args.int4_weights,
