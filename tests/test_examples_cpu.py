@@ -26,3 +26,19 @@ def test_every_example_parses_and_has_a_usage_docstring():
         tree = ast.parse(open(os.path.join(EX, f)).read())
         doc = ast.get_docstring(tree)
         assert doc and ("python " in doc or "torchrun " in doc), f
+
+
+def test_run_all_plans_the_benchmarks_per_gpu_count():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("run_all", os.path.join(ROOT, "benchmarks", "run_all.py"))
+    ra = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ra)
+    one = dict(ra.main(["--gpus", "1", "--dry-run"]))
+    assert "bench" in one and "allreduce" not in one and "serve_70b" not in one      # multi-GPU ones skipped
+    assert one["bench"][1].endswith("bench.py") and "--gpus" in one["bench"]
+    eight = dict(ra.main(["--gpus", "8", "--only", "bench,allreduce,serve_70b", "--dry-run"]))
+    assert set(eight) == {"bench", "allreduce", "serve_70b"}
+    assert all("torch.distributed.run" in cmd and "--nproc-per-node=8" in cmd for cmd in eight.values())
+    for script, _, _ in ra.BENCHES.values():                                        # every script exists
+        assert os.path.isfile(os.path.join(ROOT, script)), script
