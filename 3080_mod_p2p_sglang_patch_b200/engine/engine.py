@@ -237,7 +237,9 @@ class LLMEngine:
     def _sync_block_row(self, req):
         row = torch.zeros(self.max_blocks_per_seq, dtype=torch.int32)
         row[: len(req.blocks)] = torch.tensor(req.blocks, dtype=torch.int32)
-        self.block_table[req.slot].copy_(row.to(self.device, non_blocking=True))
+        # pinned + asynchronous: a pageable copy could stall the host behind the
+        # running stream (the host prepares the next chunk meanwhile)
+        self.block_table[req.slot].copy_(self._h2d(row), non_blocking=True)
         req._row_synced = True
 
     # ------------------------------------------------------------------ execution
