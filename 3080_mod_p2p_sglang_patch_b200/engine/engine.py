@@ -239,7 +239,8 @@ class LLMEngine:
         row[: len(req.blocks)] = torch.tensor(req.blocks, dtype=torch.int32)
         # pinned + asynchronous: a pageable copy could stall the host behind the
         # running stream (the host prepares the next chunk meanwhile)
-        self.block_table[req.slot].copy_(self._h2d(row), non_blocking=True)
+        src = row.pin_memory() if self.device.type == "cuda" else row
+        self.block_table[req.slot].copy_(src, non_blocking=True)
         req._row_synced = True
 
     # ------------------------------------------------------------------ execution
