@@ -69,30 +69,50 @@ def adjust_logits(logits: torch.Tensor, params, prompts, outputs, stop_ids) -> t
     return x
 
 
+def sample_probs(logits: torch.Tensor, params) -> torch.Tensor:
+    """The sampling distribution of every row of ``logits`` [n, V] under its
+    SamplingParams (none greedy): temperature, then top-k, then top-p (the
+    smallest prefix of the sorted distribution whose mass reaches top_p,
+    always the top token), in one batched pass. fp32 [n, V]."""
+    x = logits.float()
+    n, V = x.shape
+    dev = x.device
+    x = x / torch.tensor([p.temperature for p in params], device=dev)[:, None]
+    ks = [p.top_k if 0 < p.top_k < V else 0 for p in params]
+    if any(ks):
+        kmax = max(ks)
+        top = torch.topk(x, kmax, dim=-1).values                          # [n, kmax], sorted
+        pick = torch.tensor([max(k, 1) - 1 for k in ks], device=dev)
+        kth = top.gather(1, pick[:, None])
+        kth = torch.where(torch.tensor(ks, device=dev)[:, None] > 0, kth, torch.full_like(kth, float("-inf")))
+        x = x.masked_fill(x < kth, float("-inf"))                         # ties with the k-th stay
+    tops = [p.top_p for p in params]
+    if any(t < 1.0 for t in tops):
+        sv, si = torch.sort(x, descending=True, dim=-1)
+        pr = torch.softmax(sv, dim=-1)
+        drop = torch.cumsum(pr, dim=-1) - pr >= torch.tensor(tops, device=dev)[:, None]
+        sv = sv.masked_fill(drop, float("-inf"))
+        x = torch.full_like(x, float("-inf")).scatter(1, si, sv)
+    return torch.softmax(x, dim=-1)
+
+
 def sample(logits: torch.Tensor, params, generators=None) -> torch.Tensor:
     """Next token per row of ``logits`` [B, V] (any float dtype) under
     ``params`` (one SamplingParams per row). ``generators``: one
-    torch.Generator (or None) per row for the draws. Returns int64 [B]."""
-    B = logits.shape[0]
-    out = torch.empty(B, dtype=torch.int64, device=logits.device)
-    x = logits.float()
-    for i, p in enumerate(params):
-        row = x[i]
-        if p.greedy:
-            out[i] = row.argmax()
-            continue
-        row = row / p.temperature
-        if p.top_k and p.top_k < row.numel():
-            kth = torch.topk(row, p.top_k).values[-1]
-            row = row.masked_fill(row < kth, float("-inf"))
-        if p.top_p < 1.0:
-            sorted_vals, idx = torch.sort(row, descending=True)
-            probs = torch.softmax(sorted_vals, dim=0)
-            # keep the smallest prefix whose mass reaches top_p (always the top token)
-            drop = torch.cumsum(probs, dim=0) - probs >= p.top_p
-            sorted_vals = sorted_vals.masked_fill(drop, float("-inf"))
-            row = torch.full_like(row, float("-inf")).scatter(0, idx, sorted_vals)
-        probs = torch.softmax(row, dim=0)
-        g = generators[i] if generators is not None else None
-        out[i] = torch.multinomial(probs, 1, generator=g)[0]
+    torch.Generator (or None) per row for the draws; rows that share a
+    generator draw in one batched call, in row order. Returns int64 [B]."""
+    out = logits.float().argmax(-1)                                        # greedy rows
+    idx = [i for i, p in enumerate(params) if not p.greedy]
+    if not idx:
+        return out
+    rows = torch.tensor(idx, device=logits.device)
+    probs = sample_probs(logits.index_select(0, rows), [params[i] for i in idx])
+    gens = [generators[i] if generators is not None else None for i in idx]
+    groups = {}
+    for j, g in enumerate(gens):                                           # by generator, first-use order
+        groups.setdefault(id(g), (g, []))[1].append(j)
+    for g, js in groups.values():
+        sel = torch.tensor(js, device=logits.device)
+        draws = torch.multinomial(probs.index_select(0, sel), 1, generator=g)[:, 0]
+        out[rows.index_select(0, sel)] = draws
     return out

@@ -59,3 +59,45 @@ def test_logit_adjustments():
     assert out[2, 4] == float("-inf") and out[2, :4].eq(0).all()            # the stop id waits for 3 tokens
     assert torch.equal(logits[0], torch.tensor([2.0, -1.0, 0.5, 3.0, 0.0]))  # the input is left as it was
     assert SP().adjusts is False and SP(min_new_tokens=1).adjusts and SP(temperature=0.5).adjusts is False
+
+
+def test_batched_distribution_matches_the_per_row_definition():
+    """sample_probs (one batched pass) equals temperature -> top-k -> top-p
+    applied row by row, for a mix of settings."""
+    samp = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine.sampling")
+    SP = samp.SamplingParams
+    g = torch.Generator().manual_seed(3)
+    logits = torch.randn(6, 50, generator=g) * 3
+    params = [SP(1.0), SP(0.7, top_k=5), SP(1.3, top_p=0.8), SP(0.5, top_k=10, top_p=0.5), SP(2.0, top_k=50),
+              SP(1.0, top_k=1000)]
+
+    def one(row, p):
+        row = row / p.temperature
+        if p.top_k and p.top_k < row.numel():
+            row = row.masked_fill(row < torch.topk(row, p.top_k).values[-1], float("-inf"))
+        if p.top_p < 1.0:
+            sv, si = torch.sort(row, descending=True)
+            pr = torch.softmax(sv, 0)
+            sv = sv.masked_fill(torch.cumsum(pr, 0) - pr >= p.top_p, float("-inf"))
+            row = torch.full_like(row, float("-inf")).scatter(0, si, sv)
+        return torch.softmax(row, 0)
+
+    got = samp.sample_probs(logits, params)
+    want = torch.stack([one(logits[i], p) for i, p in enumerate(params)])
+    assert torch.allclose(got, want, atol=1e-6)
+    assert int((got[1] > 0).sum()) == 5 and int((got[5] > 0).sum()) == 50
+
+
+def test_rows_sharing_a_generator_draw_together_and_reproduce():
+    samp = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine.sampling")
+    SP = samp.SamplingParams
+    logits = torch.randn(5, 30, generator=torch.Generator().manual_seed(4))
+    params = [SP(1.0), SP(), SP(1.0, top_k=3), SP(1.0), SP(0.9)]
+
+    def run():
+        shared, own = torch.Generator().manual_seed(10), torch.Generator().manual_seed(11)
+        return samp.sample(logits, params, [shared, None, shared, own, shared])
+
+    a, b = run(), run()
+    assert torch.equal(a, b) and a[1] == logits[1].argmax()               # greedy row untouched
+    assert a[2] in torch.topk(logits[2], 3).indices
