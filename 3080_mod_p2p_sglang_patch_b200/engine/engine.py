@@ -37,7 +37,7 @@ class LLMEngine:
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
                  sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None,
-                 mixed_chunk: bool = False, schedule_policy: str = "fcfs"):
+                 mixed_chunk: bool = False, schedule_policy: str = "fcfs", sample_in_graphs: bool = False):
         if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
             use_graphs, prefill_graph = False, False
         if max_seq > cfg.max_pos:
@@ -46,6 +46,10 @@ class LLMEngine:
         self.cfg = cfg
         self.tp = tp
         self.impl = impl
+        # decode batches that need the full logits (sampling, logprobs, logit
+        # adjustments) replay a CUDA graph ending in the logits instead of
+        # running eagerly
+        self.sample_in_graphs = sample_in_graphs
         # text API (generate_text): the checkpoint's tokenizer and stop ids when
         # loaded with from_pretrained, else bytes and none
         self.tokenizer = None
@@ -386,8 +390,12 @@ class LLMEngine:
                 self._sync_block_row(r)
         ids, pos, kv_len, slots, rows = self.decode_inputs(batch.reqs)
         sampled = any(r.needs_logits for r in batch.reqs)
-        if self.graphs is not None and self.graphs.can_run(len(ids)) and not sampled:
-            return self.graphs.run(ids, pos, kv_len, slots, rows)
+        if self.graphs is not None and self.graphs.can_run(len(ids)):
+            if not sampled:
+                return self.graphs.run(ids, pos, kv_len, slots, rows)
+            if self.sample_in_graphs:
+                logits = self.graphs.run_logits(ids, pos, kv_len, slots, rows)
+                return self._sample_from_logits(logits, batch.reqs)
         B = len(ids)
         d = self._h2d(torch.tensor(ids + pos + kv_len + rows, dtype=torch.int32))
         slots_d = self._h2d(torch.tensor(slots, dtype=torch.int64))

@@ -32,6 +32,10 @@ class DecodeGraphRunner:
         self.graphs = {}
         self.outputs = {}
         self.kernels = {}
+        # graphs that end in the full logits (sampled / logprob batches), per
+        # batch size, captured on first use
+        self.logit_graphs = {}
+        self.logit_outputs = {}
         self.pool = None
         self._captured = False
 
@@ -46,7 +50,10 @@ class DecodeGraphRunner:
         rows = self.in_i32[3 * n:3 * n + bs]
         return ids, pos, kvl, self.in_slots[:bs], rows
 
-    def capture(self):
+    def _capture_sizes(self, sizes, logits: bool):
+        """Capture one graph per batch size: the decode forward ending in the
+        next tokens (greedy), or with ``logits`` in the full fp32 logits.
+        Collective on the TP ranks (warm-ups and capture run collectives)."""
         e = self.e
         nkv = e.cfg.kv_heads // e.tp_size
         # padded rows: position 0, kv_len 1, slot in the reserved block 0, table row 0
@@ -54,14 +61,21 @@ class DecodeGraphRunner:
         self.in_i32[2 * self.max_bs:3 * self.max_bs].fill_(1)
         self.in_slots.zero_()
         torch.cuda.synchronize()
+
+        def fwd(ids, pos, kvl, slots, rows, splits):
+            if not logits:
+                return e.forward_decode_eager(ids, pos, kvl, slots, rows, splits=splits)
+            hidden = e.forward_decode_eager(ids, pos, kvl, slots, rows, splits=splits, return_hidden=True)
+            return e.model.full_logits(hidden)
+
         s = torch.cuda.Stream(device=e.device)
         s.wait_stream(torch.cuda.current_stream(e.device))
         with torch.cuda.stream(s):
-            for bs in reversed(self.sizes):
+            for bs in reversed(sizes):
                 ids, pos, kvl, slots, rows = self._views(bs)
                 splits = ops.decode_splits(bs, nkv, e.max_seq)
                 for _ in range(2):  # warm-up (tensor maps, lazy init)
-                    e.forward_decode_eager(ids, pos, kvl, slots, rows, splits=splits)
+                    fwd(ids, pos, kvl, slots, rows, splits)
                 torch.cuda.synchronize()
                 g = torch.cuda.CUDAGraph()
                 comm = e.tp.ca_comm if e.tp is not None else None
@@ -69,19 +83,40 @@ class DecodeGraphRunner:
                 before = launches.get()
                 with ctx:
                     with torch.cuda.graph(g, pool=self.pool, stream=s):
-                        out = e.forward_decode_eager(ids, pos, kvl, slots, rows, splits=splits)
-                self.kernels[bs] = launches.get() - before
+                        out = fwd(ids, pos, kvl, slots, rows, splits)
+                n_kernels = launches.get() - before
                 if self.pool is None:
                     self.pool = g.pool()
-                self.graphs[bs] = g
-                self.outputs[bs] = out
+                if logits:
+                    self.logit_graphs[bs], self.logit_outputs[bs] = g, out
+                    self.kernels[("logits", bs)] = n_kernels
+                else:
+                    self.graphs[bs], self.outputs[bs] = g, out
+                    self.kernels[bs] = n_kernels
         torch.cuda.current_stream(e.device).wait_stream(s)
         torch.cuda.synchronize()
+
+    def capture(self):
+        self._capture_sizes(self.sizes, logits=False)
         self._captured = True
 
     def run(self, ids, pos, kv_len, slots, rows):
         if not self._captured:
             self.capture()
+        return self._replay(ids, pos, kv_len, slots, rows, logits=False)
+
+    def run_logits(self, ids, pos, kv_len, slots, rows):
+        """Replay the graph that ends in the full fp32 logits [B, V] (every
+        TP rank gets the same values), capturing it for this batch size on
+        first use."""
+        if not self._captured:
+            self.capture()
+        bs = next(s for s in self.sizes if s >= len(ids))
+        if bs not in self.logit_graphs:
+            self._capture_sizes((bs,), logits=True)
+        return self._replay(ids, pos, kv_len, slots, rows, logits=True)
+
+    def _replay(self, ids, pos, kv_len, slots, rows, logits):
         B = len(ids)
         bs = next(s for s in self.sizes if s >= B)
         n = self.max_bs
@@ -99,6 +134,10 @@ class DecodeGraphRunner:
         if self._copied is None:
             self._copied = torch.cuda.Event()
         self._copied.record()
+        if logits:
+            self.logit_graphs[bs].replay()
+            launches.add(self.kernels.get(("logits", bs), 0))
+            return self.logit_outputs[bs][:B]
         self.graphs[bs].replay()
         launches.add(self.kernels.get(bs, 0))
         return self.outputs[bs][:B]
@@ -106,6 +145,8 @@ class DecodeGraphRunner:
     def close(self):
         self.graphs.clear()
         self.outputs.clear()
+        self.logit_graphs.clear()
+        self.logit_outputs.clear()
 
 
 class _null:

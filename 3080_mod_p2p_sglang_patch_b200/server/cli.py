@@ -68,6 +68,9 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--schedule-policy", default=None, choices=["fcfs", "lpm"],
                     help="admission order: arrival (fcfs) or longest cached prefix first (lpm; the default with "
                          "--prefix-cache)")
+    ap.add_argument("--graph-sampled-decode", action="store_true",
+                    help="decode batches that sample (or need logprobs / logit adjustments) replay a CUDA graph "
+                         "ending in the full logits instead of running eagerly")
     ap.add_argument("--enable-mixed-chunk", dest="mixed_chunk", action="store_true",
                     help="prefill batches also carry the running requests' decode tokens")
     ap.add_argument("--int4-weights", action="store_true",
@@ -229,7 +232,8 @@ def main(argv=None):
     opts = dict(max_batch=args.max_batch, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),
                 prefix_cache=args.prefix_cache, mem_fraction=args.mem_fraction, mixed_chunk=args.mixed_chunk,
-                schedule_policy=args.schedule_policy or ("lpm" if args.prefix_cache else "fcfs"))
+                schedule_policy=args.schedule_policy or ("lpm" if args.prefix_cache else "fcfs"),
+                sample_in_graphs=args.graph_sampled_decode)
     if args.max_seq is not None:
         opts["max_seq"] = args.max_seq
     if args.max_total_tokens:

@@ -192,3 +192,22 @@ def test_native_and_oracle_score_text_alike():
     res = ppl.main(["--model", "tiny", "--tokens", "1500", "--window", "500", "--chunk", "128", "--impl", "native",
                     "--device", "cuda", "--compare", "oracle"])
     assert res["mean_abs_logprob_diff"] < 0.05 and abs(res["ppl"] / res["ppl_compare"] - 1) < 0.05
+
+
+def test_sampled_decode_in_graphs_matches_eager():
+    """Decode batches that need the full logits replay a captured graph ending
+    in the logits (``sample_in_graphs``): the same kernels as the eager step,
+    so seeded draws and logprobs come out identical."""
+    SP = eng_mod.SamplingParams
+    g = torch.Generator().manual_seed(22)
+    p1, p2 = (torch.randint(0, CFG.vocab, (n,), generator=g).tolist() for n in (30, 45))
+    outs = []
+    for in_graphs in (False, True):
+        eng = _engine(graph_sizes=(1, 2), max_batch=2, sample_in_graphs=in_graphs)
+        a = eng.add_request(p1, 6, sampling=SP(temperature=0.8, top_k=30, seed=5))
+        b = eng.add_request(p2, 6, logprobs=2)
+        eng.run()
+        outs.append((a.output, b.output, [round(x, 4) for x, _ in b.token_logprobs]))
+        if in_graphs:
+            assert eng.graphs.logit_graphs                          # the logits graph was captured and used
+    assert outs[0] == outs[1]
