@@ -134,23 +134,31 @@ class Int4Weight:
                           torch.cat([p.scales for p in parts], 1).contiguous(), g.pop())
 
 
-AWQ_GEMV_MAX_ROWS = 8
+AWQ_GEMV_MAX_ROWS = 8     # rows per int4 GEMV launch
+AWQ_GEMV_ROW_LIMIT = 64   # up to here (decode batches) the GEMV runs over 8-row chunks
 
 
 def awq_gemm(a: torch.Tensor, w: Int4Weight, out: torch.Tensor = None, residual: torch.Tensor = None):
-    """out[M, N] = a @ W^T (+ residual) for an int4 weight: the int4 GEMV
-    (CUDA cores) up to 8 rows, else the layer dequantized to bf16 into a
-    reused scratch buffer and the tcgen05 GEMM."""
+    """out[M, N] = a @ W^T (+ residual) for an int4 weight.
+
+    Up to 64 rows (decode batches): the int4 GEMV over chunks of 8 rows, each
+    reading the packed weight once (a quarter of bf16's bytes per chunk).
+    Larger batches (prefill): the layer dequantized to bf16 into a reused
+    scratch buffer and the tcgen05 GEMM (the expansion costs about 2.25x the
+    bf16 weight bytes, which only a large batch amortises)."""
     C = cuda_ext()
     M = a.shape[0]
     N, K = w.shape
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     ws = workspace(a.device)
-    if M <= AWQ_GEMV_MAX_ROWS and w.group <= 256:
-        part, _ = ws.awq(n_ws=(K // w.group) * M * N)
-        C.awq_gemv(a, w.qweight, w.qzeros, w.scales, w.group, part, out, residual)
-        launches.add(2)
+    if M <= AWQ_GEMV_ROW_LIMIT and w.group <= 256:
+        part, _ = ws.awq(n_ws=(K // w.group) * min(M, AWQ_GEMV_MAX_ROWS) * N)
+        for r0 in range(0, M, AWQ_GEMV_MAX_ROWS):
+            r1 = min(M, r0 + AWQ_GEMV_MAX_ROWS)
+            C.awq_gemv(a[r0:r1], w.qweight, w.qzeros, w.scales, w.group, part, out[r0:r1],
+                       None if residual is None else residual[r0:r1])
+            launches.add(2)
         return out
     _, wbuf = ws.awq(n_w=N * K)
     dense = wbuf[:N * K].view(N, K)
