@@ -139,9 +139,9 @@ def test_native_prompt_logprobs_match_the_dense_distribution():
 
 
 def test_native_engine_with_int4_weights():
-    """AWQ int4 weights kept packed: decode batches of up to 8 rows go through
-    the int4 GEMV (also inside the decode CUDA graph), larger batches and
-    prefill through the per-layer dequant + tcgen05 GEMM."""
+    """AWQ int4 weights kept packed: decode batches go through the int4 GEMV
+    (in 8-row chunks, also inside the decode CUDA graphs), prefill chunks of
+    more than 64 tokens through the per-layer dequant + tcgen05 GEMM."""
     from test_engine_cpu import _int4_weights
 
     ops = __import__("importlib").import_module(f"{PKG}.ops")
@@ -151,14 +151,14 @@ def test_native_engine_with_int4_weights():
             L[k] = ops.Int4Weight(v.qweight.cuda(), v.qzeros.cuda(), v.scales.cuda(), v.group) \
                 if isinstance(v, ops.Int4Weight) else v.cuda()
     w.embed, w.norm, w.lm_head = w.embed.cuda(), w.norm.cuda(), w.lm_head.cuda()
-    eng = eng_mod.LLMEngine(CFG, device="cuda", weights=w, max_batch=16, max_seq=512, chunk=64,
+    eng = eng_mod.LLMEngine(CFG, device="cuda", weights=w, max_batch=16, max_seq=512, chunk=128,
                             graph_sizes=(1, 16))
     g = torch.Generator().manual_seed(19)
     one = torch.randint(0, CFG.vocab, (70,), generator=g).tolist()
     out1 = eng.generate([one], max_new_tokens=5)[0]                     # bs 1: graph with the GEMV
     _near_argmax(CFG, dense, one, out1)
     many = [torch.randint(0, CFG.vocab, (20 + i,), generator=g).tolist() for i in range(10)]
-    outs = eng.generate(many, max_new_tokens=3)                          # bs 10: dequant + GEMM
+    outs = eng.generate(many, max_new_tokens=3)                          # prefill: dequant; bs 16 graph: 2 GEMV chunks
     for p, o in zip(many, outs):
         _near_argmax(CFG, dense, p, o)
 
