@@ -152,7 +152,7 @@ def awq_gemm(a: torch.Tensor, w: Int4Weight, out: torch.Tensor = None, residual:
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     ws = workspace(a.device)
-    if M <= AWQ_GEMV_ROW_LIMIT and w.group <= 256:
+    if M <= AWQ_GEMV_ROW_LIMIT and w.group <= 256 and w.group % 8 == 0:
         part, _ = ws.awq(n_ws=(K // w.group) * min(M, AWQ_GEMV_MAX_ROWS) * N)
         for r0 in range(0, M, AWQ_GEMV_MAX_ROWS):
             r1 = min(M, r0 + AWQ_GEMV_MAX_ROWS)

@@ -67,26 +67,38 @@ __global__ void __launch_bounds__(kGemvThreads) awq_gemv_kernel(
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[m][j] = 0.f;
   const uint32_t* wp = qw + k0 * Nq + c;
-#pragma unroll 4
-  for (int k = 0; k < G; ++k) {
-    float q[8];
-    unpack8(__ldg(wp + (int64_t)k * Nq), q);
+  // 8 rows of k per step, their loads issued before any is used: 8 loads in
+  // flight per thread (G is a multiple of 8)
+#pragma unroll 1
+  for (int k = 0; k < G; k += 8) {
+    uint32_t wv[8];
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const float xv = xs[m * G + k];
+    for (int u = 0; u < 8; ++u) wv[u] = __ldg(wp + (int64_t)(k + u) * Nq);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[m][j] = fmaf(xv, q[j], acc[m][j]);
+    for (int u = 0; u < 8; ++u) {
+      float q[8];
+      unpack8(wv[u], q);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const float xv = xs[m * G + k + u];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[m][j] = fmaf(xv, q[j], acc[m][j]);
+      }
     }
   }
   float z[8];
   unpack8(__ldg(qz + (int64_t)g * Nq + c), z);
   const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sc + (int64_t)g * N + 8 * c));
-  const __half* sh = reinterpret_cast<const __half*>(&sv);
+  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+  float sf[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)  // halves j = 2i (low) and 2i + 1 (high) of word i
+    sf[j] = __half2float(__ushort_as_half((unsigned short)(sw[j / 2] >> (16 * (j % 2)))));
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     float o[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = __half2float(sh[j]) * (acc[m][j] - z[j] * sumx[m]);
+    for (int j = 0; j < 8; ++j) o[j] = sf[j] * (acc[m][j] - z[j] * sumx[m]);
     float4* dst = reinterpret_cast<float4*>(ws + ((int64_t)g * M + m) * N + 8 * c);
     dst[0] = make_float4(o[0], o[1], o[2], o[3]);
     dst[1] = make_float4(o[4], o[5], o[6], o[7]);
@@ -154,7 +166,8 @@ void gemv_launch(const AwqGemvArgs& a, cudaStream_t s) {
 
 void awq_gemv_launch(const AwqGemvArgs& a, cudaStream_t s) {
   if (a.M < 1 || a.M > kAwqGemvMaxRows) throw std::runtime_error("awq_gemv: 1..8 rows");
-  if (a.N % 8 || a.G <= 0 || a.G > 256 || a.K % a.G) throw std::runtime_error("awq_gemv: unsupported shape");
+  if (a.N % 8 || a.G <= 0 || a.G > 256 || a.G % 8 || a.K % a.G)
+    throw std::runtime_error("awq_gemv: unsupported shape");
   switch (a.M) {
     case 1: gemv_launch<1>(a, s); break;
     case 2: gemv_launch<2>(a, s); break;
