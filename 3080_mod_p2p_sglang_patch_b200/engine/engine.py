@@ -144,19 +144,23 @@ class LLMEngine:
         """Engine over a Hugging Face checkpoint directory (this rank's shards
         only are read; see models/loader.py). ``int4_weights=True`` keeps an
         AWQ checkpoint's linears packed (int4 GEMV for decode batches, a
-        per-layer bf16 expansion for prefill) instead of expanding them once."""
+        per-layer bf16 expansion for prefill) instead of expanding them once.
+        ``tokenizer_path``: load the tokenizer from another directory."""
         from ..models.loader import load_llama, stop_token_ids
         from .tokenizer import HFTokenizer
 
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         int4 = bool(kw.pop("int4_weights", False))
+        tok_dir = kw.pop("tokenizer_path", None) or model_dir
         cfg, w = load_llama(model_dir, tp.rank if tp is not None else 0, tp.world_size if tp is not None else 1, dev,
                             int4=int4)
         kw.setdefault("max_seq", min(cfg.max_pos, 8192))
         eng = cls(cfg, tp=tp, device=dev, weights=w, **kw)
         try:
-            eng.tokenizer = HFTokenizer(model_dir)
+            eng.tokenizer = HFTokenizer(tok_dir)
         except Exception:  # noqa: BLE001 - token-id APIs still work without one
+            if tok_dir != model_dir:  # asked for explicitly: not silently dropped
+                raise
             eng.tokenizer = None
         eng.default_stop_ids = stop_token_ids(model_dir)
         return eng

@@ -48,9 +48,17 @@ class ByteTokenizer:
 class HFTokenizer:
     """A checkpoint directory's tokenizer (transformers, local files only)."""
 
+    # one of these must be present: given only config.json, transformers 5
+    # builds an empty tokenizer that maps all text to <unk>
+    FILES = ("tokenizer.json", "tokenizer.model", "vocab.json", "tokenizer_config.json")
+
     def __init__(self, path: str, chat_template: str = None):
+        import os
+
         from transformers import AutoTokenizer
 
+        if os.path.isdir(path) and not any(os.path.isfile(os.path.join(path, f)) for f in self.FILES):
+            raise FileNotFoundError(f"no tokenizer files in {path} (looked for {', '.join(self.FILES)})")
         self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
         if chat_template:  # replaces the checkpoint's own template
             self.tok.chat_template = chat_template
@@ -63,5 +71,8 @@ class HFTokenizer:
 
     def chat(self, messages) -> list:
         if getattr(self.tok, "chat_template", None):
-            return list(self.tok.apply_chat_template(messages, add_generation_prompt=True, tokenize=True))
+            r = self.tok.apply_chat_template(messages, add_generation_prompt=True, tokenize=True)
+            if hasattr(r, "keys"):  # transformers 5 returns a BatchEncoding, 4 a list of ids
+                r = r["input_ids"]
+            return [int(t) for t in r]
         return self.encode("".join(f"{m.get('role', 'user')}: {m.get('content', '')}\n" for m in messages))

@@ -163,6 +163,34 @@ def build_router_app(router: Router):
         ok = all(x.get("status_code") == 200 for x in out)
         return JSONResponse({"status": "ok" if ok else "partial", "replicas": out}, status_code=200 if ok else 503)
 
+    @app.post("/abort_request")
+    def abort_request(body: dict, request: Request):
+        """Sent to every replica: only the one running the request knows its id."""
+        import requests
+
+        aborted = False
+        for b in router.backends:
+            try:
+                r = requests.post(b + "/abort_request", json=body, timeout=30, headers=_auth(request))
+                if r.status_code == 400:
+                    return JSONResponse(r.json(), status_code=400)
+                aborted = aborted or bool(r.status_code == 200 and r.json().get("aborted"))
+            except requests.ConnectionError:
+                continue
+        return {"rid": body.get("rid"), "aborted": aborted}
+
+    @app.get("/health_generate")
+    def health_generate():
+        """One generated token on every replica."""
+        reps = []
+        for i, b in enumerate(router.backends):
+            try:
+                reps.append({"url": b, **router.get(i, "/health_generate").json()})
+            except Exception as e:  # noqa: BLE001
+                reps.append({"url": b, "status": "down", "error": str(e)})
+        ok = all(r.get("status") == "ok" for r in reps)
+        return JSONResponse({"status": "ok" if ok else "degraded", "replicas": reps}, status_code=200 if ok else 503)
+
     def _any(method, path, request, body=None):
         """A read-only call answered by the first replica that answers."""
         import requests

@@ -8,7 +8,7 @@ import signal
 import subprocess
 import sys
 
-from ..engine.tokenizer import ByteTokenizer, load_chat_template
+from ..engine.tokenizer import ByteTokenizer, HFTokenizer, load_chat_template
 from .http import build_app, start_http
 from .loop import EngineServer
 
@@ -51,6 +51,9 @@ def build_parser() -> argparse.ArgumentParser:
                     help="largest decode batch captured as a CUDA graph")
     ap.add_argument("--disable-radix-cache", action="store_true",
                     help="no prefix sharing (the default unless --prefix-cache)")
+    ap.add_argument("--tokenizer-path", default=None,
+                    help="tokenizer directory (default: the checkpoint's own; with random weights, "
+                         "replaces the byte tokenizer)")
     ap.add_argument("--chat-template", default=None,
                     help="Jinja chat template (a file, or the template text) instead of the checkpoint's own")
     ap.add_argument("--max-batch", "--max-running-requests", dest="max_batch", type=int, default=64)
@@ -246,7 +249,7 @@ def main(argv=None):
     tokenizer = None
     if model_path:
         eng = eng_mod.LLMEngine.from_pretrained(model_path, tp=tp, device=dev, int4_weights=args.int4_weights,
-                                                **opts)
+                                                tokenizer_path=args.tokenizer_path, **opts)
         cfg = eng.cfg
         tokenizer = eng.tokenizer
         if tokenizer is None:  # token-id prompts still work
@@ -257,6 +260,9 @@ def main(argv=None):
         cfg = models.LlamaConfig.by_name(name)
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
         eng = eng_mod.LLMEngine(cfg, tp=tp, device=dev, **opts)
+        if args.tokenizer_path:
+            tokenizer = eng.tokenizer = HFTokenizer(args.tokenizer_path, load_chat_template(args.chat_template)
+                                                    if args.chat_template else None)
     stop = eng.default_stop_ids
     server = EngineServer(eng, ctrl, rank, world, max_prompt=eng.max_seq, stop_ids=stop,
                           log_requests=args.log_requests, max_queued=args.max_queued_requests)

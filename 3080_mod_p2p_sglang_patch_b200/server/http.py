@@ -13,8 +13,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
     """FastAPI app with /health, /metrics, /v1/models, /v1/completions,
     /v1/chat/completions and /generate (plain or streamed; greedy or
     sampled; stop token ids and stop strings). ``api_key``: requests to the
-    model endpoints need ``Authorization: Bearer <api_key>`` (/health and
-    /metrics stay open for probes)."""
+    model endpoints need ``Authorization: Bearer <api_key>`` (/health,
+    /health_generate and /metrics stay open for probes)."""
     import hmac
 
     from fastapi import FastAPI, HTTPException, Request
@@ -28,7 +28,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
     if api_key:
         @app.middleware("http")
         async def _auth(request: Request, call_next):
-            if request.url.path not in ("/health", "/metrics"):
+            if request.url.path not in ("/health", "/health_generate", "/metrics"):
                 got = request.headers.get("authorization", "")
                 if not hmac.compare_digest(got.encode(), f"Bearer {api_key}".encode()):
                     return JSONResponse({"error": {"message": "invalid or missing API key"}}, status_code=401)
@@ -82,11 +82,13 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         return (max(t, 0.0), int(body.get("top_k") or 0), float(body.get("top_p") or 1.0),
                 None if seed is None else int(seed)) + adj
 
-    def _run(prompt, max_tokens, stop=None, sampling=None, stops=(), logprobs=None, prompt_logprobs=False):
+    def _run(prompt, max_tokens, stop=None, sampling=None, stops=(), logprobs=None, prompt_logprobs=False,
+             name=None, timeout=None):
         """(output ids, finish reason, per-token logprobs, prompt logprobs)."""
         try:
-            p = server._submit_pending(prompt, max_tokens, stop_ids=stop, sampling=sampling, stop_strs=stops,
-                                       detok=tok.decode, logprobs=logprobs, prompt_logprobs=prompt_logprobs)
+            p = server._submit_pending(prompt, max_tokens, timeout=timeout, stop_ids=stop, sampling=sampling,
+                                       stop_strs=stops, detok=tok.decode, logprobs=logprobs,
+                                       prompt_logprobs=prompt_logprobs, name=name)
             return p.output, p.reason, p.token_logprobs, p.prompt_token_logprobs
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
@@ -231,6 +233,27 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                 "prefix_cache": getattr(eng, "prefix_cache", None) is not None,
                 "max_queued_requests": server.max_queued, **server.stats}
 
+    @app.post("/abort_request")
+    def abort_request(body: dict):
+        """sglang's abort by client request id (the ``rid`` given to
+        /generate): the request ends at the next step on every rank and its
+        caller gets the tokens so far, with finish reason "abort"."""
+        rid = body.get("rid")
+        if rid is None:
+            raise HTTPException(400, "rid is required")
+        return {"rid": rid, "aborted": server.abort_request(rid)}
+
+    @app.get("/health_generate")
+    async def health_generate():
+        """Health by generating one token from a one-token prompt through
+        the whole loop (every rank steps); 503 if that fails or takes more
+        than 30 s."""
+        try:
+            await run_in_threadpool(server._submit_pending, [0], 1, 30.0)
+        except (ValueError, RuntimeError, TimeoutError) as e:
+            return JSONResponse({"status": "unhealthy", "error": str(e)}, status_code=503)
+        return {"status": "ok"}
+
     @app.post("/tokenize")
     def tokenize(body: dict):
         return {"tokens": tok.encode(str(body.get("text", "")))}
@@ -341,6 +364,9 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         top_n = int(body.get("top_logprobs_num") or 0)
         start = body.get("logprob_start_len")
         score_prompt = want_lp and start is not None and int(start) >= 0
+        rid = body.get("rid")
+        if rid is not None and not isinstance(rid, (str, int)):
+            raise HTTPException(400, "rid must be a string (one request per call)")
 
         def _lp_list(toks, lps):
             """sglang's [logprob, token id, None] triples (and top-n lists)."""
@@ -359,6 +385,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                     meta["input_token_logprobs"], itops = _lp_list(prompt[k:], list(plps)[k:])
                     if top_n:
                         meta["input_top_logprobs"] = itops
+            if rid is not None:
+                meta["id"] = rid
             return {"text": _text(out, stops), "output_ids": out, "meta_info": meta}
 
         if body.get("stream"):
@@ -368,7 +396,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                 out, reason = [], []
                 try:
                     stream = server.submit_stream(prompt, max_new, stop_ids=stop, reason_out=reason,
-                                                  sampling=sampling, stop_strs=stops, detok=tok.decode)
+                                                  sampling=sampling, stop_strs=stops, detok=tok.decode, name=rid)
                     fin = None
                     try:
                         for toks in stream:
@@ -383,13 +411,13 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                     if fin == "stop" and stops:
                         out = out[:_stop_prefix(out, stops, tok.decode) or len(out)]
                     yield "data: " + json.dumps(result(out, fin)) + "\n\n"
-                except (RuntimeError, TimeoutError) as e:
+                except (ValueError, RuntimeError, TimeoutError) as e:
                     yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(iterate_in_threadpool(gen()), media_type="text/event-stream")
         out, fin, lps, plps = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops,
-                                                      top_n if want_lp else None, score_prompt)
+                                                      top_n if want_lp else None, score_prompt, rid)
         return result(out, fin, lps, plps)
 
     return app

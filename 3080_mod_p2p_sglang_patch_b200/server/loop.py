@@ -87,6 +87,7 @@ class EngineServer:
         self.max_prompt = max_prompt
         self.q = queue.Queue()
         self._by_rid = {}
+        self._named = {}                 # rank 0: client request id (sglang's ``rid``) -> live request
         self._sids = itertools.count()   # rank 0 numbers requests; the id travels with them
         self._rid_of_sid = {}            # live requests, every rank
         self.stats = {"requests": 0, "prompt_tokens": 0, "completion_tokens": 0, "steps": 0,
@@ -133,11 +134,12 @@ class EngineServer:
         return (p.output, p.reason) if with_reason else p.output
 
     def _submit_pending(self, prompt, max_new, timeout=None, stop_ids=None, sampling=None, stop_strs=(), detok=None,
-                        logprobs=None, prompt_logprobs=False):
+                        logprobs=None, prompt_logprobs=False, name=None):
         """``submit`` returning the finished request record (output, reason,
-        token_logprobs, prompt_token_logprobs)."""
+        token_logprobs, prompt_token_logprobs). ``name``: a client request id
+        that ``abort_request`` can end the request by."""
         p = self._enqueue(prompt, max_new, stream=False, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
-                          detok=detok, logprobs=logprobs, prompt_logprobs=prompt_logprobs)
+                          detok=detok, logprobs=logprobs, prompt_logprobs=prompt_logprobs, name=name)
         if not p.event.wait(timeout):
             raise TimeoutError("request timed out")
         if isinstance(p.error, ValueError):  # the engine rejected the request itself
@@ -147,13 +149,13 @@ class EngineServer:
         return p
 
     def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None,
-                      sampling=None, stop_strs=(), detok=None):
+                      sampling=None, stop_strs=(), detok=None, name=None):
         """Like ``submit`` but yields lists of new token ids as the engine
         produces them (rank 0, from an HTTP thread); the finish reason is
         appended to ``reason_out`` (a list) at the end. Closing the generator
         early (a client that went away) aborts the request."""
         p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
-                          detok=detok)
+                          detok=detok, name=name)
         try:
             while True:
                 try:
@@ -190,6 +192,16 @@ class EngineServer:
             p.abort_sent = True
             self.q.put((self.ABORT, p.sid))
 
+    def abort_request(self, name) -> bool:
+        """End the live request submitted with client id ``name`` (rank 0, any
+        thread); False when no such request is in flight."""
+        with self._live_lock:
+            p = self._named.get(name)
+        if p is None:
+            return False
+        self.abort(p)
+        return True
+
     def _enqueue_check(self, prompt, max_new):
         if not prompt:
             raise ValueError("empty prompt")
@@ -207,14 +219,10 @@ class EngineServer:
                              f"max sequence {limit}")
 
     def _enqueue(self, prompt, max_new, stream, stop_ids=None, sampling=None, stop_strs=(), detok=None, logprobs=None,
-                 prompt_logprobs=False):
+                 prompt_logprobs=False, name=None):
         if self._stopped.is_set():
             raise RuntimeError("server stopped")
         self._enqueue_check(prompt, max_new)
-        with self._live_lock:
-            if self.max_queued is not None and self._live >= self.max_queued:
-                raise Overloaded(f"{self._live} requests in flight (limit {self.max_queued})")
-            self._live += 1
         stop_strs = tuple(x for x in stop_strs if x)
         if stop_strs and detok is None:
             raise ValueError("stop strings need a detokenizer")
@@ -222,9 +230,22 @@ class EngineServer:
                      stop_ids=self.stop_ids if stop_ids is None else stop_ids, sampling=sampling,
                      sid=next(self._sids), stop_strs=stop_strs, detok=detok, logprobs=logprobs,
                      prompt_logprobs=prompt_logprobs)
-        p.on_finish = self._release_live
+        with self._live_lock:
+            if self.max_queued is not None and self._live >= self.max_queued:
+                raise Overloaded(f"{self._live} requests in flight (limit {self.max_queued})")
+            if name is not None and name in self._named:
+                raise ValueError(f"request id {name!r} is already in flight")
+            self._live += 1
+            if name is not None:
+                self._named[name] = p
+        p.on_finish = self._release_live if name is None else (lambda: self._release_named(name))
         self.q.put(p)
         return p
+
+    def _release_named(self, name):
+        with self._live_lock:
+            self._live -= 1
+            self._named.pop(name, None)
 
     def stop(self):
         """Ask every rank's loop to exit after the current step (rank 0)."""

@@ -1,7 +1,8 @@
 // AWQ int4 weights kept packed on the device (W4A16), for sm_100a:
-//   awq_gemv     decode-sized batches (M <= 8 rows) on the CUDA cores. At that
-//                size a layer is weight-bandwidth-bound, and int4 moves a
-//                quarter of bf16's bytes.
+//   awq_gemv     decode-sized batches on the CUDA cores, up to 8 rows per
+//                launch (the Python dispatcher runs batches of up to 64 rows
+//                as 8-row chunks). At that size a layer is weight-bandwidth-
+//                bound, and int4 moves a quarter of bf16's bytes.
 //   awq_dequant  expands a layer to bf16 [N, K] for the tcgen05 GEMM of
 //                prefill-sized batches.
 // Layout (AutoAWQ "gemm" packing, the one Hugging Face AWQ checkpoints hold):

@@ -81,6 +81,8 @@ def test_router_over_two_replicas():
         assert requests.post(base + "/flush_cache", timeout=30).json()["status"] == "ok"
         assert requests.post(base + "/tokenize", json={"text": "a"}, timeout=30).json() == {"tokens": [97]}
         assert requests.get(base + "/get_model_info", timeout=30).json()["model_path"] == "fake"
+        assert requests.get(base + "/health_generate", timeout=60).json()["status"] == "ok"
+        assert requests.post(base + "/abort_request", json={"rid": "none"}, timeout=30).json()["aborted"] is False
         # one replica goes down: requests fail over to the other
         _stop(reps[1])
         time.sleep(0.5)

@@ -920,3 +920,43 @@ def test_admin_endpoints():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_abort_by_request_id_and_health_generate():
+    """sglang's ``rid`` on /generate and /abort_request: the named request ends
+    early with finish reason "abort"; a second request with a live id is
+    refused; unknown ids report aborted=False; /health_generate steps the loop."""
+    import time as _t
+
+    import requests
+
+    eng = _SlowEngine()
+    server, loop, http, base = _serve(eng)
+    try:
+        assert requests.get(base + "/health_generate", timeout=60).json() == {"status": "ok"}
+        res = []
+        th = threading.Thread(target=lambda: res.append(requests.post(
+            base + "/generate", json={"input_ids": [1, 2], "rid": "job-7",
+                                      "sampling_params": {"max_new_tokens": 1000}}, timeout=60).json()))
+        th.start()
+        deadline = _t.time() + 10
+        while "job-7" not in server._named and _t.time() < deadline:
+            _t.sleep(0.01)
+        dup = requests.post(base + "/generate", json={"input_ids": [1], "rid": "job-7",
+                                                      "sampling_params": {"max_new_tokens": 2}}, timeout=60)
+        assert dup.status_code == 400                                   # the id is in flight
+        assert requests.post(base + "/abort_request", json={"rid": "nope"}, timeout=30).json()["aborted"] is False
+        assert requests.post(base + "/abort_request", json={"rid": "job-7"}, timeout=30).json()["aborted"] is True
+        th.join(timeout=30)
+        meta = res[0]["meta_info"]
+        assert meta["finish_reason"]["type"] == "abort" and meta["id"] == "job-7"
+        assert meta["completion_tokens"] < 1000
+        assert "job-7" not in server._named and server._live == 0
+        ok = requests.post(base + "/generate", json={"input_ids": [1], "rid": "job-7",
+                                                     "sampling_params": {"max_new_tokens": 2}}, timeout=60)
+        assert ok.status_code == 200                                    # the id is free again
+        assert requests.post(base + "/abort_request", json={}, timeout=30).status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
