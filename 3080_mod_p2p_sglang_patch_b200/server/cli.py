@@ -51,6 +51,11 @@ def build_parser() -> argparse.ArgumentParser:
                     help="largest decode batch captured as a CUDA graph")
     ap.add_argument("--disable-radix-cache", action="store_true",
                     help="no prefix sharing (the default unless --prefix-cache)")
+    ap.add_argument("--disable-custom-all-reduce", action="store_true",
+                    help="TP allreduces on NCCL even with SGLANG_MAILBOX_AR=1 (sglang's switch for its custom "
+                         "allreduce, the slot MailboxAR fills)")
+    ap.add_argument("--trust-remote-code", action="store_true",
+                    help="accepted for sglang command lines; no checkpoint code is ever run")
     ap.add_argument("--tokenizer-path", default=None,
                     help="tokenizer directory (default: the checkpoint's own; with random weights, "
                          "replaces the byte tokenizer)")
@@ -230,7 +235,8 @@ def main(argv=None):
     dev = torch.device("cpu") if on_cpu else torch.device("cuda", local)
     # None: follow SGLANG_MAILBOX_AR, like the reference's launch flow (the
     # oracle takes plain torch.distributed collectives)
-    tp = par.TPGroup(None, dev, use_mailbox=False if args.impl == "oracle" else None) if world > 1 else None
+    no_custom = args.impl == "oracle" or args.disable_custom_all_reduce
+    tp = par.TPGroup(None, dev, use_mailbox=False if no_custom else None) if world > 1 else None
     ctrl = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7)) if world > 1 else None
     opts = dict(max_batch=args.max_batch, chunk=args.chunk, use_graphs=not args.no_graphs,
                 impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graphs),

@@ -865,6 +865,9 @@ def test_more_sglang_launch_flags_parse():
         p.parse_args(["--kv-cache-dtype", "fp8_e5m2"])      # not supported: refused, not ignored
     g = p.parse_args(["--cuda-graph-bs", "1", "4", "16", "--cuda-graph-max-bs", "12"])
     assert g.cuda_graph_bs == [1, 4, 16] and g.cuda_graph_max_bs == 12
+    c = p.parse_args(["--disable-custom-all-reduce", "--trust-remote-code"])
+    assert c.disable_custom_all_reduce and c.trust_remote_code
+    assert not p.parse_args([]).disable_custom_all_reduce
 
 
 def test_overload_bound_refuses_with_503_and_recovers():
