@@ -23,6 +23,8 @@ def cuda_ext():
     """Return the CUDA extension module, raising if it was not built."""
     global _C
     if _C is None:
+        import torch  # noqa: F401 - loads libc10 / libtorch, which the extension links against
+
         try:
             _C = importlib.import_module(f"{_pkg()}._C")
         except ImportError as e:  # pragma: no cover - depends on the build
@@ -37,6 +39,8 @@ def cpu_ext():
     """Return the host-runtime extension module, raising if it was not built."""
     global _cpu
     if _cpu is None:
+        import torch  # noqa: F401 - as above
+
         try:
             _cpu = importlib.import_module(f"{_pkg()}._cpu")
         except ImportError as e:  # pragma: no cover
