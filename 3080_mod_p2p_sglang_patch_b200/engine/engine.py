@@ -463,8 +463,9 @@ class LLMEngine:
         (default: the checkpoint's EOS ids), ``presence_penalty``,
         ``frequency_penalty``, ``repetition_penalty``, ``logit_bias`` ({id:
         bias}) and ``min_new_tokens``. Returns one ``{"text",
-        "token_ids", "finish_reason"}`` per prompt (a single dict for a single
-        string). ``return_logprob`` adds ``"logprobs"``: per generated token
+        "token_ids", "finish_reason", "meta_info"}`` per prompt (a single dict
+        for a single string); ``meta_info`` is sglang's (prompt and
+        completion token counts, ``finish_reason: {"type": ...}``). ``return_logprob`` adds ``"logprobs"``: per generated token
         (id, logprob, [(id, logprob)] of the ``top_logprobs_num`` most likely)."""
         from .tokenizer import ByteTokenizer
 
@@ -492,7 +493,9 @@ class LLMEngine:
         self.run()
         out = []
         for r in reqs:
-            o = {"text": tok.decode(r.output), "token_ids": list(r.output), "finish_reason": r.finish_reason}
+            o = {"text": tok.decode(r.output), "token_ids": list(r.output), "finish_reason": r.finish_reason,
+                 "meta_info": {"prompt_tokens": len(r.prompt), "completion_tokens": len(r.output),
+                               "finish_reason": {"type": r.finish_reason}}}
             if return_logprob:
                 o["logprobs"] = [(t, c, top) for t, (c, top) in zip(r.output, r.token_logprobs)]
             out.append(o)

@@ -351,7 +351,14 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         ``sampling_params`` dict (max_new_tokens, temperature, top_k, top_p,
         seed, stop, stop_token_ids). Returns ``text``, ``output_ids`` and
         ``meta_info`` (prompt / completion tokens, finish_reason); with
-        ``stream`` the same objects, cumulative, as server-sent events."""
+        ``stream`` the same objects, cumulative, as server-sent events. A
+        batch (``text`` a list of strings, or ``input_ids`` a list of id
+        lists; ``sampling_params`` and ``rid`` one per item or shared) returns
+        a list, one result per item, in order."""
+        key = "input_ids" if body.get("input_ids") is not None else "text"
+        src = body.get(key, "")
+        if isinstance(src, list) and src and all(isinstance(x, (str, list)) for x in src):
+            return await _generate_batch(body, key, src)
         if body.get("input_ids") is not None:
             prompt = _prompt_ids(body["input_ids"])
         else:
@@ -419,6 +426,29 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         out, fin, lps, plps = await run_in_threadpool(_run, prompt, max_new, stop, sampling, stops,
                                                       top_n if want_lp else None, score_prompt, rid)
         return result(out, fin, lps, plps)
+
+    async def _generate_batch(body, key, items):
+        import asyncio
+
+        if body.get("stream"):
+            raise HTTPException(400, "a batch is not supported with stream")
+        n = len(items)
+
+        def per_item(field, default):
+            v = body.get(field, default)
+            if isinstance(v, list):
+                if len(v) != n:
+                    raise HTTPException(400, f"{field} has {len(v)} entries for {n} prompts")
+                return v
+            return [v] * n
+
+        sps, rids = per_item("sampling_params", {}), per_item("rid", None)
+        if rids[0] is not None and len(set(rids)) != n:
+            raise HTTPException(400, "rid values must differ within a batch")
+        for x, sp in zip(items, sps):  # refuse the whole batch before running any of it
+            _check(_prompt_ids(x), int((sp or {}).get("max_new_tokens", 128)))
+        subs = [{**body, key: x, "sampling_params": sp, "rid": r} for x, sp, r in zip(items, sps, rids)]
+        return list(await asyncio.gather(*[generate(sb) for sb in subs]))
 
     return app
 

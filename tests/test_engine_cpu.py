@@ -307,8 +307,10 @@ def test_prefill_chunks_that_end_no_prompt_are_not_read_back():
 def test_text_api_in_the_shape_of_sglangs_offline_engine():
     eng = _engine()
     one = eng.generate_text("Hello, B200", {"max_new_tokens": 4})
-    assert set(one) == {"text", "token_ids", "finish_reason"}
+    assert set(one) == {"text", "token_ids", "finish_reason", "meta_info"}
     assert len(one["token_ids"]) == 4 and one["finish_reason"] == "length" and isinstance(one["text"], str)
+    assert one["meta_info"] == {"prompt_tokens": len("Hello, B200"), "completion_tokens": 4,
+                                "finish_reason": {"type": "length"}}
     # the same prompt as token ids gives the same tokens (byte tokenizer without a checkpoint)
     assert _engine().generate([list("Hello, B200".encode())], max_new_tokens=4)[0] == one["token_ids"]
     sp = {"max_new_tokens": 5, "temperature": 1.3, "top_k": 30, "seed": 11}

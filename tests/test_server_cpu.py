@@ -527,6 +527,17 @@ def test_sglang_native_generate_endpoint():
         c = requests.post(base + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
                                                                "max_completion_tokens": 2}, timeout=60).json()
         assert c["usage"]["completion_tokens"] == 2
+        # a batch: one result per item, in order; per-item or shared sampling params
+        rs = requests.post(base + "/generate", json={"text": ["ab", "c"], "sampling_params": [
+            {"max_new_tokens": 2}, {"max_new_tokens": 3}]}, timeout=60).json()
+        assert [x["output_ids"] for x in rs] == [expected(list(b"ab"), 2), expected(list(b"c"), 3)]
+        rs = requests.post(base + "/generate", json={"input_ids": [[7], [8, 9]], "rid": ["a", "b"],
+                                                     "sampling_params": {"max_new_tokens": 2}}, timeout=60).json()
+        assert [x["output_ids"] for x in rs] == [expected([7], 2), expected([8, 9], 2)]
+        assert [x["meta_info"]["id"] for x in rs] == ["a", "b"]
+        for bad in ({"text": ["a", "b"], "rid": ["x"]}, {"text": ["a", "b"], "rid": ["x", "x"]},
+                    {"text": ["a", "b"], "stream": True}, {"input_ids": [[1], [1] * 5000]}):
+            assert requests.post(base + "/generate", json=bad, timeout=60).status_code == 400, bad
     finally:
         server.stop()
         loop.join(timeout=30)
