@@ -26,6 +26,8 @@ BENCHES = {
     "bench_torch": ("bench.py", ["--steps", "3", "--warmup", "3", "--impl", "torch"], 1),
     "decode": ("benchmarks/decode_bench.py", [], 1),
     "decode_torch": ("benchmarks/decode_bench.py", ["--impl", "torch"], 1),
+    "decode_int4": ("benchmarks/decode_bench.py", ["--int4"], 1),
+    "perplexity": ("benchmarks/perplexity.py", ["--model", "tiny", "--compare", "oracle"], 1),
     "allreduce": ("benchmarks/allreduce_sweep.py", ["--graph"], 2),
     "fused_ar": ("benchmarks/fused_ar_bench.py", [], 2),
     "push": ("benchmarks/push_bench.py", [], 2),
