@@ -487,6 +487,18 @@ def render_metrics(server: "EngineServer") -> str:
         metric("mbx_allreduce_calls_total", "counter", "In-house collective calls by path.",
                [({"path": k}, v) for k, v in sorted(comm.counters.items())])
         metric("mbx_communicator_error", "gauge", "Sticky device error code (0 = ok).", [({}, comm.err())])
+    metric("mbx_requests_in_flight", "gauge", "Requests submitted and not finished.", [({}, server._live)])
+    sched = getattr(eng, "sched", None)
+    if sched is not None:
+        for name, attr, help_ in (("mbx_num_queue_reqs", "waiting", "Requests waiting for admission."),
+                                  ("mbx_num_prefill_reqs", "prefilling", "Requests with prompt tokens left."),
+                                  ("mbx_num_running_reqs", "running", "Requests decoding.")):
+            if hasattr(sched, attr):
+                metric(name, "gauge", help_, [({}, len(getattr(sched, attr)))])
+    alloc = getattr(getattr(eng, "kv", None), "alloc", None)
+    if alloc is not None and alloc.capacity:
+        metric("mbx_kv_cache_usage", "gauge", "Fraction of KV cache pages in use (prefix-cache pages included).",
+               [({}, round((alloc.capacity - alloc.free) / alloc.capacity, 6))])
     pc = getattr(eng, "prefix_cache", None)
     if pc is not None:
         metric("mbx_prefix_cache_hit_pages_total", "counter", "KV pages served from the prefix cache.",

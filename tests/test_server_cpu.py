@@ -161,6 +161,7 @@ def test_http_completions_and_chat():
         assert "mbx_requests_total 12" in lines
         assert any(ln.startswith('mbx_inter_token_latency_seconds{quantile="0.5"}') for ln in lines)
         assert any(ln.startswith("# TYPE mbx_generation_tokens_total counter") for ln in lines)
+        assert "mbx_requests_in_flight 0" in lines and "mbx_num_running_reqs 0" in lines
     finally:
         server.stop()
         loop.join(timeout=30)
@@ -970,6 +971,42 @@ def test_abort_by_request_id_and_health_generate():
                                                      "sampling_params": {"max_new_tokens": 2}}, timeout=60)
         assert ok.status_code == 200                                    # the id is free again
         assert requests.post(base + "/abort_request", json={}, timeout=30).status_code == 400
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
+
+
+def test_metrics_gauges_on_the_oracle_engine():
+    """Queue, running and KV-cache gauges read the real scheduler and page
+    allocator: pages held by the prefix cache after a request count as used."""
+    import requests
+
+    from conftest import free_port
+
+    eng_mod = importlib.import_module("3080_mod_p2p_sglang_patch_b200.engine")
+    models = importlib.import_module("3080_mod_p2p_sglang_patch_b200.models")
+    eng = eng_mod.LLMEngine(models.LlamaConfig.tiny(), impl="oracle", device="cpu", max_batch=2, max_seq=256,
+                            chunk=64, use_graphs=False, prefix_cache=True)
+    server = srv_mod.EngineServer(eng, max_prompt=eng.max_seq)
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "tiny"), "127.0.0.1", port)
+    base = f"http://127.0.0.1:{port}"
+    try:
+        def gauges():
+            return {ln.split()[0]: float(ln.split()[1]) for ln in requests.get(base + "/metrics", timeout=30)
+                    .text.splitlines() if ln.startswith(("mbx_num_", "mbx_kv_", "mbx_requests_in_flight"))}
+
+        g0 = gauges()
+        assert g0 == {"mbx_requests_in_flight": 0, "mbx_num_queue_reqs": 0, "mbx_num_prefill_reqs": 0,
+                      "mbx_num_running_reqs": 0, "mbx_kv_cache_usage": 0}
+        r = requests.post(base + "/v1/completions", json={"prompt": list(range(1, 40)), "max_tokens": 2}, timeout=120)
+        assert r.status_code == 200
+        g1 = gauges()
+        assert g1["mbx_num_running_reqs"] == 0 and g1["mbx_requests_in_flight"] == 0
+        assert 0 < g1["mbx_kv_cache_usage"] <= 1            # the prompt's full pages stay in the prefix cache
     finally:
         server.stop()
         loop.join(timeout=30)
