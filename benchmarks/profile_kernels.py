@@ -12,6 +12,9 @@ Cases (a few hundred MB on the device at most):
   sp     : sequence-parallel GEMM -> reduce-scatter epilogue, owned-row
            RMSNorm + all-gather push, all-gather -> GEMM (same shape)
   elem   : RMSNorm [32768, 4096] and SiLU-mul [8192, 2 x 14336] (inputs > L2)
+  int4   : AWQ int4 GEMV, 8 rows, 8B gate_up at TP=1 (N=28672, K=4096, group
+           128: 59 MB of packed weights), then its bf16 dequantization
+  rope   : q/k-norm RoPE + paged cache write, 8192 tokens, 32q/8kv heads
 The fused and sp cases run the multi-GPU kernels as a one-rank emulation
 (world = 1): the communicator context points at one local buffer laid out
 like the symmetric buffer, so every peer store lands in local memory. They
@@ -102,6 +105,27 @@ def main():
         ops.silu_mul(gu)
         torch.cuda.synchronize()
         del gu
+    if "int4" in which:
+        models = importlib.import_module(f"{PKG}.models")
+        N, K, G = 28672, 4096, 128
+        qw, qz, sc = models.awq_quantize(torch.randn(N, K, device="cuda") * 0.02, G)
+        w4 = ops.Int4Weight(qw, qz, sc, G)
+        x = torch.randn(8, K, device="cuda").to(torch.bfloat16)
+        ops.awq_gemm(x, w4)
+        ops.awq_dequant(w4)
+        torch.cuda.synchronize()
+        del w4, qw, qz, sc
+    if "rope" in which:
+        T, nq, nkv, page = 8192, 32, 8, 16
+        qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda").to(torch.bfloat16)
+        cs = ops.rope_cos_sin(T, D, 1e6, "cuda")
+        pos = torch.arange(T, dtype=torch.int32, device="cuda")
+        kc = torch.zeros(T // page, nkv, page, D, device="cuda", dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        slots = torch.arange(T, dtype=torch.int64, device="cuda")
+        nw = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+        ops.rope_and_cache(qkv, pos, cs, nq, nkv, slots, kc, vc, q_norm=nw, k_norm=nw, eps=1e-6)
+        torch.cuda.synchronize()
     assert ops.gemm_error() == 0
     print("profile_kernels done")
 
