@@ -155,26 +155,32 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         if server.overloaded():  # before a stream starts: a status code, not an error event
             raise HTTPException(503, "server overloaded")
 
-    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None, stops=()):
+    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None, stops=(), lp=None, lp_fmt=None):
         """Server-sent events: one chunk per engine step's new tokens (the text
         delta of the decoded output, cut before a stop string), a last chunk
         with finish_reason and usage, then [DONE]. A client that disconnects
-        closes the generator, which aborts the request."""
+        closes the generator, which aborts the request. With ``lp`` (k
+        alternatives) each chunk carries ``lp_fmt(tokens, logprobs)`` of its
+        tokens."""
         def gen():
             out, reason, sent = [], [], ""
             fin = None
             try:
                 stream = server.submit_stream(prompt, max_tokens, stop_ids=stop, reason_out=reason,
-                                              sampling=sampling, stop_strs=stops, detok=tok.decode)
+                                              sampling=sampling, stop_strs=stops, detok=tok.decode, logprobs=lp)
                 try:
-                    for toks in stream:
+                    for item in stream:
+                        toks, lps = item if lp is not None else (item, None)
                         out += toks
                         hit = bool(stops) and _find_stop(tok.decode(out), stops) >= 0
                         text = _text(out, stops)
                         if stops and not hit:
                             text = text[:len(text) - _held_back(text, stops)]
                         delta, sent = text[len(sent):], text
-                        yield "data: " + json.dumps(chunk_of(toks, delta, None, None)) + "\n\n"
+                        obj = chunk_of(toks, delta, None, None)
+                        if lp is not None:
+                            obj["choices"][0]["logprobs"] = lp_fmt(toks, lps)
+                        yield "data: " + json.dumps(obj) + "\n\n"
                         if hit:
                             fin = "stop"  # the server loop drops the request on every rank
                             break
@@ -285,18 +291,20 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         if score_only:
             max_tokens = 1
         stop, stops = _stop(body), _stop_strs(body)
+        lp = body.get("logprobs")
+        lp = None if lp is None or lp is False else int(lp)
         if body.get("stream"):
             _n(body)
             if len(prompts) > 1:
                 raise HTTPException(400, "several prompts are not supported with stream")
+            if echo:
+                raise HTTPException(400, "echo is not supported with stream")
             _check(prompt, max_tokens)
             cid, created = f"cmpl-{next(ids)}", int(time.time())
             return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
                 "id": cid, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
-        lp = body.get("logprobs")
-        lp = None if lp is None or lp is False else int(lp)
+                "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": fin, "logprobs": None}],
+                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops, lp, _completion_logprobs)
         n = _n(body)
         for pr in prompts:  # refuse the whole request before running any of it
             _check(pr, max_tokens)
@@ -328,6 +336,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         prompt = tok.chat(msgs)
         max_tokens = int(body.get("max_completion_tokens") or body.get("max_tokens") or 16)
         stop, stops = _stop(body), _stop_strs(body)
+        lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
         if body.get("stream"):
             _n(body)
             _check(prompt, max_tokens)
@@ -335,9 +344,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
             return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
                 "id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                 "choices": [{"index": 0, "delta": {"content": text} if (toks or text) else {},
-                             "token_ids": toks, "finish_reason": fin}],
-                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops)
-        lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
+                             "token_ids": toks, "finish_reason": fin, "logprobs": None}],
+                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops, lp, _chat_logprobs)
         runs = await _run_n(_n(body), prompt, max_tokens, stop, _sampling(body), stops, lp)
         choices = [{"index": i, "message": {"role": "assistant", "content": _text(out, stops)}, "token_ids": out,
                     "finish_reason": fin, "logprobs": _chat_logprobs(out, lps) if lp is not None else None}

@@ -149,13 +149,15 @@ class EngineServer:
         return p
 
     def submit_stream(self, prompt: list, max_new: int, timeout: float = None, stop_ids=None, reason_out=None,
-                      sampling=None, stop_strs=(), detok=None, name=None):
+                      sampling=None, stop_strs=(), detok=None, name=None, logprobs=None):
         """Like ``submit`` but yields lists of new token ids as the engine
         produces them (rank 0, from an HTTP thread); the finish reason is
         appended to ``reason_out`` (a list) at the end. Closing the generator
-        early (a client that went away) aborts the request."""
+        early (a client that went away) aborts the request. With ``logprobs``
+        (k alternatives) it yields ``(token ids, logprobs)`` pairs instead, one
+        ``(logprob, [(id, logprob)] * k)`` per token."""
         p = self._enqueue(prompt, max_new, stream=True, stop_ids=stop_ids, sampling=sampling, stop_strs=stop_strs,
-                          detok=detok, name=name)
+                          detok=detok, name=name, logprobs=logprobs)
         try:
             while True:
                 try:
@@ -164,7 +166,7 @@ class EngineServer:
                     raise TimeoutError("request timed out") from None
                 if item is None:
                     break
-                yield item
+                yield item if logprobs is not None else item[0]
         finally:
             if not p.event.is_set():
                 self.abort(p)
@@ -337,8 +339,11 @@ class EngineServer:
                 if self.rank == 0:
                     for p in self._by_rid.values():  # stream tokens as they appear
                         if p.stream is not None and p.req is not None and len(p.req.output) > p.sent:
-                            p.stream.put(list(p.req.output[p.sent:]))
-                            p.sent = len(p.req.output)
+                            n = len(p.req.output)
+                            lps = list(getattr(p.req, "token_logprobs", None) or [])[p.sent:n] \
+                                if p.logprobs is not None else []
+                            p.stream.put((list(p.req.output[p.sent:n]), lps))
+                            p.sent = n
                         if p.stop_strs and p.req is not None and len(p.req.output) > p.checked:
                             p.checked = len(p.req.output)
                             # a new match ends in the newest tokens: decode a tail

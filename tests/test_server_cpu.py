@@ -564,6 +564,27 @@ def test_openai_logprobs_formats():
         assert content[0]["bytes"] == list(content[0]["token"].encode())
         r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 2}, timeout=60).json()
         assert r["choices"][0]["logprobs"] is None
+        # streamed: each chunk carries the logprobs of its own tokens
+        import json as _json
+
+        def chunks(path, body):
+            with requests.post(base + path, json={**body, "stream": True}, stream=True, timeout=60) as resp:
+                return [_json.loads(ln[6:]) for ln in resp.iter_lines(decode_unicode=True)
+                        if ln.startswith("data: ") and ln != "data: [DONE]"]
+
+        cs = chunks("/v1/completions", {"prompt": [100], "max_tokens": 3, "logprobs": 1})
+        toks = [t for c in cs if c["choices"][0]["logprobs"] for t in c["choices"][0]["logprobs"]["tokens"]]
+        assert toks == ["d", "e", "f"] and cs[-1]["choices"][0]["logprobs"] is None      # the final chunk
+        assert all(c["choices"][0]["logprobs"]["top_logprobs"][0] == {t: -0.25}
+                   for c, t in zip(cs, "def"))
+        cs = chunks("/v1/chat/completions", {"messages": [{"role": "user", "content": "x"}], "max_tokens": 2,
+                                             "logprobs": True, "top_logprobs": 2})
+        items = [it for c in cs if c["choices"][0]["logprobs"] for it in c["choices"][0]["logprobs"]["content"]]
+        assert len(items) == 2 and all(it["logprob"] == -0.25 and len(it["top_logprobs"]) == 2 for it in items)
+        plain = chunks("/v1/completions", {"prompt": [100], "max_tokens": 2})
+        assert all(c["choices"][0]["logprobs"] is None for c in plain)
+        assert requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 2, "echo": True,
+                                                             "stream": True}, timeout=60).status_code == 400
         # with a stop string the logprobs are cut with the tokens
         r = requests.post(base + "/v1/completions", json={"prompt": [100], "max_tokens": 9, "logprobs": 0,
                                                           "stop": "fg"}, timeout=60).json()
