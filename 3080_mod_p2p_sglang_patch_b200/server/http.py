@@ -405,27 +405,33 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
             return {"text": _text(out, stops), "output_ids": out, "meta_info": meta}
 
         if body.get("stream"):
+            if score_prompt:
+                raise HTTPException(400, "logprob_start_len is not supported with stream")
             _check(prompt, max_new)
+            lpk = top_n if want_lp else None
 
             def gen():
-                out, reason = [], []
+                out, reason, lps = [], [], []
                 try:
                     stream = server.submit_stream(prompt, max_new, stop_ids=stop, reason_out=reason,
-                                                  sampling=sampling, stop_strs=stops, detok=tok.decode, name=rid)
+                                                  sampling=sampling, stop_strs=stops, detok=tok.decode, name=rid,
+                                                  logprobs=lpk)
                     fin = None
                     try:
-                        for toks in stream:
+                        for item in stream:
+                            toks, new = item if lpk is not None else (item, [])
                             out += toks
+                            lps += new
                             if stops and _find_stop(tok.decode(out), stops) >= 0:
                                 fin = "stop"
                                 break
-                            yield "data: " + json.dumps(result(out, None)) + "\n\n"
+                            yield "data: " + json.dumps(result(out, None, lps)) + "\n\n"
                     finally:
                         stream.close()
                     fin = fin or (reason[0] if reason else "length")
                     if fin == "stop" and stops:
                         out = out[:_stop_prefix(out, stops, tok.decode) or len(out)]
-                    yield "data: " + json.dumps(result(out, fin)) + "\n\n"
+                    yield "data: " + json.dumps(result(out, fin, lps[:len(out)])) + "\n\n"
                 except (ValueError, RuntimeError, TimeoutError) as e:
                     yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
                 yield "data: [DONE]\n\n"

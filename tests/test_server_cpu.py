@@ -581,6 +581,14 @@ def test_openai_logprobs_formats():
                                              "logprobs": True, "top_logprobs": 2})
         items = [it for c in cs if c["choices"][0]["logprobs"] for it in c["choices"][0]["logprobs"]["content"]]
         assert len(items) == 2 and all(it["logprob"] == -0.25 and len(it["top_logprobs"]) == 2 for it in items)
+        g = chunks("/generate", {"input_ids": [100], "return_logprob": True, "top_logprobs_num": 1,
+                                 "sampling_params": {"max_new_tokens": 3}})
+        meta = g[-1]["meta_info"]
+        assert meta["output_token_logprobs"] == [[-0.25, t, None] for t in expected([100], 3)]
+        assert meta["output_top_logprobs"][0] == [[-0.25, 100, None]]
+        assert requests.post(base + "/generate", json={"input_ids": [100], "return_logprob": True,
+                                                       "logprob_start_len": 0, "stream": True},
+                             timeout=60).status_code == 400
         plain = chunks("/v1/completions", {"prompt": [100], "max_tokens": 2})
         assert all(c["choices"][0]["logprobs"] is None for c in plain)
         assert requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 2, "echo": True,
