@@ -462,11 +462,14 @@ class LLMEngine:
         (0: greedy), ``top_k``, ``top_p``, ``seed``, ``stop_token_ids``
         (default: the checkpoint's EOS ids), ``presence_penalty``,
         ``frequency_penalty``, ``repetition_penalty``, ``logit_bias`` ({id:
-        bias}) and ``min_new_tokens``. Returns one ``{"text",
+        bias}), ``min_new_tokens`` and ``stop`` (a string or a list: the
+        request ends once its text holds one, and the text and token ids are
+        cut before it, finish reason "stop"). Returns one ``{"text",
         "token_ids", "finish_reason", "meta_info"}`` per prompt (a single dict
         for a single string); ``meta_info`` is sglang's (prompt and
         completion token counts, ``finish_reason: {"type": ...}``). ``return_logprob`` adds ``"logprobs"``: per generated token
         (id, logprob, [(id, logprob)] of the ``top_logprobs_num`` most likely)."""
+        from .stops import find_stop, stop_prefix, tail_hit
         from .tokenizer import ByteTokenizer
 
         tok = self.tokenizer or ByteTokenizer()
@@ -474,6 +477,8 @@ class LLMEngine:
         max_new = int(sp.pop("max_new_tokens", 16))
         stop = sp.pop("stop_token_ids", None)
         stop = self.default_stop_ids if stop is None else tuple(stop)
+        stop_strs = sp.pop("stop", None) or ()
+        stop_strs = tuple(x for x in ((stop_strs,) if isinstance(stop_strs, str) else stop_strs) if x)
         temp = float(sp.pop("temperature", 0.0))
         top_k, top_p, seed = int(sp.pop("top_k", 0)), float(sp.pop("top_p", 1.0)), sp.pop("seed", None)
         adj = dict(presence_penalty=float(sp.pop("presence_penalty", 0.0)),
@@ -490,13 +495,34 @@ class LLMEngine:
         lp = int(top_logprobs_num) if return_logprob else None
         reqs = [self.add_request(tok.encode(p), max_new, stop, sampling, logprobs=lp)
                 for p in ([prompts] if single else prompts)]
-        self.run()
+        if stop_strs:
+            # the same check on every TP rank (same tokens, same tokenizer), so
+            # every rank aborts a request at the same step
+            checked = {r.rid: 0 for r in reqs}
+            while self.sched.has_work():
+                self.step()
+                for r in reqs:
+                    if r.finish_reason is None and len(r.output) > checked[r.rid]:
+                        checked[r.rid] = len(r.output)
+                        if tail_hit(r.output, stop_strs, tok.decode):
+                            self.abort(r.rid)
+            self.sched.finished = []
+        else:
+            self.run()
         out = []
         for r in reqs:
-            o = {"text": tok.decode(r.output), "token_ids": list(r.output), "finish_reason": r.finish_reason,
-                 "meta_info": {"prompt_tokens": len(r.prompt), "completion_tokens": len(r.output),
-                               "finish_reason": {"type": r.finish_reason}}}
+            ids, reason = list(r.output), r.finish_reason
+            text = tok.decode(ids)
+            if stop_strs:
+                k = stop_prefix(ids, stop_strs, tok.decode)
+                if k is not None:
+                    ids, reason = ids[:k], "stop"
+                    text = tok.decode(ids)
+                    text = text[:find_stop(text, stop_strs)]
+            o = {"text": text, "token_ids": ids, "finish_reason": reason,
+                 "meta_info": {"prompt_tokens": len(r.prompt), "completion_tokens": len(ids),
+                               "finish_reason": {"type": reason}}}
             if return_logprob:
-                o["logprobs"] = [(t, c, top) for t, (c, top) in zip(r.output, r.token_logprobs)]
+                o["logprobs"] = [(t, c, top) for t, (c, top) in zip(ids, r.token_logprobs)]
             out.append(o)
         return out[0] if single else out

@@ -9,6 +9,11 @@ import queue
 import threading
 import time
 
+from ..engine.stops import find_stop as _find_stop  # noqa: F401 - also used by http.py
+from ..engine.stops import held_back as _held_back  # noqa: F401
+from ..engine.stops import stop_prefix as _stop_prefix
+from ..engine.stops import tail_hit
+
 logger = logging.getLogger(__name__)
 
 
@@ -346,10 +351,8 @@ class EngineServer:
                             p.sent = n
                         if p.stop_strs and p.req is not None and len(p.req.output) > p.checked:
                             p.checked = len(p.req.output)
-                            # a new match ends in the newest tokens: decode a tail
-                            # window, not the whole output, every step
-                            win = max(16, 4 * max(len(x) for x in p.stop_strs))
-                            if _find_stop(p.detok(p.req.output[-win:]), p.stop_strs) >= 0:
+                            # a new match ends in the newest tokens
+                            if tail_hit(p.req.output, p.stop_strs, p.detok):
                                 p.stop_hit = True
                                 self.abort(p)  # every rank drops it next step
                 done, eng.sched.finished = eng.sched.finished, []
@@ -397,32 +400,3 @@ class EngineServer:
                     break
                 if isinstance(c, _Pending):
                     c.finish(error="server stopped")
-
-
-def _find_stop(text: str, stops) -> int:
-    """Index of the earliest stop string in ``text``, or -1."""
-    hits = [i for i in (text.find(x) for x in stops) if i >= 0]
-    return min(hits) if hits else -1
-
-
-def _held_back(text: str, stops) -> int:
-    """Characters at the end of ``text`` that could begin a stop string (a
-    stream holds them until the next tokens decide)."""
-    hold = 0
-    for x in stops:
-        for k in range(min(len(x) - 1, len(text)), hold, -1):
-            if text.endswith(x[:k]):
-                hold = k
-                break
-    return hold
-
-
-def _stop_prefix(tokens, stops, detok):
-    """Length of the shortest token prefix whose text contains a stop string
-    (None if the whole output holds none)."""
-    if _find_stop(detok(tokens), stops) < 0:
-        return None
-    k = len(tokens)
-    while k > 1 and _find_stop(detok(tokens[:k - 1]), stops) >= 0:
-        k -= 1
-    return k

@@ -665,3 +665,23 @@ def _flush_worker(rank, world):
 def test_flush_cache_reaches_every_rank():
     res = run_ranks(_flush_worker, 2)
     assert res[0] == res[1] and res[0]["flushed"] == 3
+
+
+def test_text_api_stop_strings_end_the_request_early():
+    """sglang's ``stop`` in the offline API: the request ends at the step whose
+    text completes a stop string; tokens and text are cut before it."""
+    eng = _engine()
+    sp = {"max_new_tokens": 12, "logit_bias": {ord("a"): 100.0}}            # greedy: "aaaa..."
+    full = eng.generate_text("x", sp)
+    assert full["token_ids"] == [97] * 12 and full["text"] == "a" * 12
+    steps = []
+    orig = eng.step
+    eng.step = lambda: (steps.append(1), orig())[1]
+    cut = eng.generate_text(["x", "y"], {**sp, "stop": ["zz", "aaa"]})
+    for r in cut:
+        assert r["token_ids"] == [97, 97, 97] and r["text"] == "" and r["finish_reason"] == "stop"
+        assert r["meta_info"]["completion_tokens"] == 3
+    assert len(steps) < 12                                  # aborted, not run to max_new_tokens
+    none = eng.generate_text("x", {**sp, "stop": "b"})
+    assert none["finish_reason"] == "length" and none["text"] == "a" * 12
+    assert not eng.sched.has_work() and not eng.sched.finished
