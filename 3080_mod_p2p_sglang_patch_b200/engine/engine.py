@@ -462,7 +462,8 @@ class LLMEngine:
         (0: greedy), ``top_k``, ``top_p``, ``seed``, ``stop_token_ids``
         (default: the checkpoint's EOS ids), ``presence_penalty``,
         ``frequency_penalty``, ``repetition_penalty``, ``logit_bias`` ({id:
-        bias}), ``min_new_tokens`` and ``stop`` (a string or a list: the
+        bias}), ``min_new_tokens``, ``ignore_eos`` (generate past the
+        checkpoint's EOS ids) and ``stop`` (a string or a list: the
         request ends once its text holds one, and the text and token ids are
         cut before it, finish reason "stop"). Returns one ``{"text",
         "token_ids", "finish_reason", "meta_info"}`` per prompt (a single dict
@@ -476,7 +477,8 @@ class LLMEngine:
         sp = dict(sampling_params or {})
         max_new = int(sp.pop("max_new_tokens", 16))
         stop = sp.pop("stop_token_ids", None)
-        stop = self.default_stop_ids if stop is None else tuple(stop)
+        ignore_eos = bool(sp.pop("ignore_eos", False))
+        stop = (() if ignore_eos else self.default_stop_ids) if stop is None else tuple(stop)
         stop_strs = sp.pop("stop", None) or ()
         stop_strs = tuple(x for x in ((stop_strs,) if isinstance(stop_strs, str) else stop_strs) if x)
         temp = float(sp.pop("temperature", 0.0))

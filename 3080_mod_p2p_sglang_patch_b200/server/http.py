@@ -42,8 +42,12 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         raise HTTPException(400, "prompt must be a string or a list of token ids")
 
     def _stop(body):
+        """Stop token ids: ``stop_token_ids``, else none with ``ignore_eos``,
+        else None (the server's default, the checkpoint's EOS ids)."""
         ids_ = body.get("stop_token_ids")
-        return None if ids_ is None else [int(t) for t in ids_]
+        if ids_ is None:
+            return [] if body.get("ignore_eos") else None
+        return [int(t) for t in ids_]
 
     def _stop_strs(body):
         """OpenAI ``stop``: a string or a list of strings."""

@@ -685,3 +685,11 @@ def test_text_api_stop_strings_end_the_request_early():
     none = eng.generate_text("x", {**sp, "stop": "b"})
     assert none["finish_reason"] == "length" and none["text"] == "a" * 12
     assert not eng.sched.has_work() and not eng.sched.finished
+
+
+def test_text_api_ignore_eos():
+    eng = _engine()
+    eng.default_stop_ids = (97,)                       # as if "a" were the checkpoint's EOS
+    sp = {"max_new_tokens": 4, "logit_bias": {97: 100.0}}
+    assert eng.generate_text("x", sp)["token_ids"] == [97]
+    assert eng.generate_text("x", {**sp, "ignore_eos": True})["token_ids"] == [97] * 4

@@ -1040,3 +1040,30 @@ def test_metrics_gauges_on_the_oracle_engine():
         server.stop()
         loop.join(timeout=30)
         http.should_exit = True
+
+
+def test_ignore_eos_overrides_the_default_stop_ids():
+    import requests
+
+    from conftest import free_port
+
+    eng = FakeEngine()
+    server = srv_mod.EngineServer(eng, max_prompt=4096, stop_ids=(101,))    # the "EOS" is token 101
+    loop = threading.Thread(target=server.serve_forever, daemon=True)
+    loop.start()
+    port = free_port()
+    http, _ = srv_mod.start_http(srv_mod.build_app(server, "fake"), "127.0.0.1", port)
+    base = f"http://127.0.0.1:{port}"
+    try:
+        body = {"prompt": [100], "max_tokens": 4}
+        r = requests.post(base + "/v1/completions", json=body, timeout=60).json()["choices"][0]
+        assert r["token_ids"] == [100, 101] and r["finish_reason"] == "stop"
+        r = requests.post(base + "/v1/completions", json={**body, "ignore_eos": True}, timeout=60).json()
+        assert r["choices"][0]["token_ids"] == expected([100], 4)
+        g = requests.post(base + "/generate", json={"input_ids": [100], "sampling_params": {
+            "max_new_tokens": 4, "ignore_eos": True}}, timeout=60).json()
+        assert g["output_ids"] == expected([100], 4) and g["meta_info"]["finish_reason"]["type"] == "length"
+    finally:
+        server.stop()
+        loop.join(timeout=30)
+        http.should_exit = True
