@@ -159,7 +159,14 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
         if server.overloaded():  # before a stream starts: a status code, not an error event
             raise HTTPException(503, "server overloaded")
 
-    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None, stops=(), lp=None, lp_fmt=None):
+    def _no_usage(body):
+        """OpenAI ``stream_options.include_usage: false``: the last chunk
+        carries no usage (by default it does)."""
+        so = body.get("stream_options") or {}
+        return isinstance(so, dict) and so.get("include_usage") is False
+
+    def _sse(prompt, max_tokens, chunk_of, stop=None, sampling=None, stops=(), lp=None, lp_fmt=None,
+             usage=True):
         """Server-sent events: one chunk per engine step's new tokens (the text
         delta of the decoded output, cut before a stop string), a last chunk
         with finish_reason and usage, then [DONE]. A client that disconnects
@@ -194,7 +201,7 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                 if fin == "stop" and stops:
                     out = out[:_stop_prefix(out, stops, tok.decode) or len(out)]
                 rest = _text(out, stops)[len(sent):]  # text held back for a stop string that never came
-                yield "data: " + json.dumps(chunk_of([], rest, fin, _usage(prompt, out))) + "\n\n"
+                yield "data: " + json.dumps(chunk_of([], rest, fin, _usage(prompt, out) if usage else None)) + "\n\n"
             except (RuntimeError, TimeoutError) as e:
                 yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
             yield "data: [DONE]\n\n"
@@ -308,7 +315,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
             return _sse(prompt, max_tokens, lambda toks, text, fin, usage: {
                 "id": cid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": fin, "logprobs": None}],
-                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops, lp, _completion_logprobs)
+                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops, lp, _completion_logprobs,
+                not _no_usage(body))
         n = _n(body)
         for pr in prompts:  # refuse the whole request before running any of it
             _check(pr, max_tokens)
@@ -349,7 +357,8 @@ def build_app(server: EngineServer, model_name: str, tokenizer=None, api_key: st
                 "id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                 "choices": [{"index": 0, "delta": {"content": text} if (toks or text) else {},
                              "token_ids": toks, "finish_reason": fin, "logprobs": None}],
-                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops, lp, _chat_logprobs)
+                **({"usage": usage} if usage else {})}, stop, _sampling(body), stops, lp, _chat_logprobs,
+                not _no_usage(body))
         runs = await _run_n(_n(body), prompt, max_tokens, stop, _sampling(body), stops, lp)
         choices = [{"index": i, "message": {"role": "assistant", "content": _text(out, stops)}, "token_ids": out,
                     "finish_reason": fin, "logprobs": _chat_logprobs(out, lps) if lp is not None else None}

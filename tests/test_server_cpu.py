@@ -589,6 +589,11 @@ def test_openai_logprobs_formats():
         assert requests.post(base + "/generate", json={"input_ids": [100], "return_logprob": True,
                                                        "logprob_start_len": 0, "stream": True},
                              timeout=60).status_code == 400
+        assert "usage" in chunks("/v1/completions", {"prompt": [100], "max_tokens": 2})[-1]
+        for path, body in (("/v1/completions", {"prompt": [100], "max_tokens": 2}),
+                           ("/v1/chat/completions", {"messages": [{"role": "user", "content": "x"}],
+                                                     "max_tokens": 2})):
+            assert all("usage" not in c for c in chunks(path, {**body, "stream_options": {"include_usage": False}}))
         plain = chunks("/v1/completions", {"prompt": [100], "max_tokens": 2})
         assert all(c["choices"][0]["logprobs"] is None for c in plain)
         assert requests.post(base + "/v1/completions", json={"prompt": [1], "max_tokens": 2, "echo": True,
