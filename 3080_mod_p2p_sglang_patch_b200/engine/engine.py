@@ -37,7 +37,8 @@ class LLMEngine:
                  seed: int = 0, use_graphs: bool = True, impl: str = "native", kv_blocks: int = None,
                  graph_sizes=(1, 8, 32, 64), full_init: bool = False, device=None, prefill_graph: bool = False,
                  sp: bool = None, weights=None, prefix_cache: bool = False, mem_fraction: float = None,
-                 mixed_chunk: bool = False, schedule_policy: str = "fcfs", sample_in_graphs: bool = False):
+                 mixed_chunk: bool = False, schedule_policy: str = "fcfs", sample_in_graphs: bool = False,
+                 overlap: bool = None, overlap_min_rows: int = 512):
         if impl == "oracle":  # fp32 torch restatement of every kernel: eager, any device
             use_graphs, prefill_graph = False, False
         if max_seq > cfg.max_pos:
@@ -73,6 +74,15 @@ class LLMEngine:
             self.sp = tp.sp_setup(chunk, cfg.hidden)
             if self.sp is not None:
                 self.model.enable_sp(self.sp)
+        # overlapped micro-batches for large prefill batches (TP > 1, native
+        # build): each micro-batch's allreduces run while the other computes;
+        # None = follow MBX_OVERLAP (default off)
+        if overlap is None:
+            overlap = os.environ.get("MBX_OVERLAP", "0") == "1"
+        self.overlap = False
+        if overlap and tp is not None and self.tp_size > 1 and impl == "native":
+            self.model.enable_overlap(min_rows=overlap_min_rows)
+            self.overlap = self.model.overlap_min_rows is not None
         nkv = cfg.kv_heads // self.tp_size
         self.max_blocks_per_seq = (max_seq + PAGE - 1) // PAGE
         if kv_blocks is None:
@@ -354,7 +364,53 @@ class LLMEngine:
         def attn(li, q, kc, vc):
             return ops.prefill_attention(q, kc, vc, cu_d, kvl_d, bt, tiles, scale, splits=splits)
 
-        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d, return_hidden=return_hidden)
+        halves = self._attn_halves(q_lens, kv_lens, bt, T)
+        return self.model.forward(ids_d, pos_d, slots_d, self.kv.caches, attn, last_d, return_hidden=return_hidden,
+                                  attn_halves=halves)
+
+    def _attn_halves(self, q_lens, kv_lens, bt, T):
+        """Attention of each micro-batch of an overlapped prefill batch
+        (model.overlap_split), or None. A piece that straddles the split is
+        cut in two: its first rows end the first micro-batch with a kv length
+        shortened by the rows that follow; the rest start the second, whose
+        keys include the first part (written to the cache earlier in the same
+        layer)."""
+        T1 = self.model.overlap_split(T)
+        if T1 is None:
+            return None
+        parts = ([], [])  # (q_len, kv_len, piece index) per micro-batch
+        start = 0
+        for i, (q, kv) in enumerate(zip(q_lens, kv_lens)):
+            end = start + q
+            if end <= T1:
+                parts[0].append((q, kv, i))
+            elif start >= T1:
+                parts[1].append((q, kv, i))
+            else:
+                n0 = T1 - start
+                parts[0].append((n0, kv - (q - n0), i))
+                parts[1].append((q - n0, kv, i))
+            start = end
+        scale = self.model.scale
+        nq = self.cfg.heads // self.tp_size
+        fns = []
+        for pl in parts:
+            ql = [p[0] for p in pl]
+            kl = [p[1] for p in pl]
+            cu = torch.zeros(len(ql) + 1, dtype=torch.int32)
+            cu[1:] = torch.tensor(ql, dtype=torch.int32).cumsum(0)
+            meta = self._h2d(torch.cat([cu, torch.tensor(kl, dtype=torch.int32),
+                                        torch.tensor([p[2] for p in pl], dtype=torch.int32)]))
+            n = len(ql)
+            cu_h, kvl_h, sel = meta[:n + 1], meta[n + 1:2 * n + 1], meta[2 * n + 1:]
+            bt_h = bt.index_select(0, sel.long())
+            tiles_h = self._h2d(ops.prefill_tiles(ql))
+            splits_h = ops.prefill_splits(tiles_h.shape[0], nq, max(kl))
+
+            def f(li, q, kc, vc, cu_h=cu_h, kvl_h=kvl_h, bt_h=bt_h, tiles_h=tiles_h, splits_h=splits_h):
+                return ops.prefill_attention(q, kc, vc, cu_h, kvl_h, bt_h, tiles_h, scale, splits=splits_h)
+            fns.append(f)
+        return (T1, fns[0], fns[1])
 
     def decode_inputs(self, reqs):
         """(last token, position, kv length, cache slot, table row) per request."""

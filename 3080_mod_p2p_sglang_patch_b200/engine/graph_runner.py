@@ -183,6 +183,20 @@ class PrefillGraphRunner:
         nq = engine.cfg.heads // engine.tp_size
         self.splits = ops.prefill_splits(self.tiles.shape[0], nq, engine.max_seq)
         ops.workspace(dev).prefill(T * nq * self.splits * 128, T * nq * self.splits)
+        # overlapped micro-batches (model.enable_overlap): rows [0, T1) and
+        # [T1, T) of the chunk, each with its own attention metadata; the
+        # first half's kv length is the chunk's minus T - T1
+        self.T1 = engine.model.overlap_split(T)
+        self.halves = None
+        if self.T1 is not None:
+            self.halves = []
+            for n in (self.T1, T - self.T1):
+                tiles = ops.prefill_tiles([n]).to(dev)
+                splits = ops.prefill_splits(tiles.shape[0], nq, engine.max_seq)
+                ops.workspace(dev).prefill(n * nq * splits * 128, n * nq * splits)
+                self.halves.append({"cu": torch.tensor([0, n], dtype=torch.int32, device=dev), "tiles": tiles,
+                                    "splits": splits, "kvl": torch.full((1,), n, dtype=torch.int32, device=dev)})
+            self.halves[1]["kvl"] = self.kvl
         self.graph = None
         self.out = None
 
@@ -193,7 +207,15 @@ class PrefillGraphRunner:
         def attn(li, q, kc, vc):
             return ops.prefill_attention(q, kc, vc, self.cu, self.kvl, self.bt, self.tiles, scale, splits=self.splits)
 
-        return e.model.forward(self.ids, self.pos, self.slots, e.kv.caches, attn, self.last)
+        halves = None
+        if self.halves is not None:
+            def half_attn(h):
+                def f(li, q, kc, vc):
+                    return ops.prefill_attention(q, kc, vc, h["cu"], h["kvl"], self.bt, h["tiles"], scale,
+                                                 splits=h["splits"])
+                return f
+            halves = (self.T1, half_attn(self.halves[0]), half_attn(self.halves[1]))
+        return e.model.forward(self.ids, self.pos, self.slots, e.kv.caches, attn, self.last, attn_halves=halves)
 
     def capture(self):
         e = self.e
@@ -202,6 +224,8 @@ class PrefillGraphRunner:
         self.slots.zero_()
         self.pos.copy_(torch.arange(self.T, dtype=torch.int32, device=e.device))
         self.kvl.fill_(self.T)
+        if self.halves is not None:
+            self.halves[0]["kvl"].fill_(self.T1)
         torch.cuda.synchronize()
         s = torch.cuda.Stream(device=e.device)
         s.wait_stream(torch.cuda.current_stream(e.device))
@@ -229,6 +253,8 @@ class PrefillGraphRunner:
         self.pos.copy_(pos_d, non_blocking=True)
         self.slots.copy_(slots_d, non_blocking=True)
         self.kvl.fill_(kv_len)
+        if self.halves is not None:
+            self.halves[0]["kvl"].fill_(kv_len - (self.T - self.T1))
         self.bt.copy_(bt_row_d.view(1, -1), non_blocking=True)
         self.graph.replay()
         launches.add(self.kernels_per_replay)

@@ -202,6 +202,10 @@ class LlamaTP:
         # ``sp_min_rows`` tokens that fit its buffers; None = off
         self.sp = None
         self.sp_min_rows = 256
+        # overlapped micro-batches (``enable_overlap``): None = off
+        self.overlap_min_rows = None
+        self.overlap_threads = 256
+        self._comm_stream = None
 
     def enable_sp(self, sp, min_rows: int = 256):
         """Run large batches sequence-parallel (native TP build, bf16 weights)."""
@@ -209,6 +213,41 @@ class LlamaTP:
             return
         self.sp = sp
         self.sp_min_rows = int(min_rows)
+
+    def enable_overlap(self, min_rows: int = 512, threads: int = 256):
+        """Run native TP batches of at least ``min_rows`` tokens as two
+        micro-batches whose allreduces overlap the other's compute (the
+        caller passes per-micro-batch attention, see ``forward``).
+
+        The reference's answer to the same problem is its segmented
+        allreduce: the row-split GEMM output pushed by the copy engine while
+        the next segment computes (sglang/mailbox_ar_ext.cu:233-342,
+        docs/performance.md:51-65). Here whole layers overlap instead: while
+        one micro-batch's allreduce + residual + RMSNorm runs on a
+        high-priority communication stream, the other's GEMMs and attention
+        run on the compute stream. ``threads=256`` launches the collective
+        with half-size blocks, which fit on an SM beside a GEMM CTA."""
+        ok = (self.impl == "native" and self.tp_size > 1 and not self.int4 and self.tp is not None
+              and self.tp.ca_comm is not None)
+        self.overlap_min_rows = int(min_rows) if ok else None
+        self.overlap_threads = int(threads)
+
+    def overlap_split(self, T: int):
+        """Rows of the first micro-batch when a T-token batch runs overlapped
+        (a multiple of 128 near T/2, the tile height of the GEMMs and the
+        attention), else None."""
+        if self.overlap_min_rows is None or T < self.overlap_min_rows:
+            return None
+        if self.sp is not None and T >= self.sp_min_rows and self.sp.fits(T):
+            return None
+        T1 = max(128, (T // 2) // 128 * 128)
+        return T1 if T1 < T else None
+
+    def comm_stream(self):
+        """High-priority stream of the overlapped collectives (created once)."""
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(device=self.device, priority=-1)
+        return self._comm_stream
 
     # ------------------------------------------------------------ building blocks
     def _linear(self, x, w, out=None, residual=None):
@@ -303,7 +342,7 @@ class LlamaTP:
         return ops.argmax_combine(gv.contiguous(), gi.contiguous())
 
     # ------------------------------------------------------------ forward
-    def forward(self, ids, positions, slots, kv_caches, attn, last_idx, return_hidden=False):
+    def forward(self, ids, positions, slots, kv_caches, attn, last_idx, return_hidden=False, attn_halves=None):
         """One forward over T tokens.
 
         ids/positions int32 [T]; slots int64 [T] (KV write slots); kv_caches
@@ -311,11 +350,18 @@ class LlamaTP:
         [T, nq, D] (prefill or decode attention); last_idx int64 [B] rows whose
         next token is returned. Returns next-token ids int64 [B] (or the final
         normalised hidden rows [B, H] with ``return_hidden``).
+
+        ``attn_halves``: (T1, attn0, attn1), attention of rows [0, T1) and
+        [T1, T) on their own (attn1's keys include rows [0, T1), which the
+        first micro-batch writes to the cache earlier in the same layer).
+        Used when ``overlap_split(T) == T1``: the overlapped micro-batches.
         """
         cfg, w = self.cfg, self.w
         T = ids.shape[0]
         if self.sp is not None and T >= self.sp_min_rows and self.sp.fits(T):
             return self._forward_sp(ids, positions, slots, kv_caches, attn, last_idx, return_hidden)
+        if attn_halves is not None and self.overlap_split(T) == attn_halves[0]:
+            return self._forward_overlap(ids, positions, slots, kv_caches, attn_halves, last_idx, return_hidden)
         nq, nkv, D = w.nq, w.nkv, cfg.head_dim
         h = self.k.embedding(ids, w.embed, start=w.vocab_start)
         h = self._all_reduce(h)
@@ -353,6 +399,76 @@ class LlamaTP:
                 x = self._ar_norm(part, residual, nxt)
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_pop()
+        x_last = x.index_select(0, last_idx)
+        if return_hidden:
+            return x_last
+        return self._lm_argmax(x_last)
+
+    def _forward_overlap(self, ids, positions, slots, kv_caches, halves, last_idx, return_hidden=False):
+        """Two micro-batches, rows [0, T1) and [T1, T), on two streams.
+
+        Compute stream, per layer: attention block of micro-batch 0, of 1,
+        then MLP block of 0, of 1. Communication stream: each block's
+        allreduce + residual + RMSNorm as soon as its row-parallel GEMM is
+        done, so it runs while the other micro-batch computes. Every
+        communicator call is on the one communication stream, in the same
+        order on every rank (the device epochs stay in step); the compute
+        stream waits only for the collective whose output it reads next.
+        Same math as ``forward`` row by row (sums in rank order, one
+        rounding), so the tokens are identical."""
+        cfg, w, tp = self.cfg, self.w, self.tp
+        T1, attn0, attn1 = halves
+        T = ids.shape[0]
+        nq, nkv, D = w.nq, w.nkv, cfg.head_dim
+        comp = torch.cuda.current_stream(self.device)
+        comm = self.comm_stream()
+        h = ops.embedding(ids, w.embed, start=w.vocab_start)
+        residual = self._all_reduce(h)
+        x = ops.rmsnorm(residual, w.layers[0]["ln1"], cfg.eps)
+        part = torch.empty_like(residual)
+        spans = ((0, T1), (T1, T))
+        R = [residual[a:b] for a, b in spans]
+        X = [x[a:b] for a, b in spans]
+        P = [part[a:b] for a, b in spans]
+        pos = [positions[a:b] for a, b in spans]
+        sl = [slots[a:b] for a, b in spans]
+        attns = (attn0, attn1)
+        done_comp = [torch.cuda.Event(), torch.cuda.Event()]
+        done_comm = [torch.cuda.Event(), torch.cuda.Event()]
+        th = self.overlap_threads
+
+        def collective(i, norm_w):
+            done_comp[i].record(comp)
+            with torch.cuda.stream(comm):
+                comm.wait_event(done_comp[i])
+                tp.all_reduce_rmsnorm(P[i], R[i], norm_w, cfg.eps, out=X[i], threads=th)
+                done_comm[i].record(comm)
+
+        for li, L in enumerate(w.layers):
+            if nvtx.ENABLED:
+                torch.cuda.nvtx.range_push(f"layer {li}")
+            kc, vc = kv_caches[li]
+            for i in (0, 1):
+                if li > 0:
+                    comp.wait_event(done_comm[i])
+                qkv = ops.gemm(X[i], L["qkv"])
+                if cfg.qkv_bias:
+                    qkv += L["qkv_bias"]
+                q = ops.rope_and_cache(qkv, pos[i], self.cos_sin, nq, nkv, sl[i], kc, vc, **self._qk_norm_args(L))
+                o = attns[i](li, q, kc, vc)
+                ops.gemm(o.view(-1, nq * D), L["o"], out=P[i])
+                collective(i, L["ln2"])
+            nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
+            for i in (0, 1):
+                comp.wait_event(done_comm[i])
+                gu = ops.gemm(X[i], L["gate_up"])
+                a = ops.silu_mul(gu)
+                ops.gemm(a, L["down"], out=P[i])
+                collective(i, nxt)
+            if nvtx.ENABLED:
+                torch.cuda.nvtx.range_pop()
+        comp.wait_event(done_comm[0])
+        comp.wait_event(done_comm[1])
         x_last = x.index_select(0, last_idx)
         if return_hidden:
             return x_last

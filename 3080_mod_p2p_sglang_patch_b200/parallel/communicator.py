@@ -290,9 +290,13 @@ class MailboxAR:
         return out
 
     def all_reduce_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
-                           out: torch.Tensor = None, algo=None):
+                           out: torch.Tensor = None, algo=None, threads: int = 512):
         """Fused: residual <- bf16(residual + allreduce(x)); returns
-        rmsnorm(residual) * weight (bf16), in one kernel launch."""
+        rmsnorm(residual) * weight (bf16), in one kernel launch.
+
+        ``threads=256`` launches half-size blocks (half the registers per
+        block), so each fits on an SM beside a running GEMM CTA: the form
+        used when the call overlaps compute on another stream."""
         assert x.dtype == torch.bfloat16 and x.is_contiguous() and residual.is_contiguous()
         H = x.shape[-1]
         M = x.numel() // H
@@ -303,7 +307,7 @@ class MailboxAR:
         if algo is None:
             algo = ALGO_ONESHOT_PUSH if nbytes <= self.cfg.oneshot_max.get(self.world_size, 0) else ALGO_TWOSHOT_PUSH
         self._ar.ar_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(), out.data_ptr(), M, H, eps, algo,
-                            self.cfg.max_blocks, torch.cuda.current_stream(self.device).cuda_stream)
+                            self.cfg.max_blocks, torch.cuda.current_stream(self.device).cuda_stream, int(threads))
         self.counters["fused"] += 1
         launches.add(1)
         return out

@@ -57,13 +57,15 @@ class TPGroup:
         dist.all_reduce(x, group=self.group)
         return x
 
-    def all_reduce_rmsnorm(self, x, residual, weight, eps, out=None):
-        """residual += allreduce(x); return rmsnorm(residual) * weight."""
+    def all_reduce_rmsnorm(self, x, residual, weight, eps, out=None, threads: int = 512):
+        """residual += allreduce(x); return rmsnorm(residual) * weight.
+        ``threads=256``: the half-size blocks that co-reside with a GEMM
+        (calls overlapped with compute on another stream)."""
         from .. import ops
 
         if self.world_size > 1 and self.ca_comm is not None and self.ca_comm.should_custom_ar(x) and \
                 x.numel() * 2 <= self.ca_comm.fused_rmsnorm_limit():
-            return self.ca_comm.all_reduce_rmsnorm(x, residual, weight, eps, out=out)
+            return self.ca_comm.all_reduce_rmsnorm(x, residual, weight, eps, out=out, threads=threads)
         x = self.all_reduce(x)
         return ops.fused_add_rmsnorm(x, residual, weight, eps, out=out)
 

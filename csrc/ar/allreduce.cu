@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 
 #include "../kernels.h"
 #include "ar_common.cuh"
@@ -40,16 +41,15 @@ MBX_DEVICE bool poisoned(const ArCtx& c) {
 }
 
 // --------------------------------------------------------------------------
-// One-shot push ("mailbox"): slot size = half / world.
+// One-shot push ("mailbox"): slot size = half / world (256-byte aligned).
 // --------------------------------------------------------------------------
 template <typename T, int W>
-__global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                     uint4* __restrict__ out, uint64_t nvec) {
+MBX_DEVICE void ar_oneshot_push(const ArCtx& c, const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
   trace_mark(c, 0);
   if (!poisoned(c)) {
-    const uint64_t slot = c.half_bytes / W;
+    const uint64_t slot = oneshot_slot_bytes(c.half_bytes, W);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     for (uint64_t i = i0; i < nvec; i += stride) {
@@ -79,12 +79,17 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, co
   finish_call(c, epoch);
 }
 
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                     uint4* __restrict__ out, uint64_t nvec) {
+  ar_oneshot_push<T, W>(c, in, out, nvec);
+}
+
 // --------------------------------------------------------------------------
 // One-shot pull.
 // --------------------------------------------------------------------------
 template <typename T, int W>
-__global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                     uint4* __restrict__ out, uint64_t nvec) {
+MBX_DEVICE void ar_oneshot_pull(const ArCtx& c, const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
   if (!poisoned(c)) {
@@ -111,6 +116,12 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, co
   finish_call(c, epoch);
 }
 
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                     uint4* __restrict__ out, uint64_t nvec) {
+  ar_oneshot_pull<T, W>(c, in, out, nvec);
+}
+
 // --------------------------------------------------------------------------
 // Two-shot: chunk c of the message is owned by rank c.
 //   A: copy input -> own slot0             B: owner reduces its chunk from all
@@ -119,8 +130,7 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, co
 // pairwise block barrier orders exactly the data each block consumes.
 // --------------------------------------------------------------------------
 template <typename T, int W>
-__global__ void __launch_bounds__(kArThreads) ar_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                uint4* __restrict__ out, uint64_t nvec) {
+MBX_DEVICE void ar_twoshot(const ArCtx& c, const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
   if (!poisoned(c)) {
@@ -163,6 +173,12 @@ done:
   finish_call(c, epoch);
 }
 
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                uint4* __restrict__ out, uint64_t nvec) {
+  ar_twoshot<T, W>(c, in, out, nvec);
+}
+
 // --------------------------------------------------------------------------
 // Two-shot, push-push: every NVLink byte is a posted store.
 //   A: element i of chunk ch is stored into owner ch's slot[rank]
@@ -174,8 +190,7 @@ done:
 constexpr int kU = 4;  // vectors in flight per thread per loop trip
 
 template <typename T, int W>
-__global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                     uint4* __restrict__ out, uint64_t nvec) {
+MBX_DEVICE void ar_twoshot_push(const ArCtx& c, const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
   trace_mark(c, 0);
@@ -266,6 +281,12 @@ __global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, co
 done:
   trace_mark(c, 5);
   finish_call(c, epoch);
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                     uint4* __restrict__ out, uint64_t nvec) {
+  ar_twoshot_push<T, W>(c, in, out, nvec);
 }
 
 // --------------------------------------------------------------------------
@@ -388,9 +409,8 @@ MBX_DEVICE float block_sum(float v, float* red) {
 // keeps this assignment, so the block-pairwise barriers between phases cover
 // every row. Inside a block, a normalisation phase works on one row with the
 // whole block (decode: few rows, lowest latency) or, when the block owns
-// several rows, on one row per warp (prefill: kRowWarps rows in flight, no
+// several rows, on one row per warp (prefill: one row in flight per warp, no
 // block-wide reductions).
-constexpr int kRowWarps = kArThreads / 32;
 
 struct RowCtx {
   int t0, tstep;  // this thread's first 16-byte vector of the row and its stride
@@ -409,7 +429,8 @@ MBX_DEVICE void for_norm_rows(int count, Fn fn) {
     fn(RowCtx{(int)threadIdx.x, (int)blockDim.x, false}, 0);
     return;
   }
-  for (int k = threadIdx.x >> 5; k < count; k += kRowWarps) fn(RowCtx{(int)(threadIdx.x & 31), 32, true}, k);
+  const int warps = (int)(blockDim.x >> 5);
+  for (int k = threadIdx.x >> 5; k < count; k += warps) fn(RowCtx{(int)(threadIdx.x & 31), 32, true}, k);
 }
 
 // Copy/reduce phases over the block's rows (row j = b + j*g of a range):
@@ -533,16 +554,14 @@ MBX_DEVICE void for_owner_norm_rows(int M, int Mo, Fn fn) {
 }
 
 template <int W>
-__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_oneshot_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                        uint4* residual, const uint4* __restrict__ w,
-                                                                        uint4* __restrict__ out, int M, int H,
-                                                                        float eps) {
+MBX_DEVICE void ar_rmsnorm_oneshot(const ArCtx& c, const uint4* __restrict__ in, uint4* residual,
+                                   const uint4* __restrict__ w, uint4* __restrict__ out, int M, int H, float eps) {
   __shared__ bool s_ok;
   __shared__ float red[32];
   const uint32_t epoch = call_epoch(c);
   const int hvec = H / 8;
   if (!poisoned(c)) {
-    const uint64_t slot = c.half_bytes / W;
+    const uint64_t slot = oneshot_slot_bytes(c.half_bytes, W);
     const int nrows = block_rows(M);
     const int b = blockIdx.x, g = gridDim.x;
     reduce_block_vectors<1>(
@@ -567,10 +586,16 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_oneshot_kernel(ArCtx c,
 }
 
 template <int W>
-__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
+__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_oneshot_kernel(ArCtx c, const uint4* __restrict__ in,
                                                                         uint4* residual, const uint4* __restrict__ w,
                                                                         uint4* __restrict__ out, int M, int H,
                                                                         float eps) {
+  ar_rmsnorm_oneshot<W>(c, in, residual, w, out, M, H, eps);
+}
+
+template <int W>
+MBX_DEVICE void ar_rmsnorm_twoshot(const ArCtx& c, const uint4* __restrict__ in, uint4* residual,
+                                   const uint4* __restrict__ w, uint4* __restrict__ out, int M, int H, float eps) {
   __shared__ bool s_ok;
   __shared__ float red[32];
   const uint32_t epoch = call_epoch(c);
@@ -612,6 +637,14 @@ done:
   finish_call(c, epoch);
 }
 
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                        uint4* residual, const uint4* __restrict__ w,
+                                                                        uint4* __restrict__ out, int M, int H,
+                                                                        float eps) {
+  ar_rmsnorm_twoshot<W>(c, in, residual, w, out, M, H, eps);
+}
+
 // --------------------------------------------------------------------------
 // Fused row-parallel GEMM -> allreduce -> residual + RMSNorm, second half.
 // The GEMM epilogue (gemm.cu, push-RS mode) has stored every rank's partial
@@ -628,9 +661,8 @@ MBX_DEVICE char* fuse_half(const ArCtx& c, char* base, uint32_t epoch) {
 MBX_DEVICE uint32_t* fuse_flag(char* base, int src) { return reinterpret_cast<uint32_t*>(base + kTileFlagOff) + src; }
 
 template <int W>
-__global__ void __launch_bounds__(kArThreads) fused_rs_norm_kernel(ArCtx c, int M, int N, int Mo, uint4* residual,
-                                                                   const uint4* __restrict__ w,
-                                                                   uint4* __restrict__ out, float eps) {
+MBX_DEVICE void fused_rs_norm(const ArCtx& c, int M, int N, int Mo, uint4* residual, const uint4* __restrict__ w,
+                              uint4* __restrict__ out, float eps) {
   __shared__ bool s_ok;
   __shared__ float red[32];
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
@@ -672,6 +704,13 @@ __global__ void __launch_bounds__(kArThreads) fused_rs_norm_kernel(ArCtx c, int 
   }
 done:
   finish_call(c, epoch, kStFuseEpoch, kStFuseDone);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) fused_rs_norm_kernel(ArCtx c, int M, int N, int Mo, uint4* residual,
+                                                                   const uint4* __restrict__ w,
+                                                                   uint4* __restrict__ out, float eps) {
+  fused_rs_norm<W>(c, M, N, Mo, residual, w, out, eps);
 }
 
 // --------------------------------------------------------------------------
@@ -825,11 +864,8 @@ __global__ void sp_ag_wait_kernel(ArCtx c, int owners) {
 // Rows are owned in contiguous blocks of Mo = ceil(M / W).
 // --------------------------------------------------------------------------
 template <int W>
-__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                             uint4* residual,
-                                                                             const uint4* __restrict__ w,
-                                                                             uint4* __restrict__ out, int M, int H,
-                                                                             float eps) {
+MBX_DEVICE void ar_rmsnorm_twoshot_push(const ArCtx& c, const uint4* __restrict__ in, uint4* residual,
+                                        const uint4* __restrict__ w, uint4* __restrict__ out, int M, int H, float eps) {
   __shared__ bool s_ok;
   __shared__ float red[32];
   const uint32_t epoch = call_epoch(c);
@@ -876,6 +912,15 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_push_kernel(ArC
   }
 done:
   finish_call(c, epoch);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                             uint4* residual,
+                                                                             const uint4* __restrict__ w,
+                                                                             uint4* __restrict__ out, int M, int H,
+                                                                             float eps) {
+  ar_rmsnorm_twoshot_push<W>(c, in, residual, w, out, M, H, eps);
 }
 
 // --------------------------------------------------------------------------
@@ -996,13 +1041,12 @@ __global__ void __launch_bounds__(kArThreads) seg_wait_kernel(ArCtx c, const uin
 // by the vocab-parallel argmax combine and the sequence-parallel paths.
 // --------------------------------------------------------------------------
 template <int W>
-__global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const uint4* __restrict__ in,
-                                                                  uint4* __restrict__ out, uint64_t nvec) {
+MBX_DEVICE void ar_allgather(const ArCtx& c, const uint4* __restrict__ in, uint4* __restrict__ out, uint64_t nvec) {
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
   trace_mark(c, 0);
   if (!poisoned(c)) {
-    const uint64_t slot = c.half_bytes / W;
+    const uint64_t slot = oneshot_slot_bytes(c.half_bytes, W);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     for (uint64_t i = i0; i < nvec; i += stride) {
@@ -1024,6 +1068,12 @@ __global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const
     }
   }
   finish_call(c, epoch);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const uint4* __restrict__ in,
+                                                                  uint4* __restrict__ out, uint64_t nvec) {
+  ar_allgather<W>(c, in, out, nvec);
 }
 
 // --------------------------------------------------------------------------
@@ -1146,7 +1196,7 @@ static inline int ar_grid(uint64_t work_vec, int max_blocks) {
 // Largest message (bytes) one launch of `algo` can carry through the buffer.
 uint64_t ar_chunk_limit(const ArCtx& c, int algo) {
   switch (algo) {
-    case kOneShotPush: return (c.half_bytes / c.world) & ~uint64_t(15);
+    case kOneShotPush: return oneshot_slot_bytes(c.half_bytes, c.world);
     case kOneShotPull: return c.half_bytes & ~uint64_t(15);
     case kTwoShot:
     case kNvls: return (c.half_bytes / 2) & ~uint64_t(15);
@@ -1189,8 +1239,9 @@ void ar_launch(const ArCtx& c, int algo, int dtype, const void* in, void* out, u
 }
 
 void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual, const void* weight, void* out,
-                       int M, int H, float eps, int max_blocks, cudaStream_t stream) {
+                       int M, int H, float eps, int max_blocks, cudaStream_t stream, int threads) {
   if (H % 8 != 0) throw std::runtime_error("ar_rmsnorm: hidden size must be a multiple of 8");
+  if (threads != 256 && threads != kArThreads) throw std::runtime_error("ar_rmsnorm: threads must be 256 or 512");
   const uint64_t bytes = (uint64_t)M * H * 2;
   const int g = std::max(1, std::min(M, std::min(max_blocks, (int)kMaxBlocks)));
   const int W_ = c.world;
@@ -1200,16 +1251,16 @@ void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual,
   auto o4 = static_cast<uint4*>(out);
   if (algo == kOneShotPush) {
     if (bytes > ar_chunk_limit(c, kOneShotPush)) throw std::runtime_error("ar_rmsnorm: message exceeds one-shot slot");
-    MBX_DISPATCH_W1(W_, ar_rmsnorm_oneshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W1(W_, ar_rmsnorm_oneshot_kernel<W><<<g, threads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
   } else if (algo == kTwoShotPush) {
     const int Mo = (M + W_ - 1) / W_;
     if ((uint64_t)W_ * Mo * H * 2 + bytes > c.half_bytes)
       throw std::runtime_error("ar_rmsnorm: message exceeds the two-shot buffer");
     const int gp = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
-    MBX_DISPATCH_W1(W_, ar_rmsnorm_twoshot_push_kernel<W><<<gp, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W1(W_, ar_rmsnorm_twoshot_push_kernel<W><<<gp, threads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
   } else {
     if (bytes > ar_chunk_limit(c, kTwoShot)) throw std::runtime_error("ar_rmsnorm: message exceeds two-shot slot");
-    MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_kernel<W><<<g, kArThreads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_kernel<W><<<g, threads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
   }
   MBX_CUDA_CHECK(cudaGetLastError());
 }
@@ -1322,6 +1373,104 @@ void raw_transport_launch(int kind, void* dst, const void* src, uint64_t nbytes,
     default: throw std::runtime_error("raw transport: unknown kind");
   }
   MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+
+// --------------------------------------------------------------------------
+// One-GPU emulation of a W-rank call, for tests and single-GPU profiling.
+// Kernels that wait on one another cannot run as separate launches on one
+// GPU: nothing makes them co-resident. So every emulated rank's blocks run in
+// ONE cooperative launch (co-residency guaranteed, or the launch is refused):
+// blockIdx.y is the rank, blockIdx.x / gridDim.x keep their per-rank meaning,
+// and each rank brings its own context (symmetric buffers of all emulated
+// ranks, its own state and status words). The device code is the same body
+// the multi-GPU launch runs; only the memory behind the "peer" pointers is
+// local.
+// --------------------------------------------------------------------------
+template <typename T, int W>
+__global__ void __launch_bounds__(kArThreads) ar_emulated_kernel(const EmuRank* __restrict__ ranks, int op, int algo,
+                                                                 uint64_t nvec, int M, int N, float eps) {
+  const EmuRank& er = ranks[blockIdx.y];
+  const ArCtx c = er.c;
+  const uint4* in = static_cast<const uint4*>(er.in);
+  uint4* out = static_cast<uint4*>(er.out);
+  uint4* res = static_cast<uint4*>(er.residual);
+  const uint4* w = static_cast<const uint4*>(er.weight);
+  if (op == kEmuAllreduce) {
+    switch (algo) {
+      case kOneShotPush: ar_oneshot_push<T, W>(c, in, out, nvec); break;
+      case kOneShotPull: ar_oneshot_pull<T, W>(c, in, out, nvec); break;
+      case kTwoShot: ar_twoshot<T, W>(c, in, out, nvec); break;
+      case kTwoShotPush: ar_twoshot_push<T, W>(c, in, out, nvec); break;
+    }
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (op == kEmuArRmsnorm) {
+      if (algo == kOneShotPush) ar_rmsnorm_oneshot<W>(c, in, res, w, out, M, N, eps);
+      else if (algo == kTwoShotPush) ar_rmsnorm_twoshot_push<W>(c, in, res, w, out, M, N, eps);
+      else ar_rmsnorm_twoshot<W>(c, in, res, w, out, M, N, eps);
+    } else if (op == kEmuFusedRsNorm) {
+      fused_rs_norm<W>(c, M, N, (M + W - 1) / W, res, w, out, eps);
+    } else if (op == kEmuAllgather) {
+      ar_allgather<W>(c, in, out, nvec);
+    }
+  }
+}
+
+void ar_emulated_launch(const EmuRank* ranks_host, int world, int op, int algo, int dtype, uint64_t nbytes, int M,
+                        int N, float eps, int blocks, void* dev_scratch, cudaStream_t stream) {
+  if (world < 2 || world > kMaxRanks) throw std::runtime_error("emulated allreduce: world must be 2..8");
+  if (nbytes % 16 != 0) throw std::runtime_error("emulated allreduce: byte size must be a multiple of 16");
+  if (op == kEmuAllreduce) {
+    if (algo != kOneShotPush && algo != kOneShotPull && algo != kTwoShot && algo != kTwoShotPush)
+      throw std::runtime_error("emulated allreduce: algorithm must be one-shot push/pull or two-shot (push)");
+    if (nbytes > ar_chunk_limit(ranks_host[0].c, algo))
+      throw std::runtime_error("emulated allreduce: message exceeds one launch of the algorithm");
+  } else if (dtype != kBF16) {
+    throw std::runtime_error("emulated fused kernels are bf16 only");
+  } else if (op == kEmuArRmsnorm || op == kEmuFusedRsNorm) {
+    if (N % 8 != 0 || M < 1) throw std::runtime_error("emulated norm: bad shape");
+    const uint64_t bytes = (uint64_t)M * N * 2;
+    const int Mo = (M + world - 1) / world;
+    const ArCtx& c0 = ranks_host[0].c;
+    if (op == kEmuFusedRsNorm) {
+      if ((uint64_t)world * Mo * N * 2 + bytes > c0.fuse_half_bytes)
+        throw std::runtime_error("emulated fused reduce: rows exceed the fused buffer");
+    } else if (algo == kOneShotPush) {
+      if (bytes > ar_chunk_limit(c0, kOneShotPush)) throw std::runtime_error("emulated norm: exceeds one-shot slot");
+    } else if (algo == kTwoShotPush) {
+      if ((uint64_t)world * Mo * N * 2 + bytes > c0.half_bytes)
+        throw std::runtime_error("emulated norm: exceeds the two-shot buffer");
+    } else if (bytes > ar_chunk_limit(c0, kTwoShot)) {
+      throw std::runtime_error("emulated norm: exceeds two-shot slot");
+    }
+  } else if (op == kEmuAllgather) {
+    if (nbytes > ar_chunk_limit(ranks_host[0].c, kOneShotPush))
+      throw std::runtime_error("emulated all-gather: message exceeds slot");
+  } else {
+    throw std::runtime_error("emulated allreduce: unknown op");
+  }
+  if (dtype != kBF16 && dtype != kF32) throw std::runtime_error("emulated allreduce: dtype must be bf16 or fp32");
+  if (blocks < 1 || blocks > kMaxBlocks) throw std::runtime_error("emulated allreduce: bad block count");
+  MBX_CUDA_CHECK(cudaMemcpyAsync(dev_scratch, ranks_host, sizeof(EmuRank) * world, cudaMemcpyHostToDevice, stream));
+  const EmuRank* ranks = static_cast<const EmuRank*>(dev_scratch);
+  uint64_t nvec = nbytes / 16;
+  dim3 grid(blocks, world);
+  void* args[] = {&ranks, &op, &algo, &nvec, &M, &N, &eps};
+  auto go = [&](const void* fn) {
+    MBX_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, grid, dim3(kArThreads), args, 0, stream));
+  };
+  const bool f32 = dtype == kF32;
+  auto pick = [&](auto wc) -> const void* {
+    constexpr int W = decltype(wc)::value;
+    return f32 ? (const void*)ar_emulated_kernel<float, W> : (const void*)ar_emulated_kernel<__nv_bfloat16, W>;
+  };
+  switch (world) {
+    case 2: go(pick(std::integral_constant<int, 2>{})); break;
+    case 3: go(pick(std::integral_constant<int, 3>{})); break;
+    case 4: go(pick(std::integral_constant<int, 4>{})); break;
+    case 8: go(pick(std::integral_constant<int, 8>{})); break;
+    default: throw std::runtime_error("emulated allreduce: world sizes 2, 3, 4 and 8");
+  }
 }
 
 }  // namespace mbx

@@ -42,6 +42,14 @@ constexpr size_t kAgFlagOff = kTileFlagOff + sizeof(uint32_t) * 64;
 static_assert(kTileFlagOff + sizeof(uint32_t) * kTileFlagSlots * kMaxRanks <= kSigBytes,
               "signal area overflow");
 
+// One rank's slot of a one-shot half: half / world rounded down to 256 bytes.
+// Every slot must start 16-byte aligned for the vector stores whatever the
+// world size (half / 3 of a power of two is not even a multiple of 16).
+// constexpr, so host code and device code (--expt-relaxed-constexpr) share it.
+constexpr uint64_t oneshot_slot_bytes(uint64_t half_bytes, int world) {
+  return (half_bytes / (uint64_t)world) & ~uint64_t(255);
+}
+
 // Device-local (not symmetric) state words.
 enum StateWord : int {
   kStEpoch = 0,     // epoch of the last completed allreduce call

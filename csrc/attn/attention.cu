@@ -560,11 +560,8 @@ void prefill_attention_launch(const void* q, const void* kc, const void* vc, voi
   a.nkv = nkv;
   a.scale_log2 = scale * 1.4426950408889634f;
   const int smem = 5 * 16384;
-  static bool attr = false;
-  if (!attr) {
-    MBX_CUDA_CHECK(cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static SmemLimit limit;
+  limit.ensure((const void*)prefill_attention_kernel, smem);
   dim3 grid(n_tiles, nq);
   prefill_attention_kernel<<<grid, kAttnThreads, smem, s>>>(a);
   MBX_CUDA_CHECK(cudaGetLastError());
@@ -599,11 +596,8 @@ void decode_attention_launch(const void* q, const void* kc, const void* vc, void
   a.part_o = part_o;
   a.part_lse = part_lse;
   if (a.splits > 1 && (!part_o || !part_lse)) throw std::runtime_error("decode: split-KV needs scratch buffers");
-  static bool attr = false;
-  if (!attr) {
-    MBX_CUDA_CHECK(cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem));
-    attr = true;
-  }
+  static SmemLimit limit;
+  limit.ensure((const void*)decode_attention_kernel, kDecSmem);
   dim3 grid(a.splits, nkv, B);
   decode_attention_kernel<<<grid, kDecThreads, kDecSmem, s>>>(a);
   MBX_CUDA_CHECK(cudaGetLastError());

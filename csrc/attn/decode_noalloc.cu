@@ -69,7 +69,7 @@ extern "C" __attribute__((visibility("default"))) int mbx_decode_attention_noall
   if (batch < 0 || q_heads <= 0 || kv_heads <= 0 || max_blocks <= 0 || splits < 1)
     return fail(1, "mbx_decode_attention_noalloc: bad sizes (need batch >= 0, heads > 0, splits >= 1)");
   const size_t rows = (size_t)batch * (size_t)q_heads * (size_t)splits;
-  if (rows > kMaxRows) {
+  if (splits > 1 && rows > kMaxRows) {
     char msg[256];
     std::snprintf(msg, sizeof(msg),
                   "mbx_decode_attention_noalloc: batch*q_heads*splits = %zu exceeds the fixed scratch of %zu rows; "
@@ -78,11 +78,14 @@ extern "C" __attribute__((visibility("default"))) int mbx_decode_attention_noall
     return fail(2, msg);
   }
   if (batch == 0) return 0;
+  // one split writes the output directly and needs no scratch
   DeviceScratch* s = nullptr;
-  if (int rc = scratch_for_current_device(&s)) return rc;
+  if (splits > 1) {
+    if (int rc = scratch_for_current_device(&s)) return rc;
+  }
   try {
     mbx::decode_attention_launch(q, k_cache, v_cache, out, kv_len, block_table, max_blocks, batch, q_heads,
-                                 kv_heads, splits, splits > 1 ? s->o : nullptr, splits > 1 ? s->lse : nullptr, scale,
+                                 kv_heads, splits, s ? s->o : nullptr, s ? s->lse : nullptr, scale,
                                  static_cast<cudaStream_t>(stream));
   } catch (const std::exception& ex) {
     return fail(4, ex.what());

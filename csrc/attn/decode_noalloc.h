@@ -18,9 +18,11 @@
 // output.
 //
 // Limits: the scratch holds at most MBX_NOALLOC_MAX_PARTIAL_ROWS rows of
-// partial results, i.e. batch * q_heads * splits <= 16384 (8 MiB of fp32
-// partial outputs plus 256 KiB of log-sum-exps per GPU). Larger requests are
-// rejected with error code 2 and a message from mbx_noalloc_last_error().
+// partial results, i.e. batch * q_heads * splits <= 16384 when splits > 1
+// (8 MiB of fp32 partial outputs plus 64 KiB of log-sum-exps per GPU). With
+// splits == 1 the kernel writes the output directly, uses no scratch and has
+// no such limit. Larger split requests are rejected with error code 2 and a
+// message from mbx_noalloc_last_error().
 //
 // Rules for callers:
 //  * The first call on each device looks up the array's device address (with
@@ -29,7 +31,10 @@
 //    (different streams, or different host threads on the same device) race
 //    on it; serialise them. Each call overwrites every partial it reads, so
 //    nothing has to be cleared between calls.
-//  * Return value: 0 on success, non-zero on error (see mbx_noalloc_last_error).
+//  * Return value: 0 on success, non-zero on error (see mbx_noalloc_last_error):
+//    1 null pointer or bad size, 2 scratch too small for the split count,
+//    3 CUDA runtime error while looking up the scratch, 4 launch refused
+//    (e.g. q_heads not a multiple of kv_heads, or a group above 16 heads).
 #pragma once
 #include <stddef.h>
 #include <stdint.h>

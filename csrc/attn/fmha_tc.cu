@@ -491,11 +491,8 @@ void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, 
   a.part_o = part_o;
   a.part_lse = part_lse;
   if (a.splits > 1 && (!part_o || !part_lse)) throw std::runtime_error("fmha: split-KV needs scratch buffers");
-  static bool attr = false;
-  if (!attr) {
-    MBX_CUDA_CHECK(cudaFuncSetAttribute(fmha_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::kTotal));
-    attr = true;
-  }
+  static SmemLimit limit;
+  limit.ensure((const void*)fmha_tc_kernel, Smem::kTotal);
   dim3 grid(n_tiles, nq, a.splits);
   fmha_tc_kernel<<<grid, kThreads, Smem::kTotal, s>>>(tq, tk, tv, a);
   MBX_CUDA_CHECK(cudaGetLastError());

@@ -36,6 +36,8 @@ class ArComm {
          uint64_t fuse_half_bytes, uint64_t sp_bytes)
       : status_host_(reinterpret_cast<volatile uint32_t*>(status_host)) {
     TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)bufs.size() == world, "ArComm: bad world size");
+    TORCH_CHECK(half_bytes % 4096 == 0 && fuse_half_bytes % 4096 == 0 && seg_slot_bytes % 256 == 0,
+                "ArComm: buffer regions must be multiples of 4 KiB (segment slots of 256 B)");
     std::memset(&c_, 0, sizeof(c_));
     for (int i = 0; i < world; ++i) c_.bufs[i] = reinterpret_cast<char*>(bufs[i]);
     c_.mc = reinterpret_cast<char*>(mc);
@@ -60,10 +62,10 @@ class ArComm {
               stream_of(stream));
   }
   void ar_rmsnorm(int64_t in, int64_t residual, int64_t weight, int64_t out, int M, int H, double eps, int algo,
-                  int max_blocks, int64_t stream) {
+                  int max_blocks, int64_t stream, int threads) {
     ar_rmsnorm_launch(c_, algo, reinterpret_cast<const void*>(in), reinterpret_cast<void*>(residual),
                       reinterpret_cast<const void*>(weight), reinterpret_cast<void*>(out), M, H, (float)eps,
-                      max_blocks, stream_of(stream));
+                      max_blocks, stream_of(stream), threads);
   }
   void allgather(int64_t in, int64_t out, uint64_t nbytes, int max_blocks, int64_t stream) {
     ar_allgather_launch(c_, reinterpret_cast<const void*>(in), reinterpret_cast<void*>(out), nbytes, max_blocks,
@@ -91,6 +93,20 @@ class ArComm {
                            reinterpret_cast<uint32_t*>(err.data_ptr<int>()), max_blocks, push_all, cur_stream());
   }
   uint64_t fused_capacity() const { return c_.fuse_half_bytes; }
+  // The two launches of gemm_ar_rmsnorm one at a time (one-GPU emulation of
+  // the ranks runs every rank's GEMM before any rank's reduction).
+  void gemm_push(torch::Tensor a, torch::Tensor w, torch::Tensor err, bool push_all) {
+    check_bf16(a, "a");
+    check_bf16(w, "w");
+    TORCH_CHECK(w.size(1) == a.size(1), "gemm_push: K mismatch");
+    gemm_push_launch(c_, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), a.size(0), w.size(0), a.size(1),
+                     push_all, reinterpret_cast<uint32_t*>(err.data_ptr<int>()), cur_stream());
+  }
+  void fused_allsum_norm(int M, int N, int64_t residual, int64_t weight, int64_t out, double eps, int max_blocks) {
+    fused_allsum_norm_launch(c_, M, N, reinterpret_cast<void*>(residual), reinterpret_cast<const void*>(weight),
+                             reinterpret_cast<void*>(out), (float)eps, max_blocks, cur_stream());
+  }
+  const ArCtx& ctx() const { return c_; }
 
   // ---- sequence parallel (rank r owns rows [r*Mo, r*Mo+Mo), Mo = ceil(M/world))
   void gemm_rs(torch::Tensor a, torch::Tensor w, torch::Tensor err) {
@@ -485,12 +501,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("sp_gather_ptr", &ArComm::sp_gather_ptr)
       .def("sp_capacity", &ArComm::sp_capacity)
       .def("gemm_ar_rmsnorm", &ArComm::gemm_ar_rmsnorm)
+      .def("gemm_push", &ArComm::gemm_push)
+      .def("fused_allsum_norm", &ArComm::fused_allsum_norm)
       .def("fused_capacity", &ArComm::fused_capacity)
       .def("set_trace", &ArComm::set_trace)
       .def("allreduce", &ArComm::allreduce, py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("dtype"),
            py::arg("algo"), py::arg("max_blocks"), py::arg("stream"))
       .def("ar_rmsnorm", &ArComm::ar_rmsnorm, py::arg("inp"), py::arg("residual"), py::arg("weight"), py::arg("out"),
-           py::arg("M"), py::arg("H"), py::arg("eps"), py::arg("algo"), py::arg("max_blocks"), py::arg("stream"))
+           py::arg("M"), py::arg("H"), py::arg("eps"), py::arg("algo"), py::arg("max_blocks"), py::arg("stream"),
+           py::arg("threads") = 512)
       .def("allgather", &ArComm::allgather, py::arg("inp"), py::arg("out"), py::arg("nbytes"), py::arg("max_blocks"),
            py::arg("stream"))
       .def("seg_submit", &ArComm::seg_submit, py::arg("inp"), py::arg("nbytes"), py::arg("max_blocks"),
@@ -519,6 +538,36 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("dst"), py::arg("src"), py::arg("nbytes"), py::arg("stream"));
 
+  m.def(
+      "ar_emulated",
+      [](std::vector<ArComm*> comms, int op, int algo, int dtype, std::vector<int64_t> ins, std::vector<int64_t> outs,
+         std::vector<int64_t> residuals, int64_t weight, uint64_t nbytes, int M, int N, double eps, int blocks,
+         int64_t scratch, int64_t scratch_bytes) {
+        const int W = (int)comms.size();
+        TORCH_CHECK(W >= 2 && W <= kMaxRanks && (int)ins.size() == W && (int)outs.size() == W,
+                    "ar_emulated: one input and output per rank");
+        TORCH_CHECK(residuals.empty() || (int)residuals.size() == W, "ar_emulated: one residual per rank");
+        TORCH_CHECK((uint64_t)scratch_bytes >= sizeof(EmuRank) * W, "ar_emulated: scratch too small");
+        std::vector<EmuRank> r(W);
+        for (int i = 0; i < W; ++i) {
+          r[i].c = comms[i]->ctx();
+          TORCH_CHECK(r[i].c.rank == i && r[i].c.world == W, "ar_emulated: comms must be ranks 0..W-1 of one world");
+          r[i].in = reinterpret_cast<const void*>(ins[i]);
+          r[i].out = reinterpret_cast<void*>(outs[i]);
+          r[i].residual = residuals.empty() ? nullptr : reinterpret_cast<void*>(residuals[i]);
+          r[i].weight = reinterpret_cast<const void*>(weight);
+        }
+        ar_emulated_launch(r.data(), W, op, algo, dtype, nbytes, M, N, (float)eps, blocks,
+                           reinterpret_cast<void*>(scratch), cur_stream());
+      },
+      py::arg("comms"), py::arg("op"), py::arg("algo"), py::arg("dtype"), py::arg("ins"), py::arg("outs"),
+      py::arg("residuals"), py::arg("weight"), py::arg("nbytes"), py::arg("M"), py::arg("N"), py::arg("eps"),
+      py::arg("blocks"), py::arg("scratch"), py::arg("scratch_bytes"));
+  m.attr("EMU_ALLREDUCE") = (int)kEmuAllreduce;
+  m.attr("EMU_AR_RMSNORM") = (int)kEmuArRmsnorm;
+  m.attr("EMU_FUSED_RS_NORM") = (int)kEmuFusedRsNorm;
+  m.attr("EMU_ALLGATHER") = (int)kEmuAllgather;
+  m.attr("EMU_RANK_BYTES") = (int)sizeof(EmuRank);
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("residual"), py::arg("workspace"),
         py::arg("err"), py::arg("bn") = 0, py::arg("splits") = 0, py::arg("counters") = c10::nullopt);
   m.def("gemm_plan", &gemm_plan_py, py::arg("M"), py::arg("N"), py::arg("K"));

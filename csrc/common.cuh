@@ -11,6 +11,11 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
 #define MBX_DEVICE __device__ __forceinline__
 
 #define MBX_CUDA_CHECK(expr)                                                    \
@@ -24,6 +29,28 @@
   } while (0)
 
 namespace mbx {
+
+// Raises one kernel's dynamic shared-memory limit on every device it runs on.
+// The attribute belongs to a device, so a process that launches on several
+// GPUs must set it on each of them: one record per launch site (a function-
+// local static), bit d set once device d has it. The lock orders host threads
+// that reach the same site at once; after the first launch on a device the
+// check is one atomic load.
+struct SmemLimit {
+  std::atomic<uint64_t> done{0};
+  std::mutex mu;
+  void ensure(const void* kernel, int bytes) {
+    int dev = 0;
+    MBX_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw std::runtime_error("device index out of range for the kernel attribute record");
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return;
+    std::lock_guard<std::mutex> g(mu);
+    if (done.load(std::memory_order_relaxed) & bit) return;
+    MBX_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit, std::memory_order_release);
+  }
+};
 
 // dtype ids shared with Python (same numbering as the reference's dtype_id:
 // 0 = fp32, 1 = fp16, 2 = bf16).

@@ -773,11 +773,8 @@ template <int BN, int STAGES, int EPI>
 void launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
   using L = Smem2<BN, STAGES>;
   auto kern = gemm2_tcgen05_kernel<BN, STAGES, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    MBX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
-    attr_set = true;
-  }
+  static SmemLimit limit;
+  limit.ensure((const void*)kern, L::kTotal);
   kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, a);
 }
 
@@ -785,11 +782,8 @@ template <int BN, int STAGES, int EPI>
 void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
   using L = Smem<BN, STAGES, EPI == kEpiPushRS>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    MBX_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
-    attr_set = true;
-  }
+  static SmemLimit limit;
+  limit.ensure((const void*)kern, L::kTotal);
   kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, a);
 }
 
@@ -919,6 +913,18 @@ void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const vo
   launch_push_gemm(c, A, lda, B, ldb, M, N, K, Mo, push_all, err, s);
   if (push_all) fused_allsum_norm_launch(c, (int)M, (int)N, residual, norm_w, out, eps, max_blocks, s);
   else fused_rs_norm_launch(c, (int)M, (int)N, (int)Mo, residual, norm_w, out, eps, max_blocks, s);
+}
+
+void gemm_push_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                      int64_t K, bool push_all, uint32_t* err, cudaStream_t s) {
+  if (M == 0) return;
+  if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm_push: K and N must be multiples of 8");
+  const int W = c.world;
+  const int64_t Mo = (M + W - 1) / W;
+  const uint64_t need = push_all ? (uint64_t)W * M * N * 2 : (uint64_t)W * Mo * N * 2 + (uint64_t)M * N * 2;
+  if (c.fuse_half_bytes == 0 || need > c.fuse_half_bytes)
+    throw std::runtime_error("gemm_push: message exceeds the fused buffer");
+  launch_push_gemm(c, A, lda, B, ldb, M, N, K, Mo, push_all, err, s);
 }
 
 void gemm_rs_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,

@@ -15,8 +15,10 @@ namespace mbx {
 uint64_t ar_chunk_limit(const ArCtx& c, int algo);
 void ar_launch(const ArCtx& c, int algo, int dtype, const void* in, void* out, uint64_t nbytes, int max_blocks,
                cudaStream_t stream);
+// threads: 512 (default) or 256 per block; 256 halves a block's registers so
+// it fits on an SM beside a running GEMM CTA (overlapped micro-batches).
 void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual, const void* weight, void* out, int M,
-                       int H, float eps, int max_blocks, cudaStream_t stream);
+                       int H, float eps, int max_blocks, cudaStream_t stream, int threads = 512);
 void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nbytes, int max_blocks,
                          cudaStream_t stream);
 // Second launch of the fused GEMM->allreduce->RMSNorm (reduce own rows,
@@ -29,6 +31,20 @@ void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, cons
 void seg_submit_launch(const ArCtx& c, const void* in, uint64_t nbytes, int max_blocks, cudaStream_t stream);
 void seg_wait_launch(const ArCtx& c, int dtype, const void* local, void* out, uint64_t nbytes, int max_blocks,
                      cudaStream_t stream);
+// One-GPU emulation of a W-rank call (tests and single-GPU profiling): every
+// rank's blocks in one cooperative launch, rank = blockIdx.y, each with its
+// own context whose "peer" buffers are local allocations. `dev_scratch` is
+// device memory for the world x EmuRank array (copied on `stream`).
+enum EmuOp : int { kEmuAllreduce = 0, kEmuArRmsnorm = 1, kEmuFusedRsNorm = 2, kEmuAllgather = 3 };
+struct EmuRank {
+  ArCtx c;
+  const void* in;      // allreduce / all-gather input, or the norm input
+  void* out;
+  void* residual;      // norm ops: residual updated in place
+  const void* weight;  // norm ops: RMSNorm weight
+};
+void ar_emulated_launch(const EmuRank* ranks_host, int world, int op, int algo, int dtype, uint64_t nbytes, int M,
+                        int N, float eps, int blocks, void* dev_scratch, cudaStream_t stream);
 // Raw NVLink transport kernels for bandwidth benchmarks. kMcReduce* read the
 // multicast address `src` and write local `dst`; kMcStore reads local `src`
 // and stores to the multicast address `dst`.
@@ -103,6 +119,11 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 void gemm_ar_rmsnorm_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M,
                             int64_t N, int64_t K, void* residual, const void* norm_w, void* out, float eps,
                             uint32_t* err, int max_blocks, bool push_all, cudaStream_t s);
+
+// The first launch of gemm_ar_rmsnorm_launch alone (one-GPU emulation of the
+// ranks: each rank's GEMM pushes into every emulated rank's fused buffer).
+void gemm_push_launch(const ArCtx& c, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t M, int64_t N,
+                      int64_t K, bool push_all, uint32_t* err, cudaStream_t s);
 
 // ---- sequence parallel (gemm/gemm.cu, ar/allreduce.cu) ---------------------
 // Rank r owns rows [r*Mo, r*Mo+Mo) of the residual stream, Mo = ceil(M/world).

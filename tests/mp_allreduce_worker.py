@@ -302,6 +302,34 @@ def main():
     torch.cuda.synchronize()
     assert ar.err() == 0, ar.status()
     log(f"engine sequence-parallel OK (min cosine {cos:.5f})")
+
+    # 8b. engine: overlapped micro-batches (two streams, collectives of one
+    #     micro-batch under the other's compute) == the plain forward, for a
+    #     512-token chunk split 256/256 and a 700-token one split 256/444
+    eng.model.sp = None
+    eng.model.enable_overlap(min_rows=256)
+    assert eng.model.overlap_split(512) == 256 and eng.model.overlap_split(700) == 256
+    bt = eng.block_table[req.slot:req.slot + 1]
+    for n in (512, 700):
+        ids = torch.tensor(prompt[:n], dtype=torch.int32, device=dev)
+        pos = torch.arange(0, n, dtype=torch.int32, device=dev)
+        sl = torch.tensor(slots[:n], dtype=torch.int64, device=dev)
+        cu = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        kvl = torch.tensor([n], dtype=torch.int32, device=dev)
+        tiles = ops.prefill_tiles([n]).to(dev)
+        every = torch.arange(n, dtype=torch.int64, device=dev)
+        attn = lambda li, q, kc, vc: ops.prefill_attention(q, kc, vc, cu, kvl, bt, tiles, eng.model.scale)  # noqa
+        plain = eng.model.forward(ids, pos, sl, eng.kv.caches, attn, every, return_hidden=True).float()
+        halves = eng._attn_halves([n], [n], bt, n)
+        assert halves is not None and halves[0] == 256
+        for rep in range(3):
+            ov = eng.model.forward(ids, pos, sl, eng.kv.caches, attn, every, return_hidden=True,
+                                   attn_halves=halves).float()
+            torch.cuda.synchronize()
+            cos = torch.nn.functional.cosine_similarity(ov, plain, dim=1).min().item()
+            assert cos > 0.9999, f"overlap vs plain hidden cosine {cos} (n={n}, rep {rep})"
+    assert ar.err() == 0, ar.status()
+    log(f"engine overlapped micro-batches OK (min cosine {cos:.6f})")
     tp.close()
 
     # 9. host-side fault injection in the GPU handshakes: one rank's local

@@ -66,4 +66,4 @@ def test_multi_gpu_allreduce_suite():
     err_at = out.find("WORKER-ERROR")
     detail = out[err_at:err_at + 6000] if err_at >= 0 else out[-4000:]
     assert p.returncode == 0, detail
-    assert "ALLREDUCE-SUITE-PASS" in p.stdout, tail
+    assert "ALLREDUCE-SUITE-PASS" in p.stdout, detail

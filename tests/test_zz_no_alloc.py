@@ -52,7 +52,18 @@ def _call(lib, q, kc, vc, out, kvl, bt, splits):
                                             splits, 1.0 / D ** 0.5, stream)
 
 
-@pytest.mark.parametrize("nq,nkv,splits", [(32, 8, 8), (8, 1, 16)])
+def _fp32_reference(q, kc, vc, kvl, bt):
+    """Plain fp32 attention of every batch row over its gathered pages."""
+    ref = sub("ops.reference")
+    rows = []
+    for b, n in enumerate(kvl.tolist()):
+        k = ref.gather_kv(kc, bt[b], n)
+        v = ref.gather_kv(vc, bt[b], n)
+        rows.append(ref.attention(q[b:b + 1], k, v))
+    return torch.cat(rows, 0)
+
+
+@pytest.mark.parametrize("nq,nkv,splits", [(32, 8, 8), (8, 1, 16), (32, 8, 1)])
 def test_noalloc_matches_regular_entry_point_twice(nq, nkv, splits):
     ops = sub("ops")
     lib = _lib()
@@ -66,7 +77,61 @@ def test_noalloc_matches_regular_entry_point_twice(nq, nkv, splits):
         torch.cuda.synchronize()
         assert not torch.isnan(out.float()).any()
         err = (out.float() - want.float()).abs().max().item()
-        assert err < 2e-2, f"call {call}: max err {err}"
+        assert err < 2e-2, f"call {call}: max err {err} against the regular entry point"
+        err32 = (out.float() - _fp32_reference(q, kc, vc, kvl, bt)).abs().max().item()
+        assert err32 < 2e-2, f"call {call}: max err {err32} against fp32 attention"
+
+
+def test_noalloc_single_split_has_no_row_limit():
+    """One split writes the output directly: a batch whose rows exceed the
+    scratch is still served (the limit only applies to split partials)."""
+    ops = sub("ops")
+    lib = _lib()
+    cap = lib.mbx_decode_attention_noalloc_max_rows()
+    nq, nkv = 32, 8
+    B = cap // nq + 8
+    q, kc, vc, kvl, bt = _inputs(5, [40] * B, nq, nkv)
+    out = torch.full_like(q, float("nan"))
+    rc = _call(lib, q, kc, vc, out, kvl, bt, 1)
+    assert rc == 0, lib.mbx_noalloc_last_error().decode()
+    want = ops.decode_attention(q, kc, vc, kvl, bt, splits=1)
+    torch.cuda.synchronize()
+    assert (out.float() - want.float()).abs().max().item() < 2e-2
+    pick = [0, B // 2, B - 1]
+    got = out[pick].float()
+    ref = _fp32_reference(q[pick], kc, vc, kvl[pick], bt[pick])
+    assert (got - ref).abs().max().item() < 2e-2
+
+
+def test_noalloc_rejects_bad_group_and_null_pointers():
+    lib = _lib()
+    q, kc, vc, kvl, bt = _inputs(2, [64, 64], 12, 8)  # 12 query heads over 8 kv heads
+    out = torch.empty_like(q)
+    rc = _call(lib, q, kc, vc, out, kvl, bt, 4)
+    assert rc == 4
+    assert b"group size" in lib.mbx_noalloc_last_error()
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.mbx_decode_attention_noalloc(None, kc.data_ptr(), vc.data_ptr(), out.data_ptr(), kvl.data_ptr(),
+                                          bt.data_ptr(), bt.shape[1], 2, 12, 8, 4, 0.1, stream)
+    assert rc == 1
+    assert b"null pointer" in lib.mbx_noalloc_last_error()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_second_device_after_first():
+    """The scratch address and the kernel's shared-memory limit are per
+    device: a call on device 1 after device 0 must work as well."""
+    ops = sub("ops")
+    lib = _lib()
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            q, kc, vc, kvl, bt = _inputs(20 + dev, [5, 300, 1500], 32, 8)
+            out = torch.full_like(q, float("nan"))
+            rc = _call(lib, q, kc, vc, out, kvl, bt, 8)
+            assert rc == 0, lib.mbx_noalloc_last_error().decode()
+            want = ops.decode_attention(q, kc, vc, kvl, bt, splits=8)
+            torch.cuda.synchronize()
+            assert (out.float() - want.float()).abs().max().item() < 2e-2
 
 
 def test_noalloc_rejects_oversize_request():
