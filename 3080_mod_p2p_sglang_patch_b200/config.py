@@ -50,6 +50,11 @@ class CommConfig:
     fuse_half_bytes: int = 40 * MiB
     # segmented (overlap) path: bytes per slot per source rank (0 disables)
     seg_slot_bytes: int = 8 * MiB
+    # second communication lane (MailboxAR.lane): one ping-pong half of its
+    # region, which has its own signal words and epochs (0 disables)
+    lane_half_bytes: int = 32 * MiB
+    # grid cap of a lane's allreduce + norm: leaves SMs to the other lane's compute
+    lane_max_blocks: int = 64
     # bound of every device-side wait (the reference uses ~1 s, mailbox_ar_ext.cu:5)
     timeout_ns: int = 2_000_000_000
     # bound of host-side handshakes (FD exchange)
@@ -90,5 +95,7 @@ class CommConfig:
             c.nvls = False
         if "MBX_MAX_BLOCKS" in os.environ:
             c.max_blocks = int(os.environ["MBX_MAX_BLOCKS"])
+        if "MBX_LANE_MAX_BLOCKS" in os.environ:
+            c.lane_max_blocks = int(os.environ["MBX_LANE_MAX_BLOCKS"])
         c.verbose = env_flag("SGLANG_MAILBOX_AR_VERBOSE", False)
         return c

@@ -216,19 +216,19 @@ class LlamaTP:
 
     def enable_overlap(self, min_rows: int = 512, threads: int = 256):
         """Run native TP batches of at least ``min_rows`` tokens as two
-        micro-batches whose allreduces overlap the other's compute (the
+        micro-batches on two streams, each with its own communication lane,
+        so one micro-batch's allreduces run while the other computes (the
         caller passes per-micro-batch attention, see ``forward``).
 
         The reference's answer to the same problem is its segmented
         allreduce: the row-split GEMM output pushed by the copy engine while
         the next segment computes (sglang/mailbox_ar_ext.cu:233-342,
-        docs/performance.md:51-65). Here whole layers overlap instead: while
-        one micro-batch's allreduce + residual + RMSNorm runs on a
-        high-priority communication stream, the other's GEMMs and attention
-        run on the compute stream. ``threads=256`` launches the collective
-        with half-size blocks, which fit on an SM beside a GEMM CTA."""
-        ok = (self.impl == "native" and self.tp_size > 1 and not self.int4 and self.tp is not None
-              and self.tp.ca_comm is not None)
+        docs/performance.md:51-65). Here whole layers overlap instead.
+        ``threads=256`` launches the collectives with half-size blocks, which
+        fit on an SM beside a GEMM CTA of the other micro-batch."""
+        ca = self.tp.ca_comm if self.tp is not None else None
+        ok = (self.impl == "native" and self.tp_size > 1 and not self.int4 and ca is not None
+              and ca.lane() is not None)
         self.overlap_min_rows = int(min_rows) if ok else None
         self.overlap_threads = int(threads)
 
@@ -241,10 +241,17 @@ class LlamaTP:
         if self.sp is not None and T >= self.sp_min_rows and self.sp.fits(T):
             return None
         T1 = max(128, (T // 2) // 128 * 128)
-        return T1 if T1 < T else None
+        if T1 >= T:
+            return None
+        ca = self.tp.ca_comm
+        nbytes = max(T1, T - T1) * self.cfg.hidden * 2
+        if nbytes > ca.fused_rmsnorm_limit() or not ca.lane().fits_rmsnorm(nbytes):
+            return None
+        return T1
 
     def comm_stream(self):
-        """High-priority stream of the overlapped collectives (created once)."""
+        """The second micro-batch's stream (created once, high priority so its
+        collectives get SMs as soon as they are free)."""
         if self._comm_stream is None:
             self._comm_stream = torch.cuda.Stream(device=self.device, priority=-1)
         return self._comm_stream
@@ -407,21 +414,24 @@ class LlamaTP:
     def _forward_overlap(self, ids, positions, slots, kv_caches, halves, last_idx, return_hidden=False):
         """Two micro-batches, rows [0, T1) and [T1, T), on two streams.
 
-        Compute stream, per layer: attention block of micro-batch 0, of 1,
-        then MLP block of 0, of 1. Communication stream: each block's
-        allreduce + residual + RMSNorm as soon as its row-parallel GEMM is
-        done, so it runs while the other micro-batch computes. Every
-        communicator call is on the one communication stream, in the same
-        order on every rank (the device epochs stay in step); the compute
-        stream waits only for the collective whose output it reads next.
-        Same math as ``forward`` row by row (sums in rank order, one
-        rounding), so the tokens are identical."""
-        cfg, w, tp = self.cfg, self.w, self.tp
+        Micro-batch 0 runs on the current stream with the communicator's main
+        context, micro-batch 1 on a second stream with its second lane
+        (``MailboxAR.lane``): each lane's collectives come in the same order on
+        every rank, and the two lanes never share signal words, buffers or
+        epochs. While one micro-batch waits in its allreduce + residual +
+        RMSNorm, the other's GEMMs and attention use the SMs. The only
+        cross-stream dependency per layer: micro-batch 1's attention reads the
+        keys and values micro-batch 0 wrote to the cache for the same layer.
+        Lane 1's kernels use their own scratch (``ops.workspace_lane``). Same
+        math as ``forward`` row by row (sums in rank order, one rounding)."""
+        cfg, w = self.cfg, self.w
+        ca = self.tp.ca_comm
+        lane1 = ca.lane()
         T1, attn0, attn1 = halves
         T = ids.shape[0]
         nq, nkv, D = w.nq, w.nkv, cfg.head_dim
-        comp = torch.cuda.current_stream(self.device)
-        comm = self.comm_stream()
+        s0 = torch.cuda.current_stream(self.device)
+        s1 = self.comm_stream()
         h = ops.embedding(ids, w.embed, start=w.vocab_start)
         residual = self._all_reduce(h)
         x = ops.rmsnorm(residual, w.layers[0]["ln1"], cfg.eps)
@@ -432,43 +442,55 @@ class LlamaTP:
         P = [part[a:b] for a, b in spans]
         pos = [positions[a:b] for a, b in spans]
         sl = [slots[a:b] for a, b in spans]
-        attns = (attn0, attn1)
-        done_comp = [torch.cuda.Event(), torch.cuda.Event()]
-        done_comm = [torch.cuda.Event(), torch.cuda.Event()]
         th = self.overlap_threads
+        mb = ca.cfg.lane_max_blocks
+        kv_ready = torch.cuda.Event()
+        fork, join = torch.cuda.Event(), torch.cuda.Event()
+        fork.record(s0)
+        s1.wait_event(fork)
+
+        def attn_block(i, li, L, kc, vc, attn):
+            qkv = ops.gemm(X[i], L["qkv"])
+            if cfg.qkv_bias:
+                qkv += L["qkv_bias"]
+            q = ops.rope_and_cache(qkv, pos[i], self.cos_sin, nq, nkv, sl[i], kc, vc, **self._qk_norm_args(L))
+            if i == 0:
+                kv_ready.record(s0)
+            else:
+                s1.wait_event(kv_ready)
+            o = attn(li, q, kc, vc)
+            ops.gemm(o.view(-1, nq * D), L["o"], out=P[i])
+
+        def mlp_block(i, L):
+            gu = ops.gemm(X[i], L["gate_up"])
+            a = ops.silu_mul(gu)
+            ops.gemm(a, L["down"], out=P[i])
 
         def collective(i, norm_w):
-            done_comp[i].record(comp)
-            with torch.cuda.stream(comm):
-                comm.wait_event(done_comp[i])
-                tp.all_reduce_rmsnorm(P[i], R[i], norm_w, cfg.eps, out=X[i], threads=th)
-                done_comm[i].record(comm)
+            if i == 0:
+                ca.all_reduce_rmsnorm(P[0], R[0], norm_w, cfg.eps, out=X[0], threads=th, max_blocks=mb)
+            else:
+                lane1.all_reduce_rmsnorm(P[1], R[1], norm_w, cfg.eps, out=X[1], threads=th)
 
         for li, L in enumerate(w.layers):
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_push(f"layer {li}")
             kc, vc = kv_caches[li]
-            for i in (0, 1):
-                if li > 0:
-                    comp.wait_event(done_comm[i])
-                qkv = ops.gemm(X[i], L["qkv"])
-                if cfg.qkv_bias:
-                    qkv += L["qkv_bias"]
-                q = ops.rope_and_cache(qkv, pos[i], self.cos_sin, nq, nkv, sl[i], kc, vc, **self._qk_norm_args(L))
-                o = attns[i](li, q, kc, vc)
-                ops.gemm(o.view(-1, nq * D), L["o"], out=P[i])
-                collective(i, L["ln2"])
             nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
-            for i in (0, 1):
-                comp.wait_event(done_comm[i])
-                gu = ops.gemm(X[i], L["gate_up"])
-                a = ops.silu_mul(gu)
-                ops.gemm(a, L["down"], out=P[i])
-                collective(i, nxt)
+            attn_block(0, li, L, kc, vc, attn0)
+            collective(0, L["ln2"])
+            with torch.cuda.stream(s1), ops.workspace_lane(1):
+                attn_block(1, li, L, kc, vc, attn1)
+                collective(1, L["ln2"])
+            mlp_block(0, L)
+            collective(0, nxt)
+            with torch.cuda.stream(s1), ops.workspace_lane(1):
+                mlp_block(1, L)
+                collective(1, nxt)
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_pop()
-        comp.wait_event(done_comm[0])
-        comp.wait_event(done_comm[1])
+        join.record(s1)
+        s0.wait_event(join)
         x_last = x.index_select(0, last_idx)
         if return_hidden:
             return x_last

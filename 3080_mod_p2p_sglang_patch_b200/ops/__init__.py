@@ -6,8 +6,10 @@ decode split-KV partials, the GEMM error word) comes from a per-device
 workspace that is allocated once and reused, so CUDA-graph capture never
 allocates.
 """
+import contextlib
 import dataclasses
 import math
+import os
 
 import torch
 
@@ -20,9 +22,9 @@ class _Workspace:
     a new, larger one and the old one is kept alive (``_retired``): a CUDA graph
     that captured the old address keeps valid memory."""
 
-    def __init__(self, device):
+    def __init__(self, device, err=None):
         self.device = device
-        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.err = err if err is not None else torch.zeros(1, dtype=torch.int32, device=device)
         # split-K tile arrival counters (each reset by the tile's last CTA)
         self.counters = torch.zeros(65536, dtype=torch.int32, device=device)
         self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
@@ -57,15 +59,35 @@ class _Workspace:
 
 
 _WS = {}
+_LANE = [0]
+
+
+@contextlib.contextmanager
+def workspace_lane(lane: int):
+    """Kernels launched inside use lane ``lane``'s scratch buffers. Work issued
+    on a second stream that runs at the same time as the first (the
+    overlapped micro-batches) must not share the split-K or split-KV partial
+    buffers; the error word is shared by all lanes."""
+    prev = _LANE[0]
+    _LANE[0] = int(lane)
+    try:
+        yield
+    finally:
+        _LANE[0] = prev
 
 
 def workspace(device) -> _Workspace:
     key = torch.device(device).index
     if key is None:
         key = torch.cuda.current_device()
-    ws = _WS.get(key)
+    lane = _LANE[0]
+    ws = _WS.get((key, lane))
     if ws is None:
-        ws = _WS[key] = _Workspace(torch.device("cuda", key))
+        dev = torch.device("cuda", key)
+        base = _WS.get((key, 0)) if lane else None
+        if lane and base is None:
+            base = _WS[(key, 0)] = _Workspace(dev)
+        ws = _WS[(key, lane)] = _Workspace(dev, err=base.err if base is not None else None)
     return ws
 
 
@@ -99,10 +121,15 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
     s = splits or plan_splits
     wbuf = ws.gemm(s * M * N) if s > 1 else None
     # split-K partials are folded by a separate reduce kernel: the in-kernel
-    # reduction (pass ws.counters) measured no faster at 1 token and slower at 64
-    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, None)
-    launches.add(2 if s > 1 else 1)
+    # reduction (pass ws.counters) measured no faster at 1 token and slower at 64.
+    # MBX_GEMM_SPLITK_INKERNEL=1 selects it for batches above 64 rows (tuning).
+    inkernel = s > 1 and M > 64 and _SPLITK_INKERNEL
+    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, ws.counters if inkernel else None)
+    launches.add(2 if s > 1 and not inkernel else 1)
     return out
+
+
+_SPLITK_INKERNEL = os.environ.get("MBX_GEMM_SPLITK_INKERNEL", "0") == "1"
 
 
 @dataclasses.dataclass

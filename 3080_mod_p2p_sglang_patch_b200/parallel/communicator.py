@@ -126,10 +126,14 @@ class MailboxAR:
                     self.peer_mbx)
 
     # ------------------------------------------------------------------ setup
+    def _lane_bytes(self):
+        C = cuda_ext()
+        return C.SIG_BYTES + 2 * self.cfg.lane_half_bytes if self.cfg.lane_half_bytes else 0
+
     def _buffer_bytes(self):
         C = cuda_ext()
         seg = C.SEG_SLOTS * C.MAX_RANKS * self.cfg.seg_slot_bytes
-        return C.SIG_BYTES + 2 * self.cfg.half_bytes + 2 * self.cfg.fuse_half_bytes + seg
+        return C.SIG_BYTES + 2 * self.cfg.half_bytes + 2 * self.cfg.fuse_half_bytes + seg + self._lane_bytes()
 
     def _setup_gpu(self):
         from .symm import SymmetricBuffer
@@ -147,6 +151,9 @@ class MailboxAR:
         self.mbx = self._buf.local_ptr
         self.peer_mbx = self._buf.ptrs[(self.rank + 1) % self.world_size]
         self.transport = self._buf.transport + ("+nvls" if self._buf.mc_ptr else "")
+        # the second lane's region ends the buffer (after the segment slots)
+        self._lane_off = self._buffer_bytes() - self._lane_bytes()
+        self._lane = None
 
     def _setup_cpu(self):
         ext = cpu_ext()
@@ -177,6 +184,10 @@ class MailboxAR:
         self.peer_mbx = 0
 
     def _teardown(self):
+        lane = getattr(self, "_lane", None)
+        if lane is not None:
+            lane.release()
+            self._lane = None
         if self.sp is not None:
             try:
                 self.sp.close()
@@ -290,13 +301,14 @@ class MailboxAR:
         return out
 
     def all_reduce_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
-                           out: torch.Tensor = None, algo=None, threads: int = 512):
+                           out: torch.Tensor = None, algo=None, threads: int = 512, max_blocks: int = None):
         """Fused: residual <- bf16(residual + allreduce(x)); returns
         rmsnorm(residual) * weight (bf16), in one kernel launch.
 
         ``threads=256`` launches half-size blocks (half the registers per
         block), so each fits on an SM beside a running GEMM CTA: the form
-        used when the call overlaps compute on another stream."""
+        used when the call overlaps compute on another stream; ``max_blocks``
+        caps the grid below the configured one for the same reason."""
         assert x.dtype == torch.bfloat16 and x.is_contiguous() and residual.is_contiguous()
         H = x.shape[-1]
         M = x.numel() // H
@@ -307,7 +319,8 @@ class MailboxAR:
         if algo is None:
             algo = ALGO_ONESHOT_PUSH if nbytes <= self.cfg.oneshot_max.get(self.world_size, 0) else ALGO_TWOSHOT_PUSH
         self._ar.ar_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(), out.data_ptr(), M, H, eps, algo,
-                            self.cfg.max_blocks, torch.cuda.current_stream(self.device).cuda_stream, int(threads))
+                            int(max_blocks or self.cfg.max_blocks), torch.cuda.current_stream(self.device).cuda_stream,
+                            int(threads))
         self.counters["fused"] += 1
         launches.add(1)
         return out
@@ -367,6 +380,24 @@ class MailboxAR:
         self.counters["allgather"] += 1
         launches.add(1)
         return out
+
+    # ------------------------------------------------------------------ second lane
+    def lane(self):
+        """A second communication context for collectives issued from another
+        stream, concurrently with this one's (``None`` without the GPU
+        transport or with ``lane_half_bytes = 0``).
+
+        It lives in a disjoint region at the end of the same symmetric
+        buffers, with its own signal words, ping-pong halves, device epochs and
+        host-mapped status, so its calls and the main context's may run at
+        the same time and in either order; the calls of each context must
+        still come in the same order on every rank. Creating it is local (the
+        memory is mapped already)."""
+        if self._ar is None or not self.cfg.lane_half_bytes:
+            return None
+        if self._lane is None:
+            self._lane = _Lane(self)
+        return self._lane
 
     # ------------------------------------------------------------------ graph
     def capture(self):
@@ -434,6 +465,8 @@ class MailboxAR:
             code = int(self._ar.error())
             if code == 0 and self.sp is not None:
                 code = self.sp.err()
+            if code == 0 and self._lane is not None:
+                code = self._lane.err()
             return code
         if self._cpu is not None:
             return int(self._cpu.error())
@@ -465,6 +498,8 @@ class MailboxAR:
             torch.cuda.synchronize(self.device)
             if self.sp is not None:
                 self.sp.reset()
+            if self._lane is not None:
+                self._lane.reset()
         self._seg_seq = 0
         bootstrap.agree(True, self.group)
 
@@ -517,3 +552,70 @@ class MailboxAR:
             self.disabled = True
         except Exception:  # noqa: BLE001
             pass
+
+
+class _Lane:
+    """The second context of a ``MailboxAR`` (see ``MailboxAR.lane``)."""
+
+    def __init__(self, owner: MailboxAR):
+        from .symm import _raw_uint8
+
+        C = cuda_ext()
+        self.owner = owner
+        self.cfg = owner.cfg
+        self.device = owner.device
+        off = owner._lane_off
+        self._sig = _raw_uint8(owner._buf.local_ptr + off, C.SIG_BYTES, owner.device)
+        self._state = torch.zeros(C.STATE_WORDS, dtype=torch.int32, device=owner.device)
+        self._status = C.host_mapped_alloc(4 * C.STATUS_WORDS)
+        ptrs = [p + off for p in owner._buf.ptrs]
+        self._ar = C.ArComm(owner.rank, owner.world_size, ptrs, 0, self._state.data_ptr(), self._status.dev,
+                            self._status.host, self.cfg.lane_half_bytes, 0, self.cfg.timeout_ns, 0)
+        torch.cuda.synchronize(owner.device)
+
+    def err(self) -> int:
+        return int(self._ar.error()) if self._ar is not None else 0
+
+    def fits_rmsnorm(self, nbytes: int) -> bool:
+        return nbytes <= self.cfg.lane_half_bytes // 2 - 16 * self.owner.world_size * 8192
+
+    def all_reduce_rmsnorm(self, x, residual, weight, eps, out=None, threads: int = 256):
+        """Same as ``MailboxAR.all_reduce_rmsnorm`` on this lane, with the
+        lane's grid cap (``lane_max_blocks``)."""
+        assert x.dtype == torch.bfloat16 and x.is_contiguous() and residual.is_contiguous()
+        code = self.err()
+        if code:
+            raise MailboxError(f"[MailboxAR] rank {self.owner.rank}: second lane: "
+                               f"{ERROR_NAMES.get(code, 'error')} (code {code}, status {self._ar.status()})")
+        H = x.shape[-1]
+        M = x.numel() // H
+        nbytes = x.numel() * 2
+        if out is None:
+            out = torch.empty_like(x)
+        algo = ALGO_ONESHOT_PUSH if nbytes <= min(self.cfg.oneshot_max.get(self.owner.world_size, 0),
+                                                  int(self._ar.chunk_limit(ALGO_ONESHOT_PUSH))) \
+            else ALGO_TWOSHOT_PUSH
+        self._ar.ar_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(), out.data_ptr(), M, H, eps, algo,
+                            self.cfg.lane_max_blocks, torch.cuda.current_stream(self.device).cuda_stream,
+                            int(threads))
+        self.owner.counters["fused"] += 1
+        launches.add(1)
+        return out
+
+    def reset(self):
+        """Part of the owner's collective ``reset``: clear this lane's signals,
+        epochs and status."""
+        torch.cuda.synchronize(self.device)
+        self._sig.zero_()
+        self._state.zero_()
+        self._ar.clear_status()
+        torch.cuda.synchronize(self.device)
+
+    def release(self):
+        if self._status is not None:
+            try:
+                cuda_ext().host_mapped_free(self._status.host)
+            except Exception:  # noqa: BLE001
+                pass
+            self._status = None
+        self._ar = None

@@ -56,11 +56,11 @@ class EmulatedWorld:
         torch.cuda.synchronize(self.device)
 
     # ------------------------------------------------------------------ helpers
-    def _launch(self, op, algo, dtype, ins, outs, residuals=(), weight=0, nbytes=0, M=0, N=0, eps=0.0):
+    def _launch(self, op, algo, dtype, ins, outs, residuals=(), weight=0, nbytes=0, M=0, N=0, eps=0.0, threads=512):
         self.check()
         self.C.ar_emulated(self.comms, op, algo, dtype, [int(p) for p in ins], [int(p) for p in outs],
                            [int(p) for p in residuals], int(weight), int(nbytes), int(M), int(N), float(eps),
-                           self.blocks, self._scratch.data_ptr(), self._scratch.numel())
+                           self.blocks, self._scratch.data_ptr(), self._scratch.numel(), int(threads))
 
     def check(self):
         """Raise MailboxError if any emulated rank recorded a device error."""
@@ -84,13 +84,14 @@ class EmulatedWorld:
                      [o.data_ptr() for o in outs], nbytes=nbytes)
         return outs
 
-    def all_reduce_rmsnorm(self, xs, residuals, weight, eps, algo=ALGO_TWOSHOT_PUSH):
-        """residuals[r] += sum(xs); outs[r] = rmsnorm(residuals[r]) * weight."""
+    def all_reduce_rmsnorm(self, xs, residuals, weight, eps, algo=ALGO_TWOSHOT_PUSH, threads=512):
+        """residuals[r] += sum(xs); outs[r] = rmsnorm(residuals[r]) * weight.
+        ``threads=256``: the half-size blocks of overlapped micro-batches."""
         M, N = xs[0].shape
         outs = [torch.empty_like(x) for x in xs]
         self._launch(self.C.EMU_AR_RMSNORM, algo, DTYPE_IDS[torch.bfloat16], [x.data_ptr() for x in xs],
                      [o.data_ptr() for o in outs], [r.data_ptr() for r in residuals], weight.data_ptr(),
-                     nbytes=M * N * 2, M=M, N=N, eps=eps)
+                     nbytes=M * N * 2, M=M, N=N, eps=eps, threads=threads)
         return outs
 
     def all_gather(self, xs):

@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--sp", type=int, default=None, choices=[0, 1],
                    help="sequence-parallel prefill (1) or allreduce prefill (0); default: MBX_SP (off)")
+    p.add_argument("--overlap", type=int, default=None, choices=[0, 1],
+                   help="overlapped micro-batches at TP > 1 (1) or one batch per chunk (0); default: MBX_OVERLAP")
     p.add_argument("--no-graph", action="store_true", help="launch every chunk's kernels eagerly (the torch "
                    "baseline always does: like sglang, it graphs decode only)")
     return p.parse_args()
@@ -86,7 +88,8 @@ def main():
     R, S, chunk = args.requests, args.prompt_len, args.chunk
     eng = eng_mod.LLMEngine(cfg, tp=tp, max_batch=R, max_seq=S + 16, chunk=chunk, seed=0, use_graphs=False,
                             impl=args.impl, prefill_graph=(args.impl == "native" and not args.no_graph),
-                            sp=(None if args.sp is None else bool(args.sp)) if args.impl == "native" else False)
+                            sp=(None if args.sp is None else bool(args.sp)) if args.impl == "native" else False,
+                            overlap=None if args.overlap is None else bool(args.overlap))
     g = torch.Generator().manual_seed(1234)
     prompts = torch.randint(0, cfg.vocab, (R, S), generator=g).tolist()
 
@@ -208,6 +211,7 @@ def main():
                 "transport": getattr(tp.ca_comm, "transport", None) if (tp and tp.ca_comm) else None,
                 "prefill_cuda_graph": eng.prefill_graph is not None,
                 "sequence_parallel": eng.sp is not None,
+                "overlapped_micro_batches": bool(eng.overlap),
                 "gemm_cta_pair": {"0": "off", "1": "on"}.get(os.environ.get("MBX_GEMM_2CTA", ""), "by wave cost"),
                 "fused_gemm_allreduce": bool(tp is not None and tp.fused_gemm_ar),
             },

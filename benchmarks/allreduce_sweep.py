@@ -87,6 +87,10 @@ def main():
     ap.add_argument("--max-bytes", type=int, default=256 << 20)
     ap.add_argument("--out", default=None)
     ap.add_argument("--sizes", default=None, help="comma-separated byte counts (default: the full sweep)")
+    ap.add_argument("--norm", action="store_true",
+                    help="time the fused allreduce + residual + RMSNorm on [bytes/8192, 4096] bf16 rows "
+                         "(one-shot push, two-shot, two-shot push; NCCL + the norm kernel as the baseline) "
+                         "instead of the plain allreduce")
     ap.add_argument("--trace", action="store_true",
                     help="also print block 0's phase timestamps (us from kernel start) of the last of 20 "
                          "back-to-back calls, per rank")
@@ -133,8 +137,31 @@ def main():
         x = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)
         o = torch.empty_like(x)
         iters = max(10, min(1000, int(2e9 // nbytes)))
+        if args.norm:
+            H = 4096
+            M = max(1, nbytes // (2 * H))
+            xn = x[:M * H].view(M, H)
+            resn = torch.zeros(M, H, device=dev, dtype=torch.bfloat16)
+            on = torch.empty_like(xn)
+            wn = torch.ones(H, device=dev, dtype=torch.bfloat16)
+            ops = importlib.import_module(f"{PKG}.ops")
         for algo in algos:
-            if algo == "nccl":
+            if args.norm:
+                if algo == "nccl":
+                    y = xn.clone()
+
+                    def fn():
+                        dist.all_reduce(y, group=group)
+                        ops.fused_add_rmsnorm(y, resn, wn, 1e-5, out=on)
+                elif algo in ("oneshot_push", "twoshot", "twoshot_push"):
+                    if M * H * 2 > ar.fused_rmsnorm_limit() or (
+                            algo == "oneshot_push" and M * H * 2 > ar._ar.chunk_limit(comm_mod.ALGO_ONESHOT_PUSH)):
+                        continue
+                    fn = lambda a=comm_mod.ALGO_IDS[algo]: ar.all_reduce_rmsnorm(xn, resn, wn, 1e-5, out=on,  # noqa
+                                                                                 algo=a)
+                else:
+                    continue
+            elif algo == "nccl":
                 y = x.clone()
                 fn = lambda: dist.all_reduce(y, group=group)  # noqa: E731
             elif algo == "reference_mailbox":
@@ -162,7 +189,10 @@ def main():
                     del gr
                 rec = {"bytes": nbytes, "impl": algo, "mode": mode, "tp": world, "us": ms * 1e3,
                        "busbw_gbs": busbw(nbytes, ms, world)}
-                if algo == "auto":
+                if args.norm:
+                    rec["op"] = "allreduce+residual+rmsnorm"
+                    rec["rows"] = M
+                if algo == "auto" and not args.norm:
                     rec["route"] = "nccl" if nbytes > policy_max else "mailbox"
                 if rank == 0:
                     print(json.dumps(rec), flush=True)
@@ -181,7 +211,7 @@ def main():
                 dist.all_gather_object(allm, trace.tolist(), group=group)
                 if rank == 0:
                     t0 = min(m[0] for m in allm)
-                    print(json.dumps({"bytes": nbytes, "impl": algo, "trace_us": [
+                    print(json.dumps({"bytes": nbytes, "impl": algo, "norm": bool(args.norm), "trace_us": [
                         [round((v - t0) / 1e3, 2) if v else None for v in m[:6]] for m in allm]}), flush=True)
         if ar.err():
             raise SystemExit(f"communicator error {ar.status()}")

@@ -1,6 +1,8 @@
 """Row-parallel linear + allreduce + residual + RMSNorm at TP = world size:
 the fused tcgen05 GEMM -> push-reduce-scatter -> reduce/all-gather/norm pair
-vs the same kernels unfused vs cuBLAS + NCCL (+ the same norm kernel).
+vs the same kernels unfused vs two overlapped micro-batches (second half's
+GEMM under the first half's collective) vs cuBLAS + NCCL (+ the same norm
+kernel).
 
     torchrun --nproc-per-node N benchmarks/fused_ar_bench.py [--model 8b] [--rows 1024,64,8,1]
 
@@ -83,6 +85,26 @@ def main():
                 p = ops.gemm(a, w)
                 ar.all_reduce_rmsnorm(p, res, nw, 1e-5, out=out)
 
+            # two micro-batches: the second half's GEMM runs while the first
+            # half's allreduce + norm runs on a high-priority side stream
+            # (the model's overlapped prefill, reduced to one layer)
+            h = (M // 2) // 128 * 128
+            comm_s = torch.cuda.Stream(device=dev, priority=-1)
+            parts = torch.empty(M, H, device=dev, dtype=torch.bfloat16)
+            evs = [torch.cuda.Event() for _ in range(4)]
+
+            def overlapped():
+                comp = torch.cuda.current_stream()
+                for i, (r0, r1) in enumerate(((0, h), (h, M))):
+                    ops.gemm(a[r0:r1], w, out=parts[r0:r1])
+                    evs[i].record(comp)
+                    with torch.cuda.stream(comm_s):
+                        comm_s.wait_event(evs[i])
+                        ar.all_reduce_rmsnorm(parts[r0:r1], res[r0:r1], nw, 1e-5, out=out[r0:r1], threads=256)
+                        evs[2 + i].record(comm_s)
+                comp.wait_event(evs[2])
+                comp.wait_event(evs[3])
+
             def cublas_nccl():
                 p = F.linear(a, w)
                 dist.all_reduce(p)
@@ -92,6 +114,8 @@ def main():
             if fits:
                 rec["fused_us"] = timed(fused, args.iters)
             rec["unfused_us"] = timed(unfused, args.iters)
+            if h >= 128:
+                rec["overlapped_halves_us"] = timed(overlapped, args.iters)
             rec["cublas_nccl_us"] = timed(cublas_nccl, args.iters)
             flops = 2.0 * M * H * K
             link_bytes = 2.0 * (world - 1) / world * M * H * 2  # reduce-scatter + all-gather, per direction

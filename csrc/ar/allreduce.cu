@@ -560,6 +560,7 @@ MBX_DEVICE void ar_rmsnorm_oneshot(const ArCtx& c, const uint4* __restrict__ in,
   __shared__ float red[32];
   const uint32_t epoch = call_epoch(c);
   const int hvec = H / 8;
+  trace_mark(c, 0);
   if (!poisoned(c)) {
     const uint64_t slot = oneshot_slot_bytes(c.half_bytes, W);
     const int nrows = block_rows(M);
@@ -572,7 +573,9 @@ MBX_DEVICE void ar_rmsnorm_oneshot(const ArCtx& c, const uint4* __restrict__ in,
           for (int t = 0; t < W; ++t)
             st_v4(data_half(c.bufs[(c.rank + t) % W], epoch, c.half_bytes) + c.rank * slot + i * 16, v);
         });
+    trace_mark(c, 1);
     if (block_barrier(c, 0, epoch, &s_ok)) {
+      trace_mark(c, 2);
       const char* mine = data_half(c.bufs[c.rank], epoch, c.half_bytes);
       for_norm_rows(nrows, [&](const RowCtx& rc, int k) {
         const uint64_t base = (uint64_t)(b + k * g) * hvec;
@@ -582,6 +585,7 @@ MBX_DEVICE void ar_rmsnorm_oneshot(const ArCtx& c, const uint4* __restrict__ in,
       });
     }
   }
+  trace_mark(c, 5);
   finish_call(c, epoch);
 }
 
@@ -871,6 +875,7 @@ MBX_DEVICE void ar_rmsnorm_twoshot_push(const ArCtx& c, const uint4* __restrict_
   const uint32_t epoch = call_epoch(c);
   const int hvec = H / 8;
   const int Mo = (M + W - 1) / W;
+  trace_mark(c, 0);
   if (!poisoned(c)) {
     const uint64_t slot = (uint64_t)Mo * hvec * 16;
     const uint64_t regB = (uint64_t)W * slot;
@@ -887,7 +892,9 @@ MBX_DEVICE void ar_rmsnorm_twoshot_push(const ArCtx& c, const uint4* __restrict_
           [&](int j, int pv, int) { return ld_nc_v4(in + (uint64_t)(a0 + b + j * g) * hvec + pv); },
           [&](int j, int pv, const uint4& v) { st_v4(dst + ((uint64_t)(b + j * g) * hvec + pv) * 16, v); });
     }
+    trace_mark(c, 1);
     if (!block_barrier(c, 0, epoch, &s_ok)) goto done;
+    trace_mark(c, 2);
     {
       // B: sum the own rows (rank order) and push the sums into every rank's region B
       const int r0 = c.rank * Mo, r1 = min(M, r0 + Mo);
@@ -901,7 +908,9 @@ MBX_DEVICE void ar_rmsnorm_twoshot_push(const ArCtx& c, const uint4* __restrict_
               st_v4(data_half(c.bufs[(c.rank + t) % W], epoch, c.half_bytes) + regB + (row * hvec + pv) * 16, sum);
           });
     }
+    trace_mark(c, 3);
     if (!block_barrier(c, 1, epoch, &s_ok)) goto done;
+    trace_mark(c, 4);
     // C: residual + norm of every row from the local region B
     for_owner_norm_rows<W>(M, Mo, [&](const RowCtx& rc, int row) {
       const uint64_t base = (uint64_t)row * hvec;
@@ -911,6 +920,7 @@ MBX_DEVICE void ar_rmsnorm_twoshot_push(const ArCtx& c, const uint4* __restrict_
     });
   }
 done:
+  trace_mark(c, 5);
   finish_call(c, epoch);
 }
 
@@ -1417,7 +1427,8 @@ __global__ void __launch_bounds__(kArThreads) ar_emulated_kernel(const EmuRank* 
 }
 
 void ar_emulated_launch(const EmuRank* ranks_host, int world, int op, int algo, int dtype, uint64_t nbytes, int M,
-                        int N, float eps, int blocks, void* dev_scratch, cudaStream_t stream) {
+                        int N, float eps, int blocks, void* dev_scratch, cudaStream_t stream, int threads) {
+  if (threads != 256 && threads != kArThreads) throw std::runtime_error("emulated allreduce: threads must be 256 or 512");
   if (world < 2 || world > kMaxRanks) throw std::runtime_error("emulated allreduce: world must be 2..8");
   if (nbytes % 16 != 0) throw std::runtime_error("emulated allreduce: byte size must be a multiple of 16");
   if (op == kEmuAllreduce) {
@@ -1457,7 +1468,7 @@ void ar_emulated_launch(const EmuRank* ranks_host, int world, int op, int algo, 
   dim3 grid(blocks, world);
   void* args[] = {&ranks, &op, &algo, &nvec, &M, &N, &eps};
   auto go = [&](const void* fn) {
-    MBX_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, grid, dim3(kArThreads), args, 0, stream));
+    MBX_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, grid, dim3(threads), args, 0, stream));
   };
   const bool f32 = dtype == kF32;
   auto pick = [&](auto wc) -> const void* {

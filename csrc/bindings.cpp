@@ -542,7 +542,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       "ar_emulated",
       [](std::vector<ArComm*> comms, int op, int algo, int dtype, std::vector<int64_t> ins, std::vector<int64_t> outs,
          std::vector<int64_t> residuals, int64_t weight, uint64_t nbytes, int M, int N, double eps, int blocks,
-         int64_t scratch, int64_t scratch_bytes) {
+         int64_t scratch, int64_t scratch_bytes, int threads) {
         const int W = (int)comms.size();
         TORCH_CHECK(W >= 2 && W <= kMaxRanks && (int)ins.size() == W && (int)outs.size() == W,
                     "ar_emulated: one input and output per rank");
@@ -558,11 +558,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           r[i].weight = reinterpret_cast<const void*>(weight);
         }
         ar_emulated_launch(r.data(), W, op, algo, dtype, nbytes, M, N, (float)eps, blocks,
-                           reinterpret_cast<void*>(scratch), cur_stream());
+                           reinterpret_cast<void*>(scratch), cur_stream(), threads);
       },
       py::arg("comms"), py::arg("op"), py::arg("algo"), py::arg("dtype"), py::arg("ins"), py::arg("outs"),
       py::arg("residuals"), py::arg("weight"), py::arg("nbytes"), py::arg("M"), py::arg("N"), py::arg("eps"),
-      py::arg("blocks"), py::arg("scratch"), py::arg("scratch_bytes"));
+      py::arg("blocks"), py::arg("scratch"), py::arg("scratch_bytes"), py::arg("threads") = 512);
   m.attr("EMU_ALLREDUCE") = (int)kEmuAllreduce;
   m.attr("EMU_AR_RMSNORM") = (int)kEmuArRmsnorm;
   m.attr("EMU_FUSED_RS_NORM") = (int)kEmuFusedRsNorm;

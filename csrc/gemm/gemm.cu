@@ -954,22 +954,43 @@ static int pair_gemm_mode() {
   return mode;
 }
 
-static bool use_pair_gemm(int64_t M, int64_t N, const GemmPlan& p, int sms) {
+// Pair tile width (256, 192 or 128; 0 = single-CTA tiles). The pair widths
+// share the wave-cost model of plan_for: per SM a pair tile reads half of B,
+// which the per-width factors credit (0.85 at 256 measured; the narrower pair
+// tiles re-read A more often per FLOP, like their single-CTA counterparts).
+// MBX_GEMM_2CTA_BN=256|192|128 forces one width (tuning, tests).
+static int pair_gemm_bn(int64_t M, int64_t N, const GemmPlan& p, int sms) {
   const int mode = pair_gemm_mode();
-  if (mode == 0 || M < 2 * BM || p.splits > 1) return false;
-  if (mode == 1) return true;
+  if (mode == 0 || M < 2 * BM || p.splits > 1) return 0;
+  static const int forced = [] {
+    const char* v = std::getenv("MBX_GEMM_2CTA_BN");
+    const int b = v ? std::atoi(v) : 0;
+    return (b == 256 || b == 192 || b == 128) ? b : 0;
+  }();
+  if (forced) return forced;
   static const int kBN[] = {256, 224, 192, 160, 128};
   static const double kCost[] = {1.00, 1.00, 1.02, 1.10, 1.25};
   double c1 = 0.0;
   for (int i = 0; i < 5; ++i)
     if (kBN[i] == p.bn) c1 = kCost[i];
-  if (c1 == 0.0) return false;
+  if (c1 == 0.0) return 0;
   const int64_t tiles1 = ((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn);
   const double t1 = (double)((tiles1 + sms - 1) / sms) * p.bn * c1;
-  const int64_t pairs = ((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+  static const int kBN2[] = {256, 192, 128};
+  static const double kCost2[] = {0.85, 0.88, 1.0};
   const int64_t slots = std::max(1, sms / 2);
-  const double t2 = (double)((pairs + slots - 1) / slots) * 256 * 0.85;
-  return t2 < t1;
+  double best = t1;
+  int bn2 = 0;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t pairs = ((M + 2 * BM - 1) / (2 * BM)) * ((N + kBN2[i] - 1) / kBN2[i]);
+    const double t2 = (double)((pairs + slots - 1) / slots) * kBN2[i] * kCost2[i];
+    if (t2 < best * 0.999) {
+      best = t2;
+      bn2 = kBN2[i];
+    }
+  }
+  if (mode == 1 && bn2 == 0) bn2 = 256;
+  return bn2;
 }
 
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
@@ -1041,19 +1062,28 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
     MBX_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  if (ag == nullptr && bn <= 0 && splits <= 0 && N % 8 == 0 && use_pair_gemm(M, N, p, sms)) {
-    // CTA-pair tiles (256 x 256): same grid of SMs, half of B per SM per k-step
+  const int bn2 = (ag == nullptr && bn <= 0 && splits <= 0 && N % 8 == 0) ? pair_gemm_bn(M, N, p, sms) : 0;
+  if (bn2 > 0) {
+    // CTA-pair tiles (256 x bn2): same grid of SMs, half of B per SM per k-step
     GemmArgs pa = a;
     pa.splits = 1;
     pa.kb_per_split = pa.kb_total;
-    pa.num_n = (int)((N + 255) / 256);
+    pa.num_n = (int)((N + bn2 - 1) / bn2);
     pa.out = C;
     const CUtensorMap ta2 = make_map(A, M, K, lda, BM);
-    const CUtensorMap tb2 = make_map(B, N, K, ldb, 128);
+    const CUtensorMap tb2 = make_map(B, N, K, ldb, bn2 / 2);
     const int units2 = (int)((M + 2 * BM - 1) / (2 * BM)) * pa.num_n;
     const int grid2 = 2 * std::min(units2, sms / 2);
-    if (residual) launch_pair_cfg<256, 6, kEpiBf16AddResidual>(ta2, tb2, pa, grid2, s);
-    else launch_pair_cfg<256, 6, kEpiBf16>(ta2, tb2, pa, grid2, s);
+    if (bn2 == 256) {
+      if (residual) launch_pair_cfg<256, 6, kEpiBf16AddResidual>(ta2, tb2, pa, grid2, s);
+      else launch_pair_cfg<256, 6, kEpiBf16>(ta2, tb2, pa, grid2, s);
+    } else if (bn2 == 192) {
+      if (residual) launch_pair_cfg<192, 7, kEpiBf16AddResidual>(ta2, tb2, pa, grid2, s);
+      else launch_pair_cfg<192, 7, kEpiBf16>(ta2, tb2, pa, grid2, s);
+    } else {
+      if (residual) launch_pair_cfg<128, 8, kEpiBf16AddResidual>(ta2, tb2, pa, grid2, s);
+      else launch_pair_cfg<128, 8, kEpiBf16>(ta2, tb2, pa, grid2, s);
+    }
     MBX_CUDA_CHECK(cudaGetLastError());
     return;
   }

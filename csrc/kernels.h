@@ -44,7 +44,7 @@ struct EmuRank {
   const void* weight;  // norm ops: RMSNorm weight
 };
 void ar_emulated_launch(const EmuRank* ranks_host, int world, int op, int algo, int dtype, uint64_t nbytes, int M,
-                        int N, float eps, int blocks, void* dev_scratch, cudaStream_t stream);
+                        int N, float eps, int blocks, void* dev_scratch, cudaStream_t stream, int threads = 512);
 // Raw NVLink transport kernels for bandwidth benchmarks. kMcReduce* read the
 // multicast address `src` and write local `dst`; kMcStore reads local `src`
 // and stores to the multicast address `dst`.

@@ -9,7 +9,8 @@ checked against a plain PyTorch fp32 reference:
 * allreduce (one-shot push / pull, two-shot, two-shot push; bf16 and fp32):
   bit-exact against the fp32 sum in rank order with one final rounding, over
   consecutive calls with new values (ping-pong halves and epochs move on);
-* allreduce + residual + RMSNorm (one-shot push, two-shot, two-shot push);
+* allreduce + residual + RMSNorm (one-shot push, two-shot, two-shot push),
+  with 512- and 256-thread blocks (the latter is the overlapped prefill's);
 * the fused row-parallel GEMM -> allreduce -> residual + RMSNorm (push-all
   and owner-push epilogues);
 * all-gather.
@@ -66,8 +67,9 @@ def test_emulated_allreduce_bit_exact(W, dtype):
         assert ew.epochs() == [calls] * W
 
 
+@pytest.mark.parametrize("threads", [512, 256])
 @pytest.mark.parametrize("W", [2, 4, 8])
-def test_emulated_allreduce_rmsnorm(W):
+def test_emulated_allreduce_rmsnorm(W, threads):
     comm, ref = sub("parallel.communicator"), sub("ops.reference")
     H, eps = 1024, 1e-5
     w = (1.0 + 0.1 * _rand((H,), 3)).to(torch.bfloat16)
@@ -77,7 +79,7 @@ def test_emulated_allreduce_rmsnorm(W):
                 xs = [_rand((M, H), 100 * M + r) for r in range(W)]
                 res0 = _rand((M, H), 7 + M)
                 residuals = [res0.clone() for _ in range(W)]
-                outs = ew.all_reduce_rmsnorm(xs, residuals, w, eps, algo=comm.ALGO_IDS[algo])
+                outs = ew.all_reduce_rmsnorm(xs, residuals, w, eps, algo=comm.ALGO_IDS[algo], threads=threads)
                 ar = _rank_sum(xs).to(torch.bfloat16)
                 want_out, want_res = ref.fused_add_rmsnorm(ar, res0, w, eps)
                 torch.cuda.synchronize()

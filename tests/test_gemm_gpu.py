@@ -104,15 +104,17 @@ print("PAIR-OK", worst)
 """
 
 
-def test_cta_pair_gemm_matches_reference():
-    """The CTA-pair (cta_group::2) GEMM, selected with MBX_GEMM_2CTA=1 (read
-    once per process, so it runs in a child), against the fp32 reference on
-    ragged and multi-wave shapes, plain and residual epilogues."""
+@pytest.mark.parametrize("pair_bn", ["256", "192", "128"])
+def test_cta_pair_gemm_matches_reference(pair_bn):
+    """The CTA-pair (cta_group::2) GEMM at each pair tile width, selected with
+    MBX_GEMM_2CTA=1 and MBX_GEMM_2CTA_BN (read once per process, so it runs in
+    a child), against the fp32 reference on ragged and multi-wave shapes,
+    plain and residual epilogues."""
     import os
     import subprocess
     import sys
 
-    env = dict(os.environ, MBX_GEMM_2CTA="1")
+    env = dict(os.environ, MBX_GEMM_2CTA="1", MBX_GEMM_2CTA_BN=pair_bn)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     p = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT], env=env, cwd=root, capture_output=True, text=True,
                        timeout=300)
