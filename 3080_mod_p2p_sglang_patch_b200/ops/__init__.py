@@ -9,7 +9,6 @@ allocates.
 import contextlib
 import dataclasses
 import math
-import os
 
 import torch
 
@@ -121,15 +120,11 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
     s = splits or plan_splits
     wbuf = ws.gemm(s * M * N) if s > 1 else None
     # split-K partials are folded by a separate reduce kernel: the in-kernel
-    # reduction (pass ws.counters) measured no faster at 1 token and slower at 64.
-    # MBX_GEMM_SPLITK_INKERNEL=1 selects it for batches above 64 rows (tuning).
-    inkernel = s > 1 and M > 64 and _SPLITK_INKERNEL
-    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, ws.counters if inkernel else None)
-    launches.add(2 if s > 1 and not inkernel else 1)
+    # reduction (pass ws.counters) measured no faster at 1 token, slower at 64,
+    # and 1.5-2x slower at 512-1024 rows (qkv at TP=4/8)
+    C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, None)
+    launches.add(2 if s > 1 else 1)
     return out
-
-
-_SPLITK_INKERNEL = os.environ.get("MBX_GEMM_SPLITK_INKERNEL", "0") == "1"
 
 
 @dataclasses.dataclass

@@ -47,9 +47,15 @@ class DeviceTimer:
         return False
 
 
-def time_fn(fn, iters=10, warmup=3, flush_bytes=0):
+def time_fn(fn, iters=10, warmup=3, flush_bytes=0, spacer_cycles=200_000):
     """Per-iteration device ms of fn() (events per iteration, optional L2 flush
-    between iterations, excluded from the timing). Returns sorted list."""
+    between iterations, excluded from the timing). Returns sorted list.
+
+    A spin kernel of ``spacer_cycles`` runs between the flush and the start
+    event, so the host has queued fn()'s kernels before the start event fires:
+    otherwise the host's own launch time can fall inside the timed region of
+    a kernel shorter than it (the model runs such kernels from CUDA graphs,
+    where it does not)."""
     flush = torch.empty(flush_bytes // 4, dtype=torch.float32, device="cuda") if flush_bytes else None
     for _ in range(warmup):
         fn()
@@ -58,6 +64,8 @@ def time_fn(fn, iters=10, warmup=3, flush_bytes=0):
     for _ in range(iters):
         if flush is not None:
             flush.zero_()
+        if spacer_cycles:
+            torch.cuda._sleep(int(spacer_cycles))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()

@@ -1,9 +1,10 @@
 """Launch each hot sm_100a kernel once on a small-but-real case, for ncu.
 
-    python benchmarks/profile_kernels.py [--which gemm,fmha,decode]
+    python benchmarks/profile_kernels.py [--which gemm,qkv,fmha,decode]
 
 Cases (a few hundred MB on the device at most):
   gemm   : tcgen05 GEMM, 8B gate_up at TP=1 (M=1024, N=28672, K=4096)
+  qkv    : the 8B qkv projection at TP=1, M=1024 N=6144 K=4096 (CTA-pair kernel)
   fmha   : tcgen05 prefill attention, 1024 queries at context 4096, 32q/8kv heads
   decode : tensor-core decode attention, batch 64, context 4096, 32q/8kv heads
   fused  : fused row-parallel GEMM -> allreduce -> residual + RMSNorm (push-all
@@ -44,6 +45,13 @@ def main():
     if "gemm" in which:
         a = torch.randn(1024, 4096, device="cuda").to(torch.bfloat16)
         w = (torch.randn(28672, 4096, device="cuda") * 0.02).to(torch.bfloat16)
+        ops.gemm(a, w)
+        torch.cuda.synchronize()
+        del a, w
+    if "qkv" in which:
+        # the 8B qkv projection at TP=1: a 256 x 192 CTA-pair tile by wave cost
+        a = torch.randn(1024, 4096, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(6144, 4096, device="cuda") * 0.02).to(torch.bfloat16)
         ops.gemm(a, w)
         torch.cuda.synchronize()
         del a, w

@@ -285,35 +285,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tmem_ld_wait();
       const int kv0 = (tb + j) * BKV;
       const int lim = min(q_pos + 1, kvend_t[t]) - kv0;  // keys [kv0, kv0 + lim) are visible
-      float mx = -INFINITY;
-      if (lim >= BKV) {
+      if (lim < BKV) {
 #pragma unroll
-        for (int i = 0; i < BKV; ++i) {
-          const float x = __uint_as_float(v[i]) * sc;
-          v[i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < BKV; ++i) {
-          const float x = (i < lim) ? __uint_as_float(v[i]) * sc : -INFINITY;
-          v[i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+        for (int i = 0; i < BKV; ++i)
+          if (i >= lim) v[i] = __float_as_uint(-INFINITY);
       }
+      // Row max of the raw scores over 8 independent partial maxima (a
+      // 64-deep dependent fmax chain would sit on the softmax's critical
+      // path), then scaled once: sc > 0, so max(x * sc) = max(x) * sc.
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(v[k]);
+#pragma unroll
+      for (int i = 8; i < BKV; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(v[i]));
+#pragma unroll
+      for (int k = 4; k > 0; k >>= 1)
+#pragma unroll
+        for (int q = 0; q < k; ++q) m8[q] = fmaxf(m8[q], m8[q + k]);
+      const float mx = m8[0] * sc;
       const bool grow = mx > m + kRescaleThreshold || (m == -INFINITY && mx != -INFINITY);
       const float m_new = grow ? mx : m;
       const float corr = (m == -INFINITY || !grow) ? 1.f : tc::ex2(m - m_new);
-      float sum = 0.f;
+      // p = 2^(x * sc - m_new) in one FMA per score; row sum over 8 partial sums
+      const float neg = -m_new;
+      float s8[8] = {};
       uint32_t pk[BKV / 2];
 #pragma unroll
       for (int i = 0; i < BKV; i += 2) {
-        const float p0 = (m_new == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i]) - m_new);
-        const float p1 = (m_new == -INFINITY) ? 0.f : tc::ex2(__uint_as_float(v[i + 1]) - m_new);
-        sum += p0 + p1;
+        const float p0 = (m_new == -INFINITY) ? 0.f : tc::ex2(fmaf(__uint_as_float(v[i]), sc, neg));
+        const float p1 = (m_new == -INFINITY) ? 0.f : tc::ex2(fmaf(__uint_as_float(v[i + 1]), sc, neg));
+        s8[(i >> 1) & 7] += p0 + p1;
         __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
         pk[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
       }
+#pragma unroll
+      for (int k = 4; k > 0; k >>= 1)
+#pragma unroll
+        for (int q = 0; q < k; ++q) s8[q] += s8[q + k];
+      const float sum = s8[0];
       l = l * corr + sum;
       m = m_new;
       if (j > 0) {

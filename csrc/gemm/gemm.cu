@@ -75,6 +75,115 @@ MBX_DEVICE char* fused_half(const ArCtx& c, char* base, uint32_t epoch) {
   return base + c.fuse_off + (uint64_t)(epoch & 1u) * c.fuse_half_bytes;
 }
 
+// ---------------------------------------------------------------------------
+// Peer-push epilogue (GEMM -> allreduce / reduce-scatter), shared by the
+// single-CTA and the CTA-pair kernels. Each epilogue warp owns 32 rows of a
+// tile. Rows go to every rank's fused half (push-all: slot `rank` of
+// [W][M][N]) or to the row owner's (owner push: slot `rank` of [W][Mo][N]).
+// ---------------------------------------------------------------------------
+struct PushDst {
+  char* all[kMaxRanks];  // push-all: this rank's slot in every rank's buffer, rank-staggered; else nullptr
+};
+
+MBX_DEVICE void push_dst_init(const GemmArgs& args, uint32_t fepoch, PushDst& d) {
+#pragma unroll
+  for (int j = 0; j < kMaxRanks; ++j) {
+    const int r = (args.ar.rank + j) % max(1, args.ar.world);
+    d.all[j] = (j < args.ar.world && args.push_all)
+                   ? fused_half(args.ar, args.ar.bufs[r], fepoch) + (uint64_t)args.ar.rank * args.M * args.N * 2
+                   : nullptr;
+  }
+}
+
+// The 8 rows a lane flushes (row k*4 + lane/8 of the warp's 32, whose first
+// global row is row0): byte offsets from PushDst (push-all) or the owner's
+// destination row (owner push); ~0 / nullptr past M.
+struct PushRows {
+  char* row[8];
+  uint64_t off[8];
+};
+
+MBX_DEVICE void push_rows_init(const GemmArgs& args, uint32_t fepoch, int row0, int lane, PushRows& pr) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int grow2 = row0 + k * 4 + (lane >> 3);
+    pr.row[k] = nullptr;
+    pr.off[k] = ~0ull;
+    if (grow2 < args.M) {
+      if (args.push_all) {
+        pr.off[k] = (uint64_t)grow2 * args.N * 2;
+      } else {
+        const int owner = grow2 / args.Mo;
+        const int lrow = grow2 - owner * args.Mo;
+        pr.row[k] = fused_half(args.ar, args.ar.bufs[owner], fepoch) +
+                    (uint64_t)(args.ar.rank * args.Mo + lrow) * args.N * 2;
+      }
+    }
+  }
+}
+
+// Stage this warp's 32 rows x 32 columns (chunk c0 of a tile starting at
+// column col0; bf16, 64 B per row) into a [32 x 128 B] tile (16-byte units
+// XOR-swizzled by row); every second chunk, write 4 full 128-byte row
+// segments per store instruction to the destinations (NVLink moves whole
+// lines instead of 16-byte pieces of 32 different rows).
+template <int BN>
+MBX_DEVICE void push_chunk(const GemmArgs& args, uint8_t* stg, const uint32_t (&r)[32], int c0, int col0,
+                           const PushRows& pr, const PushDst& d, int lane) {
+  const int half64 = (c0 >> 5) & 1;
+  {
+    float f[8];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[g * 8 + j]);
+      const int unit = half64 * 4 + g;
+      *reinterpret_cast<uint4*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = pack_from<__nv_bfloat16>(f);
+    }
+  }
+  if (half64 == 1 || c0 + 32 >= BN) {
+    __syncwarp();
+    const int unit = lane & 7;
+    const int col = col0 + (c0 & ~63) + unit * 8;  // this lane's 8 columns of the staged 64
+    const bool col_ok = col < args.N && (half64 == 1 || unit < 4);
+    const uint64_t col_b = (uint64_t)col * 2;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int srow = k * 4 + (lane >> 3);
+      if (!col_ok) continue;
+      if (args.push_all) {
+        if (pr.off[k] == ~0ull) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
+        const uint64_t off = pr.off[k] + col_b;
+#pragma unroll
+        for (int j = 0; j < kMaxRanks; ++j)
+          if (d.all[j] != nullptr) *reinterpret_cast<uint4*>(d.all[j] + off) = v;
+      } else {
+        if (pr.row[k] == nullptr) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
+        *reinterpret_cast<uint4*>(pr.row[k] + col_b) = v;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// This CTA's rows are stored; the last CTA of the grid releases one flag per
+// rank (epoch fepoch) after every CTA's pushes (called by all epilogue warps).
+MBX_DEVICE void push_release(const GemmArgs& args, uint32_t fepoch, int warp, int lane, volatile int* abort) {
+  tc::named_bar_sync(1, kEpiWarps * 32);
+  if (warp == 2 && lane == 0 && !*abort) {
+    fence_acq_rel_sys();
+    const uint32_t prev = atomicAdd(args.ar.state + kStFuseGemmDone, 1u);
+    if (prev == gridDim.x - 1) {
+      fence_acq_rel_sys();
+      args.ar.state[kStFuseGemmDone] = 0;
+      for (int o = 0; o < args.ar.world; ++o)
+        st_release_sys(reinterpret_cast<uint32_t*>(args.ar.bufs[o] + kTileFlagOff) + args.ar.rank, fepoch);
+    }
+  }
+}
+
 // TMEM columns per accumulator buffer (power of two >= BN, so both buffers
 // start on aligned columns and the allocation is a power of two).
 template <int BN>
@@ -270,18 +379,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = quad * 32 + lane;
     const uint32_t fepoch =
         EPI == kEpiPushRS ? *reinterpret_cast<volatile uint32_t*>(args.ar.state + kStFuseEpoch) + 1u : 0u;
-    // push epilogue: destination bases fixed for the whole launch (push-all:
-    // this rank's slot in every rank's buffer, rank-staggered order)
-    char* dst_all[kMaxRanks];
-    if (EPI == kEpiPushRS) {
-#pragma unroll
-      for (int j = 0; j < kMaxRanks; ++j) {
-        const int r = (args.ar.rank + j) % max(1, args.ar.world);
-        dst_all[j] = (j < args.ar.world && args.push_all)
-                         ? fused_half(args.ar, args.ar.bufs[r], fepoch) + (uint64_t)args.ar.rank * args.M * args.N * 2
-                         : nullptr;
-      }
-    }
+    // push epilogue: destination bases fixed for the whole launch
+    PushDst pdst;
+    if (EPI == kEpiPushRS) push_dst_init(args, fepoch, pdst);
     uint32_t t = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
       const int m = u % args.num_m;
@@ -297,29 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tc_fence_after();
       const int grow = m * BM + row_in_tile;
       const bool row_ok = grow < args.M;
-      // push epilogue: the 8 rows this lane flushes (row k*4 + lane/8 of the
-      // warp's 32), as byte offsets from dst_all[] (push-all) or as the
-      // owner's destination row (owner push); nullptr / ~0 = past M
-      char* prow[8];
-      uint64_t prow_off[8];
-      if (EPI == kEpiPushRS) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int grow2 = m * BM + quad * 32 + k * 4 + (lane >> 3);
-          prow[k] = nullptr;
-          prow_off[k] = ~0ull;
-          if (grow2 < args.M) {
-            if (args.push_all) {
-              prow_off[k] = (uint64_t)grow2 * args.N * 2;
-            } else {
-              const int owner = grow2 / args.Mo;
-              const int lrow = grow2 - owner * args.Mo;
-              prow[k] = fused_half(args.ar, args.ar.bufs[owner], fepoch) +
-                        (uint64_t)(args.ar.rank * args.Mo + lrow) * args.N * 2;
-            }
-          }
-        }
-      }
+      PushRows prows;
+      if (EPI == kEpiPushRS) push_rows_init(args, fepoch, m * BM + quad * 32, lane, prows);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -327,50 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_ld_wait();
         const int gcol = n * BN + c0;
         const int valid = min(32, args.N - gcol);
-        if (EPI == kEpiPushRS) {
-          // Stage this warp's 32 rows x 32 columns (bf16, 64 B per row) into a
-          // [32 x 128 B] tile (16-byte units XOR-swizzled by row); every second
-          // chunk, write 4 full 128-byte row segments per store instruction to
-          // the row owners' symmetric buffers (NVLink moves whole lines instead
-          // of 16-byte pieces of 32 different rows).
-          uint8_t* stg = smem + L::kStageOut + (warp - 2) * (32 * 128);
-          const int half64 = (c0 >> 5) & 1;
-          {
-            float f[8];
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[g * 8 + j]);
-              const int unit = half64 * 4 + g;
-              *reinterpret_cast<uint4*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = pack_from<__nv_bfloat16>(f);
-            }
-          }
-          if (half64 == 1 || c0 + 32 >= BN) {
-            __syncwarp();
-            const int unit = lane & 7;
-            const int col = n * BN + (c0 & ~63) + unit * 8;  // this lane's 8 columns of the staged 64
-            const bool col_ok = col < args.N && (half64 == 1 || unit < 4);
-            const uint64_t col_b = (uint64_t)col * 2;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int srow = k * 4 + (lane >> 3);
-              if (!col_ok) continue;
-              if (args.push_all) {
-                if (prow_off[k] == ~0ull) continue;
-                const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
-                const uint64_t off = prow_off[k] + col_b;
-#pragma unroll
-                for (int j = 0; j < kMaxRanks; ++j)
-                  if (dst_all[j] != nullptr) *reinterpret_cast<uint4*>(dst_all[j] + off) = v;
-              } else {
-                if (prow[k] == nullptr) continue;
-                const uint4 v = *reinterpret_cast<const uint4*>(stg + srow * 128 + ((unit ^ (srow & 7)) << 4));
-                *reinterpret_cast<uint4*>(prow[k] + col_b) = v;
-              }
-            }
-            __syncwarp();
-          }
-        }
+        if (EPI == kEpiPushRS)
+          push_chunk<BN>(args, smem + L::kStageOut + (warp - 2) * (32 * 128), r, c0, n * BN, prows, pdst, lane);
         if (EPI != kEpiPushRS && row_ok && valid > 0) {
           if (EPI == kEpiPushRS) {
             // staged below (coalesced 128-byte row segments)
@@ -454,20 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (EPI == kEpiPushRS) {
-      // This CTA's rows are stored; the last CTA of the grid tells every owner.
-      tc::named_bar_sync(1, kEpiWarps * 32);
-      if (warp == 2 && lane == 0 && !*abort) {
-        fence_acq_rel_sys();
-        const uint32_t prev = atomicAdd(args.ar.state + kStFuseGemmDone, 1u);
-        if (prev == gridDim.x - 1) {
-          fence_acq_rel_sys();
-          args.ar.state[kStFuseGemmDone] = 0;
-          for (int o = 0; o < args.ar.world; ++o)
-            st_release_sys(reinterpret_cast<uint32_t*>(args.ar.bufs[o] + kTileFlagOff) + args.ar.rank, fepoch);
-        }
-      }
-    }
+    if (EPI == kEpiPushRS) push_release(args, fepoch, warp, lane, abort);
   }
 
   tc::tc_fence_before();
@@ -595,20 +619,22 @@ int num_sms() {
 // the two cluster barriers, at the start and at the end, which every thread
 // of both CTAs reaches on every path.
 // ==========================================================================
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kStaging = false>
 struct Smem2 {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = (BN / 2) * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOff = STAGES * kStageBytes;
-  static constexpr int kTotal = kBarOff + 256 + 1024;
+  // push epilogue: per epilogue warp a [32 rows x 128 B] staging tile
+  static constexpr int kStageOut = kBarOff + 256;
+  static constexpr int kTotal = kStageOut + (kStaging ? 4 * 32 * 128 : 0) + 1024;
 };
 
 template <int BN, int STAGES, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          GemmArgs args) {
-  using L = Smem2<BN, STAGES>;
+  using L = Smem2<BN, STAGES, EPI == kEpiPushRS>;
   static_assert(BN % 32 == 0 && BN <= 256, "pair tile width");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -726,6 +752,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quad = warp & 3;
+    const uint32_t fepoch =
+        EPI == kEpiPushRS ? *reinterpret_cast<volatile uint32_t*>(args.ar.state + kStFuseEpoch) + 1u : 0u;
+    PushDst pdst;
+    if (EPI == kEpiPushRS) push_dst_init(args, fepoch, pdst);
     uint32_t t = 0;
     for (int u = pair; u < units; u += npairs, ++t) {
       const int m = u % num_m2;
@@ -739,6 +769,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc::tc_fence_after();
       const int grow = m * 2 * BM + (int)rank * BM + quad * 32 + lane;
       const bool row_ok = grow < args.M;
+      PushRows prows;
+      if (EPI == kEpiPushRS) push_rows_init(args, fepoch, m * 2 * BM + (int)rank * BM + quad * 32, lane, prows);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -746,7 +778,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc::tmem_ld_wait();
         const int gcol = n * BN + c0;
         const int valid = min(32, args.N - gcol);
-        if (row_ok && valid > 0) {
+        if (EPI == kEpiPushRS) {
+          push_chunk<BN>(args, smem + L::kStageOut + (warp - 2) * (32 * 128), r, c0, n * BN, prows, pdst, lane);
+        } else if (row_ok && valid > 0) {
           __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(args.out) + (int64_t)grow * args.ldc + gcol;
           const __nv_bfloat16* res =
               EPI == kEpiBf16AddResidual ? args.residual + (int64_t)grow * args.ldc + gcol : nullptr;
@@ -760,6 +794,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         else tc::mbar_arrive_remote(&tempty[acc], 0);
       }
     }
+    if (EPI == kEpiPushRS) push_release(args, fepoch, warp, lane, abort);
   }
 
   tc::tc_fence_before();
@@ -771,7 +806,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, int EPI>
 void launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t s) {
-  using L = Smem2<BN, STAGES>;
+  using L = Smem2<BN, STAGES, EPI == kEpiPushRS>;
   auto kern = gemm2_tcgen05_kernel<BN, STAGES, EPI>;
   static SmemLimit limit;
   limit.ensure((const void*)kern, L::kTotal);
@@ -865,6 +900,8 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
   return plan_for(M, N, K, num_sms());
 }
 
+static int pair_gemm_bn(int64_t M, int64_t N, const GemmPlan& p, int sms);
+
 namespace {
 GemmArgs push_args(const ArCtx& c, int64_t M, int64_t N, int64_t K, int bn, int64_t Mo, bool push_all, uint32_t* err) {
   GemmArgs a;
@@ -890,6 +927,29 @@ void launch_push_gemm(const ArCtx& c, const void* A, int64_t lda, const void* B,
                       int64_t K, int64_t Mo, bool push_all, uint32_t* err, cudaStream_t s) {
   const int sms = num_sms();
   GemmPlan p = plan_for(M, N, K, sms);
+  int bn2 = pair_gemm_bn(M, N, p, sms);
+  // MBX_PUSH_GEMM_BN=256|192|128 forces the pair tile width of the push GEMM
+  // alone (narrower tiles give more waves, whose pushes then overlap later
+  // tiles' MMAs; tuning)
+  static const int push_bn = [] {
+    const char* v = std::getenv("MBX_PUSH_GEMM_BN");
+    const int b = v ? std::atoi(v) : 0;
+    return (b == 256 || b == 192 || b == 128) ? b : 0;
+  }();
+  if (push_bn && M >= 2 * BM) bn2 = push_bn;
+  if (bn2 > 0) {
+    // CTA-pair tiles, same tile choice as the plain GEMM of this shape
+    GemmArgs pa = push_args(c, M, N, K, bn2, Mo, push_all, err);
+    const CUtensorMap ta2 = make_map(A, M, K, lda, BM);
+    const CUtensorMap tb2 = make_map(B, N, K, ldb, bn2 / 2);
+    const int units2 = (int)((M + 2 * BM - 1) / (2 * BM)) * pa.num_n;
+    const int grid2 = 2 * std::min(units2, sms / 2);
+    if (bn2 == 256) launch_pair_cfg<256, 6, kEpiPushRS>(ta2, tb2, pa, grid2, s);
+    else if (bn2 == 192) launch_pair_cfg<192, 7, kEpiPushRS>(ta2, tb2, pa, grid2, s);
+    else launch_pair_cfg<128, 8, kEpiPushRS>(ta2, tb2, pa, grid2, s);
+    MBX_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   GemmArgs a = push_args(c, M, N, K, p.bn, Mo, push_all, err);
   const CUtensorMap ta = make_map(A, M, K, lda, BM);
   const CUtensorMap tb = make_map(B, N, K, ldb, p.bn);

@@ -152,3 +152,55 @@ def test_emulated_mixed_calls_share_epochs():
                 assert torch.all(outs[r] == torch.tensor(W * v, dtype=want, device="cuda"))
                 assert torch.all(res[r] == torch.tensor(W * v, dtype=want, device="cuda"))
         assert ew.epochs() == [24] * W
+
+
+_PAIR_PUSH_SCRIPT = r"""
+import importlib, sys, torch
+emulate = importlib.import_module("3080_mod_p2p_sglang_patch_b200.parallel.emulate")
+ref = importlib.import_module("3080_mod_p2p_sglang_patch_b200.ops.reference")
+g = torch.Generator(device="cuda").manual_seed(7)
+def rnd(*s):
+    return torch.randn(*s, generator=g, device="cuda").to(torch.bfloat16)
+K, N, eps = 1024, 2048, 1e-5
+w_norm = torch.ones(N, dtype=torch.bfloat16, device="cuda")
+worst = 0.0
+for W, push_all in ((2, True), (4, False), (8, False)):
+    with emulate.EmulatedWorld(W, fuse_half_bytes=24 << 20) as ew:
+        for M in (512, 777):
+            a_s = [rnd(M, K) for _ in range(W)]
+            w_s = [(rnd(N, K) * 0.03).to(torch.bfloat16) for _ in range(W)]
+            res0 = rnd(M, N)
+            res = [res0.clone() for _ in range(W)]
+            outs = ew.gemm_all_reduce_rmsnorm(a_s, w_s, res, w_norm, eps, push_all=push_all)
+            parts = [ref.gemm(a_s[r], w_s[r]).to(torch.bfloat16).float() for r in range(W)]
+            acc = parts[0].clone()
+            for p in parts[1:]:
+                acc += p
+            want, _ = ref.fused_add_rmsnorm(acc.to(torch.bfloat16), res0, w_norm, eps)
+            torch.cuda.synchronize()
+            ew.check()
+            assert int(ew.err.item()) == 0
+            for r in range(W):
+                assert torch.equal(res[r], res[0])
+                err = (outs[r].float() - want).abs().max().item()
+                worst = max(worst, err)
+                assert err < 6e-2, (W, push_all, M, r, err)
+print("PAIR-PUSH-OK", worst)
+"""
+
+
+@pytest.mark.parametrize("pair_bn", ["256", "192", "128"])
+def test_emulated_fused_gemm_on_cta_pair_kernel(pair_bn):
+    """The push epilogue on the CTA-pair GEMM (forced with MBX_GEMM_2CTA=1 and
+    each pair tile width; read once per process, so it runs in a child):
+    push-all at 2 ranks, owner push at 4 and 8, against fp32."""
+    import os
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    env = dict(os.environ, MBX_GEMM_2CTA="1", MBX_GEMM_2CTA_BN=pair_bn)
+    p = subprocess.run([sys.executable, "-c", _PAIR_PUSH_SCRIPT], env=env, cwd=ROOT, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0 and "PAIR-PUSH-OK" in p.stdout, p.stdout[-2000:] + p.stderr[-4000:]
