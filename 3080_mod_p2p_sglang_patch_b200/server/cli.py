@@ -1,6 +1,7 @@
 """Command line of the server: sglang-style flags, the --tp / --dp
 launchers, and ``main`` (one process per GPU)."""
 import argparse
+import dataclasses
 import datetime
 import logging
 import os
@@ -264,6 +265,10 @@ def main(argv=None):
             tokenizer.tok.chat_template = load_chat_template(args.chat_template)
     else:
         cfg = models.LlamaConfig.by_name(name)
+        if args.max_seq is not None and args.max_seq > cfg.max_pos:
+            # random weights have no trained position range: a longer context
+            # only needs a longer RoPE table (long-prompt prefill benchmarks)
+            cfg = dataclasses.replace(cfg, max_pos=args.max_seq)
         opts.setdefault("max_seq", min(16384, cfg.max_pos))
         eng = eng_mod.LLMEngine(cfg, tp=tp, device=dev, **opts)
         if args.tokenizer_path:
