@@ -8,10 +8,32 @@ pinned host->device copy; padded rows decode into a reserved scratch page.
 The communicator's buffers and epochs never move, so replays need no
 re-registration (the reference's graph story, docs/principle.md:80-83).
 """
+import contextlib
+import gc
+
 import torch
 
 from .. import ops
 from ..utils import launches
+
+
+@contextlib.contextmanager
+def no_gc():
+    """Collect garbage, then keep the collector off for the capture.
+
+    A capture in the global mode is invalidated by a graph or other CUDA
+    resource destroyed meanwhile, and the collector runs whenever allocations
+    pile up: an unreachable engine of an earlier caller freeing its captured
+    graphs in the middle of this capture ends it with
+    ``cudaErrorStreamCaptureInvalidated``."""
+    gc.collect()
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
 
 
 class DecodeGraphRunner:
@@ -81,7 +103,7 @@ class DecodeGraphRunner:
                 comm = e.tp.ca_comm if e.tp is not None else None
                 ctx = comm.capture() if comm is not None else _null()
                 before = launches.get()
-                with ctx:
+                with ctx, no_gc():
                     with torch.cuda.graph(g, pool=self.pool, stream=s):
                         out = fwd(ids, pos, kvl, slots, rows, splits)
                 n_kernels = launches.get() - before
@@ -237,7 +259,7 @@ class PrefillGraphRunner:
             comm = e.tp.ca_comm if e.tp is not None else None
             ctx = comm.capture() if comm is not None else _null()
             before = launches.get()
-            with ctx:
+            with ctx, no_gc():
                 with torch.cuda.graph(g, stream=s):
                     self.out = self._forward()
             self.kernels_per_replay = launches.get() - before
