@@ -77,8 +77,8 @@ class MailboxAR:
         self.rank = dist.get_rank(group=group)
         self.world_size = dist.get_world_size(group=group)
         self.max_size = int(max_size if max_size is not None else self.cfg.max_size_for(self.world_size))
-        self.counters = {"oneshot_push": 0, "oneshot_pull": 0, "twoshot": 0, "twoshot_push": 0, "nvls": 0, "cpu": 0,
-                         "fallback": 0, "errors": 0, "fused": 0, "allgather": 0}
+        self.counters = {**{name: 0 for name in ALGO_NAMES.values()}, "cpu": 0, "fallback": 0, "errors": 0, "fused": 0,
+                         "allgather": 0}
         self._buf = None
         self._ar = None
         self._cpu = None

@@ -76,9 +76,11 @@ class EmulatedWorld:
         return [int(s[0].item()) for s in self.states]
 
     # ------------------------------------------------------------------ collectives
-    def allreduce(self, xs, algo=ALGO_ONESHOT_PUSH):
-        """outs[r] = sum over ranks of xs (one emulated launch)."""
-        outs = [torch.empty_like(x) for x in xs]
+    def allreduce(self, xs, algo=ALGO_ONESHOT_PUSH, outs=None):
+        """outs[r] = sum over ranks of xs (one emulated launch); ``outs=xs``
+        reduces in place."""
+        if outs is None:
+            outs = [torch.empty_like(x) for x in xs]
         nbytes = xs[0].numel() * xs[0].element_size()
         self._launch(self.C.EMU_ALLREDUCE, algo, DTYPE_IDS[xs[0].dtype], [x.data_ptr() for x in xs],
                      [o.data_ptr() for o in outs], nbytes=nbytes)

@@ -414,7 +414,7 @@ MBX_DEVICE float block_sum(float v, float* red) {
 
 struct RowCtx {
   int t0, tstep;  // this thread's first 16-byte vector of the row and its stride
-  bool warp;      // one warp per row (warp reduction) or the whole block
+  int group;      // warps per row: 1 (warp reduction), G > 1 (G warps, named barrier), 0 (whole block)
 };
 
 // Rows b, b+g, ... below n owned by this block.
@@ -422,15 +422,38 @@ MBX_DEVICE int block_rows(int n) {
   return n > (int)blockIdx.x ? (n - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 }
 
-// fn(rc, k) for k in [0, count) (count uniform over the block).
+// fn(rc, k) for k in [0, count) (count uniform over the block). One row: the
+// whole block. Several rows: groups of G warps per row, G the largest power of
+// two up to 8 with 2 * count * G <= warps (more warps in flight per row when the
+// block has few rows); groups take rows k, k + groups, ... A row's partial sums
+// meet through the group's own named barrier, so a group whose rows run out
+// stops without the others.
 template <typename Fn>
 MBX_DEVICE void for_norm_rows(int count, Fn fn) {
   if (count == 1) {
-    fn(RowCtx{(int)threadIdx.x, (int)blockDim.x, false}, 0);
+    fn(RowCtx{(int)threadIdx.x, (int)blockDim.x, 0}, 0);
     return;
   }
   const int warps = (int)(blockDim.x >> 5);
-  for (int k = threadIdx.x >> 5; k < count; k += warps) fn(RowCtx{(int)(threadIdx.x & 31), 32, true}, k);
+  int G = 1;
+  while (G < 8 && count * G * 2 <= warps) G *= 2;
+  const int w = (int)(threadIdx.x >> 5);
+  const int groups = warps / G;
+  for (int k = w / G; k < count; k += groups) fn(RowCtx{(w % G) * 32 + (int)(threadIdx.x & 31), 32 * G, G}, k);
+}
+
+// Sum over the G warps of this thread's group (groups of G consecutive warps),
+// through red[] (one word per warp) and the group's named barrier 1 + group
+// (G >= 2 and at most 16 warps per block give ids 1..8 of the 16).
+MBX_DEVICE float group_sum(float v, float* red, int G) {
+  v = warp_sum(v);
+  const int w = (int)(threadIdx.x >> 5), g = w / G;
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G * 32) : "memory");  // earlier readers of red[] are done
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(G * 32) : "memory");
+  float s = 0.f;
+  for (int i = 0; i < G; ++i) s += red[g * G + i];
+  return s;
 }
 
 // Copy/reduce phases over the block's rows (row j = b + j*g of a range):
@@ -513,7 +536,7 @@ MBX_DEVICE void residual_rmsnorm_row(const RowCtx& rc, Src src, uint4* residual_
       }
     }
   }
-  const float tot = rc.warp ? warp_sum(ss) : block_sum(ss, red);
+  const float tot = rc.group == 1 ? warp_sum(ss) : (rc.group == 0 ? block_sum(ss, red) : group_sum(ss, red, rc.group));
   const float rstd = rsqrtf(tot / (float)H + eps);
   constexpr int KU2 = 4;
   for (int p0 = rc.t0; p0 < hvec; p0 += rc.tstep * KU2) {

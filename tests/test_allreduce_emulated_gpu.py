@@ -57,8 +57,9 @@ def test_emulated_allreduce_bit_exact(W, dtype):
             for numel in (8, 4096 * 3 + 40, 1 << 18):
                 for rep in range(2):
                     xs = [_rand((numel,), 1000 * calls + 17 * r + rep, dtype) for r in range(W)]
-                    outs = ew.allreduce(xs, algo=a)
                     want = _rank_sum(xs).to(dtype)
+                    # the second repetition reduces in place (out == in)
+                    outs = ew.allreduce(xs, algo=a, outs=xs if rep else None)
                     torch.cuda.synchronize()
                     ew.check()
                     for r in range(W):
@@ -141,7 +142,7 @@ def test_emulated_mixed_calls_share_epochs():
         for it in range(12):
             v = float(it % 251 + 1)
             xs = [torch.full((64, H), v, dtype=torch.bfloat16, device="cuda") for _ in range(W)]
-            outs = ew.allreduce(xs, algo=comm.ALGO_IDS[ALGOS[it % 4]])
+            outs = ew.allreduce(xs, algo=comm.ALGO_IDS[ALGOS[it % len(ALGOS)]])
             res = [torch.zeros(64, H, dtype=torch.bfloat16, device="cuda") for _ in range(W)]
             algo = comm.ALGO_TWOSHOT_PUSH if it % 2 else comm.ALGO_ONESHOT_PUSH
             ew.all_reduce_rmsnorm(xs, res, w, 1e-5, algo=algo)
