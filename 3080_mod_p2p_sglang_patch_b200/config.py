@@ -35,12 +35,13 @@ class CommConfig:
     # falls back to NCCL. The kernels chunk through the buffer, so this is a
     # policy limit, not a buffer limit. None = per world size from
     # ``max_size_by_world``: the size where NCCL's pipelined ring overtakes the
-    # in-house kernels on an 8xB200 NVSwitch box (measured with
-    # benchmarks/allreduce_sweep.py: TP=2 32 MB 80 us vs NCCL 85 us, 64 MB 160 vs
-    # 154; TP=8 64 MB 257 vs 274, 128 MB 515 vs 397).
+    # in-house kernels on an 8xB200 NVSwitch box (benchmarks/allreduce_sweep.py,
+    # graph mode: TP=2 32 MB 79 us vs NCCL 84, 64 MB 158 vs 152; TP=4 16 MB 56 vs
+    # 72, 32 MB 121 vs 121, 64 MB 231 vs 188; TP=8 64 MB 259 vs 276, 128 MB 518
+    # vs 395).
     max_size: int = None
     max_size_by_world: dict = dataclasses.field(
-        default_factory=lambda: {2: 48 * MiB, 3: 64 * MiB, 4: 64 * MiB, 5: 96 * MiB, 6: 96 * MiB, 7: 96 * MiB,
+        default_factory=lambda: {2: 48 * MiB, 3: 32 * MiB, 4: 32 * MiB, 5: 96 * MiB, 6: 96 * MiB, 7: 96 * MiB,
                                  8: 96 * MiB}
     )
     # one ping-pong data half of the symmetric buffer (two halves are mapped)
@@ -65,8 +66,11 @@ class CommConfig:
     oneshot_max: dict = dataclasses.field(
         default_factory=lambda: {2: 32 * MiB, 3: 2 * MiB, 4: 2 * MiB, 5: 1 * MiB, 6: 1 * MiB, 7: 1 * MiB, 8: 1 * MiB}
     )
-    # NVLS is preferred over two-shot at/above this many bytes
-    nvls_min: int = 64 * MiB
+    # NVLS is preferred over two-shot push at/above this many bytes on
+    # ``nvls_min_world`` ranks or more (TP=8: 32 MB 130 us vs 142, 64 MB 260 vs
+    # 268; TP=4: never faster, 64 MB 255 vs 231)
+    nvls_min: int = 32 * MiB
+    nvls_min_world: int = 8
     # grid cap of the allreduce kernels (blocks)
     max_blocks: int = 148
     # CPU transport: bytes per slot of the shared-memory mailbox

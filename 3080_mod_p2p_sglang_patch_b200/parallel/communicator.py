@@ -235,7 +235,8 @@ class MailboxAR:
         """Algorithm by size and world size (tuned thresholds in CommConfig)."""
         if nbytes <= self.cfg.oneshot_max.get(self.world_size, 0):
             return ALGO_ONESHOT_PUSH
-        if self._buf is not None and self._buf.mc_ptr and nbytes >= self.cfg.nvls_min and self.world_size >= 4:
+        if self._buf is not None and self._buf.mc_ptr and nbytes >= self.cfg.nvls_min and \
+                self.world_size >= self.cfg.nvls_min_world:
             return ALGO_NVLS
         return ALGO_TWOSHOT_PUSH
 

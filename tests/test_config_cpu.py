@@ -35,7 +35,7 @@ def test_per_world_fallback_size(monkeypatch):
         monkeypatch.delenv(k, raising=False)
     c = cfg_mod.CommConfig.from_env()
     MiB = 1 << 20
-    assert c.max_size_for(2) == 48 * MiB and c.max_size_for(4) == 64 * MiB and c.max_size_for(8) == 96 * MiB
+    assert c.max_size_for(2) == 48 * MiB and c.max_size_for(4) == 32 * MiB and c.max_size_for(8) == 96 * MiB
     # the reference's own limit is smaller: everything it handled in-house stays in-house here
     assert all(c.max_size_for(w) >= cfg_mod.REFERENCE_MAX_SIZE for w in range(2, 9))
 
