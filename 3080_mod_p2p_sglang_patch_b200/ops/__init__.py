@@ -10,6 +10,8 @@ import contextlib
 import dataclasses
 import math
 
+import os
+
 import torch
 
 from .._ext import cuda_ext
@@ -157,24 +159,28 @@ class Int4Weight:
 
 
 AWQ_GEMV_MAX_ROWS = 8     # rows per int4 GEMV launch
-AWQ_GEMV_ROW_LIMIT = 64   # up to here (decode batches) the GEMV runs over 8-row chunks
+# up to this many rows the int4 GEMV runs (in 8-row chunks); above it the layer
+# is dequantized for the tcgen05 GEMM. Measured on 8B decode at TP=1: 16 rows
+# 11.7 ms per step dequantized vs 15.6 ms as two GEMV chunks; 64 rows 15.8 vs
+# 58.3 (MBX_AWQ_GEMV_ROWS overrides)
+AWQ_GEMV_ROW_LIMIT = int(os.environ.get("MBX_AWQ_GEMV_ROWS", "8"))
 
 
 def awq_gemm(a: torch.Tensor, w: Int4Weight, out: torch.Tensor = None, residual: torch.Tensor = None):
     """out[M, N] = a @ W^T (+ residual) for an int4 weight.
 
-    Up to 64 rows (decode batches): the int4 GEMV over chunks of 8 rows, each
-    reading the packed weight once (a quarter of bf16's bytes per chunk).
-    Larger batches (prefill): the layer dequantized to bf16 into a reused
-    scratch buffer and the tcgen05 GEMM (the expansion costs about 2.25x the
-    bf16 weight bytes, which only a large batch amortises)."""
+    Up to AWQ_GEMV_ROW_LIMIT rows (small decode batches): the int4 GEMV, which
+    reads the packed weight once (a quarter of bf16's bytes) and does its
+    math on the CUDA cores. Larger batches: the layer dequantized to bf16
+    into a reused scratch buffer and the tcgen05 GEMM (the expansion costs
+    about 2.25x the bf16 weight bytes)."""
     C = cuda_ext()
     M = a.shape[0]
     N, K = w.shape
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     ws = workspace(a.device)
-    if M <= AWQ_GEMV_ROW_LIMIT and w.group <= 256 and w.group % 8 == 0:
+    if M <= AWQ_GEMV_ROW_LIMIT and w.group <= 256 and w.group % 32 == 0:
         part, _ = ws.awq(n_ws=(K // w.group) * min(M, AWQ_GEMV_MAX_ROWS) * N)
         for r0 in range(0, M, AWQ_GEMV_MAX_ROWS):
             r1 = min(M, r0 + AWQ_GEMV_MAX_ROWS)

@@ -5,6 +5,8 @@
 Cases (a few hundred MB on the device at most):
   gemm   : tcgen05 GEMM, 8B gate_up at TP=1 (M=1024, N=28672, K=4096)
   qkv    : the 8B qkv projection at TP=1, M=1024 N=6144 K=4096 (CTA-pair kernel)
+  qkv8   : the 8B qkv shard at TP=8, M=1024 N=768 K=4096 (split-K + reduce), run
+           4 times after a 256 MB L2 flush each (capture with -s 3 -c 1 or 2)
   fmha   : tcgen05 prefill attention, 1024 queries at context 4096, 32q/8kv heads
   decode : tensor-core decode attention, batch 64, context 4096, 32q/8kv heads
   fused  : fused row-parallel GEMM -> allreduce -> residual + RMSNorm (push-all
@@ -55,6 +57,16 @@ def main():
         ops.gemm(a, w)
         torch.cuda.synchronize()
         del a, w
+    if "qkv8" in which:
+        a = torch.randn(1024, 4096, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(768, 4096, device="cuda") * 0.02).to(torch.bfloat16)
+        out = torch.empty(1024, 768, device="cuda", dtype=torch.bfloat16)
+        flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+        for _ in range(4):
+            flush.zero_()
+            ops.gemm(a, w, out=out)
+        torch.cuda.synchronize()
+        del a, w, out, flush
     if "fmha" in which or "decode" in which:
         L = 4096
         nblk = L // P

@@ -125,11 +125,18 @@ def test_awq_int4_gemv_and_dequant():
             out = res.clone().cuda()
             ops.awq_gemm(x.cuda(), w, out=out, residual=out)       # in place, like the residual epilogue
             assert (out.float().cpu() - (want + res.float())).abs().max().item() < tol + 2e-2
-        # 40 rows: the GEMV over 8-row chunks; 200 rows: the dequant + tcgen05 GEMM path
+        # 40 rows: the GEMV over 8-row chunks (row limit raised for the check)
+        # and the dequant + tcgen05 GEMM path; 200 rows: the dequant path
         x = torch.randn(40, K).to(torch.bfloat16)
-        got = ops.awq_gemm(x.cuda(), w).float().cpu()
         want = x.float() @ ref_w.t()
-        assert (got - want).abs().max().item() < 2e-2 * want.abs().max().item() + 1e-2
+        limit = ops.AWQ_GEMV_ROW_LIMIT
+        for rows in (64, limit):
+            ops.AWQ_GEMV_ROW_LIMIT = rows
+            try:
+                got = ops.awq_gemm(x.cuda(), w).float().cpu()
+            finally:
+                ops.AWQ_GEMV_ROW_LIMIT = limit
+            assert (got - want).abs().max().item() < 2e-2 * want.abs().max().item() + 1e-2, rows
         x = torch.randn(200, K).to(torch.bfloat16)
         got = ops.awq_gemm(x.cuda(), w).float().cpu()
         want = x.float() @ ref_w.to(torch.bfloat16).float().t()
