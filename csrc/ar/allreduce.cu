@@ -82,6 +82,7 @@ MBX_DEVICE void ar_oneshot_push(const ArCtx& c, const uint4* __restrict__ in, ui
 template <typename T, int W>
 __global__ void __launch_bounds__(kArThreads) ar_oneshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
                                                                      uint4* __restrict__ out, uint64_t nvec) {
+  pdl_wait();
   ar_oneshot_push<T, W>(c, in, out, nvec);
 }
 
@@ -119,6 +120,7 @@ MBX_DEVICE void ar_oneshot_pull(const ArCtx& c, const uint4* __restrict__ in, ui
 template <typename T, int W>
 __global__ void __launch_bounds__(kArThreads) ar_oneshot_pull_kernel(ArCtx c, const uint4* __restrict__ in,
                                                                      uint4* __restrict__ out, uint64_t nvec) {
+  pdl_wait();
   ar_oneshot_pull<T, W>(c, in, out, nvec);
 }
 
@@ -176,6 +178,7 @@ done:
 template <typename T, int W>
 __global__ void __launch_bounds__(kArThreads) ar_twoshot_kernel(ArCtx c, const uint4* __restrict__ in,
                                                                 uint4* __restrict__ out, uint64_t nvec) {
+  pdl_wait();
   ar_twoshot<T, W>(c, in, out, nvec);
 }
 
@@ -286,6 +289,7 @@ done:
 template <typename T, int W>
 __global__ void __launch_bounds__(kArThreads) ar_twoshot_push_kernel(ArCtx c, const uint4* __restrict__ in,
                                                                      uint4* __restrict__ out, uint64_t nvec) {
+  pdl_wait();
   ar_twoshot_push<T, W>(c, in, out, nvec);
 }
 
@@ -337,6 +341,7 @@ MBX_DEVICE void multimem_st(void* mc, const uint4& v) {
 template <typename T, int W>
 __global__ void __launch_bounds__(kArThreads) ar_nvls_kernel(ArCtx c, const uint4* __restrict__ in,
                                                              uint4* __restrict__ out, uint64_t nvec) {
+  pdl_wait();
   __shared__ bool s_ok;
   const uint32_t epoch = call_epoch(c);
   trace_mark(c, 0);
@@ -617,6 +622,7 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_oneshot_kernel(ArCtx c,
                                                                         uint4* residual, const uint4* __restrict__ w,
                                                                         uint4* __restrict__ out, int M, int H,
                                                                         float eps) {
+  pdl_wait();
   ar_rmsnorm_oneshot<W>(c, in, residual, w, out, M, H, eps);
 }
 
@@ -669,6 +675,7 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_kernel(ArCtx c,
                                                                         uint4* residual, const uint4* __restrict__ w,
                                                                         uint4* __restrict__ out, int M, int H,
                                                                         float eps) {
+  pdl_wait();
   ar_rmsnorm_twoshot<W>(c, in, residual, w, out, M, H, eps);
 }
 
@@ -737,6 +744,7 @@ template <int W>
 __global__ void __launch_bounds__(kArThreads) fused_rs_norm_kernel(ArCtx c, int M, int N, int Mo, uint4* residual,
                                                                    const uint4* __restrict__ w,
                                                                    uint4* __restrict__ out, float eps) {
+  pdl_wait();
   fused_rs_norm<W>(c, M, N, Mo, residual, w, out, eps);
 }
 
@@ -751,6 +759,7 @@ template <int W>
 __global__ void __launch_bounds__(kArThreads) fused_allsum_norm_kernel(ArCtx c, int M, int N, uint4* residual,
                                                                        const uint4* __restrict__ w,
                                                                        uint4* __restrict__ out, float eps) {
+  pdl_wait();
   __shared__ bool s_ok;
   __shared__ float red[32];
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
@@ -815,6 +824,7 @@ MBX_DEVICE void grid_done_release(const ArCtx& c, int counter_word, uint32_t epo
 template <int W>
 __global__ void __launch_bounds__(kArThreads) sp_rs_push_kernel(ArCtx c, const uint4* __restrict__ x, int M, int N,
                                                                  int Mo) {
+  pdl_wait();
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
   if (poisoned(c)) return;
   const int nvec = N / 8;
@@ -834,6 +844,7 @@ __global__ void __launch_bounds__(kArThreads) sp_rs_push_kernel(ArCtx c, const u
 template <int W>
 __global__ void __launch_bounds__(kArThreads) sp_rs_norm_ag_kernel(ArCtx c, int M, int N, int Mo, uint4* res_own,
                                                                    const uint4* __restrict__ w, float eps) {
+  pdl_wait();
   __shared__ bool s_ok;
   __shared__ float red[32];
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch) + 1u;
@@ -875,6 +886,7 @@ __global__ void __launch_bounds__(kArThreads) sp_rs_norm_ag_kernel(ArCtx c, int 
 }
 
 __global__ void sp_ag_wait_kernel(ArCtx c, int owners) {
+  pdl_wait();
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(c.state + kStFuseEpoch);
   if (poisoned(c)) return;
   const int o = threadIdx.x;
@@ -953,6 +965,7 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_twoshot_push_kernel(ArC
                                                                              const uint4* __restrict__ w,
                                                                              uint4* __restrict__ out, int M, int H,
                                                                              float eps) {
+  pdl_wait();
   ar_rmsnorm_twoshot_push<W>(c, in, residual, w, out, M, H, eps);
 }
 
@@ -1106,6 +1119,7 @@ MBX_DEVICE void ar_allgather(const ArCtx& c, const uint4* __restrict__ in, uint4
 template <int W>
 __global__ void __launch_bounds__(kArThreads) ar_allgather_kernel(ArCtx c, const uint4* __restrict__ in,
                                                                   uint4* __restrict__ out, uint64_t nvec) {
+  pdl_wait();
   ar_allgather<W>(c, in, out, nvec);
 }
 
@@ -1255,15 +1269,17 @@ void ar_launch(const ArCtx& c, int algo, int dtype, const void* in, void* out, u
     if (algo == kOneShotPush || algo == kOneShotPull) {
       const int g = ar_grid(nvec, max_blocks);
       MBX_DISPATCH_T(dtype, MBX_DISPATCH_W(W_, {
-        if (algo == kOneShotPush) ar_oneshot_push_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
-        else ar_oneshot_pull_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+        if (algo == kOneShotPush) launch_k(ar_oneshot_push_kernel<T, W>, dim3(g), dim3(kArThreads), 0, stream,
+                                           c, i4, o4, nvec);
+        else launch_k(ar_oneshot_pull_kernel<T, W>, dim3(g), dim3(kArThreads), 0, stream, c, i4, o4, nvec);
       }));
     } else {
       const int g = ar_grid((nvec + W_ - 1) / W_, max_blocks);
       MBX_DISPATCH_T(dtype, MBX_DISPATCH_W(W_, {
-        if (algo == kTwoShot) ar_twoshot_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
-        else if (algo == kTwoShotPush) ar_twoshot_push_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
-        else ar_nvls_kernel<T, W><<<g, kArThreads, 0, stream>>>(c, i4, o4, nvec);
+        if (algo == kTwoShot) launch_k(ar_twoshot_kernel<T, W>, dim3(g), dim3(kArThreads), 0, stream, c, i4, o4, nvec);
+        else if (algo == kTwoShotPush) launch_k(ar_twoshot_push_kernel<T, W>, dim3(g), dim3(kArThreads), 0, stream,
+                                                c, i4, o4, nvec);
+        else launch_k(ar_nvls_kernel<T, W>, dim3(g), dim3(kArThreads), 0, stream, c, i4, o4, nvec);
       }));
     }
     MBX_CUDA_CHECK(cudaGetLastError());
@@ -1284,16 +1300,19 @@ void ar_rmsnorm_launch(const ArCtx& c, int algo, const void* in, void* residual,
   auto o4 = static_cast<uint4*>(out);
   if (algo == kOneShotPush) {
     if (bytes > ar_chunk_limit(c, kOneShotPush)) throw std::runtime_error("ar_rmsnorm: message exceeds one-shot slot");
-    MBX_DISPATCH_W1(W_, ar_rmsnorm_oneshot_kernel<W><<<g, threads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W1(W_, launch_k(ar_rmsnorm_oneshot_kernel<W>, dim3(g), dim3(threads), 0, stream,
+                                 c, i4, r4, w4, o4, M, H, eps));
   } else if (algo == kTwoShotPush) {
     const int Mo = (M + W_ - 1) / W_;
     if ((uint64_t)W_ * Mo * H * 2 + bytes > c.half_bytes)
       throw std::runtime_error("ar_rmsnorm: message exceeds the two-shot buffer");
     const int gp = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
-    MBX_DISPATCH_W1(W_, ar_rmsnorm_twoshot_push_kernel<W><<<gp, threads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W1(W_, launch_k(ar_rmsnorm_twoshot_push_kernel<W>, dim3(gp), dim3(threads), 0, stream,
+                                 c, i4, r4, w4, o4, M, H, eps));
   } else {
     if (bytes > ar_chunk_limit(c, kTwoShot)) throw std::runtime_error("ar_rmsnorm: message exceeds two-shot slot");
-    MBX_DISPATCH_W(W_, ar_rmsnorm_twoshot_kernel<W><<<g, threads, 0, stream>>>(c, i4, r4, w4, o4, M, H, eps));
+    MBX_DISPATCH_W(W_, launch_k(ar_rmsnorm_twoshot_kernel<W>, dim3(g), dim3(threads), 0, stream,
+                                c, i4, r4, w4, o4, M, H, eps));
   }
   MBX_CUDA_CHECK(cudaGetLastError());
 }
@@ -1305,7 +1324,8 @@ void ar_allgather_launch(const ArCtx& c, const void* in, void* out, uint64_t nby
   const uint64_t nvec = nbytes / 16;
   const int g = ar_grid(nvec, max_blocks);
   const int W_ = c.world;
-  MBX_DISPATCH_W(W_, ar_allgather_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(in),
+  MBX_DISPATCH_W(W_, launch_k(ar_allgather_kernel<W>, dim3(g), dim3(kArThreads), 0, stream,
+                              c, static_cast<const uint4*>(in),
                                                                            static_cast<uint4*>(out), nvec));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
@@ -1314,7 +1334,7 @@ void fused_rs_norm_launch(const ArCtx& c, int M, int N, int Mo, void* residual, 
                           float eps, int max_blocks, cudaStream_t stream) {
   const int g = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
   const int W_ = c.world;
-  MBX_DISPATCH_W1(W_, fused_rs_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
+  MBX_DISPATCH_W1(W_, launch_k(fused_rs_norm_kernel<W>, dim3(g), dim3(kArThreads), 0, stream,
                          c, M, N, Mo, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
                          static_cast<uint4*>(out), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
@@ -1324,7 +1344,7 @@ void fused_allsum_norm_launch(const ArCtx& c, int M, int N, void* residual, cons
                               int max_blocks, cudaStream_t stream) {
   const int g = std::max(1, std::min(M, std::min(max_blocks, (int)kMaxBlocks)));
   const int W_ = c.world;
-  MBX_DISPATCH_W1(W_, fused_allsum_norm_kernel<W><<<g, kArThreads, 0, stream>>>(
+  MBX_DISPATCH_W1(W_, launch_k(fused_allsum_norm_kernel<W>, dim3(g), dim3(kArThreads), 0, stream,
                          c, M, N, static_cast<uint4*>(residual), static_cast<const uint4*>(weight),
                          static_cast<uint4*>(out), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
@@ -1338,7 +1358,8 @@ void sp_rs_push_launch(const ArCtx& c, const void* x, int M, int N, int max_bloc
   if ((uint64_t)W_ * Mo * N * 2 > c.fuse_half_bytes)
     throw std::runtime_error("sp_rs_push: message exceeds the reduce-scatter buffer");
   const int g = ar_grid((uint64_t)M * N / 8, max_blocks);
-  MBX_DISPATCH_W1(W_, sp_rs_push_kernel<W><<<g, kArThreads, 0, stream>>>(c, static_cast<const uint4*>(x), M, N, Mo));
+  MBX_DISPATCH_W1(W_, launch_k(sp_rs_push_kernel<W>, dim3(g), dim3(kArThreads), 0, stream,
+                               c, static_cast<const uint4*>(x), M, N, Mo));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -1350,7 +1371,7 @@ void sp_rs_norm_ag_launch(const ArCtx& c, int M, int N, void* res_own, const voi
   const int Mo = (M + W_ - 1) / W_;
   if ((uint64_t)M * N * 2 > c.sp_bytes) throw std::runtime_error("sp_rs_norm_ag: rows exceed the gather buffer");
   const int g = std::max(1, std::min(Mo, std::min(max_blocks, (int)kMaxBlocks)));
-  MBX_DISPATCH_W1(W_, sp_rs_norm_ag_kernel<W><<<g, kArThreads, 0, stream>>>(
+  MBX_DISPATCH_W1(W_, launch_k(sp_rs_norm_ag_kernel<W>, dim3(g), dim3(kArThreads), 0, stream,
                          c, M, N, Mo, static_cast<uint4*>(res_own), static_cast<const uint4*>(w), eps));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
@@ -1359,7 +1380,7 @@ void sp_ag_wait_launch(const ArCtx& c, int M, cudaStream_t stream) {
   if (M == 0) return;
   const int Mo = (M + c.world - 1) / c.world;
   const int owners = std::min(c.world, (M + Mo - 1) / Mo);
-  sp_ag_wait_kernel<<<1, 32, 0, stream>>>(c, owners);
+  launch_k(sp_ag_wait_kernel, dim3(1), dim3(32), 0, stream, c, owners);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -106,6 +106,7 @@ MBX_DEVICE void load_kv_tile(uint32_t dst, const __nv_bfloat16* cache, const int
 }
 
 __global__ void __launch_bounds__(kAttnThreads) prefill_attention_kernel(PrefillArgs a) {
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   // [Q 64x128][K0][V0][K1][V1], each 16 KB
   const uint32_t sQ = smem_addr(smem);
@@ -321,6 +322,7 @@ MBX_DEVICE void load_page(uint32_t dst, const __nv_bfloat16* base, int lane) {
 }
 
 __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(DecodeArgs a) {
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t dsm[];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = a.nq / a.nkv;
@@ -508,6 +510,7 @@ __global__ void __launch_bounds__(32 * kCombineRows) decode_combine_kernel(const
                                                                           const float* __restrict__ part_lse,
                                                                           int splits, int64_t rows,
                                                                           __nv_bfloat16* __restrict__ o) {
+  pdl_wait();
   const int64_t bh = (int64_t)blockIdx.x * kCombineRows + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (bh >= rows) return;
@@ -563,7 +566,7 @@ void prefill_attention_launch(const void* q, const void* kc, const void* vc, voi
   static SmemLimit limit;
   limit.ensure((const void*)prefill_attention_kernel, smem);
   dim3 grid(n_tiles, nq);
-  prefill_attention_kernel<<<grid, kAttnThreads, smem, s>>>(a);
+  launch_k(prefill_attention_kernel, grid, dim3(kAttnThreads), smem, s, a);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -571,8 +574,8 @@ void attn_combine_launch(const float* part_o, const float* part_lse, int64_t row
                          cudaStream_t s) {
   if (rows == 0) return;
   const unsigned blocks = (unsigned)((rows + kCombineRows - 1) / kCombineRows);
-  decode_combine_kernel<<<blocks, 32 * kCombineRows, 0, s>>>(part_o, part_lse, splits, rows,
-                                                             static_cast<__nv_bfloat16*>(out));
+  launch_k(decode_combine_kernel, dim3(blocks), dim3(32 * kCombineRows), 0, s, part_o, part_lse, splits, rows,
+           static_cast<__nv_bfloat16*>(out));
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -599,7 +602,7 @@ void decode_attention_launch(const void* q, const void* kc, const void* vc, void
   static SmemLimit limit;
   limit.ensure((const void*)decode_attention_kernel, kDecSmem);
   dim3 grid(a.splits, nkv, B);
-  decode_attention_kernel<<<grid, kDecThreads, kDecSmem, s>>>(a);
+  launch_k(decode_attention_kernel, grid, dim3(kDecThreads), kDecSmem, s, a);
   MBX_CUDA_CHECK(cudaGetLastError());
   if (a.splits > 1) {
     attn_combine_launch(a.part_o, a.part_lse, (int64_t)B * nq, a.splits, a.o, s);

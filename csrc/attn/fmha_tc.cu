@@ -100,6 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();  // the tile list, lengths and block table may come from the previous kernel
   const int2 tile = a.tiles[blockIdx.x];
   const int r = tile.x, qoff = tile.y;
   const int head = blockIdx.y;
@@ -503,7 +504,7 @@ void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, 
   static SmemLimit limit;
   limit.ensure((const void*)fmha_tc_kernel, Smem::kTotal);
   dim3 grid(n_tiles, nq, a.splits);
-  fmha_tc_kernel<<<grid, kThreads, Smem::kTotal, s>>>(tq, tk, tv, a);
+  launch_k(fmha_tc_kernel, grid, dim3(kThreads), Smem::kTotal, s, tq, tk, tv, a);
   MBX_CUDA_CHECK(cudaGetLastError());
   if (a.splits > 1) attn_combine_launch(part_o, part_lse, (int64_t)T * nq, a.splits, o, s);
 }

@@ -12,6 +12,8 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <utility>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -29,6 +31,45 @@
   } while (0)
 
 namespace mbx {
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with `launch_k` may start
+// while the kernel before it on the stream is still finishing (its launch and
+// its own set-up overlap the other's tail). Every kernel launched that way
+// calls pdl_wait() before its first global-memory access that can depend on
+// earlier work: the wait returns once the preceding grids have completed and
+// their memory is visible (at once when the kernel was launched normally).
+// MBX_PDL=0 turns the attribute off (plain serialised launches).
+// ---------------------------------------------------------------------------
+MBX_DEVICE void pdl_wait() {
+#if defined(__CUDA_ARCH__)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MBX_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... Params, typename... Args>
+inline void launch_k(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  MBX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // Raises one kernel's dynamic shared-memory limit on every device it runs on.
 // The attribute belongs to a device, so a process that launches on several

@@ -274,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // set-up above overlaps the previous kernel; its outputs are read below
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -504,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t MN, int N,
                                      __nv_bfloat16* __restrict__ out, int64_t ldc,
                                      const __nv_bfloat16* __restrict__ residual) {
+  pdl_wait();
   const int64_t nvec = MN / 4;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += (int64_t)gridDim.x * blockDim.x) {
     float4 acc = reinterpret_cast<const float4*>(part)[v];
@@ -675,6 +677,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc::cluster_sync();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // set-up above overlaps the previous kernel; its outputs are read below
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -810,7 +813,7 @@ void launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArg
   auto kern = gemm2_tcgen05_kernel<BN, STAGES, EPI>;
   static SmemLimit limit;
   limit.ensure((const void*)kern, L::kTotal);
-  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, a);
+  launch_k(kern, dim3(grid), dim3(kThreads), L::kTotal, s, ta, tb, a);
 }
 
 template <int BN, int STAGES, int EPI>
@@ -819,7 +822,7 @@ void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
   auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI>;
   static SmemLimit limit;
   limit.ensure((const void*)kern, L::kTotal);
-  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, a);
+  launch_k(kern, dim3(grid), dim3(kThreads), L::kTotal, s, ta, tb, a);
 }
 
 template <int EPI>
@@ -1116,8 +1119,8 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
       const int64_t MN = M * N;
       const int threads = 256;
       const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
-      splitk_reduce_kernel<<<(int)std::max<int64_t>(1, blocks), threads, 0, s>>>(
-          workspace, (int)sp, MN, (int)N, (__nv_bfloat16*)C, ldc, a.residual);
+      launch_k(splitk_reduce_kernel, dim3((unsigned)std::max<int64_t>(1, blocks)), dim3(threads), 0, s,
+               (const float*)workspace, (int)sp, MN, (int)N, (__nv_bfloat16*)C, (int64_t)ldc, a.residual);
     }
     MBX_CUDA_CHECK(cudaGetLastError());
     return;
@@ -1167,8 +1170,8 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
       const int64_t MN = M * N;
       const int threads = 256;
       const int64_t blocks = std::min<int64_t>((MN / 4 + threads - 1) / threads, (int64_t)sms * 8);
-      splitk_reduce_kernel<<<(int)blocks, threads, 0, s>>>(workspace, a.splits, MN, (int)N, (__nv_bfloat16*)C, ldc,
-                                                           a.residual);
+      launch_k(splitk_reduce_kernel, dim3((unsigned)blocks), dim3(threads), 0, s, (const float*)workspace, a.splits,
+               MN, (int)N, (__nv_bfloat16*)C, (int64_t)ldc, a.residual);
     }
   }
   MBX_CUDA_CHECK(cudaGetLastError());

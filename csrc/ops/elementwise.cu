@@ -30,6 +30,7 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* red) {
 template <bool kResidual>
 __global__ void rmsnorm_kernel(const uint4* __restrict__ x, uint4* residual, const uint4* __restrict__ w,
                                uint4* __restrict__ out, int hvec, float inv_h, float eps) {
+  pdl_wait();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const uint4* xr = x + row * hvec;
@@ -75,6 +76,7 @@ __global__ void rope_and_cache_kernel(const __nv_bfloat16* __restrict__ qkv, con
                                       __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                                       __nv_bfloat16* __restrict__ v_cache, int nq, int nkv, int page) {
   constexpr int H2 = D / 2;
+  pdl_wait();
   const int t = blockIdx.x;
   const int p = pos[t];
   const float* cs = cos_sin + (int64_t)p * D;  // [cos(H2) | sin(H2)]
@@ -126,6 +128,7 @@ __global__ void rope_qknorm_cache_kernel(const __nv_bfloat16* __restrict__ qkv, 
                                          __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                                          __nv_bfloat16* __restrict__ v_cache, int nq, int nkv, int page) {
   constexpr int D = 128, H2 = 64;
+  pdl_wait();
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const float* cs = cos_sin + (int64_t)pos[t] * D;  // [cos(H2) | sin(H2)]
@@ -165,6 +168,7 @@ __global__ void rope_qknorm_cache_kernel(const __nv_bfloat16* __restrict__ qkv, 
 
 // out[m, j] = silu(x[m, j]) * x[m, I + j]
 __global__ void silu_mul_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, int ivec) {
+  pdl_wait();
   const int64_t row = blockIdx.y;
   const uint4* g = x + row * 2 * ivec;
   const uint4* u = g + ivec;
@@ -188,6 +192,7 @@ __global__ void silu_mul_kernel(const uint4* __restrict__ x, uint4* __restrict__
 // zero (the tensor-parallel allreduce then sums the shards).
 __global__ void embedding_kernel(const int* __restrict__ ids, const uint4* __restrict__ table, uint4* __restrict__ out,
                                  int hvec, int64_t start, int64_t rows) {
+  pdl_wait();
   const int t = blockIdx.x;
   const int64_t id = (int64_t)ids[t] - start;
   const bool in = id >= 0 && id < rows;
@@ -202,6 +207,7 @@ MBX_DEVICE float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ logits, int64_t ld, int V, int64_t offset,
                               float* __restrict__ best_val, int64_t* __restrict__ best_idx) {
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int64_t row = blockIdx.x;
@@ -244,6 +250,7 @@ __global__ void argmax_kernel(const T* __restrict__ logits, int64_t ld, int V, i
 // Pick the winner among per-rank (value, index) candidates: [W, B] -> [B].
 __global__ void argmax_combine_kernel(const float* __restrict__ vals, const int64_t* __restrict__ idxs, int W, int B,
                                       int64_t* __restrict__ out) {
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   float bv = vals[b];
@@ -272,11 +279,11 @@ void rmsnorm_launch(const void* x, void* residual, const void* w, void* out, int
   if (H % 8 != 0 || H / 8 > 4 * 1024) throw std::runtime_error("rmsnorm: bad hidden size");
   const int hvec = H / 8;
   if (residual)
-    rmsnorm_kernel<true><<<(unsigned)M, norm_threads(hvec), 0, s>>>(
-        (const uint4*)x, (uint4*)residual, (const uint4*)w, (uint4*)out, hvec, 1.f / H, eps);
+    launch_k(rmsnorm_kernel<true>, dim3((unsigned)M), dim3(norm_threads(hvec)), 0, s, (const uint4*)x,
+             (uint4*)residual, (const uint4*)w, (uint4*)out, hvec, 1.f / H, eps);
   else
-    rmsnorm_kernel<false><<<(unsigned)M, norm_threads(hvec), 0, s>>>((const uint4*)x, nullptr, (const uint4*)w,
-                                                                     (uint4*)out, hvec, 1.f / H, eps);
+    launch_k(rmsnorm_kernel<false>, dim3((unsigned)M), dim3(norm_threads(hvec)), 0, s, (const uint4*)x,
+             (uint4*)nullptr, (const uint4*)w, (uint4*)out, hvec, 1.f / H, eps);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -285,13 +292,12 @@ void rope_and_cache_launch(const void* qkv, const int* pos, const float* cos_sin
                            const void* q_norm, const void* k_norm, float eps) {
   if (T == 0) return;
   if (q_norm != nullptr) {
-    rope_qknorm_cache_kernel<<<(unsigned)T, 256, 0, s>>>(
-        (const __nv_bfloat16*)qkv, pos, cos_sin, slots, (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm,
-        eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, nq, nkv, page);
+    launch_k(rope_qknorm_cache_kernel, dim3((unsigned)T), dim3(256), 0, s, (const __nv_bfloat16*)qkv, pos, cos_sin,
+             slots, (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, eps, (__nv_bfloat16*)q_out,
+             (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, nq, nkv, page);
   } else {
-    rope_and_cache_kernel<128><<<(unsigned)T, 256, 0, s>>>(
-        (const __nv_bfloat16*)qkv, pos, cos_sin, slots, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache,
-        (__nv_bfloat16*)v_cache, nq, nkv, page);
+    launch_k(rope_and_cache_kernel<128>, dim3((unsigned)T), dim3(256), 0, s, (const __nv_bfloat16*)qkv, pos, cos_sin,
+             slots, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, nq, nkv, page);
   }
   MBX_CUDA_CHECK(cudaGetLastError());
 }
@@ -305,7 +311,8 @@ void silu_mul_launch(const void* x, void* out, int64_t M, int I2, cudaStream_t s
   for (int64_t r0 = 0; r0 < M; r0 += rows_per) {
     const int64_t rows = std::min(rows_per, M - r0);
     dim3 grid((ivec + threads - 1) / threads, (unsigned)rows);
-    silu_mul_kernel<<<grid, threads, 0, s>>>((const uint4*)x + r0 * 2 * ivec, (uint4*)out + r0 * ivec, ivec);
+    launch_k(silu_mul_kernel, grid, dim3(threads), 0, s, (const uint4*)x + r0 * 2 * ivec, (uint4*)out + r0 * ivec,
+             ivec);
   }
   MBX_CUDA_CHECK(cudaGetLastError());
 }
@@ -314,7 +321,8 @@ void embedding_launch(const int* ids, const void* table, void* out, int64_t T, i
                       cudaStream_t s) {
   if (T == 0) return;
   if (H % 8 != 0) throw std::runtime_error("embedding: hidden must be a multiple of 8");
-  embedding_kernel<<<(unsigned)T, 256, 0, s>>>(ids, (const uint4*)table, (uint4*)out, H / 8, start, rows);
+  launch_k(embedding_kernel, dim3((unsigned)T), dim3(256), 0, s, ids, (const uint4*)table, (uint4*)out, H / 8, start,
+           rows);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -322,16 +330,17 @@ void argmax_launch(const void* logits, bool bf16, int64_t ld, int64_t B, int V, 
                    int64_t* best_idx, cudaStream_t s) {
   if (B == 0) return;
   if (bf16)
-    argmax_kernel<__nv_bfloat16><<<(unsigned)B, 1024, 0, s>>>((const __nv_bfloat16*)logits, ld, V, offset, best_val,
-                                                               best_idx);
+    launch_k(argmax_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(1024), 0, s, (const __nv_bfloat16*)logits, ld, V,
+             offset, best_val, best_idx);
   else
-    argmax_kernel<float><<<(unsigned)B, 1024, 0, s>>>((const float*)logits, ld, V, offset, best_val, best_idx);
+    launch_k(argmax_kernel<float>, dim3((unsigned)B), dim3(1024), 0, s, (const float*)logits, ld, V, offset, best_val,
+             best_idx);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
 void argmax_combine_launch(const float* vals, const int64_t* idxs, int W, int B, int64_t* out, cudaStream_t s) {
   if (B == 0) return;
-  argmax_combine_kernel<<<(B + 127) / 128, 128, 0, s>>>(vals, idxs, W, B, out);
+  launch_k(argmax_combine_kernel, dim3((B + 127) / 128), dim3(128), 0, s, vals, idxs, W, B, out);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(kGemvThreads) awq_gemv_kernel(
   uint32_t wv[kGemvBatch];
 #pragma unroll
   for (int u = 0; u < kGemvBatch; ++u) wv[u] = (live && u < R) ? __ldg(wp + (int64_t)u * Nq) : 0u;
+  pdl_wait();  // the weights do not depend on earlier kernels; the activations do
   for (int i = threadIdx.x; i < M * G; i += blockDim.x) {
     const int m = i / G, k = i % G;
     xs[i] = __bfloat162float(x[m * ldx + k0 + k]);
@@ -162,6 +163,7 @@ constexpr int kRedOut = 32, kRedSlices = 8;
 __global__ void __launch_bounds__(kRedOut * kRedSlices) awq_reduce_kernel(
     const float* __restrict__ ws, int groups, int M, int N, const __nv_bfloat16* residual, __nv_bfloat16* out,
     int64_t ldo) {
+  pdl_wait();
   __shared__ float part[kRedSlices][kRedOut];
   const int o = threadIdx.x % kRedOut, sl = threadIdx.x / kRedOut;
   const int64_t i = (int64_t)blockIdx.x * kRedOut + o;
@@ -221,9 +223,8 @@ void gemv_launch(const AwqGemvArgs& a, cudaStream_t s) {
   const int bytes = gemv_smem_bytes(M, a.G);
   if (bytes > 48 * 1024) limit.ensure((const void*)awq_gemv_kernel<M>, gemv_smem_bytes(M, 256));
   dim3 grid((Nq + kGemvCols - 1) / kGemvCols, a.K / a.G);
-  awq_gemv_kernel<M><<<grid, kGemvThreads, bytes, s>>>(
-      (const __nv_bfloat16*)a.x, a.ldx, (const uint32_t*)a.qweight, (const uint32_t*)a.qzeros,
-      (const __half*)a.scales, a.ws, a.N, a.G);
+  launch_k(awq_gemv_kernel<M>, grid, dim3(kGemvThreads), bytes, s, (const __nv_bfloat16*)a.x, a.ldx,
+           (const uint32_t*)a.qweight, (const uint32_t*)a.qzeros, (const __half*)a.scales, a.ws, a.N, a.G);
 }
 
 }  // namespace
@@ -244,10 +245,8 @@ void awq_gemv_launch(const AwqGemvArgs& a, cudaStream_t s) {
   }
   MBX_CUDA_CHECK(cudaGetLastError());
   const int64_t MN = (int64_t)a.M * a.N;
-  awq_reduce_kernel<<<(unsigned)((MN + kRedOut - 1) / kRedOut), kRedOut * kRedSlices, 0, s>>>(a.ws, a.K / a.G, a.M,
-                                                                                            a.N,
-                                                                  (const __nv_bfloat16*)a.residual,
-                                                                  (__nv_bfloat16*)a.out, a.ldo);
+  launch_k(awq_reduce_kernel, dim3((unsigned)((MN + kRedOut - 1) / kRedOut)), dim3(kRedOut * kRedSlices), 0, s,
+           (const float*)a.ws, a.K / a.G, a.M, a.N, (const __nv_bfloat16*)a.residual, (__nv_bfloat16*)a.out, a.ldo);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 
