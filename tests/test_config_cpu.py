@@ -72,3 +72,26 @@ def test_importable_alias_resolves_to_the_same_modules():
     assert MailboxAR is integ.MailboxAR
     import mailbox_ar_b200
     assert mailbox_ar_b200.engine is real.engine
+
+
+def test_algorithm_choice_by_size_and_world():
+    """The measured routing: one-shot push up to oneshot_max, NVLS from
+    nvls_min only on nvls_min_world ranks or more (and only with multicast),
+    two-shot push otherwise."""
+    import types
+
+    comm = importlib.import_module("3080_mod_p2p_sglang_patch_b200.parallel.communicator")
+    MiB = 1 << 20
+    cfg = cfg_mod.CommConfig()
+
+    def pick(world, nbytes, mc=True):
+        ar = object.__new__(comm.MailboxAR)
+        ar.cfg, ar.world_size = cfg, world
+        ar._buf = types.SimpleNamespace(mc_ptr=1 if mc else 0)
+        return comm.ALGO_NAMES[ar.pick_algo(nbytes)]
+
+    assert pick(2, 32 * MiB) == "oneshot_push" and pick(2, 40 * MiB) == "twoshot_push"
+    assert pick(4, 2 * MiB) == "oneshot_push" and pick(4, 4 * MiB) == "twoshot_push"
+    assert pick(4, 64 * MiB) == "twoshot_push"  # NVLS never beat two-shot push at four ranks
+    assert pick(8, 1 * MiB) == "oneshot_push" and pick(8, 16 * MiB) == "twoshot_push"
+    assert pick(8, 32 * MiB) == "nvls" and pick(8, 32 * MiB, mc=False) == "twoshot_push"
