@@ -111,7 +111,8 @@ def gemm_error(device=None) -> int:
 
 def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: torch.Tensor = None,
          bn: int = 0, splits: int = 0) -> torch.Tensor:
-    """out[M, N] = a[M, K] @ w[N, K]^T (+ residual), tcgen05/TMEM kernel."""
+    """out[M, N] = a[M, K] @ w[N, K]^T (+ residual): the tcgen05/TMEM kernel,
+    or for 1-2 rows (decode) the CUDA-core GEMV, a plain weight stream."""
     C = cuda_ext()
     M, K = a.shape
     N = w.shape[0]
@@ -125,8 +126,12 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
     # reduction (pass ws.counters) measured no faster at 1 token, slower at 64,
     # and 1.5-2x slower at 512-1024 rows (qkv at TP=4/8)
     C.gemm(a, w, out, residual, wbuf, ws.err, bn, splits, None)
-    launches.add(2 if s > 1 else 1)
+    gemv = M <= C.GEMV_MAX_ROWS and not bn and not splits and K % 8 == 0 and _GEMV_ON
+    launches.add(1 if gemv or s <= 1 else 2)
     return out
+
+
+_GEMV_ON = os.environ.get("MBX_GEMV", "1") != "0"
 
 
 @dataclasses.dataclass

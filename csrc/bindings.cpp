@@ -457,6 +457,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace mbx;
   m.attr("SIG_BYTES") = (int64_t)kSigBytes;
   m.attr("BAR_WORDS") = (int64_t)kPhases * kMaxBlocks * kMaxRanks;  // barrier flags at offset 0
+  m.attr("GEMV_MAX_ROWS") = (int)kGemvMaxRows;
   m.attr("MAX_RANKS") = kMaxRanks;
   m.attr("MAX_BLOCKS") = kMaxBlocks;
   m.attr("STATE_WORDS") = (int)kStWords;

@@ -1065,6 +1065,16 @@ void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   const bool swap_ok = bn <= 0 && splits <= 0 && N % 4 == 0 && ag == nullptr;
   if (K % 8 != 0 || N % 8 != 0) throw std::runtime_error("gemm: K and N must be multiples of 8");
   if (ldc % 8 != 0 || ((uint64_t)C & 15) != 0) throw std::runtime_error("gemm: C must be 16-byte aligned rows");
+  // 1-2 rows (decode): a weight stream, served by the CUDA-core GEMV
+  // (MBX_GEMV=0 keeps the tensor-core kernels)
+  static const bool gemv_on = [] {
+    const char* v = std::getenv("MBX_GEMV");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  if (gemv_on && bn <= 0 && splits <= 0 && ag == nullptr && gemv_bf16_supported(A, lda, B, ldb, M, K)) {
+    gemv_bf16_launch(A, lda, B, ldb, C, ldc, residual, M, N, K, s);
+    return;
+  }
   const int sms = num_sms();
   GemmPlan p = plan_for(M, N, K, sms);
   if (bn > 0) p.bn = bn;

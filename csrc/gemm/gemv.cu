@@ -1,0 +1,172 @@
+// bf16 GEMV for decode batches of 1-2 rows, for sm_100a:
+//   out[m, n] = bf16(sum_k x[m, k] * W[n, k])            (fp32 accumulation)
+//   out[m, n] = bf16(bf16(sum_k ...) + residual[m, n])    (residual form, the
+//                                                          GEMM epilogue's rounding)
+// At one or two rows a linear layer is a weight stream: 2 bytes per weight
+// against 2-4 FLOPs, far below what the tensor cores need to pay off, and the
+// tile machinery (128-row MMA side, TMEM epilogue, split-K partials and their
+// reduce launch) costs more than the stream itself. Here every weight byte is
+// read once with 16-byte loads, 8 in flight per lane, by a warp per pair of
+// output rows (several warps per pair when K is long); the x rows (a few KB,
+// shared by every warp) come through L1. Measured on 8B decode at TP=1: 15 % faster per step
+// at one row, 7 % at two, 8 % slower at four (the FMAs then bind), hence the
+// two-row limit. The first weight loads are issued before the
+// programmatic-launch wait, since the weights do not depend on earlier
+// kernels.
+#include <stdexcept>
+
+#include "../common.cuh"
+#include "../kernels.h"
+
+namespace mbx {
+
+namespace {
+
+constexpr int kWarps = 8;       // warps per CTA
+constexpr int kRowsPerWarp = 2;  // output rows of a warp (a row pair)
+constexpr int kU = 4;           // 16-byte chunks per row per lane per batch (8 loads in flight)
+
+MBX_DEVICE void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// A warp owns a pair of output rows and a slice of K: `wpr` warps (a power of
+// two up to kWarps) share a pair when K is long or the rows are few; lanes are
+// 8 elements apart inside the slice.
+// With wpr > 1 the slices' sums meet in shared memory in slice order.
+template <int M>
+__global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                const __nv_bfloat16* __restrict__ w, int64_t ldw,
+                                                                __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                                const __nv_bfloat16* residual, int N, int K,
+                                                                int wpr) {
+  __shared__ float red[kWarps][kRowsPerWarp][M];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = warp / wpr, slice = warp % wpr;
+  const int n0 = (blockIdx.x * (kWarps / wpr) + pair) * kRowsPerWarp;
+  const int chunks = K / 8;  // 16-byte chunks per row
+  const int per = (chunks + wpr - 1) / wpr;
+  const int c_beg = slice * per, c_end = min(chunks, c_beg + per);
+  const uint4* wr[kRowsPerWarp];
+  bool live[kRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    live[r] = n0 + r < N;
+    wr[r] = reinterpret_cast<const uint4*>(w + (int64_t)(live[r] ? n0 + r : 0) * ldw);
+  }
+  float acc[kRowsPerWarp][M];
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+
+  uint4 wv[kRowsPerWarp][kU];
+  auto load_w = [&](int c0) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c = c0 + u * 32 + lane;
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r)
+        wv[r][u] = (live[r] && c < c_end) ? __ldg(wr[r] + c) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  load_w(c_beg);
+  pdl_wait();  // x and residual may come from the previous kernel
+#pragma unroll 1
+  for (int c0 = c_beg; c0 < c_end; c0 += 32 * kU) {
+    if (c0 > c_beg) load_w(c0);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c = c0 + u * 32 + lane;
+      float xf[M][8];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const uint4 xv = c < c_end ? __ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx) + c)
+                                   : make_uint4(0, 0, 0, 0);
+        bf16x8_to_f32(xv, xf[m]);
+      }
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        float wf[8];
+        bf16x8_to_f32(wv[r][u], wf);
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[r][m] = fmaf(xf[m][j], wf[j], acc[r][m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+  if (wpr > 1) {
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+        for (int m = 0; m < M; ++m) red[warp][r][m] = acc[r][m];
+    }
+    __syncthreads();
+    if (slice != 0 || lane != 0) return;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float v = red[warp][r][m];
+        for (int i = 1; i < wpr; ++i) v += red[warp + i][r][m];
+        acc[r][m] = v;
+      }
+  } else if (lane != 0) {
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    const int n = n0 + r;
+    if (n >= N) continue;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float v = acc[r][m];
+      if (residual != nullptr)
+        v = __bfloat162float(__float2bfloat16(v)) + __bfloat162float(residual[(int64_t)m * ldo + n]);
+      out[(int64_t)m * ldo + n] = __float2bfloat16(v);
+    }
+  }
+}
+
+template <int M>
+void launch_rows(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
+                 const void* residual, int N, int K, cudaStream_t s) {
+  // warps per row pair: enough that no warp walks more than 4096 elements of a
+  // row, and that the grid holds about 4096 warps (narrow tensor-parallel
+  // shards: 384 row pairs of an 8B qkv shard at TP=8)
+  const int pairs = (N + kRowsPerWarp - 1) / kRowsPerWarp;
+  int wpr = 1;
+  while (wpr < kWarps && ((int64_t)K > 4096 * wpr || (int64_t)pairs * wpr < 4096)) wpr *= 2;
+  const int rows_per_cta = kRowsPerWarp * (kWarps / wpr);
+  launch_k(gemv_bf16_kernel<M>, dim3((unsigned)((N + rows_per_cta - 1) / rows_per_cta)), dim3(kWarps * 32), 0, s,
+           static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), ldw,
+           static_cast<__nv_bfloat16*>(out), ldo, static_cast<const __nv_bfloat16*>(residual), N, K, wpr);
+}
+
+}  // namespace
+
+bool gemv_bf16_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t M, int64_t K) {
+  return M >= 1 && M <= kGemvMaxRows && K % 8 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
+         ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0;
+}
+
+void gemv_bf16_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
+                      const void* residual, int64_t M, int64_t N, int64_t K, cudaStream_t s) {
+  if (!gemv_bf16_supported(x, ldx, w, ldw, M, K)) throw std::runtime_error("gemv: unsupported shape or alignment");
+  if (M == 1) launch_rows<1>(x, ldx, w, ldw, out, ldo, residual, (int)N, (int)K, s);
+  else launch_rows<2>(x, ldx, w, ldw, out, ldo, residual, (int)N, (int)K, s);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace mbx

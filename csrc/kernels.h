@@ -104,6 +104,13 @@ struct GemmAgWait {
   const uint32_t* epoch_word;  // device word holding the epoch to wait for
   int Mo;                      // rows per owner
 };
+// bf16 GEMV for 1..kGemvMaxRows rows (decode): out[M, N] = x[M, K] @ W[N, K]^T (+ residual,
+// rounded like the GEMM epilogue). x and W rows 16-byte aligned, K % 8 == 0.
+constexpr int kGemvMaxRows = 2;
+bool gemv_bf16_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t M, int64_t K);
+void gemv_bf16_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
+                      const void* residual, int64_t M, int64_t N, int64_t K, cudaStream_t s);
+
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,
                  uint32_t* err, cudaStream_t s, const GemmAgWait* ag = nullptr);

@@ -44,6 +44,7 @@ ext_modules = [
             src("ar", "allreduce.cu"),
             src("ops", "elementwise.cu"),
             src("gemm", "gemm.cu"),
+            src("gemm", "gemv.cu"),
             src("attn", "attention.cu"),
             src("attn", "decode_noalloc.cu"),
             src("attn", "fmha_tc.cu"),

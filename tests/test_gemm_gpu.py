@@ -69,6 +69,29 @@ def test_gemm_residual_epilogue():
     assert (out.float() - ref).abs().max().item() < 0.1
 
 
+@pytest.mark.parametrize("M", [1, 2, 3])
+def test_gemv_rows_against_fp32(M):
+    """1-2 rows run the CUDA-core GEMV (3 the tensor-core path, same check):
+    fp32 accumulation of the bf16 stream, K slices that do not divide evenly
+    among the warps, strided activations, and the residual form's two
+    roundings."""
+    ops = sub("ops")
+    torch.manual_seed(10 + M)
+    for N, K in ((1000, 4096), (24, 200), (6144, 4096), (4096, 14336)):
+        big = (torch.randn(M, K + 64, device="cuda") / K ** 0.25).to(torch.bfloat16)
+        a = big[:, :K]
+        w = (torch.randn(N, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+        ref = a.float() @ w.float().t()
+        out = ops.gemm(a, w)
+        torch.cuda.synchronize()
+        # one rounding of an fp32 sum: within a bf16 ulp plus accumulation-order noise
+        assert (out.float() - ref).abs().max().item() <= 8e-3 * ref.abs().max().item() + 1e-3, (N, K)
+        r = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+        got = ops.gemm(a, w, residual=r)
+        want = ref.to(torch.bfloat16).float() + r.float()
+        assert (got.float() - want).abs().max().item() < 0.1, (N, K)
+
+
 def test_gemm_strided_views():
     """Operands that are row slices of bigger tensors (ld > K)."""
     ops = sub("ops")
