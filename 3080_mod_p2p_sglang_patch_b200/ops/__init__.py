@@ -26,7 +26,8 @@ class _Workspace:
     def __init__(self, device, err=None):
         self.device = device
         self.err = err if err is not None else torch.zeros(1, dtype=torch.int32, device=device)
-        # split-K tile arrival counters (each reset by the tile's last CTA)
+        # arrival counters of in-kernel merges (split-KV decode attention; each
+        # reset by the last CTA that arrives)
         self.counters = torch.zeros(65536, dtype=torch.int32, device=device)
         self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
         self.dec_o = torch.empty(0, dtype=torch.float32, device=device)
@@ -132,6 +133,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor = None, residual: t
 
 
 _GEMV_ON = os.environ.get("MBX_GEMV", "1") != "0"
+_DECODE_MERGE = os.environ.get("MBX_DECODE_MERGE", "1") != "0"
 
 
 @dataclasses.dataclass
@@ -377,9 +379,13 @@ def decode_attention(q, k_cache, v_cache, kv_len, block_table, scale=None, split
         out = torch.empty_like(q)
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     B, nq, _ = q.shape
-    po = pl = None
+    po = pl = cnt = None
     if splits > 1:
-        po, pl = workspace(q.device).decode(B * nq * splits * 128, B * nq * splits)
-    cuda_ext().decode_attention(q, k_cache, v_cache, out, kv_len, block_table, po, pl, splits, scale)
-    launches.add(2 if splits > 1 else 1)
+        ws = workspace(q.device)
+        po, pl = ws.decode(B * nq * splits * 128, B * nq * splits)
+        # the last CTA of each (request, kv head) merges the splits in the kernel
+        # (MBX_DECODE_MERGE=0: a separate combine launch)
+        cnt = ws.counters if _DECODE_MERGE and B * k_cache.shape[1] <= ws.counters.numel() else None
+    cuda_ext().decode_attention(q, k_cache, v_cache, out, kv_len, block_table, po, pl, splits, scale, cnt)
+    launches.add(2 if splits > 1 and cnt is None else 1)
     return out

@@ -299,6 +299,7 @@ struct DecodeArgs {
   float* part_lse;          // [B, nq, splits]
   const int* kv_len;        // [B]
   const int* block_table;   // [B, max_blocks]
+  int* counters;            // [B, nkv] arrival counts (zero; the last CTA resets) or nullptr
   int max_blocks, nq, nkv, splits;
   float scale_log2;
 };
@@ -319,6 +320,39 @@ MBX_DEVICE void load_page(uint32_t dst, const __nv_bfloat16* base, int lane) {
     const int row = idx >> 4, chunk = idx & 15;
     cp_async16(dst + swz(row, chunk), base + row * D + chunk * 8);
   }
+}
+
+// One (row, head) of the split-KV merge, by one warp: lane l owns dims
+// 4l..4l+3. Reads go through L2 (__ldcg): the partials may have been written
+// by other CTAs of the same kernel.
+MBX_DEVICE void combine_row(const float* part_o, const float* part_lse, int splits, int64_t bh, int lane,
+                            __nv_bfloat16* o) {
+  const float* lse = part_lse + bh * splits;
+  float mx = -INFINITY;
+  for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, __ldcg(lse + s));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float4* po = reinterpret_cast<const float4*>(part_o + bh * splits * D) + lane;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < splits; ++s) {
+    const float ls = __ldcg(lse + s);
+    const float w = (ls == -INFINITY) ? 0.f : exp2f(ls - mx);
+    const float4 v = __ldcg(po + s * (D / 4));
+    den += w;
+    acc.x += w * v.x;
+    acc.y += w * v.y;
+    acc.z += w * v.z;
+    acc.w += w * v.w;
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+  __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  uint2 packed;
+  packed.x = *reinterpret_cast<uint32_t*>(&lo);
+  packed.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(o + bh * D + lane * 4) = packed;
 }
 
 __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(DecodeArgs a) {
@@ -500,6 +534,26 @@ __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(DecodeArg
         a.part_lse[((int64_t)b * a.nq + qh) * a.splits + split] = (den > 0.f) ? mm + log2f(den) : -INFINITY;
     }
   }
+  if (a.splits == 1 || a.counters == nullptr) return;
+  // Split-KV merge in the kernel: the last CTA of (b, kvh) to finish combines
+  // the G heads' partials (the combine kernel's arithmetic, one launch fewer).
+  // Classic arrival counting: every CTA's partial stores are fenced before its
+  // count; the last one fences again before reading the others'.
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* cnt = a.counters + (int64_t)b * a.nkv + kvh;
+    s_last = atomicAdd(cnt, 1) == a.splits - 1;
+    if (s_last) *cnt = 0;  // ready for the next launch
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int row = warp; row < G; row += kDecWarps) {
+    const int64_t bh = (int64_t)b * a.nq + kvh * G + row;
+    combine_row(a.part_o, a.part_lse, a.splits, bh, lane, a.o);
+  }
 }
 
 // Split-KV combine: one warp per (row, head), lane l owns dims 4l..4l+3.
@@ -514,32 +568,7 @@ __global__ void __launch_bounds__(32 * kCombineRows) decode_combine_kernel(const
   const int64_t bh = (int64_t)blockIdx.x * kCombineRows + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (bh >= rows) return;
-  const float* lse = part_lse + bh * splits;
-  float mx = -INFINITY;
-  for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, lse[s]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  const float4* po = reinterpret_cast<const float4*>(part_o + bh * splits * D) + lane;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float den = 0.f;
-#pragma unroll 4
-  for (int s = 0; s < splits; ++s) {
-    const float ls = lse[s];
-    const float w = (ls == -INFINITY) ? 0.f : exp2f(ls - mx);
-    const float4 v = __ldg(po + s * (D / 4));
-    den += w;
-    acc.x += w * v.x;
-    acc.y += w * v.y;
-    acc.z += w * v.z;
-    acc.w += w * v.w;
-  }
-  const float inv = den > 0.f ? 1.f / den : 0.f;
-  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-  __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-  uint2 packed;
-  packed.x = *reinterpret_cast<uint32_t*>(&lo);
-  packed.y = *reinterpret_cast<uint32_t*>(&hi);
-  *reinterpret_cast<uint2*>(o + bh * D + lane * 4) = packed;
+  combine_row(part_o, part_lse, splits, bh, lane, o);
 }
 
 }  // namespace
@@ -581,7 +610,7 @@ void attn_combine_launch(const float* part_o, const float* part_lse, int64_t row
 
 void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
                              const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
-                             float* part_o, float* part_lse, float scale, cudaStream_t s) {
+                             float* part_o, float* part_lse, float scale, cudaStream_t s, int* counters) {
   if (B == 0) return;
   if (nq % nkv != 0 || nq / nkv > kMaxG) throw std::runtime_error("decode: group size must be <= 16");
   DecodeArgs a;
@@ -598,13 +627,14 @@ void decode_attention_launch(const void* q, const void* kc, const void* vc, void
   a.scale_log2 = scale * 1.4426950408889634f;
   a.part_o = part_o;
   a.part_lse = part_lse;
+  a.counters = counters;
   if (a.splits > 1 && (!part_o || !part_lse)) throw std::runtime_error("decode: split-KV needs scratch buffers");
   static SmemLimit limit;
   limit.ensure((const void*)decode_attention_kernel, kDecSmem);
   dim3 grid(a.splits, nkv, B);
   launch_k(decode_attention_kernel, grid, dim3(kDecThreads), kDecSmem, s, a);
   MBX_CUDA_CHECK(cudaGetLastError());
-  if (a.splits > 1) {
+  if (a.splits > 1 && counters == nullptr) {
     attn_combine_launch(a.part_o, a.part_lse, (int64_t)B * nq, a.splits, a.o, s);
     MBX_CUDA_CHECK(cudaGetLastError());
   }

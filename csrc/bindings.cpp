@@ -425,7 +425,8 @@ void prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor 
 
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor out,
                       torch::Tensor kv_len, torch::Tensor block_table, c10::optional<torch::Tensor> part_o,
-                      c10::optional<torch::Tensor> part_lse, int64_t splits, double scale) {
+                      c10::optional<torch::Tensor> part_lse, int64_t splits, double scale,
+                      c10::optional<torch::Tensor> counters) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(k_cache, "k_cache");
@@ -444,9 +445,16 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     po = part_o->data_ptr<float>();
     pl = part_lse->data_ptr<float>();
   }
+  int* cnt = nullptr;
+  if (splits > 1 && counters.has_value()) {
+    check_cuda(*counters, "counters");
+    TORCH_CHECK(counters->scalar_type() == torch::kInt32 && counters->numel() >= (int64_t)B * k_cache.size(1),
+                "decode: counters must be int32 with at least batch * kv_heads zeros");
+    cnt = counters->data_ptr<int>();
+  }
   decode_attention_launch(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), kv_len.data_ptr<int>(),
                           block_table.data_ptr<int>(), block_table.size(1), B, nq, k_cache.size(1), (int)splits, po,
-                          pl, (float)scale, cur_stream());
+                          pl, (float)scale, cur_stream(), cnt);
 }
 
 }  // namespace
@@ -583,5 +591,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_combine", &argmax_combine);
   m.def("prefill_attention", &prefill_attention);
   m.def("prefill_attention_tc", &prefill_attention_tc);
-  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("out"),
+        py::arg("kv_len"), py::arg("block_table"), py::arg("part_o"), py::arg("part_lse"), py::arg("splits"),
+        py::arg("scale"), py::arg("counters") = c10::nullopt);
 }

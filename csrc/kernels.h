@@ -163,8 +163,11 @@ void prefill_attention_tc_launch(const void* q, const void* kc, const void* vc, 
 // LSE-weighted merge of split partials: rows x splits x 128 -> bf16 rows x 128.
 void attn_combine_launch(const float* part_o, const float* part_lse, int64_t rows, int splits, void* out,
                          cudaStream_t s);
+// counters: int32 [B * nkv], zero, for the in-kernel split-KV merge (each
+// (batch, kv head)'s last CTA merges and resets its count); nullptr merges
+// with a separate combine launch.
 void decode_attention_launch(const void* q, const void* kc, const void* vc, void* o, const int* kv_len,
                              const int* block_table, int max_blocks, int B, int nq, int nkv, int splits,
-                             float* part_o, float* part_lse, float scale, cudaStream_t s);
+                             float* part_o, float* part_lse, float scale, cudaStream_t s, int* counters = nullptr);
 
 }  // namespace mbx

@@ -65,3 +65,31 @@ def test_decode_split_kv(splits, nq, nkv):
         want = ref.attention(q[b:b + 1], k, v)
         err = (out[b:b + 1].float() - want).abs().max().item()
         assert err < 2e-2, f"b={b}: max err {err}"
+
+
+@pytest.mark.parametrize("splits", [2, 7, 16])
+def test_decode_in_kernel_merge_matches_combine_launch(splits):
+    """The split-KV merge done by each (request, kv head)'s last CTA gives the
+    bit-identical output of the separate combine launch, call after call (the
+    arrival counts reset themselves)."""
+    ops = sub("ops")
+    C = sub("_ext").cuda_ext()
+    lens = [3, 260, 4096, 1000, 17]
+    nq, nkv = 32, 8
+    kc, vc, bt = _paged(lens, nkv, 256, seed=5)
+    B = len(lens)
+    kvl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    cnt = torch.zeros(B * nkv, dtype=torch.int32, device="cuda")
+    po = torch.empty(B * nq * splits * D, device="cuda")
+    pl = torch.empty(B * nq * splits, device="cuda")
+    scale = 1.0 / D ** 0.5
+    for it in range(3):
+        q = torch.randn(B, nq, D, device="cuda").to(torch.bfloat16)
+        want = torch.empty_like(q)
+        C.decode_attention(q, kc, vc, want, kvl, bt, po, pl, splits, scale)
+        got = torch.empty_like(q)
+        C.decode_attention(q, kc, vc, got, kvl, bt, po, pl, splits, scale, cnt)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), f"iteration {it}"
+        assert int(cnt.abs().sum().item()) == 0
+    assert torch.equal(ops.decode_attention(q, kc, vc, kvl, bt, splits=splits), want)
