@@ -393,8 +393,10 @@ class LlamaTP:
             else:
                 part = self._linear(o.view(T, nq * D), L["o"])
                 x = self._ar_norm(part, residual, L["ln2"])
-            gu = self._linear(x, L["gate_up"])
-            a = self.k.silu_mul(gu)
+            if self.impl == "native" and not isinstance(L["gate_up"], ops.Int4Weight):
+                a = ops.gemm_silu(x, L["gate_up"])  # one GEMV launch at 1-2 rows
+            else:
+                a = self.k.silu_mul(self._linear(x, L["gate_up"]))
             nxt = w.layers[li + 1]["ln1"] if li + 1 < len(w.layers) else w.norm
             if self.tp_size == 1 and self.impl == "native":
                 self._linear(a, L["down"], out=residual, residual=residual)

@@ -282,6 +282,19 @@ def silu_mul(x, out=None):
     return out
 
 
+def gemm_silu(x, w, out=None):
+    """silu(x @ gate^T) * (x @ up^T) for a gate_up weight [2F, K] (gate rows
+    first): one GEMV launch for 1-2 rows (decode), else the GEMM and
+    silu_mul. Same roundings either way."""
+    M, F = x.shape[0], w.shape[0] // 2
+    if out is None:
+        out = torch.empty((M, F), dtype=torch.bfloat16, device=x.device)
+    if M <= cuda_ext().GEMV_MAX_ROWS and _GEMV_ON and cuda_ext().gemv_silu(x, w, out):
+        launches.add(1)
+        return out
+    return silu_mul(gemm(x, w), out=out)
+
+
 def embedding(ids, table, start=0, out=None):
     if out is None:
         out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device)

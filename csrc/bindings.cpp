@@ -297,6 +297,22 @@ void silu_mul(torch::Tensor x, torch::Tensor out) {
   silu_mul_launch(x.data_ptr(), out.data_ptr(), x.numel() / I2, I2, cur_stream());
 }
 
+// out[M, F] = silu(x @ gate^T) * (x @ up^T) in one GEMV for 1-2 rows; false
+// (nothing launched) when the shape or alignment does not fit it.
+bool gemv_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2 && x.size(1) == w.size(1) &&
+                  out.size(0) == x.size(0) && out.size(1) * 2 == w.size(0),
+              "gemv_silu: shapes must be x [M, K], w [2F, K], out [M, F]");
+  TORCH_CHECK(w.stride(1) == 1 && x.stride(1) == 1 && out.stride(1) == 1, "gemv_silu: rows must be contiguous");
+  if (!gemv_bf16_supported(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), x.size(0), x.size(1))) return false;
+  gemv_silu_launch(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0), x.size(0),
+                   w.size(0), x.size(1), cur_stream());
+  return true;
+}
+
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t start) {
   check_bf16(table, "table");
   check_bf16(out, "out");
@@ -586,6 +602,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("awq_gemv", &awq_gemv);
   m.def("awq_dequant", &awq_dequant);
   m.def("silu_mul", &silu_mul);
+  m.def("gemv_silu", &gemv_silu, py::arg("x"), py::arg("w"), py::arg("out"));
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
   m.def("argmax_combine", &argmax_combine);

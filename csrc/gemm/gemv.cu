@@ -39,7 +39,11 @@ MBX_DEVICE void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
 // two up to kWarps) share a pair when K is long or the rows are few; lanes are
 // 8 elements apart inside the slice.
 // With wpr > 1 the slices' sums meet in shared memory in slice order.
-template <int M>
+// kSilu: W is a gate_up weight [2F, K] (gate rows, then up rows); a warp's
+// row pair is (j, F + j) and it writes out[m, j] = silu(gate) * up with the
+// roundings of the separate GEMM + silu_mul pair (gate and up rounded to bf16,
+// silu(gate) rounded to bf16, the product rounded to bf16).
+template <int M, bool kSilu>
 __global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                 const __nv_bfloat16* __restrict__ w, int64_t ldw,
                                                                 __nv_bfloat16* __restrict__ out, int64_t ldo,
@@ -48,7 +52,9 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloa
   __shared__ float red[kWarps][kRowsPerWarp][M];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = warp / wpr, slice = warp % wpr;
-  const int n0 = (blockIdx.x * (kWarps / wpr) + pair) * kRowsPerWarp;
+  const int p = blockIdx.x * (kWarps / wpr) + pair;  // row pair index
+  const int F = N / 2;                                // kSilu: output width
+  const int n0 = kSilu ? p : p * kRowsPerWarp;
   const int chunks = K / 8;  // 16-byte chunks per row
   const int per = (chunks + wpr - 1) / wpr;
   const int c_beg = slice * per, c_end = min(chunks, c_beg + per);
@@ -56,8 +62,9 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloa
   bool live[kRowsPerWarp];
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) {
-    live[r] = n0 + r < N;
-    wr[r] = reinterpret_cast<const uint4*>(w + (int64_t)(live[r] ? n0 + r : 0) * ldw);
+    const int n = kSilu ? p + r * F : n0 + r;
+    live[r] = kSilu ? p < F : n < N;
+    wr[r] = reinterpret_cast<const uint4*>(w + (int64_t)(live[r] ? n : 0) * ldw);
   }
   float acc[kRowsPerWarp][M];
 #pragma unroll
@@ -125,6 +132,17 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloa
   } else if (lane != 0) {
     return;
   }
+  if constexpr (kSilu) {
+    if (p >= F) return;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const float g = __bfloat162float(__float2bfloat16(acc[0][m]));
+      const float u = __bfloat162float(__float2bfloat16(acc[1][m]));
+      const float sg = __bfloat162float(__float2bfloat16(g / (1.f + __expf(-g))));
+      out[(int64_t)m * ldo + p] = __float2bfloat16(sg * u);
+    }
+    return;
+  }
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) {
     const int n = n0 + r;
@@ -139,17 +157,18 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloa
   }
 }
 
-template <int M>
+template <int M, bool kSilu>
 void launch_rows(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
                  const void* residual, int N, int K, cudaStream_t s) {
   // warps per row pair: enough that no warp walks more than 4096 elements of a
   // row, and that the grid holds about 4096 warps (narrow tensor-parallel
   // shards: 384 row pairs of an 8B qkv shard at TP=8)
-  const int pairs = (N + kRowsPerWarp - 1) / kRowsPerWarp;
+  const int pairs = kSilu ? N / 2 : (N + kRowsPerWarp - 1) / kRowsPerWarp;
   int wpr = 1;
   while (wpr < kWarps && ((int64_t)K > 4096 * wpr || (int64_t)pairs * wpr < 4096)) wpr *= 2;
-  const int rows_per_cta = kRowsPerWarp * (kWarps / wpr);
-  launch_k(gemv_bf16_kernel<M>, dim3((unsigned)((N + rows_per_cta - 1) / rows_per_cta)), dim3(kWarps * 32), 0, s,
+  const int pairs_per_cta = kWarps / wpr;
+  launch_k(gemv_bf16_kernel<M, kSilu>, dim3((unsigned)((pairs + pairs_per_cta - 1) / pairs_per_cta)),
+           dim3(kWarps * 32), 0, s,
            static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), ldw,
            static_cast<__nv_bfloat16*>(out), ldo, static_cast<const __nv_bfloat16*>(residual), N, K, wpr);
 }
@@ -164,8 +183,17 @@ bool gemv_bf16_supported(const void* x, int64_t ldx, const void* w, int64_t ldw,
 void gemv_bf16_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
                       const void* residual, int64_t M, int64_t N, int64_t K, cudaStream_t s) {
   if (!gemv_bf16_supported(x, ldx, w, ldw, M, K)) throw std::runtime_error("gemv: unsupported shape or alignment");
-  if (M == 1) launch_rows<1>(x, ldx, w, ldw, out, ldo, residual, (int)N, (int)K, s);
-  else launch_rows<2>(x, ldx, w, ldw, out, ldo, residual, (int)N, (int)K, s);
+  if (M == 1) launch_rows<1, false>(x, ldx, w, ldw, out, ldo, residual, (int)N, (int)K, s);
+  else launch_rows<2, false>(x, ldx, w, ldw, out, ldo, residual, (int)N, (int)K, s);
+  MBX_CUDA_CHECK(cudaGetLastError());
+}
+
+void gemv_silu_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo, int64_t M,
+                      int64_t N2, int64_t K, cudaStream_t s) {
+  if (!gemv_bf16_supported(x, ldx, w, ldw, M, K) || N2 % 2 != 0)
+    throw std::runtime_error("gemv_silu: unsupported shape or alignment");
+  if (M == 1) launch_rows<1, true>(x, ldx, w, ldw, out, ldo, nullptr, (int)N2, (int)K, s);
+  else launch_rows<2, true>(x, ldx, w, ldw, out, ldo, nullptr, (int)N2, (int)K, s);
   MBX_CUDA_CHECK(cudaGetLastError());
 }
 

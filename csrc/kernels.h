@@ -110,6 +110,11 @@ constexpr int kGemvMaxRows = 2;
 bool gemv_bf16_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t M, int64_t K);
 void gemv_bf16_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo,
                       const void* residual, int64_t M, int64_t N, int64_t K, cudaStream_t s);
+// Fused decode MLP input for 1..kGemvMaxRows rows: out[M, F] = silu(x @ gate^T) *
+// (x @ up^T) for a gate_up weight [2F, K] (gate rows first), rounded like
+// GEMM + silu_mul.
+void gemv_silu_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo, int64_t M,
+                      int64_t N2, int64_t K, cudaStream_t s);
 
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,

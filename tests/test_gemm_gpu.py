@@ -142,3 +142,20 @@ def test_cta_pair_gemm_matches_reference(pair_bn):
     p = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT], env=env, cwd=root, capture_output=True, text=True,
                        timeout=300)
     assert p.returncode == 0 and "PAIR-OK" in p.stdout, p.stdout[-2000:] + p.stderr[-4000:]
+
+
+@pytest.mark.parametrize("M", [1, 2, 5])
+def test_gemm_silu_matches_gemm_then_silu_mul(M):
+    """The fused decode MLP input (one GEMV launch at 1-2 rows) rounds like the
+    GEMM followed by silu_mul; 5 rows take that pair itself."""
+    ops = sub("ops")
+    torch.manual_seed(20 + M)
+    for F, K in ((1792, 4096), (520, 1024)):
+        x = (torch.randn(M, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+        w = (torch.randn(2 * F, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+        got = ops.gemm_silu(x, w)
+        gu = ops.gemm(x, w)
+        want = ops.silu_mul(gu)
+        torch.cuda.synchronize()
+        assert got.shape == (M, F)
+        assert torch.equal(got, want), (F, K, (got.float() - want.float()).abs().max().item())
