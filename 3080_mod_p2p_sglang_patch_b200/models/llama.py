@@ -377,11 +377,18 @@ class LlamaTP:
         for li, L in enumerate(w.layers):
             if nvtx.ENABLED:
                 torch.cuda.nvtx.range_push(f"layer {li}")
-            qkv = self._linear(x, L["qkv"])
-            if cfg.qkv_bias:
-                qkv += L["qkv_bias"]
             kc, vc = kv_caches[li]
-            q = self.k.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc, **self._qk_norm_args(L))
+            q = None
+            if self.impl == "native" and not cfg.qkv_bias and not self._qk_norm_args(L) and \
+                    not isinstance(L["qkv"], ops.Int4Weight):
+                # decode (1-2 tokens): projection, RoPE and cache writes in one GEMV launch
+                q = ops.qkv_rope_and_cache(x, L["qkv"], positions, self.cos_sin, nq, nkv, slots, kc, vc)
+            if q is None:
+                qkv = self._linear(x, L["qkv"])
+                if cfg.qkv_bias:
+                    qkv += L["qkv_bias"]
+                q = self.k.rope_and_cache(qkv, positions, self.cos_sin, nq, nkv, slots, kc, vc,
+                                          **self._qk_norm_args(L))
             o = attn(li, q, kc, vc)
             if self.tp_size == 1 and self.impl == "native":
                 # residual add fused into the GEMM epilogue, in place

@@ -282,6 +282,22 @@ def silu_mul(x, out=None):
     return out
 
 
+def qkv_rope_and_cache(x, w, positions, cos_sin, nq, nkv, slots=None, k_cache=None, v_cache=None, page=16):
+    """The attention input of decode: q = RoPE(x @ Wq^T) and the paged k/v
+    writes, in one GEMV launch for 1-2 tokens (no q/k norm, no bias); None
+    when the shape does not fit it (the caller runs gemm + rope_and_cache,
+    which round the same way)."""
+    C = cuda_ext()
+    T = x.shape[0]
+    if T > C.GEMV_MAX_ROWS or not _GEMV_ON:
+        return None
+    q_out = torch.empty((T, nq, 128), dtype=torch.bfloat16, device=x.device)
+    if not C.gemv_rope(x, w, positions, cos_sin, slots, q_out, k_cache, v_cache, nq, nkv, page):
+        return None
+    launches.add(1)
+    return q_out
+
+
 def gemm_silu(x, w, out=None):
     """silu(x @ gate^T) * (x @ up^T) for a gate_up weight [2F, K] (gate rows
     first): one GEMV launch for 1-2 rows (decode), else the GEMM and

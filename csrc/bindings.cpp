@@ -313,6 +313,45 @@ bool gemv_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
   return true;
 }
 
+// q_out / paged k, v = RoPE(x @ w_qkv^T) in one GEMV for 1-2 tokens (no
+// q/k norm, no bias); false (nothing launched) when it does not fit.
+bool gemv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor positions, torch::Tensor cos_sin,
+               c10::optional<torch::Tensor> slots, torch::Tensor q_out, c10::optional<torch::Tensor> k_cache,
+               c10::optional<torch::Tensor> v_cache, int64_t nq, int64_t nkv, int64_t page) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(q_out, "q_out");
+  check_cuda(positions, "positions");
+  check_cuda(cos_sin, "cos_sin");
+  const int64_t M = x.size(0);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && w.size(0) == (nq + 2 * nkv) * 128,
+              "gemv_rope: x [M, K], w [(nq + 2 nkv) * 128, K]");
+  TORCH_CHECK(positions.scalar_type() == torch::kInt32 && positions.numel() == M, "positions must be int32 [M]");
+  TORCH_CHECK(cos_sin.scalar_type() == torch::kFloat32 && cos_sin.dim() == 2 && cos_sin.size(1) == 128,
+              "cos_sin must be fp32 [P, 128]");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == M * nq * 128, "q_out must be [M, nq, 128]");
+  TORCH_CHECK(w.stride(1) == 1 && x.stride(1) == 1, "gemv_rope: rows must be contiguous");
+  const int64_t* sp = nullptr;
+  void *kc = nullptr, *vc = nullptr;
+  if (slots.has_value()) {
+    check_cuda(*slots, "slots");
+    TORCH_CHECK(slots->scalar_type() == torch::kInt64 && slots->numel() == M, "slots must be int64 [M]");
+    TORCH_CHECK(k_cache.has_value() && v_cache.has_value(), "caches required with slots");
+    check_bf16(*k_cache, "k_cache");
+    check_bf16(*v_cache, "v_cache");
+    TORCH_CHECK(k_cache->dim() == 4 && k_cache->size(1) == nkv && k_cache->size(2) == page && k_cache->size(3) == 128,
+                "k_cache must be [blocks, nkv, page, 128]");
+    sp = slots->data_ptr<int64_t>();
+    kc = k_cache->data_ptr();
+    vc = v_cache->data_ptr();
+  }
+  if (!gemv_bf16_supported(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), M, x.size(1))) return false;
+  gemv_rope_launch(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), M, x.size(1), positions.data_ptr<int>(),
+                   cos_sin.data_ptr<float>(), sp, q_out.data_ptr(), kc, vc, (int)nq, (int)nkv, (int)page,
+                   cur_stream());
+  return true;
+}
+
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t start) {
   check_bf16(table, "table");
   check_bf16(out, "out");
@@ -603,6 +642,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("awq_dequant", &awq_dequant);
   m.def("silu_mul", &silu_mul);
   m.def("gemv_silu", &gemv_silu, py::arg("x"), py::arg("w"), py::arg("out"));
+  m.def("gemv_rope", &gemv_rope, py::arg("x"), py::arg("w"), py::arg("positions"), py::arg("cos_sin"),
+        py::arg("slots"), py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"), py::arg("nq"), py::arg("nkv"),
+        py::arg("page"));
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
   m.def("argmax_combine", &argmax_combine);

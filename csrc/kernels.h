@@ -115,6 +115,13 @@ void gemv_bf16_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, vo
 // GEMM + silu_mul.
 void gemv_silu_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, void* out, int64_t ldo, int64_t M,
                       int64_t N2, int64_t K, cudaStream_t s);
+// Fused decode attention input for 1..kGemvMaxRows tokens: qkv = x @ W^T for a
+// qkv weight [(nq + 2 nkv) * 128, K], neox RoPE of q and k at pos, q to q_out
+// [M, nq, 128], k and v to the paged cache at slots (nullptr: no cache
+// write); roundings of GEMM + rope_and_cache.
+void gemv_rope_launch(const void* x, int64_t ldx, const void* w, int64_t ldw, int64_t M, int64_t K, const int* pos,
+                      const float* cos_sin, const int64_t* slots, void* q_out, void* k_cache, void* v_cache, int nq,
+                      int nkv, int page, cudaStream_t s);
 
 void gemm_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* residual,
                  int64_t M, int64_t N, int64_t K, int bn, int splits, float* workspace, uint32_t* counters,

@@ -159,3 +159,25 @@ def test_gemm_silu_matches_gemm_then_silu_mul(M):
         torch.cuda.synchronize()
         assert got.shape == (M, F)
         assert torch.equal(got, want), (F, K, (got.float() - want.float()).abs().max().item())
+
+
+@pytest.mark.parametrize("M", [1, 2])
+def test_qkv_rope_gemv_matches_gemm_then_rope(M):
+    """The fused decode attention input (projection, neox RoPE, paged k/v
+    writes in one GEMV launch) gives bit for bit what the GEMM followed by
+    rope_and_cache gives."""
+    ops = sub("ops")
+    torch.manual_seed(30 + M)
+    nq, nkv, K, page, blocks = 8, 2, 1024, 16, 6
+    x = (torch.randn(M, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+    w = (torch.randn((nq + 2 * nkv) * 128, K, device="cuda") / K ** 0.25).to(torch.bfloat16)
+    cos_sin = ops.rope_cos_sin(4096, 128, 10000.0, "cuda")
+    pos = torch.tensor([37, 4000][:M], dtype=torch.int32, device="cuda")
+    slots = torch.tensor([5 * page + 3, 2 * page + 15][:M], dtype=torch.int64, device="cuda")
+    caches = [torch.zeros(blocks, nkv, page, 128, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+    got_q = ops.qkv_rope_and_cache(x, w, pos, cos_sin, nq, nkv, slots, caches[0], caches[1])
+    assert got_q is not None
+    want_q = ops.rope_and_cache(ops.gemm(x, w), pos, cos_sin, nq, nkv, slots, caches[2], caches[3])
+    torch.cuda.synchronize()
+    assert torch.equal(got_q, want_q)
+    assert torch.equal(caches[0], caches[2]) and torch.equal(caches[1], caches[3])
