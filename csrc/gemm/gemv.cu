@@ -2,17 +2,19 @@
 //   out[m, n] = bf16(sum_k x[m, k] * W[n, k])            (fp32 accumulation)
 //   out[m, n] = bf16(bf16(sum_k ...) + residual[m, n])    (residual form, the
 //                                                          GEMM epilogue's rounding)
+// plus two fused epilogues of the decoder (SiLU-mul of a gate_up projection;
+// RoPE and paged-KV writes of a qkv projection).
 // At one or two rows a linear layer is a weight stream: 2 bytes per weight
 // against 2-4 FLOPs, far below what the tensor cores need to pay off, and the
 // tile machinery (128-row MMA side, TMEM epilogue, split-K partials and their
 // reduce launch) costs more than the stream itself. Here every weight byte is
 // read once with 16-byte loads, 8 in flight per lane, by a warp per pair of
-// output rows (several warps per pair when K is long); the x rows (a few KB,
-// shared by every warp) come through L1. Measured on 8B decode at TP=1: 15 % faster per step
-// at one row, 7 % at two, 8 % slower at four (the FMAs then bind), hence the
-// two-row limit. The first weight loads are issued before the
-// programmatic-launch wait, since the weights do not depend on earlier
-// kernels.
+// output rows (several warps per pair when K is long or the rows are few);
+// the x rows (a few KB, shared by every warp) come through L1. Measured on 8B
+// decode at TP=1: 15 % faster per step at one row, 7 % at two, 8 % slower at
+// four (the FMAs then bind), hence the two-row limit. The first weight loads
+// are issued before the programmatic-launch wait, since the weights do not
+// depend on earlier kernels.
 #include <stdexcept>
 
 #include "../common.cuh"
@@ -22,9 +24,9 @@ namespace mbx {
 
 namespace {
 
-constexpr int kWarps = 8;       // warps per CTA
+constexpr int kWarps = 8;        // warps per CTA
 constexpr int kRowsPerWarp = 2;  // output rows of a warp (a row pair)
-constexpr int kU = 4;           // 16-byte chunks per row per lane per batch (8 loads in flight)
+constexpr int kU = 4;            // 16-byte chunks per row per lane per batch (8 loads in flight)
 
 MBX_DEVICE void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -35,10 +37,6 @@ MBX_DEVICE void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
   }
 }
 
-// A warp owns a pair of output rows and a slice of K: `wpr` warps (a power of
-// two up to kWarps) share a pair when K is long or the rows are few; lanes are
-// 8 elements apart inside the slice.
-// With wpr > 1 the slices' sums meet in shared memory in slice order.
 // Epilogue modes.
 //   kPlain: out[m, n] (+ residual).
 //   kSilu:  W is a gate_up weight [2F, K] (gate rows, then up rows); a warp's
@@ -64,6 +62,10 @@ struct RopeArgs {
   int nq, nkv, page;
 };
 
+// A warp owns a pair of output rows and a slice of K: `wpr` warps (a power of
+// two up to kWarps) share a pair when K is long or the rows are few; lanes are
+// 8 elements apart inside the slice. With wpr > 1 the slices' sums meet in
+// shared memory in slice order.
 template <int M, int EPI>
 __global__ void __launch_bounds__(kWarps * 32) gemv_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                 const __nv_bfloat16* __restrict__ w, int64_t ldw,
