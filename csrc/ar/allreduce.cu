@@ -508,6 +508,59 @@ MBX_DEVICE void residual_rmsnorm_row(const RowCtx& rc, Src src, uint4* residual_
                                      StoreOut st, int hvec, int H, float eps, float* red) {
   constexpr int KU = NV >= 8 ? 1 : (NV == 1 ? 4 : 8 / NV);
   float ss = 0.f;
+  if (hvec <= rc.tstep * KU) {
+    // The thread's share of the row is one batch (decode rows on a whole block,
+    // prefill rows on 8-warp groups): the new residual and the weights stay in
+    // registers, so the scaling needs no second round of loads. Same arithmetic
+    // in the same order as the two-pass form below.
+    uint4 v[KU][NV];
+    uint4 rv[KU], wv[KU], rb[KU];
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int pv = rc.t0 + u * rc.tstep;
+      if (pv < hvec) {
+#pragma unroll
+        for (int r = 0; r < NV; ++r) v[u][r] = ld_cg_v4(src(pv, r));
+        rv[u] = residual_row[pv];
+        wv[u] = w_row[pv];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int pv = rc.t0 + u * rc.tstep;
+      if (pv < hvec) {
+        float a[8] = {};
+#pragma unroll
+        for (int r = 0; r < NV; ++r) unpack_add<__nv_bfloat16>(v[u][r], a);
+        const uint4 arb = pack_from<__nv_bfloat16>(a);
+        float q[8] = {};
+        unpack_add<__nv_bfloat16>(arb, q);
+        unpack_add<__nv_bfloat16>(rv[u], q);
+        rb[u] = pack_from<__nv_bfloat16>(q);
+        residual_row[pv] = rb[u];
+        float f[8] = {};
+        unpack_add<__nv_bfloat16>(rb[u], f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += f[k] * f[k];
+      }
+    }
+    const float tot1 =
+        rc.group == 1 ? warp_sum(ss) : (rc.group == 0 ? block_sum(ss, red) : group_sum(ss, red, rc.group));
+    const float rstd1 = rsqrtf(tot1 / (float)H + eps);
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int pv = rc.t0 + u * rc.tstep;
+      if (pv < hvec) {
+        float q[8] = {}, ww[8] = {};
+        unpack_add<__nv_bfloat16>(rb[u], q);
+        unpack_add<__nv_bfloat16>(wv[u], ww);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q[k] = q[k] * rstd1 * ww[k];
+        st(pv, pack_from<__nv_bfloat16>(q));
+      }
+    }
+    return;
+  }
   for (int p0 = rc.t0; p0 < hvec; p0 += rc.tstep * KU) {
     uint4 v[KU][NV];
     uint4 rv[KU];
